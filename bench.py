@@ -1,0 +1,468 @@
+"""IVF-USQ batched search benchmark (B200).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload B]
+
+Workload B (default): 1,000,000 x 768 fp32 base from a 1,024-component Gaussian mixture
+(centres ~ N(0,1), sigma 0.5), every vector L2-normalised; 10,000 normalised queries
+from the same mixture; IVF-USQ 4-bit, inner product, nlist 4,096, nprobe 32, k 10,
+seed 7.  Seeded synthetic data stands in for the reference's Cohere-Wiki-1M set.
+
+A step is one batched search of the 10,000 queries.  `value` = queries/s with the
+queries and the index already in HBM (CUDA events on the launching stream); `e2e` =
+the same through the host-pointer C ABI call (pinned host queries in, ids and
+distances out, copies inside the timed region).  With N > 1 (torchrun, one rank per
+GPU) the inverted lists are sharded over the ranks (LPT by list size), every rank
+searches all queries on its lists, and the per-rank top-k are merged after an NCCL
+all-gather (total work fixed: strong scaling).
+
+--impl reference times the CPU restatement of the reference's search path (the
+oracle; the Rust reference cannot be built here) on the host cores, on the same
+frozen index, one bounded sample of queries per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: n, d, comps, sigma, nq, nlist, nprobe, k, nbits, metric(0 L2/1 IP), seed, normalise
+    "B": dict(n=1_000_000, d=768, comps=1024, sigma=0.5, nq=10_000, nlist=4096, nprobe=32, k=10,
+              nbits=4, metric=1, seed=7, normalise=True),
+    "C": dict(n=1_000_000, d=768, comps=1024, sigma=0.5, nq=10_000, nlist=4096, nprobe=32, k=100,
+              nbits=8, metric=1, seed=11, normalise=True),
+    "A": dict(n=100_000, d=128, comps=64, sigma=0.3, nq=1_000, nlist=256, nprobe=16, k=10,
+              nbits=4, metric=0, seed=42, normalise=False),
+    "D": dict(n=260_000, d=3072, comps=256, sigma=0.4, nq=5_000, nlist=1024, nprobe=24, k=10,
+              nbits=8, metric=1, seed=3, normalise=True),
+}
+TRAIN_ROWS_PER_LIST = 64
+KMEANS_ITERS = 10
+CACHE_DIR = os.environ.get("HANNS_BENCH_CACHE", "/tmp/hanns_b200_bench_cache")
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ data
+def make_data(w, device="cuda"):
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(w["seed"])
+    d = w["d"]
+    centres = torch.randn(w["comps"], d, generator=g, device=device)
+
+    def draw(n):
+        lab = torch.randint(0, w["comps"], (n,), generator=g, device=device)
+        x = centres[lab] + w["sigma"] * torch.randn(n, d, generator=g, device=device)
+        if w["normalise"]:
+            x = x / x.norm(dim=1, keepdim=True)
+        return x.contiguous()
+
+    base = draw(w["n"])
+    queries = draw(w["nq"])
+    return base, queries
+
+
+def exact_topk(base, queries, k, metric):
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    out = []
+    bn = (base * base).sum(1)
+    for s in range(0, queries.shape[0], 1024):
+        q = queries[s:s + 1024]
+        ip = q @ base.T
+        score = ip if metric == 1 else -(bn[None, :] - 2 * ip)
+        out.append(score.topk(k, dim=1).indices)
+    return torch.cat(out).cpu().numpy()
+
+
+def build_index(w, base_np, device):
+    """Trains on a seeded subsample and adds every row (GPU build path, C ABI)."""
+    from hanns_b200.ivf_usq import IvfUsqConfig, IvfUsqIndex
+    cfg = IvfUsqConfig(w["d"], w["nlist"], w["nbits"], nprobe=w["nprobe"], metric_type=w["metric"],
+                       rotation_seed=42)
+    idx = IvfUsqIndex(cfg, device=device)
+    rng = np.random.default_rng(w["seed"])
+    ntrain = min(base_np.shape[0], TRAIN_ROWS_PER_LIST * w["nlist"])
+    tr = base_np[np.sort(rng.choice(base_np.shape[0], ntrain, replace=False))]
+    t0 = time.time()
+    idx.train(tr, kmeans_iters=KMEANS_ITERS, kmeans_seed=w["seed"])
+    t1 = time.time()
+    idx.add(base_np)
+    log(f"[build] train {t1 - t0:.1f}s ({ntrain} rows, {KMEANS_ITERS} iters) add {time.time() - t1:.1f}s")
+    return idx
+
+
+def cache_path(name):
+    return os.path.join(CACHE_DIR, f"workload_{name}_artifact.npz")
+
+
+def get_artifact(name, w, base, device):
+    """Frozen index of the workload: built with the GPU build path once, cached on disk."""
+    p = cache_path(name)
+    if os.path.exists(p):
+        z = np.load(p)
+        return {k: (z[k].item() if z[k].ndim == 0 else z[k]) for k in z.files}
+    idx = build_index(w, base.cpu().numpy(), device)
+    art = idx.export_artifact()
+    idx.close()
+    os.makedirs(CACHE_DIR, exist_ok=True)
+    tmp = p + f".tmp{os.getpid()}.npz"
+    np.savez(tmp, **art)
+    os.replace(tmp, p)
+    return art
+
+
+def scan_bytes(art, probes, k, nbits):
+    """Algorithmic bytes of the list-scan kernel for one batch: per (query, probe),
+    |L|*D/8 sign bytes when FastScan runs, plus (code bytes + 16 B meta + 8 B id) per
+    reranked candidate."""
+    from oracle.oracle import n_candidates
+    D = int(art["padded_dim"])
+    cb = (D * nbits + 7) // 8
+    ncand = n_candidates(nbits, k)
+    sizes = np.diff(art["list_offsets"])[probes.reshape(-1)]
+    fs = sizes > ncand
+    return int((sizes * (D // 8) * fs).sum() + (np.minimum(sizes, ncand) * (cb + 24)).sum())
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args, w, rank, world):
+    """CPU restatement of the reference search path (oracle), all host threads."""
+    if rank != 0:
+        return
+    import torch
+    from oracle import oracle as O
+    base, queries = make_data(w, "cuda" if torch.cuda.is_available() else "cpu")
+    art = get_artifact(args.workload, w, base, 0)
+    q = queries.cpu().numpy()
+    del base
+    oi = O.OracleIndex(art)
+    cores = os.cpu_count() or 1
+    # sample size: ~8 s of host work per step, measured on a first probe
+    t0 = time.perf_counter()
+    oi.search(q[:64], w["k"], w["nprobe"], nthreads=cores)
+    per_q = (time.perf_counter() - t0) / 64
+    sample = int(min(w["nq"], max(64, 8.0 / max(per_q, 1e-9))))
+    for _ in range(args.warmup):
+        oi.search(q[:min(sample, 64)], w["k"], w["nprobe"], nthreads=cores)
+    times = []
+    for s in range(args.steps):
+        off = (s * sample) % max(w["nq"] - sample + 1, 1)
+        t0 = time.perf_counter()
+        oi.search(q[off:off + sample], w["k"], w["nprobe"], nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    qps = sample * len(times) / sum(times)
+    line = {
+        "impl": "reference", "metric": "ivf_usq_search_qps", "value": qps, "unit": "queries/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u8*i8->i32, f32 epilogue", "data": "synthetic",
+        "config": config_block(args.workload, w, world),
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} queries per step of the {w['nq']}-query batch, "
+                                   "oracle restatement (AVX-512BW/VNNI semantics), OpenMP over queries"},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(name, w, world):
+    return {"workload": f"IVF-USQ {w['nbits']}-bit {'IP' if w['metric'] else 'L2'}, "
+                        f"base {w['n']}x{w['d']} Gaussian mixture ({w['comps']} comps, sigma {w['sigma']}"
+                        f"{', normalised' if w['normalise'] else ''}), {w['nq']} queries, "
+                        f"nlist {w['nlist']}, nprobe {w['nprobe']}, k {w['k']}, seed {w['seed']}",
+            "name": name, "n": w["n"], "dim": w["d"], "nlist": w["nlist"], "nprobe": w["nprobe"],
+            "k": w["k"], "nbits": w["nbits"], "query_batch": w["nq"],
+            "parallelism": "1 GPU" if world == 1 else f"lists sharded over {world} GPUs + NCCL all-gather",
+            "l2_policy": "index larger than L2 (no flush needed)",
+            "build": f"train on {TRAIN_ROWS_PER_LIST} rows/list, {KMEANS_ITERS} k-means iters (seeded)"}
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, w, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from hanns_b200 import _lib
+    from hanns_b200.ivf_usq import IvfUsqIndex
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    base, queries = make_data(w, dev)
+    # rank 0 builds the index with the GPU build path (or loads the cached artifact);
+    # the other ranks load what rank 0 wrote
+    if rank == 0:
+        art = get_artifact(args.workload, w, base, local_rank)
+    if world > 1:
+        dist.barrier()
+        if rank != 0:
+            art = get_artifact(args.workload, w, base, local_rank)
+    idx = IvfUsqIndex.from_artifact(art, device=local_rank)
+    if world > 1:
+        idx.shard(rank, world)
+    nq, k, nprobe = w["nq"], w["k"], w["nprobe"]
+    stream = torch.cuda.current_stream(dev)
+    out_ids = torch.empty(nq, k, dtype=torch.int64, device=dev)
+    out_d = torch.empty(nq, k, dtype=torch.float32, device=dev)
+    if world > 1:
+        sh_d = torch.empty(nq, k, dtype=torch.float32, device=dev)
+        sh_k = torch.empty(nq, k, dtype=torch.int64, device=dev)
+        sh_i = torch.empty(nq, k, dtype=torch.int64, device=dev)
+        g_d = torch.empty(world, nq, k, dtype=torch.float32, device=dev)
+        g_k = torch.empty(world, nq, k, dtype=torch.int64, device=dev)
+        g_i = torch.empty(world, nq, k, dtype=torch.int64, device=dev)
+    L = _lib.lib()
+    launches = [0]
+
+    def step():
+        if world == 1:
+            idx.search_device(queries.data_ptr(), nq, k, nprobe, out_ids.data_ptr(), out_d.data_ptr(),
+                              0, stream.cuda_stream)
+            launches[0] += idx.last_launches()
+        else:
+            rc = L.hanns_gpu_ivf_usq_search_shard_device(idx._h, queries.data_ptr(), nq, k, nprobe,
+                                                          sh_d.data_ptr(), sh_k.data_ptr(),
+                                                          sh_i.data_ptr(), stream.cuda_stream)
+            assert rc == 0, _lib.last_error()
+            launches[0] += idx.last_launches()
+            dist.all_gather_into_tensor(g_d, sh_d)
+            dist.all_gather_into_tensor(g_k, sh_k)
+            dist.all_gather_into_tensor(g_i, sh_i)
+            rc = L.hanns_gpu_merge_shards_device(g_d.data_ptr(), g_k.data_ptr(), g_i.data_ptr(), world,
+                                                 nq, k, out_ids.data_ptr(), out_d.data_ptr(),
+                                                 stream.cuda_stream)
+            assert rc == 0, _lib.last_error()
+            launches[0] += 1
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches[0] = 0
+    scan_ms = []
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+            scan_ms.append(float(idx.stage_ms()[3]))
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = nq * args.steps / (ms / 1e3)
+    stages = idx.stage_ms().tolist()
+    res_ids = out_ids.cpu().numpy()
+
+    # ---- e2e through the host-pointer C ABI (pinned buffers), 1 GPU
+    e2e = None
+    if world == 1:
+        hq = torch.empty(nq, w["d"], dtype=torch.float32).pin_memory()
+        hq.copy_(queries.cpu())
+        h_ids = torch.empty(nq, k, dtype=torch.int64).pin_memory()
+        h_d = torch.empty(nq, k, dtype=torch.float32).pin_memory()
+        f32p, i64p = _lib.f32p, _lib.i64p
+        import ctypes as C
+
+        def e2e_step():
+            rc = L.hanns_gpu_ivf_usq_search(idx._h, C.cast(hq.data_ptr(), f32p), nq, k, nprobe, 0, None,
+                                            0, 0, None, C.cast(h_ids.data_ptr(), i64p),
+                                            C.cast(h_d.data_ptr(), f32p), None)
+            assert rc == 0, _lib.last_error()
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        el = time.perf_counter() - t0
+        e2e = {"value": nq * args.steps / el, "unit": "queries/s",
+               "h2d_bytes_per_step": nq * w["d"] * 4, "d2h_bytes_per_step": nq * k * 12,
+               "path": "hanns_gpu_ivf_usq_search (host pointers, pinned)"}
+        assert np.array_equal(h_ids.numpy(), res_ids), "e2e and device paths disagree"
+
+    if rank != 0:
+        return
+    # ---- roofline of the list-scan kernel (rank 0's launch)
+    probes = idx.debug_query(queries.cpu().numpy(), nprobe)["probes"]
+    art_local = art if world == 1 else idx.export_artifact()
+    if world > 1:
+        own = np.diff(art_local["list_offsets"]) > 0
+        probes = np.where(own[probes], probes, -1)
+        sizes = np.diff(art_local["list_offsets"])
+        pr = probes[probes >= 0]
+        from oracle.oracle import n_candidates
+        D = int(art_local["padded_dim"])
+        cb = (D * w["nbits"] + 7) // 8
+        nc = n_candidates(w["nbits"], k)
+        sz = sizes[pr]
+        alg = int((sz * (D // 8) * (sz > nc)).sum() + (np.minimum(sz, nc) * (cb + 24)).sum())
+    else:
+        alg = scan_bytes(art_local, probes, k, w["nbits"])
+    scan_s = statistics.median(scan_ms) / 1e3
+    peak, peak_kind = peaks()
+    achieved = alg / scan_s / 1e9
+    roof = {"kernel": "scan_lists_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+            "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+            "traffic": None, "algorithmic_bytes_per_launch": alg, "launch_ms": scan_s * 1e3}
+
+    # ---- recall and parity sample
+    gt = exact_topk(base, queries, k, w["metric"])
+    rec = float(np.mean([len(set(gt[i]) & set(res_ids[i])) / k for i in range(nq)]))
+    del base
+    cpu = None
+    parity = None
+    if world == 1 and not args.no_cpu:
+        from oracle import oracle as O
+        oi = O.OracleIndex(art)
+        cores = os.cpu_count() or 1
+        qn = queries.cpu().numpy()
+        t0 = time.perf_counter()
+        oi.search(qn[:64], k, nprobe, nthreads=cores)
+        per_q = (time.perf_counter() - t0) / 64
+        sample = int(min(nq, max(64, 8.0 / max(per_q, 1e-9))))
+        t0 = time.perf_counter()
+        o_ids, o_d, _ = oi.search(qn[:sample], k, nprobe, nthreads=cores)
+        el = time.perf_counter() - t0
+        cpu = {"value": sample / el, "unit": "queries/s", "cores": cores, "kind": "port",
+               "sample": f"first {sample} of the {nq} queries, oracle restatement, OpenMP over queries"}
+        gd = out_d.cpu().numpy()[:sample]
+        parity = {"queries_checked": sample,
+                  "ids_equal_rows": int((o_ids == res_ids[:sample]).all(1).sum()),
+                  "dists_bit_equal_rows": int((o_d.view(np.uint32) == gd.view(np.uint32)).all(1).sum())}
+    line = {
+        "metric": "ivf_usq_search_qps", "value": value, "unit": "queries/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "u8*i8->i32, f32 epilogue", "data": "synthetic",
+        "config": config_block(args.workload, w, world),
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": launches[0], "clocks": clk.summary(),
+        "recall_at_k": rec, "parity_vs_oracle": parity,
+        "stage_ms_last_step": {"coarse": stages[0], "prep": stages[1], "group": stages[2],
+                               "scan": stages[3], "merge": stages[4], "total": stages[5]},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="B", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, w, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,560 @@
+// capi.cu -- the C ABI of libhanns_gpu.so (declarations and citations: include/hanns_gpu.h).
+#include <cfloat>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "hanns_gpu.h"
+#include "ivf_usq_gpu.h"
+
+struct HannsIvfUsqHandle {
+    std::unique_ptr<hanns::IvfUsqGpu> idx;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+// Maps exceptions to CError codes (src/ffi.rs:62-71).
+int32_t code_of(const std::exception& e) {
+    if (dynamic_cast<const std::invalid_argument*>(&e)) return HANNS_INVALID_ARG;
+    if (dynamic_cast<const std::domain_error*>(&e)) return HANNS_NOT_IMPLEMENTED;
+    if (auto* ce = dynamic_cast<const hanns::CudaError*>(&e))
+        return ce->code == cudaErrorMemoryAllocation ? HANNS_OUT_OF_MEMORY : HANNS_INTERNAL;
+    return HANNS_INTERNAL;
+}
+
+template <class F>
+int32_t guarded(F&& f) {
+    try {
+        f();
+        return HANNS_OK;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return code_of(e);
+    } catch (...) {
+        set_error("unknown error");
+        return HANNS_INTERNAL;
+    }
+}
+
+int default_device() {
+    const char* e = std::getenv("HANNS_GPU_DEVICE");
+    return e ? std::atoi(e) : 0;
+}
+
+int kmeans_iters() {
+    const char* e = std::getenv("HANNS_GPU_KMEANS_ITERS");
+    return e ? std::atoi(e) : 25;
+}
+
+hanns::IvfUsqGpu* as_index(const void* p) {
+    return p ? static_cast<const HannsIvfUsqHandle*>(p)->idx.get() : nullptr;
+}
+
+CSearchResult* make_result(const std::vector<int64_t>& ids, const std::vector<float>& d,
+                           float ms) {
+    auto* r = static_cast<CSearchResult*>(std::malloc(sizeof(CSearchResult)));
+    if (!r) return nullptr;
+    r->num_results = ids.size();
+    r->ids = static_cast<int64_t*>(std::malloc(sizeof(int64_t) * std::max<size_t>(ids.size(), 1)));
+    r->distances = static_cast<float*>(std::malloc(sizeof(float) * std::max<size_t>(d.size(), 1)));
+    if (!r->ids || !r->distances) {
+        std::free(r->ids);
+        std::free(r->distances);
+        std::free(r);
+        return nullptr;
+    }
+    if (!ids.empty()) std::memcpy(r->ids, ids.data(), sizeof(int64_t) * ids.size());
+    if (!d.empty()) std::memcpy(r->distances, d.data(), sizeof(float) * d.size());
+    r->elapsed_ms = ms;
+    return r;
+}
+
+CSearchResult* search_common(const void* index, const float* query, size_t count, size_t top_k,
+                             size_t dim, const CBitset* bitset) {
+    auto* idx = as_index(index);
+    if (!idx || !query || count == 0 || top_k == 0 || dim == 0) return nullptr;
+    if ((int)dim != idx->dim()) {
+        set_error("query dimension mismatch");
+        return nullptr;
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    std::vector<int64_t> ids(count * top_k), counts(count);
+    std::vector<float> dists(count * top_k);
+    bool post = false;
+    int32_t rc = guarded([&] {
+        std::lock_guard<std::mutex> lk(idx->mutex());
+        hanns::SearchOptions opt;
+        opt.k = (int)top_k;
+        opt.nprobe = idx->nprobe();
+        const uint64_t* words = nullptr;
+        if (bitset && bitset->data && bitset->len > 0) {
+            const char* mode = std::getenv("HANNS_GPU_BITSET_MODE");
+            post = mode && std::strcmp(mode, "post") == 0;
+            opt.filter_mode = post ? HANNS_FILTER_POST : HANNS_FILTER_FUSED;
+            opt.bitset_len = (int64_t)bitset->len;
+            opt.n_bitsets = 1;
+            words = bitset->data;
+        }
+        idx->search_host(query, (int64_t)count, opt, words, nullptr, ids.data(), dists.data(),
+                         counts.data());
+    });
+    if (rc != HANNS_OK) return nullptr;
+    const double us =
+        std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+    if (std::getenv("HANNS_TRACE_SEARCH")) {
+        const float* st = idx->stage_ms();
+        std::fprintf(stderr,
+                     "TRACE_SEARCH nq=%zu elapsed_us=%.0f coarse_ms=%.3f prep_ms=%.3f "
+                     "group_ms=%.3f scan_ms=%.3f merge_ms=%.3f\n",
+                     count, us, st[0], st[1], st[2], st[3], st[4]);
+    }
+    if (post) {  // reference post-filter: rows concatenated, filtered entries dropped
+        std::vector<int64_t> fid;
+        std::vector<float> fd;
+        for (size_t q = 0; q < count; ++q)
+            for (int64_t j = 0; j < counts[q]; ++j) {
+                fid.push_back(ids[q * top_k + j]);
+                fd.push_back(dists[q * top_k + j]);
+            }
+        return make_result(fid, fd, (float)(us / 1000.0));
+    }
+    return make_result(ids, dists, (float)(us / 1000.0));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* hanns_gpu_last_error(void) { return g_last_error.c_str(); }
+
+int32_t hanns_gpu_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+// ------------------------------------------------------------------ KnowHere ABI
+void* knowhere_create_index(CIndexConfig config) {
+    if (config.index_type != CINDEX_IVF_RABITQ && config.index_type != CINDEX_IVF_USQ) {
+        set_error("libhanns_gpu builds the IVF-USQ index kind only");
+        return nullptr;
+    }
+    if (config.dim == 0) {
+        set_error("dimension must be > 0");
+        return nullptr;
+    }
+    HannsIvfUsqHandle* h = nullptr;
+    guarded([&] {
+        const int nlist = config.num_clusters ? (int)config.num_clusters : 100;
+        const int nbits = config.prq_nbits ? (int)config.prq_nbits : 4;
+        const int metric = config.metric_type == CMETRIC_L2 ? 0 : 1;
+        auto idx = std::make_unique<hanns::IvfUsqGpu>((int)config.dim, nlist, nbits, metric, 42ull,
+                                                      config.nprobe ? (int)config.nprobe : 8,
+                                                      default_device());
+        h = new HannsIvfUsqHandle{std::move(idx)};
+    });
+    return h;
+}
+
+void knowhere_free_index(void* index) { delete static_cast<HannsIvfUsqHandle*>(index); }
+
+int32_t knowhere_train_index(void* index, const float* vectors, size_t count, size_t dim) {
+    auto* idx = as_index(index);
+    if (!idx || !vectors || count == 0 || dim == 0) return HANNS_INVALID_ARG;
+    if ((int)dim != idx->dim()) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(idx->mutex());
+        idx->train(vectors, (int64_t)count, kmeans_iters(), 42ull);
+    });
+}
+
+int32_t knowhere_add_index(void* index, const float* vectors, const int64_t* ids, size_t count,
+                           size_t dim) {
+    auto* idx = as_index(index);
+    if (!idx || !vectors || count == 0 || dim == 0) return HANNS_INVALID_ARG;
+    if ((int)dim != idx->dim()) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(idx->mutex());
+        idx->add(vectors, (int64_t)count, ids);
+    });
+}
+
+CSearchResult* knowhere_search(const void* index, const float* query, size_t count, size_t top_k,
+                               size_t dim) {
+    return search_common(index, query, count, top_k, dim, nullptr);
+}
+
+CSearchResult* knowhere_search_with_bitset(const void* index, const float* query, size_t count,
+                                           size_t top_k, size_t dim, const CBitset* bitset) {
+    if (!bitset) return nullptr;
+    return search_common(index, query, count, top_k, dim, bitset);
+}
+
+int32_t knowhere_set_nprobe(void* index, size_t nprobe) {
+    auto* idx = as_index(index);
+    if (!idx || nprobe == 0) return HANNS_INVALID_ARG;
+    idx->set_nprobe((int)std::min<size_t>(nprobe, 1u << 30));
+    return HANNS_OK;
+}
+
+void knowhere_free_result(CSearchResult* result) {
+    if (!result) return;
+    std::free(result->ids);
+    std::free(result->distances);
+    std::free(result);
+}
+
+size_t knowhere_get_index_count(const void* index) {
+    auto* idx = as_index(index);
+    return idx ? (size_t)idx->count() : 0;
+}
+size_t knowhere_get_index_dim(const void* index) {
+    auto* idx = as_index(index);
+    return idx ? (size_t)idx->dim() : 0;
+}
+size_t knowhere_get_index_size(const void* index) {
+    auto* idx = as_index(index);
+    return idx ? (size_t)idx->size_bytes() : 0;
+}
+const char* knowhere_get_index_type(const void* index) { return index ? "IVF-USQ" : "Unknown"; }
+const char* knowhere_get_index_metric(const void* index) {
+    auto* idx = as_index(index);
+    if (!idx) return "Unknown";
+    return idx->metric() == 0 ? "L2" : "IP";
+}
+bool knowhere_has_raw_data(const void* index) { return false; }
+
+int32_t knowhere_save_index(const void* index, const char* path) {
+    auto* idx = as_index(index);
+    if (!idx || !path) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(idx->mutex());
+        idx->save(path);
+    });
+}
+int32_t knowhere_load_index(void* index, const char* path) {
+    auto* idx = as_index(index);
+    if (!idx || !path) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(idx->mutex());
+        idx->load(path);
+    });
+}
+
+CBitset* knowhere_bitset_create(size_t len) {
+    auto* b = static_cast<CBitset*>(std::malloc(sizeof(CBitset)));
+    if (!b) return nullptr;
+    b->len = len;
+    b->cap_words = (len + 63) / 64;
+    b->data = static_cast<uint64_t*>(std::calloc(std::max<size_t>(b->cap_words, 1), 8));
+    if (!b->data) {
+        std::free(b);
+        return nullptr;
+    }
+    return b;
+}
+void knowhere_bitset_free(CBitset* b) {
+    if (!b) return;
+    std::free(b->data);
+    std::free(b);
+}
+void knowhere_bitset_set(CBitset* b, size_t i, bool v) {
+    if (!b || i >= b->len) return;
+    if (v)
+        b->data[i >> 6] |= 1ull << (i & 63);
+    else
+        b->data[i >> 6] &= ~(1ull << (i & 63));
+}
+bool knowhere_bitset_get(const CBitset* b, size_t i) {
+    if (!b || i >= b->len) return false;
+    return (b->data[i >> 6] >> (i & 63)) & 1ull;
+}
+size_t knowhere_bitset_count(const CBitset* b) {
+    if (!b) return 0;
+    size_t c = 0;
+    for (size_t w = 0; w < (b->len + 63) / 64; ++w) {
+        uint64_t x = b->data[w];
+        if (w == (b->len - 1) / 64 && (b->len & 63)) x &= (1ull << (b->len & 63)) - 1;
+        c += (size_t)__builtin_popcountll(x);
+    }
+    return c;
+}
+size_t knowhere_bitset_size(const CBitset* b) { return b ? b->len : 0; }
+const uint64_t* knowhere_bitset_data(const CBitset* b) { return b ? b->data : nullptr; }
+
+// ------------------------------------------------------------ per-index ABI
+HannsIvfUsqHandle* knowhere_ivf_exrabitq_build(uint32_t dim, uint32_t nlist, uint32_t bits_per_dim,
+                                               const float* data, uint64_t n, const int64_t* ids) {
+    if (!data || dim == 0 || nlist == 0 || bits_per_dim == 0 || n == 0) return nullptr;
+    HannsIvfUsqHandle* h = nullptr;
+    guarded([&] {
+        auto idx = std::make_unique<hanns::IvfUsqGpu>((int)dim, (int)nlist, (int)bits_per_dim, 0,
+                                                      42ull, 1, default_device());
+        idx->train(data, (int64_t)n, kmeans_iters(), 42ull);
+        idx->add(data, (int64_t)n, ids);
+        h = new HannsIvfUsqHandle{std::move(idx)};
+    });
+    return h;
+}
+
+HannsIvfUsqHandle* knowhere_ivf_exrabitq_load(const char* path) {
+    if (!path) return nullptr;
+    HannsIvfUsqHandle* h = nullptr;
+    guarded([&] {
+        std::FILE* f = std::fopen(path, "rb");
+        if (!f) throw std::runtime_error(std::string("cannot open ") + path);
+        char magic[8];
+        int64_t hdr[10];
+        const bool ok = std::fread(magic, 1, 8, f) == 8 && std::fread(hdr, 8, 10, f) == 10;
+        std::fclose(f);
+        if (!ok) throw std::runtime_error("truncated index file");
+        auto idx = std::make_unique<hanns::IvfUsqGpu>((int)hdr[0], (int)hdr[2], (int)hdr[1],
+                                                      (int)hdr[3], (uint64_t)hdr[5], (int)hdr[4],
+                                                      default_device());
+        idx->load(path);
+        h = new HannsIvfUsqHandle{std::move(idx)};
+    });
+    return h;
+}
+
+int32_t knowhere_ivf_exrabitq_save(HannsIvfUsqHandle* index, const char* path) {
+    if (!index || !path) return -1;
+    return guarded([&] { index->idx->save(path); }) == HANNS_OK ? 0 : -1;
+}
+
+int32_t knowhere_ivf_exrabitq_batch_search(const HannsIvfUsqHandle* index, const float* queries,
+                                           uint64_t nq, uint32_t k, uint32_t nprobe,
+                                           float* distances, int64_t* labels) {
+    if (!index || !queries || !distances || !labels || nq == 0 || k == 0) return -1;
+    auto* idx = index->idx.get();
+    const int32_t rc = guarded([&] {
+        std::lock_guard<std::mutex> lk(idx->mutex());
+        hanns::SearchOptions opt;
+        opt.k = (int)k;
+        opt.nprobe = (int)nprobe;
+        idx->search_host(queries, (int64_t)nq, opt, nullptr, nullptr, labels, distances, nullptr);
+    });
+    if (rc != HANNS_OK) {
+        // the reference fills failed rows with (-1, f32::MAX) and still returns 0
+        for (uint64_t i = 0; i < nq * k; ++i) {
+            labels[i] = -1;
+            distances[i] = FLT_MAX;
+        }
+    }
+    return 0;
+}
+
+int32_t knowhere_ivf_exrabitq_search(const HannsIvfUsqHandle* index, const float* query, uint32_t k,
+                                     uint32_t nprobe, float* distances, int64_t* labels) {
+    if (!index || !query || !distances || !labels || k == 0) return -1;
+    auto* idx = index->idx.get();
+    return guarded([&] {
+               std::lock_guard<std::mutex> lk(idx->mutex());
+               hanns::SearchOptions opt;
+               opt.k = (int)k;
+               opt.nprobe = (int)nprobe;
+               idx->search_host(query, 1, opt, nullptr, nullptr, labels, distances, nullptr);
+           }) == HANNS_OK
+               ? 0
+               : -1;
+}
+
+int32_t knowhere_ivf_exrabitq_has_raw_data(const HannsIvfUsqHandle* index) { return 0; }
+uint64_t knowhere_ivf_exrabitq_count(const HannsIvfUsqHandle* index) {
+    return index ? (uint64_t)index->idx->count() : 0;
+}
+uint64_t knowhere_ivf_exrabitq_size(const HannsIvfUsqHandle* index) {
+    return index ? (uint64_t)index->idx->size_bytes() : 0;
+}
+void knowhere_ivf_exrabitq_free(HannsIvfUsqHandle* index) { delete index; }
+int32_t knowhere_ivf_exrabitq_set_nprobe(HannsIvfUsqHandle* index, uint32_t nprobe) {
+    if (!index) return -1;
+    index->idx->set_nprobe((int)std::max<uint32_t>(nprobe, 1));
+    return 0;
+}
+uint32_t knowhere_ivf_exrabitq_dim(const HannsIvfUsqHandle* index) {
+    return index ? (uint32_t)index->idx->dim() : 0;
+}
+uint32_t knowhere_ivf_exrabitq_nlist(const HannsIvfUsqHandle* index) {
+    return index ? (uint32_t)index->idx->nlist() : 0;
+}
+
+// ------------------------------------------------------------ hanns_gpu extras
+HannsIvfUsqHandle* hanns_gpu_ivf_usq_create(int32_t dim, int32_t nlist, int32_t nbits,
+                                            int32_t metric, uint64_t rotation_seed, int32_t nprobe,
+                                            int32_t device) {
+    HannsIvfUsqHandle* h = nullptr;
+    guarded([&] {
+        h = new HannsIvfUsqHandle{std::make_unique<hanns::IvfUsqGpu>(
+            dim, nlist, nbits, metric, rotation_seed, nprobe, device < 0 ? default_device() : device)};
+    });
+    return h;
+}
+
+HannsIvfUsqHandle* hanns_gpu_ivf_usq_import(const hanns_ivf_usq_artifact_t* a, int32_t device) {
+    if (!a) return nullptr;
+    HannsIvfUsqHandle* h = nullptr;
+    guarded([&] {
+        auto idx = std::make_unique<hanns::IvfUsqGpu>(a->dim, a->nlist, a->nbits, a->metric, 42ull,
+                                                      1, device < 0 ? default_device() : device);
+        idx->import_artifact(a);
+        h = new HannsIvfUsqHandle{std::move(idx)};
+    });
+    return h;
+}
+
+int32_t hanns_gpu_ivf_usq_shape(const HannsIvfUsqHandle* h, int64_t* out6) {
+    if (!h || !out6) return HANNS_INVALID_ARG;
+    auto* i = h->idx.get();
+    out6[0] = i->dim();
+    out6[1] = i->padded_dim();
+    out6[2] = i->nbits();
+    out6[3] = i->nlist();
+    out6[4] = i->metric();
+    out6[5] = i->count();
+    return HANNS_OK;
+}
+
+int32_t hanns_gpu_ivf_usq_export(const HannsIvfUsqHandle* h, hanns_ivf_usq_artifact_t* out) {
+    if (!h || !out) return HANNS_INVALID_ARG;
+    return guarded([&] { h->idx->export_artifact(out); });
+}
+
+int32_t hanns_gpu_ivf_usq_train(HannsIvfUsqHandle* h, const float* data, int64_t n, int32_t iters,
+                                uint64_t seed) {
+    if (!h || !data || n <= 0) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        h->idx->train(data, n, iters, seed);
+    });
+}
+
+int32_t hanns_gpu_ivf_usq_add(HannsIvfUsqHandle* h, const float* data, int64_t n,
+                              const int64_t* ids) {
+    if (!h || !data || n <= 0) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        h->idx->add(data, n, ids);
+    });
+}
+
+int32_t hanns_gpu_ivf_usq_search(HannsIvfUsqHandle* h, const float* queries, int64_t nq, int32_t k,
+                                 int32_t nprobe, int32_t filter_mode, const uint64_t* bitsets,
+                                 int64_t bitset_len, int64_t n_bitsets,
+                                 const int32_t* query_bitset, int64_t* ids, float* dists,
+                                 int64_t* counts) {
+    if (!h || !queries || nq <= 0 || k <= 0 || !ids || !dists) return HANNS_INVALID_ARG;
+    if (filter_mode < 0 || filter_mode > 2) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        hanns::SearchOptions opt;
+        opt.k = k;
+        opt.nprobe = nprobe;
+        opt.filter_mode = bitsets ? filter_mode : 0;
+        opt.bitset_len = bitset_len;
+        opt.n_bitsets = n_bitsets;
+        h->idx->search_host(queries, nq, opt, bitsets, query_bitset, ids, dists, counts);
+    });
+}
+
+int32_t hanns_gpu_ivf_usq_search_device(HannsIvfUsqHandle* h, const float* d_queries, int64_t nq,
+                                        int32_t k, int32_t nprobe, int32_t filter_mode,
+                                        const uint64_t* d_bitsets, int64_t bitset_len,
+                                        int64_t n_bitsets, const int32_t* d_query_bitset,
+                                        int64_t* d_ids, float* d_dists, int64_t* d_counts,
+                                        void* stream) {
+    if (!h || !d_queries || nq <= 0 || k <= 0 || !d_ids || !d_dists) return HANNS_INVALID_ARG;
+    if (filter_mode < 0 || filter_mode > 2) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        hanns::SearchOptions opt;
+        opt.k = k;
+        opt.nprobe = nprobe;
+        opt.filter_mode = d_bitsets ? filter_mode : 0;
+        opt.d_bitsets = d_bitsets;
+        opt.bitset_len = bitset_len;
+        opt.n_bitsets = n_bitsets;
+        opt.d_query_bitset = d_query_bitset;
+        h->idx->search_device(d_queries, nq, opt, d_ids, d_dists, d_counts, nullptr,
+                              static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t hanns_gpu_ivf_usq_stage_ms(const HannsIvfUsqHandle* h, float* out6) {
+    if (!h || !out6) return HANNS_INVALID_ARG;
+    std::memcpy(out6, h->idx->stage_ms(), sizeof(float) * 6);
+    return HANNS_OK;
+}
+
+int64_t hanns_gpu_ivf_usq_last_launches(const HannsIvfUsqHandle* h) {
+    return h ? h->idx->last_launches() : 0;
+}
+
+int32_t hanns_gpu_ivf_usq_set_nprobe(HannsIvfUsqHandle* h, int32_t nprobe) {
+    if (!h || nprobe <= 0) return HANNS_INVALID_ARG;
+    h->idx->set_nprobe(nprobe);
+    return HANNS_OK;
+}
+
+int64_t hanns_gpu_ivf_usq_count(const HannsIvfUsqHandle* h) { return h ? h->idx->count() : 0; }
+
+void hanns_gpu_ivf_usq_free(HannsIvfUsqHandle* h) { delete h; }
+
+int32_t hanns_gpu_ivf_usq_debug_query(HannsIvfUsqHandle* h, const float* queries, int64_t nq,
+                                      int32_t nprobe, int32_t* probes, float* q_rot, int8_t* q_i8,
+                                      int8_t* lut, float* scalars) {
+    if (!h || !queries || nq <= 0) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        h->idx->debug_query(queries, nq, nprobe, probes, q_rot, q_i8, lut, scalars);
+    });
+}
+
+int32_t hanns_gpu_ivf_usq_shard(HannsIvfUsqHandle* h, int32_t rank, int32_t world) {
+    if (!h) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        h->idx->shard(rank, world);
+    });
+}
+
+int32_t hanns_gpu_ivf_usq_search_shard_device(HannsIvfUsqHandle* h, const float* d_queries,
+                                              int64_t nq, int32_t k, int32_t nprobe,
+                                              float* d_dists, uint64_t* d_keys, int64_t* d_ids,
+                                              void* stream) {
+    if (!h || !d_queries || nq <= 0 || k <= 0 || !d_dists || !d_keys || !d_ids)
+        return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        hanns::SearchOptions opt;
+        opt.k = k;
+        opt.nprobe = nprobe;
+        h->idx->search_device(d_queries, nq, opt, d_ids, d_dists, nullptr, d_keys,
+                              static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t hanns_gpu_merge_shards_device(const float* d_dists, const uint64_t* d_keys,
+                                      const int64_t* d_ids, int32_t world, int64_t nq, int32_t k,
+                                      int64_t* d_out_ids, float* d_out_dists, void* stream) {
+    if (!d_dists || !d_keys || !d_ids || world < 1 || world > 32 || nq <= 0 || k <= 0)
+        return HANNS_INVALID_ARG;
+    return guarded([&] {
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        hanns::launch_merge_shards(d_dists, d_keys, d_ids, world, nq, k, d_out_ids, d_out_dists, s);
+        HANNS_CUDA_OK(cudaGetLastError());
+        HANNS_CUDA_OK(cudaStreamSynchronize(s));
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,725 @@
+// ivf_usq_gpu.cu -- host orchestration of the IVF-USQ index on one GPU.
+#include "ivf_usq_gpu.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <numeric>
+#include <stdexcept>
+
+#include "common.cuh"
+#include "hanns_gpu.h"
+
+namespace hanns {
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) HANNS_CUDA_OK(cudaSetDevice(dev));
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int padded_of(int d) { return (d + 63) / 64 * 64; }
+
+int64_t n_candidates(int nbits, int64_t k) {
+    if (nbits == 1) return std::max<int64_t>(k * 20, 200);
+    if (nbits >= 2 && nbits <= 4) return std::max<int64_t>(k * 15, 150);
+    return std::max<int64_t>(k * 30, 300);
+}
+
+template <class T>
+void h2d(DevBuf<T>& b, const T* src, size_t count, cudaStream_t s) {
+    b.reserve(count);
+    if (count) HANNS_CUDA_OK(cudaMemcpyAsync(b.p, src, count * sizeof(T), cudaMemcpyHostToDevice, s));
+}
+
+constexpr int kQueriesPerItem = 32;
+
+}  // namespace
+
+IvfUsqGpu::IvfUsqGpu(int dim, int nlist, int nbits, int metric, uint64_t rotation_seed, int nprobe,
+                     int device)
+    : dim_(dim), nbits_(nbits), nlist_(nlist), metric_(metric), device_(device),
+      rotation_seed_(rotation_seed) {
+    if (dim <= 0) throw std::invalid_argument("dim must be > 0");
+    if (nlist <= 0) throw std::invalid_argument("nlist must be > 0");
+    if (nbits < 1 || nbits > 8) throw std::invalid_argument("nbits must be 1..=8");
+    D_ = padded_of(dim);
+    code_bytes_ = (D_ * nbits + 7) / 8;
+    nprobe_ = std::max(1, std::min(nprobe, nlist));
+    DeviceGuard g(device_);
+    ensure_stream();
+    set_list_layout(std::vector<int64_t>(nlist_ + 1, 0));
+    owned_.reserve(nlist_);
+    HANNS_CUDA_OK(cudaMemsetAsync(owned_.p, 1, nlist_, stream_));
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+}
+
+IvfUsqGpu::~IvfUsqGpu() {
+    cudaSetDevice(device_);
+    for (auto& e : ev_)
+        if (e) cudaEventDestroy(e);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void IvfUsqGpu::ensure_stream() {
+    if (!stream_) {
+        HANNS_CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+        for (auto& e : ev_) HANNS_CUDA_OK(cudaEventCreate(&e));
+        scan_grid_ = scan_grid_size();
+    }
+}
+
+void IvfUsqGpu::check_supported() const {
+    if (nbits_ != 4 && nbits_ != 8)
+        throw std::domain_error("this build searches 4-bit and 8-bit IVF-USQ codes only");
+}
+
+int64_t IvfUsqGpu::size_bytes() const {
+    // Same accounting as IvfUsqIndex::size (src/faiss/ivf_usq.rs:208-222).
+    return (int64_t)nlist_ * dim_ * 4 + ntotal_ * (8 + 16 + (int64_t)code_bytes_);
+}
+
+void IvfUsqGpu::set_list_layout(const std::vector<int64_t>& h_off) {
+    h_list_off_ = h_off;
+    max_list_ = 1;
+    std::vector<int64_t> blk(nlist_ + 1, 0);
+    for (int l = 0; l < nlist_; ++l) {
+        const int64_t len = h_off[l + 1] - h_off[l];
+        max_list_ = (int)std::max<int64_t>(max_list_, len);
+        blk[l + 1] = blk[l] + (len + 31) / 32;
+    }
+    h2d(list_off_, h_off.data(), h_off.size(), stream_);
+    h2d(fs_blk_off_, blk.data(), blk.size(), stream_);
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+}
+
+void IvfUsqGpu::rebuild_fastscan() {
+    int64_t blocks = 0;
+    for (int l = 0; l < nlist_; ++l) blocks += (h_list_off_[l + 1] - h_list_off_[l] + 31) / 32;
+    const size_t words = (size_t)std::max<int64_t>(blocks, 1) * (D_ / 64) * 32;
+    fs_.reserve(words);
+    HANNS_CUDA_OK(cudaMemsetAsync(fs_.p, 0, words * sizeof(uint2), stream_));
+    launch_build_fastscan(signs_.p, list_off_.p, fs_blk_off_.p, nlist_, D_, fs_.p, stream_);
+    HANNS_CUDA_OK(cudaGetLastError());
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+}
+
+void IvfUsqGpu::upload_rotation_centroid() {
+    std::vector<float> P((size_t)D_ * D_);
+    rotation_matrix(rotation_seed_, D_, P.data());
+    h2d(P_, P.data(), P.size(), stream_);
+    rc_.reserve(D_);
+    // rotated_centroid = P * pad(global mean)  (quantizer.rs:107-121)
+    launch_rotate(gmean_.p, 1, dim_, D_, P_.p, rc_.p, stream_);
+    HANNS_CUDA_OK(cudaGetLastError());
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+}
+
+// ---------------------------------------------------------------- import/export
+void IvfUsqGpu::import_artifact(const void* art_) {
+    const auto* a = static_cast<const hanns_ivf_usq_artifact_t*>(art_);
+    DeviceGuard g(device_);
+    if (a->dim != dim_ || a->nbits != nbits_ || a->nlist != nlist_ || a->padded_dim != D_)
+        throw std::invalid_argument("artifact shape does not match the index");
+    metric_ = a->metric;
+    ntotal_ = a->ntotal;
+    h2d(centroids_, a->centroids, (size_t)nlist_ * dim_, stream_);
+    h2d(P_, a->rotation, (size_t)D_ * D_, stream_);
+    h2d(rc_, a->rotated_centroid, (size_t)D_, stream_);
+    std::vector<int64_t> off(a->list_offsets, a->list_offsets + nlist_ + 1);
+    if (off[0] != 0 || off[nlist_] != ntotal_) throw std::invalid_argument("bad list offsets");
+    for (int l = 0; l < nlist_; ++l)
+        if (off[l + 1] < off[l]) throw std::invalid_argument("list offsets not monotone");
+    const size_t n = (size_t)ntotal_;
+    h2d(ids_, a->ids, n, stream_);
+    std::vector<float4> meta(n);
+    for (size_t i = 0; i < n; ++i)
+        meta[i] = make_float4(a->norms[i], a->norms_sq[i], a->vmaxs[i], a->quant_qualities[i]);
+    h2d(meta_, meta.data(), n, stream_);
+    h2d(codes_, a->codes, n * code_bytes_, stream_);
+    h2d(signs_, a->sign_bits, n * (D_ / 8), stream_);
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    set_list_layout(off);
+    rebuild_fastscan();
+    gmean_.reserve(dim_);
+    HANNS_CUDA_OK(cudaMemset(gmean_.p, 0, sizeof(float) * dim_));  // not part of the artifact
+    trained_ = true;
+}
+
+void IvfUsqGpu::export_artifact(void* out_) const {
+    auto* o = static_cast<hanns_ivf_usq_artifact_t*>(out_);
+    DeviceGuard g(device_);
+    const size_t n = (size_t)ntotal_;
+    auto d2h = [&](void* dst, const void* src, size_t bytes) {
+        if (dst && bytes) HANNS_CUDA_OK(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+    };
+    o->dim = dim_;
+    o->padded_dim = D_;
+    o->nbits = nbits_;
+    o->nlist = nlist_;
+    o->metric = metric_;
+    o->ntotal = ntotal_;
+    d2h((void*)o->centroids, centroids_.p, sizeof(float) * nlist_ * dim_);
+    d2h((void*)o->rotation, P_.p, sizeof(float) * D_ * D_);
+    d2h((void*)o->rotated_centroid, rc_.p, sizeof(float) * D_);
+    if (o->list_offsets)
+        std::memcpy((void*)o->list_offsets, h_list_off_.data(), sizeof(int64_t) * (nlist_ + 1));
+    d2h((void*)o->ids, ids_.p, sizeof(int64_t) * n);
+    if (n && (o->norms || o->norms_sq || o->vmaxs || o->quant_qualities)) {
+        std::vector<float4> meta(n);
+        d2h(meta.data(), meta_.p, sizeof(float4) * n);
+        for (size_t i = 0; i < n; ++i) {
+            if (o->norms) ((float*)o->norms)[i] = meta[i].x;
+            if (o->norms_sq) ((float*)o->norms_sq)[i] = meta[i].y;
+            if (o->vmaxs) ((float*)o->vmaxs)[i] = meta[i].z;
+            if (o->quant_qualities) ((float*)o->quant_qualities)[i] = meta[i].w;
+        }
+    }
+    d2h((void*)o->codes, codes_.p, n * code_bytes_);
+    d2h((void*)o->sign_bits, signs_.p, n * (D_ / 8));
+}
+
+// ---------------------------------------------------------------- train / add
+void IvfUsqGpu::train(const float* h_data, int64_t n, int kmeans_iters, uint64_t kmeans_seed) {
+    DeviceGuard g(device_);
+    if (n < nlist_) throw std::invalid_argument("training data too small: n < nlist");
+    DevBuf<float> x;
+    h2d(x, h_data, (size_t)n * dim_, stream_);
+    // k-means init: nlist distinct rows chosen by a seeded partial Fisher-Yates.
+    std::vector<int64_t> perm(n);
+    std::iota(perm.begin(), perm.end(), 0);
+    uint64_t s = kmeans_seed ^ 0xD1B54A32D192ED03ull;
+    for (int64_t i = 0; i < nlist_; ++i) {
+        s = s * 6364136223846793005ull + 1442695040888963407ull;
+        const int64_t j = i + (int64_t)((s >> 33) % (uint64_t)(n - i));
+        std::swap(perm[i], perm[j]);
+    }
+    std::vector<int64_t> init(perm.begin(), perm.begin() + nlist_);
+    DevBuf<int64_t> d_init;
+    h2d(d_init, init.data(), init.size(), stream_);
+    centroids_.reserve((size_t)nlist_ * dim_);
+    launch_gather_rows(reinterpret_cast<const uint8_t*>(x.p), d_init.p, nlist_, (int64_t)dim_ * 4,
+                       reinterpret_cast<uint8_t*>(centroids_.p), stream_);
+    DevBuf<int32_t> assign;
+    assign.reserve(n);
+    DevBuf<long long> sums;
+    sums.reserve((size_t)nlist_ * dim_);
+    DevBuf<int> counts;
+    counts.reserve(nlist_);
+    const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(n, (1ll << 28) / nlist_));
+    DevBuf<float> dist;
+    dist.reserve((size_t)chunk * nlist_);
+    for (int it = 0; it < kmeans_iters; ++it) {
+        for (int64_t b = 0; b < n; b += chunk) {
+            const int64_t m = std::min(chunk, n - b);
+            launch_coarse_l2(x.p + b * dim_, m, centroids_.p, nlist_, dim_, dist.p, stream_);
+            launch_argmin_rows(dist.p, m, nlist_, assign.p + b, stream_);
+        }
+        HANNS_CUDA_OK(cudaMemsetAsync(sums.p, 0, sizeof(long long) * nlist_ * dim_, stream_));
+        HANNS_CUDA_OK(cudaMemsetAsync(counts.p, 0, sizeof(int) * nlist_, stream_));
+        launch_kmeans_accumulate(x.p, n, dim_, assign.p, sums.p, counts.p, stream_);
+        launch_kmeans_update(sums.p, counts.p, nlist_, dim_, centroids_.p, stream_);
+        HANNS_CUDA_OK(cudaGetLastError());
+    }
+    gmean_.reserve(dim_);
+    launch_global_mean(x.p, n, dim_, gmean_.p, stream_);
+    HANNS_CUDA_OK(cudaGetLastError());
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    upload_rotation_centroid();
+    // A retrain discards stored vectors, as a fresh IvfUsqIndex would hold none.
+    ntotal_ = 0;
+    set_list_layout(std::vector<int64_t>(nlist_ + 1, 0));
+    trained_ = true;
+}
+
+void IvfUsqGpu::add(const float* h_data, int64_t n, const int64_t* h_ids) {
+    DeviceGuard g(device_);
+    if (!trained_) throw std::invalid_argument("index not trained, call train() first");
+    check_supported();
+    if (n <= 0) return;
+    const int64_t chunk = 65536;
+    DevBuf<float> x, res, nsq;
+    DevBuf<float> rot;  // chunk*D floats followed by chunk*D code bytes (encode scratch)
+    DevBuf<float> dist;
+    DevBuf<int32_t> asg;
+    DevBuf<uint8_t> ncodes, nsigns;
+    DevBuf<float4> nmeta;
+    ncodes.reserve((size_t)n * code_bytes_);
+    nsigns.reserve((size_t)n * (D_ / 8));
+    nmeta.reserve((size_t)n);
+    asg.reserve((size_t)n);
+    const int64_t cchunk = std::max<int64_t>(1, std::min<int64_t>(chunk, (1ll << 28) / nlist_));
+    dist.reserve((size_t)cchunk * nlist_);
+    for (int64_t b = 0; b < n; b += chunk) {
+        const int64_t m = std::min(chunk, n - b);
+        h2d(x, h_data + b * dim_, (size_t)m * dim_, stream_);
+        nsq.reserve(m);
+        launch_row_norm_sq(x.p, m, dim_, nsq.p, stream_);
+        res.reserve((size_t)m * D_);
+        launch_residual_pad(x.p, m, dim_, D_, gmean_.p, res.p, stream_);
+        rot.reserve((size_t)m * D_ + ((size_t)m * D_ + 3) / 4);
+        launch_rotate(res.p, m, D_, D_, P_.p, rot.p, stream_);
+        launch_encode_rotated(rot.p, m, D_, nbits_, nsq.p, ncodes.p + b * code_bytes_,
+                              nsigns.p + b * (D_ / 8), nmeta.p + b, stream_);
+        for (int64_t c = 0; c < m; c += cchunk) {
+            const int64_t mm = std::min(cchunk, m - c);
+            launch_coarse_l2(x.p + c * dim_, mm, centroids_.p, nlist_, dim_, dist.p, stream_);
+            launch_argmin_rows(dist.p, mm, nlist_, asg.p + b + c, stream_);
+        }
+        HANNS_CUDA_OK(cudaGetLastError());
+    }
+    std::vector<int32_t> h_asg(n);
+    HANNS_CUDA_OK(cudaMemcpyAsync(h_asg.data(), asg.p, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
+                                  stream_));
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    // New list order: every list keeps its old rows, then the new rows in insertion order.
+    const int64_t old_n = ntotal_, tot = old_n + n;
+    std::vector<int64_t> cnt(nlist_ + 1, 0);
+    for (int l = 0; l < nlist_; ++l) cnt[l + 1] = h_list_off_[l + 1] - h_list_off_[l];
+    for (int64_t i = 0; i < n; ++i) cnt[h_asg[i] + 1]++;
+    std::vector<int64_t> off(nlist_ + 1, 0);
+    for (int l = 0; l < nlist_; ++l) off[l + 1] = off[l] + cnt[l + 1];
+    std::vector<int64_t> cursor(off.begin(), off.end() - 1), perm(tot);
+    for (int l = 0; l < nlist_; ++l)
+        for (int64_t r = h_list_off_[l]; r < h_list_off_[l + 1]; ++r) perm[cursor[l]++] = r;
+    for (int64_t i = 0; i < n; ++i) perm[cursor[h_asg[i]]++] = old_n + i;
+    // concatenated sources [old ; new]
+    DevBuf<uint8_t> cat_codes, cat_signs;
+    DevBuf<float4> cat_meta;
+    DevBuf<int64_t> cat_ids, d_perm;
+    cat_codes.reserve((size_t)tot * code_bytes_);
+    cat_signs.reserve((size_t)tot * (D_ / 8));
+    cat_meta.reserve(tot);
+    cat_ids.reserve(tot);
+    if (old_n) {
+        HANNS_CUDA_OK(cudaMemcpyAsync(cat_codes.p, codes_.p, (size_t)old_n * code_bytes_,
+                                      cudaMemcpyDeviceToDevice, stream_));
+        HANNS_CUDA_OK(cudaMemcpyAsync(cat_signs.p, signs_.p, (size_t)old_n * (D_ / 8),
+                                      cudaMemcpyDeviceToDevice, stream_));
+        HANNS_CUDA_OK(cudaMemcpyAsync(cat_meta.p, meta_.p, sizeof(float4) * old_n,
+                                      cudaMemcpyDeviceToDevice, stream_));
+        HANNS_CUDA_OK(cudaMemcpyAsync(cat_ids.p, ids_.p, sizeof(int64_t) * old_n,
+                                      cudaMemcpyDeviceToDevice, stream_));
+    }
+    HANNS_CUDA_OK(cudaMemcpyAsync(cat_codes.p + old_n * code_bytes_, ncodes.p,
+                                  (size_t)n * code_bytes_, cudaMemcpyDeviceToDevice, stream_));
+    HANNS_CUDA_OK(cudaMemcpyAsync(cat_signs.p + old_n * (D_ / 8), nsigns.p, (size_t)n * (D_ / 8),
+                                  cudaMemcpyDeviceToDevice, stream_));
+    HANNS_CUDA_OK(cudaMemcpyAsync(cat_meta.p + old_n, nmeta.p, sizeof(float4) * n,
+                                  cudaMemcpyDeviceToDevice, stream_));
+    std::vector<int64_t> new_ids(n);
+    for (int64_t i = 0; i < n; ++i) new_ids[i] = h_ids ? h_ids[i] : old_n + i;
+    HANNS_CUDA_OK(cudaMemcpyAsync(cat_ids.p + old_n, new_ids.data(), sizeof(int64_t) * n,
+                                  cudaMemcpyHostToDevice, stream_));
+    h2d(d_perm, perm.data(), perm.size(), stream_);
+    DevBuf<uint8_t> o_codes, o_signs;
+    DevBuf<float4> o_meta;
+    DevBuf<int64_t> o_ids;
+    o_codes.reserve((size_t)tot * code_bytes_);
+    o_signs.reserve((size_t)tot * (D_ / 8));
+    o_meta.reserve(tot);
+    o_ids.reserve(tot);
+    launch_gather_rows(cat_codes.p, d_perm.p, tot, code_bytes_, o_codes.p, stream_);
+    launch_gather_rows(cat_signs.p, d_perm.p, tot, D_ / 8, o_signs.p, stream_);
+    launch_gather_rows(reinterpret_cast<const uint8_t*>(cat_meta.p), d_perm.p, tot, 16,
+                       reinterpret_cast<uint8_t*>(o_meta.p), stream_);
+    launch_gather_rows(reinterpret_cast<const uint8_t*>(cat_ids.p), d_perm.p, tot, 8,
+                       reinterpret_cast<uint8_t*>(o_ids.p), stream_);
+    HANNS_CUDA_OK(cudaGetLastError());
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    codes_.swap(o_codes);
+    signs_.swap(o_signs);
+    meta_.swap(o_meta);
+    ids_.swap(o_ids);
+    ntotal_ = tot;
+    set_list_layout(off);
+    rebuild_fastscan();
+}
+
+// ---------------------------------------------------------------- sharding
+void IvfUsqGpu::shard(int rank, int world) {
+    DeviceGuard g(device_);
+    if (world < 1 || rank < 0 || rank >= world) throw std::invalid_argument("bad rank/world");
+    // longest-processing-time assignment of lists (by size) to ranks
+    std::vector<int> order(nlist_);
+    std::iota(order.begin(), order.end(), 0);
+    auto len = [&](int l) { return h_list_off_[l + 1] - h_list_off_[l]; };
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return len(a) > len(b); });
+    std::vector<int64_t> load(world, 0);
+    std::vector<uint8_t> owned(nlist_, 0);
+    for (int l : order) {
+        int best = 0;
+        for (int r = 1; r < world; ++r)
+            if (load[r] < load[best]) best = r;
+        load[best] += len(l);
+        owned[l] = best == rank ? 1 : 0;
+    }
+    // keep only owned lists' rows
+    std::vector<int64_t> perm, off(nlist_ + 1, 0);
+    for (int l = 0; l < nlist_; ++l) {
+        if (owned[l])
+            for (int64_t r = h_list_off_[l]; r < h_list_off_[l + 1]; ++r) perm.push_back(r);
+        off[l + 1] = (int64_t)perm.size();
+    }
+    const int64_t tot = (int64_t)perm.size();
+    DevBuf<int64_t> d_perm;
+    h2d(d_perm, perm.data(), perm.size(), stream_);
+    DevBuf<uint8_t> o_codes, o_signs;
+    DevBuf<float4> o_meta;
+    DevBuf<int64_t> o_ids;
+    o_codes.reserve((size_t)tot * code_bytes_);
+    o_signs.reserve((size_t)tot * (D_ / 8));
+    o_meta.reserve(tot);
+    o_ids.reserve(tot);
+    launch_gather_rows(codes_.p, d_perm.p, tot, code_bytes_, o_codes.p, stream_);
+    launch_gather_rows(signs_.p, d_perm.p, tot, D_ / 8, o_signs.p, stream_);
+    launch_gather_rows(reinterpret_cast<const uint8_t*>(meta_.p), d_perm.p, tot, 16,
+                       reinterpret_cast<uint8_t*>(o_meta.p), stream_);
+    launch_gather_rows(reinterpret_cast<const uint8_t*>(ids_.p), d_perm.p, tot, 8,
+                       reinterpret_cast<uint8_t*>(o_ids.p), stream_);
+    h2d(owned_, owned.data(), owned.size(), stream_);
+    HANNS_CUDA_OK(cudaGetLastError());
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    codes_.swap(o_codes);
+    signs_.swap(o_signs);
+    meta_.swap(o_meta);
+    ids_.swap(o_ids);
+    ntotal_ = tot;
+    sharded_ = true;
+    set_list_layout(off);
+    rebuild_fastscan();
+}
+
+// ---------------------------------------------------------------- search
+void IvfUsqGpu::search_batch(const float* d_q, int64_t nb, const SearchOptions& opt,
+                             int64_t* d_ids, float* d_dists, int64_t* d_counts, uint64_t* d_keys,
+                             cudaStream_t s, bool time_it) {
+    const int k = std::max(opt.k, 1);
+    const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
+    const int G = D_ / 4;
+    int64_t launches = 0;
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[0], s));
+    // 1. coarse probes
+    w_probes_.reserve((size_t)nb * nprobe);
+    w_sel_.reserve((size_t)nb * 2 * nprobe);
+    const int64_t cchunk = std::max<int64_t>(1, std::min<int64_t>(nb, (1ll << 28) / nlist_));
+    w_dist_.reserve((size_t)cchunk * nlist_);
+    for (int64_t c = 0; c < nb; c += cchunk) {
+        const int64_t m = std::min(cchunk, nb - c);
+        launch_coarse_l2(d_q + c * dim_, m, centroids_.p, nlist_, dim_, w_dist_.p, s);
+        launch_select_probes(w_dist_.p, m, nlist_, nprobe, w_probes_.p + c * nprobe, w_sel_.p, s);
+        launches += 2;
+    }
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[1], s));
+    // 2. query state
+    w_qrot_.reserve((size_t)nb * D_);
+    w_qp_.reserve(nb);
+    w_qi8p_.reserve((size_t)nb * D_);
+    w_qi8n_.reserve((size_t)nb * D_);
+    w_lut_.reserve((size_t)nb * G * 16);
+    launch_rotate(d_q, nb, dim_, D_, P_.p, w_qrot_.p, s);
+    launch_query_state(d_q, w_qrot_.p, nb, dim_, D_, rc_.p, nbits_, w_qp_.p, w_qi8p_.p, w_qi8n_.p,
+                       w_lut_.p, s);
+    launches += 2;
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[2], s));
+    // 3. group (query, probe) pairs by list
+    w_cnt_.reserve(nlist_ + 1);
+    w_cursor_.reserve(nlist_ + 1);
+    w_lq_off_.reserve(nlist_ + 1);
+    w_item_off_.reserve(nlist_ + 1);
+    w_counters_.reserve(2);
+    w_lq_.reserve((size_t)nb * nprobe);
+    w_items_.reserve((size_t)nb * nprobe);
+    HANNS_CUDA_OK(cudaMemsetAsync(w_counters_.p, 0, 2 * sizeof(int), s));
+    launch_group_pairs(w_probes_.p, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr,
+                       kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p, w_item_off_.p,
+                       w_counters_.p, w_lq_.p, w_items_.p, s);
+    launches += 4;
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[3], s));
+    // 4. list scan
+    const size_t slots = (size_t)nb * nprobe;
+    w_slot_key_.reserve(slots * k);
+    w_slot_tie_.reserve(slots * k);
+    w_slot_cnt_.reserve(slots);
+    HANNS_CUDA_OK(cudaMemsetAsync(w_slot_cnt_.p, 0, slots * sizeof(int), s));
+    const int grid = scan_grid_;
+    const size_t per_warp = (size_t)max_list_;
+    w_scores_.reserve((size_t)grid * 8 * per_warp);
+    w_cand_key_.reserve((size_t)grid * 8 * per_warp);
+    w_cand_tie_.reserve((size_t)grid * 8 * per_warp);
+    ScanArgs a{};
+    a.D = D_;
+    a.nbits = nbits_;
+    a.code_bytes = code_bytes_;
+    a.nchunks = D_ / 64;
+    a.G = G;
+    a.metric_l2 = metric_ == 0 ? 1 : 0;
+    a.list_off = list_off_.p;
+    a.fs_blk_off = fs_blk_off_.p;
+    a.fs = fs_.p;
+    a.codes = codes_.p;
+    a.meta = meta_.p;
+    a.ids = ids_.p;
+    a.qp = w_qp_.p;
+    a.lut = w_lut_.p;
+    a.q_i8p = w_qi8p_.p;
+    a.lq = w_lq_.p;
+    a.items = w_items_.p;
+    a.n_items = w_counters_.p;
+    a.item_counter = w_counters_.p + 1;
+    a.k = k;
+    a.n_cand = (int)n_candidates(nbits_, k);
+    a.nprobe = nprobe;
+    a.fused = opt.filter_mode == 2 ? 1 : 0;
+    a.bitsets = opt.d_bitsets;
+    a.bitset_len = opt.bitset_len;
+    a.bitset_words = (opt.bitset_len + 63) / 64;
+    a.n_bitsets = opt.d_bitsets ? opt.n_bitsets : 0;
+    a.query_bitset = opt.d_query_bitset;
+    a.out_key = w_slot_key_.p;
+    a.out_tie = w_slot_tie_.p;
+    a.out_cnt = w_slot_cnt_.p;
+    a.scores = w_scores_.p;
+    a.cand_key = w_cand_key_.p;
+    a.cand_tie = w_cand_tie_.p;
+    a.max_len = (int)per_warp;
+    launch_scan(a, grid, s);
+    launches += 1;
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
+    // 5. merge
+    w_mkey_.reserve((size_t)nb * k);
+    w_mtie_.reserve((size_t)nb * k);
+    MergeArgs m{};
+    m.nq = nb;
+    m.nprobe = nprobe;
+    m.k = k;
+    m.nlist = nlist_;
+    m.slot_key = w_slot_key_.p;
+    m.slot_tie = w_slot_tie_.p;
+    m.slot_cnt = w_slot_cnt_.p;
+    m.probes = w_probes_.p;
+    m.list_off = list_off_.p;
+    m.ids = ids_.p;
+    m.sel_key = w_mkey_.p;
+    m.sel_tie = w_mtie_.p;
+    m.out_ids = d_ids;
+    m.out_dists = d_dists;
+    m.out_counts = d_counts;
+    if (opt.filter_mode == 1 && opt.d_bitsets) {
+        m.post_bitsets = opt.d_bitsets;
+        m.bitset_len = opt.bitset_len;
+        m.bitset_words = (opt.bitset_len + 63) / 64;
+        m.n_bitsets = opt.n_bitsets;
+        m.query_bitset = opt.d_query_bitset;
+    }
+    m.shard_mode = d_keys ? 1 : 0;
+    m.out_keys = d_keys;
+    launch_merge(m, s);
+    launches += 1;
+    HANNS_CUDA_OK(cudaGetLastError());
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[5], s));
+    last_launches_ += launches;
+}
+
+void IvfUsqGpu::search_device(const float* d_queries, int64_t nq, const SearchOptions& opt,
+                              int64_t* d_ids, float* d_dists, int64_t* d_counts, uint64_t* d_keys,
+                              cudaStream_t stream) {
+    DeviceGuard g(device_);
+    if (!trained_) throw std::invalid_argument("index not trained");
+    check_supported();
+    if (nq <= 0) throw std::invalid_argument("query dimension mismatch");
+    cudaStream_t s = stream ? stream : stream_;
+    const int k = std::max(opt.k, 1);
+    const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
+    // batch size bounded by the per-(query, probe) slot memory (~2 GiB)
+    int64_t nb_max = std::max<int64_t>(1, (2ll << 30) / ((int64_t)nprobe * k * 16));
+    nb_max = std::min<int64_t>(nb_max, 65536);
+    last_launches_ = 0;
+    for (int e = 0; e < 6; ++e) stage_ms_[e] = 0;
+    for (int64_t b = 0; b < nq; b += nb_max) {
+        const int64_t nb = std::min(nb_max, nq - b);
+        SearchOptions o = opt;
+        if (o.d_query_bitset) o.d_query_bitset += b;
+        search_batch(d_queries + b * dim_, nb, o, d_ids + b * k, d_dists + b * k,
+                     d_counts ? d_counts + b : nullptr, d_keys ? d_keys + b * k : nullptr, s, true);
+        HANNS_CUDA_OK(cudaEventSynchronize(ev_[5]));
+        float t;
+        for (int e = 0; e < 5; ++e) {
+            HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[e], ev_[e + 1]));
+            stage_ms_[e] += t;
+        }
+        HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[0], ev_[5]));
+        stage_ms_[5] += t;
+    }
+    HANNS_CUDA_OK(cudaStreamSynchronize(s));
+}
+
+void IvfUsqGpu::search_host(const float* h_queries, int64_t nq, const SearchOptions& opt_in,
+                            const uint64_t* h_bitsets, const int32_t* h_query_bitset,
+                            int64_t* h_ids, float* h_dists, int64_t* h_counts) {
+    DeviceGuard g(device_);
+    SearchOptions opt = opt_in;
+    const int k = std::max(opt.k, 1);
+    opt.k = k;
+    h2d(w_pad_queries_, h_queries, (size_t)nq * dim_, stream_);
+    if (h_bitsets && opt.n_bitsets > 0 && opt.filter_mode != 0) {
+        const size_t words = (size_t)((opt.bitset_len + 63) / 64) * opt.n_bitsets;
+        h2d(w_bits_, h_bitsets, words, stream_);
+        opt.d_bitsets = w_bits_.p;
+        if (h_query_bitset) {
+            h2d(w_qbits_, h_query_bitset, (size_t)nq, stream_);
+            opt.d_query_bitset = w_qbits_.p;
+        } else {
+            opt.d_query_bitset = nullptr;
+        }
+    } else {
+        opt.d_bitsets = nullptr;
+        opt.n_bitsets = 0;
+        opt.d_query_bitset = nullptr;
+    }
+    w_out_ids_.reserve((size_t)nq * k);
+    w_out_dists_.reserve((size_t)nq * k);
+    w_out_counts_.reserve((size_t)nq);
+    search_device(w_pad_queries_.p, nq, opt, w_out_ids_.p, w_out_dists_.p, w_out_counts_.p, nullptr,
+                  stream_);
+    HANNS_CUDA_OK(cudaMemcpyAsync(h_ids, w_out_ids_.p, sizeof(int64_t) * nq * k,
+                                  cudaMemcpyDeviceToHost, stream_));
+    HANNS_CUDA_OK(cudaMemcpyAsync(h_dists, w_out_dists_.p, sizeof(float) * nq * k,
+                                  cudaMemcpyDeviceToHost, stream_));
+    if (h_counts)
+        HANNS_CUDA_OK(cudaMemcpyAsync(h_counts, w_out_counts_.p, sizeof(int64_t) * nq,
+                                      cudaMemcpyDeviceToHost, stream_));
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+}
+
+void IvfUsqGpu::debug_query(const float* h_queries, int64_t nq, int nprobe, int32_t* probes,
+                            float* q_rot, int8_t* q_i8, int8_t* lut, float* scalars) {
+    DeviceGuard g(device_);
+    if (!trained_) throw std::invalid_argument("index not trained");
+    nprobe = std::max(1, std::min(nprobe, nlist_));
+    const int G = D_ / 4;
+    h2d(w_pad_queries_, h_queries, (size_t)nq * dim_, stream_);
+    w_probes_.reserve((size_t)nq * nprobe);
+    w_sel_.reserve((size_t)nq * 2 * nprobe);
+    w_dist_.reserve((size_t)nq * nlist_);
+    launch_coarse_l2(w_pad_queries_.p, nq, centroids_.p, nlist_, dim_, w_dist_.p, stream_);
+    launch_select_probes(w_dist_.p, nq, nlist_, nprobe, w_probes_.p, w_sel_.p, stream_);
+    w_qrot_.reserve((size_t)nq * D_);
+    w_qp_.reserve(nq);
+    w_qi8p_.reserve((size_t)nq * D_);
+    w_qi8n_.reserve((size_t)nq * D_);
+    w_lut_.reserve((size_t)nq * G * 16);
+    launch_rotate(w_pad_queries_.p, nq, dim_, D_, P_.p, w_qrot_.p, stream_);
+    launch_query_state(w_pad_queries_.p, w_qrot_.p, nq, dim_, D_, rc_.p, nbits_, w_qp_.p,
+                       w_qi8p_.p, w_qi8n_.p, w_lut_.p, stream_);
+    HANNS_CUDA_OK(cudaGetLastError());
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    if (probes)
+        HANNS_CUDA_OK(cudaMemcpy(probes, w_probes_.p, sizeof(int32_t) * nq * nprobe,
+                                 cudaMemcpyDeviceToHost));
+    if (q_rot)
+        HANNS_CUDA_OK(cudaMemcpy(q_rot, w_qrot_.p, sizeof(float) * nq * D_, cudaMemcpyDeviceToHost));
+    if (q_i8)
+        HANNS_CUDA_OK(cudaMemcpy(q_i8, w_qi8n_.p, (size_t)nq * D_, cudaMemcpyDeviceToHost));
+    if (lut) {
+        std::vector<uint8_t> u((size_t)nq * G * 16);
+        HANNS_CUDA_OK(cudaMemcpy(u.data(), w_lut_.p, u.size(), cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < u.size(); ++i) lut[i] = (int8_t)((int)u[i] - 128);
+    }
+    if (scalars) {
+        std::vector<QueryParams> qp(nq);
+        HANNS_CUDA_OK(cudaMemcpy(qp.data(), w_qp_.p, sizeof(QueryParams) * nq, cudaMemcpyDeviceToHost));
+        for (int64_t i = 0; i < nq; ++i) {
+            scalars[i * 5 + 0] = qp[i].q_scale;
+            scalars[i * 5 + 1] = qp[i].centroid_score;
+            scalars[i * 5 + 2] = qp[i].q_norm_sq;
+            scalars[i * 5 + 3] = qp[i].lut_scale;
+            std::memcpy(&scalars[i * 5 + 4], &qp[i].q_i8_sum, 4);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- persistence
+namespace {
+const char kMagic[8] = {'H', 'G', 'P', 'U', 'U', 'S', 'Q', '1'};
+}
+
+void IvfUsqGpu::save(const std::string& path) const {
+    DeviceGuard g(device_);
+    std::ofstream f(path, std::ios::binary);
+    if (!f) throw std::runtime_error("cannot open " + path);
+    const int64_t hdr[10] = {dim_, nbits_, nlist_, metric_, nprobe_, (int64_t)rotation_seed_,
+                             ntotal_, trained_ ? 1 : 0, D_, 0};
+    f.write(kMagic, 8);
+    f.write(reinterpret_cast<const char*>(hdr), sizeof(hdr));
+    auto put = [&](const void* dptr, size_t bytes) {
+        std::vector<char> h(bytes);
+        if (bytes) HANNS_CUDA_OK(cudaMemcpy(h.data(), dptr, bytes, cudaMemcpyDeviceToHost));
+        f.write(h.data(), (std::streamsize)bytes);
+    };
+    const size_t n = (size_t)ntotal_;
+    put(centroids_.p, trained_ ? sizeof(float) * nlist_ * dim_ : 0);
+    put(P_.p, trained_ ? sizeof(float) * D_ * D_ : 0);
+    put(rc_.p, trained_ ? sizeof(float) * D_ : 0);
+    put(gmean_.p, trained_ ? sizeof(float) * dim_ : 0);
+    f.write(reinterpret_cast<const char*>(h_list_off_.data()), sizeof(int64_t) * (nlist_ + 1));
+    put(ids_.p, sizeof(int64_t) * n);
+    put(meta_.p, sizeof(float4) * n);
+    put(codes_.p, n * code_bytes_);
+    put(signs_.p, n * (D_ / 8));
+    if (!f) throw std::runtime_error("write failed: " + path);
+}
+
+void IvfUsqGpu::load(const std::string& path) {
+    DeviceGuard g(device_);
+    std::ifstream f(path, std::ios::binary);
+    if (!f) throw std::runtime_error("cannot open " + path);
+    char magic[8];
+    int64_t hdr[10];
+    f.read(magic, 8);
+    f.read(reinterpret_cast<char*>(hdr), sizeof(hdr));
+    if (!f || std::memcmp(magic, kMagic, 8) != 0) throw std::runtime_error("not an HGPUUSQ1 file");
+    if (hdr[0] != dim_ || hdr[1] != nbits_ || hdr[2] != nlist_)
+        throw std::invalid_argument("saved index shape does not match the handle");
+    metric_ = (int)hdr[3];
+    nprobe_ = (int)hdr[4];
+    rotation_seed_ = (uint64_t)hdr[5];
+    ntotal_ = hdr[6];
+    trained_ = hdr[7] != 0;
+    auto get = [&](auto& buf, size_t count) {
+        using T = typename std::remove_reference<decltype(*buf.p)>::type;
+        std::vector<T> h(count);
+        f.read(reinterpret_cast<char*>(h.data()), (std::streamsize)(sizeof(T) * count));
+        if (!f) throw std::runtime_error("truncated file: " + path);
+        h2d(buf, h.data(), count, stream_);
+        HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    };
+    const size_t n = (size_t)ntotal_;
+    if (trained_) {
+        get(centroids_, (size_t)nlist_ * dim_);
+        get(P_, (size_t)D_ * D_);
+        get(rc_, (size_t)D_);
+        get(gmean_, (size_t)dim_);
+    }
+    std::vector<int64_t> off(nlist_ + 1);
+    f.read(reinterpret_cast<char*>(off.data()), sizeof(int64_t) * (nlist_ + 1));
+    get(ids_, n);
+    get(meta_, n);
+    get(codes_, n * code_bytes_);
+    get(signs_, n * (D_ / 8));
+    set_list_layout(off);
+    rebuild_fastscan();
+}
+
+}  // namespace hanns

@@ -1,0 +1,161 @@
+// ivf_usq_gpu.h -- host-side IVF-USQ index living on one B200.
+//
+// Mirrors IvfUsqIndex (reference src/faiss/ivf_usq.rs:118-127, 170-352): config,
+// train (k-means + global mean), add (assign + USQ encode + per-list layout), search.
+// The search path runs entirely on the GPU; there is no CPU fallback.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+
+namespace hanns {
+
+struct QueryParams;
+
+// Grow-only device buffer.
+template <class T>
+struct DevBuf {
+    T* p = nullptr;
+    size_t n = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    ~DevBuf() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    void reserve(size_t count) {
+        if (count <= n && p) return;
+        release();
+        if (count == 0) count = 1;
+        cudaError_t e = cudaMalloc(&p, count * sizeof(T));
+        if (e != cudaSuccess) {
+            p = nullptr;
+            throw CudaError(e, "cudaMalloc", __FILE__, __LINE__);
+        }
+        n = count;
+    }
+    void swap(DevBuf& o) {
+        std::swap(p, o.p);
+        std::swap(n, o.n);
+    }
+};
+
+struct SearchOptions {
+    int k = 10;
+    int nprobe = 8;
+    int filter_mode = 0;  // 0 none, 1 post (reference), 2 fused
+    const uint64_t* d_bitsets = nullptr;  // device
+    int64_t bitset_len = 0;
+    int64_t n_bitsets = 0;
+    const int32_t* d_query_bitset = nullptr;  // device or null
+    bool shard_output = false;                // emit merge keys (multi-GPU)
+};
+
+class IvfUsqGpu {
+   public:
+    IvfUsqGpu(int dim, int nlist, int nbits, int metric, uint64_t rotation_seed, int nprobe,
+              int device);
+    ~IvfUsqGpu();
+
+    // Frozen-artifact import / export (list order).
+    void import_artifact(const void* artifact /* hanns_ivf_usq_artifact_t* */);
+    void export_artifact(void* artifact /* hanns_ivf_usq_artifact_t* (destinations) */) const;
+
+    void train(const float* h_data, int64_t n, int kmeans_iters, uint64_t kmeans_seed);
+    void add(const float* h_data, int64_t n, const int64_t* h_ids);
+
+    // All pointers device; synchronises the stream before returning.
+    void search_device(const float* d_queries, int64_t nq, const SearchOptions& opt, int64_t* d_ids,
+                       float* d_dists, int64_t* d_counts, uint64_t* d_keys, cudaStream_t stream);
+    // Host pointers (copies in and out).
+    void search_host(const float* h_queries, int64_t nq, const SearchOptions& opt,
+                     const uint64_t* h_bitsets, const int32_t* h_query_bitset, int64_t* h_ids,
+                     float* h_dists, int64_t* h_counts);
+
+    void debug_query(const float* h_queries, int64_t nq, int nprobe, int32_t* probes, float* q_rot,
+                     int8_t* q_i8, int8_t* lut, float* scalars);
+
+    void shard(int rank, int world);
+    void save(const std::string& path) const;
+    void load(const std::string& path);
+
+    int dim() const { return dim_; }
+    int padded_dim() const { return D_; }
+    int nbits() const { return nbits_; }
+    int nlist() const { return nlist_; }
+    int metric() const { return metric_; }
+    int nprobe() const { return nprobe_; }
+    void set_nprobe(int p) { nprobe_ = p < 1 ? 1 : (p > nlist_ ? nlist_ : p); }
+    bool trained() const { return trained_; }
+    int64_t count() const { return ntotal_; }
+    int64_t size_bytes() const;
+    int device() const { return device_; }
+    const float* stage_ms() const { return stage_ms_; }
+    int64_t last_launches() const { return last_launches_; }
+    std::mutex& mutex() { return mu_; }
+
+   private:
+    void check_supported() const;
+    void upload_rotation_centroid();
+    void rebuild_fastscan();
+    void ensure_stream();
+    void search_batch(const float* d_q, int64_t nb, const SearchOptions& opt, int64_t* d_ids,
+                      float* d_dists, int64_t* d_counts, uint64_t* d_keys, cudaStream_t s,
+                      bool time_it);
+    void set_list_layout(const std::vector<int64_t>& h_off);
+
+    int dim_, D_, nbits_, nlist_, metric_, nprobe_, device_;
+    uint64_t rotation_seed_;
+    bool trained_ = false;
+    int64_t ntotal_ = 0;
+    int code_bytes_;
+
+    // device artifact (list order)
+    DevBuf<float> centroids_, P_, rc_, gmean_;
+    DevBuf<int64_t> list_off_, fs_blk_off_, ids_;
+    DevBuf<float4> meta_;
+    DevBuf<uint8_t> codes_, signs_, owned_;
+    DevBuf<uint2> fs_;
+    std::vector<int64_t> h_list_off_;
+    int max_list_ = 0;
+    bool sharded_ = false;
+
+    // search workspace
+    DevBuf<float> w_dist_, w_qrot_, w_pad_queries_;
+    DevBuf<uint32_t> w_sel_, w_slot_key_, w_mkey_;
+    DevBuf<int32_t> w_probes_;
+    DevBuf<QueryParams> w_qp_;
+    DevBuf<uint8_t> w_qi8p_, w_lut_;
+    DevBuf<int8_t> w_qi8n_;
+    DevBuf<int> w_cnt_, w_cursor_, w_lq_off_, w_item_off_, w_counters_, w_slot_cnt_;
+    DevBuf<int2> w_lq_;
+    DevBuf<int4> w_items_;
+    DevBuf<uint64_t> w_slot_tie_, w_mtie_, w_cand_tie_, w_bits_;
+    DevBuf<int16_t> w_scores_;
+    DevBuf<uint32_t> w_cand_key_;
+    DevBuf<int32_t> w_qbits_;
+    DevBuf<int64_t> w_out_ids_, w_out_counts_;
+    DevBuf<float> w_out_dists_;
+
+    cudaStream_t stream_ = nullptr;
+    cudaEvent_t ev_[6] = {};
+    float stage_ms_[6] = {0, 0, 0, 0, 0, 0};
+    int64_t last_launches_ = 0;
+    int scan_grid_ = 0;
+    std::mutex mu_;
+};
+
+// Seeded uniform [-1,1) matrix -> Householder QR -> Q (row-major, f32), the method of
+// src/quantization/usq/rotator.rs:15-39 with this library's own random stream.
+void rotation_matrix(uint64_t seed, int D, float* out);
+
+}  // namespace hanns

@@ -1,0 +1,118 @@
+// kernels.h -- kernel argument blocks and launch wrappers shared by the host code.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace hanns {
+
+struct QueryParams;
+
+struct CudaError : std::runtime_error {
+    cudaError_t code;
+    CudaError(cudaError_t c, const char* expr, const char* file, int line)
+        : std::runtime_error(std::string(cudaGetErrorString(c)) + " in " + expr + " at " + file +
+                             ":" + std::to_string(line)),
+          code(c) {}
+};
+
+struct ScanArgs {
+    // index (device)
+    int D, nbits, code_bytes, nchunks, G, metric_l2;
+    const int64_t* list_off;
+    const int64_t* fs_blk_off;
+    const uint2* fs;        // FastScan sign codes: [block][D/64][32 slots] x 8 bytes
+    const uint8_t* codes;   // [ntotal][code_bytes]
+    const float4* meta;     // [ntotal] {norm, norm_sq, vmax, quant_quality}
+    const int64_t* ids;     // [ntotal]
+    // queries
+    const QueryParams* qp;
+    const uint8_t* lut;     // [nq][G*16] offset-binary
+    const uint8_t* q_i8p;   // [nq][D] dp4a layout
+    // (list, query) grouping
+    const int2* lq;         // (query, probe rank) grouped by list
+    const int4* items;      // (list, first lq index, count, 0)
+    const int* n_items;
+    int* item_counter;
+    // selection
+    int k, n_cand, nprobe;
+    int fused;
+    const uint64_t* bitsets;
+    int64_t bitset_len, bitset_words, n_bitsets;
+    const int32_t* query_bitset;
+    // outputs: per (query, probe) slot
+    uint32_t* out_key;
+    uint64_t* out_tie;
+    int* out_cnt;
+    // scratch (per CTA / per warp)
+    int16_t* scores;
+    uint32_t* cand_key;
+    uint64_t* cand_tie;
+    int max_len;
+};
+
+struct MergeArgs {
+    int64_t nq;
+    int nprobe, k, nlist;
+    const uint32_t* slot_key;
+    const uint64_t* slot_tie;
+    const int* slot_cnt;
+    const int32_t* probes;
+    const int64_t* list_off;
+    const int64_t* ids;
+    uint32_t* sel_key;  // [nq][k] scratch
+    uint64_t* sel_tie;  // [nq][k] scratch
+    int64_t* out_ids;
+    float* out_dists;
+    int64_t* out_counts;
+    // post filter (reference semantics) -- NULL when unused
+    const uint64_t* post_bitsets;
+    int64_t bitset_len, bitset_words, n_bitsets;
+    const int32_t* query_bitset;
+    // shard mode: also emit merge keys
+    int shard_mode;
+    uint64_t* out_keys;
+};
+
+// search stages
+void launch_coarse_l2(const float* q, int64_t nq, const float* cent, int nlist, int d, float* dist,
+                      cudaStream_t s);
+void launch_select_probes(const float* dist, int64_t nq, int nlist, int nprobe, int32_t* probes,
+                          uint32_t* scratch, cudaStream_t s);
+void launch_rotate(const float* x, int64_t nq, int d, int D, const float* P, float* out,
+                   cudaStream_t s);
+void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, int D,
+                        const float* rc, int nbits, QueryParams* qp, uint8_t* q_i8p,
+                        int8_t* q_i8n, uint8_t* lut, cudaStream_t s);
+void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist,
+                        const uint8_t* owned, int qpi, int* cnt, int* cursor, int* lq_off,
+                        int* item_off, int* n_items, int2* lq, int4* items, cudaStream_t s);
+size_t scan_smem_bytes(int D);
+int scan_grid_size();
+void launch_scan(const ScanArgs& a, int grid, cudaStream_t s);
+void launch_merge(const MergeArgs& a, cudaStream_t s);
+void launch_merge_shards(const float* dists, const uint64_t* keys, const int64_t* ids, int world,
+                         int64_t nq, int k, int64_t* out_ids, float* out_dists, cudaStream_t s);
+
+// build stages
+void launch_global_mean(const float* x, int64_t n, int d, float* out, cudaStream_t s);
+void launch_row_norm_sq(const float* x, int64_t n, int d, float* out, cudaStream_t s);
+void launch_residual_pad(const float* x, int64_t n, int d, int D, const float* centroid, float* out,
+                         cudaStream_t s);
+void launch_encode_rotated(const float* rotated, int64_t n, int D, int nbits,
+                           const float* norm_sq_raw, uint8_t* codes, uint8_t* signs, float4* meta,
+                           cudaStream_t s);
+void launch_argmin_rows(const float* dist, int64_t n, int nlist, int32_t* out, cudaStream_t s);
+void launch_kmeans_accumulate(const float* x, int64_t n, int d, const int32_t* assign,
+                              long long* sums, int* counts, cudaStream_t s);
+void launch_kmeans_update(const long long* sums, const int* counts, int nlist, int d,
+                          float* centroids, cudaStream_t s);
+void launch_build_fastscan(const uint8_t* signs, const int64_t* list_off, const int64_t* blk_off,
+                           int nlist, int D, uint2* fs, cudaStream_t s);
+void launch_gather_rows(const uint8_t* src, const int64_t* perm, int64_t n, int64_t row_bytes,
+                        uint8_t* dst, cudaStream_t s);
+
+}  // namespace hanns

@@ -1,0 +1,1013 @@
+// search_kernels.cu -- batched IVF-USQ search on sm_100a.
+//
+// Pipeline for a batch of nq queries (all device-resident):
+//   coarse_l2_kernel      exact sequential L2 of every (query, IVF centroid) pair
+//                         (src/faiss/ivf_usq.rs:596-609,627-635)
+//   select_probes_kernel  per query the nprobe smallest by (distance, list id),
+//                         i.e. the reference's stable sort
+//   rotate_kernel         q_rot = P * pad(q) in the AVX-512 order of
+//                         src/quantization/usq/rotator.rs:93-120
+//   query_state_kernel    q_sum, q_scale, q_i8, sum(q_i8), centroid_score, ||q||^2 and the
+//                         FastScan LUT (quantizer.rs:236-270, fastscan.rs:22-66)
+//   count/scan/scatter    group the (query, probe) pairs by list so that every list's codes
+//                         are read once per batch and shared by all queries that probe it
+//   scan_lists_kernel     per (list, query): FastScan scores (i16-wrapped sums of
+//                         fastscan.rs:170-227), the exact fastscan_topk kept set
+//                         (fastscan.rs:86-146), integer rerank (quantizer.rs:274-400) and
+//                         the per-(query, probe) top-k
+//   merge_kernel          per query top-k over its probes by (distance, probe rank,
+//                         FastScan order, list position): the reference's stable sort of
+//                         src/faiss/ivf_usq.rs:590-593, padded with (-1, +inf)
+#include <algorithm>
+#include <cstdio>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace hanns {
+
+// ============================================================================
+// Warp-level helpers
+// ============================================================================
+
+__device__ __forceinline__ unsigned lanemask_le() {
+    unsigned m;
+    asm("mov.u32 %0, %%lanemask_le;" : "=r"(m));
+    return m;
+}
+__device__ __forceinline__ unsigned lanemask_lt() {
+    unsigned m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+__device__ __forceinline__ int warp_inclusive_scan(int v) {
+    const int lane = (int)lane_id();
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    return v;
+}
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Finds the `kth` smallest key (1-based) among the valid keys produced by
+// key_at(i) for i in [0, n), looking only at the low `bits` bits (multiple of 8).
+// Returns the key; *n_less = number of valid keys strictly smaller.
+// hist: 256 words of shared memory owned by this warp.
+template <class KeyAt>
+__device__ uint32_t warp_radix_kth(int n, int kth, int bits, KeyAt key_at, uint32_t* hist,
+                                   int* n_less) {
+    const int lane = (int)lane_id();
+    uint32_t prefix = 0, pmask = 0;
+    int remaining = kth, less = 0;
+    for (int shift = bits - 8; shift >= 0; shift -= 8) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) hist[lane * 8 + b] = 0;
+        __syncwarp();
+        for (int i = lane; i < n; i += 32) {
+            uint32_t key;
+            if (key_at(i, key) && (key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        int s = 0;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) s += (int)hist[lane * 8 + b];
+        const int incl = warp_inclusive_scan(s);
+        const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
+        const int src = __ffs(hit) - 1;  // hit != 0 because remaining <= total
+        int bin = 0, before = 0;
+        if (lane == src) {
+            int c = incl - s;
+            for (int b = 0; b < 8; ++b) {
+                const int h = (int)hist[lane * 8 + b];
+                if (c + h >= remaining) {
+                    bin = lane * 8 + b;
+                    break;
+                }
+                c += h;
+            }
+            before = c;
+        }
+        bin = __shfl_sync(0xffffffffu, bin, src);
+        before = __shfl_sync(0xffffffffu, before, src);
+        less += before;
+        remaining -= before;
+        prefix |= (uint32_t)bin << shift;
+        pmask |= 255u << shift;
+        __syncwarp();
+    }
+    *n_less = less;
+    return prefix;
+}
+
+__device__ __forceinline__ bool bit_filtered(const uint64_t* words, int64_t len, int64_t id) {
+    // Kept iff (id as usize) >= len || bit == 0 (src/faiss/ivf_usq.rs:708-710).
+    const uint64_t u = (uint64_t)id;
+    if (u >= (uint64_t)len) return false;
+    return (words[u >> 6] >> (u & 63)) & 1ull;
+}
+
+// ============================================================================
+// Coarse: exact L2 (sequential over dims, unfused) for a 64x64 tile per CTA.
+// ============================================================================
+constexpr int kCT = 64;  // tile edge
+constexpr int kCK = 16;  // dims per smem stage
+
+__global__ void __launch_bounds__(256) coarse_l2_kernel(const float* __restrict__ q, int64_t nq,
+                                                        const float* __restrict__ cent, int nlist,
+                                                        int d, float* __restrict__ dist) {
+    __shared__ float qs[kCK][kCT + 4];
+    __shared__ float cs[kCK][kCT + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int64_t q0 = (int64_t)blockIdx.y * kCT;
+    const int c0 = blockIdx.x * kCT;
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = -0.0f;
+    for (int k0 = 0; k0 < d; k0 += kCK) {
+        for (int e = threadIdx.x; e < kCT * kCK; e += 256) {
+            const int row = e / kCK, kk = e % kCK;
+            const int dim = k0 + kk;
+            const int64_t qr = q0 + row;
+            const int cr = c0 + row;
+            qs[kk][row] = (qr < nq && dim < d) ? q[qr * d + dim] : 0.0f;
+            cs[kk][row] = (cr < nlist && dim < d) ? cent[(int64_t)cr * d + dim] : 0.0f;
+        }
+        __syncthreads();
+        const int kmax = min(kCK, d - k0);
+        for (int kk = 0; kk < kmax; ++kk) {
+            float qv[4], cv[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) qv[a] = qs[kk][ty * 4 + a];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) cv[b] = cs[kk][tx * 4 + b];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const float df = __fsub_rn(qv[a], cv[b]);
+                    acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(df, df));
+                }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int64_t qr = q0 + ty * 4 + a;
+        if (qr >= nq) continue;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int cr = c0 + tx * 4 + b;
+            if (cr < nlist) dist[qr * nlist + cr] = acc[a][b];
+        }
+    }
+}
+
+// Per query (one warp): the nprobe smallest (distance, list) pairs, in order.
+__global__ void __launch_bounds__(128) select_probes_kernel(const float* __restrict__ dist,
+                                                            int64_t nq, int nlist, int nprobe,
+                                                            int32_t* __restrict__ probes,
+                                                            uint32_t* __restrict__ sel_scratch) {
+    __shared__ uint32_t hist[4][256];
+    const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    const int64_t qi = (int64_t)blockIdx.x * 4 + w;
+    if (qi >= nq) return;
+    const float* row = dist + qi * nlist;
+    auto key_at = [&](int i, uint32_t& k) {
+        k = total_order_key(row[i]);
+        return true;
+    };
+    int less = 0;
+    const uint32_t tau = warp_radix_kth(nlist, nprobe, 32, key_at, hist[w], &less);
+    // Gather the selected (key, idx): all keys < tau, then the lowest-index ties.
+    uint32_t* sk = sel_scratch + qi * 2 * (int64_t)nprobe;
+    uint32_t* si = sk + nprobe;
+    int cnt = 0, ties_needed = nprobe - less;
+    for (int base = 0; base < nlist; base += 32) {
+        const int i = base + lane;
+        uint32_t k = 0xFFFFFFFFu;
+        if (i < nlist) k = total_order_key(row[i]);
+        const bool lt = i < nlist && k < tau;
+        const bool eq = i < nlist && k == tau;
+        const unsigned beq = __ballot_sync(0xffffffffu, eq);
+        const int eq_rank = __popc(beq & lanemask_lt());
+        const bool take = lt || (eq && eq_rank < ties_needed);
+        const unsigned bt = __ballot_sync(0xffffffffu, take);
+        if (take) {
+            const int pos = cnt + __popc(bt & lanemask_lt());
+            sk[pos] = k;
+            si[pos] = (uint32_t)i;
+        }
+        cnt += __popc(bt);
+        ties_needed -= min(__popc(beq), max(ties_needed, 0));
+    }
+    __syncwarp();
+    // rank sort by (key, idx)
+    for (int a = lane; a < nprobe; a += 32) {
+        const uint32_t ka = sk[a], ia = si[a];
+        int rank = 0;
+        for (int b = 0; b < nprobe; ++b) {
+            const uint32_t kb = sk[b], ib = si[b];
+            rank += (kb < ka || (kb == ka && ib < ia)) ? 1 : 0;
+        }
+        probes[qi * nprobe + rank] = (int32_t)ia;
+    }
+}
+
+// ============================================================================
+// Query preparation
+// ============================================================================
+constexpr int kRotQ = 8;      // queries per CTA
+constexpr int kRotRows = 64;  // rows per CTA
+
+// q_rot[q][r] = tree16( lane j: fma chain over c = j, j+16, ... of P[r][c]*x[c] ).
+__global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x, int64_t nq,
+                                                     int d, int D, const float* __restrict__ P,
+                                                     float* __restrict__ out) {
+    extern __shared__ float xs[];  // [kRotQ][D]
+    const int64_t q0 = (int64_t)blockIdx.y * kRotQ;
+    for (int e = threadIdx.x; e < kRotQ * D; e += blockDim.x) {
+        const int t = e / D, c = e % D;
+        const int64_t qq = q0 + t;
+        xs[e] = (qq < nq && c < d) ? x[qq * d + c] : 0.0f;
+    }
+    __syncthreads();
+    const int half = threadIdx.x >> 4, j = threadIdx.x & 15;
+    const unsigned hmask = 0xFFFFu << (threadIdx.x & 16);
+    for (int rr = half; rr < kRotRows; rr += 16) {
+        const int r = blockIdx.x * kRotRows + rr;
+        if (r >= D) break;  // uniform across the half-warp
+        const float* prow = P + (int64_t)r * D;
+        float acc[kRotQ];
+#pragma unroll
+        for (int t = 0; t < kRotQ; ++t) acc[t] = 0.0f;
+        for (int c = j; c < D; c += 16) {
+            const float p = __ldg(prow + c);
+#pragma unroll
+            for (int t = 0; t < kRotQ; ++t) acc[t] = __fmaf_rn(p, xs[t * D + c], acc[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < kRotQ; ++t) {
+            float v = acc[t];
+            v = __fadd_rn(v, __shfl_down_sync(hmask, v, 8, 16));
+            v = __fadd_rn(v, __shfl_down_sync(hmask, v, 4, 16));
+            v = __fadd_rn(v, __shfl_down_sync(hmask, v, 2, 16));
+            v = __fadd_rn(v, __shfl_down_sync(hmask, v, 1, 16));
+            acc[t] = v;
+        }
+        if (j == 0) {
+#pragma unroll
+            for (int t = 0; t < kRotQ; ++t)
+                if (q0 + t < nq) out[(q0 + t) * D + r] = acc[t];
+        }
+    }
+}
+
+__device__ __forceinline__ float lut_entry(const float* q4, int nib) {
+    float v = 0.0f;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) v = __fadd_rn(v, ((nib >> b) & 1) ? q4[b] : -q4[b]);
+    return v;
+}
+
+// One warp per query.
+__global__ void __launch_bounds__(128) query_state_kernel(
+    const float* __restrict__ x, const float* __restrict__ q_rot, int64_t nq, int d, int D,
+    const float* __restrict__ rc, int nbits, QueryParams* __restrict__ qp,
+    uint8_t* __restrict__ q_i8p, int8_t* __restrict__ q_i8n, uint8_t* __restrict__ lut) {
+    const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    const int64_t qi = (int64_t)blockIdx.x * 4 + w;
+    if (qi >= nq) return;
+    const float* r = q_rot + qi * D;
+    // sequential sums (Rust Sum<f32> starts from -0.0)
+    float cs = -0.0f, qn = -0.0f;
+    if (lane == 1)
+        for (int i = 0; i < D; ++i) cs = __fadd_rn(cs, __fmul_rn(r[i], rc[i]));
+    if (lane == 2) {
+        const float* xq = x + qi * d;
+        for (int i = 0; i < d; ++i) qn = __fadd_rn(qn, __fmul_rn(xq[i], xq[i]));
+    }
+    cs = __shfl_sync(0xffffffffu, cs, 1);
+    qn = __shfl_sync(0xffffffffu, qn, 2);
+    float m = 0.0f;
+    for (int i = lane; i < D; i += 32) m = fmaxf(m, fabsf(r[i]));
+    m = fmaxf(warp_max(m), 1e-6f);
+    const float q_scale = __fdiv_rn(m, 127.0f);
+    int s = 0;
+    for (int i = lane; i < D; i += 32) {
+        const int v = round_clamp(__fdiv_rn(r[i], q_scale), -127.0f, 127.0f);
+        s += v;
+        q_i8n[qi * D + i] = (int8_t)v;
+        // dp4a layout: 4-bit codes unpack to (even dims, odd dims) per 8 dims.
+        int pos = i;
+        if (nbits == 4) {
+            const int g8 = i >> 3, o = i & 7;
+            pos = g8 * 8 + ((o & 1) ? 4 : 0) + (o >> 1);
+        }
+        q_i8p[qi * D + pos] = (uint8_t)(int8_t)v;
+    }
+    s = warp_sum(s);
+    // FastScan LUT
+    const int G = D / 4;
+    float lm = 0.0f;
+    for (int g = lane; g < G; g += 32) {
+        const float* q4 = r + 4 * g;
+        for (int nib = 0; nib < 16; ++nib) lm = fmaxf(lm, fabsf(lut_entry(q4, nib)));
+    }
+    lm = fmaxf(warp_max(lm), 1e-6f);
+    const float lut_scale = fmaxf(__fdiv_rn(lm, 127.0f), 1e-6f);
+    for (int g = lane; g < G; g += 32) {
+        const float* q4 = r + 4 * g;
+        for (int nib = 0; nib < 16; ++nib) {
+            const int v = round_clamp(__fdiv_rn(lut_entry(q4, nib), lut_scale), -127.0f, 127.0f);
+            lut[qi * (int64_t)G * 16 + g * 16 + nib] = (uint8_t)(v + 128);  // offset binary
+        }
+    }
+    if (lane == 0) {
+        QueryParams p;
+        p.q_scale = q_scale;
+        p.centroid_score = cs;
+        p.q_norm_sq = qn;
+        p.lut_scale = lut_scale;
+        p.q_i8_sum = s;
+        p.pad[0] = p.pad[1] = p.pad[2] = 0;
+        qp[qi] = p;
+    }
+}
+
+// ============================================================================
+// Group (query, probe) pairs by list
+// ============================================================================
+__global__ void count_lists_kernel(const int32_t* __restrict__ probes, int64_t n_pairs, int nlist,
+                                   const uint8_t* __restrict__ owned, int* __restrict__ cnt) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_pairs;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int l = probes[i];
+        if (l < 0 || l >= nlist) continue;
+        if (!owned || owned[l]) atomicAdd(&cnt[l], 1);
+    }
+}
+
+// Single CTA of 1024 threads: exclusive scans of cnt and of items-per-list.
+__global__ void __launch_bounds__(1024) prefix_lists_kernel(const int* __restrict__ cnt, int nlist,
+                                                          int qpi, int* __restrict__ lq_off,
+                                                          int* __restrict__ item_off,
+                                                          int* __restrict__ n_items) {
+    __shared__ int wsum_a[32], wsum_b[32];
+    __shared__ int carry_a, carry_b;
+    const int lane = (int)lane_id(), w = threadIdx.x >> 5;
+    if (threadIdx.x == 0) carry_a = carry_b = 0;
+    __syncthreads();
+    for (int base = 0; base < nlist; base += 1024) {
+        const int l = base + threadIdx.x;
+        const int a = l < nlist ? cnt[l] : 0;
+        const int b = (a + qpi - 1) / qpi;
+        const int ia = warp_inclusive_scan(a), ib = warp_inclusive_scan(b);
+        if (lane == 31) {
+            wsum_a[w] = ia;
+            wsum_b[w] = ib;
+        }
+        __syncthreads();
+        if (w == 0) {
+            const int xa = warp_inclusive_scan(wsum_a[lane]);
+            const int xb = warp_inclusive_scan(wsum_b[lane]);
+            wsum_a[lane] = xa;
+            wsum_b[lane] = xb;
+        }
+        __syncthreads();
+        const int pa = (w ? wsum_a[w - 1] : 0) + ia - a + carry_a;
+        const int pb = (w ? wsum_b[w - 1] : 0) + ib - b + carry_b;
+        if (l < nlist) {
+            lq_off[l] = pa;
+            item_off[l] = pb;
+        }
+        __syncthreads();
+        if (threadIdx.x == 1023) {
+            carry_a = pa + a;
+            carry_b = pb + b;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        lq_off[nlist] = carry_a;
+        item_off[nlist] = carry_b;
+        *n_items = carry_b;
+    }
+}
+
+__global__ void scatter_pairs_kernel(const int32_t* __restrict__ probes, int64_t nq, int nprobe,
+                                     int nlist, const uint8_t* __restrict__ owned,
+                                     const int* __restrict__ lq_off, int* __restrict__ cursor,
+                                     int2* __restrict__ lq) {
+    const int64_t n_pairs = nq * nprobe;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_pairs;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int l = probes[i];
+        if (l < 0 || l >= nlist) continue;
+        if (owned && !owned[l]) continue;
+        const int pos = lq_off[l] + atomicAdd(&cursor[l], 1);
+        lq[pos] = make_int2((int)(i / nprobe), (int)(i % nprobe));
+    }
+}
+
+__global__ void make_items_kernel(const int* __restrict__ cnt, const int* __restrict__ lq_off,
+                                  const int* __restrict__ item_off, int nlist, int qpi,
+                                  int4* __restrict__ items) {
+    for (int l = blockIdx.x * blockDim.x + threadIdx.x; l < nlist; l += gridDim.x * blockDim.x) {
+        const int c = cnt[l];
+        int o = item_off[l];
+        for (int s = 0; s < c; s += qpi) items[o++] = make_int4(l, lq_off[l] + s, min(qpi, c - s), 0);
+    }
+}
+
+// ============================================================================
+// List scan: FastScan + exact kept set + integer rerank + per-(query, probe) top-k
+// ============================================================================
+constexpr int kScanThreads = 256;
+constexpr int kScanWarps = kScanThreads / 32;  // queries handled concurrently
+
+struct ScanSmem {
+    uint32_t hist[kScanWarps][256];
+    int item;
+    int pad[3];  // keeps the dynamic arrays after it 16-byte aligned
+};
+
+__device__ __forceinline__ int32_t wrap16(int32_t v) { return (int32_t)(int16_t)v; }
+
+// Integer dot of one stored vector with the warp's quantised query (shared memory).
+__device__ __forceinline__ int int_ip_row(const uint8_t* __restrict__ code, const uint8_t* qs,
+                                          int D, int nbits) {
+    int acc = 0;
+    if (nbits == 8) {
+        const uint4* c4 = reinterpret_cast<const uint4*>(code);
+        const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+        for (int i = 0; i < D / 16; ++i) {
+            const uint4 c = __ldg(c4 + i);
+            const uint4 qv = q4[i];
+            acc = dp4a_us(c.x, qv.x, acc);
+            acc = dp4a_us(c.y, qv.y, acc);
+            acc = dp4a_us(c.z, qv.z, acc);
+            acc = dp4a_us(c.w, qv.w, acc);
+        }
+    } else {  // nbits == 4: 16 code bytes = 32 dims; q layout (even, odd) per 8 dims
+        const uint4* c4 = reinterpret_cast<const uint4*>(code);
+        const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+        for (int i = 0; i < D / 32; ++i) {
+            const uint4 c = __ldg(c4 + i);
+            const uint4 qa = q4[2 * i], qb = q4[2 * i + 1];
+            acc = dp4a_us(c.x & 0x0F0F0F0Fu, qa.x, acc);
+            acc = dp4a_us((c.x >> 4) & 0x0F0F0F0Fu, qa.y, acc);
+            acc = dp4a_us(c.y & 0x0F0F0F0Fu, qa.z, acc);
+            acc = dp4a_us((c.y >> 4) & 0x0F0F0F0Fu, qa.w, acc);
+            acc = dp4a_us(c.z & 0x0F0F0F0Fu, qb.x, acc);
+            acc = dp4a_us((c.z >> 4) & 0x0F0F0F0Fu, qb.y, acc);
+            acc = dp4a_us(c.w & 0x0F0F0F0Fu, qb.z, acc);
+            acc = dp4a_us((c.w >> 4) & 0x0F0F0F0Fu, qb.w, acc);
+        }
+    }
+    return acc;
+}
+
+// score_with_meta + distance, in the reference's operation order.
+__device__ __forceinline__ float rerank_distance(int iip, float4 m, const QueryParams& p, int nbits,
+                                                 bool l2) {
+    // m = {norm, norm_sq, vmax, quant_quality}
+    float score;
+    if (m.w <= 1e-12f) {
+        score = p.centroid_score;
+    } else {
+        const float levels = (float)(1u << nbits);
+        const float code_scale = __fdiv_rn(__fmul_rn(2.0f, m.z), fmaxf(levels, 1.0f));
+        const float offset = -m.z;
+        const float ip = __fmul_rn(
+            p.q_scale, __fadd_rn(__fmul_rn(code_scale, __int2float_rn(iip)),
+                                 __fmul_rn(offset, __int2float_rn(p.q_i8_sum))));
+        score = __fadd_rn(p.centroid_score, __fdiv_rn(__fmul_rn(m.x, ip), m.w));
+    }
+    return l2 ? __fsub_rn(__fadd_rn(p.q_norm_sq, m.y), __fmul_rn(2.0f, score)) : -score;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    ScanSmem& sm = *reinterpret_cast<ScanSmem*>(smem_raw);
+    uint32_t* lut4 = reinterpret_cast<uint32_t*>(smem_raw + sizeof(ScanSmem));  // [G*16]
+    uint8_t* qi8_s = reinterpret_cast<uint8_t*>(lut4 + a.G * 16);              // [warps][D]
+    const int tid = threadIdx.x, w = tid >> 5, lane = (int)lane_id();
+    const int64_t slot_base = (int64_t)blockIdx.x * kScanWarps + w;
+    int16_t* my_scores_base = a.scores + (int64_t)blockIdx.x * kScanWarps * a.max_len;
+    uint64_t* my_tie = a.cand_tie + slot_base * a.max_len;
+    uint32_t* my_key = a.cand_key + slot_base * a.max_len;
+    const bool l2 = a.metric_l2 != 0;
+
+    for (;;) {
+        if (tid == 0) sm.item = atomicAdd(a.item_counter, 1);
+        __syncthreads();
+        const int item = sm.item;
+        __syncthreads();
+        if (item >= *a.n_items) break;
+        const int4 it = a.items[item];
+        const int l = it.x;
+        const int64_t beg = a.list_off[l];
+        const int n = (int)(a.list_off[l + 1] - beg);
+        const bool use_fs = n > a.n_cand;
+        const uint2* fsb = a.fs + a.fs_blk_off[l] * (int64_t)a.nchunks * 32;
+
+        for (int qg = 0; qg < it.z; qg += kScanWarps) {
+            const int nq_here = min(kScanWarps, it.z - qg);
+            if (use_fs) {
+                for (int sub = 0; sub * 4 < nq_here; ++sub) {
+                    // interleave 4 queries' offset-binary LUTs: word g*16+nib = q0|q1<<8|q2<<16|q3<<24
+                    for (int e = tid; e < a.G * 16; e += kScanThreads) {
+                        uint32_t wv = 0;
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const int qq = qg + sub * 4 + t;
+                            uint32_t b = 128u;
+                            if (qq < it.z) {
+                                const int qidx = a.lq[it.y + qq].x;
+                                b = a.lut[(int64_t)qidx * a.G * 16 + e];
+                            }
+                            wv |= b << (8 * t);
+                        }
+                        lut4[e] = wv;
+                    }
+                    __syncthreads();
+                    for (int v = tid; v < n; v += kScanThreads) {
+                        const int blk = v >> 5, slot = v & 31;
+                        const uint2* src = fsb + (int64_t)blk * a.nchunks * 32 + slot;
+                        uint32_t acc02 = 0, acc13 = 0;
+                        int tot0 = 0, tot1 = 0, tot2 = 0, tot3 = 0;
+                        for (int c = 0; c < a.nchunks; ++c) {
+                            const uint2 wd = __ldg(src + c * 32);
+                            const uint32_t* lrow = lut4 + c * 256;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const uint32_t word = j < 8 ? wd.x : wd.y;
+                                const uint32_t nib = (word >> (4 * (j & 7))) & 15u;
+                                const uint32_t e = lrow[j * 16 + nib];
+                                acc02 += e & 0x00FF00FFu;
+                                acc13 += (e >> 8) & 0x00FF00FFu;
+                            }
+                            if ((c & 15) == 15) {
+                                tot0 += (int)(acc02 & 0xFFFFu);
+                                tot2 += (int)(acc02 >> 16);
+                                tot1 += (int)(acc13 & 0xFFFFu);
+                                tot3 += (int)(acc13 >> 16);
+                                acc02 = acc13 = 0;
+                            }
+                        }
+                        tot0 += (int)(acc02 & 0xFFFFu);
+                        tot2 += (int)(acc02 >> 16);
+                        tot1 += (int)(acc13 & 0xFFFFu);
+                        tot3 += (int)(acc13 >> 16);
+                        const int bias = 128 * a.G;
+                        int16_t* srow = my_scores_base + (int64_t)(sub * 4) * a.max_len;
+                        srow[v] = (int16_t)wrap16(tot0 - bias);
+                        srow[a.max_len + v] = (int16_t)wrap16(tot1 - bias);
+                        srow[2 * (int64_t)a.max_len + v] = (int16_t)wrap16(tot2 - bias);
+                        srow[3 * (int64_t)a.max_len + v] = (int16_t)wrap16(tot3 - bias);
+                    }
+                    __syncthreads();
+                }
+            }
+            if (w < nq_here) {
+                const int2 pr = a.lq[it.y + qg + w];
+                const int q = pr.x, rank = pr.y;
+                const QueryParams p = a.qp[q];
+                // stage the quantised query
+                uint8_t* qs = qi8_s + w * a.D;
+                for (int i = lane * 16; i < a.D; i += 32 * 16)
+                    *reinterpret_cast<uint4*>(qs + i) =
+                        *reinterpret_cast<const uint4*>(a.q_i8p + (int64_t)q * a.D + i);
+                const uint64_t* bw = nullptr;
+                if (a.fused && a.bitsets) {
+                    const int b = a.query_bitset ? a.query_bitset[q] : 0;
+                    if (b >= 0 && b < a.n_bitsets) bw = a.bitsets + (int64_t)b * a.bitset_words;
+                }
+                auto live = [&](int v) {
+                    return !bw || !bit_filtered(bw, a.bitset_len, a.ids[beg + v]);
+                };
+                int n_live = n;
+                if (bw) {
+                    int c = 0;
+                    for (int v = lane; v < n; v += 32) c += live(v) ? 1 : 0;
+                    n_live = warp_sum(c);
+                }
+                const int16_t* sc = my_scores_base + (int64_t)w * a.max_len;
+                int n_c = 0;  // candidates written to my_tie
+                if (use_fs && n_live > a.n_cand) {
+                    // s* = n_cand-th largest score among live rows (key = 32767 - score)
+                    auto key_at = [&](int v, uint32_t& k) {
+                        if (!live(v)) return false;
+                        k = (uint32_t)(32767 - (int)sc[v]);
+                        return true;
+                    };
+                    int c_gt = 0;
+                    const uint32_t tau = warp_radix_kth(n, a.n_cand, 16, key_at, sm.hist[w], &c_gt);
+                    // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
+                    int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = 0;
+                    for (int base = 0; base < n; base += 32) {
+                        const int v = base + lane;
+                        uint32_t k = 0xFFFFFFFFu;
+                        const bool valid = v < n && key_at(v, k);
+                        const bool ge = valid && k <= tau, gt = valid && k < tau;
+                        const unsigned bge = __ballot_sync(0xffffffffu, ge);
+                        const unsigned bgt = __ballot_sync(0xffffffffu, gt);
+                        const int c = __popc(bge);
+                        if (cnt_ge + c >= a.n_cand) {
+                            const int need = a.n_cand - cnt_ge;
+                            const bool here = ge && __popc(bge & lanemask_le()) == need;
+                            const int pos = __ffs(__ballot_sync(0xffffffffu, here)) - 1;
+                            p_end = base + pos;
+                            gt_f = cnt_gt + __popc(bgt & (pos == 31 ? 0xffffffffu : ((2u << pos) - 1u)));
+                            break;
+                        }
+                        cnt_ge += c;
+                        cnt_gt += __popc(bgt);
+                    }
+                    const int m_drop = c_gt - gt_f;  // lowest-index ties evicted by later rows
+                    int eq_seen = 0;
+                    for (int base = 0; base < n; base += 32) {
+                        const int v = base + lane;
+                        uint32_t k = 0xFFFFFFFFu;
+                        const bool valid = v < n && key_at(v, k);
+                        const bool gt = valid && k < tau;
+                        const bool eq = valid && k == tau && v <= p_end;
+                        const unsigned beq = __ballot_sync(0xffffffffu, eq);
+                        const int eq_rank = eq_seen + __popc(beq & lanemask_le());
+                        const bool keep = gt || (eq && eq_rank > m_drop);
+                        const unsigned bk = __ballot_sync(0xffffffffu, keep);
+                        if (keep) {
+                            const int pos = n_c + __popc(bk & lanemask_lt());
+                            my_tie[pos] = ((uint64_t)k << 32) | (uint32_t)v;
+                        }
+                        n_c += __popc(bk);
+                        eq_seen += __popc(beq);
+                    }
+                } else {
+                    for (int base = 0; base < n; base += 32) {
+                        const int v = base + lane;
+                        const bool keep = v < n && live(v);
+                        const unsigned bk = __ballot_sync(0xffffffffu, keep);
+                        if (keep) my_tie[n_c + __popc(bk & lanemask_lt())] = (uint32_t)v;
+                        n_c += __popc(bk);
+                    }
+                }
+                __syncwarp();
+                // integer rerank of the kept candidates
+                for (int i = lane; i < n_c; i += 32) {
+                    const uint32_t v = (uint32_t)my_tie[i];
+                    const int64_t row = beg + v;
+                    const float4 m = __ldg(a.meta + row);
+                    int iip = 0;
+                    if (m.w > 1e-12f) iip = int_ip_row(a.codes + row * a.code_bytes, qs, a.D, a.nbits);
+                    my_key[i] = total_order_key(rerank_distance(iip, m, p, a.nbits, l2));
+                }
+                __syncwarp();
+                // top-k of (dist, fastscan key, index) into the (query, probe) slot
+                const int64_t slot = (int64_t)q * a.nprobe + rank;
+                uint32_t* ok = a.out_key + slot * a.k;
+                uint64_t* ot = a.out_tie + slot * a.k;
+                if (n_c <= a.k) {
+                    for (int i = lane; i < n_c; i += 32) {
+                        ok[i] = my_key[i];
+                        ot[i] = my_tie[i];
+                    }
+                    if (lane == 0) a.out_cnt[slot] = n_c;
+                } else {
+                    auto kk = [&](int i, uint32_t& key) {
+                        key = my_key[i];
+                        return true;
+                    };
+                    int less = 0;
+                    const uint32_t tau = warp_radix_kth(n_c, a.k, 32, kk, sm.hist[w], &less);
+                    int written = 0;
+                    for (int base = 0; base < n_c; base += 32) {
+                        const int i = base + lane;
+                        const bool lt = i < n_c && my_key[i] < tau;
+                        const unsigned bl = __ballot_sync(0xffffffffu, lt);
+                        if (lt) {
+                            const int pos = written + __popc(bl & lanemask_lt());
+                            ok[pos] = my_key[i];
+                            ot[pos] = my_tie[i];
+                        }
+                        written += __popc(bl);
+                    }
+                    // ties at tau: chosen in increasing (fastscan key, index) order
+                    uint64_t floor_t = 0;
+                    bool have_floor = false;
+                    while (written < a.k) {
+                        uint64_t best = ~0ull;
+                        for (int i = lane; i < n_c; i += 32) {
+                            const uint64_t t = my_tie[i];
+                            if (my_key[i] == tau && (!have_floor || t > floor_t) && t < best) best = t;
+                        }
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+                            best = ob < best ? ob : best;
+                        }
+                        if (lane == 0) {
+                            ok[written] = tau;
+                            ot[written] = best;
+                        }
+                        floor_t = best;
+                        have_floor = true;
+                        ++written;
+                    }
+                    if (lane == 0) a.out_cnt[slot] = a.k;
+                }
+                __syncwarp();
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// ============================================================================
+// Final merge: per query (one warp) top-k over nprobe slots.
+// ============================================================================
+__global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
+    __shared__ uint32_t hist[4][256];
+    const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    const int64_t q = (int64_t)blockIdx.x * 4 + w;
+    if (q >= a.nq) return;
+    const int total = a.nprobe * a.k;
+    const uint32_t* keys = a.slot_key + q * total;
+    const uint64_t* ties = a.slot_tie + q * total;
+    const int* cnts = a.slot_cnt + q * a.nprobe;
+    auto valid_at = [&](int e) { return (e % a.k) < cnts[e / a.k]; };
+    auto key_at = [&](int e, uint32_t& k) {
+        if (!valid_at(e)) return false;
+        k = keys[e];
+        return true;
+    };
+    int n_valid = 0;
+    for (int r = lane; r < a.nprobe; r += 32) n_valid += cnts[r];
+    n_valid = warp_sum(n_valid);
+    const int take = min(a.k, n_valid);
+    uint32_t* sk = a.sel_key + q * a.k;
+    uint64_t* st = a.sel_tie + q * a.k;  // probe rank << 48 | fastscan key << 32 | index
+    int written = 0;
+    if (take > 0) {
+        int less = 0;
+        uint32_t tau = 0xFFFFFFFFu;
+        if (n_valid > a.k) tau = warp_radix_kth(total, a.k, 32, key_at, hist[w], &less);
+        for (int base = 0; base < total; base += 32) {
+            const int e = base + lane;
+            uint32_t k = 0;
+            const bool ok = e < total && key_at(e, k);
+            const bool lt = ok && (n_valid <= a.k || k < tau);
+            const unsigned bl = __ballot_sync(0xffffffffu, lt);
+            if (lt) {
+                const int pos = written + __popc(bl & lanemask_lt());
+                sk[pos] = k;
+                st[pos] = ((uint64_t)(e / a.k) << 48) | ties[e];
+            }
+            written += __popc(bl);
+        }
+        // ties at tau: chosen in increasing (probe rank, fastscan key, index) order
+        uint64_t floor_t = 0;
+        bool have_floor = false;
+        while (written < take) {
+            uint64_t best = ~0ull;
+            for (int e = lane; e < total; e += 32) {
+                uint32_t k;
+                if (key_at(e, k) && k == tau) {
+                    const uint64_t t = ((uint64_t)(e / a.k) << 48) | ties[e];
+                    if ((!have_floor || t > floor_t) && t < best) best = t;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+                best = ob < best ? ob : best;
+            }
+            if (lane == 0) {
+                sk[written] = tau;
+                st[written] = best;
+            }
+            floor_t = best;
+            have_floor = true;
+            ++written;
+        }
+    }
+    __syncwarp();
+    // sort the selected entries by (key, tie) and write the row
+    for (int i = lane; i < a.k; i += 32) {
+        if (i >= take) {
+            if (!a.shard_mode) {
+                a.out_ids[q * a.k + i] = -1;
+                a.out_dists[q * a.k + i] = __int_as_float(0x7f800000);
+            } else {
+                a.out_ids[q * a.k + i] = -1;
+                a.out_dists[q * a.k + i] = __int_as_float(0x7f800000);
+                a.out_keys[q * a.k + i] = ~0ull;
+            }
+            continue;
+        }
+        const uint32_t ki = sk[i];
+        const uint64_t ti = st[i];
+        int rank = 0;
+        for (int j = 0; j < take; ++j) {
+            const uint32_t kj = sk[j];
+            const uint64_t tj = st[j];
+            rank += (kj < ki || (kj == ki && tj < ti)) ? 1 : 0;
+        }
+        const int r = (int)(ti >> 48);
+        const uint32_t idx = (uint32_t)(ti & 0xFFFFFFFFull);
+        int64_t id = -1;
+        if (r < a.nprobe) {
+            const int l = a.probes[q * a.nprobe + r];
+            if (l >= 0 && l < a.nlist && idx < (uint32_t)(a.list_off[l + 1] - a.list_off[l]))
+                id = a.ids[a.list_off[l] + idx];
+        }
+        a.out_ids[q * a.k + rank] = id;
+        a.out_dists[q * a.k + rank] = key_to_float(ki);
+        if (a.shard_mode) a.out_keys[q * a.k + rank] = ti;
+    }
+    __syncwarp();
+    if (a.post_bitsets) {  // reference post-filter: drop filtered ids, keep order
+        const uint64_t* bw = nullptr;
+        const int b = a.query_bitset ? a.query_bitset[q] : 0;
+        if (b >= 0 && b < a.n_bitsets) bw = a.post_bitsets + (int64_t)b * a.bitset_words;
+        int n_out = 0;
+        for (int base = 0; base < a.k; base += 32) {
+            const int i = base + lane;
+            int64_t id = 0;
+            float dd = 0;
+            bool keep = false;
+            if (i < a.k) {
+                id = a.out_ids[q * a.k + i];
+                dd = a.out_dists[q * a.k + i];
+                keep = !bw || !bit_filtered(bw, a.bitset_len, id);
+            }
+            const unsigned bk = __ballot_sync(0xffffffffu, keep);
+            __syncwarp();
+            if (keep) {
+                const int pos = n_out + __popc(bk & lanemask_lt());
+                a.out_ids[q * a.k + pos] = id;
+                a.out_dists[q * a.k + pos] = dd;
+            }
+            n_out += __popc(bk);
+            __syncwarp();
+        }
+        for (int i = n_out + lane; i < a.k; i += 32) {
+            a.out_ids[q * a.k + i] = -1;
+            a.out_dists[q * a.k + i] = __int_as_float(0x7f800000);
+        }
+        if (lane == 0 && a.out_counts) a.out_counts[q] = n_out;
+    } else if (lane == 0 && a.out_counts) {
+        a.out_counts[q] = a.k;
+    }
+}
+
+}  // namespace hanns
+
+namespace hanns {
+
+// Cross-shard merge: per query (one warp) the k best of world sorted shard rows by
+// (distance, merge key).  Keys are unique per query, so the result equals the
+// single-GPU order.
+__global__ void __launch_bounds__(128) merge_shards_kernel(const float* __restrict__ dists,
+                                                           const uint64_t* __restrict__ keys,
+                                                           const int64_t* __restrict__ ids,
+                                                           int world, int64_t nq, int k,
+                                                           int64_t* __restrict__ out_ids,
+                                                           float* __restrict__ out_dists) {
+    const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    const int64_t q = (int64_t)blockIdx.x * 4 + w;
+    if (q >= nq) return;
+    // k-way merge by repeated warp argmin over the shard heads (world <= 32).
+    int head = 0;  // lane s < world owns shard s's cursor
+    for (int out = 0; out < k; ++out) {
+        uint32_t dk = 0xFFFFFFFFu;
+        uint64_t mk = ~0ull;
+        if (lane < world && head < k) {
+            const int64_t e = ((int64_t)lane * nq + q) * k + head;
+            if (keys[e] != ~0ull) {
+                dk = total_order_key(dists[e]);
+                mk = keys[e];
+            }
+        }
+        uint32_t bdk = dk;
+        uint64_t bmk = mk;
+        int bl = lane;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint32_t odk = __shfl_xor_sync(0xffffffffu, bdk, o);
+            const uint64_t omk = __shfl_xor_sync(0xffffffffu, bmk, o);
+            const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+            if (odk < bdk || (odk == bdk && (omk < bmk || (omk == bmk && ol < bl)))) {
+                bdk = odk;
+                bmk = omk;
+                bl = ol;
+            }
+        }
+        if (bmk == ~0ull) {
+            if (lane == 0) {
+                for (int j = out; j < k; ++j) {
+                    out_ids[q * k + j] = -1;
+                    out_dists[q * k + j] = __int_as_float(0x7f800000);
+                }
+            }
+            return;
+        }
+        if (lane == bl) {
+            const int64_t e = ((int64_t)lane * nq + q) * k + head;
+            out_ids[q * k + out] = ids[e];
+            out_dists[q * k + out] = dists[e];
+            ++head;
+        }
+    }
+}
+
+void launch_coarse_l2(const float* q, int64_t nq, const float* cent, int nlist, int d, float* dist,
+                      cudaStream_t s) {
+    if (nq <= 0) return;
+    dim3 grid((nlist + kCT - 1) / kCT, (unsigned)((nq + kCT - 1) / kCT));
+    coarse_l2_kernel<<<grid, 256, 0, s>>>(q, nq, cent, nlist, d, dist);
+}
+
+void launch_select_probes(const float* dist, int64_t nq, int nlist, int nprobe, int32_t* probes,
+                          uint32_t* scratch, cudaStream_t s) {
+    if (nq <= 0) return;
+    select_probes_kernel<<<(unsigned)((nq + 3) / 4), 128, 0, s>>>(dist, nq, nlist, nprobe, probes,
+                                                                  scratch);
+}
+
+void launch_rotate(const float* x, int64_t nq, int d, int D, const float* P, float* out,
+                   cudaStream_t s) {
+    if (nq <= 0) return;
+    const size_t smem = (size_t)kRotQ * D * sizeof(float);
+    cudaFuncSetAttribute(rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    dim3 grid((D + kRotRows - 1) / kRotRows, (unsigned)((nq + kRotQ - 1) / kRotQ));
+    rotate_kernel<<<grid, 256, smem, s>>>(x, nq, d, D, P, out);
+}
+
+void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, int D,
+                        const float* rc, int nbits, QueryParams* qp, uint8_t* q_i8p,
+                        int8_t* q_i8n, uint8_t* lut, cudaStream_t s) {
+    if (nq <= 0) return;
+    query_state_kernel<<<(unsigned)((nq + 3) / 4), 128, 0, s>>>(x, q_rot, nq, d, D, rc, nbits, qp,
+                                                                q_i8p, q_i8n, lut);
+}
+
+void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist,
+                        const uint8_t* owned, int qpi, int* cnt, int* cursor, int* lq_off,
+                        int* item_off, int* n_items, int2* lq, int4* items, cudaStream_t s) {
+    cudaMemsetAsync(cnt, 0, sizeof(int) * nlist, s);
+    cudaMemsetAsync(cursor, 0, sizeof(int) * nlist, s);
+    const int64_t pairs = nq * nprobe;
+    const int blocks = (int)std::min<int64_t>((pairs + 255) / 256, 4096);
+    count_lists_kernel<<<blocks, 256, 0, s>>>(probes, pairs, nlist, owned, cnt);
+    prefix_lists_kernel<<<1, 1024, 0, s>>>(cnt, nlist, qpi, lq_off, item_off, n_items);
+    scatter_pairs_kernel<<<blocks, 256, 0, s>>>(probes, nq, nprobe, nlist, owned, lq_off, cursor, lq);
+    make_items_kernel<<<(nlist + 255) / 256, 256, 0, s>>>(cnt, lq_off, item_off, nlist, qpi, items);
+}
+
+size_t scan_smem_bytes(int D) {
+    return sizeof(ScanSmem) + (size_t)(D / 4) * 16 * sizeof(uint32_t) + (size_t)kScanWarps * D;
+}
+
+int scan_grid_size() {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms * 2;
+}
+
+void launch_scan(const ScanArgs& a, int grid, cudaStream_t s) {
+    const size_t smem = scan_smem_bytes(a.D);
+    cudaFuncSetAttribute(scan_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    scan_lists_kernel<<<grid, kScanThreads, smem, s>>>(a);
+}
+
+void launch_merge(const MergeArgs& a, cudaStream_t s) {
+    if (a.nq <= 0) return;
+    merge_kernel<<<(unsigned)((a.nq + 3) / 4), 128, 0, s>>>(a);
+}
+
+void launch_merge_shards(const float* dists, const uint64_t* keys, const int64_t* ids, int world,
+                         int64_t nq, int k, int64_t* out_ids, float* out_dists, cudaStream_t s) {
+    if (nq <= 0) return;
+    merge_shards_kernel<<<(unsigned)((nq + 3) / 4), 128, 0, s>>>(dists, keys, ids, world, nq, k,
+                                                                 out_ids, out_dists);
+}
+
+}  // namespace hanns

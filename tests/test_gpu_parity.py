@@ -1,0 +1,160 @@
+"""Parity of the CUDA search path (through the C ABI) with the CPU oracle.
+
+Bit-exact: coarse probes, q_rot, q_i8, sum(q_i8), the FastScan LUT and its scale,
+the per-query scalars, result ids and distances (float bits), fused and post
+bitset filtering.  Inputs: the committed golden fixtures (oracle outputs) and
+freshly oracle-built artifacts at larger sizes.
+"""
+import ctypes as C
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from tests.golden.make_golden import load
+
+pytestmark = pytest.mark.gpu
+
+FIXTURES = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
+IDS = [os.path.basename(p)[:-4] for p in FIXTURES]
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    from hanns_b200 import _lib
+    L = _lib.lib()
+    if L.hanns_gpu_device_count() < 1:
+        pytest.fail("no CUDA device visible to libhanns_gpu")
+    return L
+
+
+def bits_eq(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=IDS)
+def test_query_state_and_probes_bit_exact(gpu, path):
+    from hanns_b200.ivf_usq import IvfUsqIndex
+    art, z = load(path)
+    idx = IvfUsqIndex.from_artifact(art)
+    st = idx.debug_query(z["queries"], z["nprobe"])
+    assert np.array_equal(st["probes"], z["exp_probes"])
+    assert bits_eq(st["q_rot"], z["exp_q_rot"])
+    assert np.array_equal(st["q_i8"], z["exp_q_i8"])
+    assert np.array_equal(st["q_i8_sum"], z["exp_q_i8_sum"])
+    assert np.array_equal(st["lut"], z["exp_lut"])
+    assert bits_eq(st["q_scale"], z["exp_scalars"][:, 0])
+    assert bits_eq(st["centroid_score"], z["exp_scalars"][:, 1])
+    assert bits_eq(st["q_norm_sq"], z["exp_scalars"][:, 2])
+    assert bits_eq(st["lut_scale"], z["exp_scalars"][:, 3])
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=IDS)
+def test_search_bit_exact(gpu, path):
+    from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
+    art, z = load(path)
+    idx = IvfUsqIndex.from_artifact(art)
+    r = idx.search(z["queries"], SearchRequest(top_k=z["k"], nprobe=z["nprobe"]))
+    ids = r.ids.reshape(z["exp_ids"].shape)
+    d = r.distances.reshape(z["exp_ids"].shape)
+    assert np.array_equal(ids, z["exp_ids"])
+    assert bits_eq(d, z["exp_dists"])
+    # run twice: workspace reuse must not change results
+    r2 = idx.search(z["queries"], SearchRequest(top_k=z["k"], nprobe=z["nprobe"]))
+    assert np.array_equal(r2.ids, r.ids) and bits_eq(r2.distances, r.distances)
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=IDS)
+def test_bitset_fused_and_post(gpu, path):
+    from hanns_b200.ivf_usq import FILTER_FUSED, FILTER_POST, IvfUsqIndex, SearchRequest
+    art, z = load(path)
+    idx = IvfUsqIndex.from_artifact(art)
+    req = SearchRequest(top_k=z["k"], nprobe=z["nprobe"])
+    blen = int(z["bitset_len"][0])
+    f = idx.search(z["queries"], req, FILTER_FUSED, z["bitsets"], blen, z["query_bitset"])
+    assert np.array_equal(f.ids.reshape(z["exp_fused_ids"].shape), z["exp_fused_ids"])
+    assert bits_eq(f.distances.reshape(z["exp_fused_ids"].shape), z["exp_fused_dists"])
+    p = idx.search(z["queries"], req, FILTER_POST, z["bitsets"], blen, z["query_bitset"])
+    assert np.array_equal(p.counts, z["exp_post_counts"])
+    assert np.array_equal(p.ids.reshape(z["exp_post_ids"].shape), z["exp_post_ids"])
+
+
+def test_knowhere_c_abi_search(gpu):
+    """knowhere_search / knowhere_search_with_bitset on an imported index."""
+    from hanns_b200 import _lib
+    from hanns_b200.ivf_usq import IvfUsqIndex
+    art, z = load(FIXTURES[0])
+    idx = IvfUsqIndex.from_artifact(art)
+    h = idx._h
+    assert gpu.knowhere_set_nprobe(h, int(z["nprobe"])) == 0
+    q = np.ascontiguousarray(z["queries"], np.float32)
+    nq, k = q.shape[0], int(z["k"])
+    r = gpu.knowhere_search(h, q.ctypes.data_as(_lib.f32p), nq, k, q.shape[1])
+    assert r
+    n = r.contents.num_results
+    ids = np.ctypeslib.as_array(r.contents.ids, (n,)).copy()
+    ds = np.ctypeslib.as_array(r.contents.distances, (n,)).copy()
+    gpu.knowhere_free_result(r)
+    assert n == nq * k
+    assert np.array_equal(ids.reshape(nq, k), z["exp_ids"])
+    assert bits_eq(ds.reshape(nq, k), z["exp_dists"])
+    # wrong dim -> NULL, no crash
+    assert not gpu.knowhere_search(h, q.ctypes.data_as(_lib.f32p), nq, k, q.shape[1] + 1)
+    # one bitset for the whole batch, fused (default) semantics
+    blen = int(z["bitset_len"][0])
+    b = gpu.knowhere_bitset_create(blen)
+    words = z["bitsets"][0]
+    for i in range(blen):
+        if (int(words[i >> 6]) >> (i & 63)) & 1:
+            gpu.knowhere_bitset_set(b, i, True)
+    r = gpu.knowhere_search_with_bitset(h, q.ctypes.data_as(_lib.f32p), nq, k, q.shape[1], b)
+    n = r.contents.num_results
+    fid = np.ctypeslib.as_array(r.contents.ids, (n,)).copy()
+    gpu.knowhere_free_result(r)
+    gpu.knowhere_bitset_free(b)
+    from oracle import oracle as O
+    oi = O.OracleIndex(art)
+    exp, _, _ = oi.search(q, k, int(z["nprobe"]), filter_mode=O.FILTER_FUSED,
+                          bitsets=z["bitsets"][:1], bitset_len=blen)
+    assert np.array_equal(fid.reshape(nq, k), exp)
+
+
+@pytest.mark.parametrize("nbits,metric,k,d", [(4, 0, 10, 128), (8, 1, 10, 200), (4, 1, 50, 64),
+                                              (8, 0, 100, 96)])
+def test_search_bit_exact_larger(gpu, oracle_mod, nbits, metric, k, d):
+    """Oracle-built artifacts with 20k rows: FastScan lists, k up to 100."""
+    from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
+    from tests.golden.make_golden import mixture
+    O = oracle_mod
+    rng = np.random.default_rng(100 + nbits + k)
+    x, _ = mixture(rng, 20000, d, 32, 0.4, metric == 1)
+    q, _ = mixture(rng, 300, d, 32, 0.4, metric == 1)
+    art = O.build_artifact(x, 24, nbits, metric, rotation_seed=9, kmeans_iters=6, kmeans_seed=3)
+    oi = O.OracleIndex(art)
+    exp_ids, exp_d, _ = oi.search(q, k, 6)
+    idx = IvfUsqIndex.from_artifact(art)
+    r = idx.search(q, SearchRequest(top_k=k, nprobe=6))
+    assert np.array_equal(r.ids.reshape(exp_ids.shape), exp_ids)
+    assert bits_eq(r.distances.reshape(exp_ids.shape), exp_d)
+
+
+def test_empty_and_tiny_index(gpu, oracle_mod):
+    """Lists of 0, 1, 31, 32, 33 rows; k larger than everything probed."""
+    from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
+    O = oracle_mod
+    rng = np.random.default_rng(1)
+    sizes = [0, 1, 31, 32, 33, 0, 2]
+    d = 40
+    cent = rng.normal(size=(len(sizes), d)).astype(np.float32) * 5
+    x = np.concatenate([cent[i] + 0.1 * rng.normal(size=(s, d)) for i, s in enumerate(sizes) if s]).astype(np.float32)
+    art = O.build_artifact(x, len(sizes), 4, O.METRIC_L2, centroids=cent)
+    assert np.diff(art["list_offsets"]).tolist() == sizes
+    q = np.concatenate([cent + 0.05, x[:3]]).astype(np.float32)
+    oi = O.OracleIndex(art)
+    idx = IvfUsqIndex.from_artifact(art)
+    for k, npr in [(5, 1), (200, 7), (40, 3)]:
+        e_ids, e_d, _ = oi.search(q, k, npr)
+        r = idx.search(q, SearchRequest(top_k=k, nprobe=npr))
+        assert np.array_equal(r.ids.reshape(e_ids.shape), e_ids)
+        assert bits_eq(r.distances.reshape(e_ids.shape), e_d)
