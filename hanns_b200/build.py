@@ -22,7 +22,8 @@ OUT_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(OUT_DIR, "libhanns_gpu.so")
 OBJ_DIR = os.path.join(HERE, "_build")
 
-CU_SOURCES = ["search_kernels.cu", "build_kernels.cu", "ivf_usq_gpu.cu", "capi.cu"]
+CU_SOURCES = ["search_kernels.cu", "build_kernels.cu", "ivf_usq_gpu.cu", "capi.cu",
+              "coarse_static.cu"]
 CPP_SOURCES = ["rotation.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "ivf_usq_gpu.h"]
 

@@ -23,6 +23,14 @@ thread_local std::string g_last_error;
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
+}  // namespace
+
+namespace hanns {
+void set_last_error(const std::string& msg) { set_error(msg); }
+}  // namespace hanns
+
+namespace {
+
 // Maps exceptions to CError codes (src/ffi.rs:62-71).
 int32_t code_of(const std::exception& e) {
     if (dynamic_cast<const std::invalid_argument*>(&e)) return HANNS_INVALID_ARG;

@@ -77,6 +77,9 @@ struct MergeArgs {
     uint64_t* out_keys;
 };
 
+// Records the message returned by hanns_gpu_last_error() on this thread.
+void set_last_error(const std::string& msg);
+
 // search stages
 void launch_coarse_l2(const float* q, int64_t nq, const float* cent, int nlist, int d, float* dist,
                       cudaStream_t s);

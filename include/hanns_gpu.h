@@ -259,6 +259,22 @@ int32_t hanns_gpu_merge_shards_device(const float* d_dists, const uint64_t* d_ke
                                       const int64_t* d_ids, int32_t world, int64_t nq, int32_t k,
                                       int64_t* d_out_ids, float* d_out_dists, void* stream);
 
+/* Coarse-probe step without any device allocation.  No counterpart in the reference.
+ * For callers that cannot call cudaMalloc: processes that give all GPU memory to their
+ * own pool at start-up, and latency-critical paths where cudaMalloc/cudaFree (which may
+ * synchronise the device) are not allowed.  Computes, for nq device-resident queries,
+ * the exact L2 to the nlist device-resident centroids (dim floats each) and writes the
+ * nprobe nearest list ids per query, in order, to d_probes[nq*nprobe] -- the same
+ * probes the search path uses.  Scratch is a fixed 16 MiB array inside the library (held
+ * on every GPU that loads it until exit); nq*nlist*4 + nq*nprobe*8 bytes (distances
+ * rounded up to 256) must fit, else HANNS_INVALID_ARG and nothing runs.  The first call
+ * on a device looks up the scratch address (make it before any stream capture).
+ * Asynchronous on `stream`; all calls share the scratch, so calls that overlap on the
+ * GPU race -- order them on one stream. */
+int32_t hanns_gpu_coarse_probes_static(const float* d_queries, int64_t nq,
+                                       const float* d_centroids, int32_t nlist, int32_t dim,
+                                       int32_t nprobe, int32_t* d_probes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
