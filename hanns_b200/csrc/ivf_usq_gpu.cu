@@ -76,7 +76,6 @@ void IvfUsqGpu::ensure_stream() {
     if (!stream_) {
         HANNS_CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
         for (auto& e : ev_) HANNS_CUDA_OK(cudaEventCreate(&e));
-        scan_grid_ = scan_grid_size();
     }
 }
 
@@ -115,6 +114,34 @@ void IvfUsqGpu::rebuild_fastscan() {
     HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
 }
 
+void IvfUsqGpu::update_centroid_norms() {
+    cn_.reserve(nlist_);
+    launch_centroid_norms(centroids_.p, nlist_, dim_, cn_.p, stream_);
+    HANNS_CUDA_OK(cudaGetLastError());
+    std::vector<float> h(nlist_);
+    HANNS_CUDA_OK(cudaMemcpyAsync(h.data(), cn_.p, sizeof(float) * nlist_, cudaMemcpyDeviceToHost,
+                                  stream_));
+    HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    float m = 0.0f;
+    for (float v : h) m = (v != v) ? INFINITY : std::max(m, v);
+    cmax_ = std::sqrt(m);
+}
+
+// Probes of nb device queries: approximate GEMM + exact re-score (launch_coarse_fast),
+// in chunks bounded by the approximation matrix (1 GiB).
+void IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes,
+                              cudaStream_t s) {
+    const int64_t cchunk = std::max<int64_t>(1, std::min<int64_t>(nb, (1ll << 28) / nlist_));
+    w_dist_.reserve((size_t)cchunk * nlist_);
+    w_fallbacks_.reserve(1);
+    HANNS_CUDA_OK(cudaMemsetAsync(w_fallbacks_.p, 0, sizeof(int), s));
+    for (int64_t c = 0; c < nb; c += cchunk) {
+        const int64_t m = std::min(cchunk, nb - c);
+        launch_coarse_fast(d_q + c * dim_, m, centroids_.p, cn_.p, cmax_, nlist_, dim_, nprobe,
+                           w_dist_.p, d_probes + c * nprobe, w_fallbacks_.p, s);
+    }
+}
+
 void IvfUsqGpu::upload_rotation_centroid() {
     std::vector<float> P((size_t)D_ * D_);
     rotation_matrix(rotation_seed_, D_, P.data());
@@ -135,6 +162,7 @@ void IvfUsqGpu::import_artifact(const void* art_) {
     metric_ = a->metric;
     ntotal_ = a->ntotal;
     h2d(centroids_, a->centroids, (size_t)nlist_ * dim_, stream_);
+    update_centroid_norms();
     h2d(P_, a->rotation, (size_t)D_ * D_, stream_);
     h2d(rc_, a->rotated_centroid, (size_t)D_, stream_);
     std::vector<int64_t> off(a->list_offsets, a->list_offsets + nlist_ + 1);
@@ -232,6 +260,7 @@ void IvfUsqGpu::train(const float* h_data, int64_t n, int kmeans_iters, uint64_t
         launch_kmeans_update(sums.p, counts.p, nlist_, dim_, centroids_.p, stream_);
         HANNS_CUDA_OK(cudaGetLastError());
     }
+    update_centroid_norms();
     gmean_.reserve(dim_);
     launch_global_mean(x.p, n, dim_, gmean_.p, stream_);
     HANNS_CUDA_OK(cudaGetLastError());
@@ -413,14 +442,8 @@ void IvfUsqGpu::search_batch(const float* d_q, int64_t nb, const SearchOptions& 
     // 1. coarse probes
     w_probes_.reserve((size_t)nb * nprobe);
     w_sel_.reserve((size_t)nb * 2 * nprobe);
-    const int64_t cchunk = std::max<int64_t>(1, std::min<int64_t>(nb, (1ll << 28) / nlist_));
-    w_dist_.reserve((size_t)cchunk * nlist_);
-    for (int64_t c = 0; c < nb; c += cchunk) {
-        const int64_t m = std::min(cchunk, nb - c);
-        launch_coarse_l2(d_q + c * dim_, m, centroids_.p, nlist_, dim_, w_dist_.p, s);
-        launch_select_probes(w_dist_.p, m, nlist_, nprobe, w_probes_.p + c * nprobe, w_sel_.p, s);
-        launches += 2;
-    }
+    coarse_probes(d_q, nb, nprobe, w_probes_.p, s);
+    launches += 2 * ((nb + ((1ll << 28) / nlist_) - 1) / std::max<int64_t>(1, (1ll << 28) / nlist_));
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[1], s));
     // 2. query state
     w_qrot_.reserve((size_t)nb * D_);
@@ -453,6 +476,7 @@ void IvfUsqGpu::search_batch(const float* d_q, int64_t nb, const SearchOptions& 
     w_slot_tie_.reserve(slots * k);
     w_slot_cnt_.reserve(slots);
     HANNS_CUDA_OK(cudaMemsetAsync(w_slot_cnt_.p, 0, slots * sizeof(int), s));
+    if (!scan_grid_) scan_grid_ = scan_grid_size(D_);
     const int grid = scan_grid_;
     const size_t per_warp = (size_t)max_list_;
     w_scores_.reserve((size_t)grid * 8 * per_warp);
@@ -612,9 +636,7 @@ void IvfUsqGpu::debug_query(const float* h_queries, int64_t nq, int nprobe, int3
     h2d(w_pad_queries_, h_queries, (size_t)nq * dim_, stream_);
     w_probes_.reserve((size_t)nq * nprobe);
     w_sel_.reserve((size_t)nq * 2 * nprobe);
-    w_dist_.reserve((size_t)nq * nlist_);
-    launch_coarse_l2(w_pad_queries_.p, nq, centroids_.p, nlist_, dim_, w_dist_.p, stream_);
-    launch_select_probes(w_dist_.p, nq, nlist_, nprobe, w_probes_.p, w_sel_.p, stream_);
+    coarse_probes(w_pad_queries_.p, nq, nprobe, w_probes_.p, stream_);
     w_qrot_.reserve((size_t)nq * D_);
     w_qp_.reserve(nq);
     w_qi8p_.reserve((size_t)nq * D_);
@@ -708,6 +730,7 @@ void IvfUsqGpu::load(const std::string& path) {
     const size_t n = (size_t)ntotal_;
     if (trained_) {
         get(centroids_, (size_t)nlist_ * dim_);
+        update_centroid_norms();
         get(P_, (size_t)D_ * D_);
         get(rc_, (size_t)D_);
         get(gmean_, (size_t)dim_);

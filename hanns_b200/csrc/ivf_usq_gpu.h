@@ -112,6 +112,8 @@ class IvfUsqGpu {
                       float* d_dists, int64_t* d_counts, uint64_t* d_keys, cudaStream_t s,
                       bool time_it);
     void set_list_layout(const std::vector<int64_t>& h_off);
+    void update_centroid_norms();
+    void coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes, cudaStream_t s);
 
     int dim_, D_, nbits_, nlist_, metric_, nprobe_, device_;
     uint64_t rotation_seed_;
@@ -120,7 +122,8 @@ class IvfUsqGpu {
     int code_bytes_;
 
     // device artifact (list order)
-    DevBuf<float> centroids_, P_, rc_, gmean_;
+    DevBuf<float> centroids_, P_, rc_, gmean_, cn_;
+    float cmax_ = 0.0f;  // max ||centroid|| (bound of the approximate coarse step)
     DevBuf<int64_t> list_off_, fs_blk_off_, ids_;
     DevBuf<float4> meta_;
     DevBuf<uint8_t> codes_, signs_, owned_;
@@ -150,6 +153,7 @@ class IvfUsqGpu {
     cudaEvent_t ev_[6] = {};
     float stage_ms_[6] = {0, 0, 0, 0, 0, 0};
     int64_t last_launches_ = 0;
+    DevBuf<int> w_fallbacks_;
     int scan_grid_ = 0;
     std::mutex mu_;
 };

@@ -85,6 +85,11 @@ void launch_coarse_l2(const float* q, int64_t nq, const float* cent, int nlist, 
                       cudaStream_t s);
 void launch_select_probes(const float* dist, int64_t nq, int nlist, int nprobe, int32_t* probes,
                           uint32_t* scratch, cudaStream_t s);
+// Approximate-then-exact coarse step (same probes as the two launches above).
+void launch_coarse_fast(const float* q, int64_t nq, const float* cent, const float* cn, float cmax,
+                        int nlist, int d, int nprobe, float* approx, int32_t* probes,
+                        int* fallbacks, cudaStream_t s);
+void launch_centroid_norms(const float* cent, int nlist, int d, float* cn, cudaStream_t s);
 void launch_rotate(const float* x, int64_t nq, int d, int D, const float* P, float* out,
                    cudaStream_t s);
 void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, int D,
@@ -94,7 +99,7 @@ void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist
                         const uint8_t* owned, int qpi, int* cnt, int* cursor, int* lq_off,
                         int* item_off, int* n_items, int2* lq, int4* items, cudaStream_t s);
 size_t scan_smem_bytes(int D);
-int scan_grid_size();
+int scan_grid_size(int D);
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s);
 void launch_merge(const MergeArgs& a, cudaStream_t s);
 void launch_merge_shards(const float* dists, const uint64_t* keys, const int64_t* ids, int world,

@@ -230,21 +230,252 @@ __global__ void __launch_bounds__(128) select_probes_kernel(const float* __restr
 }
 
 // ============================================================================
+// Coarse, fast path.  a(q,c) = ||c||^2 - 2 q.c is computed with an FP32 GEMM (FMA,
+// sequential over dims inside each thread), then per query every centroid whose a(q,c)
+// lies within a rigorous rounding-error bound of the nprobe-th smallest is re-scored
+// with the reference's exact sequential L2 and the nprobe best are selected exactly.
+// The bound guarantees the exact top-nprobe set is among the re-scored centroids, so
+// the probes equal those of coarse_l2_kernel + select_probes_kernel.  A query whose
+// candidate set is larger than kCoarseCap (or smaller than nprobe, e.g. NaN inputs)
+// takes the exact scan of every centroid instead.
+// ============================================================================
+constexpr int kGM = 128, kGN = 128, kGK = 16;
+constexpr int kCoarseCap = 512;
+
+template <bool kVec>
+__global__ void __launch_bounds__(256) coarse_gemm_kernel(const float* __restrict__ q, int64_t nq,
+                                                          const float* __restrict__ cent, int nlist,
+                                                          int d, const float* __restrict__ cn,
+                                                          float* __restrict__ out) {
+    __shared__ __align__(16) float As[kGK][kGM + 4];
+    __shared__ __align__(16) float Bs[kGK][kGN + 4];
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int64_t q0 = (int64_t)blockIdx.y * kGM;
+    const int c0 = blockIdx.x * kGN;
+    const int lr = tid >> 2, lk = (tid & 3) * 4;
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < d; k0 += kGK) {
+        float ra[2][4], rb[2][4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int row = lr + 64 * h;
+            const int64_t qr = q0 + row;
+            const int cr = c0 + row;
+            const int kk = k0 + lk;
+            if (kVec) {
+                float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
+                if (qr < nq && kk < d) va = __ldg(reinterpret_cast<const float4*>(q + qr * d + kk));
+                if (cr < nlist && kk < d)
+                    vb = __ldg(reinterpret_cast<const float4*>(cent + (int64_t)cr * d + kk));
+                ra[h][0] = va.x; ra[h][1] = va.y; ra[h][2] = va.z; ra[h][3] = va.w;
+                rb[h][0] = vb.x; rb[h][1] = vb.y; rb[h][2] = vb.z; rb[h][3] = vb.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    ra[h][j] = (qr < nq && kk + j < d) ? q[qr * d + kk + j] : 0.0f;
+                    rb[h][j] = (cr < nlist && kk + j < d) ? cent[(int64_t)cr * d + kk + j] : 0.0f;
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                As[lk + j][lr + 64 * h] = ra[h][j];
+                Bs[lk + j][lr + 64 * h] = rb[h][j];
+            }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < kGK; ++kk) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][64 + ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kk][64 + tx * 4]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int64_t qr = q0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+        if (qr >= nq) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int cr = c0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+            if (cr < nlist) out[qr * nlist + cr] = __fmaf_rn(-2.0f, acc[i][j], cn[cr]);
+        }
+    }
+}
+
+// Exact sequential L2 (the reference's l2_distance) of one query (shared memory) to one
+// centroid.
+__device__ __forceinline__ float exact_l2(const float* qs, const float* __restrict__ c, int d) {
+    float s = -0.0f;
+    if ((d & 3) == 0) {
+        const float4* c4 = reinterpret_cast<const float4*>(c);
+        for (int i = 0; i < d / 4; ++i) {
+            const float4 v = __ldg(c4 + i);
+            float df = __fsub_rn(qs[4 * i], v.x);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+            df = __fsub_rn(qs[4 * i + 1], v.y);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+            df = __fsub_rn(qs[4 * i + 2], v.z);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+            df = __fsub_rn(qs[4 * i + 3], v.w);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+        }
+    } else {
+        for (int i = 0; i < d; ++i) {
+            const float df = __fsub_rn(qs[i], __ldg(c + i));
+            s = __fadd_rn(s, __fmul_rn(df, df));
+        }
+    }
+    return s;
+}
+
+// One warp per query.  `approx` rows are per-query scratch (overwritten on fallback).
+__global__ void __launch_bounds__(128) coarse_select_exact_kernel(
+    float* __restrict__ approx, const float* __restrict__ q, int64_t nq,
+    const float* __restrict__ cent, int nlist, int d, int nprobe, float cmax,
+    int32_t* __restrict__ probes, int* __restrict__ fallbacks) {
+    extern __shared__ __align__(16) float qsm[];  // [4][d]
+    __shared__ uint32_t hist[4][256];
+    __shared__ uint32_t ckey[4][kCoarseCap];
+    __shared__ int cidx[4][kCoarseCap];
+    const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    const int64_t qi = (int64_t)blockIdx.x * 4 + w;
+    if (qi >= nq) return;
+    float* qs = qsm + w * d;
+    float qn = 0.0f;
+    for (int i = lane; i < d; i += 32) {
+        const float v = q[qi * d + i];
+        qs[i] = v;
+        qn = __fmaf_rn(v, v, qn);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) qn = __fadd_rn(qn, __shfl_xor_sync(0xffffffffu, qn, o));
+    __syncwarp();
+    float* row = approx + qi * nlist;
+    auto key_at = [&](int i, uint32_t& k) {
+        k = total_order_key(row[i]);
+        return true;
+    };
+    int less = 0;
+    const float tau = key_to_float(warp_radix_kth(nlist, nprobe, 32, key_at, hist[w], &less));
+    // rounding-error bound (all in double; u = 2^-24, gamma = (d + 8) u)
+    const double gam = (double)(d + 8) * 5.9604644775390625e-8;
+    const double Qn = (double)qn, eQ = 2.0 * gam * Qn + 1e-30;
+    const double qnorm = sqrt(Qn) * (1.0 + 2.0 * gam);
+    const double cm = (double)cmax * (1.0 + 2.0 * gam);
+    const double err = 4.0 * gam * qnorm * cm + 2.0 * gam * cm * cm +
+                       2.384185791015625e-7 * (cm * cm + 2.0 * qnorm * cm) + 1e-30;
+    const double e_ub = ((double)tau + Qn + eQ + err) * (1.0 + 2.0 * gam);
+    const double thr = e_ub * (1.0 + 2.0 * gam) - Qn + eQ + err;
+    int cnt = 0;
+    for (int base = 0; base < nlist; base += 32) {
+        const int c = base + lane;
+        const bool in = c < nlist && (double)row[c] <= thr;
+        const unsigned b = __ballot_sync(0xffffffffu, in);
+        if (in) {
+            const int pos = cnt + __popc(b & lanemask_lt());
+            if (pos < kCoarseCap) cidx[w][pos] = c;
+        }
+        cnt += __popc(b);
+    }
+    __syncwarp();
+    if (cnt <= kCoarseCap && cnt >= nprobe) {
+        for (int i = lane; i < cnt; i += 32)
+            ckey[w][i] = total_order_key(exact_l2(qs, cent + (int64_t)cidx[w][i] * d, d));
+        __syncwarp();
+        for (int i = lane; i < cnt; i += 32) {
+            const uint32_t ki = ckey[w][i];
+            const int ii = cidx[w][i];
+            int rank = 0;
+            for (int j = 0; j < cnt; ++j) {
+                const uint32_t kj = ckey[w][j];
+                rank += (kj < ki || (kj == ki && cidx[w][j] < ii)) ? 1 : 0;
+            }
+            if (rank < nprobe) probes[qi * nprobe + rank] = ii;
+        }
+        return;
+    }
+    // fallback: exact distance to every centroid, then the stable selection
+    if (lane == 0) atomicAdd(fallbacks, 1);
+    for (int c = lane; c < nlist; c += 32) row[c] = exact_l2(qs, cent + (int64_t)c * d, d);
+    __syncwarp();
+    const uint32_t ktau = warp_radix_kth(nlist, nprobe, 32, key_at, hist[w], &less);
+    int taken = 0, ties_needed = nprobe - less;
+    uint32_t* sk = ckey[w];
+    int* si = cidx[w];
+    for (int base = 0; base < nlist && taken < nprobe; base += 32) {
+        const int i = base + lane;
+        uint32_t k = 0xFFFFFFFFu;
+        if (i < nlist) k = total_order_key(row[i]);
+        const bool lt = i < nlist && k < ktau;
+        const bool eq = i < nlist && k == ktau;
+        const unsigned beq = __ballot_sync(0xffffffffu, eq);
+        const int eq_rank = __popc(beq & lanemask_lt());
+        const bool take = lt || (eq && eq_rank < ties_needed);
+        const unsigned bt = __ballot_sync(0xffffffffu, take);
+        if (take) {
+            const int pos = taken + __popc(bt & lanemask_lt());
+            if (pos < kCoarseCap) {
+                sk[pos] = k;
+                si[pos] = i;
+            }
+        }
+        taken += __popc(bt);
+        ties_needed -= min(__popc(beq), max(ties_needed, 0));
+    }
+    __syncwarp();
+    const int m = min(taken, min(nprobe, kCoarseCap));
+    for (int a = lane; a < m; a += 32) {
+        const uint32_t ka = sk[a];
+        const int ia = si[a];
+        int rank = 0;
+        for (int b = 0; b < m; ++b) rank += (sk[b] < ka || (sk[b] == ka && si[b] < ia)) ? 1 : 0;
+        probes[qi * nprobe + rank] = ia;
+    }
+}
+
+__global__ void centroid_norms_kernel(const float* __restrict__ cent, int nlist, int d,
+                                      float* __restrict__ cn) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= nlist) return;
+    float s = 0.0f;
+    for (int i = 0; i < d; ++i) s = __fmaf_rn(cent[(int64_t)c * d + i], cent[(int64_t)c * d + i], s);
+    cn[c] = s;
+}
+
+// ============================================================================
 // Query preparation
 // ============================================================================
-constexpr int kRotQ = 8;      // queries per CTA
 constexpr int kRotRows = 64;  // rows per CTA
 
 // q_rot[q][r] = tree16( lane j: fma chain over c = j, j+16, ... of P[r][c]*x[c] ).
+// QT queries per CTA, staged transposed in shared memory ([D][QT+4] floats) so a lane
+// reads the QT query values of one column with 16-byte loads; a half-warp owns a row.
+template <int QT>
 __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x, int64_t nq,
                                                      int d, int D, const float* __restrict__ P,
                                                      float* __restrict__ out) {
-    extern __shared__ float xs[];  // [kRotQ][D]
-    const int64_t q0 = (int64_t)blockIdx.y * kRotQ;
-    for (int e = threadIdx.x; e < kRotQ * D; e += blockDim.x) {
+    constexpr int LD = QT + 4;
+    extern __shared__ __align__(16) float xs[];  // [D][LD]
+    const int64_t q0 = (int64_t)blockIdx.y * QT;
+    for (int e = threadIdx.x; e < QT * D; e += blockDim.x) {
         const int t = e / D, c = e % D;
         const int64_t qq = q0 + t;
-        xs[e] = (qq < nq && c < d) ? x[qq * d + c] : 0.0f;
+        xs[c * LD + t] = (qq < nq && c < d) ? x[qq * d + c] : 0.0f;
     }
     __syncthreads();
     const int half = threadIdx.x >> 4, j = threadIdx.x & 15;
@@ -253,16 +484,23 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x
         const int r = blockIdx.x * kRotRows + rr;
         if (r >= D) break;  // uniform across the half-warp
         const float* prow = P + (int64_t)r * D;
-        float acc[kRotQ];
+        float acc[QT];
 #pragma unroll
-        for (int t = 0; t < kRotQ; ++t) acc[t] = 0.0f;
+        for (int t = 0; t < QT; ++t) acc[t] = 0.0f;
         for (int c = j; c < D; c += 16) {
             const float p = __ldg(prow + c);
+            const float4* xv = reinterpret_cast<const float4*>(xs + c * LD);
 #pragma unroll
-            for (int t = 0; t < kRotQ; ++t) acc[t] = __fmaf_rn(p, xs[t * D + c], acc[t]);
+            for (int t4 = 0; t4 < QT / 4; ++t4) {
+                const float4 v = xv[t4];
+                acc[4 * t4 + 0] = __fmaf_rn(p, v.x, acc[4 * t4 + 0]);
+                acc[4 * t4 + 1] = __fmaf_rn(p, v.y, acc[4 * t4 + 1]);
+                acc[4 * t4 + 2] = __fmaf_rn(p, v.z, acc[4 * t4 + 2]);
+                acc[4 * t4 + 3] = __fmaf_rn(p, v.w, acc[4 * t4 + 3]);
+            }
         }
 #pragma unroll
-        for (int t = 0; t < kRotQ; ++t) {
+        for (int t = 0; t < QT; ++t) {
             float v = acc[t];
             v = __fadd_rn(v, __shfl_down_sync(hmask, v, 8, 16));
             v = __fadd_rn(v, __shfl_down_sync(hmask, v, 4, 16));
@@ -272,7 +510,7 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x
         }
         if (j == 0) {
 #pragma unroll
-            for (int t = 0; t < kRotQ; ++t)
+            for (int t = 0; t < QT; ++t)
                 if (q0 + t < nq) out[(q0 + t) * D + r] = acc[t];
         }
     }
@@ -951,13 +1189,42 @@ void launch_select_probes(const float* dist, int64_t nq, int nlist, int nprobe, 
                                                                   scratch);
 }
 
+void launch_coarse_fast(const float* q, int64_t nq, const float* cent, const float* cn, float cmax,
+                        int nlist, int d, int nprobe, float* approx, int32_t* probes,
+                        int* fallbacks, cudaStream_t s) {
+    if (nq <= 0) return;
+    dim3 grid((nlist + kGN - 1) / kGN, (unsigned)((nq + kGM - 1) / kGM));
+    if ((d & 3) == 0)
+        coarse_gemm_kernel<true><<<grid, 256, 0, s>>>(q, nq, cent, nlist, d, cn, approx);
+    else
+        coarse_gemm_kernel<false><<<grid, 256, 0, s>>>(q, nq, cent, nlist, d, cn, approx);
+    const size_t smem = (size_t)4 * d * sizeof(float);
+    cudaFuncSetAttribute(coarse_select_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         150 * 1024);
+    coarse_select_exact_kernel<<<(unsigned)((nq + 3) / 4), 128, smem, s>>>(
+        approx, q, nq, cent, nlist, d, nprobe, cmax, probes, fallbacks);
+}
+
+void launch_centroid_norms(const float* cent, int nlist, int d, float* cn, cudaStream_t s) {
+    centroid_norms_kernel<<<(nlist + 127) / 128, 128, 0, s>>>(cent, nlist, d, cn);
+}
+
 void launch_rotate(const float* x, int64_t nq, int d, int D, const float* P, float* out,
                    cudaStream_t s) {
     if (nq <= 0) return;
-    const size_t smem = (size_t)kRotQ * D * sizeof(float);
-    cudaFuncSetAttribute(rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    dim3 grid((D + kRotRows - 1) / kRotRows, (unsigned)((nq + kRotQ - 1) / kRotQ));
-    rotate_kernel<<<grid, 256, smem, s>>>(x, nq, d, D, P, out);
+    if (D <= 1536 && nq > 8) {
+        constexpr int QT = 16;
+        const size_t smem = (size_t)D * (QT + 4) * sizeof(float);
+        cudaFuncSetAttribute(rotate_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        dim3 grid((D + kRotRows - 1) / kRotRows, (unsigned)((nq + QT - 1) / QT));
+        rotate_kernel<QT><<<grid, 256, smem, s>>>(x, nq, d, D, P, out);
+    } else {
+        constexpr int QT = 8;
+        const size_t smem = (size_t)D * (QT + 4) * sizeof(float);
+        cudaFuncSetAttribute(rotate_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        dim3 grid((D + kRotRows - 1) / kRotRows, (unsigned)((nq + QT - 1) / QT));
+        rotate_kernel<QT><<<grid, 256, smem, s>>>(x, nq, d, D, P, out);
+    }
 }
 
 void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, int D,
@@ -985,11 +1252,16 @@ size_t scan_smem_bytes(int D) {
     return sizeof(ScanSmem) + (size_t)(D / 4) * 16 * sizeof(uint32_t) + (size_t)kScanWarps * D;
 }
 
-int scan_grid_size() {
-    int dev = 0, sms = 0;
+int scan_grid_size(int D) {
+    int dev = 0, sms = 0, per_sm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    return sms * 2;
+    cudaFuncSetAttribute(scan_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_lists_kernel, kScanThreads,
+                                                      scan_smem_bytes(D)) != cudaSuccess ||
+        per_sm < 1)
+        per_sm = 1;
+    return sms * per_sm;
 }
 
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s) {

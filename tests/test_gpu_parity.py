@@ -158,3 +158,50 @@ def test_empty_and_tiny_index(gpu, oracle_mod):
         r = idx.search(q, SearchRequest(top_k=k, nprobe=npr))
         assert np.array_equal(r.ids.reshape(e_ids.shape), e_ids)
         assert bits_eq(r.distances.reshape(e_ids.shape), e_d)
+
+
+def _empty_artifact(cent, D, nbits=4, metric=0):
+    nlist, d = cent.shape
+    rng = np.random.default_rng(0)
+    P = np.linalg.qr(rng.normal(size=(D, D)))[0].astype(np.float32)
+    cb = (D * nbits + 7) // 8
+    return dict(dim=d, padded_dim=D, nbits=nbits, nlist=nlist, metric=metric, centroids=cent,
+                rotation=P, rotated_centroid=np.zeros(D, np.float32),
+                list_offsets=np.zeros(nlist + 1, np.int64), ids=np.zeros(0, np.int64),
+                norms=np.zeros(0, np.float32), norms_sq=np.zeros(0, np.float32),
+                vmaxs=np.zeros(0, np.float32), quant_qualities=np.zeros(0, np.float32),
+                codes=np.zeros((0, cb), np.uint8), sign_bits=np.zeros((0, D // 8), np.uint8))
+
+
+def test_coarse_fast_path_equals_exact(gpu, oracle_mod):
+    """Approximate-GEMM + exact re-score coarse step == exact sequential L2 selection:
+    checked against the exact kernels (static entry point) and the oracle, with 600
+    duplicate centroids (exact ties, candidate sets beyond the cap -> fallback)."""
+    import torch
+    from hanns_b200 import _lib
+    from hanns_b200.ivf_usq import IvfUsqIndex
+    O = oracle_mod
+    rng = np.random.default_rng(5)
+    nlist, d, nprobe = 4096, 768, 32
+    cent = rng.normal(size=(nlist, d)).astype(np.float32)
+    cent /= np.linalg.norm(cent, axis=1, keepdims=True)
+    cent[100:700] = cent[99]
+    q = rng.normal(size=(1000, d)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    q[:50] = cent[99] + 0.01 * rng.normal(size=(50, d)).astype(np.float32)
+    q[50:60] = cent[5]  # exact hits
+    art = _empty_artifact(cent, d)
+    idx = IvfUsqIndex.from_artifact(art)
+    fast = idx.debug_query(q, nprobe)["probes"]
+    qt = torch.from_numpy(q).cuda()
+    ct = torch.from_numpy(cent).cuda()
+    exact = torch.empty(1000, nprobe, dtype=torch.int32, device="cuda")
+    for s in range(0, 1000, 500):
+        rc = gpu.hanns_gpu_coarse_probes_static(qt[s:].data_ptr(), min(500, 1000 - s), ct.data_ptr(),
+                                                nlist, d, nprobe, exact[s:].data_ptr(), None)
+        assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    assert np.array_equal(fast, exact.cpu().numpy())
+    oi = O.OracleIndex(art)
+    _, _, _, op = oi.search(q[:120], 5, nprobe, want_probes=True)
+    assert np.array_equal(fast[:120], op)
