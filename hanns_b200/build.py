@@ -23,7 +23,7 @@ LIB = os.path.join(OUT_DIR, "libhanns_gpu.so")
 OBJ_DIR = os.path.join(HERE, "_build")
 
 CU_SOURCES = ["search_kernels.cu", "build_kernels.cu", "ivf_usq_gpu.cu", "capi.cu",
-              "coarse_static.cu"]
+              "coarse_static.cu", "coarse_tc.cu"]
 CPP_SOURCES = ["rotation.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "ivf_usq_gpu.h"]
 

@@ -124,7 +124,7 @@ CSearchResult* search_common(const void* index, const float* query, size_t count
         std::fprintf(stderr,
                      "TRACE_SEARCH nq=%zu elapsed_us=%.0f coarse_ms=%.3f prep_ms=%.3f "
                      "group_ms=%.3f scan_ms=%.3f merge_ms=%.3f\n",
-                     count, us, st[0], st[1], st[2], st[3], st[4]);
+                     count, us, st[0] + st[1], st[2] + st[3], st[4], st[5], st[6]);
     }
     if (post) {  // reference post-filter: rows concatenated, filtered entries dropped
         std::vector<int64_t> fid;
@@ -498,9 +498,9 @@ int32_t hanns_gpu_ivf_usq_search_device(HannsIvfUsqHandle* h, const float* d_que
     });
 }
 
-int32_t hanns_gpu_ivf_usq_stage_ms(const HannsIvfUsqHandle* h, float* out6) {
-    if (!h || !out6) return HANNS_INVALID_ARG;
-    std::memcpy(out6, h->idx->stage_ms(), sizeof(float) * 6);
+int32_t hanns_gpu_ivf_usq_stage_ms(const HannsIvfUsqHandle* h, float* out8) {
+    if (!h || !out8) return HANNS_INVALID_ARG;
+    std::memcpy(out8, h->idx->stage_ms(), sizeof(float) * 8);
     return HANNS_OK;
 }
 

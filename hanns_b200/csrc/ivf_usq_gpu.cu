@@ -117,6 +117,11 @@ void IvfUsqGpu::rebuild_fastscan() {
 void IvfUsqGpu::update_centroid_norms() {
     cn_.reserve(nlist_);
     launch_centroid_norms(centroids_.p, nlist_, dim_, cn_.p, stream_);
+    // bf16 hi/lo split of the centroids for the tensor-core coarse approximation
+    tc_k_ = coarse_tc_k(dim_);
+    cent_hi_.reserve((size_t)nlist_ * tc_k_);
+    cent_lo_.reserve((size_t)nlist_ * tc_k_);
+    launch_split_bf16(centroids_.p, nlist_, dim_, tc_k_, cent_hi_.p, cent_lo_.p, stream_);
     HANNS_CUDA_OK(cudaGetLastError());
     std::vector<float> h(nlist_);
     HANNS_CUDA_OK(cudaMemcpyAsync(h.data(), cn_.p, sizeof(float) * nlist_, cudaMemcpyDeviceToHost,
@@ -127,18 +132,52 @@ void IvfUsqGpu::update_centroid_norms() {
     cmax_ = std::sqrt(m);
 }
 
-// Probes of nb device queries: approximate GEMM + exact re-score (launch_coarse_fast),
-// in chunks bounded by the approximation matrix (1 GiB).
+// Probes of nb device queries: approximate scores (tcgen05 bf16x3 GEMM, or the FP32 SIMT
+// GEMM) + exact re-score, in chunks bounded by the approximation matrix (1 GiB).
 void IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes,
-                              cudaStream_t s) {
+                              cudaStream_t s, cudaEvent_t mid_event) {
     const int64_t cchunk = std::max<int64_t>(1, std::min<int64_t>(nb, (1ll << 28) / nlist_));
     w_dist_.reserve((size_t)cchunk * nlist_);
-    w_fallbacks_.reserve(1);
-    HANNS_CUDA_OK(cudaMemsetAsync(w_fallbacks_.p, 0, sizeof(int), s));
+    w_fallbacks_.reserve(2);
+    HANNS_CUDA_OK(cudaMemsetAsync(w_fallbacks_.p, 0, 2 * sizeof(int), s));
+    if (nprobe > 256) {  // candidate buffers hold 512: large nprobe takes the exact kernels
+        w_sel_.reserve((size_t)cchunk * 2 * nprobe);
+        for (int64_t c = 0; c < nb; c += cchunk) {
+            const int64_t m = std::min(cchunk, nb - c);
+            launch_coarse_l2(d_q + c * dim_, m, centroids_.p, nlist_, dim_, w_dist_.p, s);
+            if (mid_event && c == 0) HANNS_CUDA_OK(cudaEventRecord(mid_event, s));
+            launch_select_probes(w_dist_.p, m, nlist_, nprobe, d_probes + c * nprobe, w_sel_.p, s);
+        }
+        return;
+    }
+    const char* mode = std::getenv("HANNS_GPU_COARSE");
+    bool tc = !(mode && std::strcmp(mode, "simt") == 0);
+    // |computed q.c - q.c| <= dot_rel * sum|q_i c_i|:
+    //   SIMT FP32 FMA chain: (d + 8) 2^-24;
+    //   bf16 hi/lo x3: representation 3.2 * 2^-16 plus tensor-core accumulation, taken as
+    //   2^-21 per K16 step (3K/16 steps), both doubled.
+    const float rel_simt = (float)((dim_ + 8) * 5.9604644775390625e-8);
+    const float rel_tc =
+        (float)(2.0 * (3.2 * 1.52587890625e-5 + (3.0 * tc_k_ / 16.0 + 2.0) * 4.76837158203125e-7));
+    if (tc) {
+        w_qhi_.reserve((size_t)cchunk * tc_k_);
+        w_qlo_.reserve((size_t)cchunk * tc_k_);
+    }
     for (int64_t c = 0; c < nb; c += cchunk) {
         const int64_t m = std::min(cchunk, nb - c);
-        launch_coarse_fast(d_q + c * dim_, m, centroids_.p, cn_.p, cmax_, nlist_, dim_, nprobe,
-                           w_dist_.p, d_probes + c * nprobe, w_fallbacks_.p, s);
+        bool used_tc = false;
+        if (tc) {
+            launch_split_bf16(d_q + c * dim_, m, dim_, tc_k_, w_qhi_.p, w_qlo_.p, s);
+            used_tc = launch_coarse_tc(w_qhi_.p, w_qlo_.p, m, cent_hi_.p, cent_lo_.p, nlist_, tc_k_,
+                                       cn_.p, w_dist_.p, w_fallbacks_.p + 1, s);
+            tc = used_tc;
+        }
+        if (!used_tc)
+            launch_coarse_gemm(d_q + c * dim_, m, centroids_.p, cn_.p, nlist_, dim_, w_dist_.p, s);
+        if (mid_event && c == 0) HANNS_CUDA_OK(cudaEventRecord(mid_event, s));
+        launch_coarse_select(w_dist_.p, d_q + c * dim_, m, centroids_.p, nlist_, dim_, nprobe, cmax_,
+                             used_tc ? rel_tc : rel_simt, used_tc ? w_fallbacks_.p + 1 : nullptr,
+                             d_probes + c * nprobe, w_fallbacks_.p, s);
     }
 }
 
@@ -442,9 +481,9 @@ void IvfUsqGpu::search_batch(const float* d_q, int64_t nb, const SearchOptions& 
     // 1. coarse probes
     w_probes_.reserve((size_t)nb * nprobe);
     w_sel_.reserve((size_t)nb * 2 * nprobe);
-    coarse_probes(d_q, nb, nprobe, w_probes_.p, s);
-    launches += 2 * ((nb + ((1ll << 28) / nlist_) - 1) / std::max<int64_t>(1, (1ll << 28) / nlist_));
-    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[1], s));
+    coarse_probes(d_q, nb, nprobe, w_probes_.p, s, time_it ? ev_[1] : nullptr);
+    launches += 3 * ((nb + ((1ll << 28) / nlist_) - 1) / std::max<int64_t>(1, (1ll << 28) / nlist_));
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[2], s));
     // 2. query state
     w_qrot_.reserve((size_t)nb * D_);
     w_qp_.reserve(nb);
@@ -452,10 +491,11 @@ void IvfUsqGpu::search_batch(const float* d_q, int64_t nb, const SearchOptions& 
     w_qi8n_.reserve((size_t)nb * D_);
     w_lut_.reserve((size_t)nb * G * 16);
     launch_rotate(d_q, nb, dim_, D_, P_.p, w_qrot_.p, s);
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[3], s));
     launch_query_state(d_q, w_qrot_.p, nb, dim_, D_, rc_.p, nbits_, w_qp_.p, w_qi8p_.p, w_qi8n_.p,
                        w_lut_.p, s);
     launches += 2;
-    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[2], s));
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
     // 3. group (query, probe) pairs by list
     w_cnt_.reserve(nlist_ + 1);
     w_cursor_.reserve(nlist_ + 1);
@@ -469,7 +509,7 @@ void IvfUsqGpu::search_batch(const float* d_q, int64_t nb, const SearchOptions& 
                        kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p, w_item_off_.p,
                        w_counters_.p, w_lq_.p, w_items_.p, s);
     launches += 4;
-    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[3], s));
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[5], s));
     // 4. list scan
     const size_t slots = (size_t)nb * nprobe;
     w_slot_key_.reserve(slots * k);
@@ -520,7 +560,7 @@ void IvfUsqGpu::search_batch(const float* d_q, int64_t nb, const SearchOptions& 
     a.max_len = (int)per_warp;
     launch_scan(a, grid, s);
     launches += 1;
-    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[6], s));
     // 5. merge
     w_mkey_.reserve((size_t)nb * k);
     w_mtie_.reserve((size_t)nb * k);
@@ -552,7 +592,7 @@ void IvfUsqGpu::search_batch(const float* d_q, int64_t nb, const SearchOptions& 
     launch_merge(m, s);
     launches += 1;
     HANNS_CUDA_OK(cudaGetLastError());
-    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[5], s));
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[7], s));
     last_launches_ += launches;
 }
 
@@ -570,21 +610,21 @@ void IvfUsqGpu::search_device(const float* d_queries, int64_t nq, const SearchOp
     int64_t nb_max = std::max<int64_t>(1, (2ll << 30) / ((int64_t)nprobe * k * 16));
     nb_max = std::min<int64_t>(nb_max, 65536);
     last_launches_ = 0;
-    for (int e = 0; e < 6; ++e) stage_ms_[e] = 0;
+    for (int e = 0; e < kStages + 1; ++e) stage_ms_[e] = 0;
     for (int64_t b = 0; b < nq; b += nb_max) {
         const int64_t nb = std::min(nb_max, nq - b);
         SearchOptions o = opt;
         if (o.d_query_bitset) o.d_query_bitset += b;
         search_batch(d_queries + b * dim_, nb, o, d_ids + b * k, d_dists + b * k,
                      d_counts ? d_counts + b : nullptr, d_keys ? d_keys + b * k : nullptr, s, true);
-        HANNS_CUDA_OK(cudaEventSynchronize(ev_[5]));
+        HANNS_CUDA_OK(cudaEventSynchronize(ev_[kStages]));
         float t;
-        for (int e = 0; e < 5; ++e) {
+        for (int e = 0; e < kStages; ++e) {
             HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[e], ev_[e + 1]));
             stage_ms_[e] += t;
         }
-        HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[0], ev_[5]));
-        stage_ms_[5] += t;
+        HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[0], ev_[kStages]));
+        stage_ms_[kStages] += t;
     }
     HANNS_CUDA_OK(cudaStreamSynchronize(s));
 }

@@ -113,7 +113,8 @@ class IvfUsqGpu {
                       bool time_it);
     void set_list_layout(const std::vector<int64_t>& h_off);
     void update_centroid_norms();
-    void coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes, cudaStream_t s);
+    void coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes, cudaStream_t s,
+                       cudaEvent_t mid_event = nullptr);
 
     int dim_, D_, nbits_, nlist_, metric_, nprobe_, device_;
     uint64_t rotation_seed_;
@@ -124,6 +125,8 @@ class IvfUsqGpu {
     // device artifact (list order)
     DevBuf<float> centroids_, P_, rc_, gmean_, cn_;
     float cmax_ = 0.0f;  // max ||centroid|| (bound of the approximate coarse step)
+    DevBuf<uint16_t> cent_hi_, cent_lo_;  // bf16 split of the centroids [nlist][tc_k_]
+    int tc_k_ = 64;
     DevBuf<int64_t> list_off_, fs_blk_off_, ids_;
     DevBuf<float4> meta_;
     DevBuf<uint8_t> codes_, signs_, owned_;
@@ -150,10 +153,13 @@ class IvfUsqGpu {
     DevBuf<float> w_out_dists_;
 
     cudaStream_t stream_ = nullptr;
-    cudaEvent_t ev_[6] = {};
-    float stage_ms_[6] = {0, 0, 0, 0, 0, 0};
+    // stages: coarse GEMM, coarse select, rotate, query state, group, scan, merge; then total
+    static constexpr int kStages = 7;
+    cudaEvent_t ev_[kStages + 1] = {};
+    float stage_ms_[kStages + 1] = {};
     int64_t last_launches_ = 0;
-    DevBuf<int> w_fallbacks_;
+    DevBuf<int> w_fallbacks_;  // [0] exact fallbacks, [1] tensor-core error flag
+    DevBuf<uint16_t> w_qhi_, w_qlo_;
     int scan_grid_ = 0;
     std::mutex mu_;
 };

@@ -86,9 +86,18 @@ void launch_coarse_l2(const float* q, int64_t nq, const float* cent, int nlist, 
 void launch_select_probes(const float* dist, int64_t nq, int nlist, int nprobe, int32_t* probes,
                           uint32_t* scratch, cudaStream_t s);
 // Approximate-then-exact coarse step (same probes as the two launches above).
-void launch_coarse_fast(const float* q, int64_t nq, const float* cent, const float* cn, float cmax,
-                        int nlist, int d, int nprobe, float* approx, int32_t* probes,
-                        int* fallbacks, cudaStream_t s);
+void launch_coarse_gemm(const float* q, int64_t nq, const float* cent, const float* cn, int nlist,
+                        int d, float* approx, cudaStream_t s);
+void launch_coarse_select(float* approx, const float* q, int64_t nq, const float* cent, int nlist,
+                          int d, int nprobe, float cmax, float dot_rel, const int* tc_err,
+                          int32_t* probes, int* fallbacks, cudaStream_t s);
+// Tensor-core approximation of the coarse scores (coarse_tc.cu).
+int coarse_tc_k(int d);
+void launch_split_bf16(const float* x, int64_t rows, int d, int K, void* hi, void* lo,
+                       cudaStream_t s);
+bool launch_coarse_tc(const void* qh, const void* ql, int64_t nq, const void* ch, const void* cl,
+                      int nlist, int K, const float* cn, float* out, int* err_flag,
+                      cudaStream_t s);
 void launch_centroid_norms(const float* cent, int nlist, int d, float* cn, cudaStream_t s);
 void launch_rotate(const float* x, int64_t nq, int d, int D, const float* P, float* out,
                    cudaStream_t s);

@@ -343,80 +343,35 @@ __device__ __forceinline__ float exact_l2(const float* qs, const float* __restri
     return s;
 }
 
-// One warp per query.  `approx` rows are per-query scratch (overwritten on fallback).
-__global__ void __launch_bounds__(128) coarse_select_exact_kernel(
-    float* __restrict__ approx, const float* __restrict__ q, int64_t nq,
-    const float* __restrict__ cent, int nlist, int d, int nprobe, float cmax,
-    int32_t* __restrict__ probes, int* __restrict__ fallbacks) {
-    extern __shared__ __align__(16) float qsm[];  // [4][d]
-    __shared__ uint32_t hist[4][256];
-    __shared__ uint32_t ckey[4][kCoarseCap];
-    __shared__ int cidx[4][kCoarseCap];
-    const int w = threadIdx.x >> 5, lane = (int)lane_id();
-    const int64_t qi = (int64_t)blockIdx.x * 4 + w;
-    if (qi >= nq) return;
-    float* qs = qsm + w * d;
-    float qn = 0.0f;
-    for (int i = lane; i < d; i += 32) {
-        const float v = q[qi * d + i];
-        qs[i] = v;
-        qn = __fmaf_rn(v, v, qn);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) qn = __fadd_rn(qn, __shfl_xor_sync(0xffffffffu, qn, o));
-    __syncwarp();
-    float* row = approx + qi * nlist;
+// Rounding-error threshold of the approximate coarse step.  For every centroid c of the
+// exact top-nprobe set, a(q,c) <= threshold (derivation in the DESIGN notes):
+//   |a(q,c) - (||q-c||^2 - ||q||^2)| <= err,  E(c) <= T(c)(1+g),  T(c) <= E(c)/(1-g)
+// with g = (d + 8) 2^-24 bounding the relative error of a sequential sum of d terms.
+// dot_rel bounds |computed q.c - q.c| / sum|q_i c_i| for the GEMM that produced a(q,c).
+__device__ __forceinline__ double coarse_threshold(float tau, float qn, float cmax, int d,
+                                                   float dot_rel) {
+    const double gam = (double)(d + 8) * 5.9604644775390625e-8;
+    const double Qn = (double)qn, eQ = 2.0 * gam * Qn + 1e-30;
+    const double qnorm = sqrt(Qn) * (1.0 + 2.0 * gam);
+    const double cm = (double)cmax * (1.0 + 2.0 * gam);
+    const double err = 4.0 * (double)dot_rel * qnorm * cm + 2.0 * gam * cm * cm +
+                       2.384185791015625e-7 * (cm * cm + 2.0 * qnorm * cm) + 1e-30;
+    const double e_ub = ((double)tau + Qn + eQ + err) * (1.0 + 2.0 * gam);
+    return e_ub * (1.0 + 2.0 * gam) - Qn + eQ + err;
+}
+
+// One warp: the nprobe (<= kCoarseCap) smallest of row[0..nlist) by (total-order key,
+// index) -- the stable sort of rank_centroids -- written in order to out[].
+__device__ void warp_select_stable(const float* row, int nlist, int nprobe, uint32_t* hist,
+                                   uint32_t* sk, int* si, int32_t* out) {
+    const int lane = (int)lane_id();
     auto key_at = [&](int i, uint32_t& k) {
         k = total_order_key(row[i]);
         return true;
     };
     int less = 0;
-    const float tau = key_to_float(warp_radix_kth(nlist, nprobe, 32, key_at, hist[w], &less));
-    // rounding-error bound (all in double; u = 2^-24, gamma = (d + 8) u)
-    const double gam = (double)(d + 8) * 5.9604644775390625e-8;
-    const double Qn = (double)qn, eQ = 2.0 * gam * Qn + 1e-30;
-    const double qnorm = sqrt(Qn) * (1.0 + 2.0 * gam);
-    const double cm = (double)cmax * (1.0 + 2.0 * gam);
-    const double err = 4.0 * gam * qnorm * cm + 2.0 * gam * cm * cm +
-                       2.384185791015625e-7 * (cm * cm + 2.0 * qnorm * cm) + 1e-30;
-    const double e_ub = ((double)tau + Qn + eQ + err) * (1.0 + 2.0 * gam);
-    const double thr = e_ub * (1.0 + 2.0 * gam) - Qn + eQ + err;
-    int cnt = 0;
-    for (int base = 0; base < nlist; base += 32) {
-        const int c = base + lane;
-        const bool in = c < nlist && (double)row[c] <= thr;
-        const unsigned b = __ballot_sync(0xffffffffu, in);
-        if (in) {
-            const int pos = cnt + __popc(b & lanemask_lt());
-            if (pos < kCoarseCap) cidx[w][pos] = c;
-        }
-        cnt += __popc(b);
-    }
-    __syncwarp();
-    if (cnt <= kCoarseCap && cnt >= nprobe) {
-        for (int i = lane; i < cnt; i += 32)
-            ckey[w][i] = total_order_key(exact_l2(qs, cent + (int64_t)cidx[w][i] * d, d));
-        __syncwarp();
-        for (int i = lane; i < cnt; i += 32) {
-            const uint32_t ki = ckey[w][i];
-            const int ii = cidx[w][i];
-            int rank = 0;
-            for (int j = 0; j < cnt; ++j) {
-                const uint32_t kj = ckey[w][j];
-                rank += (kj < ki || (kj == ki && cidx[w][j] < ii)) ? 1 : 0;
-            }
-            if (rank < nprobe) probes[qi * nprobe + rank] = ii;
-        }
-        return;
-    }
-    // fallback: exact distance to every centroid, then the stable selection
-    if (lane == 0) atomicAdd(fallbacks, 1);
-    for (int c = lane; c < nlist; c += 32) row[c] = exact_l2(qs, cent + (int64_t)c * d, d);
-    __syncwarp();
-    const uint32_t ktau = warp_radix_kth(nlist, nprobe, 32, key_at, hist[w], &less);
+    const uint32_t ktau = warp_radix_kth(nlist, nprobe, 32, key_at, hist, &less);
     int taken = 0, ties_needed = nprobe - less;
-    uint32_t* sk = ckey[w];
-    int* si = cidx[w];
     for (int base = 0; base < nlist && taken < nprobe; base += 32) {
         const int i = base + lane;
         uint32_t k = 0xFFFFFFFFu;
@@ -444,8 +399,191 @@ __global__ void __launch_bounds__(128) coarse_select_exact_kernel(
         const int ia = si[a];
         int rank = 0;
         for (int b = 0; b < m; ++b) rank += (sk[b] < ka || (sk[b] == ka && si[b] < ia)) ? 1 : 0;
-        probes[qi * nprobe + rank] = ia;
+        out[rank] = ia;
     }
+    __syncwarp();
+}
+
+// One warp per query, row in global memory (any nlist).  `approx` rows are per-query
+// scratch (overwritten with exact distances on fallback).  nprobe <= kCoarseCap / 2.
+__global__ void __launch_bounds__(128) coarse_select_exact_kernel(
+    float* __restrict__ approx, const float* __restrict__ q, int64_t nq,
+    const float* __restrict__ cent, int nlist, int d, int nprobe, float cmax, float dot_rel,
+    const int* __restrict__ tc_err, int32_t* __restrict__ probes, int* __restrict__ fallbacks) {
+    extern __shared__ __align__(16) float qsm[];  // [4][d]
+    __shared__ uint32_t hist[4][256];
+    __shared__ uint32_t ckey[4][kCoarseCap];
+    __shared__ int cidx[4][kCoarseCap];
+    const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    const int64_t qi = (int64_t)blockIdx.x * 4 + w;
+    if (qi >= nq) return;
+    float* qs = qsm + w * d;
+    float* row = approx + qi * nlist;
+    float qn = 0.0f;
+    for (int i = lane; i < d; i += 32) {
+        const float v = q[qi * d + i];
+        qs[i] = v;
+        qn = __fmaf_rn(v, v, qn);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) qn = __fadd_rn(qn, __shfl_xor_sync(0xffffffffu, qn, o));
+    __syncwarp();
+    auto key_at = [&](int i, uint32_t& k) {
+        k = total_order_key(row[i]);
+        return true;
+    };
+    int less = 0;
+    const float tau = key_to_float(warp_radix_kth(nlist, nprobe, 32, key_at, hist[w], &less));
+    const double thr = coarse_threshold(tau, qn, cmax, d, dot_rel);
+    const bool approx_ok = !tc_err || *tc_err == 0;
+    int cnt = 0;
+    for (int base = 0; base < nlist; base += 32) {
+        const int c = base + lane;
+        const bool in = c < nlist && (double)row[c] <= thr;
+        const unsigned b = __ballot_sync(0xffffffffu, in);
+        if (in) {
+            const int pos = cnt + __popc(b & lanemask_lt());
+            if (pos < kCoarseCap) cidx[w][pos] = c;
+        }
+        cnt += __popc(b);
+    }
+    __syncwarp();
+    if (approx_ok && cnt <= kCoarseCap && cnt >= nprobe) {
+        for (int i = lane; i < cnt; i += 32)
+            ckey[w][i] = total_order_key(exact_l2(qs, cent + (int64_t)cidx[w][i] * d, d));
+        __syncwarp();
+        for (int i = lane; i < cnt; i += 32) {
+            const uint32_t ki = ckey[w][i];
+            const int ii = cidx[w][i];
+            int rank = 0;
+            for (int j = 0; j < cnt; ++j) {
+                const uint32_t kj = ckey[w][j];
+                rank += (kj < ki || (kj == ki && cidx[w][j] < ii)) ? 1 : 0;
+            }
+            if (rank < nprobe) probes[qi * nprobe + rank] = ii;
+        }
+        return;
+    }
+    // fallback: exact distance to every centroid, then the stable selection
+    if (lane == 0) atomicAdd(fallbacks, 1);
+    for (int c = lane; c < nlist; c += 32) row[c] = exact_l2(qs, cent + (int64_t)c * d, d);
+    __syncwarp();
+    warp_select_stable(row, nlist, nprobe, hist[w], ckey[w], cidx[w], probes + qi * nprobe);
+}
+
+// Block-wide k-th smallest total-order key of row[0..n) (256 threads).
+constexpr int kSelThreads = 256;
+
+__device__ uint32_t block_radix_kth(const float* row, int n, int kth, uint32_t* hist, int* bcast,
+                                    int* n_less) {
+    const int tid = threadIdx.x;
+    uint32_t prefix = 0, pmask = 0;
+    int remaining = kth, less = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        hist[tid] = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += kSelThreads) {
+            const uint32_t k = total_order_key(row[i]);
+            if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (tid < 32) {
+            int s = 0;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) s += (int)hist[tid * 8 + b];
+            const int incl = warp_inclusive_scan(s);
+            const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
+            const int src = __ffs(hit) - 1;
+            if (tid == src) {
+                int c = incl - s, bin = tid * 8;
+                for (int b = 0; b < 8; ++b) {
+                    const int h = (int)hist[tid * 8 + b];
+                    if (c + h >= remaining) {
+                        bin = tid * 8 + b;
+                        break;
+                    }
+                    c += h;
+                }
+                bcast[0] = bin;
+                bcast[1] = c;
+            }
+        }
+        __syncthreads();
+        const int bin = bcast[0], before = bcast[1];
+        less += before;
+        remaining -= before;
+        prefix |= (uint32_t)bin << shift;
+        pmask |= 255u << shift;
+        __syncthreads();
+    }
+    *n_less = less;
+    return prefix;
+}
+
+// One 256-thread block per query with the approximate row staged in shared memory
+// (nlist small enough); same result as coarse_select_exact_kernel.
+__global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
+    const float* __restrict__ approx, const float* __restrict__ q, int64_t nq,
+    const float* __restrict__ cent, int nlist, int d, int nprobe, float cmax, float dot_rel,
+    const int* __restrict__ tc_err, int32_t* __restrict__ probes, int* __restrict__ fallbacks) {
+    extern __shared__ __align__(16) float sm[];  // row[nlist4], qs[d]
+    __shared__ uint32_t hist[256];
+    __shared__ int bcast[4];
+    __shared__ float red[kSelThreads / 32];
+    __shared__ int cidx[kCoarseCap];
+    __shared__ uint32_t ckey[kCoarseCap];
+    __shared__ int cnt_s;
+    __shared__ double thr_s;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int64_t qi = blockIdx.x;
+    float* row = sm;
+    float* qs = sm + ((nlist + 3) & ~3);
+    const float* grow = approx + qi * nlist;
+    for (int i = tid; i < nlist; i += kSelThreads) row[i] = grow[i];
+    float qn = 0.0f;
+    for (int i = tid; i < d; i += kSelThreads) {
+        const float v = q[qi * d + i];
+        qs[i] = v;
+        qn = __fmaf_rn(v, v, qn);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) qn = __fadd_rn(qn, __shfl_xor_sync(0xffffffffu, qn, o));
+    if (lane == 0) red[w] = qn;
+    if (tid == 0) cnt_s = 0;
+    __syncthreads();
+    qn = 0.0f;
+    for (int i = 0; i < kSelThreads / 32; ++i) qn = __fadd_rn(qn, red[i]);
+    int less = 0;
+    const float tau = key_to_float(block_radix_kth(row, nlist, nprobe, hist, bcast, &less));
+    if (tid == 0) thr_s = coarse_threshold(tau, qn, cmax, d, dot_rel);
+    __syncthreads();
+    const double thr = thr_s;
+    for (int c = tid; c < nlist; c += kSelThreads) {
+        if ((double)row[c] <= thr) {
+            const int pos = atomicAdd(&cnt_s, 1);
+            if (pos < kCoarseCap) cidx[pos] = c;
+        }
+    }
+    __syncthreads();
+    const int cnt = cnt_s;
+    const bool approx_ok = !tc_err || *tc_err == 0;
+    if (approx_ok && cnt <= kCoarseCap && cnt >= nprobe) {
+        for (int i = tid; i < cnt; i += kSelThreads)
+            ckey[i] = total_order_key(exact_l2(qs, cent + (int64_t)cidx[i] * d, d));
+        __syncthreads();
+        for (int i = tid; i < cnt; i += kSelThreads) {
+            const uint32_t ki = ckey[i];
+            const int ii = cidx[i];
+            int rank = 0;
+            for (int j = 0; j < cnt; ++j) rank += (ckey[j] < ki || (ckey[j] == ki && cidx[j] < ii)) ? 1 : 0;
+            if (rank < nprobe) probes[qi * nprobe + rank] = ii;
+        }
+        return;
+    }
+    if (tid == 0) atomicAdd(fallbacks, 1);
+    for (int c = tid; c < nlist; c += kSelThreads) row[c] = exact_l2(qs, cent + (int64_t)c * d, d);
+    __syncthreads();
+    if (w == 0) warp_select_stable(row, nlist, nprobe, hist, ckey, cidx, probes + qi * nprobe);
 }
 
 __global__ void centroid_norms_kernel(const float* __restrict__ cent, int nlist, int d,
@@ -464,7 +602,9 @@ constexpr int kRotRows = 64;  // rows per CTA
 
 // q_rot[q][r] = tree16( lane j: fma chain over c = j, j+16, ... of P[r][c]*x[c] ).
 // QT queries per CTA, staged transposed in shared memory ([D][QT+4] floats) so a lane
-// reads the QT query values of one column with 16-byte loads; a half-warp owns a row.
+// reads the QT query values of one column with 16-byte loads.  A half-warp owns 4
+// consecutive rows (64 rows per CTA); lane j keeps the chain of column class j for
+// 4 rows x QT queries, so every P value and query value loaded feeds 4*QT or 4 FMAs.
 template <int QT>
 __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x, int64_t nq,
                                                      int d, int D, const float* __restrict__ P,
@@ -472,47 +612,74 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x
     constexpr int LD = QT + 4;
     extern __shared__ __align__(16) float xs[];  // [D][LD]
     const int64_t q0 = (int64_t)blockIdx.y * QT;
-    for (int e = threadIdx.x; e < QT * D; e += blockDim.x) {
-        const int t = e / D, c = e % D;
+    // fill: each thread moves 4 consecutive dims of one query (16-byte loads when d % 4 == 0)
+    const int D4 = D / 4;
+#pragma unroll 4
+    for (int e = threadIdx.x; e < QT * D4; e += blockDim.x) {
+        const int t = e / D4, c = (e - t * D4) * 4;
         const int64_t qq = q0 + t;
-        xs[c * LD + t] = (qq < nq && c < d) ? x[qq * d + c] : 0.0f;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (qq < nq) {
+            if ((d & 3) == 0) {
+                if (c < d) {
+                    const float4 f = __ldg(reinterpret_cast<const float4*>(x + qq * d + c));
+                    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (c + k < d) v[k] = x[qq * d + c + k];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xs[(c + k) * LD + t] = v[k];
     }
     __syncthreads();
     const int half = threadIdx.x >> 4, j = threadIdx.x & 15;
     const unsigned hmask = 0xFFFFu << (threadIdx.x & 16);
-    for (int rr = half; rr < kRotRows; rr += 16) {
-        const int r = blockIdx.x * kRotRows + rr;
-        if (r >= D) break;  // uniform across the half-warp
-        const float* prow = P + (int64_t)r * D;
-        float acc[QT];
+    const int rbase = blockIdx.x * kRotRows + half * 4;  // D % 64 == 0: all 4 rows exist
+    if (rbase >= D) return;
+    const float* p0 = P + (int64_t)rbase * D;
+    float acc[4][QT];
 #pragma unroll
-        for (int t = 0; t < QT; ++t) acc[t] = 0.0f;
-        for (int c = j; c < D; c += 16) {
-            const float p = __ldg(prow + c);
-            const float4* xv = reinterpret_cast<const float4*>(xs + c * LD);
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-            for (int t4 = 0; t4 < QT / 4; ++t4) {
-                const float4 v = xv[t4];
-                acc[4 * t4 + 0] = __fmaf_rn(p, v.x, acc[4 * t4 + 0]);
-                acc[4 * t4 + 1] = __fmaf_rn(p, v.y, acc[4 * t4 + 1]);
-                acc[4 * t4 + 2] = __fmaf_rn(p, v.z, acc[4 * t4 + 2]);
-                acc[4 * t4 + 3] = __fmaf_rn(p, v.w, acc[4 * t4 + 3]);
+        for (int t = 0; t < QT; ++t) acc[r][t] = 0.0f;
+#pragma unroll 4
+    for (int c = j; c < D; c += 16) {
+        float p[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) p[r] = __ldg(p0 + (int64_t)r * D + c);
+        const float4* xv = reinterpret_cast<const float4*>(xs + c * LD);
+#pragma unroll
+        for (int t4 = 0; t4 < QT / 4; ++t4) {
+            const float4 v = xv[t4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                acc[r][4 * t4 + 0] = __fmaf_rn(p[r], v.x, acc[r][4 * t4 + 0]);
+                acc[r][4 * t4 + 1] = __fmaf_rn(p[r], v.y, acc[r][4 * t4 + 1]);
+                acc[r][4 * t4 + 2] = __fmaf_rn(p[r], v.z, acc[r][4 * t4 + 2]);
+                acc[r][4 * t4 + 3] = __fmaf_rn(p[r], v.w, acc[r][4 * t4 + 3]);
             }
         }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
-            float v = acc[t];
+            float v = acc[r][t];
             v = __fadd_rn(v, __shfl_down_sync(hmask, v, 8, 16));
             v = __fadd_rn(v, __shfl_down_sync(hmask, v, 4, 16));
             v = __fadd_rn(v, __shfl_down_sync(hmask, v, 2, 16));
             v = __fadd_rn(v, __shfl_down_sync(hmask, v, 1, 16));
-            acc[t] = v;
+            acc[r][t] = v;
         }
-        if (j == 0) {
+    if (j == 0) {
 #pragma unroll
-            for (int t = 0; t < QT; ++t)
-                if (q0 + t < nq) out[(q0 + t) * D + r] = acc[t];
-        }
+        for (int t = 0; t < QT; ++t)
+            if (q0 + t < nq)
+                *reinterpret_cast<float4*>(out + (q0 + t) * D + rbase) =
+                    make_float4(acc[0][t], acc[1][t], acc[2][t], acc[3][t]);
     }
 }
 
@@ -528,18 +695,27 @@ __global__ void __launch_bounds__(128) query_state_kernel(
     const float* __restrict__ x, const float* __restrict__ q_rot, int64_t nq, int d, int D,
     const float* __restrict__ rc, int nbits, QueryParams* __restrict__ qp,
     uint8_t* __restrict__ q_i8p, int8_t* __restrict__ q_i8n, uint8_t* __restrict__ lut) {
+    // shared: rc[D], then per warp q_rot[D] and x[d]
+    extern __shared__ __align__(16) float qsh[];
     const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    float* rc_s = qsh;
+    float* r = qsh + D + w * (D + d);
+    float* xq = r + D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) rc_s[i] = rc[i];
     const int64_t qi = (int64_t)blockIdx.x * 4 + w;
-    if (qi >= nq) return;
-    const float* r = q_rot + qi * D;
-    // sequential sums (Rust Sum<f32> starts from -0.0)
+    const bool valid = qi < nq;
+    if (valid) {
+        for (int i = lane; i < D; i += 32) r[i] = q_rot[qi * D + i];
+        for (int i = lane; i < d; i += 32) xq[i] = x[qi * d + i];
+    }
+    __syncthreads();
+    if (!valid) return;
+    // sequential sums (Rust Sum<f32> starts from -0.0), from shared memory
     float cs = -0.0f, qn = -0.0f;
     if (lane == 1)
-        for (int i = 0; i < D; ++i) cs = __fadd_rn(cs, __fmul_rn(r[i], rc[i]));
-    if (lane == 2) {
-        const float* xq = x + qi * d;
+        for (int i = 0; i < D; ++i) cs = __fadd_rn(cs, __fmul_rn(r[i], rc_s[i]));
+    if (lane == 2)
         for (int i = 0; i < d; ++i) qn = __fadd_rn(qn, __fmul_rn(xq[i], xq[i]));
-    }
     cs = __shfl_sync(0xffffffffu, cs, 1);
     qn = __shfl_sync(0xffffffffu, qn, 2);
     float m = 0.0f;
@@ -571,10 +747,13 @@ __global__ void __launch_bounds__(128) query_state_kernel(
     const float lut_scale = fmaxf(__fdiv_rn(lm, 127.0f), 1e-6f);
     for (int g = lane; g < G; g += 32) {
         const float* q4 = r + 4 * g;
+        uint32_t wv[4] = {0, 0, 0, 0};
         for (int nib = 0; nib < 16; ++nib) {
             const int v = round_clamp(__fdiv_rn(lut_entry(q4, nib), lut_scale), -127.0f, 127.0f);
-            lut[qi * (int64_t)G * 16 + g * 16 + nib] = (uint8_t)(v + 128);  // offset binary
+            wv[nib >> 2] |= (uint32_t)(v + 128) << (8 * (nib & 3));  // offset binary
         }
+        *reinterpret_cast<uint4*>(lut + qi * (int64_t)G * 16 + g * 16) =
+            make_uint4(wv[0], wv[1], wv[2], wv[3]);
     }
     if (lane == 0) {
         QueryParams p;
@@ -1189,20 +1368,33 @@ void launch_select_probes(const float* dist, int64_t nq, int nlist, int nprobe, 
                                                                   scratch);
 }
 
-void launch_coarse_fast(const float* q, int64_t nq, const float* cent, const float* cn, float cmax,
-                        int nlist, int d, int nprobe, float* approx, int32_t* probes,
-                        int* fallbacks, cudaStream_t s) {
+void launch_coarse_gemm(const float* q, int64_t nq, const float* cent, const float* cn, int nlist,
+                        int d, float* approx, cudaStream_t s) {
     if (nq <= 0) return;
     dim3 grid((nlist + kGN - 1) / kGN, (unsigned)((nq + kGM - 1) / kGM));
     if ((d & 3) == 0)
         coarse_gemm_kernel<true><<<grid, 256, 0, s>>>(q, nq, cent, nlist, d, cn, approx);
     else
         coarse_gemm_kernel<false><<<grid, 256, 0, s>>>(q, nq, cent, nlist, d, cn, approx);
-    const size_t smem = (size_t)4 * d * sizeof(float);
-    cudaFuncSetAttribute(coarse_select_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         150 * 1024);
-    coarse_select_exact_kernel<<<(unsigned)((nq + 3) / 4), 128, smem, s>>>(
-        approx, q, nq, cent, nlist, d, nprobe, cmax, probes, fallbacks);
+}
+
+void launch_coarse_select(float* approx, const float* q, int64_t nq, const float* cent, int nlist,
+                          int d, int nprobe, float cmax, float dot_rel, const int* tc_err,
+                          int32_t* probes, int* fallbacks, cudaStream_t s) {
+    if (nq <= 0) return;
+    const size_t blk_bytes = ((size_t)((nlist + 3) & ~3) + d) * sizeof(float);
+    if (blk_bytes <= 96 * 1024) {
+        cudaFuncSetAttribute(coarse_select_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             100 * 1024);
+        coarse_select_block_kernel<<<(unsigned)nq, kSelThreads, blk_bytes, s>>>(
+            approx, q, nq, cent, nlist, d, nprobe, cmax, dot_rel, tc_err, probes, fallbacks);
+    } else {
+        const size_t qbytes = (size_t)4 * d * sizeof(float);
+        cudaFuncSetAttribute(coarse_select_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             180 * 1024);
+        coarse_select_exact_kernel<<<(unsigned)((nq + 3) / 4), 128, qbytes, s>>>(
+            approx, q, nq, cent, nlist, d, nprobe, cmax, dot_rel, tc_err, probes, fallbacks);
+    }
 }
 
 void launch_centroid_norms(const float* cent, int nlist, int d, float* cn, cudaStream_t s) {
@@ -1231,7 +1423,9 @@ void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, i
                         const float* rc, int nbits, QueryParams* qp, uint8_t* q_i8p,
                         int8_t* q_i8n, uint8_t* lut, cudaStream_t s) {
     if (nq <= 0) return;
-    query_state_kernel<<<(unsigned)((nq + 3) / 4), 128, 0, s>>>(x, q_rot, nq, d, D, rc, nbits, qp,
+    const size_t smem = (size_t)(D + 4 * (D + d)) * sizeof(float);
+    cudaFuncSetAttribute(query_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    query_state_kernel<<<(unsigned)((nq + 3) / 4), 128, smem, s>>>(x, q_rot, nq, d, D, rc, nbits, qp,
                                                                 q_i8p, q_i8n, lut);
 }
 

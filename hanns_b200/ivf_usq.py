@@ -222,8 +222,12 @@ class IvfUsqIndex:
             n_bitsets, d_query_bitset or None, d_ids, d_dists, d_counts or None, stream or None),
             "search_device")
 
+    STAGES = ("coarse_gemm", "coarse_select", "rotate", "query_state", "group", "scan", "merge",
+              "total")
+
     def stage_ms(self) -> np.ndarray:
-        out = np.zeros(6, np.float32)
+        """Device ms of the last search per stage (names in STAGES)."""
+        out = np.zeros(8, np.float32)
         _check(L.lib().hanns_gpu_ivf_usq_stage_ms(self._h, _p(out, L.f32p)), "stage_ms")
         return out
 

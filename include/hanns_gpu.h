@@ -228,8 +228,9 @@ int32_t hanns_gpu_ivf_usq_search_device(HannsIvfUsqHandle* h, const float* d_que
                                         int64_t n_bitsets, const int32_t* d_query_bitset,
                                         int64_t* d_ids, float* d_dists, int64_t* d_counts,
                                         void* stream);
-/* Device time (ms) of the stages of the last search: coarse, prep, items, scan, merge, total. */
-int32_t hanns_gpu_ivf_usq_stage_ms(const HannsIvfUsqHandle* h, float* out6);
+/* Device time (ms) of the stages of the last search, out8 = {coarse GEMM, coarse select,
+ * rotation, query state, list grouping, list scan, merge, total}. */
+int32_t hanns_gpu_ivf_usq_stage_ms(const HannsIvfUsqHandle* h, float* out8);
 /* Number of kernel launches of the last search. */
 int64_t hanns_gpu_ivf_usq_last_launches(const HannsIvfUsqHandle* h);
 int32_t hanns_gpu_ivf_usq_set_nprobe(HannsIvfUsqHandle* h, int32_t nprobe);

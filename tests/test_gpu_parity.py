@@ -173,7 +173,12 @@ def _empty_artifact(cent, D, nbits=4, metric=0):
                 codes=np.zeros((0, cb), np.uint8), sign_bits=np.zeros((0, D // 8), np.uint8))
 
 
-def test_coarse_fast_path_equals_exact(gpu, oracle_mod):
+@pytest.mark.parametrize("nlist,d,nprobe,normalise", [
+    (4096, 768, 32, True),     # block-per-query select (row in shared memory)
+    (40000, 64, 16, False),    # warp-per-query select (row in global memory)
+    (2048, 96, 300, True),     # nprobe > 256: exact kernels
+])
+def test_coarse_fast_path_equals_exact(gpu, oracle_mod, nlist, d, nprobe, normalise):
     """Approximate-GEMM + exact re-score coarse step == exact sequential L2 selection:
     checked against the exact kernels (static entry point) and the oracle, with 600
     duplicate centroids (exact ties, candidate sets beyond the cap -> fallback)."""
@@ -182,26 +187,30 @@ def test_coarse_fast_path_equals_exact(gpu, oracle_mod):
     from hanns_b200.ivf_usq import IvfUsqIndex
     O = oracle_mod
     rng = np.random.default_rng(5)
-    nlist, d, nprobe = 4096, 768, 32
     cent = rng.normal(size=(nlist, d)).astype(np.float32)
-    cent /= np.linalg.norm(cent, axis=1, keepdims=True)
+    if normalise:
+        cent /= np.linalg.norm(cent, axis=1, keepdims=True)
     cent[100:700] = cent[99]
-    q = rng.normal(size=(1000, d)).astype(np.float32)
-    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    nq = 1000
+    q = rng.normal(size=(nq, d)).astype(np.float32)
+    if normalise:
+        q /= np.linalg.norm(q, axis=1, keepdims=True)
     q[:50] = cent[99] + 0.01 * rng.normal(size=(50, d)).astype(np.float32)
     q[50:60] = cent[5]  # exact hits
-    art = _empty_artifact(cent, d)
+    art = _empty_artifact(cent, (d + 63) // 64 * 64)
     idx = IvfUsqIndex.from_artifact(art)
     fast = idx.debug_query(q, nprobe)["probes"]
     qt = torch.from_numpy(q).cuda()
     ct = torch.from_numpy(cent).cuda()
-    exact = torch.empty(1000, nprobe, dtype=torch.int32, device="cuda")
-    for s in range(0, 1000, 500):
-        rc = gpu.hanns_gpu_coarse_probes_static(qt[s:].data_ptr(), min(500, 1000 - s), ct.data_ptr(),
-                                                nlist, d, nprobe, exact[s:].data_ptr(), None)
+    exact = torch.empty(nq, nprobe, dtype=torch.int32, device="cuda")
+    step = max(1, ((16 << 20) - nq * nprobe * 8) // (4 * nlist) - 1)
+    for s in range(0, nq, step):
+        m = min(step, nq - s)
+        rc = gpu.hanns_gpu_coarse_probes_static(qt[s:].data_ptr(), m, ct.data_ptr(), nlist, d, nprobe,
+                                                exact[s:].data_ptr(), None)
         assert rc == 0, _lib.last_error()
     torch.cuda.synchronize()
     assert np.array_equal(fast, exact.cpu().numpy())
     oi = O.OracleIndex(art)
-    _, _, _, op = oi.search(q[:120], 5, nprobe, want_probes=True)
-    assert np.array_equal(fast[:120], op)
+    _, _, _, op = oi.search(q[:60], 5, nprobe, want_probes=True)
+    assert np.array_equal(fast[:60], op)
