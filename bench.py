@@ -348,6 +348,19 @@ def run_ours(args, w, rank, world, local_rank):
     value = nq * args.steps / (ms / 1e3)
     stages = idx.stage_ms().tolist()
     res_ids = out_ids.cpu().numpy()
+    shard_parity = None
+    if world > 1 and rank == 0:
+        # the merged multi-GPU rows must equal a single-GPU search of the whole index
+        full = IvfUsqIndex.from_artifact(art, device=local_rank)
+        f_ids = torch.empty(nq, k, dtype=torch.int64, device=dev)
+        f_d = torch.empty(nq, k, dtype=torch.float32, device=dev)
+        full.search_device(queries.data_ptr(), nq, k, nprobe, f_ids.data_ptr(), f_d.data_ptr(), 0,
+                           stream.cuda_stream)
+        shard_parity = {"queries_checked": nq,
+                        "ids_equal_rows": int((f_ids.cpu().numpy() == res_ids).all(1).sum()),
+                        "dists_bit_equal_rows": int((f_d.cpu().numpy().view(np.uint32) ==
+                                                     out_d.cpu().numpy().view(np.uint32)).all(1).sum())}
+        full.close()
 
     # ---- e2e through the host-pointer C ABI (pinned buffers), 1 GPU
     e2e = None
@@ -375,6 +388,48 @@ def run_ours(args, w, rank, world, local_rank):
                "h2d_bytes_per_step": nq * w["d"] * 4, "d2h_bytes_per_step": nq * k * 12,
                "path": "hanns_gpu_ivf_usq_search (host pointers, pinned)"}
         assert np.array_equal(h_ids.numpy(), res_ids), "e2e and device paths disagree"
+    else:
+        # every rank copies the pinned host queries in (replicated H2D), searches its
+        # shard, all-gathers and merges; rank 0 copies the merged ids/distances out
+        hq = torch.empty(nq, w["d"], dtype=torch.float32).pin_memory()
+        hq.copy_(queries.cpu())
+        h_ids = torch.empty(nq, k, dtype=torch.int64).pin_memory()
+        h_d = torch.empty(nq, k, dtype=torch.float32).pin_memory()
+        qdev = torch.empty_like(queries)
+
+        def e2e_step():
+            qdev.copy_(hq, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            rc = L.hanns_gpu_ivf_usq_search_shard_device(idx._h, qdev.data_ptr(), nq, k, nprobe,
+                                                          sh_d.data_ptr(), sh_k.data_ptr(),
+                                                          sh_i.data_ptr(), stream.cuda_stream)
+            assert rc == 0, _lib.last_error()
+            dist.all_gather_into_tensor(g_d, sh_d)
+            dist.all_gather_into_tensor(g_k, sh_k)
+            dist.all_gather_into_tensor(g_i, sh_i)
+            rc = L.hanns_gpu_merge_shards_device(g_d.data_ptr(), g_k.data_ptr(), g_i.data_ptr(), world,
+                                                 nq, k, out_ids.data_ptr(), out_d.data_ptr(),
+                                                 stream.cuda_stream)
+            assert rc == 0, _lib.last_error()
+            if rank == 0:
+                h_ids.copy_(out_ids, non_blocking=True)
+                h_d.copy_(out_d, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        el = torch.tensor([time.perf_counter() - t0], device=dev)
+        dist.all_reduce(el, op=dist.ReduceOp.MAX)
+        e2e = {"value": nq * args.steps / float(el.item()), "unit": "queries/s",
+               "h2d_bytes_per_step": nq * w["d"] * 4 * world, "d2h_bytes_per_step": nq * k * 12,
+               "path": "per rank: pinned H2D of the queries, shard search, NCCL all-gather, merge; "
+                       "rank 0 D2H (max over ranks)"}
+        if rank == 0:
+            assert np.array_equal(h_ids.numpy(), res_ids), "e2e and device paths disagree"
 
     if rank != 0:
         return
@@ -435,7 +490,7 @@ def run_ours(args, w, rank, world, local_rank):
         "config": config_block(args.workload, w, world),
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": launches[0], "clocks": clk.summary(),
-        "recall_at_k": rec, "parity_vs_oracle": parity,
+        "recall_at_k": rec, "parity_vs_oracle": parity, "parity_vs_single_gpu": shard_parity,
         "stage_ms_last_step": dict(zip(IvfUsqIndex.STAGES, stages)),
     }
     print(json.dumps(line), flush=True)

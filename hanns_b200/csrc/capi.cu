@@ -552,6 +552,12 @@ int32_t hanns_gpu_ivf_usq_search_shard_device(HannsIvfUsqHandle* h, const float*
     });
 }
 
+int32_t hanns_gpu_shard_owners(const int64_t* list_sizes, int32_t nlist, int32_t world,
+                               int32_t* owner) {
+    if (!list_sizes || !owner || nlist <= 0 || world < 1) return HANNS_INVALID_ARG;
+    return guarded([&] { hanns::shard_owners(list_sizes, nlist, world, owner); });
+}
+
 int32_t hanns_gpu_merge_shards_device(const float* d_dists, const uint64_t* d_keys,
                                       const int64_t* d_ids, int32_t world, int64_t nq, int32_t k,
                                       int64_t* d_out_ids, float* d_out_dists, void* stream) {

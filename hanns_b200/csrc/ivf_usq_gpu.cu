@@ -416,23 +416,33 @@ void IvfUsqGpu::add(const float* h_data, int64_t n, const int64_t* h_ids) {
 }
 
 // ---------------------------------------------------------------- sharding
-void IvfUsqGpu::shard(int rank, int world) {
-    DeviceGuard g(device_);
-    if (world < 1 || rank < 0 || rank >= world) throw std::invalid_argument("bad rank/world");
-    // longest-processing-time assignment of lists (by size) to ranks
-    std::vector<int> order(nlist_);
+// Longest-processing-time assignment: lists in decreasing size (ties: lower id first) go
+// to the currently least-loaded rank (ties: lower rank).  Host-only and deterministic, so
+// every rank computes the same owners.
+void shard_owners(const int64_t* sizes, int nlist, int world, int32_t* owner) {
+    std::vector<int> order(nlist);
     std::iota(order.begin(), order.end(), 0);
-    auto len = [&](int l) { return h_list_off_[l + 1] - h_list_off_[l]; };
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return len(a) > len(b); });
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int a, int b) { return sizes[a] > sizes[b]; });
     std::vector<int64_t> load(world, 0);
-    std::vector<uint8_t> owned(nlist_, 0);
     for (int l : order) {
         int best = 0;
         for (int r = 1; r < world; ++r)
             if (load[r] < load[best]) best = r;
-        load[best] += len(l);
-        owned[l] = best == rank ? 1 : 0;
+        load[best] += sizes[l];
+        owner[l] = best;
     }
+}
+
+void IvfUsqGpu::shard(int rank, int world) {
+    DeviceGuard g(device_);
+    if (world < 1 || rank < 0 || rank >= world) throw std::invalid_argument("bad rank/world");
+    std::vector<int64_t> sizes(nlist_);
+    for (int l = 0; l < nlist_; ++l) sizes[l] = h_list_off_[l + 1] - h_list_off_[l];
+    std::vector<int32_t> owner(nlist_);
+    shard_owners(sizes.data(), nlist_, world, owner.data());
+    std::vector<uint8_t> owned(nlist_, 0);
+    for (int l = 0; l < nlist_; ++l) owned[l] = owner[l] == rank ? 1 : 0;
     // keep only owned lists' rows
     std::vector<int64_t> perm, off(nlist_ + 1, 0);
     for (int l = 0; l < nlist_; ++l) {

@@ -168,4 +168,7 @@ class IvfUsqGpu {
 // src/quantization/usq/rotator.rs:15-39 with this library's own random stream.
 void rotation_matrix(uint64_t seed, int D, float* out);
 
+// List -> rank assignment used by IvfUsqGpu::shard (host only).
+void shard_owners(const int64_t* sizes, int nlist, int world, int32_t* owner);
+
 }  // namespace hanns

@@ -254,6 +254,10 @@ int32_t hanns_gpu_ivf_usq_search_shard_device(HannsIvfUsqHandle* h, const float*
                                               int64_t nq, int32_t k, int32_t nprobe,
                                               float* d_dists, uint64_t* d_keys, int64_t* d_ids,
                                               void* stream);
+/* The list -> rank owner map that hanns_gpu_ivf_usq_shard uses (host only, no GPU):
+ * lists by decreasing size, each to the least-loaded rank. */
+int32_t hanns_gpu_shard_owners(const int64_t* list_sizes, int32_t nlist, int32_t world,
+                               int32_t* owner);
 /* Merges world shard results laid out [world][nq][k] into the global top-k
  * (ties broken by key, matching the single-GPU stable order); device buffers. */
 int32_t hanns_gpu_merge_shards_device(const float* d_dists, const uint64_t* d_keys,
