@@ -598,25 +598,26 @@ __global__ void centroid_norms_kernel(const float* __restrict__ cent, int nlist,
 // ============================================================================
 // Query preparation
 // ============================================================================
-constexpr int kRotRows = 64;  // rows per CTA
 
 // q_rot[q][r] = tree16( lane j: fma chain over c = j, j+16, ... of P[r][c]*x[c] ).
 // QT queries per CTA, staged transposed in shared memory ([D][QT+4] floats) so a lane
-// reads the QT query values of one column with 16-byte loads.  A half-warp owns 4
-// consecutive rows (64 rows per CTA); lane j keeps the chain of column class j for
-// 4 rows x QT queries, so every P value and query value loaded feeds 4*QT or 4 FMAs.
-template <int QT>
+// reads the QT query values of one column with 16-byte loads.  A half-warp owns R
+// consecutive rows (16*R rows per CTA); lane j keeps the chain of column class j for
+// R rows x QT queries, so every query value loaded feeds R FMAs and every P value QT.
+template <int QT, int R>
 __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x, int64_t nq,
                                                      int d, int D, const float* __restrict__ P,
                                                      float* __restrict__ out) {
     constexpr int LD = QT + 4;
     extern __shared__ __align__(16) float xs[];  // [D][LD]
     const int64_t q0 = (int64_t)blockIdx.y * QT;
-    // fill: each thread moves 4 consecutive dims of one query (16-byte loads when d % 4 == 0)
+    // fill: each thread moves 4 consecutive dims of one query (16-byte loads when d % 4 == 0);
+    // consecutive threads take consecutive queries so the transposed stores hit
+    // consecutive banks
     const int D4 = D / 4;
 #pragma unroll 4
     for (int e = threadIdx.x; e < QT * D4; e += blockDim.x) {
-        const int t = e / D4, c = (e - t * D4) * 4;
+        const int t = e % QT, c = (e / QT) * 4;
         const int64_t qq = q0 + t;
         float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (qq < nq) {
@@ -637,25 +638,25 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x
     __syncthreads();
     const int half = threadIdx.x >> 4, j = threadIdx.x & 15;
     const unsigned hmask = 0xFFFFu << (threadIdx.x & 16);
-    const int rbase = blockIdx.x * kRotRows + half * 4;  // D % 64 == 0: all 4 rows exist
-    if (rbase >= D) return;
+    const int rbase = blockIdx.x * (16 * R) + half * R;
+    if (rbase >= D) return;  // D % 64 == 0 and R divides 64: all R rows exist
     const float* p0 = P + (int64_t)rbase * D;
-    float acc[4][QT];
+    float acc[R][QT];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int t = 0; t < QT; ++t) acc[r][t] = 0.0f;
-#pragma unroll 4
+#pragma unroll 2
     for (int c = j; c < D; c += 16) {
-        float p[4];
+        float p[R];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) p[r] = __ldg(p0 + (int64_t)r * D + c);
+        for (int r = 0; r < R; ++r) p[r] = __ldg(p0 + (int64_t)r * D + c);
         const float4* xv = reinterpret_cast<const float4*>(xs + c * LD);
 #pragma unroll
         for (int t4 = 0; t4 < QT / 4; ++t4) {
             const float4 v = xv[t4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
+            for (int r = 0; r < R; ++r) {
                 acc[r][4 * t4 + 0] = __fmaf_rn(p[r], v.x, acc[r][4 * t4 + 0]);
                 acc[r][4 * t4 + 1] = __fmaf_rn(p[r], v.y, acc[r][4 * t4 + 1]);
                 acc[r][4 * t4 + 2] = __fmaf_rn(p[r], v.z, acc[r][4 * t4 + 2]);
@@ -664,7 +665,7 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x
         }
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
             float v = acc[r][t];
@@ -678,8 +679,10 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x
 #pragma unroll
         for (int t = 0; t < QT; ++t)
             if (q0 + t < nq)
-                *reinterpret_cast<float4*>(out + (q0 + t) * D + rbase) =
-                    make_float4(acc[0][t], acc[1][t], acc[2][t], acc[3][t]);
+#pragma unroll
+                for (int r4 = 0; r4 < R; r4 += 4)
+                    *reinterpret_cast<float4*>(out + (q0 + t) * D + rbase + r4) =
+                        make_float4(acc[r4][t], acc[r4 + 1][t], acc[r4 + 2][t], acc[r4 + 3][t]);
     }
 }
 
@@ -873,6 +876,7 @@ __device__ __forceinline__ int int_ip_row(const uint8_t* __restrict__ code, cons
     if (nbits == 8) {
         const uint4* c4 = reinterpret_cast<const uint4*>(code);
         const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+#pragma unroll 4
         for (int i = 0; i < D / 16; ++i) {
             const uint4 c = __ldg(c4 + i);
             const uint4 qv = q4[i];
@@ -884,6 +888,7 @@ __device__ __forceinline__ int int_ip_row(const uint8_t* __restrict__ code, cons
     } else {  // nbits == 4: 16 code bytes = 32 dims; q layout (even, odd) per 8 dims
         const uint4* c4 = reinterpret_cast<const uint4*>(code);
         const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+#pragma unroll 4
         for (int i = 0; i < D / 32; ++i) {
             const uint4 c = __ldg(c4 + i);
             const uint4 qa = q4[2 * i], qb = q4[2 * i + 1];
@@ -949,19 +954,32 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
             if (use_fs) {
                 for (int sub = 0; sub * 4 < nq_here; ++sub) {
                     // interleave 4 queries' offset-binary LUTs: word g*16+nib = q0|q1<<8|q2<<16|q3<<24
-                    for (int e = tid; e < a.G * 16; e += kScanThreads) {
-                        uint32_t wv = 0;
+                    // (16 LUT bytes of each query per thread, 4x4 byte transposes with PRMT)
+                    for (int m = tid; m < a.G; m += kScanThreads) {
+                        uint4 L[4];
 #pragma unroll
                         for (int t = 0; t < 4; ++t) {
                             const int qq = qg + sub * 4 + t;
-                            uint32_t b = 128u;
+                            L[t] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
                             if (qq < it.z) {
                                 const int qidx = a.lq[it.y + qq].x;
-                                b = a.lut[(int64_t)qidx * a.G * 16 + e];
+                                L[t] = __ldg(reinterpret_cast<const uint4*>(a.lut + (int64_t)qidx * a.G * 16) + m);
                             }
-                            wv |= b << (8 * t);
                         }
-                        lut4[e] = wv;
+                        const uint32_t w0[4] = {L[0].x, L[0].y, L[0].z, L[0].w};
+                        const uint32_t w1[4] = {L[1].x, L[1].y, L[1].z, L[1].w};
+                        const uint32_t w2[4] = {L[2].x, L[2].y, L[2].z, L[2].w};
+                        const uint32_t w3[4] = {L[3].x, L[3].y, L[3].z, L[3].w};
+                        uint4* dst = reinterpret_cast<uint4*>(lut4 + m * 16);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t t0 = __byte_perm(w0[i], w1[i], 0x5140);
+                            const uint32_t t1 = __byte_perm(w2[i], w3[i], 0x5140);
+                            const uint32_t t2 = __byte_perm(w0[i], w1[i], 0x7362);
+                            const uint32_t t3 = __byte_perm(w2[i], w3[i], 0x7362);
+                            dst[i] = make_uint4(__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632),
+                                                __byte_perm(t2, t3, 0x5410), __byte_perm(t2, t3, 0x7632));
+                        }
                     }
                     __syncthreads();
                     for (int v = tid; v < n; v += kScanThreads) {
@@ -969,23 +987,32 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                         const uint2* src = fsb + (int64_t)blk * a.nchunks * 32 + slot;
                         uint32_t acc02 = 0, acc13 = 0;
                         int tot0 = 0, tot1 = 0, tot2 = 0, tot3 = 0;
-                        for (int c = 0; c < a.nchunks; ++c) {
-                            const uint2 wd = __ldg(src + c * 32);
-                            const uint32_t* lrow = lut4 + c * 256;
+                        for (int c0 = 0; c0 < a.nchunks; c0 += 4) {
+                            uint2 wds[4];
 #pragma unroll
-                            for (int j = 0; j < 16; ++j) {
-                                const uint32_t word = j < 8 ? wd.x : wd.y;
-                                const uint32_t nib = (word >> (4 * (j & 7))) & 15u;
-                                const uint32_t e = lrow[j * 16 + nib];
-                                acc02 += e & 0x00FF00FFu;
-                                acc13 += (e >> 8) & 0x00FF00FFu;
-                            }
-                            if ((c & 15) == 15) {
-                                tot0 += (int)(acc02 & 0xFFFFu);
-                                tot2 += (int)(acc02 >> 16);
-                                tot1 += (int)(acc13 & 0xFFFFu);
-                                tot3 += (int)(acc13 >> 16);
-                                acc02 = acc13 = 0;
+                            for (int u = 0; u < 4; ++u)
+                                wds[u] = c0 + u < a.nchunks ? __ldg(src + (c0 + u) * 32) : make_uint2(0u, 0u);
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int c = c0 + u;
+                                if (c >= a.nchunks) break;
+                                const uint2 wd = wds[u];
+                                const uint32_t* lrow = lut4 + c * 256;
+#pragma unroll
+                                for (int j = 0; j < 16; ++j) {
+                                    const uint32_t word = j < 8 ? wd.x : wd.y;
+                                    const uint32_t nib = (word >> (4 * (j & 7))) & 15u;
+                                    const uint32_t e = lrow[j * 16 + nib];
+                                    acc02 += e & 0x00FF00FFu;
+                                    acc13 += (e >> 8) & 0x00FF00FFu;
+                                }
+                                if ((c & 15) == 15) {
+                                    tot0 += (int)(acc02 & 0xFFFFu);
+                                    tot2 += (int)(acc02 >> 16);
+                                    tot1 += (int)(acc13 & 0xFFFFu);
+                                    tot3 += (int)(acc13 >> 16);
+                                    acc02 = acc13 = 0;
+                                }
                             }
                         }
                         tot0 += (int)(acc02 & 0xFFFFu);
@@ -1404,19 +1431,11 @@ void launch_centroid_norms(const float* cent, int nlist, int d, float* cn, cudaS
 void launch_rotate(const float* x, int64_t nq, int d, int D, const float* P, float* out,
                    cudaStream_t s) {
     if (nq <= 0) return;
-    if (D <= 1536 && nq > 8) {
-        constexpr int QT = 16;
-        const size_t smem = (size_t)D * (QT + 4) * sizeof(float);
-        cudaFuncSetAttribute(rotate_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        dim3 grid((D + kRotRows - 1) / kRotRows, (unsigned)((nq + QT - 1) / QT));
-        rotate_kernel<QT><<<grid, 256, smem, s>>>(x, nq, d, D, P, out);
-    } else {
-        constexpr int QT = 8;
-        const size_t smem = (size_t)D * (QT + 4) * sizeof(float);
-        cudaFuncSetAttribute(rotate_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        dim3 grid((D + kRotRows - 1) / kRotRows, (unsigned)((nq + QT - 1) / QT));
-        rotate_kernel<QT><<<grid, 256, smem, s>>>(x, nq, d, D, P, out);
-    }
+    constexpr int QT = 8, R = 8;
+    const size_t smem = (size_t)D * (QT + 4) * sizeof(float);
+    cudaFuncSetAttribute(rotate_kernel<QT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    dim3 grid((D + 16 * R - 1) / (16 * R), (unsigned)((nq + QT - 1) / QT));
+    rotate_kernel<QT, R><<<grid, 256, smem, s>>>(x, nq, d, D, P, out);
 }
 
 void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, int D,
