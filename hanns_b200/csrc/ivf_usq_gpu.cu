@@ -69,13 +69,20 @@ IvfUsqGpu::~IvfUsqGpu() {
     cudaSetDevice(device_);
     for (auto& e : ev_)
         if (e) cudaEventDestroy(e);
+    for (auto& e : ev_up_)
+        if (e) cudaEventDestroy(e);
+    if (ev_ready_) cudaEventDestroy(ev_ready_);
+    if (copy_stream_) cudaStreamDestroy(copy_stream_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
 void IvfUsqGpu::ensure_stream() {
     if (!stream_) {
         HANNS_CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+        HANNS_CUDA_OK(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
         for (auto& e : ev_) HANNS_CUDA_OK(cudaEventCreate(&e));
+        for (auto& e : ev_up_) HANNS_CUDA_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_ready_, cudaEventDisableTiming));
     }
 }
 
@@ -134,8 +141,9 @@ void IvfUsqGpu::update_centroid_norms() {
 
 // Probes of nb device queries: approximate scores (tcgen05 bf16x3 GEMM, or the FP32 SIMT
 // GEMM) + exact re-score, in chunks bounded by the approximation matrix (1 GiB).
-void IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes,
-                              cudaStream_t s, cudaEvent_t mid_event) {
+int64_t IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes,
+                                  cudaStream_t s, cudaEvent_t mid_event) {
+    int64_t launches = 0;
     const int64_t cchunk = std::max<int64_t>(1, std::min<int64_t>(nb, (1ll << 28) / nlist_));
     w_dist_.reserve((size_t)cchunk * nlist_);
     w_fallbacks_.reserve(2);
@@ -147,8 +155,9 @@ void IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t*
             launch_coarse_l2(d_q + c * dim_, m, centroids_.p, nlist_, dim_, w_dist_.p, s);
             if (mid_event && c == 0) HANNS_CUDA_OK(cudaEventRecord(mid_event, s));
             launch_select_probes(w_dist_.p, m, nlist_, nprobe, d_probes + c * nprobe, w_sel_.p, s);
+            launches += 2;
         }
-        return;
+        return launches;
     }
     const char* mode = std::getenv("HANNS_GPU_COARSE");
     bool tc = !(mode && std::strcmp(mode, "simt") == 0);
@@ -171,6 +180,7 @@ void IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t*
             used_tc = launch_coarse_tc(w_qhi_.p, w_qlo_.p, m, cent_hi_.p, cent_lo_.p, nlist_, tc_k_,
                                        cn_.p, w_dist_.p, w_fallbacks_.p + 1, s);
             tc = used_tc;
+            launches += used_tc ? 2 : 1;
         }
         if (!used_tc)
             launch_coarse_gemm(d_q + c * dim_, m, centroids_.p, cn_.p, nlist_, dim_, w_dist_.p, s);
@@ -178,7 +188,9 @@ void IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t*
         launch_coarse_select(w_dist_.p, d_q + c * dim_, m, centroids_.p, nlist_, dim_, nprobe, cmax_,
                              used_tc ? rel_tc : rel_simt, used_tc ? w_fallbacks_.p + 1 : nullptr,
                              d_probes + c * nprobe, w_fallbacks_.p, s);
+        launches += used_tc ? 1 : 2;
     }
+    return launches;
 }
 
 void IvfUsqGpu::upload_rotation_centroid() {
@@ -480,31 +492,58 @@ void IvfUsqGpu::shard(int rank, int world) {
 }
 
 // ---------------------------------------------------------------- search
-void IvfUsqGpu::search_batch(const float* d_q, int64_t nb, const SearchOptions& opt,
-                             int64_t* d_ids, float* d_dists, int64_t* d_counts, uint64_t* d_keys,
-                             cudaStream_t s, bool time_it) {
+void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
+                             const SearchOptions& opt, int64_t* d_ids, float* d_dists,
+                             int64_t* d_counts, uint64_t* d_keys, cudaStream_t s, bool time_it) {
     const int k = std::max(opt.k, 1);
     const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
     const int G = D_ / 4;
     int64_t launches = 0;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[0], s));
-    // 1. coarse probes
+    // 1-2. per-query stages: coarse probes, rotation, query state.  Host queries are uploaded
+    // in up to kMaxUploadChunks chunks on copy_stream_; chunk c's per-query stages wait only
+    // for chunk c's copy, so the copy of chunk c+1 runs under them.
     w_probes_.reserve((size_t)nb * nprobe);
     w_sel_.reserve((size_t)nb * 2 * nprobe);
-    coarse_probes(d_q, nb, nprobe, w_probes_.p, s, time_it ? ev_[1] : nullptr);
-    launches += 3 * ((nb + ((1ll << 28) / nlist_) - 1) / std::max<int64_t>(1, (1ll << 28) / nlist_));
-    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[2], s));
-    // 2. query state
     w_qrot_.reserve((size_t)nb * D_);
     w_qp_.reserve(nb);
     w_qi8p_.reserve((size_t)nb * D_);
     w_qi8n_.reserve((size_t)nb * D_);
     w_lut_.reserve((size_t)nb * G * 16);
-    launch_rotate(d_q, nb, dim_, D_, P_.p, w_qrot_.p, s);
-    if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[3], s));
-    launch_query_state(d_q, w_qrot_.p, nb, dim_, D_, rc_.p, nbits_, w_qp_.p, w_qi8p_.p, w_qi8n_.p,
-                       w_lut_.p, s);
-    launches += 2;
+    int nchunks = 1;
+    if (h_q) nchunks = (int)std::min<int64_t>(kMaxUploadChunks, std::max<int64_t>(1, nb / 2048));
+    const int64_t per = (nb + nchunks - 1) / nchunks;
+    if (h_q) {
+        HANNS_CUDA_OK(cudaEventRecord(ev_ready_, s));
+        HANNS_CUDA_OK(cudaStreamWaitEvent(copy_stream_, ev_ready_, 0));
+        for (int c = 0; c < nchunks; ++c) {
+            const int64_t q0 = c * per, m = std::min(per, nb - q0);
+            if (m <= 0) break;
+            HANNS_CUDA_OK(cudaMemcpyAsync(const_cast<float*>(d_q) + q0 * dim_, h_q + q0 * dim_,
+                                          sizeof(float) * m * dim_, cudaMemcpyHostToDevice,
+                                          copy_stream_));
+            HANNS_CUDA_OK(cudaEventRecord(ev_up_[c], copy_stream_));
+        }
+    }
+    const bool per_stage = time_it && nchunks == 1;
+    for (int c = 0; c < nchunks; ++c) {
+        const int64_t q0 = c * per, m = std::min(per, nb - q0);
+        if (m <= 0) break;
+        const float* q = d_q + q0 * dim_;
+        if (h_q) HANNS_CUDA_OK(cudaStreamWaitEvent(s, ev_up_[c], 0));
+        launches += coarse_probes(q, m, nprobe, w_probes_.p + q0 * nprobe, s,
+                                  per_stage ? ev_[1] : nullptr);
+        if (per_stage) HANNS_CUDA_OK(cudaEventRecord(ev_[2], s));
+        launch_rotate(q, m, dim_, D_, P_.p, w_qrot_.p + q0 * D_, s);
+        if (per_stage) HANNS_CUDA_OK(cudaEventRecord(ev_[3], s));
+        launch_query_state(q, w_qrot_.p + q0 * D_, m, dim_, D_, rc_.p, nbits_, w_qp_.p + q0,
+                           w_qi8p_.p + q0 * D_, w_qi8n_.p + q0 * D_, w_lut_.p + q0 * G * 16, s);
+        launches += 2;
+    }
+    if (time_it && !per_stage) {
+        // chunked upload: the first stage spans upload + all per-query stages
+        for (int e = 1; e <= 3; ++e) HANNS_CUDA_OK(cudaEventRecord(ev_[e], s));
+    }
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
     // 3. group (query, probe) pairs by list
     w_cnt_.reserve(nlist_ + 1);
@@ -610,6 +649,12 @@ void IvfUsqGpu::search_device(const float* d_queries, int64_t nq, const SearchOp
                               int64_t* d_ids, float* d_dists, int64_t* d_counts, uint64_t* d_keys,
                               cudaStream_t stream) {
     DeviceGuard g(device_);
+    run_search(d_queries, nullptr, nq, opt, d_ids, d_dists, d_counts, d_keys, stream);
+}
+
+void IvfUsqGpu::run_search(const float* d_queries, const float* h_queries, int64_t nq,
+                           const SearchOptions& opt, int64_t* d_ids, float* d_dists,
+                           int64_t* d_counts, uint64_t* d_keys, cudaStream_t stream) {
     if (!trained_) throw std::invalid_argument("index not trained");
     check_supported();
     if (nq <= 0) throw std::invalid_argument("query dimension mismatch");
@@ -625,8 +670,9 @@ void IvfUsqGpu::search_device(const float* d_queries, int64_t nq, const SearchOp
         const int64_t nb = std::min(nb_max, nq - b);
         SearchOptions o = opt;
         if (o.d_query_bitset) o.d_query_bitset += b;
-        search_batch(d_queries + b * dim_, nb, o, d_ids + b * k, d_dists + b * k,
-                     d_counts ? d_counts + b : nullptr, d_keys ? d_keys + b * k : nullptr, s, true);
+        search_batch(d_queries + b * dim_, h_queries ? h_queries + b * dim_ : nullptr, nb, o,
+                     d_ids + b * k, d_dists + b * k, d_counts ? d_counts + b : nullptr,
+                     d_keys ? d_keys + b * k : nullptr, s, true);
         HANNS_CUDA_OK(cudaEventSynchronize(ev_[kStages]));
         float t;
         for (int e = 0; e < kStages; ++e) {
@@ -646,7 +692,9 @@ void IvfUsqGpu::search_host(const float* h_queries, int64_t nq, const SearchOpti
     SearchOptions opt = opt_in;
     const int k = std::max(opt.k, 1);
     opt.k = k;
-    h2d(w_pad_queries_, h_queries, (size_t)nq * dim_, stream_);
+    if (!trained_) throw std::invalid_argument("index not trained");
+    if (nq <= 0) throw std::invalid_argument("query dimension mismatch");
+    w_pad_queries_.reserve((size_t)nq * dim_);
     if (h_bitsets && opt.n_bitsets > 0 && opt.filter_mode != 0) {
         const size_t words = (size_t)((opt.bitset_len + 63) / 64) * opt.n_bitsets;
         h2d(w_bits_, h_bitsets, words, stream_);
@@ -665,8 +713,8 @@ void IvfUsqGpu::search_host(const float* h_queries, int64_t nq, const SearchOpti
     w_out_ids_.reserve((size_t)nq * k);
     w_out_dists_.reserve((size_t)nq * k);
     w_out_counts_.reserve((size_t)nq);
-    search_device(w_pad_queries_.p, nq, opt, w_out_ids_.p, w_out_dists_.p, w_out_counts_.p, nullptr,
-                  stream_);
+    run_search(w_pad_queries_.p, h_queries, nq, opt, w_out_ids_.p, w_out_dists_.p, w_out_counts_.p,
+               nullptr, stream_);
     HANNS_CUDA_OK(cudaMemcpyAsync(h_ids, w_out_ids_.p, sizeof(int64_t) * nq * k,
                                   cudaMemcpyDeviceToHost, stream_));
     HANNS_CUDA_OK(cudaMemcpyAsync(h_dists, w_out_dists_.p, sizeof(float) * nq * k,

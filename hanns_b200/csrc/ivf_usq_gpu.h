@@ -108,13 +108,19 @@ class IvfUsqGpu {
     void upload_rotation_centroid();
     void rebuild_fastscan();
     void ensure_stream();
-    void search_batch(const float* d_q, int64_t nb, const SearchOptions& opt, int64_t* d_ids,
-                      float* d_dists, int64_t* d_counts, uint64_t* d_keys, cudaStream_t s,
-                      bool time_it);
+    // d_q: device query rows.  h_q (nullable): host rows to upload into d_q first, in chunks
+    // on copy_stream_ that overlap the per-query stages of the preceding chunk.
+    void search_batch(const float* d_q, const float* h_q, int64_t nb, const SearchOptions& opt,
+                      int64_t* d_ids, float* d_dists, int64_t* d_counts, uint64_t* d_keys,
+                      cudaStream_t s, bool time_it);
+    void run_search(const float* d_queries, const float* h_queries, int64_t nq,
+                    const SearchOptions& opt, int64_t* d_ids, float* d_dists, int64_t* d_counts,
+                    uint64_t* d_keys, cudaStream_t stream);
     void set_list_layout(const std::vector<int64_t>& h_off);
     void update_centroid_norms();
-    void coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes, cudaStream_t s,
-                       cudaEvent_t mid_event = nullptr);
+    // returns the number of kernels launched
+    int64_t coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes,
+                          cudaStream_t s, cudaEvent_t mid_event = nullptr);
 
     int dim_, D_, nbits_, nlist_, metric_, nprobe_, device_;
     uint64_t rotation_seed_;
@@ -153,6 +159,10 @@ class IvfUsqGpu {
     DevBuf<float> w_out_dists_;
 
     cudaStream_t stream_ = nullptr;
+    cudaStream_t copy_stream_ = nullptr;  // host->device query upload
+    static constexpr int kMaxUploadChunks = 8;
+    cudaEvent_t ev_up_[kMaxUploadChunks] = {};
+    cudaEvent_t ev_ready_ = nullptr;  // copy_stream_ waits for earlier work on the search stream
     // stages: coarse GEMM, coarse select, rotate, query state, group, scan, merge; then total
     static constexpr int kStages = 7;
     cudaEvent_t ev_[kStages + 1] = {};

@@ -139,6 +139,32 @@ def test_search_bit_exact_larger(gpu, oracle_mod, nbits, metric, k, d):
     assert bits_eq(r.distances.reshape(exp_ids.shape), exp_d)
 
 
+def test_host_search_chunked_upload(gpu, oracle_mod):
+    """Host-pointer search of 9000 queries: the upload runs in 4 chunks on the copy stream,
+    each chunk's per-query stages waiting only for its own copy.  Equal to the oracle and
+    to the device-pointer path."""
+    import torch
+    from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
+    from tests.golden.make_golden import mixture
+    O = oracle_mod
+    rng = np.random.default_rng(77)
+    d, k, nprobe = 96, 10, 5
+    x, _ = mixture(rng, 20000, d, 32, 0.4, False)
+    q, _ = mixture(rng, 9000, d, 32, 0.4, False)
+    art = O.build_artifact(x, 40, 4, O.METRIC_L2, rotation_seed=4, kmeans_iters=5, kmeans_seed=2)
+    e_ids, e_d, _ = O.OracleIndex(art).search(q, k, nprobe)
+    idx = IvfUsqIndex.from_artifact(art)
+    r = idx.search(q, SearchRequest(top_k=k, nprobe=nprobe))
+    assert np.array_equal(r.ids.reshape(e_ids.shape), e_ids)
+    assert bits_eq(r.distances.reshape(e_ids.shape), e_d)
+    dq = torch.from_numpy(q).cuda()
+    ids = torch.empty(q.shape[0], k, dtype=torch.int64, device="cuda")
+    dist = torch.empty(q.shape[0], k, dtype=torch.float32, device="cuda")
+    idx.search_device(dq.data_ptr(), q.shape[0], k, nprobe, ids.data_ptr(), dist.data_ptr())
+    assert np.array_equal(ids.cpu().numpy(), e_ids)
+    assert bits_eq(dist.cpu().numpy(), e_d)
+
+
 def test_empty_and_tiny_index(gpu, oracle_mod):
     """Lists of 0, 1, 31, 32, 33 rows; k larger than everything probed."""
     from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
