@@ -47,6 +47,15 @@ constexpr int kQueriesPerItem = 32;
 
 }  // namespace
 
+// Entries of one query's candidate region: the probes' min(|list|, n_cand) summed is at
+// most nprobe * min(n_cand, longest list) and at most the index size.
+int64_t IvfUsqGpu::cand_stride(int nprobe, int k) const {
+    const int64_t per = std::min<int64_t>(n_candidates(nbits_, k), std::max(max_list_, 1));
+    const int64_t st = std::max<int64_t>(1, std::min<int64_t>((int64_t)nprobe * per, std::max<int64_t>(ntotal_, 1)));
+    if (st > (int64_t)INT32_MAX) throw std::invalid_argument("nprobe x candidates per probe too large");
+    return st;
+}
+
 IvfUsqGpu::IvfUsqGpu(int dim, int nlist, int nbits, int metric, uint64_t rotation_seed, int nprobe,
                      int device)
     : dim_(dim), nbits_(nbits), nlist_(nlist), metric_(metric), device_(device),
@@ -557,20 +566,20 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     launch_group_pairs(w_probes_.p, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr,
                        kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p, w_item_off_.p,
                        w_counters_.p, w_lq_.p, w_items_.p, s);
-    launches += 4;
+    const int n_cand = (int)n_candidates(nbits_, k);
+    const int64_t q_stride = cand_stride(nprobe, k);
+    w_pair_off_.reserve((size_t)nb * (nprobe + 1));
+    launch_pair_offsets(w_probes_.p, nb, nprobe, list_off_.p, nlist_, sharded_ ? owned_.p : nullptr,
+                        n_cand, w_pair_off_.p, s);
+    launches += 5;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[5], s));
-    // 4. list scan
-    const size_t slots = (size_t)nb * nprobe;
-    w_slot_key_.reserve(slots * k);
-    w_slot_tie_.reserve(slots * k);
-    w_slot_cnt_.reserve(slots);
-    HANNS_CUDA_OK(cudaMemsetAsync(w_slot_cnt_.p, 0, slots * sizeof(int), s));
+    // 4. list scan: kept candidates of every (query, probe) pair with their distance keys
+    w_cand_key_.reserve((size_t)nb * q_stride);
+    w_cand_tie_.reserve((size_t)nb * q_stride);
     if (!scan_grid_) scan_grid_ = scan_grid_size(D_);
     const int grid = scan_grid_;
     const size_t per_warp = (size_t)max_list_;
     w_scores_.reserve((size_t)grid * 8 * per_warp);
-    w_cand_key_.reserve((size_t)grid * 8 * per_warp);
-    w_cand_tie_.reserve((size_t)grid * 8 * per_warp);
     ScanArgs a{};
     a.D = D_;
     a.nbits = nbits_;
@@ -592,7 +601,7 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     a.n_items = w_counters_.p;
     a.item_counter = w_counters_.p + 1;
     a.k = k;
-    a.n_cand = (int)n_candidates(nbits_, k);
+    a.n_cand = n_cand;
     a.nprobe = nprobe;
     a.fused = opt.filter_mode == 2 ? 1 : 0;
     a.bitsets = opt.d_bitsets;
@@ -600,12 +609,11 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     a.bitset_words = (opt.bitset_len + 63) / 64;
     a.n_bitsets = opt.d_bitsets ? opt.n_bitsets : 0;
     a.query_bitset = opt.d_query_bitset;
-    a.out_key = w_slot_key_.p;
-    a.out_tie = w_slot_tie_.p;
-    a.out_cnt = w_slot_cnt_.p;
-    a.scores = w_scores_.p;
+    a.pair_off = w_pair_off_.p;
+    a.q_stride = q_stride;
     a.cand_key = w_cand_key_.p;
     a.cand_tie = w_cand_tie_.p;
+    a.scores = w_scores_.p;
     a.max_len = (int)per_warp;
     launch_scan(a, grid, s);
     launches += 1;
@@ -618,9 +626,10 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     m.nprobe = nprobe;
     m.k = k;
     m.nlist = nlist_;
-    m.slot_key = w_slot_key_.p;
-    m.slot_tie = w_slot_tie_.p;
-    m.slot_cnt = w_slot_cnt_.p;
+    m.cand_key = w_cand_key_.p;
+    m.cand_tie = w_cand_tie_.p;
+    m.pair_off = w_pair_off_.p;
+    m.q_stride = q_stride;
     m.probes = w_probes_.p;
     m.list_off = list_off_.p;
     m.ids = ids_.p;
@@ -661,8 +670,8 @@ void IvfUsqGpu::run_search(const float* d_queries, const float* h_queries, int64
     cudaStream_t s = stream ? stream : stream_;
     const int k = std::max(opt.k, 1);
     const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
-    // batch size bounded by the per-(query, probe) slot memory (~2 GiB)
-    int64_t nb_max = std::max<int64_t>(1, (2ll << 30) / ((int64_t)nprobe * k * 16));
+    // batch size bounded by the candidate regions (12 bytes per entry, ~4 GiB per batch)
+    int64_t nb_max = std::max<int64_t>(1, (4ll << 30) / (cand_stride(nprobe, k) * 12));
     nb_max = std::min<int64_t>(nb_max, 65536);
     last_launches_ = 0;
     for (int e = 0; e < kStages + 1; ++e) stage_ms_[e] = 0;

@@ -117,6 +117,7 @@ class IvfUsqGpu {
                     const SearchOptions& opt, int64_t* d_ids, float* d_dists, int64_t* d_counts,
                     uint64_t* d_keys, cudaStream_t stream);
     void set_list_layout(const std::vector<int64_t>& h_off);
+    int64_t cand_stride(int nprobe, int k) const;
     void update_centroid_norms();
     // returns the number of kernels launched
     int64_t coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes,
@@ -143,15 +144,15 @@ class IvfUsqGpu {
 
     // search workspace
     DevBuf<float> w_dist_, w_qrot_, w_pad_queries_;
-    DevBuf<uint32_t> w_sel_, w_slot_key_, w_mkey_;
+    DevBuf<uint32_t> w_sel_, w_mkey_;
     DevBuf<int32_t> w_probes_;
     DevBuf<QueryParams> w_qp_;
     DevBuf<uint8_t> w_qi8p_, w_lut_;
     DevBuf<int8_t> w_qi8n_;
-    DevBuf<int> w_cnt_, w_cursor_, w_lq_off_, w_item_off_, w_counters_, w_slot_cnt_;
+    DevBuf<int> w_cnt_, w_cursor_, w_lq_off_, w_item_off_, w_counters_, w_pair_off_;
     DevBuf<int2> w_lq_;
     DevBuf<int4> w_items_;
-    DevBuf<uint64_t> w_slot_tie_, w_mtie_, w_cand_tie_, w_bits_;
+    DevBuf<uint64_t> w_mtie_, w_cand_tie_, w_bits_;
     DevBuf<int16_t> w_scores_;
     DevBuf<uint32_t> w_cand_key_;
     DevBuf<int32_t> w_qbits_;

@@ -43,23 +43,25 @@ struct ScanArgs {
     const uint64_t* bitsets;
     int64_t bitset_len, bitset_words, n_bitsets;
     const int32_t* query_bitset;
-    // outputs: per (query, probe) slot
-    uint32_t* out_key;
-    uint64_t* out_tie;
-    int* out_cnt;
-    // scratch (per CTA / per warp)
-    int16_t* scores;
+    // outputs: every kept candidate of a (query, probe) pair, at
+    // cand_*[q * q_stride + pair_off[q * (nprobe + 1) + rank] + j]; tie = rank << 48 |
+    // FastScan key << 32 | list position; unused entries hold key ~0u, tie ~0ull
+    const int* pair_off;
+    int64_t q_stride;
     uint32_t* cand_key;
     uint64_t* cand_tie;
+    // FastScan scores scratch: per CTA, kScanWarps rows of max_len
+    int16_t* scores;
     int max_len;
 };
 
 struct MergeArgs {
     int64_t nq;
     int nprobe, k, nlist;
-    const uint32_t* slot_key;
-    const uint64_t* slot_tie;
-    const int* slot_cnt;
+    const uint32_t* cand_key;  // candidate regions written by the list scan
+    const uint64_t* cand_tie;
+    const int* pair_off;
+    int64_t q_stride;
     const int32_t* probes;
     const int64_t* list_off;
     const int64_t* ids;
@@ -107,6 +109,11 @@ void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, i
 void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist,
                         const uint8_t* owned, int qpi, int* cnt, int* cursor, int* lq_off,
                         int* item_off, int* n_items, int2* lq, int4* items, cudaStream_t s);
+// pair_off[q][r] = sum over earlier probes of min(|list|, n_cand) (0 for lists this
+// index does not own); pair_off[q][nprobe] = the query's candidate total
+void launch_pair_offsets(const int32_t* probes, int64_t nq, int nprobe, const int64_t* list_off,
+                         int nlist, const uint8_t* owned, int n_cand, int* pair_off,
+                         cudaStream_t s);
 size_t scan_smem_bytes(int D);
 int scan_grid_size(int D);
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s);

@@ -855,53 +855,90 @@ __global__ void make_items_kernel(const int* __restrict__ cnt, const int* __rest
     }
 }
 
+// Candidate region of each (query, probe) pair: min(|list|, n_cand) entries (0 for lists
+// this index does not own), laid out in probe order.
+__global__ void pair_offsets_kernel(const int32_t* __restrict__ probes, int64_t nq, int nprobe,
+                                    const int64_t* __restrict__ list_off, int nlist,
+                                    const uint8_t* __restrict__ owned, int n_cand,
+                                    int* __restrict__ pair_off) {
+    const int lane = (int)lane_id();
+    const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (q >= nq) return;
+    int carry = 0;
+    for (int r0 = 0; r0 < nprobe; r0 += 32) {
+        const int r = r0 + lane;
+        int cap = 0;
+        if (r < nprobe) {
+            const int l = probes[q * nprobe + r];
+            if (l >= 0 && l < nlist && (!owned || owned[l]))
+                cap = (int)min(list_off[l + 1] - list_off[l], (int64_t)n_cand);
+        }
+        const int inc = warp_inclusive_scan(cap);
+        if (r < nprobe) pair_off[q * (nprobe + 1) + r] = carry + inc - cap;
+        carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) pair_off[q * (nprobe + 1) + nprobe] = carry;
+}
+
 // ============================================================================
-// List scan: FastScan + exact kept set + integer rerank + per-(query, probe) top-k
+// List scan: FastScan + exact kept set + integer rerank.  Every kept candidate of a
+// (query, probe) pair is written with its distance key to the query's candidate
+// region; the top-k is taken once per query over all probes by the merge.
 // ============================================================================
 constexpr int kScanThreads = 256;
 constexpr int kScanWarps = kScanThreads / 32;  // queries handled concurrently
 
 struct ScanSmem {
     uint32_t hist[kScanWarps][256];
+    int64_t base[kScanWarps];  // candidate region of each warp's (query, probe) pair
+    int nc[kScanWarps];        // kept candidates of each warp's pair
     int item;
     int pad[3];  // keeps the dynamic arrays after it 16-byte aligned
 };
 
 __device__ __forceinline__ int32_t wrap16(int32_t v) { return (int32_t)(int16_t)v; }
 
-// Integer dot of one stored vector with the warp's quantised query (shared memory).
-__device__ __forceinline__ int int_ip_row(const uint8_t* __restrict__ code, const uint8_t* qs,
-                                          int D, int nbits) {
-    int acc = 0;
-    if (nbits == 8) {
+// Integer dot of one stored vector with one quantised query (dp4a layout), by the 8
+// lanes of a group (lane bits 0-2 = sub); every lane of the warp must call it.  The
+// sum is exact, so the split into lanes does not change it.  Groups with active ==
+// false contribute nothing and read nothing.
+__device__ __forceinline__ int int_ip_group8(const uint8_t* __restrict__ code,
+                                             const uint8_t* __restrict__ q, int D, int nbits,
+                                             int sub, bool active) {
+    int acc0 = 0, acc1 = 0;
+    if (active) {
         const uint4* c4 = reinterpret_cast<const uint4*>(code);
-        const uint4* q4 = reinterpret_cast<const uint4*>(qs);
-#pragma unroll 4
-        for (int i = 0; i < D / 16; ++i) {
-            const uint4 c = __ldg(c4 + i);
-            const uint4 qv = q4[i];
-            acc = dp4a_us(c.x, qv.x, acc);
-            acc = dp4a_us(c.y, qv.y, acc);
-            acc = dp4a_us(c.z, qv.z, acc);
-            acc = dp4a_us(c.w, qv.w, acc);
-        }
-    } else {  // nbits == 4: 16 code bytes = 32 dims; q layout (even, odd) per 8 dims
-        const uint4* c4 = reinterpret_cast<const uint4*>(code);
-        const uint4* q4 = reinterpret_cast<const uint4*>(qs);
-#pragma unroll 4
-        for (int i = 0; i < D / 32; ++i) {
-            const uint4 c = __ldg(c4 + i);
-            const uint4 qa = q4[2 * i], qb = q4[2 * i + 1];
-            acc = dp4a_us(c.x & 0x0F0F0F0Fu, qa.x, acc);
-            acc = dp4a_us((c.x >> 4) & 0x0F0F0F0Fu, qa.y, acc);
-            acc = dp4a_us(c.y & 0x0F0F0F0Fu, qa.z, acc);
-            acc = dp4a_us((c.y >> 4) & 0x0F0F0F0Fu, qa.w, acc);
-            acc = dp4a_us(c.z & 0x0F0F0F0Fu, qb.x, acc);
-            acc = dp4a_us((c.z >> 4) & 0x0F0F0F0Fu, qb.y, acc);
-            acc = dp4a_us(c.w & 0x0F0F0F0Fu, qb.z, acc);
-            acc = dp4a_us((c.w >> 4) & 0x0F0F0F0Fu, qb.w, acc);
+        const uint4* q4 = reinterpret_cast<const uint4*>(q);
+        if (nbits == 8) {
+#pragma unroll 2
+            for (int i = sub; i < D / 16; i += 8) {
+                const uint4 c = __ldg(c4 + i);
+                const uint4 qv = __ldg(q4 + i);
+                acc0 = dp4a_us(c.x, qv.x, acc0);
+                acc1 = dp4a_us(c.y, qv.y, acc1);
+                acc0 = dp4a_us(c.z, qv.z, acc0);
+                acc1 = dp4a_us(c.w, qv.w, acc1);
+            }
+        } else {  // nbits == 4: 16 code bytes = 32 dims; q layout (even, odd) per 8 dims
+#pragma unroll 2
+            for (int i = sub; i < D / 32; i += 8) {
+                const uint4 c = __ldg(c4 + i);
+                const uint4 qa = __ldg(q4 + 2 * i), qb = __ldg(q4 + 2 * i + 1);
+                acc0 = dp4a_us(c.x & 0x0F0F0F0Fu, qa.x, acc0);
+                acc1 = dp4a_us((c.x >> 4) & 0x0F0F0F0Fu, qa.y, acc1);
+                acc0 = dp4a_us(c.y & 0x0F0F0F0Fu, qa.z, acc0);
+                acc1 = dp4a_us((c.y >> 4) & 0x0F0F0F0Fu, qa.w, acc1);
+                acc0 = dp4a_us(c.z & 0x0F0F0F0Fu, qb.x, acc0);
+                acc1 = dp4a_us((c.z >> 4) & 0x0F0F0F0Fu, qb.y, acc1);
+                acc0 = dp4a_us(c.w & 0x0F0F0F0Fu, qb.z, acc0);
+                acc1 = dp4a_us((c.w >> 4) & 0x0F0F0F0Fu, qb.w, acc1);
+            }
         }
     }
+    int acc = acc0 + acc1;
+    acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     return acc;
 }
 
@@ -924,17 +961,21 @@ __device__ __forceinline__ float rerank_distance(int iip, float4 m, const QueryP
     return l2 ? __fsub_rn(__fadd_rn(p.q_norm_sq, m.y), __fmul_rn(2.0f, score)) : -score;
 }
 
+__device__ __forceinline__ const uint64_t* query_bitset_words(const ScanArgs& a, int q) {
+    if (!a.fused || !a.bitsets) return nullptr;
+    const int b = a.query_bitset ? a.query_bitset[q] : 0;
+    return (b >= 0 && b < a.n_bitsets) ? a.bitsets + (int64_t)b * a.bitset_words : nullptr;
+}
+
 __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ScanSmem& sm = *reinterpret_cast<ScanSmem*>(smem_raw);
     uint32_t* lut4 = reinterpret_cast<uint32_t*>(smem_raw + sizeof(ScanSmem));  // [G*16]
-    uint8_t* qi8_s = reinterpret_cast<uint8_t*>(lut4 + a.G * 16);              // [warps][D]
     const int tid = threadIdx.x, w = tid >> 5, lane = (int)lane_id();
-    const int64_t slot_base = (int64_t)blockIdx.x * kScanWarps + w;
+    const int grp = lane >> 3, sub = lane & 7;  // 4 groups of 8 lanes per warp
     int16_t* my_scores_base = a.scores + (int64_t)blockIdx.x * kScanWarps * a.max_len;
-    uint64_t* my_tie = a.cand_tie + slot_base * a.max_len;
-    uint32_t* my_key = a.cand_key + slot_base * a.max_len;
     const bool l2 = a.metric_l2 != 0;
+    const int pstride = a.nprobe + 1;
 
     for (;;) {
         if (tid == 0) sm.item = atomicAdd(a.item_counter, 1);
@@ -946,103 +987,127 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
         const int l = it.x;
         const int64_t beg = a.list_off[l];
         const int n = (int)(a.list_off[l + 1] - beg);
-        const bool use_fs = n > a.n_cand;
+        if (n <= a.n_cand) {
+            // no FastScan: every live row is a candidate of every query of the item;
+            // (query, row) pairs spread over the CTA's 8-lane groups
+            const int total = it.z * n;
+            for (int e0 = w * 4; e0 < total; e0 += kScanWarps * 4) {
+                const int e = e0 + grp;
+                const bool act = e < total;
+                int v = 0, q = 0, rank = 0;
+                if (act) {
+                    const int i = e / n;
+                    v = e - i * n;
+                    const int2 pr = a.lq[it.y + i];
+                    q = pr.x;
+                    rank = pr.y;
+                }
+                const int64_t row = beg + v;
+                bool dead = false;
+                float4 m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (act) {
+                    const uint64_t* bw = query_bitset_words(a, q);
+                    dead = bw && bit_filtered(bw, a.bitset_len, a.ids[row]);
+                    m = __ldg(a.meta + row);
+                }
+                const int iip = int_ip_group8(a.codes + row * a.code_bytes, a.q_i8p + (int64_t)q * a.D,
+                                              a.D, a.nbits, sub, act && !dead && m.w > 1e-12f);
+                if (act && sub == 0) {
+                    const int64_t dst = (int64_t)q * a.q_stride + a.pair_off[(int64_t)q * pstride + rank] + v;
+                    if (dead) {
+                        a.cand_key[dst] = 0xFFFFFFFFu;
+                        a.cand_tie[dst] = ~0ull;
+                    } else {
+                        a.cand_key[dst] = total_order_key(rerank_distance(iip, m, a.qp[q], a.nbits, l2));
+                        a.cand_tie[dst] = ((uint64_t)rank << 48) | (uint32_t)v;
+                    }
+                }
+            }
+            continue;
+        }
         const uint2* fsb = a.fs + a.fs_blk_off[l] * (int64_t)a.nchunks * 32;
-
         for (int qg = 0; qg < it.z; qg += kScanWarps) {
             const int nq_here = min(kScanWarps, it.z - qg);
-            if (use_fs) {
-                for (int sub = 0; sub * 4 < nq_here; ++sub) {
-                    // interleave 4 queries' offset-binary LUTs: word g*16+nib = q0|q1<<8|q2<<16|q3<<24
-                    // (16 LUT bytes of each query per thread, 4x4 byte transposes with PRMT)
-                    for (int m = tid; m < a.G; m += kScanThreads) {
-                        uint4 L[4];
+            for (int quad = 0; quad * 4 < nq_here; ++quad) {
+                // interleave 4 queries' offset-binary LUTs: word g*16+nib = q0|q1<<8|q2<<16|q3<<24
+                // (16 LUT bytes of each query per thread, 4x4 byte transposes with PRMT)
+                for (int m = tid; m < a.G; m += kScanThreads) {
+                    uint4 L[4];
 #pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            const int qq = qg + sub * 4 + t;
-                            L[t] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
-                            if (qq < it.z) {
-                                const int qidx = a.lq[it.y + qq].x;
-                                L[t] = __ldg(reinterpret_cast<const uint4*>(a.lut + (int64_t)qidx * a.G * 16) + m);
-                            }
-                        }
-                        const uint32_t w0[4] = {L[0].x, L[0].y, L[0].z, L[0].w};
-                        const uint32_t w1[4] = {L[1].x, L[1].y, L[1].z, L[1].w};
-                        const uint32_t w2[4] = {L[2].x, L[2].y, L[2].z, L[2].w};
-                        const uint32_t w3[4] = {L[3].x, L[3].y, L[3].z, L[3].w};
-                        uint4* dst = reinterpret_cast<uint4*>(lut4 + m * 16);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const uint32_t t0 = __byte_perm(w0[i], w1[i], 0x5140);
-                            const uint32_t t1 = __byte_perm(w2[i], w3[i], 0x5140);
-                            const uint32_t t2 = __byte_perm(w0[i], w1[i], 0x7362);
-                            const uint32_t t3 = __byte_perm(w2[i], w3[i], 0x7362);
-                            dst[i] = make_uint4(__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632),
-                                                __byte_perm(t2, t3, 0x5410), __byte_perm(t2, t3, 0x7632));
+                    for (int t = 0; t < 4; ++t) {
+                        const int qq = qg + quad * 4 + t;
+                        L[t] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+                        if (qq < it.z) {
+                            const int qidx = a.lq[it.y + qq].x;
+                            L[t] = __ldg(reinterpret_cast<const uint4*>(a.lut + (int64_t)qidx * a.G * 16) + m);
                         }
                     }
-                    __syncthreads();
-                    for (int v = tid; v < n; v += kScanThreads) {
-                        const int blk = v >> 5, slot = v & 31;
-                        const uint2* src = fsb + (int64_t)blk * a.nchunks * 32 + slot;
-                        uint32_t acc02 = 0, acc13 = 0;
-                        int tot0 = 0, tot1 = 0, tot2 = 0, tot3 = 0;
-                        for (int c0 = 0; c0 < a.nchunks; c0 += 4) {
-                            uint2 wds[4];
+                    const uint32_t w0[4] = {L[0].x, L[0].y, L[0].z, L[0].w};
+                    const uint32_t w1[4] = {L[1].x, L[1].y, L[1].z, L[1].w};
+                    const uint32_t w2[4] = {L[2].x, L[2].y, L[2].z, L[2].w};
+                    const uint32_t w3[4] = {L[3].x, L[3].y, L[3].z, L[3].w};
+                    uint4* dst = reinterpret_cast<uint4*>(lut4 + m * 16);
 #pragma unroll
-                            for (int u = 0; u < 4; ++u)
-                                wds[u] = c0 + u < a.nchunks ? __ldg(src + (c0 + u) * 32) : make_uint2(0u, 0u);
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const int c = c0 + u;
-                                if (c >= a.nchunks) break;
-                                const uint2 wd = wds[u];
-                                const uint32_t* lrow = lut4 + c * 256;
-#pragma unroll
-                                for (int j = 0; j < 16; ++j) {
-                                    const uint32_t word = j < 8 ? wd.x : wd.y;
-                                    const uint32_t nib = (word >> (4 * (j & 7))) & 15u;
-                                    const uint32_t e = lrow[j * 16 + nib];
-                                    acc02 += e & 0x00FF00FFu;
-                                    acc13 += (e >> 8) & 0x00FF00FFu;
-                                }
-                                if ((c & 15) == 15) {
-                                    tot0 += (int)(acc02 & 0xFFFFu);
-                                    tot2 += (int)(acc02 >> 16);
-                                    tot1 += (int)(acc13 & 0xFFFFu);
-                                    tot3 += (int)(acc13 >> 16);
-                                    acc02 = acc13 = 0;
-                                }
-                            }
-                        }
-                        tot0 += (int)(acc02 & 0xFFFFu);
-                        tot2 += (int)(acc02 >> 16);
-                        tot1 += (int)(acc13 & 0xFFFFu);
-                        tot3 += (int)(acc13 >> 16);
-                        const int bias = 128 * a.G;
-                        int16_t* srow = my_scores_base + (int64_t)(sub * 4) * a.max_len;
-                        srow[v] = (int16_t)wrap16(tot0 - bias);
-                        srow[a.max_len + v] = (int16_t)wrap16(tot1 - bias);
-                        srow[2 * (int64_t)a.max_len + v] = (int16_t)wrap16(tot2 - bias);
-                        srow[3 * (int64_t)a.max_len + v] = (int16_t)wrap16(tot3 - bias);
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t t0 = __byte_perm(w0[i], w1[i], 0x5140);
+                        const uint32_t t1 = __byte_perm(w2[i], w3[i], 0x5140);
+                        const uint32_t t2 = __byte_perm(w0[i], w1[i], 0x7362);
+                        const uint32_t t3 = __byte_perm(w2[i], w3[i], 0x7362);
+                        dst[i] = make_uint4(__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632),
+                                            __byte_perm(t2, t3, 0x5410), __byte_perm(t2, t3, 0x7632));
                     }
-                    __syncthreads();
                 }
+                __syncthreads();
+                for (int v = tid; v < n; v += kScanThreads) {
+                    const int blk = v >> 5, slot = v & 31;
+                    const uint2* src = fsb + (int64_t)blk * a.nchunks * 32 + slot;
+                    uint32_t acc02 = 0, acc13 = 0;
+                    int tot0 = 0, tot1 = 0, tot2 = 0, tot3 = 0;
+                    for (int c0 = 0; c0 < a.nchunks; c0 += 4) {
+                        uint2 wds[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            wds[u] = c0 + u < a.nchunks ? __ldg(src + (c0 + u) * 32) : make_uint2(0u, 0u);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int c = c0 + u;
+                            if (c >= a.nchunks) break;
+                            const uint2 wd = wds[u];
+                            const uint32_t* lrow = lut4 + c * 256;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const uint32_t word = j < 8 ? wd.x : wd.y;
+                                const uint32_t nib = (word >> (4 * (j & 7))) & 15u;
+                                const uint32_t e = lrow[j * 16 + nib];
+                                acc02 += e & 0x00FF00FFu;
+                                acc13 += (e >> 8) & 0x00FF00FFu;
+                            }
+                            if ((c & 15) == 15) {
+                                tot0 += (int)(acc02 & 0xFFFFu);
+                                tot2 += (int)(acc02 >> 16);
+                                tot1 += (int)(acc13 & 0xFFFFu);
+                                tot3 += (int)(acc13 >> 16);
+                                acc02 = acc13 = 0;
+                            }
+                        }
+                    }
+                    tot0 += (int)(acc02 & 0xFFFFu);
+                    tot2 += (int)(acc02 >> 16);
+                    tot1 += (int)(acc13 & 0xFFFFu);
+                    tot3 += (int)(acc13 >> 16);
+                    const int bias = 128 * a.G;
+                    int16_t* srow = my_scores_base + (int64_t)(quad * 4) * a.max_len;
+                    srow[v] = (int16_t)wrap16(tot0 - bias);
+                    srow[a.max_len + v] = (int16_t)wrap16(tot1 - bias);
+                    srow[2 * (int64_t)a.max_len + v] = (int16_t)wrap16(tot2 - bias);
+                    srow[3 * (int64_t)a.max_len + v] = (int16_t)wrap16(tot3 - bias);
+                }
+                __syncthreads();
             }
             if (w < nq_here) {
                 const int2 pr = a.lq[it.y + qg + w];
                 const int q = pr.x, rank = pr.y;
-                const QueryParams p = a.qp[q];
-                // stage the quantised query
-                uint8_t* qs = qi8_s + w * a.D;
-                for (int i = lane * 16; i < a.D; i += 32 * 16)
-                    *reinterpret_cast<uint4*>(qs + i) =
-                        *reinterpret_cast<const uint4*>(a.q_i8p + (int64_t)q * a.D + i);
-                const uint64_t* bw = nullptr;
-                if (a.fused && a.bitsets) {
-                    const int b = a.query_bitset ? a.query_bitset[q] : 0;
-                    if (b >= 0 && b < a.n_bitsets) bw = a.bitsets + (int64_t)b * a.bitset_words;
-                }
+                const uint64_t* bw = query_bitset_words(a, q);
                 auto live = [&](int v) {
                     return !bw || !bit_filtered(bw, a.bitset_len, a.ids[beg + v]);
                 };
@@ -1053,8 +1118,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                     n_live = warp_sum(c);
                 }
                 const int16_t* sc = my_scores_base + (int64_t)w * a.max_len;
-                int n_c = 0;  // candidates written to my_tie
-                if (use_fs && n_live > a.n_cand) {
+                const int64_t rbase = (int64_t)q * a.q_stride + a.pair_off[(int64_t)q * pstride + rank];
+                uint64_t* my_tie = a.cand_tie + rbase;
+                const uint64_t rank_bits = (uint64_t)rank << 48;
+                int n_c = 0;  // kept candidates written to my_tie
+                if (n_live > a.n_cand) {
                     // s* = n_cand-th largest score among live rows (key = 32767 - score)
                     auto key_at = [&](int v, uint32_t& k) {
                         if (!live(v)) return false;
@@ -1098,7 +1166,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                         const unsigned bk = __ballot_sync(0xffffffffu, keep);
                         if (keep) {
                             const int pos = n_c + __popc(bk & lanemask_lt());
-                            my_tie[pos] = ((uint64_t)k << 32) | (uint32_t)v;
+                            if (pos < a.n_cand) my_tie[pos] = rank_bits | ((uint64_t)k << 32) | (uint32_t)v;
                         }
                         n_c += __popc(bk);
                         eq_seen += __popc(beq);
@@ -1108,75 +1176,44 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                         const int v = base + lane;
                         const bool keep = v < n && live(v);
                         const unsigned bk = __ballot_sync(0xffffffffu, keep);
-                        if (keep) my_tie[n_c + __popc(bk & lanemask_lt())] = (uint32_t)v;
+                        if (keep) my_tie[n_c + __popc(bk & lanemask_lt())] = rank_bits | (uint32_t)v;
                         n_c += __popc(bk);
                     }
                 }
-                __syncwarp();
-                // integer rerank of the kept candidates
-                for (int i = lane; i < n_c; i += 32) {
-                    const uint32_t v = (uint32_t)my_tie[i];
-                    const int64_t row = beg + v;
-                    const float4 m = __ldg(a.meta + row);
-                    int iip = 0;
-                    if (m.w > 1e-12f) iip = int_ip_row(a.codes + row * a.code_bytes, qs, a.D, a.nbits);
-                    my_key[i] = total_order_key(rerank_distance(iip, m, p, a.nbits, l2));
+                n_c = min(n_c, a.n_cand);  // the kept set has exactly n_cand rows
+                // unused entries of the pair's region (rows removed by the filter)
+                for (int j = n_c + lane; j < a.n_cand; j += 32) {
+                    my_tie[j] = ~0ull;
+                    a.cand_key[rbase + j] = 0xFFFFFFFFu;
                 }
-                __syncwarp();
-                // top-k of (dist, fastscan key, index) into the (query, probe) slot
-                const int64_t slot = (int64_t)q * a.nprobe + rank;
-                uint32_t* ok = a.out_key + slot * a.k;
-                uint64_t* ot = a.out_tie + slot * a.k;
-                if (n_c <= a.k) {
-                    for (int i = lane; i < n_c; i += 32) {
-                        ok[i] = my_key[i];
-                        ot[i] = my_tie[i];
-                    }
-                    if (lane == 0) a.out_cnt[slot] = n_c;
-                } else {
-                    auto kk = [&](int i, uint32_t& key) {
-                        key = my_key[i];
-                        return true;
-                    };
-                    int less = 0;
-                    const uint32_t tau = warp_radix_kth(n_c, a.k, 32, kk, sm.hist[w], &less);
-                    int written = 0;
-                    for (int base = 0; base < n_c; base += 32) {
-                        const int i = base + lane;
-                        const bool lt = i < n_c && my_key[i] < tau;
-                        const unsigned bl = __ballot_sync(0xffffffffu, lt);
-                        if (lt) {
-                            const int pos = written + __popc(bl & lanemask_lt());
-                            ok[pos] = my_key[i];
-                            ot[pos] = my_tie[i];
-                        }
-                        written += __popc(bl);
-                    }
-                    // ties at tau: chosen in increasing (fastscan key, index) order
-                    uint64_t floor_t = 0;
-                    bool have_floor = false;
-                    while (written < a.k) {
-                        uint64_t best = ~0ull;
-                        for (int i = lane; i < n_c; i += 32) {
-                            const uint64_t t = my_tie[i];
-                            if (my_key[i] == tau && (!have_floor || t > floor_t) && t < best) best = t;
-                        }
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) {
-                            const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
-                            best = ob < best ? ob : best;
-                        }
-                        if (lane == 0) {
-                            ok[written] = tau;
-                            ot[written] = best;
-                        }
-                        floor_t = best;
-                        have_floor = true;
-                        ++written;
-                    }
-                    if (lane == 0) a.out_cnt[slot] = a.k;
+                if (lane == 0) {
+                    sm.base[w] = rbase;
+                    sm.nc[w] = n_c;
                 }
-                __syncwarp();
+            }
+            __syncthreads();
+            // integer rerank of the group's kept candidates, 4 per warp at a time
+            const int total = nq_here * a.n_cand;
+            for (int e0 = w * 4; e0 < total; e0 += kScanWarps * 4) {
+                const int e = e0 + grp;
+                int i = 0, j = 0;
+                if (e < total) {
+                    i = e / a.n_cand;
+                    j = e - i * a.n_cand;
+                }
+                const bool act = e < total && j < sm.nc[i];
+                const int q = a.lq[it.y + qg + i].x;
+                uint32_t v = 0;
+                float4 m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (act) {
+                    v = (uint32_t)a.cand_tie[sm.base[i] + j];  // written by this CTA: coherent load
+                    m = __ldg(a.meta + beg + v);
+                }
+                const int64_t row = beg + v;
+                const int iip = int_ip_group8(a.codes + row * a.code_bytes, a.q_i8p + (int64_t)q * a.D,
+                                              a.D, a.nbits, sub, act && m.w > 1e-12f);
+                if (act && sub == 0)
+                    a.cand_key[sm.base[i] + j] = total_order_key(rerank_distance(iip, m, a.qp[q], a.nbits, l2));
             }
             __syncthreads();
         }
@@ -1184,25 +1221,24 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
 }
 
 // ============================================================================
-// Final merge: per query (one warp) top-k over nprobe slots.
+// Final merge: per query (one warp) top-k over all kept candidates of its probes,
+// ordered by (distance key, probe rank, FastScan key, list position).
 // ============================================================================
 __global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
     __shared__ uint32_t hist[4][256];
     const int w = threadIdx.x >> 5, lane = (int)lane_id();
     const int64_t q = (int64_t)blockIdx.x * 4 + w;
     if (q >= a.nq) return;
-    const int total = a.nprobe * a.k;
-    const uint32_t* keys = a.slot_key + q * total;
-    const uint64_t* ties = a.slot_tie + q * total;
-    const int* cnts = a.slot_cnt + q * a.nprobe;
-    auto valid_at = [&](int e) { return (e % a.k) < cnts[e / a.k]; };
+    const int total = a.pair_off[q * (a.nprobe + 1) + a.nprobe];
+    const uint32_t* keys = a.cand_key + q * a.q_stride;
+    const uint64_t* ties = a.cand_tie + q * a.q_stride;
     auto key_at = [&](int e, uint32_t& k) {
-        if (!valid_at(e)) return false;
+        if (ties[e] == ~0ull) return false;
         k = keys[e];
         return true;
     };
     int n_valid = 0;
-    for (int r = lane; r < a.nprobe; r += 32) n_valid += cnts[r];
+    for (int e = lane; e < total; e += 32) n_valid += ties[e] != ~0ull ? 1 : 0;
     n_valid = warp_sum(n_valid);
     const int take = min(a.k, n_valid);
     uint32_t* sk = a.sel_key + q * a.k;
@@ -1221,7 +1257,7 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
             if (lt) {
                 const int pos = written + __popc(bl & lanemask_lt());
                 sk[pos] = k;
-                st[pos] = ((uint64_t)(e / a.k) << 48) | ties[e];
+                st[pos] = ties[e];
             }
             written += __popc(bl);
         }
@@ -1233,7 +1269,7 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
             for (int e = lane; e < total; e += 32) {
                 uint32_t k;
                 if (key_at(e, k) && k == tau) {
-                    const uint64_t t = ((uint64_t)(e / a.k) << 48) | ties[e];
+                    const uint64_t t = ties[e];
                     if ((!have_floor || t > floor_t) && t < best) best = t;
                 }
             }
@@ -1462,7 +1498,7 @@ void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist
 }
 
 size_t scan_smem_bytes(int D) {
-    return sizeof(ScanSmem) + (size_t)(D / 4) * 16 * sizeof(uint32_t) + (size_t)kScanWarps * D;
+    return sizeof(ScanSmem) + (size_t)(D / 4) * 16 * sizeof(uint32_t);
 }
 
 int scan_grid_size(int D) {
@@ -1475,6 +1511,14 @@ int scan_grid_size(int D) {
         per_sm < 1)
         per_sm = 1;
     return sms * per_sm;
+}
+
+void launch_pair_offsets(const int32_t* probes, int64_t nq, int nprobe, const int64_t* list_off,
+                         int nlist, const uint8_t* owned, int n_cand, int* pair_off,
+                         cudaStream_t s) {
+    if (nq <= 0) return;
+    pair_offsets_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(probes, nq, nprobe, list_off, nlist,
+                                                                owned, n_cand, pair_off);
 }
 
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s) {
