@@ -23,9 +23,9 @@ LIB = os.path.join(OUT_DIR, "libhanns_gpu.so")
 OBJ_DIR = os.path.join(HERE, "_build")
 
 CU_SOURCES = ["search_kernels.cu", "build_kernels.cu", "ivf_usq_gpu.cu", "capi.cu",
-              "coarse_static.cu", "coarse_tc.cu"]
+              "coarse_static.cu", "coarse_tc.cu", "scan_tc.cu"]
 CPP_SOURCES = ["rotation.cpp"]
-HEADERS = ["common.cuh", "kernels.h", "ivf_usq_gpu.h"]
+HEADERS = ["common.cuh", "kernels.h", "ivf_usq_gpu.h", "warp_select.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -49,6 +49,65 @@ struct QueryParams {
     int32_t pad[3];
 };
 
+// score_with_meta + distance, in the reference's operation order
+// (src/quantization/usq/quantizer.rs:274-288, src/faiss/ivf_usq.rs:581-593).
+__device__ __forceinline__ float rerank_distance(int iip, float4 m, const QueryParams& p, int nbits,
+                                                 bool l2) {
+    // m = {norm, norm_sq, vmax, quant_quality}
+    float score;
+    if (m.w <= 1e-12f) {
+        score = p.centroid_score;
+    } else {
+        const float levels = (float)(1u << nbits);
+        const float code_scale = __fdiv_rn(__fmul_rn(2.0f, m.z), fmaxf(levels, 1.0f));
+        const float offset = -m.z;
+        const float ip = __fmul_rn(
+            p.q_scale, __fadd_rn(__fmul_rn(code_scale, __int2float_rn(iip)),
+                                 __fmul_rn(offset, __int2float_rn(p.q_i8_sum))));
+        score = __fadd_rn(p.centroid_score, __fdiv_rn(__fmul_rn(m.x, ip), m.w));
+    }
+    return l2 ? __fsub_rn(__fadd_rn(p.q_norm_sq, m.y), __fmul_rn(2.0f, score)) : -score;
+}
+
+// Packed two-lane fp32 arithmetic of sm_100 (add/sub/mul/fma .rn.f32x2): each lane is
+// rounded exactly like the scalar instruction, one instruction serves two lanes.
+__device__ __forceinline__ float2 sub2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
 }  // namespace hanns
 
 #define HANNS_CUDA_OK(expr)                                                             \

@@ -81,6 +81,12 @@ IvfUsqGpu::~IvfUsqGpu() {
     for (auto& e : ev_up_)
         if (e) cudaEventDestroy(e);
     if (ev_ready_) cudaEventDestroy(ev_ready_);
+    if (ev_fork_) cudaEventDestroy(ev_fork_);
+    if (ev_join_) cudaEventDestroy(ev_join_);
+    for (auto& e : ev_aux_)
+        if (e) cudaEventDestroy(e);
+    if (aux_stream_) cudaStreamDestroy(aux_stream_);
+    if (h_scan_err_) cudaFreeHost(h_scan_err_);
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -89,9 +95,17 @@ void IvfUsqGpu::ensure_stream() {
     if (!stream_) {
         HANNS_CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
         HANNS_CUDA_OK(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+        HANNS_CUDA_OK(cudaStreamCreateWithFlags(&aux_stream_, cudaStreamNonBlocking));
+        HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
+        HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming));
+        for (auto& e : ev_aux_) HANNS_CUDA_OK(cudaEventCreate(&e));
         for (auto& e : ev_) HANNS_CUDA_OK(cudaEventCreate(&e));
         for (auto& e : ev_up_) HANNS_CUDA_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_ready_, cudaEventDisableTiming));
+        HANNS_CUDA_OK(cudaHostAlloc(reinterpret_cast<void**>(&h_scan_err_), sizeof(int),
+                                    cudaHostAllocDefault));
+        *h_scan_err_ = 0;
+        HANNS_CUDA_OK(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, device_));
     }
 }
 
@@ -534,24 +548,42 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
             HANNS_CUDA_OK(cudaEventRecord(ev_up_[c], copy_stream_));
         }
     }
+    // the coarse step runs on s, rotation + query state on aux_stream_ (independent work on
+    // the same queries, so the two latency-bound chains overlap); s joins aux before grouping
     const bool per_stage = time_it && nchunks == 1;
+    aux_timed_ = per_stage;
+    HANNS_CUDA_OK(cudaEventRecord(ev_fork_, s));
+    HANNS_CUDA_OK(cudaStreamWaitEvent(aux_stream_, ev_fork_, 0));
+    if (per_stage) HANNS_CUDA_OK(cudaEventRecord(ev_aux_[0], aux_stream_));
     for (int c = 0; c < nchunks; ++c) {
         const int64_t q0 = c * per, m = std::min(per, nb - q0);
         if (m <= 0) break;
         const float* q = d_q + q0 * dim_;
-        if (h_q) HANNS_CUDA_OK(cudaStreamWaitEvent(s, ev_up_[c], 0));
+        if (h_q) {
+            HANNS_CUDA_OK(cudaStreamWaitEvent(s, ev_up_[c], 0));
+            HANNS_CUDA_OK(cudaStreamWaitEvent(aux_stream_, ev_up_[c], 0));
+        }
         launches += coarse_probes(q, m, nprobe, w_probes_.p + q0 * nprobe, s,
                                   per_stage ? ev_[1] : nullptr);
-        if (per_stage) HANNS_CUDA_OK(cudaEventRecord(ev_[2], s));
-        launch_rotate(q, m, dim_, D_, P_.p, w_qrot_.p + q0 * D_, s);
-        if (per_stage) HANNS_CUDA_OK(cudaEventRecord(ev_[3], s));
+        launch_rotate(q, m, dim_, D_, P_.p, w_qrot_.p + q0 * D_, aux_stream_);
+        if (per_stage) HANNS_CUDA_OK(cudaEventRecord(ev_aux_[1], aux_stream_));
         launch_query_state(q, w_qrot_.p + q0 * D_, m, dim_, D_, rc_.p, nbits_, w_qp_.p + q0,
-                           w_qi8p_.p + q0 * D_, w_qi8n_.p + q0 * D_, w_lut_.p + q0 * G * 16, s);
+                           w_qi8p_.p + q0 * D_, w_qi8n_.p + q0 * D_, w_lut_.p + q0 * G * 16,
+                           aux_stream_);
         launches += 2;
     }
-    if (time_it && !per_stage) {
-        // chunked upload: the first stage spans upload + all per-query stages
-        for (int e = 1; e <= 3; ++e) HANNS_CUDA_OK(cudaEventRecord(ev_[e], s));
+    if (per_stage) {
+        HANNS_CUDA_OK(cudaEventRecord(ev_aux_[2], aux_stream_));
+        HANNS_CUDA_OK(cudaEventRecord(ev_[2], s));  // coarse step done
+    }
+    HANNS_CUDA_OK(cudaEventRecord(ev_join_, aux_stream_));
+    HANNS_CUDA_OK(cudaStreamWaitEvent(s, ev_join_, 0));
+    if (time_it) {
+        if (!per_stage) {  // chunked upload: the first stage spans upload + per-query stages
+            HANNS_CUDA_OK(cudaEventRecord(ev_[1], s));
+            HANNS_CUDA_OK(cudaEventRecord(ev_[2], s));
+        }
+        HANNS_CUDA_OK(cudaEventRecord(ev_[3], s));  // per-query stages done
     }
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
     // 3. group (query, probe) pairs by list
@@ -559,10 +591,10 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     w_cursor_.reserve(nlist_ + 1);
     w_lq_off_.reserve(nlist_ + 1);
     w_item_off_.reserve(nlist_ + 1);
-    w_counters_.reserve(2);
+    w_counters_.reserve(3);
     w_lq_.reserve((size_t)nb * nprobe);
     w_items_.reserve((size_t)nb * nprobe);
-    HANNS_CUDA_OK(cudaMemsetAsync(w_counters_.p, 0, 2 * sizeof(int), s));
+    HANNS_CUDA_OK(cudaMemsetAsync(w_counters_.p, 0, 3 * sizeof(int), s));
     launch_group_pairs(w_probes_.p, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr,
                        kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p, w_item_off_.p,
                        w_counters_.p, w_lq_.p, w_items_.p, s);
@@ -615,6 +647,49 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     a.cand_tie = w_cand_tie_.p;
     a.scores = w_scores_.p;
     a.max_len = (int)per_warp;
+    // HANNS_GPU_SCAN=tc: lists with n_cand < |list| <= scan_tc_max_rows() (FastScan runs)
+    // go to the tensor-core scan; by default every list takes the SIMT scan
+    const char* scan_mode = std::getenv("HANNS_GPU_SCAN");
+    const bool use_tc = scan_mode && std::strcmp(scan_mode, "tc") == 0 && max_list_ > n_cand;
+    a.tc_rows = use_tc ? scan_tc_max_rows() : 0;
+    if (use_tc) {
+        w_scan_err_.reserve(1);
+        HANNS_CUDA_OK(cudaMemsetAsync(w_scan_err_.p, 0, sizeof(int), s));
+        TcScanArgs t{};
+        t.D = D_;
+        t.nbits = nbits_;
+        t.code_bytes = code_bytes_;
+        t.G = G;
+        t.metric_l2 = a.metric_l2;
+        t.list_off = list_off_.p;
+        t.signs = signs_.p;
+        t.codes = codes_.p;
+        t.meta = meta_.p;
+        t.ids = ids_.p;
+        t.qp = w_qp_.p;
+        t.lut = w_lut_.p;
+        t.q_i8 = w_qi8n_.p;
+        t.lq = w_lq_.p;
+        t.items = w_items_.p;
+        t.n_items = w_counters_.p;
+        t.item_counter = w_counters_.p + 2;
+        t.k = k;
+        t.n_cand = n_cand;
+        t.nprobe = nprobe;
+        t.fused = a.fused;
+        t.bitsets = a.bitsets;
+        t.bitset_len = a.bitset_len;
+        t.bitset_words = a.bitset_words;
+        t.n_bitsets = a.n_bitsets;
+        t.query_bitset = a.query_bitset;
+        t.pair_off = w_pair_off_.p;
+        t.q_stride = q_stride;
+        t.cand_key = w_cand_key_.p;
+        t.cand_tie = w_cand_tie_.p;
+        t.err_flag = w_scan_err_.p;
+        launch_scan_tc(t, sm_count_, s);
+        launches += 1;
+    }
     launch_scan(a, grid, s);
     launches += 1;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[6], s));
@@ -649,6 +724,10 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     m.out_keys = d_keys;
     launch_merge(m, s);
     launches += 1;
+    if (use_tc)
+        HANNS_CUDA_OK(cudaMemcpyAsync(h_scan_err_, w_scan_err_.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    else
+        *h_scan_err_ = 0;
     HANNS_CUDA_OK(cudaGetLastError());
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[7], s));
     last_launches_ += launches;
@@ -683,8 +762,20 @@ void IvfUsqGpu::run_search(const float* d_queries, const float* h_queries, int64
                      d_ids + b * k, d_dists + b * k, d_counts ? d_counts + b : nullptr,
                      d_keys ? d_keys + b * k : nullptr, s, true);
         HANNS_CUDA_OK(cudaEventSynchronize(ev_[kStages]));
+        if (*h_scan_err_ != 0)
+            throw std::runtime_error("tensor-core list scan: a bounded wait expired (code " +
+                                     std::to_string(*h_scan_err_) + ")");
+        // stages 0-1 (coarse step) and 2-3 (rotation, query state) overlap on two streams;
+        // ev_[3] -> ev_[4] is empty (the join)
         float t;
         for (int e = 0; e < kStages; ++e) {
+            if (e == 2 || e == 3) {
+                if (aux_timed_) {
+                    HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_aux_[e - 2], ev_aux_[e - 1]));
+                    stage_ms_[e] += t;
+                }
+                continue;
+            }
             HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[e], ev_[e + 1]));
             stage_ms_[e] += t;
         }

@@ -161,9 +161,16 @@ class IvfUsqGpu {
 
     cudaStream_t stream_ = nullptr;
     cudaStream_t copy_stream_ = nullptr;  // host->device query upload
+    cudaStream_t aux_stream_ = nullptr;   // rotation + query state, beside the coarse step
+    cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
+    cudaEvent_t ev_aux_[3] = {};          // rotation start / end, query state end
+    bool aux_timed_ = false;
     static constexpr int kMaxUploadChunks = 8;
     cudaEvent_t ev_up_[kMaxUploadChunks] = {};
     cudaEvent_t ev_ready_ = nullptr;  // copy_stream_ waits for earlier work on the search stream
+    int* h_scan_err_ = nullptr;       // pinned: error code of the tensor-core list scan
+    DevBuf<int> w_scan_err_;
+    int sm_count_ = 0;
     // stages: coarse GEMM, coarse select, rotate, query state, group, scan, merge; then total
     static constexpr int kStages = 7;
     cudaEvent_t ev_[kStages + 1] = {};

@@ -53,6 +53,34 @@ struct ScanArgs {
     // FastScan scores scratch: per CTA, kScanWarps rows of max_len
     int16_t* scores;
     int max_len;
+    // items whose list has n_cand < |list| <= tc_rows belong to scan_tc_kernel (0: none)
+    int tc_rows;
+};
+
+// Tensor-core list scan of the FastScan-sized lists (scan_tc.cu).
+struct TcScanArgs {
+    int D, nbits, code_bytes, G, metric_l2;
+    const int64_t* list_off;
+    const uint8_t* signs;   // [ntotal][D/8] sign bits, list order
+    const uint8_t* codes;   // [ntotal][code_bytes]
+    const float4* meta;
+    const int64_t* ids;
+    const QueryParams* qp;
+    const uint8_t* lut;     // [nq][G*16] offset-binary
+    const int8_t* q_i8;     // [nq][D] natural order
+    const int2* lq;
+    const int4* items;
+    const int* n_items;
+    int* item_counter;
+    int k, n_cand, nprobe, fused;
+    const uint64_t* bitsets;
+    int64_t bitset_len, bitset_words, n_bitsets;
+    const int32_t* query_bitset;
+    const int* pair_off;
+    int64_t q_stride;
+    uint32_t* cand_key;
+    uint64_t* cand_tie;
+    int* err_flag;          // set to 4 when a bounded wait expired
 };
 
 struct MergeArgs {
@@ -115,6 +143,9 @@ void launch_pair_offsets(const int32_t* probes, int64_t nq, int nprobe, const in
                          int nlist, const uint8_t* owned, int n_cand, int* pair_off,
                          cudaStream_t s);
 size_t scan_smem_bytes(int D);
+int scan_tc_max_rows();
+size_t scan_tc_smem_bytes();
+void launch_scan_tc(const TcScanArgs& a, int grid, cudaStream_t s);
 int scan_grid_size(int D);
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s);
 void launch_merge(const MergeArgs& a, cudaStream_t s);

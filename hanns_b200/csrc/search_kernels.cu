@@ -13,9 +13,9 @@
 //                         are read once per batch and shared by all queries that probe it
 //   scan_lists_kernel     per (list, query): FastScan scores (i16-wrapped sums of
 //                         fastscan.rs:170-227), the exact fastscan_topk kept set
-//                         (fastscan.rs:86-146), integer rerank (quantizer.rs:274-400) and
-//                         the per-(query, probe) top-k
-//   merge_kernel          per query top-k over its probes by (distance, probe rank,
+//                         (fastscan.rs:86-146) and integer rerank (quantizer.rs:274-400);
+//                         every kept candidate goes to the query's candidate region
+//   merge_kernel          per query top-k over its candidates by (distance, probe rank,
 //                         FastScan order, list position): the reference's stable sort of
 //                         src/faiss/ivf_usq.rs:590-593, padded with (-1, +inf)
 #include <algorithm>
@@ -23,95 +23,9 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "warp_select.cuh"
 
 namespace hanns {
-
-// ============================================================================
-// Warp-level helpers
-// ============================================================================
-
-__device__ __forceinline__ unsigned lanemask_le() {
-    unsigned m;
-    asm("mov.u32 %0, %%lanemask_le;" : "=r"(m));
-    return m;
-}
-__device__ __forceinline__ unsigned lanemask_lt() {
-    unsigned m;
-    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
-    return m;
-}
-
-__device__ __forceinline__ int warp_inclusive_scan(int v) {
-    const int lane = (int)lane_id();
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        int t = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += t;
-    }
-    return v;
-}
-
-__device__ __forceinline__ int warp_sum(int v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-
-// Finds the `kth` smallest key (1-based) among the valid keys produced by
-// key_at(i) for i in [0, n), looking only at the low `bits` bits (multiple of 8).
-// Returns the key; *n_less = number of valid keys strictly smaller.
-// hist: 256 words of shared memory owned by this warp.
-template <class KeyAt>
-__device__ uint32_t warp_radix_kth(int n, int kth, int bits, KeyAt key_at, uint32_t* hist,
-                                   int* n_less) {
-    const int lane = (int)lane_id();
-    uint32_t prefix = 0, pmask = 0;
-    int remaining = kth, less = 0;
-    for (int shift = bits - 8; shift >= 0; shift -= 8) {
-#pragma unroll
-        for (int b = 0; b < 8; ++b) hist[lane * 8 + b] = 0;
-        __syncwarp();
-        for (int i = lane; i < n; i += 32) {
-            uint32_t key;
-            if (key_at(i, key) && (key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-        }
-        __syncwarp();
-        int s = 0;
-#pragma unroll
-        for (int b = 0; b < 8; ++b) s += (int)hist[lane * 8 + b];
-        const int incl = warp_inclusive_scan(s);
-        const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
-        const int src = __ffs(hit) - 1;  // hit != 0 because remaining <= total
-        int bin = 0, before = 0;
-        if (lane == src) {
-            int c = incl - s;
-            for (int b = 0; b < 8; ++b) {
-                const int h = (int)hist[lane * 8 + b];
-                if (c + h >= remaining) {
-                    bin = lane * 8 + b;
-                    break;
-                }
-                c += h;
-            }
-            before = c;
-        }
-        bin = __shfl_sync(0xffffffffu, bin, src);
-        before = __shfl_sync(0xffffffffu, before, src);
-        less += before;
-        remaining -= before;
-        prefix |= (uint32_t)bin << shift;
-        pmask |= 255u << shift;
-        __syncwarp();
-    }
-    *n_less = less;
-    return prefix;
-}
 
 __device__ __forceinline__ bool bit_filtered(const uint64_t* words, int64_t len, int64_t id) {
     // Kept iff (id as usize) >= len || bit == 0 (src/faiss/ivf_usq.rs:708-710).
@@ -193,7 +107,7 @@ __global__ void __launch_bounds__(128) select_probes_kernel(const float* __restr
         return true;
     };
     int less = 0;
-    const uint32_t tau = warp_radix_kth(nlist, nprobe, 32, key_at, hist[w], &less);
+    const uint32_t tau = warp_radix_kth(nlist, nprobe, key_at, hist[w], &less);
     // Gather the selected (key, idx): all keys < tau, then the lowest-index ties.
     uint32_t* sk = sel_scratch + qi * 2 * (int64_t)nprobe;
     uint32_t* si = sk + nprobe;
@@ -317,21 +231,44 @@ __global__ void __launch_bounds__(256) coarse_gemm_kernel(const float* __restric
     }
 }
 
-// Exact sequential L2 (the reference's l2_distance) of one query (shared memory) to one
-// centroid.
+// Exact sequential L2 (the reference's l2_distance) of one query (shared memory, 16-byte
+// aligned) to one centroid.  The centroid row comes from L2 in blocks of 16 float4 loads
+// issued together, so the dependent add chain waits for one round trip per 64 dims
+// instead of one per 4.
 __device__ __forceinline__ float exact_l2(const float* qs, const float* __restrict__ c, int d) {
     float s = -0.0f;
     if ((d & 3) == 0) {
         const float4* c4 = reinterpret_cast<const float4*>(c);
-        for (int i = 0; i < d / 4; ++i) {
+        const float4* q4 = reinterpret_cast<const float4*>(qs);
+        const int n4 = d / 4;
+        int i = 0;
+        for (; i + 16 <= n4; i += 16) {
+            float4 v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = __ldg(c4 + i + u);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const float4 qv = q4[i + u];
+                float df = __fsub_rn(qv.x, v[u].x);
+                s = __fadd_rn(s, __fmul_rn(df, df));
+                df = __fsub_rn(qv.y, v[u].y);
+                s = __fadd_rn(s, __fmul_rn(df, df));
+                df = __fsub_rn(qv.z, v[u].z);
+                s = __fadd_rn(s, __fmul_rn(df, df));
+                df = __fsub_rn(qv.w, v[u].w);
+                s = __fadd_rn(s, __fmul_rn(df, df));
+            }
+        }
+        for (; i < n4; ++i) {
             const float4 v = __ldg(c4 + i);
-            float df = __fsub_rn(qs[4 * i], v.x);
+            const float4 qv = q4[i];
+            float df = __fsub_rn(qv.x, v.x);
             s = __fadd_rn(s, __fmul_rn(df, df));
-            df = __fsub_rn(qs[4 * i + 1], v.y);
+            df = __fsub_rn(qv.y, v.y);
             s = __fadd_rn(s, __fmul_rn(df, df));
-            df = __fsub_rn(qs[4 * i + 2], v.z);
+            df = __fsub_rn(qv.z, v.z);
             s = __fadd_rn(s, __fmul_rn(df, df));
-            df = __fsub_rn(qs[4 * i + 3], v.w);
+            df = __fsub_rn(qv.w, v.w);
             s = __fadd_rn(s, __fmul_rn(df, df));
         }
     } else {
@@ -370,7 +307,7 @@ __device__ void warp_select_stable(const float* row, int nlist, int nprobe, uint
         return true;
     };
     int less = 0;
-    const uint32_t ktau = warp_radix_kth(nlist, nprobe, 32, key_at, hist, &less);
+    const uint32_t ktau = warp_radix_kth(nlist, nprobe, key_at, hist, &less);
     int taken = 0, ties_needed = nprobe - less;
     for (int base = 0; base < nlist && taken < nprobe; base += 32) {
         const int i = base + lane;
@@ -433,7 +370,7 @@ __global__ void __launch_bounds__(128) coarse_select_exact_kernel(
         return true;
     };
     int less = 0;
-    const float tau = key_to_float(warp_radix_kth(nlist, nprobe, 32, key_at, hist[w], &less));
+    const float tau = key_to_float(warp_radix_kth(nlist, nprobe, key_at, hist[w], &less));
     const double thr = coarse_threshold(tau, qn, cmax, d, dot_rel);
     const bool approx_ok = !tc_err || *tc_err == 0;
     int cnt = 0;
@@ -471,53 +408,125 @@ __global__ void __launch_bounds__(128) coarse_select_exact_kernel(
     warp_select_stable(row, nlist, nprobe, hist[w], ckey[w], cidx[w], probes + qi * nprobe);
 }
 
-// Block-wide k-th smallest total-order key of row[0..n) (256 threads).
+// Block-wide k-th smallest total-order key (256 threads).
 constexpr int kSelThreads = 256;
+constexpr int kSelBins = 4096;  // 12 bits per histogram pass
+constexpr int kSelList = 1024;  // shared scratch words (keys of the final bin, block sums)
+constexpr int kSelRank = 64;    // a bin this small is ranked exactly
 
-__device__ uint32_t block_radix_kth(const float* row, int n, int kth, uint32_t* hist, int* bcast,
-                                    int* n_less) {
-    const int tid = threadIdx.x;
-    uint32_t prefix = 0, pmask = 0;
-    int remaining = kth, less = 0;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        hist[tid] = 0;
-        __syncthreads();
-        for (int i = tid; i < n; i += kSelThreads) {
-            const uint32_t k = total_order_key(row[i]);
-            if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+// k-th smallest (1-based) of the keys each thread produces through for_each(f) (f is
+// called once per key of the calling thread).  One pass finds the key range; 12-bit
+// histogram passes over the bits in which the keys differ, each restricted to the keys
+// whose higher bits match the bins chosen so far, narrow the search until the bin of the
+// k-th key holds at most kSelRank keys, which are then ranked exactly.  Keys of nearby
+// scores share their high bits, so a histogram of fixed high bytes would pile every key
+// into one bin.  hist: kSelBins words, list: kSelList words, bcast: 8 ints (shared).
+template <class ForEach>
+__device__ uint32_t block_select_kth(ForEach for_each, int kth, uint32_t* hist, uint32_t* list,
+                                     int* bcast) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+    for_each([&](uint32_t k) {
+        kmin = min(kmin, k);
+        kmax = max(kmax, k);
+    });
+    kmin = warp_min_u32(kmin);
+    kmax = warp_max_u32(kmax);
+    if (lane == 0) {
+        list[w] = kmin;
+        list[32 + w] = kmax;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        uint32_t a = tid < kSelThreads / 32 ? list[tid] : 0xFFFFFFFFu;
+        uint32_t b = tid < kSelThreads / 32 ? list[32 + tid] : 0u;
+        a = warp_min_u32(a);
+        b = warp_max_u32(b);
+        if (tid == 0) {
+            bcast[6] = (int)a;
+            bcast[7] = (int)b;
         }
+    }
+    __syncthreads();
+    kmin = (uint32_t)bcast[6];
+    const uint32_t range = (uint32_t)bcast[7] - kmin;
+    int res = 32 - __clz(range);  // bits >= res of (key - kmin) are resolved (zero so far)
+    uint32_t prefix = 0;
+    int r = kth;
+    while (res > 0) {
+        const int shift = res > 12 ? res - 12 : 0;
+        for (int i = tid; i < kSelBins; i += kSelThreads) hist[i] = 0;
         __syncthreads();
-        if (tid < 32) {
-            int s = 0;
+        for_each([&](uint32_t k) {
+            const uint32_t kp = k - kmin;
+            if (res >= 32 || ((kp ^ prefix) >> res) == 0) atomicAdd(&hist[(kp >> shift) & (kSelBins - 1)], 1u);
+        });
+        __syncthreads();
+        // bin of the r-th key: thread t owns bins 16t .. 16t+15
+        int s = 0;
 #pragma unroll
-            for (int b = 0; b < 8; ++b) s += (int)hist[tid * 8 + b];
-            const int incl = warp_inclusive_scan(s);
-            const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
-            const int src = __ffs(hit) - 1;
-            if (tid == src) {
-                int c = incl - s, bin = tid * 8;
-                for (int b = 0; b < 8; ++b) {
-                    const int h = (int)hist[tid * 8 + b];
-                    if (c + h >= remaining) {
-                        bin = tid * 8 + b;
-                        break;
-                    }
-                    c += h;
+        for (int b = 0; b < 16; ++b) s += (int)hist[tid * 16 + b];
+        const int incl = warp_inclusive_scan(s);
+        if (lane == 31) list[64 + w] = (uint32_t)incl;
+        __syncthreads();
+        int off = 0;
+        for (int j = 0; j < w; ++j) off += (int)list[64 + j];
+        const int lo = off + incl - s, hi = off + incl;
+        if (lo < r && r <= hi) {
+            int c = lo, bin = tid * 16;
+            for (int b = 0; b < 16; ++b) {
+                const int h = (int)hist[tid * 16 + b];
+                if (c + h >= r) {
+                    bin = tid * 16 + b;
+                    break;
                 }
-                bcast[0] = bin;
-                bcast[1] = c;
+                c += h;
             }
+            bcast[0] = bin;
+            bcast[1] = c;
+            bcast[2] = (int)hist[bin];
         }
         __syncthreads();
-        const int bin = bcast[0], before = bcast[1];
-        less += before;
-        remaining -= before;
-        prefix |= (uint32_t)bin << shift;
-        pmask |= 255u << shift;
+        const uint32_t bin = (uint32_t)bcast[0];
+        r -= bcast[1];
+        const int cnt = bcast[2];
+        prefix |= (bin << shift) & ~((res >= 32) ? 0u : (0xFFFFFFFFu << res));
+        res = shift;
+        if (cnt <= kSelRank) break;
         __syncthreads();
     }
-    *n_less = less;
-    return prefix;
+    if (res == 0) return kmin + prefix;  // every key of the bin is equal
+    // rank the (<= kSelRank) keys of the final bin exactly
+    if (tid == 0) bcast[3] = 0;
+    __syncthreads();
+    for_each([&](uint32_t k) {
+        const uint32_t kp = k - kmin;
+        if (((kp ^ prefix) >> res) == 0) list[atomicAdd(&bcast[3], 1)] = kp;
+    });
+    __syncthreads();
+    const int cnt = bcast[3];
+    for (int t = tid; t < cnt; t += kSelThreads) {
+        const uint32_t x = list[t];
+        int less = 0, eq_before = 0;
+        for (int j = 0; j < cnt; ++j) {
+            const uint32_t u = list[j];
+            less += u < x ? 1 : 0;
+            eq_before += (u == x && j < t) ? 1 : 0;
+        }
+        if (less + eq_before == r - 1) bcast[4] = (int)x;
+    }
+    __syncthreads();
+    return kmin + (uint32_t)bcast[4];
+}
+
+// k-th smallest total-order key of row[0..n) (shared or global memory).
+__device__ uint32_t block_radix_kth(const float* row, int n, int kth, uint32_t* hist,
+                                    uint32_t* list, int* bcast) {
+    return block_select_kth(
+        [&](auto f) {
+            for (int i = threadIdx.x; i < n; i += kSelThreads) f(total_order_key(row[i]));
+        },
+        kth, hist, list, bcast);
 }
 
 // One 256-thread block per query with the approximate row staged in shared memory
@@ -526,9 +535,8 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
     const float* __restrict__ approx, const float* __restrict__ q, int64_t nq,
     const float* __restrict__ cent, int nlist, int d, int nprobe, float cmax, float dot_rel,
     const int* __restrict__ tc_err, int32_t* __restrict__ probes, int* __restrict__ fallbacks) {
-    extern __shared__ __align__(16) float sm[];  // row[nlist4], qs[d]
-    __shared__ uint32_t hist[256];
-    __shared__ int bcast[4];
+    extern __shared__ __align__(16) float sm[];  // row[nlist4], qs[d4], hist[kSelBins], list[kSelList]
+    __shared__ int bcast[8];
     __shared__ float red[kSelThreads / 32];
     __shared__ int cidx[kCoarseCap];
     __shared__ uint32_t ckey[kCoarseCap];
@@ -538,13 +546,47 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
     const int64_t qi = blockIdx.x;
     float* row = sm;
     float* qs = sm + ((nlist + 3) & ~3);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(qs + ((d + 3) & ~3));
+    uint32_t* list = hist + kSelBins;
+    // stage the approximate row and the query: every load of a thread is issued before
+    // its first store, so the staging costs one memory round trip per 4 loads
     const float* grow = approx + qi * nlist;
-    for (int i = tid; i < nlist; i += kSelThreads) row[i] = grow[i];
+    if ((nlist & 3) == 0) {
+        const float4* g4 = reinterpret_cast<const float4*>(grow);
+        float4* r4 = reinterpret_cast<float4*>(row);
+        const int n4 = nlist >> 2;
+        for (int b = 0; b < n4; b += 4 * kSelThreads) {
+            float4 t[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = b + j * kSelThreads + tid;
+                if (i < n4) t[j] = __ldcs(g4 + i);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = b + j * kSelThreads + tid;
+                if (i < n4) r4[i] = t[j];
+            }
+        }
+    } else {
+        for (int i = tid; i < nlist; i += kSelThreads) row[i] = grow[i];
+    }
     float qn = 0.0f;
-    for (int i = tid; i < d; i += kSelThreads) {
-        const float v = q[qi * d + i];
-        qs[i] = v;
-        qn = __fmaf_rn(v, v, qn);
+    for (int b = 0; b < d; b += 4 * kSelThreads) {
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = b + j * kSelThreads + tid;
+            v[j] = i < d ? __ldg(q + qi * d + i) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = b + j * kSelThreads + tid;
+            if (i < d) {
+                qs[i] = v[j];
+                qn = __fmaf_rn(v[j], v[j], qn);
+            }
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) qn = __fadd_rn(qn, __shfl_xor_sync(0xffffffffu, qn, o));
@@ -553,8 +595,7 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
     __syncthreads();
     qn = 0.0f;
     for (int i = 0; i < kSelThreads / 32; ++i) qn = __fadd_rn(qn, red[i]);
-    int less = 0;
-    const float tau = key_to_float(block_radix_kth(row, nlist, nprobe, hist, bcast, &less));
+    const float tau = key_to_float(block_radix_kth(row, nlist, nprobe, hist, list, bcast));
     if (tid == 0) thr_s = coarse_threshold(tau, qn, cmax, d, dot_rel);
     __syncthreads();
     const double thr = thr_s;
@@ -584,6 +625,174 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
     for (int c = tid; c < nlist; c += kSelThreads) row[c] = exact_l2(qs, cent + (int64_t)c * d, d);
     __syncthreads();
     if (w == 0) warp_select_stable(row, nlist, nprobe, hist, ckey, cidx, probes + qi * nprobe);
+}
+
+// Re-score staging: candidates (<= kRsMax) x 32-dimension chunks, 4 slots; the row stride
+// of 36 floats keeps each thread's 16-byte reads of its own row conflict-free.
+constexpr int kRsDims = 32, kRsSlots = 4, kRsMax = 64, kRsStride = 36;
+constexpr size_t kRsBytes = (size_t)kRsSlots * kRsMax * kRsStride * sizeof(float);
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     (uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// One 256-thread block per query, the approximate row held in registers (NV4 float4 per
+// thread, nlist <= 1024 * NV4, nlist % 4 == 0, d % 4 == 0).  Same result as
+// coarse_select_block_kernel: k-th approximate key -> rigorous threshold -> exact
+// re-score of the candidates (two per thread, packed f32x2) -> stable order.
+template <int NV4>
+__global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
+    float* __restrict__ approx, const float* __restrict__ q, int64_t nq,
+    const float* __restrict__ cent, int nlist, int d, int nprobe, float cmax, float dot_rel,
+    const int* __restrict__ tc_err, int32_t* __restrict__ probes, int* __restrict__ fallbacks) {
+    extern __shared__ __align__(16) float sm[];  // qs[d], {hist[kSelBins], list[kSelList]} | ring
+    __shared__ int bcast[8];
+    __shared__ float red[kSelThreads / 32];
+    __shared__ int cidx[kCoarseCap];
+    __shared__ uint32_t ckey[kCoarseCap];
+    __shared__ int cnt_s;
+    __shared__ float thr_s;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int64_t qi = blockIdx.x;
+    float* qs = sm;
+    uint32_t* hist = reinterpret_cast<uint32_t*>(sm + d);
+    uint32_t* list = hist + kSelBins;
+    const int n4 = nlist >> 2;
+    float* grow = approx + qi * nlist;
+    // the row: float4 index tid + 256 j, all loads issued before the first use
+    float4 v[NV4];
+#pragma unroll
+    for (int j = 0; j < NV4; ++j) {
+        const int i4 = tid + j * kSelThreads;
+        v[j] = i4 < n4 ? __ldcs(reinterpret_cast<const float4*>(grow) + i4)
+                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    float qn = 0.0f;
+    for (int b = 0; b < d; b += 4 * kSelThreads) {
+        float t[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = b + j * kSelThreads + tid;
+            t[j] = i < d ? __ldg(q + qi * d + i) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = b + j * kSelThreads + tid;
+            if (i < d) {
+                qs[i] = t[j];
+                qn = __fmaf_rn(t[j], t[j], qn);
+            }
+        }
+    }
+    auto val = [&](int j, int e) -> float {
+        return e == 0 ? v[j].x : e == 1 ? v[j].y : e == 2 ? v[j].z : v[j].w;
+    };
+    auto valid = [&](int j) { return tid + j * kSelThreads < n4; };
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) qn = __fadd_rn(qn, __shfl_xor_sync(0xffffffffu, qn, o));
+    if (lane == 0) red[w] = qn;
+    if (tid == 0) cnt_s = 0;
+    const uint32_t tau_key = block_select_kth(
+        [&](auto f) {
+#pragma unroll
+            for (int j = 0; j < NV4; ++j)
+                if (valid(j))
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) f(total_order_key(val(j, e)));
+        },
+        nprobe, hist, list, bcast);
+    if (tid == 0) {
+        float qsum = 0.0f;
+        for (int i = 0; i < kSelThreads / 32; ++i) qsum = __fadd_rn(qsum, red[i]);
+        // (double)x <= thr  <=>  x <= thr rounded down to a float
+        thr_s = __double2float_rd(coarse_threshold(key_to_float(tau_key), qsum, cmax, d, dot_rel));
+    }
+    __syncthreads();
+    const float thr = thr_s;
+#pragma unroll
+    for (int j = 0; j < NV4; ++j)
+        if (valid(j))
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (val(j, e) <= thr) {
+                    const int pos = atomicAdd(&cnt_s, 1);
+                    if (pos < kCoarseCap) cidx[pos] = 4 * (tid + j * kSelThreads) + e;
+                }
+    __syncthreads();
+    const int cnt = cnt_s;
+    const bool approx_ok = !tc_err || *tc_err == 0;
+    if (approx_ok && cnt <= kCoarseCap && cnt >= nprobe) {
+        if (cnt <= kRsMax) {
+            // candidate rows stream through a 4-slot ring of 32-dimension chunks (cp.async,
+            // all threads); thread c runs candidate c's sequential sum from shared memory
+            float* ring = reinterpret_cast<float*>(hist);  // [kRsSlots][kRsMax][kRsStride]
+            const int nch = (d + kRsDims - 1) / kRsDims;
+            auto issue = [&](int k) {
+                if (k < nch) {
+                    float* slot = ring + (k % kRsSlots) * kRsMax * kRsStride;
+                    for (int e = tid; e < cnt * (kRsDims / 4); e += kSelThreads) {
+                        const int c = e / (kRsDims / 4), p = e % (kRsDims / 4);
+                        const int d0 = k * kRsDims + 4 * p;
+                        if (d0 < d) cp_async16(slot + c * kRsStride + 4 * p, cent + (int64_t)cidx[c] * d + d0);
+                    }
+                }
+                cp_async_commit();
+            };
+            for (int k = 0; k < kRsSlots - 1; ++k) issue(k);
+            float sacc = -0.0f;
+            for (int k = 0; k < nch; ++k) {
+                cp_async_wait<kRsSlots - 2>();
+                __syncthreads();
+                if (tid < cnt) {
+                    const float4* c4 = reinterpret_cast<const float4*>(
+                        ring + (k % kRsSlots) * kRsMax * kRsStride + tid * kRsStride);
+                    const float4* q4 = reinterpret_cast<const float4*>(qs + k * kRsDims);
+                    const int nd4 = min(kRsDims, d - k * kRsDims) / 4;
+                    for (int j = 0; j < nd4; ++j) {
+                        const float4 cv = c4[j], qv = q4[j];
+                        float df = __fsub_rn(qv.x, cv.x);
+                        sacc = __fadd_rn(sacc, __fmul_rn(df, df));
+                        df = __fsub_rn(qv.y, cv.y);
+                        sacc = __fadd_rn(sacc, __fmul_rn(df, df));
+                        df = __fsub_rn(qv.z, cv.z);
+                        sacc = __fadd_rn(sacc, __fmul_rn(df, df));
+                        df = __fsub_rn(qv.w, cv.w);
+                        sacc = __fadd_rn(sacc, __fmul_rn(df, df));
+                    }
+                }
+                __syncthreads();
+                issue(k + kRsSlots - 1);
+            }
+            cp_async_wait<0>();
+            if (tid < cnt) ckey[tid] = total_order_key(sacc);
+        } else {
+            for (int i = tid; i < cnt; i += kSelThreads)
+                ckey[i] = total_order_key(exact_l2(qs, cent + (int64_t)cidx[i] * d, d));
+        }
+        __syncthreads();
+        for (int i = tid; i < cnt; i += kSelThreads) {
+            const uint32_t ki = ckey[i];
+            const int ii = cidx[i];
+            int rank = 0;
+            for (int j = 0; j < cnt; ++j) rank += (ckey[j] < ki || (ckey[j] == ki && cidx[j] < ii)) ? 1 : 0;
+            if (rank < nprobe) probes[qi * nprobe + rank] = ii;
+        }
+        return;
+    }
+    // fallback: exact distances to every centroid (into the query's scratch row), then the
+    // stable selection
+    if (tid == 0) atomicAdd(fallbacks, 1);
+    for (int c = tid; c < nlist; c += kSelThreads) grow[c] = exact_l2(qs, cent + (int64_t)c * d, d);
+    __syncthreads();
+    if (w == 0) warp_select_stable(grow, nlist, nprobe, hist, ckey, cidx, probes + qi * nprobe);
 }
 
 __global__ void centroid_norms_kernel(const float* __restrict__ cent, int nlist, int d,
@@ -942,24 +1151,6 @@ __device__ __forceinline__ int int_ip_group8(const uint8_t* __restrict__ code,
     return acc;
 }
 
-// score_with_meta + distance, in the reference's operation order.
-__device__ __forceinline__ float rerank_distance(int iip, float4 m, const QueryParams& p, int nbits,
-                                                 bool l2) {
-    // m = {norm, norm_sq, vmax, quant_quality}
-    float score;
-    if (m.w <= 1e-12f) {
-        score = p.centroid_score;
-    } else {
-        const float levels = (float)(1u << nbits);
-        const float code_scale = __fdiv_rn(__fmul_rn(2.0f, m.z), fmaxf(levels, 1.0f));
-        const float offset = -m.z;
-        const float ip = __fmul_rn(
-            p.q_scale, __fadd_rn(__fmul_rn(code_scale, __int2float_rn(iip)),
-                                 __fmul_rn(offset, __int2float_rn(p.q_i8_sum))));
-        score = __fadd_rn(p.centroid_score, __fdiv_rn(__fmul_rn(m.x, ip), m.w));
-    }
-    return l2 ? __fsub_rn(__fadd_rn(p.q_norm_sq, m.y), __fmul_rn(2.0f, score)) : -score;
-}
 
 __device__ __forceinline__ const uint64_t* query_bitset_words(const ScanArgs& a, int q) {
     if (!a.fused || !a.bitsets) return nullptr;
@@ -987,6 +1178,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
         const int l = it.x;
         const int64_t beg = a.list_off[l];
         const int n = (int)(a.list_off[l + 1] - beg);
+        if (n > a.n_cand && n <= a.tc_rows) continue;  // scanned by scan_tc_kernel
         if (n <= a.n_cand) {
             // no FastScan: every live row is a candidate of every query of the item;
             // (query, row) pairs spread over the CTA's 8-lane groups
@@ -1130,7 +1322,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                         return true;
                     };
                     int c_gt = 0;
-                    const uint32_t tau = warp_radix_kth(n, a.n_cand, 16, key_at, sm.hist[w], &c_gt);
+                    const uint32_t tau = warp_radix_kth(n, a.n_cand, key_at, sm.hist[w], &c_gt);
                     // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
                     int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = 0;
                     for (int base = 0; base < n; base += 32) {
@@ -1247,7 +1439,7 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
     if (take > 0) {
         int less = 0;
         uint32_t tau = 0xFFFFFFFFu;
-        if (n_valid > a.k) tau = warp_radix_kth(total, a.k, 32, key_at, hist[w], &less);
+        if (n_valid > a.k) tau = warp_radix_kth(total, a.k, key_at, hist[w], &less);
         for (int base = 0; base < total; base += 32) {
             const int e = base + lane;
             uint32_t k = 0;
@@ -1445,10 +1637,27 @@ void launch_coarse_select(float* approx, const float* q, int64_t nq, const float
                           int d, int nprobe, float cmax, float dot_rel, const int* tc_err,
                           int32_t* probes, int* fallbacks, cudaStream_t s) {
     if (nq <= 0) return;
-    const size_t blk_bytes = ((size_t)((nlist + 3) & ~3) + d) * sizeof(float);
-    if (blk_bytes <= 96 * 1024) {
+    const size_t reg_bytes =
+        (size_t)d * sizeof(float) + std::max((size_t)(kSelBins + kSelList) * sizeof(float), kRsBytes);
+    if ((nlist & 3) == 0 && (d & 3) == 0 && nlist <= 16 * kSelThreads &&
+        reg_bytes <= 112 * 1024) {
+        const int nv4 = (nlist / 4 + kSelThreads - 1) / kSelThreads;  // float4 per thread
+        auto go = [&](auto kern) {
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
+            kern<<<(unsigned)nq, kSelThreads, reg_bytes, s>>>(approx, q, nq, cent, nlist, d, nprobe,
+                                                               cmax, dot_rel, tc_err, probes, fallbacks);
+        };
+        if (nv4 <= 1) go(coarse_select_reg_kernel<1>);
+        else if (nv4 == 2) go(coarse_select_reg_kernel<2>);
+        else if (nv4 == 3) go(coarse_select_reg_kernel<3>);
+        else go(coarse_select_reg_kernel<4>);
+        return;
+    }
+    const size_t blk_bytes =
+        ((size_t)((nlist + 3) & ~3) + ((d + 3) & ~3) + kSelBins + kSelList) * sizeof(float);
+    if (blk_bytes <= 112 * 1024) {
         cudaFuncSetAttribute(coarse_select_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             100 * 1024);
+                             112 * 1024);
         coarse_select_block_kernel<<<(unsigned)nq, kSelThreads, blk_bytes, s>>>(
             approx, q, nq, cent, nlist, d, nprobe, cmax, dot_rel, tc_err, probes, fallbacks);
     } else {

@@ -139,6 +139,59 @@ def test_search_bit_exact_larger(gpu, oracle_mod, nbits, metric, k, d):
     assert bits_eq(r.distances.reshape(exp_ids.shape), exp_d)
 
 
+@pytest.mark.parametrize("nbits,metric,k,nlist,fused", [(4, 1, 10, 12, False), (8, 0, 10, 40, True),
+                                                         (4, 0, 20, 6, True)])
+def test_tensor_core_and_simt_scans_agree(gpu, oracle_mod, nbits, metric, k, nlist, fused):
+    """Lists above n_cand and up to 1,792 rows take the tcgen05 scan (one-hot FastScan GEMM,
+    int8 rerank GEMM), longer ones the SIMT scan: both equal the oracle, with and without
+    a fused bitset (HANNS_GPU_SCAN=tc and =simt)."""
+    from hanns_b200.ivf_usq import FILTER_FUSED, FILTER_NONE, IvfUsqIndex, SearchRequest
+    from tests.golden.make_golden import mixture
+    O = oracle_mod
+    rng = np.random.default_rng(300 + nbits + nlist)
+    d = 192
+    x, _ = mixture(rng, 20000, d, 16, 0.4, metric == 1)
+    q, _ = mixture(rng, 200, d, 16, 0.4, metric == 1)
+    art = O.build_artifact(x, nlist, nbits, metric, rotation_seed=5, kmeans_iters=4, kmeans_seed=1)
+    sizes = np.diff(art["list_offsets"])
+    n_cand = O.n_candidates(nbits, k)
+    assert (sizes > n_cand).any()
+    oi = O.OracleIndex(art)
+    nprobe = min(4, nlist)
+    kw = {}
+    okw = {}
+    mode = FILTER_NONE
+    if fused:
+        blen = 20000
+        bits = (rng.random(blen) < 0.3)
+        words = np.zeros((1, (blen + 63) // 64), np.uint64)
+        for i in np.nonzero(bits)[0]:
+            words[0, i >> 6] |= np.uint64(1) << np.uint64(i & 63)
+        mode = FILTER_FUSED
+        kw = dict(bitsets=words, bitset_len=blen, query_bitset=np.zeros(q.shape[0], np.int32))
+        okw = dict(filter_mode=O.FILTER_FUSED, bitsets=words, bitset_len=blen,
+                   query_bitset=np.zeros(q.shape[0], np.int32))
+    e_ids, e_d, _ = oi.search(q, k, nprobe, **okw)
+    idx = IvfUsqIndex.from_artifact(art)
+    req = SearchRequest(top_k=k, nprobe=nprobe)
+    old = os.environ.pop("HANNS_GPU_SCAN", None)
+    try:
+        res = {}
+        for m in ("tc", "simt"):
+            os.environ["HANNS_GPU_SCAN"] = m
+            if fused:
+                r = idx.search(q, req, mode, kw["bitsets"], kw["bitset_len"], kw["query_bitset"])
+            else:
+                r = idx.search(q, req)
+            res[m] = r
+            assert np.array_equal(r.ids.reshape(e_ids.shape), e_ids), m
+            assert bits_eq(r.distances.reshape(e_ids.shape), e_d), m
+    finally:
+        os.environ.pop("HANNS_GPU_SCAN", None)
+        if old is not None:
+            os.environ["HANNS_GPU_SCAN"] = old
+
+
 def test_host_search_chunked_upload(gpu, oracle_mod):
     """Host-pointer search of 9000 queries: the upload runs in 4 chunks on the copy stream,
     each chunk's per-query stages waiting only for its own copy.  Equal to the oracle and
