@@ -147,6 +147,17 @@ def scan_bytes(art, probes, k, nbits):
     return int((sizes * (D // 8) * fs).sum() + (np.minimum(sizes, ncand) * (cb + 24)).sum())
 
 
+def measured_traffic(name):
+    """DRAM bytes per scan launch from the committed ncu summary of this workload (or None)."""
+    import re
+    try:
+        with open(os.path.join(ROOT, "profiles", f"scan_lists_kernel_workload_{name}.md")) as f:
+            m = re.search(r"dram_bytes_per_launch \| (\d+)", f.read())
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons polled through NVML every 2 ms while the
     timed region runs (read-only queries; no setting is changed)."""
@@ -454,7 +465,10 @@ def run_ours(args, w, rank, world, local_rank):
     achieved = alg / scan_s / 1e9
     roof = {"kernel": "scan_lists_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
             "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
-            "traffic": None, "algorithmic_bytes_per_launch": alg, "launch_ms": scan_s * 1e3}
+            "traffic": measured_traffic(args.workload) if world == 1 else None,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
+                              f"profiles/scan_lists_kernel_workload_{args.workload}.md",
+            "algorithmic_bytes_per_launch": alg, "launch_ms": scan_s * 1e3}
 
     # ---- recall and parity sample
     rec = None
