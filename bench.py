@@ -11,9 +11,10 @@ A step is one batched search of the 10,000 queries.  `value` = queries/s with th
 queries and the index already in HBM (CUDA events on the launching stream); `e2e` =
 the same through the host-pointer C ABI call (pinned host queries in, ids and
 distances out, copies inside the timed region).  With N > 1 (torchrun, one rank per
-GPU) the inverted lists are sharded over the ranks (LPT by list size), every rank
-searches all queries on its lists, and the per-rank top-k are merged after an NCCL
-all-gather (total work fixed: strong scaling).
+GPU) the inverted lists are sharded over the ranks (LPT by list size); each rank
+prepares 1/N of the queries (coarse probes, rotation, query state), the query state is
+all-gathered over NCCL, every rank scans its lists for all queries, and the per-rank
+top-k are merged after a second NCCL all-gather (total work fixed: strong scaling).
 
 --impl reference times the CPU restatement of the reference's search path (the
 oracle; the Rust reference cannot be built here) on the host cores, on the same
@@ -310,6 +311,41 @@ def run_ours(args, w, rank, world, local_rank):
         g_i = torch.empty(world, nq, k, dtype=torch.int64, device=dev)
     L = _lib.lib()
     launches = [0]
+    if world > 1:
+        # query split: rank r prepares queries [r*per, (r+1)*per) (coarse step, rotation,
+        # query state) and the per-query state is all-gathered; every rank then scans its
+        # own lists for all queries
+        assert nq % world == 0, "query batch must split evenly over the ranks"
+        per = nq // world
+        parts = np.zeros(5, np.int64)
+        assert L.hanns_gpu_ivf_usq_query_state_bytes(idx._h, nprobe, parts.ctypes.data_as(_lib.i64p)) == 0
+        use_qi8n = os.environ.get("HANNS_GPU_SCAN") == "tc"  # dimension-order q_i8: tensor-core scan only
+        n_state = 5 if use_qi8n else 4
+        st_local = [torch.empty(per * int(b), dtype=torch.uint8, device=dev) for b in parts[:n_state]]
+        st_full = [torch.empty(nq * int(b), dtype=torch.uint8, device=dev) for b in parts[:n_state]]
+        st_ptrs = [t.data_ptr() for t in st_full] + [None] * (5 - n_state)
+        st_lptrs = [t.data_ptr() for t in st_local] + [None] * (5 - n_state)
+
+    def shard_step(qptr):
+        # qptr: this rank's `per` queries on the device
+        rc = L.hanns_gpu_ivf_usq_prepare_device(idx._h, qptr, per, nprobe, *st_lptrs, stream.cuda_stream)
+        assert rc == 0, _lib.last_error()
+        launches[0] += idx.last_launches()
+        for full_t, loc_t in zip(st_full, st_local):
+            dist.all_gather_into_tensor(full_t, loc_t)
+        rc = L.hanns_gpu_ivf_usq_search_prepared_shard_device(idx._h, nq, k, nprobe, *st_ptrs,
+                                                               sh_d.data_ptr(), sh_k.data_ptr(),
+                                                               sh_i.data_ptr(), stream.cuda_stream)
+        assert rc == 0, _lib.last_error()
+        launches[0] += idx.last_launches()
+        dist.all_gather_into_tensor(g_d, sh_d)
+        dist.all_gather_into_tensor(g_k, sh_k)
+        dist.all_gather_into_tensor(g_i, sh_i)
+        rc = L.hanns_gpu_merge_shards_device(g_d.data_ptr(), g_k.data_ptr(), g_i.data_ptr(), world,
+                                             nq, k, out_ids.data_ptr(), out_d.data_ptr(),
+                                             stream.cuda_stream)
+        assert rc == 0, _lib.last_error()
+        launches[0] += 1
 
     def step():
         if world == 1:
@@ -317,19 +353,7 @@ def run_ours(args, w, rank, world, local_rank):
                               0, stream.cuda_stream)
             launches[0] += idx.last_launches()
         else:
-            rc = L.hanns_gpu_ivf_usq_search_shard_device(idx._h, queries.data_ptr(), nq, k, nprobe,
-                                                          sh_d.data_ptr(), sh_k.data_ptr(),
-                                                          sh_i.data_ptr(), stream.cuda_stream)
-            assert rc == 0, _lib.last_error()
-            launches[0] += idx.last_launches()
-            dist.all_gather_into_tensor(g_d, sh_d)
-            dist.all_gather_into_tensor(g_k, sh_k)
-            dist.all_gather_into_tensor(g_i, sh_i)
-            rc = L.hanns_gpu_merge_shards_device(g_d.data_ptr(), g_k.data_ptr(), g_i.data_ptr(), world,
-                                                 nq, k, out_ids.data_ptr(), out_d.data_ptr(),
-                                                 stream.cuda_stream)
-            assert rc == 0, _lib.last_error()
-            launches[0] += 1
+            shard_step(queries.data_ptr() + rank * per * w["d"] * 4)
 
     for _ in range(args.warmup):
         step()
@@ -400,28 +424,17 @@ def run_ours(args, w, rank, world, local_rank):
                "path": "hanns_gpu_ivf_usq_search (host pointers, pinned)"}
         assert np.array_equal(h_ids.numpy(), res_ids), "e2e and device paths disagree"
     else:
-        # every rank copies the pinned host queries in (replicated H2D), searches its
-        # shard, all-gathers and merges; rank 0 copies the merged ids/distances out
-        hq = torch.empty(nq, w["d"], dtype=torch.float32).pin_memory()
-        hq.copy_(queries.cpu())
+        # every rank copies its share of the pinned host queries in, prepares it, and the
+        # query state is all-gathered; rank 0 copies the merged ids/distances out
+        hq = torch.empty(per, w["d"], dtype=torch.float32).pin_memory()
+        hq.copy_(queries[rank * per:(rank + 1) * per].cpu())
         h_ids = torch.empty(nq, k, dtype=torch.int64).pin_memory()
         h_d = torch.empty(nq, k, dtype=torch.float32).pin_memory()
-        qdev = torch.empty_like(queries)
+        qdev = torch.empty(per, w["d"], dtype=torch.float32, device=dev)
 
         def e2e_step():
             qdev.copy_(hq, non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()
-            rc = L.hanns_gpu_ivf_usq_search_shard_device(idx._h, qdev.data_ptr(), nq, k, nprobe,
-                                                          sh_d.data_ptr(), sh_k.data_ptr(),
-                                                          sh_i.data_ptr(), stream.cuda_stream)
-            assert rc == 0, _lib.last_error()
-            dist.all_gather_into_tensor(g_d, sh_d)
-            dist.all_gather_into_tensor(g_k, sh_k)
-            dist.all_gather_into_tensor(g_i, sh_i)
-            rc = L.hanns_gpu_merge_shards_device(g_d.data_ptr(), g_k.data_ptr(), g_i.data_ptr(), world,
-                                                 nq, k, out_ids.data_ptr(), out_d.data_ptr(),
-                                                 stream.cuda_stream)
-            assert rc == 0, _lib.last_error()
+            shard_step(qdev.data_ptr())
             if rank == 0:
                 h_ids.copy_(out_ids, non_blocking=True)
                 h_d.copy_(out_d, non_blocking=True)
@@ -436,9 +449,10 @@ def run_ours(args, w, rank, world, local_rank):
         el = torch.tensor([time.perf_counter() - t0], device=dev)
         dist.all_reduce(el, op=dist.ReduceOp.MAX)
         e2e = {"value": nq * args.steps / float(el.item()), "unit": "queries/s",
-               "h2d_bytes_per_step": nq * w["d"] * 4 * world, "d2h_bytes_per_step": nq * k * 12,
-               "path": "per rank: pinned H2D of the queries, shard search, NCCL all-gather, merge; "
-                       "rank 0 D2H (max over ranks)"}
+               "h2d_bytes_per_step": nq * w["d"] * 4, "d2h_bytes_per_step": nq * k * 12,
+               "path": "per rank: pinned H2D of its 1/N of the queries, query preparation, NCCL "
+                       "all-gather of the query state, scan of its lists, NCCL all-gather of the "
+                       "top-k, merge; rank 0 D2H (max over ranks)"}
         if rank == 0:
             assert np.array_equal(h_ids.numpy(), res_ids), "e2e and device paths disagree"
 

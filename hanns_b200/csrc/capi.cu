@@ -558,6 +558,47 @@ int32_t hanns_gpu_shard_owners(const int64_t* list_sizes, int32_t nlist, int32_t
     return guarded([&] { hanns::shard_owners(list_sizes, nlist, world, owner); });
 }
 
+int32_t hanns_gpu_ivf_usq_query_state_bytes(HannsIvfUsqHandle* h, int32_t nprobe, int64_t* out5) {
+    if (!h || !out5) return HANNS_INVALID_ARG;
+    return guarded([&] { h->idx->query_state_bytes(nprobe, out5); });
+}
+
+int32_t hanns_gpu_ivf_usq_prepare_device(HannsIvfUsqHandle* h, const float* d_queries, int64_t nq,
+                                         int32_t nprobe, void* d_probes, void* d_qp, void* d_lut,
+                                         void* d_qi8p, void* d_qi8n, void* stream) {
+    if (!h || !d_queries || nq <= 0 || !d_probes || !d_qp || !d_lut || !d_qi8p)
+        return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        hanns::QueryState st{static_cast<int32_t*>(d_probes), static_cast<hanns::QueryParams*>(d_qp),
+                             static_cast<uint8_t*>(d_lut), static_cast<uint8_t*>(d_qi8p),
+                             static_cast<int8_t*>(d_qi8n)};
+        h->idx->prepare_device(d_queries, nq, nprobe, st, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t hanns_gpu_ivf_usq_search_prepared_shard_device(
+    HannsIvfUsqHandle* h, int64_t nq, int32_t k, int32_t nprobe, const void* d_probes,
+    const void* d_qp, const void* d_lut, const void* d_qi8p, const void* d_qi8n, float* d_dists,
+    uint64_t* d_keys, int64_t* d_ids, void* stream) {
+    if (!h || nq <= 0 || k <= 0 || !d_probes || !d_qp || !d_lut || !d_qi8p || !d_dists ||
+        !d_keys || !d_ids)
+        return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        hanns::SearchOptions opt;
+        opt.k = k;
+        opt.nprobe = nprobe;
+        hanns::QueryState st{const_cast<int32_t*>(static_cast<const int32_t*>(d_probes)),
+                             const_cast<hanns::QueryParams*>(static_cast<const hanns::QueryParams*>(d_qp)),
+                             const_cast<uint8_t*>(static_cast<const uint8_t*>(d_lut)),
+                             const_cast<uint8_t*>(static_cast<const uint8_t*>(d_qi8p)),
+                             const_cast<int8_t*>(static_cast<const int8_t*>(d_qi8n))};
+        h->idx->search_prepared_device(nq, opt, st, d_ids, d_dists, nullptr, d_keys,
+                                       static_cast<cudaStream_t>(stream));
+    });
+}
+
 int32_t hanns_gpu_merge_shards_device(const float* d_dists, const uint64_t* d_keys,
                                       const int64_t* d_ids, int32_t world, int64_t nq, int32_t k,
                                       int64_t* d_out_ids, float* d_out_dists, void* stream) {

@@ -518,21 +518,29 @@ void IvfUsqGpu::shard(int rank, int world) {
 void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
                              const SearchOptions& opt, int64_t* d_ids, float* d_dists,
                              int64_t* d_counts, uint64_t* d_keys, cudaStream_t s, bool time_it) {
-    const int k = std::max(opt.k, 1);
     const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
     const int G = D_ / 4;
-    int64_t launches = 0;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[0], s));
-    // 1-2. per-query stages: coarse probes, rotation, query state.  Host queries are uploaded
-    // in up to kMaxUploadChunks chunks on copy_stream_; chunk c's per-query stages wait only
-    // for chunk c's copy, so the copy of chunk c+1 runs under them.
     w_probes_.reserve((size_t)nb * nprobe);
-    w_sel_.reserve((size_t)nb * 2 * nprobe);
-    w_qrot_.reserve((size_t)nb * D_);
     w_qp_.reserve(nb);
     w_qi8p_.reserve((size_t)nb * D_);
     w_qi8n_.reserve((size_t)nb * D_);
     w_lut_.reserve((size_t)nb * G * 16);
+    const QueryState st{w_probes_.p, w_qp_.p, w_lut_.p, w_qi8p_.p, w_qi8n_.p};
+    int64_t launches = prepare_batch(d_q, h_q, nb, nprobe, st, s, time_it);
+    launches += scan_merge_batch(nb, opt, st, d_ids, d_dists, d_counts, d_keys, s, time_it);
+    last_launches_ += launches;
+}
+
+int64_t IvfUsqGpu::prepare_batch(const float* d_q, const float* h_q, int64_t nb, int nprobe,
+                                 const QueryState& st, cudaStream_t s, bool time_it) {
+    const int G = D_ / 4;
+    int64_t launches = 0;
+    w_qrot_.reserve((size_t)nb * D_);
+    // 1-2. per-query stages: coarse probes, rotation, query state.  Host queries are uploaded
+    // in up to kMaxUploadChunks chunks on copy_stream_; chunk c's per-query stages wait only
+    // for chunk c's copy, so the copy of chunk c+1 runs under them.
+    w_sel_.reserve((size_t)nb * 2 * nprobe);
     int nchunks = 1;
     if (h_q) nchunks = (int)std::min<int64_t>(kMaxUploadChunks, std::max<int64_t>(1, nb / 2048));
     const int64_t per = (nb + nchunks - 1) / nchunks;
@@ -563,12 +571,12 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
             HANNS_CUDA_OK(cudaStreamWaitEvent(s, ev_up_[c], 0));
             HANNS_CUDA_OK(cudaStreamWaitEvent(aux_stream_, ev_up_[c], 0));
         }
-        launches += coarse_probes(q, m, nprobe, w_probes_.p + q0 * nprobe, s,
+        launches += coarse_probes(q, m, nprobe, st.probes + q0 * nprobe, s,
                                   per_stage ? ev_[1] : nullptr);
         launch_rotate(q, m, dim_, D_, P_.p, w_qrot_.p + q0 * D_, aux_stream_);
         if (per_stage) HANNS_CUDA_OK(cudaEventRecord(ev_aux_[1], aux_stream_));
-        launch_query_state(q, w_qrot_.p + q0 * D_, m, dim_, D_, rc_.p, nbits_, w_qp_.p + q0,
-                           w_qi8p_.p + q0 * D_, w_qi8n_.p + q0 * D_, w_lut_.p + q0 * G * 16,
+        launch_query_state(q, w_qrot_.p + q0 * D_, m, dim_, D_, rc_.p, nbits_, st.qp + q0,
+                           st.q_i8p + q0 * D_, st.q_i8n + q0 * D_, st.lut + q0 * G * 16,
                            aux_stream_);
         launches += 2;
     }
@@ -585,6 +593,16 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
         }
         HANNS_CUDA_OK(cudaEventRecord(ev_[3], s));  // per-query stages done
     }
+    return launches;
+}
+
+int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const QueryState& st,
+                                    int64_t* d_ids, float* d_dists, int64_t* d_counts,
+                                    uint64_t* d_keys, cudaStream_t s, bool time_it) {
+    const int k = std::max(opt.k, 1);
+    const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
+    const int G = D_ / 4;
+    int64_t launches = 0;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
     // 3. group (query, probe) pairs by list
     w_cnt_.reserve(nlist_ + 1);
@@ -595,13 +613,13 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     w_lq_.reserve((size_t)nb * nprobe);
     w_items_.reserve((size_t)nb * nprobe);
     HANNS_CUDA_OK(cudaMemsetAsync(w_counters_.p, 0, 3 * sizeof(int), s));
-    launch_group_pairs(w_probes_.p, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr,
+    launch_group_pairs(st.probes, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr,
                        kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p, w_item_off_.p,
                        w_counters_.p, w_lq_.p, w_items_.p, s);
     const int n_cand = (int)n_candidates(nbits_, k);
     const int64_t q_stride = cand_stride(nprobe, k);
     w_pair_off_.reserve((size_t)nb * (nprobe + 1));
-    launch_pair_offsets(w_probes_.p, nb, nprobe, list_off_.p, nlist_, sharded_ ? owned_.p : nullptr,
+    launch_pair_offsets(st.probes, nb, nprobe, list_off_.p, nlist_, sharded_ ? owned_.p : nullptr,
                         n_cand, w_pair_off_.p, s);
     launches += 5;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[5], s));
@@ -625,9 +643,9 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     a.codes = codes_.p;
     a.meta = meta_.p;
     a.ids = ids_.p;
-    a.qp = w_qp_.p;
-    a.lut = w_lut_.p;
-    a.q_i8p = w_qi8p_.p;
+    a.qp = st.qp;
+    a.lut = st.lut;
+    a.q_i8p = st.q_i8p;
     a.lq = w_lq_.p;
     a.items = w_items_.p;
     a.n_items = w_counters_.p;
@@ -666,9 +684,9 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
         t.codes = codes_.p;
         t.meta = meta_.p;
         t.ids = ids_.p;
-        t.qp = w_qp_.p;
-        t.lut = w_lut_.p;
-        t.q_i8 = w_qi8n_.p;
+        t.qp = st.qp;
+        t.lut = st.lut;
+        t.q_i8 = st.q_i8n;
         t.lq = w_lq_.p;
         t.items = w_items_.p;
         t.n_items = w_counters_.p;
@@ -705,7 +723,7 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
     m.cand_tie = w_cand_tie_.p;
     m.pair_off = w_pair_off_.p;
     m.q_stride = q_stride;
-    m.probes = w_probes_.p;
+    m.probes = st.probes;
     m.list_off = list_off_.p;
     m.ids = ids_.p;
     m.sel_key = w_mkey_.p;
@@ -730,8 +748,9 @@ void IvfUsqGpu::search_batch(const float* d_q, const float* h_q, int64_t nb,
         *h_scan_err_ = 0;
     HANNS_CUDA_OK(cudaGetLastError());
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[7], s));
-    last_launches_ += launches;
+    return launches;
 }
+
 
 void IvfUsqGpu::search_device(const float* d_queries, int64_t nq, const SearchOptions& opt,
                               int64_t* d_ids, float* d_dists, int64_t* d_counts, uint64_t* d_keys,
@@ -767,20 +786,95 @@ void IvfUsqGpu::run_search(const float* d_queries, const float* h_queries, int64
                                      std::to_string(*h_scan_err_) + ")");
         // stages 0-1 (coarse step) and 2-3 (rotation, query state) overlap on two streams;
         // ev_[3] -> ev_[4] is empty (the join)
-        float t;
-        for (int e = 0; e < kStages; ++e) {
-            if (e == 2 || e == 3) {
-                if (aux_timed_) {
-                    HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_aux_[e - 2], ev_aux_[e - 1]));
-                    stage_ms_[e] += t;
-                }
-                continue;
+        collect_stage_ms(0, kStages);
+    }
+    HANNS_CUDA_OK(cudaStreamSynchronize(s));
+}
+
+void IvfUsqGpu::query_state_bytes(int nprobe, int64_t* parts) const {
+    nprobe = std::max(1, std::min(nprobe, nlist_));
+    parts[0] = (int64_t)nprobe * sizeof(int32_t);
+    parts[1] = sizeof(QueryParams);
+    parts[2] = (int64_t)(D_ / 4) * 16;
+    parts[3] = D_;
+    parts[4] = D_;
+}
+
+// stage_ms_[e] = ev_[e] -> ev_[e + 1] for first <= e < last (stages 2-3 from the rotation
+// stream's events), total = ev_[first] -> ev_[last].
+void IvfUsqGpu::collect_stage_ms(int first, int last) {
+    float t;
+    for (int e = first; e < last; ++e) {
+        if (e == 2 || e == 3) {
+            if (aux_timed_) {
+                HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_aux_[e - 2], ev_aux_[e - 1]));
+                stage_ms_[e] += t;
             }
-            HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[e], ev_[e + 1]));
-            stage_ms_[e] += t;
+            continue;
         }
-        HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[0], ev_[kStages]));
-        stage_ms_[kStages] += t;
+        HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[e], ev_[e + 1]));
+        stage_ms_[e] += t;
+    }
+    HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[first], ev_[last]));
+    stage_ms_[kStages] += t;
+}
+
+void IvfUsqGpu::prepare_device(const float* d_queries, int64_t nq, int nprobe, QueryState st,
+                               cudaStream_t stream) {
+    DeviceGuard g(device_);
+    if (!trained_) throw std::invalid_argument("index not trained");
+    check_supported();
+    if (nq <= 0) throw std::invalid_argument("query dimension mismatch");
+    if (!st.probes || !st.qp || !st.lut || !st.q_i8p) throw std::invalid_argument("null query state");
+    cudaStream_t s = stream ? stream : stream_;
+    nprobe = std::max(1, std::min(nprobe, nlist_));
+    if (!st.q_i8n) {
+        w_qi8n_.reserve((size_t)nq * D_);
+        st.q_i8n = w_qi8n_.p;
+    }
+    for (int e = 0; e < kStages + 1; ++e) stage_ms_[e] = 0;
+    HANNS_CUDA_OK(cudaEventRecord(ev_[0], s));
+    last_launches_ = prepare_batch(d_queries, nullptr, nq, nprobe, st, s, true);
+    HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
+    HANNS_CUDA_OK(cudaEventSynchronize(ev_[4]));
+    collect_stage_ms(0, 4);
+    HANNS_CUDA_OK(cudaStreamSynchronize(s));
+}
+
+void IvfUsqGpu::search_prepared_device(int64_t nq, const SearchOptions& opt, QueryState st,
+                                       int64_t* d_ids, float* d_dists, int64_t* d_counts,
+                                       uint64_t* d_keys, cudaStream_t stream) {
+    DeviceGuard g(device_);
+    if (!trained_) throw std::invalid_argument("index not trained");
+    check_supported();
+    if (nq <= 0) throw std::invalid_argument("query dimension mismatch");
+    if (!st.probes || !st.qp || !st.lut || !st.q_i8p) throw std::invalid_argument("null query state");
+    const char* scan_mode = std::getenv("HANNS_GPU_SCAN");
+    if (!st.q_i8n && scan_mode && std::strcmp(scan_mode, "tc") == 0)
+        throw std::invalid_argument("the tensor-core scan needs q_i8 in dimension order");
+    cudaStream_t s = stream ? stream : stream_;
+    const int k = std::max(opt.k, 1);
+    const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
+    const int G = D_ / 4;
+    int64_t nb_max = std::max<int64_t>(1, (4ll << 30) / (cand_stride(nprobe, k) * 12));
+    nb_max = std::min<int64_t>(nb_max, 65536);
+    last_launches_ = 0;
+    for (int e = 0; e < kStages + 1; ++e) stage_ms_[e] = 0;
+    for (int64_t b = 0; b < nq; b += nb_max) {
+        const int64_t nb = std::min(nb_max, nq - b);
+        SearchOptions o = opt;
+        if (o.d_query_bitset) o.d_query_bitset += b;
+        const QueryState sb{st.probes + b * nprobe, st.qp + b, st.lut + b * G * 16,
+                            st.q_i8p + b * D_, st.q_i8n ? st.q_i8n + b * D_ : nullptr};
+        HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
+        last_launches_ += scan_merge_batch(nb, o, sb, d_ids + b * k, d_dists + b * k,
+                                           d_counts ? d_counts + b : nullptr,
+                                           d_keys ? d_keys + b * k : nullptr, s, true);
+        HANNS_CUDA_OK(cudaEventSynchronize(ev_[kStages]));
+        if (*h_scan_err_ != 0)
+            throw std::runtime_error("tensor-core list scan: a bounded wait expired (code " +
+                                     std::to_string(*h_scan_err_) + ")");
+        collect_stage_ms(4, kStages);
     }
     HANNS_CUDA_OK(cudaStreamSynchronize(s));
 }

@@ -60,6 +60,17 @@ struct SearchOptions {
     bool shard_output = false;                // emit merge keys (multi-GPU)
 };
 
+// Per-query search state of a batch (device pointers): probes [nq][nprobe], scalars [nq],
+// FastScan LUT [nq][D/4*16] (offset-binary), q_i8 in the dp4a layout [nq][D], q_i8 in
+// dimension order [nq][D].
+struct QueryState {
+    int32_t* probes;
+    QueryParams* qp;
+    uint8_t* lut;
+    uint8_t* q_i8p;
+    int8_t* q_i8n;
+};
+
 class IvfUsqGpu {
    public:
     IvfUsqGpu(int dim, int nlist, int nbits, int metric, uint64_t rotation_seed, int nprobe,
@@ -80,6 +91,18 @@ class IvfUsqGpu {
     void search_host(const float* h_queries, int64_t nq, const SearchOptions& opt,
                      const uint64_t* h_bitsets, const int32_t* h_query_bitset, int64_t* h_ids,
                      float* h_dists, int64_t* h_counts);
+
+    // Per-query stages only (coarse probes, rotation, query state) into st (q_i8n may be
+    // null); synchronises the stream.
+    void prepare_device(const float* d_queries, int64_t nq, int nprobe, QueryState st,
+                        cudaStream_t stream);
+    // Grouping, list scan and merge over query state made by prepare_device (of this index
+    // or of another shard of it); synchronises the stream.
+    void search_prepared_device(int64_t nq, const SearchOptions& opt, QueryState st,
+                                int64_t* d_ids, float* d_dists, int64_t* d_counts,
+                                uint64_t* d_keys, cudaStream_t stream);
+    // Bytes per query of the five QueryState arrays.
+    void query_state_bytes(int nprobe, int64_t* parts) const;
 
     void debug_query(const float* h_queries, int64_t nq, int nprobe, int32_t* probes, float* q_rot,
                      int8_t* q_i8, int8_t* lut, float* scalars);
@@ -113,6 +136,12 @@ class IvfUsqGpu {
     void search_batch(const float* d_q, const float* h_q, int64_t nb, const SearchOptions& opt,
                       int64_t* d_ids, float* d_dists, int64_t* d_counts, uint64_t* d_keys,
                       cudaStream_t s, bool time_it);
+    int64_t prepare_batch(const float* d_q, const float* h_q, int64_t nb, int nprobe,
+                          const QueryState& st, cudaStream_t s, bool time_it);
+    int64_t scan_merge_batch(int64_t nb, const SearchOptions& opt, const QueryState& st,
+                             int64_t* d_ids, float* d_dists, int64_t* d_counts, uint64_t* d_keys,
+                             cudaStream_t s, bool time_it);
+    void collect_stage_ms(int first, int last);
     void run_search(const float* d_queries, const float* h_queries, int64_t nq,
                     const SearchOptions& opt, int64_t* d_ids, float* d_dists, int64_t* d_counts,
                     uint64_t* d_keys, cudaStream_t stream);

@@ -254,6 +254,25 @@ int32_t hanns_gpu_ivf_usq_search_shard_device(HannsIvfUsqHandle* h, const float*
                                               int64_t nq, int32_t k, int32_t nprobe,
                                               float* d_dists, uint64_t* d_keys, int64_t* d_ids,
                                               void* stream);
+/* Query-split multi-GPU search (no counterpart in the reference, whose search runs on one
+ * host).  Each rank prepares the per-query state of its share of the queries, the ranks
+ * all-gather it, and every rank scans its own lists for all queries:
+ *   hanns_gpu_ivf_usq_query_state_bytes: bytes per query of the five state arrays
+ *     (probes int32[nprobe], scalars, FastScan LUT, q_i8 dp4a layout, q_i8 in dimension
+ *     order) into out5.
+ *   hanns_gpu_ivf_usq_prepare_device: coarse probes, rotation and query state of nq
+ *     device-resident queries into the caller's device arrays (d_qi8n may be NULL).
+ *   hanns_gpu_ivf_usq_search_prepared_shard_device: grouping, list scan and merge of nq
+ *     queries from such arrays (concatenated over the ranks); output as
+ *     hanns_gpu_ivf_usq_search_shard_device. */
+int32_t hanns_gpu_ivf_usq_query_state_bytes(HannsIvfUsqHandle* h, int32_t nprobe, int64_t* out5);
+int32_t hanns_gpu_ivf_usq_prepare_device(HannsIvfUsqHandle* h, const float* d_queries, int64_t nq,
+                                         int32_t nprobe, void* d_probes, void* d_qp, void* d_lut,
+                                         void* d_qi8p, void* d_qi8n, void* stream);
+int32_t hanns_gpu_ivf_usq_search_prepared_shard_device(
+    HannsIvfUsqHandle* h, int64_t nq, int32_t k, int32_t nprobe, const void* d_probes,
+    const void* d_qp, const void* d_lut, const void* d_qi8p, const void* d_qi8n, float* d_dists,
+    uint64_t* d_keys, int64_t* d_ids, void* stream);
 /* The list -> rank owner map that hanns_gpu_ivf_usq_shard uses (host only, no GPU):
  * lists by decreasing size, each to the least-loaded rank. */
 int32_t hanns_gpu_shard_owners(const int64_t* list_sizes, int32_t nlist, int32_t world,

@@ -293,3 +293,50 @@ def test_coarse_fast_path_equals_exact(gpu, oracle_mod, nlist, d, nprobe, normal
     oi = O.OracleIndex(art)
     _, _, _, op = oi.search(q[:60], 5, nprobe, want_probes=True)
     assert np.array_equal(fast[:60], op)
+
+
+def test_query_split_shards_equal_single_gpu(gpu, oracle_mod):
+    """Query-split multi-GPU protocol on one device: two list shards of one index, each
+    prepares the state of half of the queries, the halves are concatenated (the NCCL
+    all-gather), each shard scans its lists for all queries, and merge_shards gives the
+    single-index rows bit for bit."""
+    import torch
+    from hanns_b200 import _lib
+    from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
+    from tests.golden.make_golden import mixture
+    O = oracle_mod
+    rng = np.random.default_rng(21)
+    d, k, nprobe, nq, world = 128, 10, 6, 600, 2
+    x, _ = mixture(rng, 20000, d, 32, 0.4, False)
+    q, _ = mixture(rng, nq, d, 32, 0.4, False)
+    art = O.build_artifact(x, 24, 4, O.METRIC_L2, rotation_seed=3, kmeans_iters=5, kmeans_seed=2)
+    full = IvfUsqIndex.from_artifact(art)
+    exp = full.search(q, SearchRequest(top_k=k, nprobe=nprobe))
+    shards = []
+    for r in range(world):
+        s = IvfUsqIndex.from_artifact(art)
+        s.shard(r, world)
+        shards.append(s)
+    L = gpu
+    parts = np.zeros(5, np.int64)
+    assert L.hanns_gpu_ivf_usq_query_state_bytes(shards[0]._h, nprobe, parts.ctypes.data_as(_lib.i64p)) == 0
+    bufs = [torch.zeros(nq * int(b), dtype=torch.uint8, device="cuda") for b in parts]
+    dq = torch.from_numpy(q).cuda()
+    per = nq // world
+    for r, s in enumerate(shards):
+        ptrs = [b.data_ptr() + r * per * int(p) for b, p in zip(bufs, parts)]
+        assert L.hanns_gpu_ivf_usq_prepare_device(s._h, dq.data_ptr() + r * per * d * 4, per, nprobe,
+                                                  *ptrs, None) == 0, _lib.last_error()
+    g_d = torch.empty(world, nq, k, dtype=torch.float32, device="cuda")
+    g_k = torch.empty(world, nq, k, dtype=torch.int64, device="cuda")
+    g_i = torch.empty(world, nq, k, dtype=torch.int64, device="cuda")
+    for r, s in enumerate(shards):
+        assert L.hanns_gpu_ivf_usq_search_prepared_shard_device(
+            s._h, nq, k, nprobe, *[b.data_ptr() for b in bufs], g_d[r].data_ptr(), g_k[r].data_ptr(),
+            g_i[r].data_ptr(), None) == 0, _lib.last_error()
+    out_i = torch.empty(nq, k, dtype=torch.int64, device="cuda")
+    out_d = torch.empty(nq, k, dtype=torch.float32, device="cuda")
+    assert L.hanns_gpu_merge_shards_device(g_d.data_ptr(), g_k.data_ptr(), g_i.data_ptr(), world, nq, k,
+                                           out_i.data_ptr(), out_d.data_ptr(), None) == 0
+    assert np.array_equal(out_i.cpu().numpy(), exp.ids.reshape(nq, k))
+    assert bits_eq(out_d.cpu().numpy(), exp.distances.reshape(nq, k))
