@@ -455,16 +455,20 @@ void IvfUsqGpu::add(const float* h_data, int64_t n, const int64_t* h_ids) {
 // to the currently least-loaded rank (ties: lower rank).  Host-only and deterministic, so
 // every rank computes the same owners.
 void shard_owners(const int64_t* sizes, int nlist, int world, int32_t* owner) {
+    // expected scan work of a list ~ |L| x (queries that probe it, ~ |L| when queries
+    // follow the data): longest-processing-time on |L|^2
+    std::vector<int64_t> weights(nlist);
+    for (int l = 0; l < nlist; ++l) weights[l] = sizes[l] * sizes[l];
     std::vector<int> order(nlist);
     std::iota(order.begin(), order.end(), 0);
     std::stable_sort(order.begin(), order.end(),
-                     [&](int a, int b) { return sizes[a] > sizes[b]; });
+                     [&](int a, int b) { return weights[a] > weights[b]; });
     std::vector<int64_t> load(world, 0);
     for (int l : order) {
         int best = 0;
         for (int r = 1; r < world; ++r)
             if (load[r] < load[best]) best = r;
-        load[best] += sizes[l];
+        load[best] += weights[l];
         owner[l] = best;
     }
 }

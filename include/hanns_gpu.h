@@ -274,7 +274,8 @@ int32_t hanns_gpu_ivf_usq_search_prepared_shard_device(
     const void* d_qp, const void* d_lut, const void* d_qi8p, const void* d_qi8n, float* d_dists,
     uint64_t* d_keys, int64_t* d_ids, void* stream);
 /* The list -> rank owner map that hanns_gpu_ivf_usq_shard uses (host only, no GPU):
- * lists by decreasing size, each to the least-loaded rank. */
+ * longest-processing-time on |L|^2 (scan work ~ list size x probes of the list), lists
+ * by decreasing weight, each to the least-loaded rank. */
 int32_t hanns_gpu_shard_owners(const int64_t* list_sizes, int32_t nlist, int32_t world,
                                int32_t* owner);
 /* Merges world shard results laid out [world][nq][k] into the global top-k

@@ -106,6 +106,7 @@ def test_shard_owners_balanced():
         owner = np.zeros(4096, np.int32)
         assert L.hanns_gpu_shard_owners(sizes.ctypes.data_as(_lib.i64p), 4096, world,
                                         owner.ctypes.data_as(_lib.i32p)) == 0
-        loads = np.bincount(owner, weights=sizes, minlength=world)
+        w = sizes.astype(np.float64) ** 2
+        loads = np.bincount(owner, weights=w, minlength=world)
         assert owner.min() >= 0 and owner.max() < world
-        assert loads.max() - loads.min() <= sizes.max()
+        assert loads.max() - loads.min() <= w.max()
