@@ -170,6 +170,7 @@ int64_t IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32
     const int64_t cchunk = std::max<int64_t>(1, std::min<int64_t>(nb, (1ll << 28) / nlist_));
     w_dist_.reserve((size_t)cchunk * nlist_);
     w_fallbacks_.reserve(2);
+    w_rs_.reserve((size_t)cchunk * (kCoarseRescoreMax + 1));
     HANNS_CUDA_OK(cudaMemsetAsync(w_fallbacks_.p, 0, 2 * sizeof(int), s));
     if (nprobe > 256) {  // candidate buffers hold 512: large nprobe takes the exact kernels
         w_sel_.reserve((size_t)cchunk * 2 * nprobe);
@@ -208,10 +209,11 @@ int64_t IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32
         if (!used_tc)
             launch_coarse_gemm(d_q + c * dim_, m, centroids_.p, cn_.p, nlist_, dim_, w_dist_.p, s);
         if (mid_event && c == 0) HANNS_CUDA_OK(cudaEventRecord(mid_event, s));
-        launch_coarse_select(w_dist_.p, d_q + c * dim_, m, centroids_.p, nlist_, dim_, nprobe, cmax_,
-                             used_tc ? rel_tc : rel_simt, used_tc ? w_fallbacks_.p + 1 : nullptr,
-                             d_probes + c * nprobe, w_fallbacks_.p, s);
-        launches += used_tc ? 1 : 2;
+        launches += launch_coarse_select(w_dist_.p, d_q + c * dim_, m, centroids_.p, nlist_, dim_,
+                                         nprobe, cmax_, used_tc ? rel_tc : rel_simt,
+                                         used_tc ? w_fallbacks_.p + 1 : nullptr,
+                                         d_probes + c * nprobe, w_fallbacks_.p, w_rs_.p, s);
+        launches += used_tc ? 0 : 1;
     }
     return launches;
 }

@@ -178,7 +178,7 @@ class IvfUsqGpu {
     DevBuf<QueryParams> w_qp_;
     DevBuf<uint8_t> w_qi8p_, w_lut_;
     DevBuf<int8_t> w_qi8n_;
-    DevBuf<int> w_cnt_, w_cursor_, w_lq_off_, w_item_off_, w_counters_, w_pair_off_;
+    DevBuf<int> w_cnt_, w_cursor_, w_lq_off_, w_item_off_, w_counters_, w_pair_off_, w_rs_;
     DevBuf<int2> w_lq_;
     DevBuf<int4> w_items_;
     DevBuf<uint64_t> w_mtie_, w_cand_tie_, w_bits_;

@@ -118,9 +118,13 @@ void launch_select_probes(const float* dist, int64_t nq, int nlist, int nprobe, 
 // Approximate-then-exact coarse step (same probes as the two launches above).
 void launch_coarse_gemm(const float* q, int64_t nq, const float* cent, const float* cn, int nlist,
                         int d, float* approx, cudaStream_t s);
-void launch_coarse_select(float* approx, const float* q, int64_t nq, const float* cent, int nlist,
+// Candidates per query handed from the select kernel to the re-score kernel; rs holds
+// nq x (kCoarseRescoreMax + 1) ints (count, then centroid ids).  rs may be null (the
+// select kernel then re-scores itself).
+constexpr int kCoarseRescoreMax = 64;
+int launch_coarse_select(float* approx, const float* q, int64_t nq, const float* cent, int nlist,
                           int d, int nprobe, float cmax, float dot_rel, const int* tc_err,
-                          int32_t* probes, int* fallbacks, cudaStream_t s);
+                          int32_t* probes, int* fallbacks, int* rs, cudaStream_t s);
 // Tensor-core approximation of the coarse scores (coarse_tc.cu).
 int coarse_tc_k(int d);
 void launch_split_bf16(const float* x, int64_t rows, int d, int K, void* hi, void* lo,

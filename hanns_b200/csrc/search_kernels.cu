@@ -519,6 +519,81 @@ __device__ uint32_t block_select_kth(ForEach for_each, int kth, uint32_t* hist, 
     return kmin + (uint32_t)bcast[4];
 }
 
+// An upper bound of the k-th smallest value, for a threshold that only has to admit the
+// k smallest: one pass bins the values uniformly between their minimum and maximum
+// (the binning is monotone in the value), the bin holding the k-th value is found from
+// the histogram, and the largest value in that bin is returned.  for_each(f) calls f(v)
+// for every value of the calling thread; hist: kSelBins words, list: 64 words, bcast: 8.
+template <class ForEach>
+__device__ float block_kth_upper(ForEach for_each, int kth, uint32_t* hist, uint32_t* list,
+                                 int* bcast) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    float lo = __int_as_float(0x7f800000), hi = -__int_as_float(0x7f800000);
+    for_each([&](float v) {
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+    });
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if (lane == 0) {
+        list[w] = __float_as_uint(lo);
+        list[32 + w] = __float_as_uint(hi);
+    }
+    for (int i = tid; i < kSelBins; i += kSelThreads) hist[i] = 0;
+    __syncthreads();
+    if (tid == 0) {
+        float a = __uint_as_float(list[0]), b = __uint_as_float(list[32]);
+        for (int j = 1; j < kSelThreads / 32; ++j) {
+            a = fminf(a, __uint_as_float(list[j]));
+            b = fmaxf(b, __uint_as_float(list[32 + j]));
+        }
+        reinterpret_cast<float*>(bcast)[6] = a;
+        reinterpret_cast<float*>(bcast)[7] = b;
+    }
+    __syncthreads();
+    const float vmin = reinterpret_cast<float*>(bcast)[6], vmax = reinterpret_cast<float*>(bcast)[7];
+    if (!(vmax > vmin)) return vmax;
+    const float scale = __fdiv_rn((float)kSelBins, __fsub_rn(vmax, vmin));
+    auto bin_of = [&](float v) {
+        const int b = (int)__fmul_rz(__fsub_rn(v, vmin), scale);
+        return min(max(b, 0), kSelBins - 1);
+    };
+    for_each([&](float v) { atomicAdd(&hist[bin_of(v)], 1u); });
+    __syncthreads();
+    int s = 0;
+#pragma unroll
+    for (int b = 0; b < 16; ++b) s += (int)hist[tid * 16 + b];
+    const int incl = warp_inclusive_scan(s);
+    if (lane == 31) list[w] = (uint32_t)incl;
+    __syncthreads();
+    int off = 0;
+    for (int j = 0; j < w; ++j) off += (int)list[j];
+    const int lo_c = off + incl - s, hi_c = off + incl;
+    if (lo_c < kth && kth <= hi_c) {
+        int c = lo_c, bin = tid * 16;
+        for (int b = 0; b < 16; ++b) {
+            const int h = (int)hist[tid * 16 + b];
+            if (c + h >= kth) {
+                bin = tid * 16 + b;
+                break;
+            }
+            c += h;
+        }
+        bcast[0] = bin;
+        bcast[1] = 0;  // total-order key of the bin's largest value
+    }
+    __syncthreads();
+    const int bin = bcast[0];
+    for_each([&](float v) {
+        if (bin_of(v) == bin) atomicMax(reinterpret_cast<unsigned*>(&bcast[1]), total_order_key(v));
+    });
+    __syncthreads();
+    return key_to_float((uint32_t)bcast[1]);
+}
+
 // k-th smallest total-order key of row[0..n) (shared or global memory).
 __device__ uint32_t block_radix_kth(const float* row, int n, int kth, uint32_t* hist,
                                     uint32_t* list, int* bcast) {
@@ -627,23 +702,6 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
     if (w == 0) warp_select_stable(row, nlist, nprobe, hist, ckey, cidx, probes + qi * nprobe);
 }
 
-// Re-score staging: candidates (<= kRsMax) x 32-dimension chunks, 4 slots; the row stride
-// of 36 floats keeps each thread's 16-byte reads of its own row conflict-free.
-constexpr int kRsDims = 32, kRsSlots = 4, kRsMax = 64, kRsStride = 36;
-constexpr size_t kRsBytes = (size_t)kRsSlots * kRsMax * kRsStride * sizeof(float);
-
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                     (uint32_t)__cvta_generic_to_shared(smem_dst)),
-                 "l"(gsrc)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // One 256-thread block per query, the approximate row held in registers (NV4 float4 per
 // thread, nlist <= 1024 * NV4, nlist % 4 == 0, d % 4 == 0).  Same result as
 // coarse_select_block_kernel: k-th approximate key -> rigorous threshold -> exact
@@ -652,8 +710,9 @@ template <int NV4>
 __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
     float* __restrict__ approx, const float* __restrict__ q, int64_t nq,
     const float* __restrict__ cent, int nlist, int d, int nprobe, float cmax, float dot_rel,
-    const int* __restrict__ tc_err, int32_t* __restrict__ probes, int* __restrict__ fallbacks) {
-    extern __shared__ __align__(16) float sm[];  // qs[d], {hist[kSelBins], list[kSelList]} | ring
+    const int* __restrict__ tc_err, int32_t* __restrict__ probes, int* __restrict__ fallbacks,
+    int* __restrict__ rs) {
+    extern __shared__ __align__(16) float sm[];  // qs[d], hist[kSelBins], list[kSelList]
     __shared__ int bcast[8];
     __shared__ float red[kSelThreads / 32];
     __shared__ int cidx[kCoarseCap];
@@ -667,6 +726,7 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
     uint32_t* list = hist + kSelBins;
     const int n4 = nlist >> 2;
     float* grow = approx + qi * nlist;
+    if (rs && tid == 0) rs[qi * (kCoarseRescoreMax + 1)] = 0;  // 0: probes written here
     // the row: float4 index tid + 256 j, all loads issued before the first use
     float4 v[NV4];
 #pragma unroll
@@ -700,20 +760,22 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
     for (int o = 16; o > 0; o >>= 1) qn = __fadd_rn(qn, __shfl_xor_sync(0xffffffffu, qn, o));
     if (lane == 0) red[w] = qn;
     if (tid == 0) cnt_s = 0;
-    const uint32_t tau_key = block_select_kth(
+    // an upper bound of the nprobe-th smallest approximate score is enough: the threshold
+    // only has to admit the exact top nprobe
+    const float tau_up = block_kth_upper(
         [&](auto f) {
 #pragma unroll
             for (int j = 0; j < NV4; ++j)
                 if (valid(j))
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) f(total_order_key(val(j, e)));
+                    for (int e = 0; e < 4; ++e) f(val(j, e));
         },
         nprobe, hist, list, bcast);
     if (tid == 0) {
         float qsum = 0.0f;
         for (int i = 0; i < kSelThreads / 32; ++i) qsum = __fadd_rn(qsum, red[i]);
         // (double)x <= thr  <=>  x <= thr rounded down to a float
-        thr_s = __double2float_rd(coarse_threshold(key_to_float(tau_key), qsum, cmax, d, dot_rel));
+        thr_s = __double2float_rd(coarse_threshold(tau_up, qsum, cmax, d, dot_rel));
     }
     __syncthreads();
     const float thr = thr_s;
@@ -730,53 +792,14 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
     const int cnt = cnt_s;
     const bool approx_ok = !tc_err || *tc_err == 0;
     if (approx_ok && cnt <= kCoarseCap && cnt >= nprobe) {
-        if (cnt <= kRsMax) {
-            // candidate rows stream through a 4-slot ring of 32-dimension chunks (cp.async,
-            // all threads); thread c runs candidate c's sequential sum from shared memory
-            float* ring = reinterpret_cast<float*>(hist);  // [kRsSlots][kRsMax][kRsStride]
-            const int nch = (d + kRsDims - 1) / kRsDims;
-            auto issue = [&](int k) {
-                if (k < nch) {
-                    float* slot = ring + (k % kRsSlots) * kRsMax * kRsStride;
-                    for (int e = tid; e < cnt * (kRsDims / 4); e += kSelThreads) {
-                        const int c = e / (kRsDims / 4), p = e % (kRsDims / 4);
-                        const int d0 = k * kRsDims + 4 * p;
-                        if (d0 < d) cp_async16(slot + c * kRsStride + 4 * p, cent + (int64_t)cidx[c] * d + d0);
-                    }
-                }
-                cp_async_commit();
-            };
-            for (int k = 0; k < kRsSlots - 1; ++k) issue(k);
-            float sacc = -0.0f;
-            for (int k = 0; k < nch; ++k) {
-                cp_async_wait<kRsSlots - 2>();
-                __syncthreads();
-                if (tid < cnt) {
-                    const float4* c4 = reinterpret_cast<const float4*>(
-                        ring + (k % kRsSlots) * kRsMax * kRsStride + tid * kRsStride);
-                    const float4* q4 = reinterpret_cast<const float4*>(qs + k * kRsDims);
-                    const int nd4 = min(kRsDims, d - k * kRsDims) / 4;
-                    for (int j = 0; j < nd4; ++j) {
-                        const float4 cv = c4[j], qv = q4[j];
-                        float df = __fsub_rn(qv.x, cv.x);
-                        sacc = __fadd_rn(sacc, __fmul_rn(df, df));
-                        df = __fsub_rn(qv.y, cv.y);
-                        sacc = __fadd_rn(sacc, __fmul_rn(df, df));
-                        df = __fsub_rn(qv.z, cv.z);
-                        sacc = __fadd_rn(sacc, __fmul_rn(df, df));
-                        df = __fsub_rn(qv.w, cv.w);
-                        sacc = __fadd_rn(sacc, __fmul_rn(df, df));
-                    }
-                }
-                __syncthreads();
-                issue(k + kRsSlots - 1);
-            }
-            cp_async_wait<0>();
-            if (tid < cnt) ckey[tid] = total_order_key(sacc);
-        } else {
-            for (int i = tid; i < cnt; i += kSelThreads)
-                ckey[i] = total_order_key(exact_l2(qs, cent + (int64_t)cidx[i] * d, d));
+        if (cnt <= kCoarseRescoreMax && rs) {
+            // the exact re-score runs in coarse_rescore_kernel (one thread per candidate)
+            for (int i = tid; i < cnt; i += kSelThreads) rs[qi * (kCoarseRescoreMax + 1) + 1 + i] = cidx[i];
+            if (tid == 0) rs[qi * (kCoarseRescoreMax + 1)] = cnt;
+            return;
         }
+        for (int i = tid; i < cnt; i += kSelThreads)
+            ckey[i] = total_order_key(exact_l2(qs, cent + (int64_t)cidx[i] * d, d));
         __syncthreads();
         for (int i = tid; i < cnt; i += kSelThreads) {
             const uint32_t ki = ckey[i];
@@ -793,6 +816,35 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
     for (int c = tid; c < nlist; c += kSelThreads) grow[c] = exact_l2(qs, cent + (int64_t)c * d, d);
     __syncthreads();
     if (w == 0) warp_select_stable(grow, nlist, nprobe, hist, ckey, cidx, probes + qi * nprobe);
+}
+
+// Exact re-score of the candidates coarse_select_reg_kernel left in rs (per query: count,
+// then up to kCoarseRescoreMax centroid ids): one thread per candidate runs the reference's
+// sequential sum (exact_l2), so thousands of these latency-bound chains are in flight per
+// SM; then the block orders its query's candidates stably and writes the probes.
+__global__ void __launch_bounds__(kCoarseRescoreMax) coarse_rescore_kernel(const float* __restrict__ q, int64_t nq,
+                                                                 const float* __restrict__ cent, int d,
+                                                                 int nprobe, const int* __restrict__ rs,
+                                                                 int32_t* __restrict__ probes) {
+    extern __shared__ __align__(16) float qsm[];  // [d]
+    __shared__ uint32_t ckey[kCoarseRescoreMax];
+    __shared__ int cidx[kCoarseRescoreMax];
+    const int64_t qi = blockIdx.x;
+    const int cnt = rs[qi * (kCoarseRescoreMax + 1)];
+    if (cnt == 0) return;  // done by the select kernel
+    const int tid = threadIdx.x;
+    for (int i = tid; i < d; i += kCoarseRescoreMax) qsm[i] = q[qi * d + i];
+    const int ci = tid < cnt ? rs[qi * (kCoarseRescoreMax + 1) + 1 + tid] : 0;
+    cidx[tid] = ci;
+    __syncthreads();
+    if (tid < cnt) ckey[tid] = total_order_key(exact_l2(qsm, cent + (int64_t)ci * d, d));
+    __syncthreads();
+    if (tid < cnt) {
+        const uint32_t ki = ckey[tid];
+        int rank = 0;
+        for (int j = 0; j < cnt; ++j) rank += (ckey[j] < ki || (ckey[j] == ki && cidx[j] < ci)) ? 1 : 0;
+        if (rank < nprobe) probes[qi * nprobe + rank] = ci;
+    }
 }
 
 __global__ void centroid_norms_kernel(const float* __restrict__ cent, int nlist, int d,
@@ -1633,25 +1685,27 @@ void launch_coarse_gemm(const float* q, int64_t nq, const float* cent, const flo
         coarse_gemm_kernel<false><<<grid, 256, 0, s>>>(q, nq, cent, nlist, d, cn, approx);
 }
 
-void launch_coarse_select(float* approx, const float* q, int64_t nq, const float* cent, int nlist,
+int launch_coarse_select(float* approx, const float* q, int64_t nq, const float* cent, int nlist,
                           int d, int nprobe, float cmax, float dot_rel, const int* tc_err,
-                          int32_t* probes, int* fallbacks, cudaStream_t s) {
-    if (nq <= 0) return;
-    const size_t reg_bytes =
-        (size_t)d * sizeof(float) + std::max((size_t)(kSelBins + kSelList) * sizeof(float), kRsBytes);
+                          int32_t* probes, int* fallbacks, int* rs, cudaStream_t s) {
+    if (nq <= 0) return 0;
+    const size_t reg_bytes = ((size_t)d + kSelBins + kSelList) * sizeof(float);
     if ((nlist & 3) == 0 && (d & 3) == 0 && nlist <= 16 * kSelThreads &&
         reg_bytes <= 112 * 1024) {
         const int nv4 = (nlist / 4 + kSelThreads - 1) / kSelThreads;  // float4 per thread
         auto go = [&](auto kern) {
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
             kern<<<(unsigned)nq, kSelThreads, reg_bytes, s>>>(approx, q, nq, cent, nlist, d, nprobe,
-                                                               cmax, dot_rel, tc_err, probes, fallbacks);
+                                                               cmax, dot_rel, tc_err, probes, fallbacks, rs);
         };
         if (nv4 <= 1) go(coarse_select_reg_kernel<1>);
         else if (nv4 == 2) go(coarse_select_reg_kernel<2>);
         else if (nv4 == 3) go(coarse_select_reg_kernel<3>);
         else go(coarse_select_reg_kernel<4>);
-        return;
+        if (rs)
+            coarse_rescore_kernel<<<(unsigned)nq, kCoarseRescoreMax, (size_t)d * sizeof(float), s>>>(
+                q, nq, cent, d, nprobe, rs, probes);
+        return rs ? 2 : 1;
     }
     const size_t blk_bytes =
         ((size_t)((nlist + 3) & ~3) + ((d + 3) & ~3) + kSelBins + kSelList) * sizeof(float);
@@ -1667,6 +1721,7 @@ void launch_coarse_select(float* approx, const float* q, int64_t nq, const float
         coarse_select_exact_kernel<<<(unsigned)((nq + 3) / 4), 128, qbytes, s>>>(
             approx, q, nq, cent, nlist, d, nprobe, cmax, dot_rel, tc_err, probes, fallbacks);
     }
+    return 1;
 }
 
 void launch_centroid_norms(const float* cent, int nlist, int d, float* cn, cudaStream_t s) {
