@@ -1149,10 +1149,18 @@ __global__ void pair_offsets_kernel(const int32_t* __restrict__ probes, int64_t 
 constexpr int kScanThreads = 256;
 constexpr int kScanWarps = kScanThreads / 32;  // queries handled concurrently
 
+constexpr int kScanMaxQ = 32;  // queries per item (the grouping step's limit)
+constexpr int kSvMax = 384;    // kept rows per (query, list) held in shared memory
+
 struct ScanSmem {
     uint32_t hist[kScanWarps][256];
-    int64_t base[kScanWarps];  // candidate region of each warp's (query, probe) pair
-    int nc[kScanWarps];        // kept candidates of each warp's pair
+    // the item's queries: scalars, candidate region of the (query, probe) pair, query id,
+    // probe rank, bitset row (-1: none)
+    QueryParams qp[kScanMaxQ];
+    int64_t qbase[kScanMaxQ];
+    int q[kScanMaxQ], rank[kScanMaxQ], bsi[kScanMaxQ];
+    uint32_t sv[kScanWarps][kSvMax];  // kept rows of each warp's (query, list) pair
+    int nc[kScanWarps];               // kept candidates of each warp's pair
     int item;
     int pad[3];  // keeps the dynamic arrays after it 16-byte aligned
 };
@@ -1204,18 +1212,65 @@ __device__ __forceinline__ int int_ip_group8(const uint8_t* __restrict__ code,
 }
 
 
-__device__ __forceinline__ const uint64_t* query_bitset_words(const ScanArgs& a, int q) {
-    if (!a.fused || !a.bitsets) return nullptr;
-    const int b = a.query_bitset ? a.query_bitset[q] : 0;
-    return (b >= 0 && b < a.n_bitsets) ? a.bitsets + (int64_t)b * a.bitset_words : nullptr;
+// int_ip_group8 with every code load of the lane issued before the first dot product (one
+// memory round trip per row); nu_max = NU * 8 code uint4 per row at most.  q is read in
+// the dot loop (shared memory or L1-resident rows).
+template <int NU>
+__device__ __forceinline__ int int_ip_group8_pf(const uint8_t* __restrict__ code, const uint8_t* q,
+                                                int D, int nbits, int sub, bool active) {
+    int acc0 = 0, acc1 = 0;
+    if (active) {
+        const uint4* c4 = reinterpret_cast<const uint4*>(code);
+        const uint4* q4 = reinterpret_cast<const uint4*>(q);
+        const int nu = nbits == 8 ? D / 16 : D / 32;
+        uint4 c[NU];
+#pragma unroll
+        for (int u = 0; u < NU; ++u) {
+            const int i = sub + 8 * u;
+            c[u] = i < nu ? __ldg(c4 + i) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < NU; ++u) {
+            const int i = sub + 8 * u;
+            if (i >= nu) break;
+            if (nbits == 8) {
+                const uint4 qv = q4[i];
+                acc0 = dp4a_us(c[u].x, qv.x, acc0);
+                acc1 = dp4a_us(c[u].y, qv.y, acc1);
+                acc0 = dp4a_us(c[u].z, qv.z, acc0);
+                acc1 = dp4a_us(c[u].w, qv.w, acc1);
+            } else {
+                const uint4 qa = q4[2 * i], qb = q4[2 * i + 1];
+                acc0 = dp4a_us(c[u].x & 0x0F0F0F0Fu, qa.x, acc0);
+                acc1 = dp4a_us((c[u].x >> 4) & 0x0F0F0F0Fu, qa.y, acc1);
+                acc0 = dp4a_us(c[u].y & 0x0F0F0F0Fu, qa.z, acc0);
+                acc1 = dp4a_us((c[u].y >> 4) & 0x0F0F0F0Fu, qa.w, acc1);
+                acc0 = dp4a_us(c[u].z & 0x0F0F0F0Fu, qb.x, acc0);
+                acc1 = dp4a_us((c[u].z >> 4) & 0x0F0F0F0Fu, qb.y, acc1);
+                acc0 = dp4a_us(c[u].w & 0x0F0F0F0Fu, qb.z, acc0);
+                acc1 = dp4a_us((c[u].w >> 4) & 0x0F0F0F0Fu, qb.w, acc1);
+            }
+        }
+    }
+    int acc = acc0 + acc1;
+    acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    return acc;
 }
+
+constexpr int kPfUnits = 3;  // rows of up to 24 code uint4 (4-bit D <= 768, 8-bit D <= 384)
 
 __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ScanSmem& sm = *reinterpret_cast<ScanSmem*>(smem_raw);
     uint32_t* lut4 = reinterpret_cast<uint32_t*>(smem_raw + sizeof(ScanSmem));  // [G*16]
+    // q_i8 (dp4a layout) of the current FastScan query group, rows padded by 16 bytes
+    uint8_t* qsm = reinterpret_cast<uint8_t*>(lut4 + a.G * 16);  // [kScanWarps][D + 16]
+    const int qld = a.D + 16;
     const int tid = threadIdx.x, w = tid >> 5, lane = (int)lane_id();
     const int grp = lane >> 3, sub = lane & 7;  // 4 groups of 8 lanes per warp
+    const bool pf = (a.nbits == 8 ? a.D / 16 : a.D / 32) <= 8 * kPfUnits;
     int16_t* my_scores_base = a.scores + (int64_t)blockIdx.x * kScanWarps * a.max_len;
     const bool l2 = a.metric_l2 != 0;
     const int pstride = a.nprobe + 1;
@@ -1231,6 +1286,21 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
         const int64_t beg = a.list_off[l];
         const int n = (int)(a.list_off[l + 1] - beg);
         if (n > a.n_cand && n <= a.tc_rows) continue;  // scanned by scan_tc_kernel
+        // the item's queries, staged once (no dependent global loads in the rerank loops)
+        if (tid < it.z) {
+            const int2 pr = a.lq[it.y + tid];
+            sm.q[tid] = pr.x;
+            sm.rank[tid] = pr.y;
+            sm.qbase[tid] = (int64_t)pr.x * a.q_stride + a.pair_off[(int64_t)pr.x * pstride + pr.y];
+            sm.qp[tid] = a.qp[pr.x];
+            int b = -1;
+            if (a.fused && a.bitsets) {
+                b = a.query_bitset ? a.query_bitset[pr.x] : 0;
+                if (b < 0 || b >= a.n_bitsets) b = -1;
+            }
+            sm.bsi[tid] = b;
+        }
+        __syncthreads();
         if (n <= a.n_cand) {
             // no FastScan: every live row is a candidate of every query of the item;
             // (query, row) pairs spread over the CTA's 8-lane groups
@@ -1238,32 +1308,33 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
             for (int e0 = w * 4; e0 < total; e0 += kScanWarps * 4) {
                 const int e = e0 + grp;
                 const bool act = e < total;
-                int v = 0, q = 0, rank = 0;
+                int i = 0, v = 0;
                 if (act) {
-                    const int i = e / n;
+                    i = e / n;
                     v = e - i * n;
-                    const int2 pr = a.lq[it.y + i];
-                    q = pr.x;
-                    rank = pr.y;
                 }
+                const int q = sm.q[i];
                 const int64_t row = beg + v;
                 bool dead = false;
                 float4 m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 if (act) {
-                    const uint64_t* bw = query_bitset_words(a, q);
-                    dead = bw && bit_filtered(bw, a.bitset_len, a.ids[row]);
+                    const int b = sm.bsi[i];
+                    dead = b >= 0 && bit_filtered(a.bitsets + (int64_t)b * a.bitset_words, a.bitset_len, a.ids[row]);
                     m = __ldg(a.meta + row);
                 }
-                const int iip = int_ip_group8(a.codes + row * a.code_bytes, a.q_i8p + (int64_t)q * a.D,
-                                              a.D, a.nbits, sub, act && !dead && m.w > 1e-12f);
+                const uint8_t* crow = a.codes + row * a.code_bytes;
+                const uint8_t* qrow = a.q_i8p + (int64_t)q * a.D;
+                const bool need = act && !dead && m.w > 1e-12f;
+                const int iip = pf ? int_ip_group8_pf<kPfUnits>(crow, qrow, a.D, a.nbits, sub, need)
+                                   : int_ip_group8(crow, qrow, a.D, a.nbits, sub, need);
                 if (act && sub == 0) {
-                    const int64_t dst = (int64_t)q * a.q_stride + a.pair_off[(int64_t)q * pstride + rank] + v;
+                    const int64_t dst = sm.qbase[i] + v;
                     if (dead) {
                         a.cand_key[dst] = 0xFFFFFFFFu;
                         a.cand_tie[dst] = ~0ull;
                     } else {
-                        a.cand_key[dst] = total_order_key(rerank_distance(iip, m, a.qp[q], a.nbits, l2));
-                        a.cand_tie[dst] = ((uint64_t)rank << 48) | (uint32_t)v;
+                        a.cand_key[dst] = total_order_key(rerank_distance(iip, m, sm.qp[i], a.nbits, l2));
+                        a.cand_tie[dst] = ((uint64_t)sm.rank[i] << 48) | (uint32_t)v;
                     }
                 }
             }
@@ -1281,10 +1352,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                     for (int t = 0; t < 4; ++t) {
                         const int qq = qg + quad * 4 + t;
                         L[t] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
-                        if (qq < it.z) {
-                            const int qidx = a.lq[it.y + qq].x;
-                            L[t] = __ldg(reinterpret_cast<const uint4*>(a.lut + (int64_t)qidx * a.G * 16) + m);
-                        }
+                        if (qq < it.z)
+                            L[t] = __ldg(reinterpret_cast<const uint4*>(a.lut + (int64_t)sm.q[qq] * a.G * 16) + m);
                     }
                     const uint32_t w0[4] = {L[0].x, L[0].y, L[0].z, L[0].w};
                     const uint32_t w1[4] = {L[1].x, L[1].y, L[1].z, L[1].w};
@@ -1349,9 +1418,9 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                 __syncthreads();
             }
             if (w < nq_here) {
-                const int2 pr = a.lq[it.y + qg + w];
-                const int q = pr.x, rank = pr.y;
-                const uint64_t* bw = query_bitset_words(a, q);
+                const int qs_ = qg + w;
+                const int rank = sm.rank[qs_];
+                const uint64_t* bw = sm.bsi[qs_] >= 0 ? a.bitsets + (int64_t)sm.bsi[qs_] * a.bitset_words : nullptr;
                 auto live = [&](int v) {
                     return !bw || !bit_filtered(bw, a.bitset_len, a.ids[beg + v]);
                 };
@@ -1362,8 +1431,9 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                     n_live = warp_sum(c);
                 }
                 const int16_t* sc = my_scores_base + (int64_t)w * a.max_len;
-                const int64_t rbase = (int64_t)q * a.q_stride + a.pair_off[(int64_t)q * pstride + rank];
+                const int64_t rbase = sm.qbase[qs_];
                 uint64_t* my_tie = a.cand_tie + rbase;
+                uint32_t* my_sv = a.n_cand <= kSvMax ? sm.sv[w] : nullptr;
                 const uint64_t rank_bits = (uint64_t)rank << 48;
                 int n_c = 0;  // kept candidates written to my_tie
                 if (n_live > a.n_cand) {
@@ -1410,7 +1480,10 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                         const unsigned bk = __ballot_sync(0xffffffffu, keep);
                         if (keep) {
                             const int pos = n_c + __popc(bk & lanemask_lt());
-                            if (pos < a.n_cand) my_tie[pos] = rank_bits | ((uint64_t)k << 32) | (uint32_t)v;
+                            if (pos < a.n_cand) {
+                                my_tie[pos] = rank_bits | ((uint64_t)k << 32) | (uint32_t)v;
+                                if (my_sv) my_sv[pos] = (uint32_t)v;
+                            }
                         }
                         n_c += __popc(bk);
                         eq_seen += __popc(beq);
@@ -1420,7 +1493,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                         const int v = base + lane;
                         const bool keep = v < n && live(v);
                         const unsigned bk = __ballot_sync(0xffffffffu, keep);
-                        if (keep) my_tie[n_c + __popc(bk & lanemask_lt())] = rank_bits | (uint32_t)v;
+                        if (keep) {
+                            const int pos = n_c + __popc(bk & lanemask_lt());
+                            my_tie[pos] = rank_bits | (uint32_t)v;
+                            if (my_sv) my_sv[pos] = (uint32_t)v;
+                        }
                         n_c += __popc(bk);
                     }
                 }
@@ -1430,10 +1507,14 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                     my_tie[j] = ~0ull;
                     a.cand_key[rbase + j] = 0xFFFFFFFFu;
                 }
-                if (lane == 0) {
-                    sm.base[w] = rbase;
-                    sm.nc[w] = n_c;
-                }
+                if (lane == 0) sm.nc[w] = n_c;
+            }
+            __syncthreads();
+            // the group's q_i8 rows into shared memory
+            for (int e = tid; e < nq_here * (a.D / 16); e += kScanThreads) {
+                const int i = e / (a.D / 16), c = e - i * (a.D / 16);
+                *reinterpret_cast<uint4*>(qsm + i * qld + 16 * c) =
+                    __ldg(reinterpret_cast<const uint4*>(a.q_i8p + (int64_t)sm.q[qg + i] * a.D) + c);
             }
             __syncthreads();
             // integer rerank of the group's kept candidates, 4 per warp at a time
@@ -1446,18 +1527,22 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                     j = e - i * a.n_cand;
                 }
                 const bool act = e < total && j < sm.nc[i];
-                const int q = a.lq[it.y + qg + i].x;
+                const int qs_ = qg + i;
                 uint32_t v = 0;
                 float4 m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 if (act) {
-                    v = (uint32_t)a.cand_tie[sm.base[i] + j];  // written by this CTA: coherent load
+                    // kept rows: shared memory, or the ties this CTA wrote (coherent load)
+                    v = a.n_cand <= kSvMax ? sm.sv[i][j] : (uint32_t)a.cand_tie[sm.qbase[qs_] + j];
                     m = __ldg(a.meta + beg + v);
                 }
                 const int64_t row = beg + v;
-                const int iip = int_ip_group8(a.codes + row * a.code_bytes, a.q_i8p + (int64_t)q * a.D,
-                                              a.D, a.nbits, sub, act && m.w > 1e-12f);
+                const uint8_t* crow = a.codes + row * a.code_bytes;
+                const bool need = act && m.w > 1e-12f;
+                const int iip = pf ? int_ip_group8_pf<kPfUnits>(crow, qsm + i * qld, a.D, a.nbits, sub, need)
+                                   : int_ip_group8(crow, qsm + i * qld, a.D, a.nbits, sub, need);
                 if (act && sub == 0)
-                    a.cand_key[sm.base[i] + j] = total_order_key(rerank_distance(iip, m, a.qp[q], a.nbits, l2));
+                    a.cand_key[sm.qbase[qs_] + j] =
+                        total_order_key(rerank_distance(iip, m, sm.qp[qs_], a.nbits, l2));
             }
             __syncthreads();
         }
@@ -1762,7 +1847,7 @@ void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist
 }
 
 size_t scan_smem_bytes(int D) {
-    return sizeof(ScanSmem) + (size_t)(D / 4) * 16 * sizeof(uint32_t);
+    return sizeof(ScanSmem) + (size_t)(D / 4) * 16 * sizeof(uint32_t) + (size_t)kScanWarps * (D + 16);
 }
 
 int scan_grid_size(int D) {
