@@ -58,8 +58,11 @@ __device__ __forceinline__ float rerank_distance(int iip, float4 m, const QueryP
     if (m.w <= 1e-12f) {
         score = p.centroid_score;
     } else {
-        const float levels = (float)(1u << nbits);
-        const float code_scale = __fdiv_rn(__fmul_rn(2.0f, m.z), fmaxf(levels, 1.0f));
+        // (2 vmax) / 2^nbits: dividing by a power of two and multiplying by its exact
+        // reciprocal round the same real number, so the product equals the reference's
+        // quotient bit for bit
+        const float inv_levels = __uint_as_float((uint32_t)(127 - nbits) << 23);
+        const float code_scale = __fmul_rn(__fmul_rn(2.0f, m.z), inv_levels);
         const float offset = -m.z;
         const float ip = __fmul_rn(
             p.q_scale, __fadd_rn(__fmul_rn(code_scale, __int2float_rn(iip)),

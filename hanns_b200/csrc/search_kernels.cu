@@ -1259,6 +1259,58 @@ __device__ __forceinline__ int int_ip_group8_pf(const uint8_t* __restrict__ code
     return acc;
 }
 
+// Two rows at once (their code loads all issued before either dot product).
+template <int NU>
+__device__ __forceinline__ int2 int_ip_group8_pf2(const uint8_t* __restrict__ code_a, const uint8_t* qa_,
+                                                  bool act_a, const uint8_t* __restrict__ code_b,
+                                                  const uint8_t* qb_, bool act_b, int D, int nbits,
+                                                  int sub) {
+    const int nu = nbits == 8 ? D / 16 : D / 32;
+    uint4 ca[NU], cb[NU];
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+        const int i = sub + 8 * u;
+        ca[u] = act_a && i < nu ? __ldg(reinterpret_cast<const uint4*>(code_a) + i) : make_uint4(0u, 0u, 0u, 0u);
+        cb[u] = act_b && i < nu ? __ldg(reinterpret_cast<const uint4*>(code_b) + i) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    auto dot = [&](const uint4 (&c)[NU], const uint8_t* q, bool act) {
+        int acc0 = 0, acc1 = 0;
+        if (act) {
+            const uint4* q4 = reinterpret_cast<const uint4*>(q);
+#pragma unroll
+            for (int u = 0; u < NU; ++u) {
+                const int i = sub + 8 * u;
+                if (i >= nu) break;
+                if (nbits == 8) {
+                    const uint4 qv = q4[i];
+                    acc0 = dp4a_us(c[u].x, qv.x, acc0);
+                    acc1 = dp4a_us(c[u].y, qv.y, acc1);
+                    acc0 = dp4a_us(c[u].z, qv.z, acc0);
+                    acc1 = dp4a_us(c[u].w, qv.w, acc1);
+                } else {
+                    const uint4 q0 = q4[2 * i], q1 = q4[2 * i + 1];
+                    acc0 = dp4a_us(c[u].x & 0x0F0F0F0Fu, q0.x, acc0);
+                    acc1 = dp4a_us((c[u].x >> 4) & 0x0F0F0F0Fu, q0.y, acc1);
+                    acc0 = dp4a_us(c[u].y & 0x0F0F0F0Fu, q0.z, acc0);
+                    acc1 = dp4a_us((c[u].y >> 4) & 0x0F0F0F0Fu, q0.w, acc1);
+                    acc0 = dp4a_us(c[u].z & 0x0F0F0F0Fu, q1.x, acc0);
+                    acc1 = dp4a_us((c[u].z >> 4) & 0x0F0F0F0Fu, q1.y, acc1);
+                    acc0 = dp4a_us(c[u].w & 0x0F0F0F0Fu, q1.z, acc0);
+                    acc1 = dp4a_us((c[u].w >> 4) & 0x0F0F0F0Fu, q1.w, acc1);
+                }
+            }
+        }
+        return acc0 + acc1;
+    };
+    int x = dot(ca, qa_, act_a), y = dot(cb, qb_, act_b);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+        x += __shfl_xor_sync(0xffffffffu, x, o);
+        y += __shfl_xor_sync(0xffffffffu, y, o);
+    }
+    return make_int2(x, y);
+}
+
 constexpr int kPfUnits = 3;  // rows of up to 24 code uint4 (4-bit D <= 768, 8-bit D <= 384)
 
 __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
@@ -1517,32 +1569,50 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                     __ldg(reinterpret_cast<const uint4*>(a.q_i8p + (int64_t)sm.q[qg + i] * a.D) + c);
             }
             __syncthreads();
-            // integer rerank of the group's kept candidates, 4 per warp at a time
+            // integer rerank of the group's kept candidates, 8 per warp at a time (two per
+            // group of 8 lanes, their loads issued together)
             const int total = nq_here * a.n_cand;
-            for (int e0 = w * 4; e0 < total; e0 += kScanWarps * 4) {
-                const int e = e0 + grp;
-                int i = 0, j = 0;
+            auto entry = [&](int e, int& i, int& j, bool& act, uint32_t& v, float4& m) {
+                i = 0;
+                j = 0;
                 if (e < total) {
                     i = e / a.n_cand;
                     j = e - i * a.n_cand;
                 }
-                const bool act = e < total && j < sm.nc[i];
-                const int qs_ = qg + i;
-                uint32_t v = 0;
-                float4 m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                act = e < total && j < sm.nc[i];
+                v = 0;
+                m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 if (act) {
                     // kept rows: shared memory, or the ties this CTA wrote (coherent load)
-                    v = a.n_cand <= kSvMax ? sm.sv[i][j] : (uint32_t)a.cand_tie[sm.qbase[qs_] + j];
+                    v = a.n_cand <= kSvMax ? sm.sv[i][j] : (uint32_t)a.cand_tie[sm.qbase[qg + i] + j];
                     m = __ldg(a.meta + beg + v);
                 }
-                const int64_t row = beg + v;
-                const uint8_t* crow = a.codes + row * a.code_bytes;
-                const bool need = act && m.w > 1e-12f;
-                const int iip = pf ? int_ip_group8_pf<kPfUnits>(crow, qsm + i * qld, a.D, a.nbits, sub, need)
-                                   : int_ip_group8(crow, qsm + i * qld, a.D, a.nbits, sub, need);
+            };
+            auto finish = [&](int i, int j, bool act, float4 m, int iip) {
                 if (act && sub == 0)
-                    a.cand_key[sm.qbase[qs_] + j] =
-                        total_order_key(rerank_distance(iip, m, sm.qp[qs_], a.nbits, l2));
+                    a.cand_key[sm.qbase[qg + i] + j] =
+                        total_order_key(rerank_distance(iip, m, sm.qp[qg + i], a.nbits, l2));
+            };
+            for (int e0 = w * 8; e0 < total; e0 += kScanWarps * 8) {
+                int ia, ja, ib, jb;
+                bool acta, actb;
+                uint32_t va, vb;
+                float4 ma, mb;
+                entry(e0 + grp, ia, ja, acta, va, ma);
+                entry(e0 + 4 + grp, ib, jb, actb, vb, mb);
+                const uint8_t* ca = a.codes + (beg + va) * a.code_bytes;
+                const uint8_t* cb = a.codes + (beg + vb) * a.code_bytes;
+                const bool na = acta && ma.w > 1e-12f, nb = actb && mb.w > 1e-12f;
+                int2 ip;
+                if (pf) {
+                    ip = int_ip_group8_pf2<kPfUnits>(ca, qsm + ia * qld, na, cb, qsm + ib * qld, nb, a.D,
+                                                     a.nbits, sub);
+                } else {
+                    ip.x = int_ip_group8(ca, qsm + ia * qld, a.D, a.nbits, sub, na);
+                    ip.y = int_ip_group8(cb, qsm + ib * qld, a.D, a.nbits, sub, nb);
+                }
+                finish(ia, ja, acta, ma, ip.x);
+                finish(ib, jb, actb, mb, ip.y);
             }
             __syncthreads();
         }
