@@ -548,7 +548,7 @@ int64_t IvfUsqGpu::prepare_batch(const float* d_q, const float* h_q, int64_t nb,
     // for chunk c's copy, so the copy of chunk c+1 runs under them.
     w_sel_.reserve((size_t)nb * 2 * nprobe);
     int nchunks = 1;
-    if (h_q) nchunks = (int)std::min<int64_t>(kMaxUploadChunks, std::max<int64_t>(1, nb / 2048));
+    if (h_q) nchunks = (int)std::min<int64_t>(kMaxUploadChunks, std::max<int64_t>(1, nb / 1024));
     const int64_t per = (nb + nchunks - 1) / nchunks;
     if (h_q) {
         HANNS_CUDA_OK(cudaEventRecord(ev_ready_, s));

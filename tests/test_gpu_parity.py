@@ -193,7 +193,7 @@ def test_tensor_core_and_simt_scans_agree(gpu, oracle_mod, nbits, metric, k, nli
 
 
 def test_host_search_chunked_upload(gpu, oracle_mod):
-    """Host-pointer search of 9000 queries: the upload runs in 4 chunks on the copy stream,
+    """Host-pointer search of 9000 queries: the upload runs in chunks on the copy stream,
     each chunk's per-query stages waiting only for its own copy.  Equal to the oracle and
     to the device-pointer path."""
     import torch
