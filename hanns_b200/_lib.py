@@ -141,6 +141,12 @@ SIGNATURES = [
     ("hanns_gpu_ivf_usq_search_prepared_shard_device", C.c_int32,
      [vp, C.c_int64, C.c_int32, C.c_int32, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     ("hanns_gpu_shard_owners", C.c_int32, [i64p, C.c_int32, C.c_int32, i32p]),
+    ("hanns_ivfusq00_read_header", C.c_int32, [C.c_char_p, i64p]),
+    ("hanns_ivfusq00_read", C.c_int32, [C.c_char_p, C.POINTER(Artifact)]),
+    ("hanns_ivfusq00_write", C.c_int32, [C.c_char_p, C.POINTER(Artifact), C.c_int64, C.c_uint64,
+                                         C.c_int64]),
+    ("hanns_gpu_ivf_usq_load_ivfusq00", vp, [C.c_char_p, C.c_int32]),
+    ("hanns_gpu_ivf_usq_save_ivfusq00", C.c_int32, [vp, C.c_char_p, C.c_uint64, C.c_int64]),
     ("hanns_gpu_coarse_probes_static", C.c_int32,
      [vp, C.c_int64, vp, C.c_int32, C.c_int32, C.c_int32, vp, vp]),
 ]

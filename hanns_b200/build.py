@@ -24,7 +24,7 @@ OBJ_DIR = os.path.join(HERE, "_build")
 
 CU_SOURCES = ["search_kernels.cu", "build_kernels.cu", "ivf_usq_gpu.cu", "capi.cu",
               "coarse_static.cu", "coarse_tc.cu", "scan_tc.cu"]
-CPP_SOURCES = ["rotation.cpp"]
+CPP_SOURCES = ["rotation.cpp", "ivfusq00.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "ivf_usq_gpu.h", "warp_select.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <fstream>
 #include <memory>
 #include <string>
 #include <vector>
@@ -250,12 +251,80 @@ int32_t knowhere_save_index(const void* index, const char* path) {
         idx->save(path);
     });
 }
+namespace {
+
+// Host copy of an IVFUSQ00 snapshot in artifact form (owning arrays).
+struct Ivfusq00Artifact {
+    int64_t hdr[10];
+    std::vector<float> cent, rot, rc, norms, norms_sq, vmaxs, quals;
+    std::vector<int64_t> off, ids;
+    std::vector<uint8_t> codes, signs;
+    hanns_ivf_usq_artifact_t art{};
+};
+
+bool is_ivfusq00(const char* path) {
+    std::ifstream f(path, std::ios::binary);
+    char m[8] = {};
+    f.read(m, 8);
+    return f && (std::memcmp(m, "IVFUSQ00", 8) == 0 || std::memcmp(m, "IVFXRBTQ", 8) == 0);
+}
+
+void read_ivfusq00(const char* path, Ivfusq00Artifact& s) {
+    if (hanns_ivfusq00_read_header(path, s.hdr) != HANNS_OK)
+        throw std::invalid_argument(hanns_gpu_last_error());
+    const int64_t d = s.hdr[0], D = s.hdr[1], nbits = s.hdr[2], nlist = s.hdr[3], n = s.hdr[5];
+    const int64_t cb = (D * nbits + 7) / 8;
+    s.cent.resize(nlist * d);
+    s.rot.resize(D * D);
+    s.rc.resize(D);
+    s.off.resize(nlist + 1);
+    s.ids.resize(n);
+    s.norms.resize(n);
+    s.norms_sq.resize(n);
+    s.vmaxs.resize(n);
+    s.quals.resize(n);
+    s.codes.resize(n * cb);
+    s.signs.resize(n * (D / 8));
+    hanns_ivf_usq_artifact_t& a = s.art;
+    a.dim = (int32_t)d;
+    a.padded_dim = (int32_t)D;
+    a.nbits = (int32_t)nbits;
+    a.nlist = (int32_t)nlist;
+    a.metric = (int32_t)s.hdr[4];
+    a.ntotal = n;
+    a.centroids = s.cent.data();
+    a.rotation = s.rot.data();
+    a.rotated_centroid = s.rc.data();
+    a.list_offsets = s.off.data();
+    a.ids = s.ids.data();
+    a.norms = s.norms.data();
+    a.norms_sq = s.norms_sq.data();
+    a.vmaxs = s.vmaxs.data();
+    a.quant_qualities = s.quals.data();
+    a.codes = s.codes.data();
+    a.sign_bits = s.signs.data();
+    if (hanns_ivfusq00_read(path, &a) != HANNS_OK) throw std::invalid_argument(hanns_gpu_last_error());
+    if (!(s.hdr[9] & 1)) throw std::invalid_argument("IVFUSQ00 snapshot of an untrained index");
+    if (a.metric > 2) throw std::invalid_argument("IVFUSQ00: Hamming metric is not an IVF-USQ search metric");
+}
+
+}  // namespace
+
 int32_t knowhere_load_index(void* index, const char* path) {
     auto* idx = as_index(index);
     if (!idx || !path) return HANNS_INVALID_ARG;
     return guarded([&] {
         std::lock_guard<std::mutex> lk(idx->mutex());
-        idx->load(path);
+        if (is_ivfusq00(path)) {  // the reference's IvfUsqIndex::save format
+            Ivfusq00Artifact s;
+            read_ivfusq00(path, s);
+            if (s.art.dim != idx->dim() || s.art.nlist != idx->nlist() || s.art.nbits != idx->nbits())
+                throw std::invalid_argument("IVFUSQ00 snapshot shape differs from the index config");
+            idx->import_artifact(&s.art);
+            idx->set_nprobe((int)s.hdr[6]);
+        } else {
+            idx->load(path);
+        }
     });
 }
 
@@ -419,6 +488,50 @@ HannsIvfUsqHandle* hanns_gpu_ivf_usq_import(const hanns_ivf_usq_artifact_t* a, i
         h = new HannsIvfUsqHandle{std::move(idx)};
     });
     return h;
+}
+
+HannsIvfUsqHandle* hanns_gpu_ivf_usq_load_ivfusq00(const char* path, int32_t device) {
+    if (!path) return nullptr;
+    HannsIvfUsqHandle* h = nullptr;
+    guarded([&] {
+        Ivfusq00Artifact s;
+        read_ivfusq00(path, s);
+        auto idx = std::make_unique<hanns::IvfUsqGpu>(s.art.dim, s.art.nlist, s.art.nbits, s.art.metric,
+                                                      (uint64_t)s.hdr[7], (int)s.hdr[6],
+                                                      device < 0 ? default_device() : device);
+        idx->import_artifact(&s.art);
+        h = new HannsIvfUsqHandle{std::move(idx)};
+    });
+    return h;
+}
+
+int32_t hanns_gpu_ivf_usq_save_ivfusq00(HannsIvfUsqHandle* h, const char* path, uint64_t rotation_seed,
+                                        int64_t rerank_k) {
+    if (!h || !path) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        auto* i = h->idx.get();
+        const int64_t n = i->count(), D = i->padded_dim(), cb = (D * i->nbits() + 7) / 8;
+        std::vector<float> cent((size_t)i->nlist() * i->dim()), rot((size_t)D * D), rc(D), norms(n),
+            norms_sq(n), vmaxs(n), quals(n);
+        std::vector<int64_t> off(i->nlist() + 1), ids(n);
+        std::vector<uint8_t> codes(n * cb), signs(n * (D / 8));
+        hanns_ivf_usq_artifact_t a{};
+        a.centroids = cent.data();
+        a.rotation = rot.data();
+        a.rotated_centroid = rc.data();
+        a.list_offsets = off.data();
+        a.ids = ids.data();
+        a.norms = norms.data();
+        a.norms_sq = norms_sq.data();
+        a.vmaxs = vmaxs.data();
+        a.quant_qualities = quals.data();
+        a.codes = codes.data();
+        a.sign_bits = signs.data();
+        i->export_artifact(&a);
+        if (hanns_ivfusq00_write(path, &a, i->nprobe(), rotation_seed, rerank_k) != HANNS_OK)
+            throw std::invalid_argument(hanns_gpu_last_error());
+    });
 }
 
 int32_t hanns_gpu_ivf_usq_shape(const HannsIvfUsqHandle* h, int64_t* out6) {

@@ -129,6 +129,25 @@ class IvfUsqIndex:
         cfg = IvfUsqConfig(s.dim, s.nlist, s.nbits, metric_type=s.metric)
         return cls(cfg, device, _handle=h)
 
+    @classmethod
+    def load_ivfusq00(cls, path: str, device: int = 0) -> "IvfUsqIndex":
+        """Opens a snapshot written by the reference's IvfUsqIndex::save ("IVFUSQ00",
+        src/faiss/ivf_usq.rs:353-406); loaded like IvfUsqIndex::load (zero global centroid)."""
+        hdr = np.zeros(10, np.int64)
+        _check(L.lib().hanns_ivfusq00_read_header(str(path).encode(), _p(hdr, L.i64p)), "IVFUSQ00 header")
+        h = L.lib().hanns_gpu_ivf_usq_load_ivfusq00(str(path).encode(), device)
+        if not h:
+            raise ValueError(f"load IVFUSQ00: {L.last_error()}")
+        cfg = IvfUsqConfig(int(hdr[0]), int(hdr[3]), int(hdr[2]), nprobe=int(hdr[6]), metric_type=int(hdr[4]),
+                           rotation_seed=int(hdr[7]))
+        return cls(cfg, device, _handle=h)
+
+    def save_ivfusq00(self, path: str, rerank_k: int = 64):
+        """Writes the index in the reference's snapshot format."""
+        _check(L.lib().hanns_gpu_ivf_usq_save_ivfusq00(self._h, str(path).encode(),
+                                                        self.config.rotation_seed, rerank_k),
+               "save IVFUSQ00")
+
     def export_artifact(self) -> dict:
         shp = np.zeros(6, np.int64)
         _check(L.lib().hanns_gpu_ivf_usq_shape(self._h, _p(shp, L.i64p)), "shape")

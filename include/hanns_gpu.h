@@ -254,6 +254,26 @@ int32_t hanns_gpu_ivf_usq_search_shard_device(HannsIvfUsqHandle* h, const float*
                                               int64_t nq, int32_t k, int32_t nprobe,
                                               float* d_dists, uint64_t* d_keys, int64_t* d_ids,
                                               void* stream);
+/* The reference's snapshot file (IvfUsqIndex::save, src/faiss/ivf_usq.rs:353-406:
+ * "IVFUSQ00", version 3, bincode 1.3 StoredSnapshot); no counterpart in the reference's
+ * C ABI.  Host only, no GPU:
+ *   hanns_ivfusq00_read_header: out10 = {dim, padded_dim, nbits, nlist, metric, ntotal,
+ *     nprobe, rotation_seed, rerank_k, flags (bit 0 trained, bit 1 high-accuracy scan)}.
+ *   hanns_ivfusq00_read: fills the caller's artifact arrays (shape fields must match the
+ *     header).  As IvfUsqIndex::load does (:408-506), the global centroid is zero, so
+ *     rotated_centroid = 0; the rotation is regenerated from rotation_seed by this
+ *     library's generator (parity of P with the Rust build is not claimed).
+ *   hanns_ivfusq00_write: writes an artifact in that format (list order = clusters).
+ * On the GPU: hanns_gpu_ivf_usq_load_ivfusq00 opens such a file as a new index;
+ * knowhere_load_index also accepts it (the shape must match the handle's config);
+ * hanns_gpu_ivf_usq_save_ivfusq00 writes an index in that format. */
+int32_t hanns_ivfusq00_read_header(const char* path, int64_t* out10);
+int32_t hanns_ivfusq00_read(const char* path, hanns_ivf_usq_artifact_t* out);
+int32_t hanns_ivfusq00_write(const char* path, const hanns_ivf_usq_artifact_t* artifact,
+                             int64_t nprobe, uint64_t rotation_seed, int64_t rerank_k);
+HannsIvfUsqHandle* hanns_gpu_ivf_usq_load_ivfusq00(const char* path, int32_t device);
+int32_t hanns_gpu_ivf_usq_save_ivfusq00(HannsIvfUsqHandle* h, const char* path,
+                                        uint64_t rotation_seed, int64_t rerank_k);
 /* Query-split multi-GPU search (no counterpart in the reference, whose search runs on one
  * host).  Each rank prepares the per-query state of its share of the queries, the ranks
  * all-gather it, and every rank scans its own lists for all queries:
