@@ -121,7 +121,8 @@ CSearchResult* search_common(const void* index, const float* query, size_t count
     const double us =
         std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
     if (std::getenv("HANNS_TRACE_SEARCH")) {
-        const float* st = idx->stage_ms();
+        float st[8];
+        idx->stage_ms(1, st);
         std::fprintf(stderr,
                      "TRACE_SEARCH nq=%zu elapsed_us=%.0f coarse_ms=%.3f prep_ms=%.3f "
                      "group_ms=%.3f scan_ms=%.3f merge_ms=%.3f\n",
@@ -611,10 +612,17 @@ int32_t hanns_gpu_ivf_usq_search_device(HannsIvfUsqHandle* h, const float* d_que
     });
 }
 
-int32_t hanns_gpu_ivf_usq_stage_ms(const HannsIvfUsqHandle* h, float* out8) {
+int32_t hanns_gpu_ivf_usq_stage_ms(HannsIvfUsqHandle* h, float* out8) {
     if (!h || !out8) return HANNS_INVALID_ARG;
-    std::memcpy(out8, h->idx->stage_ms(), sizeof(float) * 8);
-    return HANNS_OK;
+    return guarded([&] { h->idx->stage_ms(1, out8); });
+}
+
+int32_t hanns_gpu_ivf_usq_stage_ms_recent(HannsIvfUsqHandle* h, int32_t n_calls, float* out8,
+                                          int32_t* counts8) {
+    if (!h || !out8 || n_calls <= 0) return HANNS_INVALID_ARG;
+    int covered = 0;
+    const int32_t rc = guarded([&] { covered = h->idx->stage_ms(n_calls, out8, counts8); });
+    return rc == HANNS_OK ? covered : -rc;
 }
 
 int64_t hanns_gpu_ivf_usq_last_launches(const HannsIvfUsqHandle* h) {

@@ -76,15 +76,17 @@ IvfUsqGpu::IvfUsqGpu(int dim, int nlist, int nbits, int metric, uint64_t rotatio
 
 IvfUsqGpu::~IvfUsqGpu() {
     cudaSetDevice(device_);
-    for (auto& e : ev_)
-        if (e) cudaEventDestroy(e);
+    for (auto& sl : ring_) {
+        for (auto& e : sl.ev)
+            if (e) cudaEventDestroy(e);
+        for (auto& e : sl.aux)
+            if (e) cudaEventDestroy(e);
+    }
     for (auto& e : ev_up_)
         if (e) cudaEventDestroy(e);
     if (ev_ready_) cudaEventDestroy(ev_ready_);
     if (ev_fork_) cudaEventDestroy(ev_fork_);
     if (ev_join_) cudaEventDestroy(ev_join_);
-    for (auto& e : ev_aux_)
-        if (e) cudaEventDestroy(e);
     if (aux_stream_) cudaStreamDestroy(aux_stream_);
     if (h_scan_err_) cudaFreeHost(h_scan_err_);
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
@@ -98,8 +100,10 @@ void IvfUsqGpu::ensure_stream() {
         HANNS_CUDA_OK(cudaStreamCreateWithFlags(&aux_stream_, cudaStreamNonBlocking));
         HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
         HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming));
-        for (auto& e : ev_aux_) HANNS_CUDA_OK(cudaEventCreate(&e));
-        for (auto& e : ev_) HANNS_CUDA_OK(cudaEventCreate(&e));
+        for (auto& sl : ring_) {
+            for (auto& e : sl.aux) HANNS_CUDA_OK(cudaEventCreate(&e));
+            for (auto& e : sl.ev) HANNS_CUDA_OK(cudaEventCreate(&e));
+        }
         for (auto& e : ev_up_) HANNS_CUDA_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_ready_, cudaEventDisableTiming));
         HANNS_CUDA_OK(cudaHostAlloc(reinterpret_cast<void**>(&h_scan_err_), sizeof(int),
@@ -565,7 +569,7 @@ int64_t IvfUsqGpu::prepare_batch(const float* d_q, const float* h_q, int64_t nb,
     // the coarse step runs on s, rotation + query state on aux_stream_ (independent work on
     // the same queries, so the two latency-bound chains overlap); s joins aux before grouping
     const bool per_stage = time_it && nchunks == 1;
-    aux_timed_ = per_stage;
+    cur_->aux_timed = per_stage;
     HANNS_CUDA_OK(cudaEventRecord(ev_fork_, s));
     HANNS_CUDA_OK(cudaStreamWaitEvent(aux_stream_, ev_fork_, 0));
     if (per_stage) HANNS_CUDA_OK(cudaEventRecord(ev_aux_[0], aux_stream_));
@@ -748,10 +752,9 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     m.out_keys = d_keys;
     launch_merge(m, s);
     launches += 1;
+    used_tc_ = use_tc;
     if (use_tc)
         HANNS_CUDA_OK(cudaMemcpyAsync(h_scan_err_, w_scan_err_.p, sizeof(int), cudaMemcpyDeviceToHost, s));
-    else
-        *h_scan_err_ = 0;
     HANNS_CUDA_OK(cudaGetLastError());
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[7], s));
     return launches;
@@ -763,6 +766,7 @@ void IvfUsqGpu::search_device(const float* d_queries, int64_t nq, const SearchOp
                               cudaStream_t stream) {
     DeviceGuard g(device_);
     run_search(d_queries, nullptr, nq, opt, d_ids, d_dists, d_counts, d_keys, stream);
+    if (!stream) HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
 }
 
 void IvfUsqGpu::run_search(const float* d_queries, const float* h_queries, int64_t nq,
@@ -778,23 +782,19 @@ void IvfUsqGpu::run_search(const float* d_queries, const float* h_queries, int64
     int64_t nb_max = std::max<int64_t>(1, (4ll << 30) / (cand_stride(nprobe, k) * 12));
     nb_max = std::min<int64_t>(nb_max, 65536);
     last_launches_ = 0;
-    for (int e = 0; e < kStages + 1; ++e) stage_ms_[e] = 0;
+    begin_call();
     for (int64_t b = 0; b < nq; b += nb_max) {
         const int64_t nb = std::min(nb_max, nq - b);
         SearchOptions o = opt;
         if (o.d_query_bitset) o.d_query_bitset += b;
+        // stages 0-1 (coarse step) and 2-3 (rotation, query state) overlap on two streams;
+        // ev_[3] -> ev_[4] is empty (the join)
+        next_slot(0, kStages);
         search_batch(d_queries + b * dim_, h_queries ? h_queries + b * dim_ : nullptr, nb, o,
                      d_ids + b * k, d_dists + b * k, d_counts ? d_counts + b : nullptr,
                      d_keys ? d_keys + b * k : nullptr, s, true);
-        HANNS_CUDA_OK(cudaEventSynchronize(ev_[kStages]));
-        if (*h_scan_err_ != 0)
-            throw std::runtime_error("tensor-core list scan: a bounded wait expired (code " +
-                                     std::to_string(*h_scan_err_) + ")");
-        // stages 0-1 (coarse step) and 2-3 (rotation, query state) overlap on two streams;
-        // ev_[3] -> ev_[4] is empty (the join)
-        collect_stage_ms(0, kStages);
+        check_tc_scan();
     }
-    HANNS_CUDA_OK(cudaStreamSynchronize(s));
 }
 
 void IvfUsqGpu::query_state_bytes(int nprobe, int64_t* parts) const {
@@ -806,23 +806,65 @@ void IvfUsqGpu::query_state_bytes(int nprobe, int64_t* parts) const {
     parts[4] = D_;
 }
 
-// stage_ms_[e] = ev_[e] -> ev_[e + 1] for first <= e < last (stages 2-3 from the rotation
-// stream's events), total = ev_[first] -> ev_[last].
-void IvfUsqGpu::collect_stage_ms(int first, int last) {
-    float t;
-    for (int e = first; e < last; ++e) {
-        if (e == 2 || e == 3) {
-            if (aux_timed_) {
-                HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_aux_[e - 2], ev_aux_[e - 1]));
-                stage_ms_[e] += t;
-            }
-            continue;
-        }
-        HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[e], ev_[e + 1]));
-        stage_ms_[e] += t;
+void IvfUsqGpu::begin_call() {
+    calls_.emplace_back(slot_seq_, 0);
+    while ((int)calls_.size() > kEvRing) calls_.pop_front();
+}
+
+void IvfUsqGpu::next_slot(int first, int last) {
+    cur_ = &ring_[slot_seq_ % kEvRing];
+    cur_->first = first;
+    cur_->last = last;
+    cur_->aux_timed = false;
+    ev_ = cur_->ev;
+    ev_aux_ = cur_->aux;
+    ++slot_seq_;
+    if (!calls_.empty()) ++calls_.back().second;
+}
+
+// The tensor-core scan reports an expired bounded wait through a pinned flag: only then
+// does the call wait for the device before returning.
+void IvfUsqGpu::check_tc_scan() {
+    if (!used_tc_) return;
+    HANNS_CUDA_OK(cudaEventSynchronize(ev_[kStages]));
+    if (*h_scan_err_ != 0)
+        throw std::runtime_error("tensor-core list scan: a bounded wait expired (code " +
+                                 std::to_string(*h_scan_err_) + ")");
+}
+
+// stage e = ev[e] -> ev[e + 1] for first <= e < last (stages 2-3 from the rotation stream's
+// events), total = ev[first] -> ev[last]; summed over the slots of the last n_calls calls.
+int IvfUsqGpu::stage_ms(int n_calls, float* out, int* counts) {
+    for (int e = 0; e < kStages + 1; ++e) {
+        out[e] = 0;
+        if (counts) counts[e] = 0;
     }
-    HANNS_CUDA_OK(cudaEventElapsedTime(&t, ev_[first], ev_[last]));
-    stage_ms_[kStages] += t;
+    int covered = 0;
+    for (auto it = calls_.rbegin(); it != calls_.rend() && covered < n_calls; ++it, ++covered) {
+        if (slot_seq_ - it->first > kEvRing) break;  // its slots were reused
+        for (int j = 0; j < it->second; ++j) {
+            const StageSlot& sl = ring_[(it->first + j) % kEvRing];
+            HANNS_CUDA_OK(cudaEventSynchronize(sl.ev[sl.last]));
+            float t;
+            for (int e = sl.first; e < sl.last; ++e) {
+                if (e == 2 || e == 3) {
+                    if (sl.aux_timed) {
+                        HANNS_CUDA_OK(cudaEventElapsedTime(&t, sl.aux[e - 2], sl.aux[e - 1]));
+                        out[e] += t;
+                        if (counts) ++counts[e];
+                    }
+                    continue;
+                }
+                HANNS_CUDA_OK(cudaEventElapsedTime(&t, sl.ev[e], sl.ev[e + 1]));
+                out[e] += t;
+                if (counts) ++counts[e];
+            }
+            HANNS_CUDA_OK(cudaEventElapsedTime(&t, sl.ev[sl.first], sl.ev[sl.last]));
+            out[kStages] += t;
+            if (counts) ++counts[kStages];
+        }
+    }
+    return covered;
 }
 
 void IvfUsqGpu::prepare_device(const float* d_queries, int64_t nq, int nprobe, QueryState st,
@@ -838,13 +880,12 @@ void IvfUsqGpu::prepare_device(const float* d_queries, int64_t nq, int nprobe, Q
         w_qi8n_.reserve((size_t)nq * D_);
         st.q_i8n = w_qi8n_.p;
     }
-    for (int e = 0; e < kStages + 1; ++e) stage_ms_[e] = 0;
+    begin_call();
+    next_slot(0, 4);
     HANNS_CUDA_OK(cudaEventRecord(ev_[0], s));
     last_launches_ = prepare_batch(d_queries, nullptr, nq, nprobe, st, s, true);
     HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
-    HANNS_CUDA_OK(cudaEventSynchronize(ev_[4]));
-    collect_stage_ms(0, 4);
-    HANNS_CUDA_OK(cudaStreamSynchronize(s));
+    if (!stream) HANNS_CUDA_OK(cudaStreamSynchronize(s));
 }
 
 void IvfUsqGpu::search_prepared_device(int64_t nq, const SearchOptions& opt, QueryState st,
@@ -865,24 +906,21 @@ void IvfUsqGpu::search_prepared_device(int64_t nq, const SearchOptions& opt, Que
     int64_t nb_max = std::max<int64_t>(1, (4ll << 30) / (cand_stride(nprobe, k) * 12));
     nb_max = std::min<int64_t>(nb_max, 65536);
     last_launches_ = 0;
-    for (int e = 0; e < kStages + 1; ++e) stage_ms_[e] = 0;
+    begin_call();
     for (int64_t b = 0; b < nq; b += nb_max) {
         const int64_t nb = std::min(nb_max, nq - b);
         SearchOptions o = opt;
         if (o.d_query_bitset) o.d_query_bitset += b;
         const QueryState sb{st.probes + b * nprobe, st.qp + b, st.lut + b * G * 16,
                             st.q_i8p + b * D_, st.q_i8n ? st.q_i8n + b * D_ : nullptr};
+        next_slot(4, kStages);
         HANNS_CUDA_OK(cudaEventRecord(ev_[4], s));
         last_launches_ += scan_merge_batch(nb, o, sb, d_ids + b * k, d_dists + b * k,
                                            d_counts ? d_counts + b : nullptr,
                                            d_keys ? d_keys + b * k : nullptr, s, true);
-        HANNS_CUDA_OK(cudaEventSynchronize(ev_[kStages]));
-        if (*h_scan_err_ != 0)
-            throw std::runtime_error("tensor-core list scan: a bounded wait expired (code " +
-                                     std::to_string(*h_scan_err_) + ")");
-        collect_stage_ms(4, kStages);
+        check_tc_scan();
     }
-    HANNS_CUDA_OK(cudaStreamSynchronize(s));
+    if (!stream) HANNS_CUDA_OK(cudaStreamSynchronize(s));
 }
 
 void IvfUsqGpu::search_host(const float* h_queries, int64_t nq, const SearchOptions& opt_in,

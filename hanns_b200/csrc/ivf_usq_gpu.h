@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <deque>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -122,7 +123,11 @@ class IvfUsqGpu {
     int64_t count() const { return ntotal_; }
     int64_t size_bytes() const;
     int device() const { return device_; }
-    const float* stage_ms() const { return stage_ms_; }
+    // Per-stage device ms (coarse GEMM, coarse select, rotate, query state, group, scan,
+    // merge, total) summed over the last n_calls search / prepare calls; waits for their
+    // events.  counts (nullable): batches that timed each stage.  Returns the number of
+    // calls covered (calls older than the event ring are not).
+    int stage_ms(int n_calls, float* out, int* counts = nullptr);
     int64_t last_launches() const { return last_launches_; }
     std::mutex& mutex() { return mu_; }
 
@@ -141,7 +146,11 @@ class IvfUsqGpu {
     int64_t scan_merge_batch(int64_t nb, const SearchOptions& opt, const QueryState& st,
                              int64_t* d_ids, float* d_dists, int64_t* d_counts, uint64_t* d_keys,
                              cudaStream_t s, bool time_it);
-    void collect_stage_ms(int first, int last);
+    // Stage events: each search batch takes the next slot of a ring (ev_ / ev_aux_ point into
+    // it), so that calls need not wait for the device before their events are reused.
+    void begin_call();
+    void next_slot(int first, int last);
+    void check_tc_scan();
     void run_search(const float* d_queries, const float* h_queries, int64_t nq,
                     const SearchOptions& opt, int64_t* d_ids, float* d_dists, int64_t* d_counts,
                     uint64_t* d_keys, cudaStream_t stream);
@@ -192,8 +201,7 @@ class IvfUsqGpu {
     cudaStream_t copy_stream_ = nullptr;  // host->device query upload
     cudaStream_t aux_stream_ = nullptr;   // rotation + query state, beside the coarse step
     cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
-    cudaEvent_t ev_aux_[3] = {};          // rotation start / end, query state end
-    bool aux_timed_ = false;
+
     static constexpr int kMaxUploadChunks = 8;
     cudaEvent_t ev_up_[kMaxUploadChunks] = {};
     cudaEvent_t ev_ready_ = nullptr;  // copy_stream_ waits for earlier work on the search stream
@@ -202,8 +210,20 @@ class IvfUsqGpu {
     int sm_count_ = 0;
     // stages: coarse GEMM, coarse select, rotate, query state, group, scan, merge; then total
     static constexpr int kStages = 7;
-    cudaEvent_t ev_[kStages + 1] = {};
-    float stage_ms_[kStages + 1] = {};
+    static constexpr int kEvRing = 64;
+    struct StageSlot {
+        cudaEvent_t ev[kStages + 1] = {};
+        cudaEvent_t aux[3] = {};  // rotation start / end, query state end (aux stream)
+        bool aux_timed = false;
+        int first = 0, last = 0;  // events first..last were recorded
+    };
+    StageSlot ring_[kEvRing];
+    int64_t slot_seq_ = 0;                           // slots handed out so far
+    std::deque<std::pair<int64_t, int>> calls_;      // (first slot, slot count) per call
+    StageSlot* cur_ = &ring_[0];
+    cudaEvent_t* ev_ = ring_[0].ev;
+    cudaEvent_t* ev_aux_ = ring_[0].aux;
+    bool used_tc_ = false;  // the last scan ran the tensor-core kernel (host reads its error flag)
     int64_t last_launches_ = 0;
     DevBuf<int> w_fallbacks_;  // [0] exact fallbacks, [1] tensor-core error flag
     DevBuf<uint16_t> w_qhi_, w_qlo_;

@@ -245,10 +245,21 @@ class IvfUsqIndex:
               "total")
 
     def stage_ms(self) -> np.ndarray:
-        """Device ms of the last search per stage (names in STAGES)."""
+        """Device ms of the last search per stage (names in STAGES); waits for it."""
         out = np.zeros(8, np.float32)
         _check(L.lib().hanns_gpu_ivf_usq_stage_ms(self._h, _p(out, L.f32p)), "stage_ms")
         return out
+
+    def stage_ms_recent(self, n_calls: int):
+        """(sum of device ms per stage, batches that timed each stage, calls covered) over
+        the last n_calls search / prepare calls."""
+        out = np.zeros(8, np.float32)
+        cnt = np.zeros(8, np.int32)
+        rc = L.lib().hanns_gpu_ivf_usq_stage_ms_recent(self._h, int(n_calls), _p(out, L.f32p),
+                                                       _p(cnt, L.i32p))
+        if rc < 0:
+            _check(-rc, "stage_ms_recent")
+        return out, cnt, int(rc)
 
     def last_launches(self) -> int:
         return int(L.lib().hanns_gpu_ivf_usq_last_launches(self._h))

@@ -220,8 +220,10 @@ int32_t hanns_gpu_ivf_usq_search(HannsIvfUsqHandle* h, const float* queries, int
                                  const uint64_t* bitsets, int64_t bitset_len, int64_t n_bitsets,
                                  const int32_t* query_bitset, int64_t* ids, float* dists,
                                  int64_t* counts);
-/* Same with every buffer in device memory of the handle's GPU, on `stream`
- * (cudaStream_t, NULL = the handle's stream).  Synchronises before returning. */
+/* Same with every buffer in device memory of the handle's GPU, on `stream` (cudaStream_t).
+ * With a stream the call is stream-ordered: it returns once the work is enqueued (the
+ * opt-in tensor-core scan waits for its error flag).  NULL = the handle's own stream,
+ * and the call returns when the search has finished. */
 int32_t hanns_gpu_ivf_usq_search_device(HannsIvfUsqHandle* h, const float* d_queries, int64_t nq,
                                         int32_t k, int32_t nprobe, int32_t filter_mode,
                                         const uint64_t* d_bitsets, int64_t bitset_len,
@@ -229,8 +231,13 @@ int32_t hanns_gpu_ivf_usq_search_device(HannsIvfUsqHandle* h, const float* d_que
                                         int64_t* d_ids, float* d_dists, int64_t* d_counts,
                                         void* stream);
 /* Device time (ms) of the stages of the last search, out8 = {coarse GEMM, coarse select,
- * rotation, query state, list grouping, list scan, merge, total}. */
-int32_t hanns_gpu_ivf_usq_stage_ms(const HannsIvfUsqHandle* h, float* out8);
+ * rotation, query state, list grouping, list scan, merge, total}; waits for that search. */
+int32_t hanns_gpu_ivf_usq_stage_ms(HannsIvfUsqHandle* h, float* out8);
+/* The same summed over the last n_calls search / prepare calls (their stage events sit in
+ * a ring of 64 batches); counts8 (may be NULL) = how many batches timed each stage.
+ * Returns how many calls it covered, or -(error code). */
+int32_t hanns_gpu_ivf_usq_stage_ms_recent(HannsIvfUsqHandle* h, int32_t n_calls, float* out8,
+                                          int32_t* counts8);
 /* Number of kernel launches of the last search. */
 int64_t hanns_gpu_ivf_usq_last_launches(const HannsIvfUsqHandle* h);
 int32_t hanns_gpu_ivf_usq_set_nprobe(HannsIvfUsqHandle* h, int32_t nprobe);
@@ -284,7 +291,8 @@ int32_t hanns_gpu_ivf_usq_save_ivfusq00(HannsIvfUsqHandle* h, const char* path,
  *     device-resident queries into the caller's device arrays (d_qi8n may be NULL).
  *   hanns_gpu_ivf_usq_search_prepared_shard_device: grouping, list scan and merge of nq
  *     queries from such arrays (concatenated over the ranks); output as
- *     hanns_gpu_ivf_usq_search_shard_device. */
+ *     hanns_gpu_ivf_usq_search_shard_device.
+ * Both are stream-ordered like hanns_gpu_ivf_usq_search_device (NULL stream: synchronous). */
 int32_t hanns_gpu_ivf_usq_query_state_bytes(HannsIvfUsqHandle* h, int32_t nprobe, int64_t* out5);
 int32_t hanns_gpu_ivf_usq_prepare_device(HannsIvfUsqHandle* h, const float* d_queries, int64_t nq,
                                          int32_t nprobe, void* d_probes, void* d_qp, void* d_lut,

@@ -218,6 +218,38 @@ def test_host_search_chunked_upload(gpu, oracle_mod):
     assert bits_eq(dist.cpu().numpy(), e_d)
 
 
+def test_stream_ordered_device_search(gpu, oracle_mod):
+    """On a created stream the device search returns once enqueued: five back-to-back
+    searches of different batches into different outputs, read after one synchronize,
+    equal the oracle; the stage-event ring times each of them."""
+    import torch
+    from hanns_b200.ivf_usq import IvfUsqIndex
+    from tests.golden.make_golden import mixture
+    O = oracle_mod
+    rng = np.random.default_rng(78)
+    d, k, nprobe, nq, nb = 96, 10, 5, 700, 5
+    x, _ = mixture(rng, 20000, d, 32, 0.4, False)
+    q, _ = mixture(rng, nq * nb, d, 32, 0.4, False)
+    art = O.build_artifact(x, 40, 4, O.METRIC_IP, rotation_seed=6, kmeans_iters=5, kmeans_seed=3)
+    e_ids, e_d, _ = O.OracleIndex(art).search(q, k, nprobe)
+    idx = IvfUsqIndex.from_artifact(art)
+    dq = torch.from_numpy(q).cuda()
+    ids = torch.full((nq * nb, k), -9, dtype=torch.int64, device="cuda")
+    dist = torch.empty(nq * nb, k, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    st = torch.cuda.Stream()
+    for b in range(nb):
+        idx.search_device(dq.data_ptr() + b * nq * d * 4, nq, k, nprobe,
+                          ids.data_ptr() + b * nq * k * 8, dist.data_ptr() + b * nq * k * 4,
+                          stream=st.cuda_stream)
+    st.synchronize()
+    assert np.array_equal(ids.cpu().numpy(), e_ids)
+    assert bits_eq(dist.cpu().numpy(), e_d)
+    tot, cnt, covered = idx.stage_ms_recent(nb)
+    assert covered == nb and cnt[5] == nb and cnt[7] == nb
+    assert tot[5] > 0 and tot[7] >= tot[5]
+
+
 def test_empty_and_tiny_index(gpu, oracle_mod):
     """Lists of 0, 1, 31, 32, 33 rows; k larger than everything probed."""
     from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
