@@ -15,6 +15,14 @@
 namespace hanns {
 
 namespace {
+// Candidate regions of one internal batch: 12 bytes per entry, at most 16 GiB (of the
+// 180 GB HBM); per-query kernels index queries in grid.y in tiles of >= 8, so 262,144
+// queries per batch stay inside the 65,535 grid.y limit.
+constexpr int64_t kCandBudget = 16ll << 30;
+constexpr int64_t kMaxBatch = 262144;
+}  // namespace
+
+namespace {
 
 struct DeviceGuard {
     int prev = -1;
@@ -174,7 +182,7 @@ int64_t IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32
     const int64_t cchunk = std::max<int64_t>(1, std::min<int64_t>(nb, (1ll << 28) / nlist_));
     w_dist_.reserve((size_t)cchunk * nlist_);
     w_fallbacks_.reserve(2);
-    w_rs_.reserve((size_t)cchunk * (kCoarseRescoreMax + 1));
+    w_rs_.reserve((size_t)cchunk * kCoarseRsStride);
     HANNS_CUDA_OK(cudaMemsetAsync(w_fallbacks_.p, 0, 2 * sizeof(int), s));
     if (nprobe > 256) {  // candidate buffers hold 512: large nprobe takes the exact kernels
         w_sel_.reserve((size_t)cchunk * 2 * nprobe);
@@ -222,13 +230,20 @@ int64_t IvfUsqGpu::coarse_probes(const float* d_q, int64_t nb, int nprobe, int32
     return launches;
 }
 
+void IvfUsqGpu::refresh_rotation() {
+    Pc_.reserve((size_t)D_ * D_);
+    launch_rotation_chain_major(P_.p, D_, Pc_.p, stream_);
+    HANNS_CUDA_OK(cudaGetLastError());
+}
+
 void IvfUsqGpu::upload_rotation_centroid() {
     std::vector<float> P((size_t)D_ * D_);
     rotation_matrix(rotation_seed_, D_, P.data());
     h2d(P_, P.data(), P.size(), stream_);
+    refresh_rotation();
     rc_.reserve(D_);
     // rotated_centroid = P * pad(global mean)  (quantizer.rs:107-121)
-    launch_rotate(gmean_.p, 1, dim_, D_, P_.p, rc_.p, stream_);
+    launch_rotate(gmean_.p, 1, dim_, D_, Pc_.p, rc_.p, stream_);
     HANNS_CUDA_OK(cudaGetLastError());
     HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
 }
@@ -244,6 +259,7 @@ void IvfUsqGpu::import_artifact(const void* art_) {
     h2d(centroids_, a->centroids, (size_t)nlist_ * dim_, stream_);
     update_centroid_norms();
     h2d(P_, a->rotation, (size_t)D_ * D_, stream_);
+    refresh_rotation();
     h2d(rc_, a->rotated_centroid, (size_t)D_, stream_);
     std::vector<int64_t> off(a->list_offsets, a->list_offsets + nlist_ + 1);
     if (off[0] != 0 || off[nlist_] != ntotal_) throw std::invalid_argument("bad list offsets");
@@ -378,7 +394,7 @@ void IvfUsqGpu::add(const float* h_data, int64_t n, const int64_t* h_ids) {
         res.reserve((size_t)m * D_);
         launch_residual_pad(x.p, m, dim_, D_, gmean_.p, res.p, stream_);
         rot.reserve((size_t)m * D_ + ((size_t)m * D_ + 3) / 4);
-        launch_rotate(res.p, m, D_, D_, P_.p, rot.p, stream_);
+        launch_rotate(res.p, m, D_, D_, Pc_.p, rot.p, stream_);
         launch_encode_rotated(rot.p, m, D_, nbits_, nsq.p, ncodes.p + b * code_bytes_,
                               nsigns.p + b * (D_ / 8), nmeta.p + b, stream_);
         for (int64_t c = 0; c < m; c += cchunk) {
@@ -583,7 +599,7 @@ int64_t IvfUsqGpu::prepare_batch(const float* d_q, const float* h_q, int64_t nb,
         }
         launches += coarse_probes(q, m, nprobe, st.probes + q0 * nprobe, s,
                                   per_stage ? ev_[1] : nullptr);
-        launch_rotate(q, m, dim_, D_, P_.p, w_qrot_.p + q0 * D_, aux_stream_);
+        launch_rotate(q, m, dim_, D_, Pc_.p, w_qrot_.p + q0 * D_, aux_stream_);
         if (per_stage) HANNS_CUDA_OK(cudaEventRecord(ev_aux_[1], aux_stream_));
         launch_query_state(q, w_qrot_.p + q0 * D_, m, dim_, D_, rc_.p, nbits_, st.qp + q0,
                            st.q_i8p + q0 * D_, st.q_i8n + q0 * D_, st.lut + q0 * G * 16,
@@ -778,9 +794,9 @@ void IvfUsqGpu::run_search(const float* d_queries, const float* h_queries, int64
     cudaStream_t s = stream ? stream : stream_;
     const int k = std::max(opt.k, 1);
     const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
-    // batch size bounded by the candidate regions (12 bytes per entry, ~4 GiB per batch)
-    int64_t nb_max = std::max<int64_t>(1, (4ll << 30) / (cand_stride(nprobe, k) * 12));
-    nb_max = std::min<int64_t>(nb_max, 65536);
+    // batch size bounded by the candidate regions (12 bytes per entry)
+    int64_t nb_max = std::max<int64_t>(1, kCandBudget / (cand_stride(nprobe, k) * 12));
+    nb_max = std::min<int64_t>(nb_max, kMaxBatch);
     last_launches_ = 0;
     begin_call();
     for (int64_t b = 0; b < nq; b += nb_max) {
@@ -903,8 +919,8 @@ void IvfUsqGpu::search_prepared_device(int64_t nq, const SearchOptions& opt, Que
     const int k = std::max(opt.k, 1);
     const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
     const int G = D_ / 4;
-    int64_t nb_max = std::max<int64_t>(1, (4ll << 30) / (cand_stride(nprobe, k) * 12));
-    nb_max = std::min<int64_t>(nb_max, 65536);
+    int64_t nb_max = std::max<int64_t>(1, kCandBudget / (cand_stride(nprobe, k) * 12));
+    nb_max = std::min<int64_t>(nb_max, kMaxBatch);
     last_launches_ = 0;
     begin_call();
     for (int64_t b = 0; b < nq; b += nb_max) {
@@ -978,7 +994,7 @@ void IvfUsqGpu::debug_query(const float* h_queries, int64_t nq, int nprobe, int3
     w_qi8p_.reserve((size_t)nq * D_);
     w_qi8n_.reserve((size_t)nq * D_);
     w_lut_.reserve((size_t)nq * G * 16);
-    launch_rotate(w_pad_queries_.p, nq, dim_, D_, P_.p, w_qrot_.p, stream_);
+    launch_rotate(w_pad_queries_.p, nq, dim_, D_, Pc_.p, w_qrot_.p, stream_);
     launch_query_state(w_pad_queries_.p, w_qrot_.p, nq, dim_, D_, rc_.p, nbits_, w_qp_.p,
                        w_qi8p_.p, w_qi8n_.p, w_lut_.p, stream_);
     HANNS_CUDA_OK(cudaGetLastError());
@@ -1068,6 +1084,7 @@ void IvfUsqGpu::load(const std::string& path) {
         get(centroids_, (size_t)nlist_ * dim_);
         update_centroid_norms();
         get(P_, (size_t)D_ * D_);
+        refresh_rotation();
         get(rc_, (size_t)D_);
         get(gmean_, (size_t)dim_);
     }

@@ -169,6 +169,8 @@ class IvfUsqGpu {
 
     // device artifact (list order)
     DevBuf<float> centroids_, P_, rc_, gmean_, cn_;
+    DevBuf<float> Pc_;  // P in the rotation kernel's chain-major order (refresh_rotation())
+    void refresh_rotation();
     float cmax_ = 0.0f;  // max ||centroid|| (bound of the approximate coarse step)
     DevBuf<uint16_t> cent_hi_, cent_lo_;  // bf16 split of the centroids [nlist][tc_k_]
     int tc_k_ = 64;

@@ -118,10 +118,12 @@ void launch_select_probes(const float* dist, int64_t nq, int nlist, int nprobe, 
 // Approximate-then-exact coarse step (same probes as the two launches above).
 void launch_coarse_gemm(const float* q, int64_t nq, const float* cent, const float* cn, int nlist,
                         int d, float* approx, cudaStream_t s);
-// Candidates per query handed from the select kernel to the re-score kernel; rs holds
-// nq x (kCoarseRescoreMax + 1) ints (count, then centroid ids).  rs may be null (the
-// select kernel then re-scores itself).
+// Candidates per query handed from the select kernel to the ordering kernel; rs holds
+// nq x kCoarseRsStride ints (count, ||q||^2 bits, kCoarseRescoreMax centroid ids,
+// kCoarseRescoreMax approximate-score bits).  rs may be null (the select kernel then
+// re-scores every candidate itself).
 constexpr int kCoarseRescoreMax = 64;
+constexpr int kCoarseRsStride = 2 + 2 * kCoarseRescoreMax;
 int launch_coarse_select(float* approx, const float* q, int64_t nq, const float* cent, int nlist,
                           int d, int nprobe, float cmax, float dot_rel, const int* tc_err,
                           int32_t* probes, int* fallbacks, int* rs, cudaStream_t s);
@@ -133,7 +135,10 @@ bool launch_coarse_tc(const void* qh, const void* ql, int64_t nq, const void* ch
                       int nlist, int K, const float* cn, float* out, int* err_flag,
                       cudaStream_t s);
 void launch_centroid_norms(const float* cent, int nlist, int d, float* cn, cudaStream_t s);
-void launch_rotate(const float* x, int64_t nq, int d, int D, const float* P, float* out,
+// q_rot = P * pad(x) in the reference's FMA order; Pc is P in chain-major order
+// (launch_rotation_chain_major).
+void launch_rotation_chain_major(const float* P, int D, float* Pc, cudaStream_t s);
+void launch_rotate(const float* x, int64_t nq, int d, int D, const float* Pc, float* out,
                    cudaStream_t s);
 void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, int D,
                         const float* rc, int nbits, QueryParams* qp, uint8_t* q_i8p,

@@ -20,6 +20,8 @@
 //                         src/faiss/ivf_usq.rs:590-593, padded with (-1, +inf)
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -285,16 +287,28 @@ __device__ __forceinline__ float exact_l2(const float* qs, const float* __restri
 //   |a(q,c) - (||q-c||^2 - ||q||^2)| <= err,  E(c) <= T(c)(1+g),  T(c) <= E(c)/(1-g)
 // with g = (d + 8) 2^-24 bounding the relative error of a sequential sum of d terms.
 // dot_rel bounds |computed q.c - q.c| / sum|q_i c_i| for the GEMM that produced a(q,c).
+struct CoarseErr {
+    double gam;  // relative error bound of a sequential sum of d terms
+    double Qn;   // computed ||q||^2
+    double eQ;   // |Qn - ||q||^2| bound
+    double err;  // |a(q,c) - (||q-c||^2 - ||q||^2)| bound, every c
+};
+__device__ __forceinline__ CoarseErr coarse_err(float qn, float cmax, int d, float dot_rel) {
+    CoarseErr e;
+    e.gam = (double)(d + 8) * 5.9604644775390625e-8;
+    e.Qn = (double)qn;
+    e.eQ = 2.0 * e.gam * e.Qn + 1e-30;
+    const double qnorm = sqrt(e.Qn) * (1.0 + 2.0 * e.gam);
+    const double cm = (double)cmax * (1.0 + 2.0 * e.gam);
+    e.err = 4.0 * (double)dot_rel * qnorm * cm + 2.0 * e.gam * cm * cm +
+            2.384185791015625e-7 * (cm * cm + 2.0 * qnorm * cm) + 1e-30;
+    return e;
+}
 __device__ __forceinline__ double coarse_threshold(float tau, float qn, float cmax, int d,
                                                    float dot_rel) {
-    const double gam = (double)(d + 8) * 5.9604644775390625e-8;
-    const double Qn = (double)qn, eQ = 2.0 * gam * Qn + 1e-30;
-    const double qnorm = sqrt(Qn) * (1.0 + 2.0 * gam);
-    const double cm = (double)cmax * (1.0 + 2.0 * gam);
-    const double err = 4.0 * (double)dot_rel * qnorm * cm + 2.0 * gam * cm * cm +
-                       2.384185791015625e-7 * (cm * cm + 2.0 * qnorm * cm) + 1e-30;
-    const double e_ub = ((double)tau + Qn + eQ + err) * (1.0 + 2.0 * gam);
-    return e_ub * (1.0 + 2.0 * gam) - Qn + eQ + err;
+    const CoarseErr e = coarse_err(qn, cmax, d, dot_rel);
+    const double e_ub = ((double)tau + e.Qn + e.eQ + e.err) * (1.0 + 2.0 * e.gam);
+    return e_ub * (1.0 + 2.0 * e.gam) - e.Qn + e.eQ + e.err;
 }
 
 // One warp: the nprobe (<= kCoarseCap) smallest of row[0..nlist) by (total-order key,
@@ -717,8 +731,9 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
     __shared__ float red[kSelThreads / 32];
     __shared__ int cidx[kCoarseCap];
     __shared__ uint32_t ckey[kCoarseCap];
+    __shared__ float capx[kCoarseRescoreMax];
     __shared__ int cnt_s;
-    __shared__ float thr_s;
+    __shared__ float thr_s, thr_q;
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int64_t qi = blockIdx.x;
     float* qs = sm;
@@ -726,7 +741,7 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
     uint32_t* list = hist + kSelBins;
     const int n4 = nlist >> 2;
     float* grow = approx + qi * nlist;
-    if (rs && tid == 0) rs[qi * (kCoarseRescoreMax + 1)] = 0;  // 0: probes written here
+    if (rs && tid == 0) rs[qi * kCoarseRsStride] = 0;  // 0: probes written here
     // the row: float4 index tid + 256 j, all loads issued before the first use
     float4 v[NV4];
 #pragma unroll
@@ -776,6 +791,7 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
         for (int i = 0; i < kSelThreads / 32; ++i) qsum = __fadd_rn(qsum, red[i]);
         // (double)x <= thr  <=>  x <= thr rounded down to a float
         thr_s = __double2float_rd(coarse_threshold(tau_up, qsum, cmax, d, dot_rel));
+        thr_q = qsum;
     }
     __syncthreads();
     const float thr = thr_s;
@@ -786,16 +802,26 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
             for (int e = 0; e < 4; ++e)
                 if (val(j, e) <= thr) {
                     const int pos = atomicAdd(&cnt_s, 1);
-                    if (pos < kCoarseCap) cidx[pos] = 4 * (tid + j * kSelThreads) + e;
+                    if (pos < kCoarseCap) {
+                        cidx[pos] = 4 * (tid + j * kSelThreads) + e;
+                        if (pos < kCoarseRescoreMax) capx[pos] = val(j, e);
+                    }
                 }
     __syncthreads();
     const int cnt = cnt_s;
     const bool approx_ok = !tc_err || *tc_err == 0;
     if (approx_ok && cnt <= kCoarseCap && cnt >= nprobe) {
         if (cnt <= kCoarseRescoreMax && rs) {
-            // the exact re-score runs in coarse_rescore_kernel (one thread per candidate)
-            for (int i = tid; i < cnt; i += kSelThreads) rs[qi * (kCoarseRescoreMax + 1) + 1 + i] = cidx[i];
-            if (tid == 0) rs[qi * (kCoarseRescoreMax + 1)] = cnt;
+            // ordering (and the few exact sums it needs) in coarse_rescore_kernel
+            int* r = rs + qi * kCoarseRsStride;
+            for (int i = tid; i < cnt; i += kSelThreads) {
+                r[2 + i] = cidx[i];
+                r[2 + kCoarseRescoreMax + i] = __float_as_int(capx[i]);
+            }
+            if (tid == 0) {
+                r[0] = cnt;
+                r[1] = __float_as_int(thr_q);
+            }
             return;
         }
         for (int i = tid; i < cnt; i += kSelThreads)
@@ -818,31 +844,68 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
     if (w == 0) warp_select_stable(grow, nlist, nprobe, hist, ckey, cidx, probes + qi * nprobe);
 }
 
-// Exact re-score of the candidates coarse_select_reg_kernel left in rs (per query: count,
-// then up to kCoarseRescoreMax centroid ids): one thread per candidate runs the reference's
-// sequential sum (exact_l2), so thousands of these latency-bound chains are in flight per
-// SM; then the block orders its query's candidates stably and writes the probes.
+// Order of the candidates coarse_select_reg_kernel left in rs (per query: count, ||q||^2,
+// up to kCoarseRescoreMax centroid ids, their approximate scores a).  Each a bounds the
+// reference's sequential sum E(c) = exact_l2(q, c):
+//   ||q-c||^2 in [a + Qn - eQ - err, a + Qn + eQ + err]   (the coarse threshold's error terms)
+//   E(c) in [||q-c||^2 (1 - g), ||q-c||^2 (1 + g)]          (g: sequential-sum bound)
+// widened by (1 -/+ 2g).  Two candidates whose intervals are disjoint are ordered by
+// them; a candidate whose interval meets another's gets its exact sum (one thread, the
+// reference's order), and such pairs are ordered by (exact key, centroid id) -- the stable
+// sort.  Typically a handful of the ~nprobe candidates of a query need the exact sum.
 __global__ void __launch_bounds__(kCoarseRescoreMax) coarse_rescore_kernel(const float* __restrict__ q, int64_t nq,
                                                                  const float* __restrict__ cent, int d,
-                                                                 int nprobe, const int* __restrict__ rs,
+                                                                 int nprobe, float cmax, float dot_rel,
+                                                                 const int* __restrict__ rs,
                                                                  int32_t* __restrict__ probes) {
     extern __shared__ __align__(16) float qsm[];  // [d]
+    __shared__ double lo_s[kCoarseRescoreMax], hi_s[kCoarseRescoreMax];
     __shared__ uint32_t ckey[kCoarseRescoreMax];
     __shared__ int cidx[kCoarseRescoreMax];
+    __shared__ int need_s[kCoarseRescoreMax];
+    __shared__ int any_s;
     const int64_t qi = blockIdx.x;
-    const int cnt = rs[qi * (kCoarseRescoreMax + 1)];
+    const int* r = rs + qi * kCoarseRsStride;
+    const int cnt = r[0];
     if (cnt == 0) return;  // done by the select kernel
     const int tid = threadIdx.x;
-    for (int i = tid; i < d; i += kCoarseRescoreMax) qsm[i] = q[qi * d + i];
-    const int ci = tid < cnt ? rs[qi * (kCoarseRescoreMax + 1) + 1 + tid] : 0;
-    cidx[tid] = ci;
-    __syncthreads();
-    if (tid < cnt) ckey[tid] = total_order_key(exact_l2(qsm, cent + (int64_t)ci * d, d));
-    __syncthreads();
+    const CoarseErr e = coarse_err(__int_as_float(r[1]), cmax, d, dot_rel);
+    int ci = 0;
+    double lo = 0.0, hi = 0.0;
     if (tid < cnt) {
-        const uint32_t ki = ckey[tid];
+        ci = r[2 + tid];
+        const double a = (double)__int_as_float(r[2 + kCoarseRescoreMax + tid]);
+        lo = (a + e.Qn - e.eQ - e.err) * (1.0 - 2.0 * e.gam);
+        hi = (a + e.Qn + e.eQ + e.err) * (1.0 + 2.0 * e.gam);
+        lo_s[tid] = lo;
+        hi_s[tid] = hi;
+        cidx[tid] = ci;
+    }
+    if (tid == 0) any_s = 0;
+    __syncthreads();
+    bool need = false;
+    if (tid < cnt)
+        for (int j = 0; j < cnt; ++j)
+            if (j != tid && !(hi_s[j] < lo || hi < lo_s[j])) need = true;
+    need_s[tid] = need ? 1 : 0;
+    if (need) any_s = 1;
+    __syncthreads();
+    if (any_s) {
+        for (int i = tid; i < d; i += kCoarseRescoreMax) qsm[i] = q[qi * d + i];
+        __syncthreads();
+        if (need) ckey[tid] = total_order_key(exact_l2(qsm, cent + (int64_t)ci * d, d));
+        __syncthreads();
+    }
+    if (tid < cnt) {
+        const uint32_t ki = need ? ckey[tid] : 0u;
         int rank = 0;
-        for (int j = 0; j < cnt; ++j) rank += (ckey[j] < ki || (ckey[j] == ki && cidx[j] < ci)) ? 1 : 0;
+        for (int j = 0; j < cnt; ++j) {
+            if (j == tid) continue;
+            if (need && need_s[j])
+                rank += (ckey[j] < ki || (ckey[j] == ki && cidx[j] < ci)) ? 1 : 0;
+            else
+                rank += hi_s[j] < lo ? 1 : 0;
+        }
         if (rank < nprobe) probes[qi * nprobe + rank] = ci;
     }
 }
@@ -860,14 +923,29 @@ __global__ void centroid_norms_kernel(const float* __restrict__ cent, int nlist,
 // Query preparation
 // ============================================================================
 
+// P in chain-major order: within each row, Pc[tb*64 + j*4 + k] = P[j + 16*(4*tb + k)]
+// (tb < D/64, j < 16, k < 4), so that the four consecutive terms of chain j inside a
+// 64-column block are one 16-byte load and a half-warp's loads are 256 contiguous bytes.
+__global__ void rotation_chain_major_kernel(const float* __restrict__ P, int D,
+                                            float* __restrict__ Pc) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (int64_t)D * D) return;
+    const int64_t r = e / D;
+    const int i = (int)(e - r * D);
+    const int tb = i >> 6, j = (i & 63) >> 2, k = i & 3;
+    Pc[e] = P[r * D + j + 16 * (4 * tb + k)];
+}
+
 // q_rot[q][r] = tree16( lane j: fma chain over c = j, j+16, ... of P[r][c]*x[c] ).
 // QT queries per CTA, staged transposed in shared memory ([D][QT+4] floats) so a lane
 // reads the QT query values of one column with 16-byte loads.  A half-warp owns R
 // consecutive rows (16*R rows per CTA); lane j keeps the chain of column class j for
 // R rows x QT queries, so every query value loaded feeds R FMAs and every P value QT.
+// Pc is P in chain-major order (rotation_chain_major_kernel): one 16-byte load per row
+// brings chain j's next four terms.
 template <int QT, int R>
 __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x, int64_t nq,
-                                                     int d, int D, const float* __restrict__ P,
+                                                     int d, int D, const float* __restrict__ Pc,
                                                      float* __restrict__ out) {
     constexpr int LD = QT + 4;
     extern __shared__ __align__(16) float xs[];  // [D][LD]
@@ -901,27 +979,31 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x
     const unsigned hmask = 0xFFFFu << (threadIdx.x & 16);
     const int rbase = blockIdx.x * (16 * R) + half * R;
     if (rbase >= D) return;  // D % 64 == 0 and R divides 64: all R rows exist
-    const float* p0 = P + (int64_t)rbase * D;
+    const float4* p0 = reinterpret_cast<const float4*>(Pc + (int64_t)rbase * D) + j;
+    const int D4r = D / 4;  // float4 per row
     float acc[R][QT];
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int t = 0; t < QT; ++t) acc[r][t] = 0.0f;
-#pragma unroll 2
-    for (int c = j; c < D; c += 16) {
-        float p[R];
+    for (int tb = 0; tb < D / 64; ++tb) {
+        float4 p4[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) p[r] = __ldg(p0 + (int64_t)r * D + c);
-        const float4* xv = reinterpret_cast<const float4*>(xs + c * LD);
+        for (int r = 0; r < R; ++r) p4[r] = __ldg(p0 + (int64_t)r * D4r + tb * 16);
 #pragma unroll
-        for (int t4 = 0; t4 < QT / 4; ++t4) {
-            const float4 v = xv[t4];
+        for (int k = 0; k < 4; ++k) {
+            const float4* xv = reinterpret_cast<const float4*>(xs + (64 * tb + 16 * k + j) * LD);
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                acc[r][4 * t4 + 0] = __fmaf_rn(p[r], v.x, acc[r][4 * t4 + 0]);
-                acc[r][4 * t4 + 1] = __fmaf_rn(p[r], v.y, acc[r][4 * t4 + 1]);
-                acc[r][4 * t4 + 2] = __fmaf_rn(p[r], v.z, acc[r][4 * t4 + 2]);
-                acc[r][4 * t4 + 3] = __fmaf_rn(p[r], v.w, acc[r][4 * t4 + 3]);
+            for (int t4 = 0; t4 < QT / 4; ++t4) {
+                const float4 v = xv[t4];
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const float p = k == 0 ? p4[r].x : k == 1 ? p4[r].y : k == 2 ? p4[r].z : p4[r].w;
+                    acc[r][4 * t4 + 0] = __fmaf_rn(p, v.x, acc[r][4 * t4 + 0]);
+                    acc[r][4 * t4 + 1] = __fmaf_rn(p, v.y, acc[r][4 * t4 + 1]);
+                    acc[r][4 * t4 + 2] = __fmaf_rn(p, v.z, acc[r][4 * t4 + 2]);
+                    acc[r][4 * t4 + 3] = __fmaf_rn(p, v.w, acc[r][4 * t4 + 3]);
+                }
             }
         }
     }
@@ -1859,7 +1941,7 @@ int launch_coarse_select(float* approx, const float* q, int64_t nq, const float*
         else go(coarse_select_reg_kernel<4>);
         if (rs)
             coarse_rescore_kernel<<<(unsigned)nq, kCoarseRescoreMax, (size_t)d * sizeof(float), s>>>(
-                q, nq, cent, d, nprobe, rs, probes);
+                q, nq, cent, d, nprobe, cmax, dot_rel, rs, probes);
         return rs ? 2 : 1;
     }
     const size_t blk_bytes =
@@ -1883,14 +1965,19 @@ void launch_centroid_norms(const float* cent, int nlist, int d, float* cn, cudaS
     centroid_norms_kernel<<<(nlist + 127) / 128, 128, 0, s>>>(cent, nlist, d, cn);
 }
 
-void launch_rotate(const float* x, int64_t nq, int d, int D, const float* P, float* out,
+void launch_rotation_chain_major(const float* P, int D, float* Pc, cudaStream_t s) {
+    const int64_t n = (int64_t)D * D;
+    rotation_chain_major_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(P, D, Pc);
+}
+
+void launch_rotate(const float* x, int64_t nq, int d, int D, const float* Pc, float* out,
                    cudaStream_t s) {
     if (nq <= 0) return;
     constexpr int QT = 8, R = 8;
     const size_t smem = (size_t)D * (QT + 4) * sizeof(float);
     cudaFuncSetAttribute(rotate_kernel<QT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     dim3 grid((D + 16 * R - 1) / (16 * R), (unsigned)((nq + QT - 1) / QT));
-    rotate_kernel<QT, R><<<grid, 256, smem, s>>>(x, nq, d, D, P, out);
+    rotate_kernel<QT, R><<<grid, 256, smem, s>>>(x, nq, d, D, Pc, out);
 }
 
 void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, int D,

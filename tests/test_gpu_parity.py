@@ -327,6 +327,49 @@ def test_coarse_fast_path_equals_exact(gpu, oracle_mod, nlist, d, nprobe, normal
     assert np.array_equal(fast[:60], op)
 
 
+@pytest.mark.parametrize("d", [768, 128])
+def test_coarse_near_ties_order(gpu, oracle_mod, d):
+    """Candidates a rounding apart: pairs and triples of equal centroids and centroids one
+    ulp apart in one coordinate, with queries next to them, so that the approximate-score
+    intervals of several top-nprobe candidates overlap and their order comes from the
+    exact sums (ties by centroid id).  Probes equal the exact kernels and the oracle."""
+    import torch
+    from hanns_b200 import _lib
+    from hanns_b200.ivf_usq import IvfUsqIndex
+    O = oracle_mod
+    rng = np.random.default_rng(15)
+    nlist, nprobe, nq = 4096, 32, 800
+    cent = rng.normal(size=(nlist, d)).astype(np.float32)
+    cent /= np.linalg.norm(cent, axis=1, keepdims=True)
+    for i in range(0, 400, 8):
+        cent[i + 1] = cent[i]                                   # exact tie
+        cent[i + 2] = cent[i]
+        cent[i + 2, i % d] = np.nextafter(cent[i, i % d], np.float32(2))   # one ulp
+        cent[i + 3] = cent[i]
+        cent[i + 3, (i + 1) % d] = np.nextafter(cent[i, (i + 1) % d], np.float32(-2))
+    q = rng.normal(size=(nq, d)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    base = rng.integers(0, 50, nq) * 8
+    q[:600] = cent[base[:600]] + 0.05 * rng.normal(size=(600, d)).astype(np.float32)
+    art = _empty_artifact(cent, (d + 63) // 64 * 64)
+    idx = IvfUsqIndex.from_artifact(art)
+    fast = idx.debug_query(q, nprobe)["probes"]
+    qt = torch.from_numpy(q).cuda()
+    ct = torch.from_numpy(cent).cuda()
+    exact = torch.empty(nq, nprobe, dtype=torch.int32, device="cuda")
+    step = max(1, ((16 << 20) - nq * nprobe * 8) // (4 * nlist) - 1)
+    for s in range(0, nq, step):
+        m = min(step, nq - s)
+        rc = gpu.hanns_gpu_coarse_probes_static(qt[s:].data_ptr(), m, ct.data_ptr(), nlist, d, nprobe,
+                                                exact[s:].data_ptr(), None)
+        assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    assert np.array_equal(fast, exact.cpu().numpy())
+    oi = O.OracleIndex(art)
+    _, _, _, op = oi.search(q[:40], 5, nprobe, want_probes=True)
+    assert np.array_equal(fast[:40], op)
+
+
 def test_query_split_shards_equal_single_gpu(gpu, oracle_mod):
     """Query-split multi-GPU protocol on one device: two list shards of one index, each
     prepares the state of half of the queries, the halves are concatenated (the NCCL
