@@ -12,6 +12,7 @@
 // for each 64-dim chunk c, the 32 vectors' 8 sign bytes contiguously
 // ([block][D/64][32 slots][8 bytes]).  Nibble j of a chunk's 64-bit word is the
 // reference's FastScan nibble of group 16c+j (dims 4j..4j+3, LSB = lowest dim).
+#include <algorithm>
 #include <cstdint>
 
 #include "common.cuh"
@@ -206,15 +207,106 @@ __global__ void kmeans_accumulate_kernel(const float* __restrict__ x, int64_t n,
     }
 }
 
+// One warp per centroid: new mean of its rows (kept in place when it has none) and the
+// L2 shift from the old position (kmeans.rs:246-271), 0 for empty centroids.
 __global__ void kmeans_update_kernel(const long long* __restrict__ sums,
                                      const int* __restrict__ counts, int nlist, int d,
-                                     float* __restrict__ cent) {
-    const int64_t total = (int64_t)nlist * d;
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
-         e += (int64_t)gridDim.x * blockDim.x) {
-        const int c = (int)(e / d);
-        if (counts[c] > 0) cent[e] = (float)((double)sums[e] / 4294967296.0 / (double)counts[c]);
+                                     float* __restrict__ cent, float* __restrict__ shift) {
+    const int c = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (c >= nlist) return;
+    const int cnt = counts[c];
+    float ss = 0.0f;
+    if (cnt > 0) {
+        for (int j = lane; j < d; j += 32) {
+            const int64_t e = (int64_t)c * d + j;
+            const float nv = (float)((double)sums[e] / 4294967296.0 / (double)cnt);
+            const float df = nv - cent[e];
+            ss = fmaf(df, df, ss);
+            cent[e] = nv;
+        }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) shift[c] = sqrtf(ss);
+}
+
+// k-means++ seeding (kmeans.rs:138-183), with this library's seeded random stream.
+// kpp_dist: min_d[i] = min(min_d[i], ||x_i - c||^2) for the newest centroid c, one warp
+// per row; block b covers rows [b*per, (b+1)*per) and writes sum(max(min_d, 0)) of them.
+__global__ void kpp_dist_kernel(const float* __restrict__ x, int64_t n, int d,
+                                const float* __restrict__ c, int64_t per,
+                                float* __restrict__ min_d, double* __restrict__ block_sum) {
+    __shared__ double part[8];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r0 = (int64_t)blockIdx.x * per;
+    const int64_t r1 = min(n, r0 + per);
+    double acc = 0.0;
+    for (int64_t i = r0 + w; i < r1; i += 8) {
+        const float* xi = x + i * d;
+        float s = 0.0f;
+        for (int j = lane; j < d; j += 32) {
+            const float df = xi[j] - c[j];
+            s = fmaf(df, df, s);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        float m = min_d[i];
+        if (s < m) m = s;
+        if (lane == 0) min_d[i] = m;
+        acc += (double)fmaxf(m, 0.0f);
+    }
+    if (lane == 0) part[w] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < 8; ++k) t += part[k];
+        block_sum[blockIdx.x] = t;
+    }
+}
+
+// kpp_pick: draw row i with probability max(min_d[i], 0) / total (a uniform row when the
+// total is 0) and copy it into centroid slot `slot`.  One thread walks the block sums,
+// then the rows of the chosen block, in order.
+__global__ void kpp_pick_kernel(const float* __restrict__ x, int64_t n, int d,
+                                const float* __restrict__ min_d, const double* __restrict__ block_sum,
+                                int nblocks, int64_t per, double u_target, double u_uniform,
+                                float* __restrict__ cent, int slot) {
+    __shared__ int64_t chosen;
+    if (threadIdx.x == 0) {
+        double total = 0.0;
+        for (int b = 0; b < nblocks; ++b) total += block_sum[b];
+        int64_t idx = n - 1;
+        if (!(total > 0.0)) {
+            idx = min(n - 1, (int64_t)(u_uniform * (double)n));
+        } else {
+            const double target = u_target * total;
+            double cum = 0.0;
+            int b = 0;
+            for (; b < nblocks - 1; ++b) {
+                if (cum + block_sum[b] >= target) break;
+                cum += block_sum[b];
+            }
+            const int64_t r1 = min(n, (int64_t)(b + 1) * per);
+            for (int64_t i = (int64_t)b * per; i < r1; ++i) {
+                cum += (double)fmaxf(min_d[i], 0.0f);
+                if (cum >= target) {
+                    idx = i;
+                    break;
+                }
+            }
+        }
+        chosen = idx;
+    }
+    __syncthreads();
+    const int64_t idx = chosen;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) cent[(int64_t)slot * d + j] = x[idx * d + j];
+}
+
+__global__ void fill_f32_kernel(float* __restrict__ p, int64_t n, float v) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+         e += (int64_t)gridDim.x * blockDim.x)
+        p[e] = v;
 }
 
 // One CTA per list: copy every row's sign bytes into the GPU FastScan blocks.
@@ -280,9 +372,29 @@ void launch_kmeans_accumulate(const float* x, int64_t n, int d, const int32_t* a
             x, n, d, assign, reinterpret_cast<unsigned long long*>(sums), counts);
 }
 void launch_kmeans_update(const long long* sums, const int* counts, int nlist, int d,
-                          float* centroids, cudaStream_t s) {
-    kmeans_update_kernel<<<grid_for((int64_t)nlist * d), 256, 0, s>>>(sums, counts, nlist, d,
-                                                                      centroids);
+                          float* centroids, float* shift, cudaStream_t s) {
+    kmeans_update_kernel<<<(unsigned)(((int64_t)nlist * 32 + 255) / 256), 256, 0, s>>>(
+        sums, counts, nlist, d, centroids, shift);
+}
+
+int kpp_blocks(int64_t n, int64_t* per) {
+    const int64_t nb = std::min<int64_t>(1024, std::max<int64_t>(1, (n + 255) / 256));
+    *per = (n + nb - 1) / nb;
+    return (int)((n + *per - 1) / *per);
+}
+
+void launch_kpp_init_min(float* min_d, int64_t n, cudaStream_t s) {
+    fill_f32_kernel<<<grid_for(n), 256, 0, s>>>(min_d, n, 3.402823466e38f);
+}
+
+void launch_kpp_step(const float* x, int64_t n, int d, float* cent, int slot, float* min_d,
+                     double* block_sum, double u_target, double u_uniform, cudaStream_t s) {
+    int64_t per = 0;
+    const int nb = kpp_blocks(n, &per);
+    kpp_dist_kernel<<<nb, 256, 0, s>>>(x, n, d, cent + (int64_t)(slot - 1) * d, per, min_d,
+                                       block_sum);
+    kpp_pick_kernel<<<1, 256, 0, s>>>(x, n, d, min_d, block_sum, nb, per, u_target, u_uniform,
+                                      cent, slot);
 }
 void launch_build_fastscan(const uint8_t* signs, const int64_t* list_off, const int64_t* blk_off,
                            int nlist, int D, uint2* fs, cudaStream_t s) {

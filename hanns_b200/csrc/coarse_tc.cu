@@ -8,10 +8,12 @@
 // the bf16 representation and the tensor-core accumulation.
 //
 // One CTA computes one 128 (queries) x 256 (centroids) tile.  Warp roles:
-//   warp 0  TMA producer: 4-stage ring of {A 128x64, B 256x64} bf16 tiles, 128-byte
-//           swizzle, one mbarrier per stage with the transaction byte count
+//   warp 0  TMA producer: 2-stage ring of {A hi, A lo 128x64; B hi, B lo 256x64} bf16
+//           tiles (one 64-wide K block of both splits, so every tile crosses L2 once),
+//           128-byte swizzle, one mbarrier per stage with the transaction byte count
 //   warp 1  TMEM allocation (256 fp32 columns) and the single-thread MMA issuer:
-//           4 x (M128 N256 K16) per stage, tcgen05.commit releases the stage
+//           4 x 3 (hi.hi, hi.lo, lo.hi) M128 N256 K16 per stage, tcgen05.commit releases
+//           the stage
 //   warps 2-5  epilogue: tcgen05.ld of the 128x256 accumulator (32 rows per warp),
 //           out = fma(-2, acc, ||c||^2) stored row-major [nq][nlist]
 // Every mbarrier wait is bounded; on expiry the kernel records an error code and
@@ -29,10 +31,11 @@ namespace hanns {
 namespace {
 
 constexpr int kTM = 128, kTN = 256, kTK = 64;  // tile; kTK bf16 = 128 bytes (one swizzle row)
-constexpr int kStagesTC = 4;
+constexpr int kStagesTC = 2;
 constexpr int kABytes = kTM * kTK * 2;  // 16 KiB
 constexpr int kBBytes = kTN * kTK * 2;  // 32 KiB
-constexpr int kStageBytes = kABytes + kBBytes;
+// stage layout: A hi | A lo | B hi | B lo (each 1024-byte aligned)
+constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
 constexpr int kTcThreads = 192;
 constexpr uint32_t kWaitLimit = 1u << 26;  // bounded spins (seconds), then error
 
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kTN;
     const int64_t m0 = (int64_t)blockIdx.y * kTM;
-    const int total_kb = 3 * kblocks;  // hi.hi, hi.lo, lo.hi
+    const int total_kb = kblocks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStagesTC; ++s) {
@@ -182,12 +185,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(
                     atomicExch(err_flag, 1);
                     break;
                 }
-                const int seg = kb / kblocks, kk = (kb % kblocks) * kTK;
-                uint8_t* a_dst = smem + s * kStageBytes;
-                uint8_t* b_dst = a_dst + kABytes;
+                const int kk = kb * kTK;
+                uint8_t* dst = smem + s * kStageBytes;
                 mbar_expect_tx(&full[s], kStageBytes);
-                tma_load_2d(a_dst, seg == 2 ? &maps.ql : &maps.qh, &full[s], kk, (int)m0);
-                tma_load_2d(b_dst, seg == 1 ? &maps.cl : &maps.ch, &full[s], kk, n0);
+                tma_load_2d(dst, &maps.qh, &full[s], kk, (int)m0);
+                tma_load_2d(dst + kABytes, &maps.ql, &full[s], kk, (int)m0);
+                tma_load_2d(dst + 2 * kABytes, &maps.ch, &full[s], kk, n0);
+                tma_load_2d(dst + 2 * kABytes + kBBytes, &maps.cl, &full[s], kk, n0);
             }
         }
     } else if (warp == 1) {
@@ -200,12 +204,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t a_addr = smem_u32(smem + s * kStageBytes);
-                const uint32_t b_addr = a_addr + kABytes;
+                const uint32_t ah = smem_u32(smem + s * kStageBytes);
+                const uint32_t al = ah + kABytes;
+                const uint32_t bh = ah + 2 * kABytes;
+                const uint32_t bl = bh + kBBytes;
 #pragma unroll
-                for (int k = 0; k < kTK / 16; ++k)  // K16 steps = 32 bytes inside the swizzle row
-                    umma_f16(tmem, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32),
+                for (int k = 0; k < kTK / 16; ++k) {  // K16 steps = 32 bytes inside the swizzle row
+                    umma_f16(tmem, sw128_desc(ah + k * 32), sw128_desc(bh + k * 32),
                              (kb > 0 || k > 0) ? 1u : 0u);
+                    umma_f16(tmem, sw128_desc(ah + k * 32), sw128_desc(bl + k * 32), 1u);
+                    umma_f16(tmem, sw128_desc(al + k * 32), sw128_desc(bh + k * 32), 1u);
+                }
                 umma_commit(&empty[s]);
             }
             umma_commit(acc_full);

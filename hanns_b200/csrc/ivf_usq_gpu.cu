@@ -320,30 +320,49 @@ void IvfUsqGpu::train(const float* h_data, int64_t n, int kmeans_iters, uint64_t
     if (n < nlist_) throw std::invalid_argument("training data too small: n < nlist");
     DevBuf<float> x;
     h2d(x, h_data, (size_t)n * dim_, stream_);
-    // k-means init: nlist distinct rows chosen by a seeded partial Fisher-Yates.
-    std::vector<int64_t> perm(n);
-    std::iota(perm.begin(), perm.end(), 0);
+    // Seeded uniform stream in [0, 1) (the reference draws from an entropy-seeded StdRng).
     uint64_t s = kmeans_seed ^ 0xD1B54A32D192ED03ull;
-    for (int64_t i = 0; i < nlist_; ++i) {
+    auto uniform = [&s]() {
         s = s * 6364136223846793005ull + 1442695040888963407ull;
-        const int64_t j = i + (int64_t)((s >> 33) % (uint64_t)(n - i));
-        std::swap(perm[i], perm[j]);
-    }
-    std::vector<int64_t> init(perm.begin(), perm.begin() + nlist_);
-    DevBuf<int64_t> d_init;
-    h2d(d_init, init.data(), init.size(), stream_);
+        return (double)(s >> 11) * (1.0 / 9007199254740992.0);
+    };
+    // k-means++ seeding (kmeans.rs:138-183): the first centroid a uniform row, each next one
+    // a row drawn with probability proportional to its squared distance to the nearest
+    // centroid so far.
     centroids_.reserve((size_t)nlist_ * dim_);
-    launch_gather_rows(reinterpret_cast<const uint8_t*>(x.p), d_init.p, nlist_, (int64_t)dim_ * 4,
-                       reinterpret_cast<uint8_t*>(centroids_.p), stream_);
+    {
+        const int64_t first = std::min<int64_t>(n - 1, (int64_t)(uniform() * (double)n));
+        HANNS_CUDA_OK(cudaMemcpyAsync(centroids_.p, x.p + first * dim_, sizeof(float) * dim_,
+                                      cudaMemcpyDeviceToDevice, stream_));
+        DevBuf<float> min_d;
+        min_d.reserve(n);
+        int64_t per = 0;
+        DevBuf<double> block_sum;
+        block_sum.reserve(kpp_blocks(n, &per));
+        launch_kpp_init_min(min_d.p, n, stream_);
+        for (int c = 1; c < nlist_; ++c) {
+            const double ut = uniform(), uu = uniform();
+            launch_kpp_step(x.p, n, dim_, centroids_.p, c, min_d.p, block_sum.p, ut, uu, stream_);
+        }
+        HANNS_CUDA_OK(cudaGetLastError());
+        HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    }
     DevBuf<int32_t> assign;
     assign.reserve(n);
     DevBuf<long long> sums;
     sums.reserve((size_t)nlist_ * dim_);
     DevBuf<int> counts;
     counts.reserve(nlist_);
+    DevBuf<float> shift;
+    shift.reserve(nlist_);
+    std::vector<int> h_counts(nlist_);
+    std::vector<float> h_shift(nlist_);
+    std::vector<int32_t> h_assign;
+    std::vector<float> row(dim_);
     const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(n, (1ll << 28) / nlist_));
     DevBuf<float> dist;
     dist.reserve((size_t)chunk * nlist_);
+    constexpr float kTolerance = 1e-2f;  // KMeans::new (kmeans.rs:44-56)
     for (int it = 0; it < kmeans_iters; ++it) {
         for (int64_t b = 0; b < n; b += chunk) {
             const int64_t m = std::min(chunk, n - b);
@@ -353,8 +372,39 @@ void IvfUsqGpu::train(const float* h_data, int64_t n, int kmeans_iters, uint64_t
         HANNS_CUDA_OK(cudaMemsetAsync(sums.p, 0, sizeof(long long) * nlist_ * dim_, stream_));
         HANNS_CUDA_OK(cudaMemsetAsync(counts.p, 0, sizeof(int) * nlist_, stream_));
         launch_kmeans_accumulate(x.p, n, dim_, assign.p, sums.p, counts.p, stream_);
-        launch_kmeans_update(sums.p, counts.p, nlist_, dim_, centroids_.p, stream_);
+        launch_kmeans_update(sums.p, counts.p, nlist_, dim_, centroids_.p, shift.p, stream_);
         HANNS_CUDA_OK(cudaGetLastError());
+        HANNS_CUDA_OK(cudaMemcpyAsync(h_counts.data(), counts.p, sizeof(int) * nlist_,
+                                      cudaMemcpyDeviceToHost, stream_));
+        HANNS_CUDA_OK(cudaMemcpyAsync(h_shift.data(), shift.p, sizeof(float) * nlist_,
+                                      cudaMemcpyDeviceToHost, stream_));
+        HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+        // empty centroids restart at a random row of the largest list (the last one among
+        // equal counts), scaled by 1 + 1e-4 (u - 0.5) per element (kmeans.rs:272-290)
+        int largest = 0;
+        for (int c = 0; c < nlist_; ++c)
+            if (h_counts[c] >= h_counts[largest]) largest = c;
+        std::vector<int64_t> members;
+        for (int c = 0; c < nlist_; ++c) {
+            if (h_counts[c] > 0) continue;
+            if (members.empty()) {
+                h_assign.resize(n);
+                HANNS_CUDA_OK(cudaMemcpy(h_assign.data(), assign.p, sizeof(int32_t) * n,
+                                         cudaMemcpyDeviceToHost));
+                for (int64_t i = 0; i < n; ++i)
+                    if (h_assign[i] == largest) members.push_back(i);
+                if (members.empty()) break;
+            }
+            const int64_t pick = members[std::min<size_t>(
+                members.size() - 1, (size_t)(uniform() * (double)members.size()))];
+            for (int j = 0; j < dim_; ++j)
+                row[j] = h_data[pick * dim_ + j] * (1.0f + 1e-4f * ((float)uniform() - 0.5f));
+            HANNS_CUDA_OK(cudaMemcpy(centroids_.p + (int64_t)c * dim_, row.data(),
+                                     sizeof(float) * dim_, cudaMemcpyHostToDevice));
+        }
+        float max_shift = 0.0f;
+        for (int c = 0; c < nlist_; ++c) max_shift = std::max(max_shift, h_shift[c]);
+        if (max_shift < kTolerance) break;
     }
     update_centroid_norms();
     gmean_.reserve(dim_);

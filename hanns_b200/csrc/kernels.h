@@ -173,7 +173,13 @@ void launch_argmin_rows(const float* dist, int64_t n, int nlist, int32_t* out, c
 void launch_kmeans_accumulate(const float* x, int64_t n, int d, const int32_t* assign,
                               long long* sums, int* counts, cudaStream_t s);
 void launch_kmeans_update(const long long* sums, const int* counts, int nlist, int d,
-                          float* centroids, cudaStream_t s);
+                          float* centroids, float* shift, cudaStream_t s);
+// k-means++ seeding steps (build_kernels.cu): blocks of the distance pass for n rows, the
+// min-distance reset, and one step (distances to centroid slot-1, draw of centroid slot).
+int kpp_blocks(int64_t n, int64_t* per);
+void launch_kpp_init_min(float* min_d, int64_t n, cudaStream_t s);
+void launch_kpp_step(const float* x, int64_t n, int d, float* cent, int slot, float* min_d,
+                     double* block_sum, double u_target, double u_uniform, cudaStream_t s);
 void launch_build_fastscan(const uint8_t* signs, const int64_t* list_off, const int64_t* blk_off,
                            int nlist, int D, uint2* fs, cudaStream_t s);
 void launch_gather_rows(const uint8_t* src, const int64_t* perm, int64_t n, int64_t row_bytes,

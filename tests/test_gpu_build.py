@@ -55,6 +55,31 @@ def test_gpu_build_matches_oracle(oracle_mod):
         assert (sizes > 0).sum() >= 10
 
 
+def test_kmeans_seeding_and_empty_list_restart():
+    """k-means++ seeding and the restart of empty centroids (src/quantization/kmeans.rs:
+    138-183, 272-290): 64 lists over 8 tight clusters -- random seeding leaves most
+    centroids without rows, the reference's scheme keeps every list populated."""
+    from hanns_b200.ivf_usq import IvfUsqConfig, IvfUsqIndex
+    from tests.golden.make_golden import mixture
+    rng = np.random.default_rng(91)
+    d, nlist = 64, 64
+    x, _ = mixture(rng, 8000, d, 8, 0.05, False)
+    idx = IvfUsqIndex(IvfUsqConfig(d, nlist, 4, rotation_seed=3))
+    idx.train(x, kmeans_iters=25, kmeans_seed=4)
+    idx.add(x)
+    art = idx.export_artifact()
+    sizes = np.diff(art["list_offsets"])
+    assert sizes.sum() == 8000
+    assert (sizes == 0).sum() == 0, sizes
+    cent = art["centroids"]
+    assert len(np.unique(cent.round(6), axis=0)) == nlist
+    # same seed, same centroids
+    idx2 = IvfUsqIndex(IvfUsqConfig(d, nlist, 4, rotation_seed=3))
+    idx2.train(x, kmeans_iters=25, kmeans_seed=4)
+    idx2.add(x[:10])
+    assert np.array_equal(idx2.export_artifact()["centroids"].view(np.uint32), cent.view(np.uint32))
+
+
 def test_knowhere_lifecycle_and_persistence(tmp_path):
     """create -> train -> add -> search -> save -> load -> search (C ABI)."""
     from hanns_b200 import _lib
