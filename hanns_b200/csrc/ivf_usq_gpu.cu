@@ -787,7 +787,22 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     launch_scan(a, grid, s);
     launches += 1;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[6], s));
-    // 5. merge
+    // 5. each (query, probe) pair's top-k into a compact region of nprobe * k entries
+    w_cmp_key_.reserve((size_t)nb * nprobe * k);
+    w_cmp_tie_.reserve((size_t)nb * nprobe * k);
+    CompactArgs c{};
+    c.nq = nb;
+    c.nprobe = nprobe;
+    c.k = k;
+    c.cand_key = w_cand_key_.p;
+    c.cand_tie = w_cand_tie_.p;
+    c.pair_off = w_pair_off_.p;
+    c.q_stride = q_stride;
+    c.out_key = w_cmp_key_.p;
+    c.out_tie = w_cmp_tie_.p;
+    launch_compact_pairs(c, s);
+    launches += 1;
+    // 6. merge over the compact regions
     w_mkey_.reserve((size_t)nb * k);
     w_mtie_.reserve((size_t)nb * k);
     MergeArgs m{};
@@ -795,10 +810,11 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     m.nprobe = nprobe;
     m.k = k;
     m.nlist = nlist_;
-    m.cand_key = w_cand_key_.p;
-    m.cand_tie = w_cand_tie_.p;
-    m.pair_off = w_pair_off_.p;
-    m.q_stride = q_stride;
+    m.cand_key = w_cmp_key_.p;
+    m.cand_tie = w_cmp_tie_.p;
+    m.pair_off = nullptr;
+    m.q_stride = (int64_t)nprobe * k;
+    m.fixed_total = nprobe * k;
     m.probes = st.probes;
     m.list_off = list_off_.p;
     m.ids = ids_.p;

@@ -195,6 +195,8 @@ class IvfUsqGpu {
     DevBuf<uint64_t> w_mtie_, w_cand_tie_, w_bits_;
     DevBuf<int16_t> w_scores_;
     DevBuf<uint32_t> w_cand_key_;
+    DevBuf<uint32_t> w_cmp_key_;  // per (query, probe) top-k, nprobe * k per query
+    DevBuf<uint64_t> w_cmp_tie_;
     DevBuf<int32_t> w_qbits_;
     DevBuf<int64_t> w_out_ids_, w_out_counts_;
     DevBuf<float> w_out_dists_;

@@ -83,13 +83,27 @@ struct TcScanArgs {
     int* err_flag;          // set to 4 when a bounded wait expired
 };
 
-struct MergeArgs {
+// Per (query, probe) pair top-k of the scan's candidate regions into a compact region
+// of nprobe * k entries per query (slot rank * k).
+struct CompactArgs {
     int64_t nq;
-    int nprobe, k, nlist;
-    const uint32_t* cand_key;  // candidate regions written by the list scan
+    int nprobe, k;
+    const uint32_t* cand_key;
     const uint64_t* cand_tie;
     const int* pair_off;
     int64_t q_stride;
+    uint32_t* out_key;
+    uint64_t* out_tie;
+};
+
+struct MergeArgs {
+    int64_t nq;
+    int nprobe, k, nlist;
+    const uint32_t* cand_key;  // candidate regions written by the list scan (or compacted)
+    const uint64_t* cand_tie;
+    const int* pair_off;
+    int64_t q_stride;
+    int fixed_total;  // > 0: every query has this many entries (compact regions)
     const int32_t* probes;
     const int64_t* list_off;
     const int64_t* ids;
@@ -157,6 +171,7 @@ size_t scan_tc_smem_bytes();
 void launch_scan_tc(const TcScanArgs& a, int grid, cudaStream_t s);
 int scan_grid_size(int D);
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s);
+void launch_compact_pairs(const CompactArgs& a, cudaStream_t s);
 void launch_merge(const MergeArgs& a, cudaStream_t s);
 void launch_merge_shards(const float* dists, const uint64_t* keys, const int64_t* ids, int world,
                          int64_t nq, int k, int64_t* out_ids, float* out_dists, cudaStream_t s);

@@ -1247,6 +1247,70 @@ struct ScanSmem {
     int pad[3];  // keeps the dynamic arrays after it 16-byte aligned
 };
 
+// ============================================================================
+// Top-k of a set of candidate entries (one warp): the k smallest by (distance key, tie)
+// among entries whose tie is not ~0, written unsorted to sk/st; returns how many.
+// ============================================================================
+__device__ int warp_select_topk(const uint32_t* keys, const uint64_t* ties, int total, int k,
+                                uint32_t* sk, uint64_t* st, uint32_t* hist) {
+    const int lane = (int)lane_id();
+    auto key_at = [&](int e, uint32_t& kk) {
+        if (ties[e] == ~0ull) return false;
+        kk = keys[e];
+        return true;
+    };
+    int n_valid = 0;
+    for (int e = lane; e < total; e += 32) n_valid += ties[e] != ~0ull ? 1 : 0;
+    n_valid = warp_sum(n_valid);
+    const int take = min(k, n_valid);
+    int written = 0;
+    if (take > 0) {
+        int less = 0;
+        uint32_t tau = 0xFFFFFFFFu;
+        if (n_valid > k) tau = warp_radix_kth(total, k, key_at, hist, &less);
+        for (int base = 0; base < total; base += 32) {
+            const int e = base + lane;
+            uint32_t kk = 0;
+            const bool ok = e < total && key_at(e, kk);
+            const bool lt = ok && (n_valid <= k || kk < tau);
+            const unsigned bl = __ballot_sync(0xffffffffu, lt);
+            if (lt) {
+                const int pos = written + __popc(bl & lanemask_lt());
+                sk[pos] = kk;
+                st[pos] = ties[e];
+            }
+            written += __popc(bl);
+        }
+        // ties at tau: chosen in increasing (probe rank, fastscan key, index) order
+        uint64_t floor_t = 0;
+        bool have_floor = false;
+        while (written < take) {
+            uint64_t best = ~0ull;
+            for (int e = lane; e < total; e += 32) {
+                uint32_t kk;
+                if (key_at(e, kk) && kk == tau) {
+                    const uint64_t t = ties[e];
+                    if ((!have_floor || t > floor_t) && t < best) best = t;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+                best = ob < best ? ob : best;
+            }
+            if (lane == 0) {
+                sk[written] = tau;
+                st[written] = best;
+            }
+            floor_t = best;
+            have_floor = true;
+            ++written;
+        }
+    }
+    __syncwarp();
+    return take;
+}
+
 __device__ __forceinline__ int32_t wrap16(int32_t v) { return (int32_t)(int16_t)v; }
 
 // Integer dot of one stored vector with one quantised query (dp4a layout), by the 8
@@ -1701,6 +1765,31 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
     }
 }
 
+// Per (query, probe) pair (one warp): the k best of the pair's kept candidates, into a
+// fixed slot of k entries (rank * k) of the query's compact region; unused entries get
+// key ~0u and tie ~0ull.  The top-k of a query over the union of its pairs' top-k equals
+// its top-k over all candidates.
+__global__ void __launch_bounds__(128) compact_pairs_kernel(CompactArgs a) {
+    __shared__ uint32_t hist[4][256];
+    const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    const int64_t pr = (int64_t)blockIdx.x * 4 + w;
+    if (pr >= a.nq * a.nprobe) return;
+    const int64_t q = pr / a.nprobe;
+    const int r = (int)(pr - q * a.nprobe);
+    const int* po = a.pair_off + q * (a.nprobe + 1);
+    const int64_t base = q * a.q_stride + po[r];
+    const int total = po[r + 1] - po[r];
+    uint32_t* ok = a.out_key + pr * a.k;
+    uint64_t* ot = a.out_tie + pr * a.k;
+    const int take = total > 0 ? warp_select_topk(a.cand_key + base, a.cand_tie + base, total, a.k,
+                                                  ok, ot, hist[w])
+                               : 0;
+    for (int i = take + lane; i < a.k; i += 32) {
+        ok[i] = 0xFFFFFFFFu;
+        ot[i] = ~0ull;
+    }
+}
+
 // ============================================================================
 // Final merge: per query (one warp) top-k over all kept candidates of its probes,
 // ordered by (distance key, probe rank, FastScan key, list position).
@@ -1710,65 +1799,11 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
     const int w = threadIdx.x >> 5, lane = (int)lane_id();
     const int64_t q = (int64_t)blockIdx.x * 4 + w;
     if (q >= a.nq) return;
-    const int total = a.pair_off[q * (a.nprobe + 1) + a.nprobe];
-    const uint32_t* keys = a.cand_key + q * a.q_stride;
-    const uint64_t* ties = a.cand_tie + q * a.q_stride;
-    auto key_at = [&](int e, uint32_t& k) {
-        if (ties[e] == ~0ull) return false;
-        k = keys[e];
-        return true;
-    };
-    int n_valid = 0;
-    for (int e = lane; e < total; e += 32) n_valid += ties[e] != ~0ull ? 1 : 0;
-    n_valid = warp_sum(n_valid);
-    const int take = min(a.k, n_valid);
+    const int total = a.fixed_total > 0 ? a.fixed_total : a.pair_off[q * (a.nprobe + 1) + a.nprobe];
     uint32_t* sk = a.sel_key + q * a.k;
     uint64_t* st = a.sel_tie + q * a.k;  // probe rank << 48 | fastscan key << 32 | index
-    int written = 0;
-    if (take > 0) {
-        int less = 0;
-        uint32_t tau = 0xFFFFFFFFu;
-        if (n_valid > a.k) tau = warp_radix_kth(total, a.k, key_at, hist[w], &less);
-        for (int base = 0; base < total; base += 32) {
-            const int e = base + lane;
-            uint32_t k = 0;
-            const bool ok = e < total && key_at(e, k);
-            const bool lt = ok && (n_valid <= a.k || k < tau);
-            const unsigned bl = __ballot_sync(0xffffffffu, lt);
-            if (lt) {
-                const int pos = written + __popc(bl & lanemask_lt());
-                sk[pos] = k;
-                st[pos] = ties[e];
-            }
-            written += __popc(bl);
-        }
-        // ties at tau: chosen in increasing (probe rank, fastscan key, index) order
-        uint64_t floor_t = 0;
-        bool have_floor = false;
-        while (written < take) {
-            uint64_t best = ~0ull;
-            for (int e = lane; e < total; e += 32) {
-                uint32_t k;
-                if (key_at(e, k) && k == tau) {
-                    const uint64_t t = ties[e];
-                    if ((!have_floor || t > floor_t) && t < best) best = t;
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
-                best = ob < best ? ob : best;
-            }
-            if (lane == 0) {
-                sk[written] = tau;
-                st[written] = best;
-            }
-            floor_t = best;
-            have_floor = true;
-            ++written;
-        }
-    }
-    __syncwarp();
+    const int take = warp_select_topk(a.cand_key + q * a.q_stride, a.cand_tie + q * a.q_stride,
+                                      total, a.k, sk, st, hist[w]);
     // sort the selected entries by (key, tie) and write the row
     for (int i = lane; i < a.k; i += 32) {
         if (i >= take) {
@@ -2031,6 +2066,11 @@ void launch_scan(const ScanArgs& a, int grid, cudaStream_t s) {
     const size_t smem = scan_smem_bytes(a.D);
     cudaFuncSetAttribute(scan_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     scan_lists_kernel<<<grid, kScanThreads, smem, s>>>(a);
+}
+
+void launch_compact_pairs(const CompactArgs& a, cudaStream_t s) {
+    const int64_t pairs = a.nq * a.nprobe;
+    if (pairs > 0) compact_pairs_kernel<<<(unsigned)((pairs + 3) / 4), 128, 0, s>>>(a);
 }
 
 void launch_merge(const MergeArgs& a, cudaStream_t s) {
