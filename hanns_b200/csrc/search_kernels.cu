@@ -1462,9 +1462,11 @@ constexpr int kPfUnits = 3;  // rows of up to 24 code uint4 (4-bit D <= 768, 8-b
 __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ScanSmem& sm = *reinterpret_cast<ScanSmem*>(smem_raw);
-    uint32_t* lut4 = reinterpret_cast<uint32_t*>(smem_raw + sizeof(ScanSmem));  // [G*16]
+    // FastScan LUT of the current 8 queries: word pair (g*16 + nib) = (queries 0-3, 4-7),
+    // one offset-binary byte per query
+    uint2* lut8 = reinterpret_cast<uint2*>(smem_raw + sizeof(ScanSmem));  // [G*16]
     // q_i8 (dp4a layout) of the current FastScan query group, rows padded by 16 bytes
-    uint8_t* qsm = reinterpret_cast<uint8_t*>(lut4 + a.G * 16);  // [kScanWarps][D + 16]
+    uint8_t* qsm = reinterpret_cast<uint8_t*>(lut8 + a.G * 16);  // [kScanWarps][D + 16]
     const int qld = a.D + 16;
     const int tid = threadIdx.x, w = tid >> 5, lane = (int)lane_id();
     const int grp = lane >> 3, sub = lane & 7;  // 4 groups of 8 lanes per warp
@@ -1541,39 +1543,50 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
         const uint2* fsb = a.fs + a.fs_blk_off[l] * (int64_t)a.nchunks * 32;
         for (int qg = 0; qg < it.z; qg += kScanWarps) {
             const int nq_here = min(kScanWarps, it.z - qg);
-            for (int quad = 0; quad * 4 < nq_here; ++quad) {
-                // interleave 4 queries' offset-binary LUTs: word g*16+nib = q0|q1<<8|q2<<16|q3<<24
-                // (16 LUT bytes of each query per thread, 4x4 byte transposes with PRMT)
+            {
+                // interleave the 8 queries' offset-binary LUTs: word g*16+nib of quad h =
+                // q(4h)|q(4h+1)<<8|q(4h+2)<<16|q(4h+3)<<24 (16 LUT bytes of each query per
+                // thread, 4x4 byte transposes with PRMT); absent queries read 0x80 (zero)
                 for (int m = tid; m < a.G; m += kScanThreads) {
-                    uint4 L[4];
+                    uint4 L[8];
 #pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const int qq = qg + quad * 4 + t;
+                    for (int t = 0; t < 8; ++t) {
+                        const int qq = qg + t;
                         L[t] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
                         if (qq < it.z)
                             L[t] = __ldg(reinterpret_cast<const uint4*>(a.lut + (int64_t)sm.q[qq] * a.G * 16) + m);
                     }
-                    const uint32_t w0[4] = {L[0].x, L[0].y, L[0].z, L[0].w};
-                    const uint32_t w1[4] = {L[1].x, L[1].y, L[1].z, L[1].w};
-                    const uint32_t w2[4] = {L[2].x, L[2].y, L[2].z, L[2].w};
-                    const uint32_t w3[4] = {L[3].x, L[3].y, L[3].z, L[3].w};
-                    uint4* dst = reinterpret_cast<uint4*>(lut4 + m * 16);
+                    uint32_t out[2][16];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint32_t t0 = __byte_perm(w0[i], w1[i], 0x5140);
-                        const uint32_t t1 = __byte_perm(w2[i], w3[i], 0x5140);
-                        const uint32_t t2 = __byte_perm(w0[i], w1[i], 0x7362);
-                        const uint32_t t3 = __byte_perm(w2[i], w3[i], 0x7362);
-                        dst[i] = make_uint4(__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632),
-                                            __byte_perm(t2, t3, 0x5410), __byte_perm(t2, t3, 0x7632));
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t w0[4] = {L[4 * h].x, L[4 * h].y, L[4 * h].z, L[4 * h].w};
+                        const uint32_t w1[4] = {L[4 * h + 1].x, L[4 * h + 1].y, L[4 * h + 1].z, L[4 * h + 1].w};
+                        const uint32_t w2[4] = {L[4 * h + 2].x, L[4 * h + 2].y, L[4 * h + 2].z, L[4 * h + 2].w};
+                        const uint32_t w3[4] = {L[4 * h + 3].x, L[4 * h + 3].y, L[4 * h + 3].z, L[4 * h + 3].w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t t0 = __byte_perm(w0[i], w1[i], 0x5140);
+                            const uint32_t t1 = __byte_perm(w2[i], w3[i], 0x5140);
+                            const uint32_t t2 = __byte_perm(w0[i], w1[i], 0x7362);
+                            const uint32_t t3 = __byte_perm(w2[i], w3[i], 0x7362);
+                            out[h][4 * i + 0] = __byte_perm(t0, t1, 0x5410);
+                            out[h][4 * i + 1] = __byte_perm(t0, t1, 0x7632);
+                            out[h][4 * i + 2] = __byte_perm(t2, t3, 0x5410);
+                            out[h][4 * i + 3] = __byte_perm(t2, t3, 0x7632);
+                        }
                     }
+                    uint4* dst = reinterpret_cast<uint4*>(lut8 + m * 16);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        dst[i] = make_uint4(out[0][2 * i], out[1][2 * i], out[0][2 * i + 1], out[1][2 * i + 1]);
                 }
                 __syncthreads();
+                // FastScan scores of 8 queries per row: one 8-byte LUT load per nibble
                 for (int v = tid; v < n; v += kScanThreads) {
                     const int blk = v >> 5, slot = v & 31;
                     const uint2* src = fsb + (int64_t)blk * a.nchunks * 32 + slot;
-                    uint32_t acc02 = 0, acc13 = 0;
-                    int tot0 = 0, tot1 = 0, tot2 = 0, tot3 = 0;
+                    uint32_t a02 = 0, a13 = 0, b02 = 0, b13 = 0;
+                    int tot[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                     for (int c0 = 0; c0 < a.nchunks; c0 += 4) {
                         uint2 wds[4];
 #pragma unroll
@@ -1584,34 +1597,43 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                             const int c = c0 + u;
                             if (c >= a.nchunks) break;
                             const uint2 wd = wds[u];
-                            const uint32_t* lrow = lut4 + c * 256;
+                            const uint2* lrow = lut8 + c * 256;
 #pragma unroll
                             for (int j = 0; j < 16; ++j) {
                                 const uint32_t word = j < 8 ? wd.x : wd.y;
                                 const uint32_t nib = (word >> (4 * (j & 7))) & 15u;
-                                const uint32_t e = lrow[j * 16 + nib];
-                                acc02 += e & 0x00FF00FFu;
-                                acc13 += (e >> 8) & 0x00FF00FFu;
+                                const uint2 e = lrow[j * 16 + nib];
+                                a02 += e.x & 0x00FF00FFu;
+                                a13 += (e.x >> 8) & 0x00FF00FFu;
+                                b02 += e.y & 0x00FF00FFu;
+                                b13 += (e.y >> 8) & 0x00FF00FFu;
                             }
                             if ((c & 15) == 15) {
-                                tot0 += (int)(acc02 & 0xFFFFu);
-                                tot2 += (int)(acc02 >> 16);
-                                tot1 += (int)(acc13 & 0xFFFFu);
-                                tot3 += (int)(acc13 >> 16);
-                                acc02 = acc13 = 0;
+                                tot[0] += (int)(a02 & 0xFFFFu);
+                                tot[2] += (int)(a02 >> 16);
+                                tot[1] += (int)(a13 & 0xFFFFu);
+                                tot[3] += (int)(a13 >> 16);
+                                tot[4] += (int)(b02 & 0xFFFFu);
+                                tot[6] += (int)(b02 >> 16);
+                                tot[5] += (int)(b13 & 0xFFFFu);
+                                tot[7] += (int)(b13 >> 16);
+                                a02 = a13 = b02 = b13 = 0;
                             }
                         }
                     }
-                    tot0 += (int)(acc02 & 0xFFFFu);
-                    tot2 += (int)(acc02 >> 16);
-                    tot1 += (int)(acc13 & 0xFFFFu);
-                    tot3 += (int)(acc13 >> 16);
+                    tot[0] += (int)(a02 & 0xFFFFu);
+                    tot[2] += (int)(a02 >> 16);
+                    tot[1] += (int)(a13 & 0xFFFFu);
+                    tot[3] += (int)(a13 >> 16);
+                    tot[4] += (int)(b02 & 0xFFFFu);
+                    tot[6] += (int)(b02 >> 16);
+                    tot[5] += (int)(b13 & 0xFFFFu);
+                    tot[7] += (int)(b13 >> 16);
                     const int bias = 128 * a.G;
-                    int16_t* srow = my_scores_base + (int64_t)(quad * 4) * a.max_len;
-                    srow[v] = (int16_t)wrap16(tot0 - bias);
-                    srow[a.max_len + v] = (int16_t)wrap16(tot1 - bias);
-                    srow[2 * (int64_t)a.max_len + v] = (int16_t)wrap16(tot2 - bias);
-                    srow[3 * (int64_t)a.max_len + v] = (int16_t)wrap16(tot3 - bias);
+#pragma unroll
+                    for (int t = 0; t < 8; ++t)
+                        if (t < nq_here)
+                            my_scores_base[(int64_t)t * a.max_len + v] = (int16_t)wrap16(tot[t] - bias);
                 }
                 __syncthreads();
             }
@@ -2039,7 +2061,7 @@ void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist
 }
 
 size_t scan_smem_bytes(int D) {
-    return sizeof(ScanSmem) + (size_t)(D / 4) * 16 * sizeof(uint32_t) + (size_t)kScanWarps * (D + 16);
+    return sizeof(ScanSmem) + (size_t)(D / 4) * 16 * sizeof(uint2) + (size_t)kScanWarps * (D + 16);
 }
 
 int scan_grid_size(int D) {
