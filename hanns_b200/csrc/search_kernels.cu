@@ -1739,48 +1739,47 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
             __syncthreads();
             // integer rerank of the group's kept candidates, 8 per warp at a time (two per
             // group of 8 lanes, their loads issued together)
-            const int total = nq_here * a.n_cand;
-            auto entry = [&](int e, int& i, int& j, bool& act, uint32_t& v, float4& m) {
-                i = 0;
-                j = 0;
-                if (e < total) {
-                    i = e / a.n_cand;
-                    j = e - i * a.n_cand;
-                }
-                act = e < total && j < sm.nc[i];
-                v = 0;
-                m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (act) {
+            // warps per query: wpq = 8 / nq_here; warp w reranks query w / wpq, candidates
+            // j = part*8 + 0..7, part = w % wpq, stepping by wpq*8: groups of 8 lanes take
+            // j0 + grp and j0 + 4 + grp (their code loads issued together), then lanes 0-7
+            // each finish one of the 8 (distance, key store) in parallel
+            const int wpq = kScanWarps / nq_here;
+            const int iq = w / wpq, part = w - iq * wpq;
+            if (iq < nq_here) {
+                const int nc_i = sm.nc[iq];
+                const uint8_t* qrow = qsm + iq * qld;
+                const uint32_t* svi = sm.sv[iq];
+                const int64_t rb = sm.qbase[qg + iq];
+                const QueryParams& qpi = sm.qp[qg + iq];
+                auto row_of = [&](int j) -> uint32_t {
                     // kept rows: shared memory, or the ties this CTA wrote (coherent load)
-                    v = a.n_cand <= kSvMax ? sm.sv[i][j] : (uint32_t)a.cand_tie[sm.qbase[qg + i] + j];
-                    m = __ldg(a.meta + beg + v);
+                    return a.n_cand <= kSvMax ? svi[j] : (uint32_t)a.cand_tie[rb + j];
+                };
+                for (int j0 = part * 8; j0 < nc_i; j0 += wpq * 8) {
+                    const int ja = j0 + grp, jb = j0 + 4 + grp;
+                    const bool acta = ja < nc_i, actb = jb < nc_i;
+                    const uint32_t va = acta ? row_of(ja) : 0u;
+                    const uint32_t vb = actb ? row_of(jb) : 0u;
+                    const uint8_t* ca = a.codes + (beg + va) * a.code_bytes;
+                    const uint8_t* cb = a.codes + (beg + vb) * a.code_bytes;
+                    int2 ip;
+                    if (pf) {
+                        ip = int_ip_group8_pf2<kPfUnits>(ca, qrow, acta, cb, qrow, actb, a.D, a.nbits, sub);
+                    } else {
+                        ip.x = int_ip_group8(ca, qrow, a.D, a.nbits, sub, acta);
+                        ip.y = int_ip_group8(cb, qrow, a.D, a.nbits, sub, actb);
+                    }
+                    // lane L < 8 finishes candidate j0 + L (group L & 3, slot L >> 2)
+                    const int src = (lane & 3) * 8;
+                    const int ipx = __shfl_sync(0xffffffffu, ip.x, src);
+                    const int ipy = __shfl_sync(0xffffffffu, ip.y, src);
+                    const int jl = j0 + lane;
+                    if (lane < 8 && jl < nc_i) {
+                        const float4 m = __ldg(a.meta + beg + row_of(jl));
+                        a.cand_key[rb + jl] = total_order_key(
+                            rerank_distance(lane < 4 ? ipx : ipy, m, qpi, a.nbits, l2));
+                    }
                 }
-            };
-            auto finish = [&](int i, int j, bool act, float4 m, int iip) {
-                if (act && sub == 0)
-                    a.cand_key[sm.qbase[qg + i] + j] =
-                        total_order_key(rerank_distance(iip, m, sm.qp[qg + i], a.nbits, l2));
-            };
-            for (int e0 = w * 8; e0 < total; e0 += kScanWarps * 8) {
-                int ia, ja, ib, jb;
-                bool acta, actb;
-                uint32_t va, vb;
-                float4 ma, mb;
-                entry(e0 + grp, ia, ja, acta, va, ma);
-                entry(e0 + 4 + grp, ib, jb, actb, vb, mb);
-                const uint8_t* ca = a.codes + (beg + va) * a.code_bytes;
-                const uint8_t* cb = a.codes + (beg + vb) * a.code_bytes;
-                const bool na = acta && ma.w > 1e-12f, nb = actb && mb.w > 1e-12f;
-                int2 ip;
-                if (pf) {
-                    ip = int_ip_group8_pf2<kPfUnits>(ca, qsm + ia * qld, na, cb, qsm + ib * qld, nb, a.D,
-                                                     a.nbits, sub);
-                } else {
-                    ip.x = int_ip_group8(ca, qsm + ia * qld, a.D, a.nbits, sub, na);
-                    ip.y = int_ip_group8(cb, qsm + ib * qld, a.D, a.nbits, sub, nb);
-                }
-                finish(ia, ja, acta, ma, ip.x);
-                finish(ib, jb, actb, mb, ip.y);
             }
             __syncthreads();
         }
