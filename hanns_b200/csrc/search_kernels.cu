@@ -1502,38 +1502,42 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
         }
         __syncthreads();
         if (n <= a.n_cand) {
-            // no FastScan: every live row is a candidate of every query of the item;
-            // (query, row) pairs spread over the CTA's 8-lane groups
-            const int total = it.z * n;
-            for (int e0 = w * 4; e0 < total; e0 += kScanWarps * 4) {
-                const int e = e0 + grp;
-                const bool act = e < total;
-                int i = 0, v = 0;
-                if (act) {
-                    i = e / n;
-                    v = e - i * n;
+            // no FastScan: every live row is a candidate of every query of the item; blocks
+            // of 8 rows of one query spread over the warps (groups of 8 lanes take rows
+            // j0 + grp and j0 + 4 + grp), then lanes 0-7 finish the 8 rows in parallel
+            const int nbq = (n + 7) >> 3;  // row blocks per query
+            const int total = it.z * nbq;
+            for (int blk = w; blk < total; blk += kScanWarps) {
+                const int i = blk / nbq;
+                const int j0 = (blk - i * nbq) * 8;
+                const int ja = j0 + grp, jb = j0 + 4 + grp;
+                const uint8_t* qrow = a.q_i8p + (int64_t)sm.q[i] * a.D;
+                const uint8_t* ca = a.codes + (beg + min(ja, n - 1)) * a.code_bytes;
+                const uint8_t* cb = a.codes + (beg + min(jb, n - 1)) * a.code_bytes;
+                int2 ip;
+                if (pf) {
+                    ip = int_ip_group8_pf2<kPfUnits>(ca, qrow, ja < n, cb, qrow, jb < n, a.D, a.nbits, sub);
+                } else {
+                    ip.x = int_ip_group8(ca, qrow, a.D, a.nbits, sub, ja < n);
+                    ip.y = int_ip_group8(cb, qrow, a.D, a.nbits, sub, jb < n);
                 }
-                const int q = sm.q[i];
-                const int64_t row = beg + v;
-                bool dead = false;
-                float4 m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (act) {
+                const int src = (lane & 3) * 8;
+                const int ipx = __shfl_sync(0xffffffffu, ip.x, src);
+                const int ipy = __shfl_sync(0xffffffffu, ip.y, src);
+                const int v = j0 + lane;
+                if (lane < 8 && v < n) {
+                    const int64_t row = beg + v;
                     const int b = sm.bsi[i];
-                    dead = b >= 0 && bit_filtered(a.bitsets + (int64_t)b * a.bitset_words, a.bitset_len, a.ids[row]);
-                    m = __ldg(a.meta + row);
-                }
-                const uint8_t* crow = a.codes + row * a.code_bytes;
-                const uint8_t* qrow = a.q_i8p + (int64_t)q * a.D;
-                const bool need = act && !dead && m.w > 1e-12f;
-                const int iip = pf ? int_ip_group8_pf<kPfUnits>(crow, qrow, a.D, a.nbits, sub, need)
-                                   : int_ip_group8(crow, qrow, a.D, a.nbits, sub, need);
-                if (act && sub == 0) {
+                    const bool dead =
+                        b >= 0 && bit_filtered(a.bitsets + (int64_t)b * a.bitset_words, a.bitset_len, a.ids[row]);
                     const int64_t dst = sm.qbase[i] + v;
                     if (dead) {
                         a.cand_key[dst] = 0xFFFFFFFFu;
                         a.cand_tie[dst] = ~0ull;
                     } else {
-                        a.cand_key[dst] = total_order_key(rerank_distance(iip, m, sm.qp[i], a.nbits, l2));
+                        const float4 m = __ldg(a.meta + row);
+                        a.cand_key[dst] =
+                            total_order_key(rerank_distance(lane < 4 ? ipx : ipy, m, sm.qp[i], a.nbits, l2));
                         a.cand_tie[dst] = ((uint64_t)sm.rank[i] << 48) | (uint32_t)v;
                     }
                 }
