@@ -50,7 +50,7 @@ struct ScanArgs {
     int64_t q_stride;
     uint32_t* cand_key;
     uint64_t* cand_tie;
-    // FastScan scores scratch: per CTA, kScanWarps rows of max_len
+    // FastScan scores scratch: per CTA, kScanWarps rows of max_len (the longest list)
     int16_t* scores;
     int max_len;
     // items whose list has n_cand < |list| <= tc_rows belong to scan_tc_kernel (0: none)

@@ -1241,7 +1241,7 @@ struct ScanSmem {
     QueryParams qp[kScanMaxQ];
     int64_t qbase[kScanMaxQ];
     int q[kScanMaxQ], rank[kScanMaxQ], bsi[kScanMaxQ];
-    uint32_t sv[kScanWarps][kSvMax];  // kept rows of each warp's (query, list) pair
+    uint16_t sv[kScanWarps][kSvMax];  // kept rows of each warp's (query, list) pair (lists < 64 Ki rows)
     int nc[kScanWarps];               // kept candidates of each warp's pair
     int item;
     int pad[3];  // keeps the dynamic arrays after it 16-byte aligned
@@ -1318,7 +1318,7 @@ __device__ __forceinline__ int32_t wrap16(int32_t v) { return (int32_t)(int16_t)
 // sum is exact, so the split into lanes does not change it.  Groups with active ==
 // false contribute nothing and read nothing.
 __device__ __forceinline__ int int_ip_group8(const uint8_t* __restrict__ code,
-                                             const uint8_t* __restrict__ q, int D, int nbits,
+                                             const uint8_t* q, int D, int nbits,
                                              int sub, bool active) {
     int acc0 = 0, acc1 = 0;
     if (active) {
@@ -1328,7 +1328,7 @@ __device__ __forceinline__ int int_ip_group8(const uint8_t* __restrict__ code,
 #pragma unroll 2
             for (int i = sub; i < D / 16; i += 8) {
                 const uint4 c = __ldg(c4 + i);
-                const uint4 qv = __ldg(q4 + i);
+                const uint4 qv = q4[i];  // q: shared or global memory
                 acc0 = dp4a_us(c.x, qv.x, acc0);
                 acc1 = dp4a_us(c.y, qv.y, acc1);
                 acc0 = dp4a_us(c.z, qv.z, acc0);
@@ -1338,7 +1338,7 @@ __device__ __forceinline__ int int_ip_group8(const uint8_t* __restrict__ code,
 #pragma unroll 2
             for (int i = sub; i < D / 32; i += 8) {
                 const uint4 c = __ldg(c4 + i);
-                const uint4 qa = __ldg(q4 + 2 * i), qb = __ldg(q4 + 2 * i + 1);
+                const uint4 qa = q4[2 * i], qb = q4[2 * i + 1];
                 acc0 = dp4a_us(c.x & 0x0F0F0F0Fu, qa.x, acc0);
                 acc1 = dp4a_us((c.x >> 4) & 0x0F0F0F0Fu, qa.y, acc1);
                 acc0 = dp4a_us(c.y & 0x0F0F0F0Fu, qa.z, acc0);
@@ -1459,12 +1459,13 @@ __device__ __forceinline__ int2 int_ip_group8_pf2(const uint8_t* __restrict__ co
 
 constexpr int kPfUnits = 3;  // rows of up to 24 code uint4 (4-bit D <= 768, 8-bit D <= 384)
 
-__global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
+__global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ScanSmem& sm = *reinterpret_cast<ScanSmem*>(smem_raw);
     // FastScan LUT of the current 8 queries: word pair (g*16 + nib) = (queries 0-3, 4-7),
     // one offset-binary byte per query
     uint2* lut8 = reinterpret_cast<uint2*>(smem_raw + sizeof(ScanSmem));  // [G*16]
+    const bool use_sv = a.n_cand <= kSvMax && a.max_len <= 65536;
     // q_i8 (dp4a layout) of the current FastScan query group, rows padded by 16 bytes
     uint8_t* qsm = reinterpret_cast<uint8_t*>(lut8 + a.G * 16);  // [kScanWarps][D + 16]
     const int qld = a.D + 16;
@@ -1657,7 +1658,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                 const int16_t* sc = my_scores_base + (int64_t)w * a.max_len;
                 const int64_t rbase = sm.qbase[qs_];
                 uint64_t* my_tie = a.cand_tie + rbase;
-                uint32_t* my_sv = a.n_cand <= kSvMax ? sm.sv[w] : nullptr;
+                uint16_t* my_sv = use_sv ? sm.sv[w] : nullptr;
                 const uint64_t rank_bits = (uint64_t)rank << 48;
                 int n_c = 0;  // kept candidates written to my_tie
                 if (n_live > a.n_cand) {
@@ -1706,7 +1707,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                             const int pos = n_c + __popc(bk & lanemask_lt());
                             if (pos < a.n_cand) {
                                 my_tie[pos] = rank_bits | ((uint64_t)k << 32) | (uint32_t)v;
-                                if (my_sv) my_sv[pos] = (uint32_t)v;
+                                if (my_sv) my_sv[pos] = (uint16_t)v;
                             }
                         }
                         n_c += __popc(bk);
@@ -1720,7 +1721,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
                         if (keep) {
                             const int pos = n_c + __popc(bk & lanemask_lt());
                             my_tie[pos] = rank_bits | (uint32_t)v;
-                            if (my_sv) my_sv[pos] = (uint32_t)v;
+                            if (my_sv) my_sv[pos] = (uint16_t)v;
                         }
                         n_c += __popc(bk);
                     }
@@ -1752,12 +1753,12 @@ __global__ void __launch_bounds__(kScanThreads) scan_lists_kernel(ScanArgs a) {
             if (iq < nq_here) {
                 const int nc_i = sm.nc[iq];
                 const uint8_t* qrow = qsm + iq * qld;
-                const uint32_t* svi = sm.sv[iq];
+                const uint16_t* svi = sm.sv[iq];
                 const int64_t rb = sm.qbase[qg + iq];
                 const QueryParams& qpi = sm.qp[qg + iq];
                 auto row_of = [&](int j) -> uint32_t {
                     // kept rows: shared memory, or the ties this CTA wrote (coherent load)
-                    return a.n_cand <= kSvMax ? svi[j] : (uint32_t)a.cand_tie[rb + j];
+                    return use_sv ? (uint32_t)svi[j] : (uint32_t)a.cand_tie[rb + j];
                 };
                 for (int j0 = part * 8; j0 < nc_i; j0 += wpq * 8) {
                     const int ja = j0 + grp, jb = j0 + 4 + grp;

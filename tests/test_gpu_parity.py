@@ -121,9 +121,11 @@ def test_knowhere_c_abi_search(gpu):
 
 
 @pytest.mark.parametrize("nbits,metric,k,d", [(4, 0, 10, 128), (8, 1, 10, 200), (4, 1, 50, 64),
-                                              (8, 0, 100, 96)])
+                                              (8, 0, 100, 96), (4, 1, 10, 1100), (8, 0, 10, 520)])
 def test_search_bit_exact_larger(gpu, oracle_mod, nbits, metric, k, d):
-    """Oracle-built artifacts with 20k rows: FastScan lists, k up to 100."""
+    """Oracle-built artifacts with 20k rows: FastScan lists, k up to 100; d = 520 (8-bit,
+    padded 576) and d = 1100 (padded 1152) take the rerank without the prefetched code
+    registers (query rows in shared memory)."""
     from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
     from tests.golden.make_golden import mixture
     O = oracle_mod
