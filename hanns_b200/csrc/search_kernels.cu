@@ -1669,7 +1669,7 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                         return true;
                     };
                     int c_gt = 0;
-                    const uint32_t tau = warp_radix_kth(n, a.n_cand, key_at, sm.hist[w], &c_gt);
+                    const uint32_t tau = warp_radix_kth16(n, a.n_cand, key_at, sm.hist[w], &c_gt);
                     // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
                     int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = 0;
                     for (int base = 0; base < n; base += 32) {

@@ -116,4 +116,51 @@ __device__ uint32_t warp_radix_kth(int n, int kth, KeyAt key_at, uint32_t* hist,
     return kmin + prefix;
 }
 
+// warp_radix_kth for keys known to lie in [0, 65535] (16-bit FastScan keys): two 8-bit
+// passes, no range pass.  Same contract as warp_radix_kth.
+template <typename KeyAt>
+__device__ uint32_t warp_radix_kth16(int n, int kth, KeyAt key_at, uint32_t* hist, int* n_less) {
+    const int lane = (int)lane_id();
+    uint32_t prefix = 0;
+    int remaining = kth, less = 0;
+    for (int shift = 8; shift >= 0; shift -= 8) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) hist[lane * 8 + b] = 0;
+        __syncwarp();
+        for (int i = lane; i < n; i += 32) {
+            uint32_t key;
+            if (key_at(i, key) && (shift == 8 || (key >> 8) == (prefix >> 8)))
+                atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        int s = 0;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) s += (int)hist[lane * 8 + b];
+        const int incl = warp_inclusive_scan(s);
+        const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
+        const int src = __ffs(hit) - 1;  // hit != 0 because remaining <= total
+        int bin = 0, before = 0;
+        if (lane == src) {
+            int c = incl - s;
+            for (int b = 0; b < 8; ++b) {
+                const int h = (int)hist[lane * 8 + b];
+                if (c + h >= remaining) {
+                    bin = lane * 8 + b;
+                    break;
+                }
+                c += h;
+            }
+            before = c;
+        }
+        bin = __shfl_sync(0xffffffffu, bin, src);
+        before = __shfl_sync(0xffffffffu, before, src);
+        less += before;
+        remaining -= before;
+        prefix |= (uint32_t)bin << shift;
+        __syncwarp();
+    }
+    *n_less = less;
+    return prefix;
+}
+
 }  // namespace hanns
