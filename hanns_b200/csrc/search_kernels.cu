@@ -1791,6 +1791,116 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
     }
 }
 
+// warp_select_topk for at most 32 * S entries: the keys are read once into registers and
+// the radix passes run on them (same result and contract).
+template <int S>
+__device__ int warp_select_topk_small(const uint32_t* keys, const uint64_t* ties, int total, int k,
+                                      uint32_t* sk, uint64_t* st, uint32_t* hist) {
+    const int lane = (int)lane_id();
+    uint32_t kk[S];
+    bool ok[S];
+    int cnt = 0;
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+        const int e = lane + 32 * j;
+        ok[j] = e < total && ties[e] != ~0ull;
+        kk[j] = ok[j] ? keys[e] : 0xFFFFFFFFu;
+        if (ok[j]) {
+            ++cnt;
+            kmin = min(kmin, kk[j]);
+            kmax = max(kmax, kk[j]);
+        }
+    }
+    const int n_valid = warp_sum(cnt);
+    const int take = min(k, n_valid);
+    if (take == 0) return 0;
+    uint32_t tau = 0xFFFFFFFFu;
+    if (n_valid > k) {
+        kmin = warp_min_u32(kmin);
+        kmax = warp_max_u32(kmax);
+        const uint32_t range = kmax - kmin;
+        uint32_t prefix = 0;
+        int remaining = k;
+        for (int hi = 32 - __clz(range); hi > 0; hi -= 8) {
+            const int shift = hi > 8 ? hi - 8 : 0;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) hist[lane * 8 + b] = 0;
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < S; ++j)
+                if (ok[j]) {
+                    const uint32_t kp = kk[j] - kmin;
+                    if (hi >= 32 || ((kp ^ prefix) >> hi) == 0) atomicAdd(&hist[(kp >> shift) & 255u], 1u);
+                }
+            __syncwarp();
+            int sum = 0;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) sum += (int)hist[lane * 8 + b];
+            const int incl = warp_inclusive_scan(sum);
+            const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
+            const int src = __ffs(hit) - 1;
+            int bin = 0, before = 0;
+            if (lane == src) {
+                int c = incl - sum;
+                for (int b = 0; b < 8; ++b) {
+                    const int h = (int)hist[lane * 8 + b];
+                    if (c + h >= remaining) {
+                        bin = lane * 8 + b;
+                        break;
+                    }
+                    c += h;
+                }
+                before = c;
+            }
+            bin = __shfl_sync(0xffffffffu, bin, src);
+            before = __shfl_sync(0xffffffffu, before, src);
+            remaining -= before;
+            prefix |= (uint32_t)bin << shift;
+            __syncwarp();
+        }
+        tau = kmin + prefix;
+    }
+    int written = 0;
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+        const bool lt = ok[j] && (n_valid <= k || kk[j] < tau);
+        const unsigned bl = __ballot_sync(0xffffffffu, lt);
+        if (lt) {
+            const int pos = written + __popc(bl & lanemask_lt());
+            sk[pos] = kk[j];
+            st[pos] = ties[lane + 32 * j];
+        }
+        written += __popc(bl);
+    }
+    // ties at tau: chosen in increasing (probe rank, fastscan key, index) order
+    uint64_t floor_t = 0;
+    bool have_floor = false;
+    while (written < take) {
+        uint64_t best = ~0ull;
+#pragma unroll
+        for (int j = 0; j < S; ++j)
+            if (ok[j] && kk[j] == tau) {
+                const uint64_t t = ties[lane + 32 * j];
+                if ((!have_floor || t > floor_t) && t < best) best = t;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+            best = ob < best ? ob : best;
+        }
+        if (lane == 0) {
+            sk[written] = tau;
+            st[written] = best;
+        }
+        floor_t = best;
+        have_floor = true;
+        ++written;
+    }
+    __syncwarp();
+    return take;
+}
+
 // Per (query, probe) pair (one warp): the k best of the pair's kept candidates, into a
 // fixed slot of k entries (rank * k) of the query's compact region; unused entries get
 // key ~0u and tie ~0ull.  The top-k of a query over the union of its pairs' top-k equals
@@ -1807,9 +1917,12 @@ __global__ void __launch_bounds__(128) compact_pairs_kernel(CompactArgs a) {
     const int total = po[r + 1] - po[r];
     uint32_t* ok = a.out_key + pr * a.k;
     uint64_t* ot = a.out_tie + pr * a.k;
-    const int take = total > 0 ? warp_select_topk(a.cand_key + base, a.cand_tie + base, total, a.k,
-                                                  ok, ot, hist[w])
-                               : 0;
+    int take = 0;
+    if (total > 0 && total <= 32 * 8)
+        take = warp_select_topk_small<8>(a.cand_key + base, a.cand_tie + base, total, a.k, ok, ot,
+                                         hist[w]);
+    else if (total > 0)
+        take = warp_select_topk(a.cand_key + base, a.cand_tie + base, total, a.k, ok, ot, hist[w]);
     for (int i = take + lane; i < a.k; i += 32) {
         ok[i] = 0xFFFFFFFFu;
         ot[i] = ~0ull;
