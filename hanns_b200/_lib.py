@@ -137,6 +137,7 @@ SIGNATURES = [
     ("hanns_gpu_merge_shards_device", C.c_int32,
      [vp, vp, vp, C.c_int32, C.c_int64, C.c_int32, vp, vp, vp]),
     ("hanns_gpu_ivf_usq_query_state_bytes", C.c_int32, [vp, C.c_int32, i64p]),
+    ("hanns_gpu_ivf_usq_rerank_rows_device", C.c_int32, [vp, vp, C.c_int64, vp, C.c_int32, vp, vp]),
     ("hanns_gpu_ivf_usq_prepare_device", C.c_int32,
      [vp, vp, C.c_int64, C.c_int32, vp, vp, vp, vp, vp, vp]),
     ("hanns_gpu_ivf_usq_search_prepared_shard_device", C.c_int32,

@@ -698,6 +698,17 @@ int32_t hanns_gpu_ivf_usq_prepare_device(HannsIvfUsqHandle* h, const float* d_qu
     });
 }
 
+int32_t hanns_gpu_ivf_usq_rerank_rows_device(HannsIvfUsqHandle* h, const float* d_queries,
+                                              int64_t nq, const int64_t* d_rows, int32_t m,
+                                              float* d_dists, void* stream) {
+    if (!h || !d_queries || nq <= 0 || !d_rows || m <= 0 || !d_dists) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        h->idx->rerank_rows_device(d_queries, nq, d_rows, m, d_dists,
+                                   static_cast<cudaStream_t>(stream));
+    });
+}
+
 int32_t hanns_gpu_ivf_usq_search_prepared_shard_device(
     HannsIvfUsqHandle* h, int64_t nq, int32_t k, int32_t nprobe, const void* d_probes,
     const void* d_qp, const void* d_lut, const void* d_qi8p, const void* d_qi8n, float* d_dists,

@@ -949,6 +949,42 @@ int IvfUsqGpu::stage_ms(int n_calls, float* out, int* counts) {
     return covered;
 }
 
+void IvfUsqGpu::rerank_rows_device(const float* d_queries, int64_t nq, const int64_t* d_rows,
+                                   int m, float* d_dists, cudaStream_t stream) {
+    DeviceGuard g(device_);
+    if (!trained_) throw std::invalid_argument("index not trained");
+    check_supported();
+    if (nq <= 0 || m <= 0) throw std::invalid_argument("empty rerank request");
+    cudaStream_t s = stream ? stream : stream_;
+    const int G = D_ / 4;
+    w_qrot_.reserve((size_t)nq * D_);
+    w_qp_.reserve(nq);
+    w_qi8p_.reserve((size_t)nq * D_);
+    w_qi8n_.reserve((size_t)nq * D_);
+    w_lut_.reserve((size_t)nq * G * 16);
+    launch_rotate(d_queries, nq, dim_, D_, Pc_.p, w_qrot_.p, s);
+    launch_query_state(d_queries, w_qrot_.p, nq, dim_, D_, rc_.p, nbits_, w_qp_.p, w_qi8p_.p,
+                       w_qi8n_.p, w_lut_.p, s);
+    RerankRowsArgs a{};
+    a.D = D_;
+    a.nbits = nbits_;
+    a.code_bytes = code_bytes_;
+    a.metric_l2 = metric_ == 0 ? 1 : 0;
+    a.codes = codes_.p;
+    a.meta = meta_.p;
+    a.ntotal = ntotal_;
+    a.qp = w_qp_.p;
+    a.q_i8p = w_qi8p_.p;
+    a.rows = d_rows;
+    a.nq = nq;
+    a.m = m;
+    a.out = d_dists;
+    launch_rerank_rows(a, s);
+    HANNS_CUDA_OK(cudaGetLastError());
+    last_launches_ = 3;
+    if (!stream) HANNS_CUDA_OK(cudaStreamSynchronize(s));
+}
+
 void IvfUsqGpu::prepare_device(const float* d_queries, int64_t nq, int nprobe, QueryState st,
                                cudaStream_t stream) {
     DeviceGuard g(device_);

@@ -99,6 +99,10 @@ class IvfUsqGpu {
                         cudaStream_t stream);
     // Grouping, list scan and merge over query state made by prepare_device (of this index
     // or of another shard of it); synchronises the stream.
+    // USQ distances of caller-chosen stored rows (storage order) for nq device queries:
+    // query state (rotation, q_i8, scalars) then the integer rerank and score epilogue.
+    void rerank_rows_device(const float* d_queries, int64_t nq, const int64_t* d_rows, int m,
+                            float* d_dists, cudaStream_t stream);
     void search_prepared_device(int64_t nq, const SearchOptions& opt, QueryState st,
                                 int64_t* d_ids, float* d_dists, int64_t* d_counts,
                                 uint64_t* d_keys, cudaStream_t stream);

@@ -83,6 +83,22 @@ struct TcScanArgs {
     int* err_flag;          // set to 4 when a bounded wait expired
 };
 
+// USQ rerank of caller-chosen stored rows: out[q * m + j] = distance of row rows[q*m+j]
+// (+inf for rows outside [0, ntotal)).
+struct RerankRowsArgs {
+    int D, nbits, code_bytes, metric_l2;
+    const uint8_t* codes;
+    const float4* meta;
+    int64_t ntotal;
+    const QueryParams* qp;
+    const uint8_t* q_i8p;
+    const int64_t* rows;
+    int64_t nq;
+    int m;
+    float* out;
+};
+void launch_rerank_rows(const RerankRowsArgs& a, cudaStream_t s);
+
 // Per (query, probe) pair top-k of the scan's candidate regions into a compact region
 // of nprobe * k entries per query (slot rank * k).
 struct CompactArgs {

@@ -1340,17 +1340,18 @@ __device__ __forceinline__ int int_ip_group8(const uint8_t* __restrict__ code,
                 const uint4 c = __ldg(c4 + i);
                 const uint4 qa = q4[2 * i], qb = q4[2 * i + 1];
                 acc0 = dp4a_us(c.x & 0x0F0F0F0Fu, qa.x, acc0);
-                acc1 = dp4a_us((c.x >> 4) & 0x0F0F0F0Fu, qa.y, acc1);
+                acc1 = dp4a_us(c.x & 0xF0F0F0F0u, qa.y, acc1);
                 acc0 = dp4a_us(c.y & 0x0F0F0F0Fu, qa.z, acc0);
-                acc1 = dp4a_us((c.y >> 4) & 0x0F0F0F0Fu, qa.w, acc1);
+                acc1 = dp4a_us(c.y & 0xF0F0F0F0u, qa.w, acc1);
                 acc0 = dp4a_us(c.z & 0x0F0F0F0Fu, qb.x, acc0);
-                acc1 = dp4a_us((c.z >> 4) & 0x0F0F0F0Fu, qb.y, acc1);
+                acc1 = dp4a_us(c.z & 0xF0F0F0F0u, qb.y, acc1);
                 acc0 = dp4a_us(c.w & 0x0F0F0F0Fu, qb.z, acc0);
-                acc1 = dp4a_us((c.w >> 4) & 0x0F0F0F0Fu, qb.w, acc1);
+                acc1 = dp4a_us(c.w & 0xF0F0F0F0u, qb.w, acc1);
             }
         }
     }
-    int acc = acc0 + acc1;
+    // 4-bit: acc1 summed the high nibbles in place (16 x their value), an exact multiple of 16
+    int acc = acc0 + (nbits == 8 ? acc1 : acc1 >> 4);
     acc += __shfl_xor_sync(0xffffffffu, acc, 4);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
@@ -1388,17 +1389,18 @@ __device__ __forceinline__ int int_ip_group8_pf(const uint8_t* __restrict__ code
             } else {
                 const uint4 qa = q4[2 * i], qb = q4[2 * i + 1];
                 acc0 = dp4a_us(c[u].x & 0x0F0F0F0Fu, qa.x, acc0);
-                acc1 = dp4a_us((c[u].x >> 4) & 0x0F0F0F0Fu, qa.y, acc1);
+                acc1 = dp4a_us(c[u].x & 0xF0F0F0F0u, qa.y, acc1);
                 acc0 = dp4a_us(c[u].y & 0x0F0F0F0Fu, qa.z, acc0);
-                acc1 = dp4a_us((c[u].y >> 4) & 0x0F0F0F0Fu, qa.w, acc1);
+                acc1 = dp4a_us(c[u].y & 0xF0F0F0F0u, qa.w, acc1);
                 acc0 = dp4a_us(c[u].z & 0x0F0F0F0Fu, qb.x, acc0);
-                acc1 = dp4a_us((c[u].z >> 4) & 0x0F0F0F0Fu, qb.y, acc1);
+                acc1 = dp4a_us(c[u].z & 0xF0F0F0F0u, qb.y, acc1);
                 acc0 = dp4a_us(c[u].w & 0x0F0F0F0Fu, qb.z, acc0);
-                acc1 = dp4a_us((c[u].w >> 4) & 0x0F0F0F0Fu, qb.w, acc1);
+                acc1 = dp4a_us(c[u].w & 0xF0F0F0F0u, qb.w, acc1);
             }
         }
     }
-    int acc = acc0 + acc1;
+    // 4-bit: acc1 summed the high nibbles in place (16 x their value), an exact multiple of 16
+    int acc = acc0 + (nbits == 8 ? acc1 : acc1 >> 4);
     acc += __shfl_xor_sync(0xffffffffu, acc, 4);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
@@ -1436,17 +1438,17 @@ __device__ __forceinline__ int2 int_ip_group8_pf2(const uint8_t* __restrict__ co
                 } else {
                     const uint4 q0 = q4[2 * i], q1 = q4[2 * i + 1];
                     acc0 = dp4a_us(c[u].x & 0x0F0F0F0Fu, q0.x, acc0);
-                    acc1 = dp4a_us((c[u].x >> 4) & 0x0F0F0F0Fu, q0.y, acc1);
+                    acc1 = dp4a_us(c[u].x & 0xF0F0F0F0u, q0.y, acc1);
                     acc0 = dp4a_us(c[u].y & 0x0F0F0F0Fu, q0.z, acc0);
-                    acc1 = dp4a_us((c[u].y >> 4) & 0x0F0F0F0Fu, q0.w, acc1);
+                    acc1 = dp4a_us(c[u].y & 0xF0F0F0F0u, q0.w, acc1);
                     acc0 = dp4a_us(c[u].z & 0x0F0F0F0Fu, q1.x, acc0);
-                    acc1 = dp4a_us((c[u].z >> 4) & 0x0F0F0F0Fu, q1.y, acc1);
+                    acc1 = dp4a_us(c[u].z & 0xF0F0F0F0u, q1.y, acc1);
                     acc0 = dp4a_us(c[u].w & 0x0F0F0F0Fu, q1.z, acc0);
-                    acc1 = dp4a_us((c[u].w >> 4) & 0x0F0F0F0Fu, q1.w, acc1);
+                    acc1 = dp4a_us(c[u].w & 0xF0F0F0F0u, q1.w, acc1);
                 }
             }
         }
-        return acc0 + acc1;
+        return acc0 + (nbits == 8 ? acc1 : acc1 >> 4);  // 4-bit: high nibbles in place
     };
     int x = dot(ca, qa_, act_a), y = dot(cb, qb_, act_b);
 #pragma unroll
@@ -1901,6 +1903,31 @@ __device__ int warp_select_topk_small(const uint32_t* keys, const uint64_t* ties
     return take;
 }
 
+// USQ rerank of caller-chosen stored rows (the reference's score_with_meta + distance,
+// quantizer.rs:274-288,382-400, ivf_usq.rs:581-586): pair p = (query p / m, row
+// rows[p]) per group of 8 lanes; rows outside [0, ntotal) give +inf.
+__global__ void __launch_bounds__(256) rerank_rows_kernel(RerankRowsArgs a) {
+    const int lane = (int)lane_id(), grp = lane >> 3, sub = lane & 7;
+    const int64_t total = a.nq * a.m;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t p0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4; p0 < total;
+         p0 += warps * 4) {
+        const int64_t p = p0 + grp;
+        int64_t row = -1;
+        int64_t q = 0;
+        if (p < total) {
+            q = p / a.m;
+            row = a.rows[p];
+        }
+        const bool act = row >= 0 && row < a.ntotal;
+        const uint8_t* code = a.codes + (act ? row : 0) * a.code_bytes;
+        const int iip = int_ip_group8(code, a.q_i8p + q * a.D, a.D, a.nbits, sub, act);
+        if (p < total && sub == 0)
+            a.out[p] = act ? rerank_distance(iip, a.meta[row], a.qp[q], a.nbits, a.metric_l2 != 0)
+                           : __int_as_float(0x7f800000);
+    }
+}
+
 // Per (query, probe) pair (one warp): the k best of the pair's kept candidates, into a
 // fixed slot of k entries (rank * k) of the query's compact region; unused entries get
 // key ~0u and tie ~0ull.  The top-k of a query over the union of its pairs' top-k equals
@@ -2205,6 +2232,13 @@ void launch_scan(const ScanArgs& a, int grid, cudaStream_t s) {
     const size_t smem = scan_smem_bytes(a.D);
     cudaFuncSetAttribute(scan_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     scan_lists_kernel<<<grid, kScanThreads, smem, s>>>(a);
+}
+
+void launch_rerank_rows(const RerankRowsArgs& a, cudaStream_t s) {
+    const int64_t groups = a.nq * a.m;
+    if (groups <= 0) return;
+    const int64_t blocks = std::min<int64_t>((groups + 31) / 32, 148 * 16);
+    rerank_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(a);
 }
 
 void launch_compact_pairs(const CompactArgs& a, cudaStream_t s) {

@@ -241,6 +241,21 @@ class IvfUsqIndex:
             n_bitsets, d_query_bitset or None, d_ids, d_dists, d_counts or None, stream or None),
             "search_device")
 
+    def rerank_rows(self, queries: np.ndarray, rows: np.ndarray) -> np.ndarray:
+        """USQ distances of stored rows (storage order, as export_artifact lists them):
+        rows[q, j] for query q; rows outside [0, count) give +inf.  The score_with_meta
+        rerank the reference's graph indexes reuse (faiss/hnsw_pca_usq.rs:55-63)."""
+        import torch
+        q = np.ascontiguousarray(queries, np.float32).reshape(-1, self.config.dim)
+        r = np.ascontiguousarray(rows, np.int64).reshape(q.shape[0], -1)
+        dq = torch.from_numpy(q).to(f"cuda:{self.device}")
+        dr = torch.from_numpy(r).to(f"cuda:{self.device}")
+        out = torch.empty(r.shape, dtype=torch.float32, device=dq.device)
+        _check(L.lib().hanns_gpu_ivf_usq_rerank_rows_device(self._h, dq.data_ptr(), q.shape[0],
+                                                            dr.data_ptr(), r.shape[1],
+                                                            out.data_ptr(), None), "rerank_rows")
+        return out.cpu().numpy()
+
     STAGES = ("coarse_gemm", "coarse_select", "rotate", "query_state", "group", "scan", "merge",
               "total")
 

@@ -301,6 +301,17 @@ int32_t hanns_gpu_ivf_usq_search_prepared_shard_device(
     HannsIvfUsqHandle* h, int64_t nq, int32_t k, int32_t nprobe, const void* d_probes,
     const void* d_qp, const void* d_lut, const void* d_qi8p, const void* d_qi8n, float* d_dists,
     uint64_t* d_keys, int64_t* d_ids, void* stream);
+/* Batched USQ rerank of caller-chosen stored rows: for each of nq device queries and each
+ * of its m rows (d_rows[q*m + j], positions in the index's storage order as exported;
+ * rows outside [0, count) give +inf), the distance the search computes for that row --
+ * query state (quantizer.rs:236-270), integer inner product and score_with_meta
+ * (quantizer.rs:274-288, 382-400), L2 / IP distance (ivf_usq.rs:581-586).  The arithmetic
+ * the reference reuses in HNSW-HVQ (faiss/hnsw_hvq.rs:601), HNSW-PCA-USQ
+ * (faiss/hnsw_pca_usq.rs:55-63) and DiskANN-PCA-USQ (faiss/diskann_pca_usq.rs:77-85) to
+ * rerank graph candidates.  Stream-ordered like hanns_gpu_ivf_usq_search_device. */
+int32_t hanns_gpu_ivf_usq_rerank_rows_device(HannsIvfUsqHandle* h, const float* d_queries,
+                                              int64_t nq, const int64_t* d_rows, int32_t m,
+                                              float* d_dists, void* stream);
 /* The list -> rank owner map that hanns_gpu_ivf_usq_shard uses (host only, no GPU):
  * longest-processing-time on |L|^2 (scan work ~ list size x probes of the list), lists
  * by decreasing weight, each to the least-loaded rank. */

@@ -252,6 +252,34 @@ def test_stream_ordered_device_search(gpu, oracle_mod):
     assert tot[5] > 0 and tot[7] >= tot[5]
 
 
+@pytest.mark.parametrize("path", FIXTURES[:3], ids=IDS[:3])
+def test_rerank_rows_equals_candidate_distances(gpu, oracle_mod, path):
+    """hanns_gpu_ivf_usq_rerank_rows_device on the rows the oracle reranks for each query
+    gives the oracle's candidate distances bit for bit; rows outside the index give +inf."""
+    from hanns_b200.ivf_usq import IvfUsqIndex
+    O = oracle_mod
+    art, z = load(path)
+    oi = O.OracleIndex(art)
+    idx = IvfUsqIndex.from_artifact(art)
+    off = np.asarray(art["list_offsets"], np.int64)
+    qs = z["queries"][:12]
+    rows, exp = [], []
+    for qv in qs:
+        c = oi.candidates(qv, int(z["k"]), int(z["nprobe"]))
+        r = off[np.asarray(c["list"], np.int64)] + np.asarray(c["local"], np.int64)
+        rows.append(r[:40])
+        exp.append(np.asarray(c["dist"], np.float32)[:40])
+    m = max(len(r) for r in rows) + 2
+    R = np.full((len(qs), m), -1, np.int64)
+    E = np.full((len(qs), m), np.inf, np.float32)
+    for i, (r, e) in enumerate(zip(rows, exp)):
+        R[i, :len(r)] = r
+        E[i, :len(e)] = e
+    R[:, -1] = len(art["ids"]) + 5  # beyond the index
+    got = idx.rerank_rows(qs, R)
+    assert bits_eq(got, E)
+
+
 def test_empty_and_tiny_index(gpu, oracle_mod):
     """Lists of 0, 1, 31, 32, 33 rows; k larger than everything probed."""
     from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
