@@ -1610,10 +1610,12 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                                 const uint32_t word = j < 8 ? wd.x : wd.y;
                                 const uint32_t nib = (word >> (4 * (j & 7))) & 15u;
                                 const uint2 e = lrow[j * 16 + nib];
+                                // bytes 0, 2 and bytes 1, 3 of each word into 16-bit lanes
+                                // (one PRMT with a zero source for the odd bytes)
                                 a02 += e.x & 0x00FF00FFu;
-                                a13 += (e.x >> 8) & 0x00FF00FFu;
+                                a13 += __byte_perm(e.x, 0u, 0x4341);
                                 b02 += e.y & 0x00FF00FFu;
-                                b13 += (e.y >> 8) & 0x00FF00FFu;
+                                b13 += __byte_perm(e.y, 0u, 0x4341);
                             }
                             if ((c & 15) == 15) {
                                 tot[0] += (int)(a02 & 0xFFFFu);
