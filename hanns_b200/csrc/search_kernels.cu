@@ -1608,8 +1608,11 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
 #pragma unroll
                             for (int j = 0; j < 16; ++j) {
                                 const uint32_t word = j < 8 ? wd.x : wd.y;
-                                const uint32_t nib = (word >> (4 * (j & 7))) & 15u;
-                                const uint2 e = lrow[j * 16 + nib];
+                                const int sh = 4 * (j & 7);
+                                // byte offset of entry (j, nibble) in the 16-entry row
+                                const uint32_t off = (sh == 0 ? word << 3 : word >> (sh - 3)) & 0x78u;
+                                const uint2 e = *reinterpret_cast<const uint2*>(
+                                    reinterpret_cast<const char*>(lrow + j * 16) + off);
                                 // bytes 0, 2 and bytes 1, 3 of each word into 16-bit lanes
                                 // (one PRMT with a zero source for the odd bytes)
                                 a02 += e.x & 0x00FF00FFu;
