@@ -32,7 +32,7 @@ namespace {
 constexpr size_t kStaticScratchBytes = 16u << 20;
 constexpr int kMaxDevices = 64;
 
-__device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {};

@@ -1466,7 +1466,11 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
     ScanSmem& sm = *reinterpret_cast<ScanSmem*>(smem_raw);
     // FastScan LUT of the current 8 queries: word pair (g*16 + nib) = (queries 0-3, 4-7),
     // one offset-binary byte per query
-    uint2* lut8 = reinterpret_cast<uint2*>(smem_raw + sizeof(ScanSmem));  // [G*16]
+    // (128-byte aligned, so a LUT row base OR a nibble's byte offset is its address)
+    const uint32_t smem_base = (uint32_t)__cvta_generic_to_shared(smem_raw);
+    const uint32_t lut_pad = (128u - ((smem_base + (uint32_t)sizeof(ScanSmem)) & 127u)) & 127u;
+    uint2* lut8 = reinterpret_cast<uint2*>(smem_raw + sizeof(ScanSmem) + lut_pad);  // [G*16]
+    const uint32_t lut8_s = smem_base + (uint32_t)sizeof(ScanSmem) + lut_pad;
     const bool use_sv = a.n_cand <= kSvMax && a.max_len <= 65536;
     // q_i8 (dp4a layout) of the current FastScan query group, rows padded by 16 bytes
     uint8_t* qsm = reinterpret_cast<uint8_t*>(lut8 + a.G * 16);  // [kScanWarps][D + 16]
@@ -1604,22 +1608,29 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                             const int c = c0 + u;
                             if (c >= a.nchunks) break;
                             const uint2 wd = wds[u];
-                            const uint2* lrow = lut8 + c * 256;
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) {
-                                const uint32_t word = j < 8 ? wd.x : wd.y;
-                                const int sh = 4 * (j & 7);
-                                // byte offset of entry (j, nibble) in the 16-entry row
-                                const uint32_t off = (sh == 0 ? word << 3 : word >> (sh - 3)) & 0x78u;
-                                const uint2 e = *reinterpret_cast<const uint2*>(
-                                    reinterpret_cast<const char*>(lrow + j * 16) + off);
-                                // bytes 0, 2 and bytes 1, 3 of each word into 16-bit lanes
-                                // (one PRMT with a zero source for the odd bytes)
-                                a02 += e.x & 0x00FF00FFu;
-                                a13 += __byte_perm(e.x, 0u, 0x4341);
-                                b02 += e.y & 0x00FF00FFu;
-                                b13 += __byte_perm(e.y, 0u, 0x4341);
-                            }
+                            const uint32_t lrow_s = lut8_s + (uint32_t)c * 2048u;  // 128-aligned
+                            // nibble J: shared address = row base | nibble * 8, plus the entry
+                            // block J * 128 as the load's immediate; bytes 0, 2 and bytes 1, 3
+                            // of each word go into 16-bit lanes (one PRMT with a zero source)
+#define HANNS_FS_NIBBLE(J)                                                                     \
+    {                                                                                          \
+        const uint32_t word_ = (J) < 8 ? wd.x : wd.y;                                          \
+        const int sh_ = 4 * ((J) & 7);                                                         \
+        const uint32_t addr_ = ((sh_ == 0 ? word_ << 3 : word_ >> (sh_ - 3)) & 0x78u) | lrow_s; \
+        uint32_t ex_, ey_;                                                                     \
+        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2+%3];"                                     \
+                     : "=r"(ex_), "=r"(ey_)                                                    \
+                     : "r"(addr_), "n"((J) * 128));                                            \
+        a02 += ex_ & 0x00FF00FFu;                                                              \
+        a13 += __byte_perm(ex_, 0u, 0x4341);                                                   \
+        b02 += ey_ & 0x00FF00FFu;                                                              \
+        b13 += __byte_perm(ey_, 0u, 0x4341);                                                   \
+    }
+                            HANNS_FS_NIBBLE(0) HANNS_FS_NIBBLE(1) HANNS_FS_NIBBLE(2) HANNS_FS_NIBBLE(3)
+                            HANNS_FS_NIBBLE(4) HANNS_FS_NIBBLE(5) HANNS_FS_NIBBLE(6) HANNS_FS_NIBBLE(7)
+                            HANNS_FS_NIBBLE(8) HANNS_FS_NIBBLE(9) HANNS_FS_NIBBLE(10) HANNS_FS_NIBBLE(11)
+                            HANNS_FS_NIBBLE(12) HANNS_FS_NIBBLE(13) HANNS_FS_NIBBLE(14) HANNS_FS_NIBBLE(15)
+#undef HANNS_FS_NIBBLE
                             if ((c & 15) == 15) {
                                 tot[0] += (int)(a02 & 0xFFFFu);
                                 tot[2] += (int)(a02 >> 16);
@@ -2210,7 +2221,7 @@ void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist
 }
 
 size_t scan_smem_bytes(int D) {
-    return sizeof(ScanSmem) + (size_t)(D / 4) * 16 * sizeof(uint2) + (size_t)kScanWarps * (D + 16);
+    return sizeof(ScanSmem) + 128 + (size_t)(D / 4) * 16 * sizeof(uint2) + (size_t)kScanWarps * (D + 16);
 }
 
 int scan_grid_size(int D) {

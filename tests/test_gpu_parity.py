@@ -445,3 +445,64 @@ def test_query_split_shards_equal_single_gpu(gpu, oracle_mod):
                                            out_i.data_ptr(), out_d.data_ptr(), None) == 0
     assert np.array_equal(out_i.cpu().numpy(), exp.ids.reshape(nq, k))
     assert bits_eq(out_d.cpu().numpy(), exp.distances.reshape(nq, k))
+
+
+def _gpu_built(d, nlist, nbits, metric, n, comps, sigma, seed):
+    from hanns_b200.ivf_usq import IvfUsqConfig, IvfUsqIndex
+    from tests.golden.make_golden import mixture
+    rng = np.random.default_rng(seed)
+    x, _ = mixture(rng, n, d, comps, sigma, metric == 1)
+    idx = IvfUsqIndex(IvfUsqConfig(d, nlist, nbits, metric_type=metric, rotation_seed=seed))
+    idx.train(x, kmeans_iters=6, kmeans_seed=seed)
+    idx.add(x)
+    return idx, rng
+
+
+def test_config_8bit_k100_deletion_bitsets(gpu, oracle_mod):
+    """The shape of the 8-bit configuration: 8-bit codes, inner product, d = 768, k = 100,
+    10 % of the queries with a deletion bitset masking ids with probability 0.2; fused
+    and reference post filtering equal the oracle on the GPU-built index."""
+    from hanns_b200.ivf_usq import FILTER_FUSED, FILTER_POST, SearchRequest
+    from tests.golden.make_golden import mixture
+    O = oracle_mod
+    idx, rng = _gpu_built(768, 32, 8, 1, 12000, 64, 0.5, 11)
+    art = idx.export_artifact()
+    q, _ = mixture(rng, 200, 768, 64, 0.5, True)
+    k, nprobe, n = 100, 8, 12000
+    n_bs = 20
+    bitsets = np.zeros((n_bs, (n + 63) // 64), np.uint64)  # bit id & 63 of word id >> 6
+    for b in range(n_bs):
+        dead = np.nonzero(rng.random(n) < 0.2)[0].astype(np.uint64)
+        np.bitwise_or.at(bitsets[b], (dead >> np.uint64(6)).astype(np.int64),
+                         np.uint64(1) << (dead & np.uint64(63)))
+    qb = np.full(q.shape[0], -1, np.int32)
+    qb[rng.choice(q.shape[0], q.shape[0] // 10, replace=False)] = np.arange(q.shape[0] // 10) % n_bs
+    oi = O.OracleIndex(art)
+    req = SearchRequest(top_k=k, nprobe=nprobe)
+    for mode, fm in ((FILTER_FUSED, O.FILTER_FUSED), (FILTER_POST, O.FILTER_POST)):
+        e_ids, e_d, e_c = oi.search(q, k, nprobe, filter_mode=fm, bitsets=bitsets, bitset_len=n,
+                                    query_bitset=qb)
+        r = idx.search(q, req, mode, bitsets, n, qb)
+        if mode == FILTER_FUSED:
+            assert np.array_equal(r.ids.reshape(e_ids.shape), e_ids)
+            assert bits_eq(r.distances.reshape(e_ids.shape), e_d)
+        else:
+            assert np.array_equal(r.counts, e_c)
+            got = r.ids.reshape(e_ids.shape)
+            assert all(np.array_equal(got[i, :c], e_ids[i, :c]) for i, c in enumerate(e_c))
+
+
+def test_config_3072_dims_8bit(gpu, oracle_mod):
+    """The shape of the 3,072-dimension configuration (8-bit codes, inner product, k = 10,
+    nprobe 24 of 32 lists) on a GPU-built index: D > 1024 takes the 8 x 8 rotation tiles
+    and the rerank without prefetched code registers."""
+    from hanns_b200.ivf_usq import SearchRequest
+    from tests.golden.make_golden import mixture
+    O = oracle_mod
+    idx, rng = _gpu_built(3072, 32, 8, 1, 6000, 16, 0.4, 3)
+    art = idx.export_artifact()
+    q, _ = mixture(rng, 64, 3072, 16, 0.4, True)
+    e_ids, e_d, _ = O.OracleIndex(art).search(q, 10, 24)
+    r = idx.search(q, SearchRequest(top_k=10, nprobe=24))
+    assert np.array_equal(r.ids.reshape(e_ids.shape), e_ids)
+    assert bits_eq(r.distances.reshape(e_ids.shape), e_d)
