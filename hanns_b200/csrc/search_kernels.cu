@@ -1686,11 +1686,13 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                         k = (uint32_t)(32767 - (int)sc[v]);
                         return true;
                     };
-                    int c_gt = 0;
-                    const uint32_t tau = warp_radix_kth16(n, a.n_cand, key_at, sm.hist[w], &c_gt);
+                    int c_gt = 0, c_eq = 0;
+                    const uint32_t tau =
+                        warp_radix_kth16(n, a.n_cand, key_at, sm.hist[w], &c_gt, &c_eq);
                     // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
-                    int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = 0;
-                    for (int base = 0; base < n; base += 32) {
+                    // When exactly n_cand rows score >= s*, F is all of them (no pass needed).
+                    int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = c_gt;
+                    for (int base = 0; c_gt + c_eq != a.n_cand && base < n; base += 32) {
                         const int v = base + lane;
                         uint32_t k = 0xFFFFFFFFu;
                         const bool valid = v < n && key_at(v, k);

@@ -117,9 +117,11 @@ __device__ uint32_t warp_radix_kth(int n, int kth, KeyAt key_at, uint32_t* hist,
 }
 
 // warp_radix_kth for keys known to lie in [0, 65535] (16-bit FastScan keys): two 8-bit
-// passes, no range pass.  Same contract as warp_radix_kth.
+// passes, no range pass.  Same contract as warp_radix_kth; *n_equal = keys equal to the
+// returned one.
 template <typename KeyAt>
-__device__ uint32_t warp_radix_kth16(int n, int kth, KeyAt key_at, uint32_t* hist, int* n_less) {
+__device__ uint32_t warp_radix_kth16(int n, int kth, KeyAt key_at, uint32_t* hist, int* n_less,
+                                     int* n_equal) {
     const int lane = (int)lane_id();
     uint32_t prefix = 0;
     int remaining = kth, less = 0;
@@ -160,6 +162,8 @@ __device__ uint32_t warp_radix_kth16(int n, int kth, KeyAt key_at, uint32_t* his
         __syncwarp();
     }
     *n_less = less;
+    *n_equal = (int)hist[prefix & 255u];  // the last pass counted keys by their low byte
+    __syncwarp();
     return prefix;
 }
 
