@@ -1554,6 +1554,13 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
         const uint2* fsb = a.fs + a.fs_blk_off[l] * (int64_t)a.nchunks * 32;
         for (int qg = 0; qg < it.z; qg += kScanWarps) {
             const int nq_here = min(kScanWarps, it.z - qg);
+            // the group's q_i8 rows into shared memory (read by the rerank, behind the barriers
+            // of the FastScan phases; the previous group's rerank ended with a barrier)
+            for (int e = tid; e < nq_here * (a.D / 16); e += kScanThreads) {
+                const int i = e / (a.D / 16), c = e - i * (a.D / 16);
+                *reinterpret_cast<uint4*>(qsm + i * qld + 16 * c) =
+                    __ldg(reinterpret_cast<const uint4*>(a.q_i8p + (int64_t)sm.q[qg + i] * a.D) + c);
+            }
             {
                 // interleave the 8 queries' offset-binary LUTs: word g*16+nib of quad h =
                 // q(4h)|q(4h+1)<<8|q(4h+2)<<16|q(4h+3)<<24 (16 LUT bytes of each query per
@@ -1753,13 +1760,6 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                     a.cand_key[rbase + j] = 0xFFFFFFFFu;
                 }
                 if (lane == 0) sm.nc[w] = n_c;
-            }
-            __syncthreads();
-            // the group's q_i8 rows into shared memory
-            for (int e = tid; e < nq_here * (a.D / 16); e += kScanThreads) {
-                const int i = e / (a.D / 16), c = e - i * (a.D / 16);
-                *reinterpret_cast<uint4*>(qsm + i * qld + 16 * c) =
-                    __ldg(reinterpret_cast<const uint4*>(a.q_i8p + (int64_t)sm.q[qg + i] * a.D) + c);
             }
             __syncthreads();
             // integer rerank of the group's kept candidates, 8 per warp at a time (two per
