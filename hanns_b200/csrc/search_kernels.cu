@@ -1761,7 +1761,12 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                 }
                 if (lane == 0) sm.nc[w] = n_c;
             }
-            __syncthreads();
+            // a full group reranks warp by warp the query each warp just selected (its own
+            // sm.nc / sv / ties): the warp only waits for itself
+            if (nq_here == kScanWarps)
+                __syncwarp();
+            else
+                __syncthreads();
             // integer rerank of the group's kept candidates, 8 per warp at a time (two per
             // group of 8 lanes, their loads issued together)
             // warps per query: wpq = 8 / nq_here; warp w reranks query w / wpq, candidates
