@@ -51,6 +51,14 @@ WORKLOADS = {
               nbits=4, metric=0, seed=42, normalise=False),
     "D": dict(n=260_000, d=3072, comps=256, sigma=0.4, nq=5_000, nlist=1024, nprobe=24, k=10,
               nbits=8, metric=1, seed=3, normalise=True),
+    # the 8x-compression variant of D: 4-bit codes, FastScan runs on lists above 150 rows
+    "D4": dict(n=260_000, d=3072, comps=256, sigma=0.4, nq=5_000, nlist=1024, nprobe=24, k=10,
+               nbits=4, metric=1, seed=3, normalise=True),
+    # scale-out shape: one step is one 16,384-query batch of the 100,000-query set; every
+    # list is at most n_cand = 1,500 rows, so FastScan never runs and the rerank is the scan
+    "E": dict(n=20_000_000, d=768, comps=16384, sigma=0.5, nq=16_384, nlist=65536, nprobe=64,
+              k=100, nbits=4, metric=1, seed=19, normalise=True, train_per_list=16,
+              kmeans_iters=10, query_set=100_000),
 }
 TRAIN_ROWS_PER_LIST = 64
 KMEANS_ITERS = 25  # KMeans::new max_iter (src/quantization/kmeans.rs:44-56), early stop at shift < 1e-2
@@ -85,12 +93,23 @@ def _centres(w, g, device):
     return torch.randn(w["comps"], w["d"], generator=g, device=device)
 
 
+def _mixture_draw_chunked(w, centres, g, n, chunk=1 << 21):
+    """The same mixture drawn 2 Mi rows at a time into one preallocated tensor (a base of
+    tens of GB leaves no room for the single-shot draw's temporaries)."""
+    import torch
+    x = torch.empty(n, w["d"], dtype=torch.float32, device=centres.device)
+    for s in range(0, n, chunk):
+        x[s:s + chunk] = _mixture_draw(w, centres, g, min(chunk, n - s))
+    return x
+
+
 def make_data(w, device="cuda"):
     import torch
     g = torch.Generator(device=device)
     g.manual_seed(w["seed"])
     centres = _centres(w, g, device)
-    base = _mixture_draw(w, centres, g, w["n"])
+    draw = _mixture_draw_chunked if w["n"] > (1 << 22) else _mixture_draw
+    base = draw(w, centres, g, w["n"])
     queries = _mixture_draw(w, centres, g, w["nq"])
     return base, queries
 
@@ -106,16 +125,28 @@ def extra_queries(w, device, r):
     return _mixture_draw(w, centres, g2, w["nq"])
 
 
-def exact_topk(base, queries, k, metric):
+def exact_topk(base, queries, k, metric, base_chunk=1 << 22):
+    """Exact fp32 top-k ids (no TF32), base rows taken 4 Mi at a time."""
     import torch
     torch.backends.cuda.matmul.allow_tf32 = False
     out = []
-    bn = (base * base).sum(1)
     for s in range(0, queries.shape[0], 1024):
         q = queries[s:s + 1024]
-        ip = q @ base.T
-        score = ip if metric == 1 else -(bn[None, :] - 2 * ip)
-        out.append(score.topk(k, dim=1).indices)
+        best_v = best_i = None
+        for b0 in range(0, base.shape[0], base_chunk):
+            xb = base[b0:b0 + base_chunk]
+            ip = q @ xb.T
+            score = ip if metric == 1 else -((xb * xb).sum(1)[None, :] - 2 * ip)
+            v, i = score.topk(min(k, xb.shape[0]), dim=1)
+            i = i + b0
+            if best_v is None:
+                best_v, best_i = v, i
+            else:
+                v = torch.cat([best_v, v], 1)
+                i = torch.cat([best_i, i], 1)
+                best_v, j = v.topk(k, dim=1)
+                best_i = i.gather(1, j)
+        out.append(best_i)
     return torch.cat(out).cpu().numpy()
 
 
@@ -126,26 +157,35 @@ def build_index(w, base_np, device):
                        rotation_seed=42)
     idx = IvfUsqIndex(cfg, device=device)
     rng = np.random.default_rng(w["seed"])
-    ntrain = min(base_np.shape[0], TRAIN_ROWS_PER_LIST * w["nlist"])
+    ntrain = train_rows(w)
     tr = base_np[np.sort(rng.choice(base_np.shape[0], ntrain, replace=False))]
+    iters = w.get("kmeans_iters", KMEANS_ITERS)
     t0 = time.time()
-    idx.train(tr, kmeans_iters=KMEANS_ITERS, kmeans_seed=w["seed"])
+    idx.train(tr, kmeans_iters=iters, kmeans_seed=w["seed"])
     t1 = time.time()
     idx.add(base_np)
-    log(f"[build] train {t1 - t0:.1f}s ({ntrain} rows, {KMEANS_ITERS} iters) add {time.time() - t1:.1f}s")
+    log(f"[build] train {t1 - t0:.1f}s ({ntrain} rows, {iters} iters) add {time.time() - t1:.1f}s")
     return idx
+
+
+def train_rows(w):
+    return min(w["n"], w.get("train_per_list", TRAIN_ROWS_PER_LIST) * w["nlist"])
 
 
 def cache_path(name):
     return os.path.join(CACHE_DIR, f"workload_{name}_kpp_artifact.npz")
 
 
+def load_artifact(name):
+    z = np.load(cache_path(name))
+    return {k: (z[k].item() if z[k].ndim == 0 else z[k]) for k in z.files}
+
+
 def get_artifact(name, w, base, device):
     """Frozen index of the workload: built with the GPU build path once, cached on disk."""
     p = cache_path(name)
     if os.path.exists(p):
-        z = np.load(p)
-        return {k: (z[k].item() if z[k].ndim == 0 else z[k]) for k in z.files}
+        return load_artifact(name)
     idx = build_index(w, base.cpu().numpy(), device)
     art = idx.export_artifact()
     idx.close()
@@ -169,15 +209,72 @@ def scan_bytes(art, probes, k, nbits):
     return int((sizes * (D // 8) * fs).sum() + (np.minimum(sizes, ncand) * (cb + 24)).sum())
 
 
-def measured_traffic(name):
-    """DRAM bytes per scan launch from the committed ncu summary of this workload (or None)."""
+def measured_traffic(name, kernel):
+    """(DRAM bytes per launch, kernel ms under ncu, file) from the committed ncu summary of
+    this kernel on this workload, or (None, None, None)."""
     import re
+    path = os.path.join("profiles", f"{kernel}_workload_{name}.md")
     try:
-        with open(os.path.join(ROOT, "profiles", f"scan_lists_kernel_workload_{name}.md")) as f:
-            m = re.search(r"dram_bytes_per_launch \| (\d+)", f.read())
-        return int(m.group(1)) if m else None
+        with open(os.path.join(ROOT, path)) as f:
+            txt = f.read()
     except OSError:
-        return None
+        return None, None, None
+    m = re.search(r"dram_bytes_per_launch \| (\d+)", txt)
+    t = re.search(r"gpu__time_duration_ms \| ([0-9.]+)", txt)
+    return (int(m.group(1)) if m else None), (float(t.group(1)) if t else None), path
+
+
+def index_stats(art, probes, k, nbits):
+    """List-size and list-grouping figures of one batch: what the scan's work depends on."""
+    from oracle.oracle import n_candidates
+    sizes = np.diff(np.asarray(art["list_offsets"], dtype=np.int64))
+    nlist = sizes.shape[0]
+    ncand = n_candidates(nbits, k)
+    pr = probes.reshape(-1)
+    pr = pr[(pr >= 0) & (pr < nlist)]
+    q_per_list = np.bincount(pr, minlength=nlist)
+    probed = q_per_list > 0
+    psz = sizes[pr]
+    return {"list_rows": {"min": int(sizes.min()), "median": float(np.median(sizes)),
+                          "mean": float(sizes.mean()), "p99": float(np.percentile(sizes, 99)),
+                          "max": int(sizes.max()), "empty": int((sizes == 0).sum())},
+            "probed_list_rows_mean": float(psz.mean()) if psz.size else 0.0,
+            "queries_per_probed_list": {"mean": float(q_per_list[probed].mean()) if probed.any() else 0.0,
+                                        "max": int(q_per_list.max())},
+            "n_cand": int(ncand),
+            "pairs_with_fastscan": float((psz > ncand).mean()) if psz.size else 0.0,
+            "reranked_rows_per_query": float(np.minimum(psz, ncand).sum() / max(probes.shape[0], 1))}
+
+
+def scan_roofline(workload, alg_bytes, scan_s, world):
+    """Roofline of the list scan (the dominant stage).
+
+    achieved / frac use the DRAM bytes ncu measured for one launch on this workload (the
+    committed summary under profiles/) over the live CUDA-event launch time; the
+    per-(query, probe) stream bytes of the reference's loop (sign bytes of every FastScan
+    list plus code + meta + id bytes of every reranked row) are reported beside it as
+    algorithmic_* -- list grouping reads each list once per batch, so those bytes mostly
+    come from L2 and the scan is limited by instruction issue, not by HBM."""
+    peak, peak_kind = peaks()
+    kernel = "scan_lists_kernel"
+    traffic, ncu_ms, path = measured_traffic(workload, kernel) if world == 1 else (None, None, None)
+    alg_gbs = alg_bytes / scan_s / 1e9
+    roof = {"kernel": kernel, "bound": "hbm", "unit": "GB/s", "peak": peak,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
+            "launch_ms": scan_s * 1e3, "traffic": traffic,
+            "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch ({path}, "
+                               f"{ncu_ms} ms under ncu)") if traffic else "no ncu capture for this workload",
+            "limiter": "integer instruction issue (FastScan LUT lookups, dp4a rerank, kept-set selection)",
+            "algorithmic_bytes_per_launch": alg_bytes, "algorithmic_gbs": alg_gbs,
+            "algorithmic_frac_of_hbm": alg_gbs / peak}
+    if traffic:
+        roof["achieved"] = traffic / scan_s / 1e9
+        roof["achieved_basis"] = "measured DRAM bytes per launch / CUDA-event launch time"
+    else:
+        roof["achieved"] = alg_gbs
+        roof["achieved_basis"] = "algorithmic stream bytes (no DRAM capture for this workload)"
+    roof["frac"] = roof["achieved"] / peak
+    return roof
 
 
 class ClockSampler:
@@ -248,8 +345,13 @@ def run_reference(args, w, rank, world):
         return
     import torch
     from oracle import oracle as O
+    if not os.path.exists(cache_path(args.workload)):
+        # the frozen index is built by the GPU build path in a process of its own: the timed
+        # process maps no library of this repository
+        subprocess.run([sys.executable, os.path.abspath(__file__), "--prepare-artifact",
+                        "--workload", args.workload], check=True)
+    art = load_artifact(args.workload)
     base, queries = make_data(w, "cuda" if torch.cuda.is_available() else "cpu")
-    art = get_artifact(args.workload, w, base, 0)
     q = queries.cpu().numpy()
     del base
     oi = O.OracleIndex(art)
@@ -301,8 +403,10 @@ def config_block(name, w, world, split=False):
             "global_batch": w["nq"] if (world == 1 or split) else w["nq"] * world,
             "parallelism": par,
             "l2_policy": "index larger than L2 (no flush needed)",
-            "build": f"train on {TRAIN_ROWS_PER_LIST} rows/list: seeded k-means++ seeding, empty lists "
-                     f"restarted, at most {KMEANS_ITERS} iterations (shift < 1e-2 stops)"}
+            "build": f"train on {train_rows(w)} sampled rows ({w.get('train_per_list', TRAIN_ROWS_PER_LIST)} "
+                     f"per list): seeded k-means++ seeding, empty lists restarted, at most "
+                     f"{w.get('kmeans_iters', KMEANS_ITERS)} iterations (shift < 1e-2 stops); "
+                     f"every base row added"}
 
 
 # ------------------------------------------------------------------ our arm
@@ -500,6 +604,7 @@ def run_ours(args, w, rank, world, local_rank):
         allq = queries
     probes = idx.debug_query(allq.cpu().numpy(), nprobe)["probes"]
     del allq
+    stats = index_stats(art, probes, k, w["nbits"])
     art_local = art if world == 1 else idx.export_artifact()
     if world > 1:
         # the shard's lists: lists it does not own are empty in its export
@@ -507,14 +612,7 @@ def run_ours(args, w, rank, world, local_rank):
         probes = probes[own[probes]]
     alg = scan_bytes(art_local, probes, k, w["nbits"])
     scan_s = statistics.median(scan_ms) / 1e3
-    peak, peak_kind = peaks()
-    achieved = alg / scan_s / 1e9
-    roof = {"kernel": "scan_lists_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
-            "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
-            "traffic": measured_traffic(args.workload) if world == 1 else None,
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
-                              f"profiles/scan_lists_kernel_workload_{args.workload}.md",
-            "algorithmic_bytes_per_launch": alg, "launch_ms": scan_s * 1e3}
+    roof = scan_roofline(args.workload, alg, scan_s, world)
 
     # ---- recall and parity sample
     rec = None
@@ -550,7 +648,11 @@ def run_ours(args, w, rank, world, local_rank):
         "config": config_block(args.workload, w, world, split),
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": launches[0], "clocks": clk.summary(),
-        "recall_at_k": rec, "parity_vs_oracle": parity, "parity_vs_single_gpu": shard_parity,
+        "recall_at_k": rec,
+        "recall_note": f"exact fp32 ground truth over all {w['n']} rows; the index's k-means saw "
+                       f"{train_rows(w)} sampled rows (the reference trains on every row)",
+        "index_stats": stats,
+        "parity_vs_oracle": parity, "parity_vs_single_gpu": shard_parity,
         "stage_ms_last_step": dict(zip(IvfUsqIndex.STAGES, stages)),
     }
     print(json.dumps(line), flush=True)
@@ -565,6 +667,8 @@ def main():
     ap.add_argument("--workload", default="B", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline / parity sample")
     ap.add_argument("--no-recall", action="store_true", help="skip exact ground truth (frees the base early)")
+    ap.add_argument("--prepare-artifact", action="store_true",
+                    help="build and cache the workload's frozen index, then exit")
     ap.add_argument("--split", action="store_true",
                     help="N > 1: one batch split over the ranks (strong scaling) instead of one "
                          "batch per rank (weak scaling)")
@@ -573,6 +677,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     w = WORKLOADS[args.workload]
+    if args.prepare_artifact:
+        base, _ = make_data(w, "cuda")
+        get_artifact(args.workload, w, base, 0)
+        return
     if args.impl == "reference":
         run_reference(args, w, rank, world)
         return
