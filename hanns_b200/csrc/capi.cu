@@ -649,6 +649,30 @@ int32_t hanns_gpu_ivf_usq_debug_query(HannsIvfUsqHandle* h, const float* queries
     });
 }
 
+int32_t hanns_gpu_ivf_usq_debug_candidates(HannsIvfUsqHandle* h, const float* queries, int64_t nq,
+                                           int32_t k, int32_t nprobe, int32_t filter_mode,
+                                           const uint64_t* bitsets, int64_t bitset_len,
+                                           int64_t n_bitsets, const int32_t* query_bitset,
+                                           int64_t cap, int64_t* counts, int32_t* lists,
+                                           int64_t* local, int32_t* fs, int32_t* int_ip,
+                                           float* dists) {
+    if (!h || !queries || nq <= 0 || k <= 0 || cap <= 0 || !counts || !lists || !local || !fs ||
+        !int_ip || !dists)
+        return HANNS_INVALID_ARG;
+    if (filter_mode < 0 || filter_mode > 2) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        hanns::SearchOptions opt;
+        opt.k = k;
+        opt.nprobe = nprobe;
+        opt.filter_mode = bitsets ? filter_mode : 0;
+        opt.bitset_len = bitset_len;
+        opt.n_bitsets = n_bitsets;
+        h->idx->debug_candidates(queries, nq, opt, bitsets, query_bitset, cap, counts, lists, local,
+                                 fs, int_ip, dists);
+    });
+}
+
 int32_t hanns_gpu_ivf_usq_shard(HannsIvfUsqHandle* h, int32_t rank, int32_t world) {
     if (!h) return HANNS_INVALID_ARG;
     return guarded([&] {

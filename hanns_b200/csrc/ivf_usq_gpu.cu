@@ -93,6 +93,7 @@ IvfUsqGpu::~IvfUsqGpu() {
     for (auto& e : ev_up_)
         if (e) cudaEventDestroy(e);
     if (ev_ready_) cudaEventDestroy(ev_ready_);
+    if (ev_scan_err_) cudaEventDestroy(ev_scan_err_);
     if (ev_fork_) cudaEventDestroy(ev_fork_);
     if (ev_join_) cudaEventDestroy(ev_join_);
     if (aux_stream_) cudaStreamDestroy(aux_stream_);
@@ -114,6 +115,7 @@ void IvfUsqGpu::ensure_stream() {
         }
         for (auto& e : ev_up_) HANNS_CUDA_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_ready_, cudaEventDisableTiming));
+        HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_scan_err_, cudaEventDisableTiming));
         HANNS_CUDA_OK(cudaHostAlloc(reinterpret_cast<void**>(&h_scan_err_), sizeof(int),
                                     cudaHostAllocDefault));
         *h_scan_err_ = 0;
@@ -689,9 +691,12 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     w_lq_.reserve((size_t)nb * nprobe);
     w_items_.reserve((size_t)nb * nprobe);
     HANNS_CUDA_OK(cudaMemsetAsync(w_counters_.p, 0, 3 * sizeof(int), s));
-    launch_group_pairs(st.probes, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr,
-                       kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p, w_item_off_.p,
-                       w_counters_.p, w_lq_.p, w_items_.p, s);
+    // lists of at most kTcMaxRows rows take the tensor-core scan (HANNS_GPU_SCAN=simt: none)
+    const char* scan_mode = std::getenv("HANNS_GPU_SCAN");
+    const bool use_tc = !(scan_mode && std::strcmp(scan_mode, "simt") == 0);
+    launch_group_pairs(st.probes, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr, list_off_.p,
+                       use_tc ? kTcMaxRows : 0, kQueriesPerItem, w_cnt_.p, w_cursor_.p,
+                       w_lq_off_.p, w_item_off_.p, w_counters_.p, w_lq_.p, w_items_.p, s);
     const int n_cand = (int)n_candidates(nbits_, k);
     const int64_t q_stride = cand_stride(nprobe, k);
     w_pair_off_.reserve((size_t)nb * (nprobe + 1));
@@ -741,28 +746,33 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     a.cand_tie = w_cand_tie_.p;
     a.scores = w_scores_.p;
     a.max_len = (int)per_warp;
-    // HANNS_GPU_SCAN=tc: lists with n_cand < |list| <= scan_tc_max_rows() (FastScan runs)
-    // go to the tensor-core scan; by default every list takes the SIMT scan
-    const char* scan_mode = std::getenv("HANNS_GPU_SCAN");
-    const bool use_tc = scan_mode && std::strcmp(scan_mode, "tc") == 0 && max_list_ > n_cand;
-    a.tc_rows = use_tc ? scan_tc_max_rows() : 0;
+    if (debug_candidates_) {
+        w_cand_dbg_.reserve((size_t)nb * q_stride);
+        a.cand_dbg = w_cand_dbg_.p;
+    }
     if (use_tc) {
-        w_scan_err_.reserve(1);
-        HANNS_CUDA_OK(cudaMemsetAsync(w_scan_err_.p, 0, sizeof(int), s));
+        if (!w_scan_err_.p) {
+            // sticky: an expired bounded wait stays visible to every later check
+            w_scan_err_.reserve(1);
+            HANNS_CUDA_OK(cudaMemsetAsync(w_scan_err_.p, 0, sizeof(int), s));
+        }
         TcScanArgs t{};
         t.D = D_;
         t.nbits = nbits_;
         t.code_bytes = code_bytes_;
         t.G = G;
         t.metric_l2 = a.metric_l2;
+        t.nchunks = D_ / 64;
         t.list_off = list_off_.p;
-        t.signs = signs_.p;
+        t.fs_blk_off = fs_blk_off_.p;
+        t.fs = fs_.p;
         t.codes = codes_.p;
         t.meta = meta_.p;
         t.ids = ids_.p;
         t.qp = st.qp;
         t.lut = st.lut;
-        t.q_i8 = st.q_i8n;
+        t.q_i8p = st.q_i8p;
+        t.cand_dbg = a.cand_dbg;
         t.lq = w_lq_.p;
         t.items = w_items_.p;
         t.n_items = w_counters_.p;
@@ -834,9 +844,11 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     m.out_keys = d_keys;
     launch_merge(m, s);
     launches += 1;
-    used_tc_ = use_tc;
-    if (use_tc)
+    used_tc_ = used_tc_ || use_tc;
+    if (use_tc) {
         HANNS_CUDA_OK(cudaMemcpyAsync(h_scan_err_, w_scan_err_.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+        HANNS_CUDA_OK(cudaEventRecord(ev_scan_err_, s));
+    }
     HANNS_CUDA_OK(cudaGetLastError());
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[7], s));
     return launches;
@@ -848,7 +860,10 @@ void IvfUsqGpu::search_device(const float* d_queries, int64_t nq, const SearchOp
                               cudaStream_t stream) {
     DeviceGuard g(device_);
     run_search(d_queries, nullptr, nq, opt, d_ids, d_dists, d_counts, d_keys, stream);
-    if (!stream) HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    if (!stream) {
+        HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+        check_tc_scan();
+    }
 }
 
 void IvfUsqGpu::run_search(const float* d_queries, const float* h_queries, int64_t nq,
@@ -904,11 +919,13 @@ void IvfUsqGpu::next_slot(int first, int last) {
     if (!calls_.empty()) ++calls_.back().second;
 }
 
-// The tensor-core scan reports an expired bounded wait through a pinned flag: only then
-// does the call wait for the device before returning.
+// The tensor-core scan reports an expired bounded wait through a sticky device flag that
+// each scan copies to pinned memory.  The check does not wait for the device: it reads the
+// copy once the event behind it has completed (a stream-ordered call returns once
+// enqueued, and a later call or a synchronising one reports the error).
 void IvfUsqGpu::check_tc_scan() {
     if (!used_tc_) return;
-    HANNS_CUDA_OK(cudaEventSynchronize(ev_[kStages]));
+    if (cudaEventQuery(ev_scan_err_) != cudaSuccess) return;
     if (*h_scan_err_ != 0)
         throw std::runtime_error("tensor-core list scan: a bounded wait expired (code " +
                                  std::to_string(*h_scan_err_) + ")");
@@ -1014,9 +1031,6 @@ void IvfUsqGpu::search_prepared_device(int64_t nq, const SearchOptions& opt, Que
     check_supported();
     if (nq <= 0) throw std::invalid_argument("query dimension mismatch");
     if (!st.probes || !st.qp || !st.lut || !st.q_i8p) throw std::invalid_argument("null query state");
-    const char* scan_mode = std::getenv("HANNS_GPU_SCAN");
-    if (!st.q_i8n && scan_mode && std::strcmp(scan_mode, "tc") == 0)
-        throw std::invalid_argument("the tensor-core scan needs q_i8 in dimension order");
     cudaStream_t s = stream ? stream : stream_;
     const int k = std::max(opt.k, 1);
     const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
@@ -1038,7 +1052,10 @@ void IvfUsqGpu::search_prepared_device(int64_t nq, const SearchOptions& opt, Que
                                            d_keys ? d_keys + b * k : nullptr, s, true);
         check_tc_scan();
     }
-    if (!stream) HANNS_CUDA_OK(cudaStreamSynchronize(s));
+    if (!stream) {
+        HANNS_CUDA_OK(cudaStreamSynchronize(s));
+        check_tc_scan();
+    }
 }
 
 void IvfUsqGpu::search_host(const float* h_queries, int64_t nq, const SearchOptions& opt_in,
@@ -1079,6 +1096,64 @@ void IvfUsqGpu::search_host(const float* h_queries, int64_t nq, const SearchOpti
         HANNS_CUDA_OK(cudaMemcpyAsync(h_counts, w_out_counts_.p, sizeof(int64_t) * nq,
                                       cudaMemcpyDeviceToHost, stream_));
     HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+    check_tc_scan();
+}
+
+void IvfUsqGpu::debug_candidates(const float* h_queries, int64_t nq, const SearchOptions& opt_in,
+                                 const uint64_t* h_bitsets, const int32_t* h_query_bitset,
+                                 int64_t cap, int64_t* counts, int32_t* lists, int64_t* local,
+                                 int32_t* fs, int32_t* int_ip, float* dists) {
+    DeviceGuard g(device_);
+    SearchOptions opt = opt_in;
+    const int k = std::max(opt.k, 1);
+    const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
+    const int64_t stride = cand_stride(nprobe, k);
+    if (nq > std::min<int64_t>(kMaxBatch, std::max<int64_t>(1, kCandBudget / (stride * 12))))
+        throw std::invalid_argument("debug_candidates: more queries than one internal batch");
+    std::vector<int64_t> ids((size_t)nq * k), cnt(nq);
+    std::vector<float> d((size_t)nq * k);
+    debug_candidates_ = true;
+    try {
+        search_host(h_queries, nq, opt, h_bitsets, h_query_bitset, ids.data(), d.data(), cnt.data());
+    } catch (...) {
+        debug_candidates_ = false;
+        throw;
+    }
+    debug_candidates_ = false;
+    std::vector<int> off((size_t)nq * (nprobe + 1));
+    std::vector<int32_t> probes((size_t)nq * nprobe);
+    std::vector<uint32_t> key((size_t)nq * stride);
+    std::vector<uint64_t> tie((size_t)nq * stride);
+    std::vector<int2> dbg((size_t)nq * stride);
+    HANNS_CUDA_OK(cudaMemcpy(off.data(), w_pair_off_.p, sizeof(int) * off.size(), cudaMemcpyDeviceToHost));
+    HANNS_CUDA_OK(cudaMemcpy(probes.data(), w_probes_.p, sizeof(int32_t) * probes.size(), cudaMemcpyDeviceToHost));
+    HANNS_CUDA_OK(cudaMemcpy(key.data(), w_cand_key_.p, sizeof(uint32_t) * key.size(), cudaMemcpyDeviceToHost));
+    HANNS_CUDA_OK(cudaMemcpy(tie.data(), w_cand_tie_.p, sizeof(uint64_t) * tie.size(), cudaMemcpyDeviceToHost));
+    HANNS_CUDA_OK(cudaMemcpy(dbg.data(), w_cand_dbg_.p, sizeof(int2) * dbg.size(), cudaMemcpyDeviceToHost));
+    std::vector<int64_t> order;
+    for (int64_t q = 0; q < nq; ++q) {
+        const int64_t base = q * stride;
+        const int total = off[q * (nprobe + 1) + nprobe];
+        order.clear();
+        for (int e = 0; e < total; ++e)
+            if (tie[base + e] != ~0ull) order.push_back(base + e);
+        // tie = probe rank << 48 | FastScan key (32767 - score, 0 without FastScan) << 32 |
+        // position: increasing ties are the reference's candidate order
+        std::sort(order.begin(), order.end(), [&](int64_t x, int64_t y) { return tie[x] < tie[y]; });
+        if ((int64_t)order.size() > cap) throw std::invalid_argument("debug_candidates: cap too small");
+        counts[q] = (int64_t)order.size();
+        for (size_t j = 0; j < order.size(); ++j) {
+            const int64_t e = order[j], o = q * cap + (int64_t)j;
+            const uint64_t t = tie[e];
+            lists[o] = probes[q * nprobe + (int)(t >> 48)];
+            local[o] = (int64_t)(t & 0xFFFFFFFFull);
+            fs[o] = dbg[e].y;
+            int_ip[o] = dbg[e].x;
+            const uint32_t kk = key[e];
+            const uint32_t bits = (kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk;
+            std::memcpy(&dists[o], &bits, 4);
+        }
+    }
 }
 
 void IvfUsqGpu::debug_query(const float* h_queries, int64_t nq, int nprobe, int32_t* probes,

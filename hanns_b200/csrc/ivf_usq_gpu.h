@@ -111,6 +111,15 @@ class IvfUsqGpu {
 
     void debug_query(const float* h_queries, int64_t nq, int nprobe, int32_t* probes, float* q_rot,
                      int8_t* q_i8, int8_t* lut, float* scalars);
+    // The list scan's kept candidates of nq host queries (one internal batch), each query's
+    // in the reference's candidate order (probe order; inside a list that ran FastScan,
+    // score descending then position): list, position in the list, FastScan score
+    // (INT32_MIN where FastScan did not select the row), int_ip and distance, at q * cap;
+    // counts[q] = the query's candidates.  Throws if a query has more than cap.
+    void debug_candidates(const float* h_queries, int64_t nq, const SearchOptions& opt,
+                          const uint64_t* h_bitsets, const int32_t* h_query_bitset, int64_t cap,
+                          int64_t* counts, int32_t* lists, int64_t* local, int32_t* fs,
+                          int32_t* int_ip, float* dists);
 
     void shard(int rank, int world);
     void save(const std::string& path) const;
@@ -214,6 +223,9 @@ class IvfUsqGpu {
     cudaEvent_t ev_up_[kMaxUploadChunks] = {};
     cudaEvent_t ev_ready_ = nullptr;  // copy_stream_ waits for earlier work on the search stream
     int* h_scan_err_ = nullptr;       // pinned: error code of the tensor-core list scan
+    cudaEvent_t ev_scan_err_ = nullptr;  // completes when h_scan_err_ holds the last scan's code
+    bool debug_candidates_ = false;      // scans also write (int_ip, FastScan score) per candidate
+    DevBuf<int2> w_cand_dbg_;
     DevBuf<int> w_scan_err_;
     int sm_count_ = 0;
     // stages: coarse GEMM, coarse select, rotate, query state, group, scan, merge; then total

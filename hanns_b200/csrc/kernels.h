@@ -50,24 +50,44 @@ struct ScanArgs {
     int64_t q_stride;
     uint32_t* cand_key;
     uint64_t* cand_tie;
+    // nullable (parity debugging): (int_ip, FastScan score or INT32_MIN when FastScan did
+    // not select the row) of every kept candidate, at the same index as cand_key
+    int2* cand_dbg;
     // FastScan scores scratch: per CTA, kScanWarps rows of max_len (the longest list)
     int16_t* scores;
     int max_len;
-    // items whose list has n_cand < |list| <= tc_rows belong to scan_tc_kernel (0: none)
-    int tc_rows;
 };
 
-// Tensor-core list scan of the FastScan-sized lists (scan_tc.cu).
+#ifdef __CUDACC__
+#define HANNS_HD __host__ __device__
+#else
+#define HANNS_HD
+#endif
+
+// Lists of at most kTcMaxRows rows are scanned by the tensor-core kernel (scan_tc.cu),
+// longer ones by the SIMT kernel.  A tensor-core item holds one list's rows in T =
+// ceil(n / 128) tiles of 128 (the MMA's M) and N queries (the MMA's N, a multiple of 16,
+// at most 128), with T * N <= 256 so that an item's accumulators fill half of the 512
+// TMEM columns.
+constexpr int kTcMaxRows = 2048;
+HANNS_HD inline int tc_queries_per_item(long long n) {
+    const int t = (int)((n + 127) / 128);
+    const int q = (256 / (t < 1 ? 1 : t)) & ~15;
+    return q > 128 ? 128 : q;
+}
+
+// Tensor-core list scan (scan_tc.cu): the items flagged for it by the grouping step.
 struct TcScanArgs {
-    int D, nbits, code_bytes, G, metric_l2;
+    int D, nbits, code_bytes, G, metric_l2, nchunks;
     const int64_t* list_off;
-    const uint8_t* signs;   // [ntotal][D/8] sign bits, list order
+    const int64_t* fs_blk_off;
+    const uint2* fs;        // FastScan sign codes: [block][D/64][32 slots] x 8 bytes
     const uint8_t* codes;   // [ntotal][code_bytes]
     const float4* meta;
     const int64_t* ids;
     const QueryParams* qp;
     const uint8_t* lut;     // [nq][G*16] offset-binary
-    const int8_t* q_i8;     // [nq][D] natural order
+    const uint8_t* q_i8p;   // [nq][D] dp4a layout (4-bit: even then odd dims per 8)
     const int2* lq;
     const int4* items;
     const int* n_items;
@@ -80,7 +100,8 @@ struct TcScanArgs {
     int64_t q_stride;
     uint32_t* cand_key;
     uint64_t* cand_tie;
-    int* err_flag;          // set to 4 when a bounded wait expired
+    int2* cand_dbg;         // nullable, as in ScanArgs
+    int* err_flag;          // set to a nonzero code when a bounded wait expired
 };
 
 // USQ rerank of caller-chosen stored rows: out[q * m + j] = distance of row rows[q*m+j]
@@ -173,16 +194,19 @@ void launch_rotate(const float* x, int64_t nq, int d, int D, const float* Pc, fl
 void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, int D,
                         const float* rc, int nbits, QueryParams* qp, uint8_t* q_i8p,
                         int8_t* q_i8n, uint8_t* lut, cudaStream_t s);
+// Items (list, first lq index, queries, kind): lists of at most tc_max_rows rows (0:
+// none) become tensor-core items (kind 1) of tc_queries_per_item(|list|) queries, the
+// others SIMT items (kind 0) of qpi queries.
 void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist,
-                        const uint8_t* owned, int qpi, int* cnt, int* cursor, int* lq_off,
-                        int* item_off, int* n_items, int2* lq, int4* items, cudaStream_t s);
+                        const uint8_t* owned, const int64_t* list_off, int tc_max_rows, int qpi,
+                        int* cnt, int* cursor, int* lq_off, int* item_off, int* n_items, int2* lq,
+                        int4* items, cudaStream_t s);
 // pair_off[q][r] = sum over earlier probes of min(|list|, n_cand) (0 for lists this
 // index does not own); pair_off[q][nprobe] = the query's candidate total
 void launch_pair_offsets(const int32_t* probes, int64_t nq, int nprobe, const int64_t* list_off,
                          int nlist, const uint8_t* owned, int n_cand, int* pair_off,
                          cudaStream_t s);
 size_t scan_smem_bytes(int D);
-int scan_tc_max_rows();
 size_t scan_tc_smem_bytes();
 void launch_scan_tc(const TcScanArgs& a, int grid, cudaStream_t s);
 int scan_grid_size(int D);

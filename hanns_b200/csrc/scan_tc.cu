@@ -1,36 +1,40 @@
-// scan_tc.cu -- list scan of the FastScan-sized lists on the sm_100a tensor cores.
+// scan_tc.cu -- list scan on the sm_100a tensor cores.
 //
-// One persistent CTA per SM takes whole (list, <= 32 queries) items whose list is longer
-// than the candidate count n_cand (so the reference runs FastScan on it) and at most
-// kMaxTiles * 128 rows.  Both integer stages are int8 GEMMs (tcgen05.mma kind::i8, int32
+// One persistent CTA per SM takes items (one list of at most kTcMaxRows rows, up to 128 of
+// the queries that probe it).  The list's rows are the MMA's M side, in T tiles of 128;
+// the item's queries are its N side (N = queries rounded up to 16, T * N <= 256).  Both
+// integer stages of the reference's search are int8 GEMMs (tcgen05.mma kind::i8, int32
 // accumulation in TMEM, exact):
 //
-//   FastScan   raw[v][i] = sum_g LUT_i[g][nib_g(v)]
-//              = onehot(v) . LUT_i  over K = 16 * G bytes, A = one-hot rows (u8 0/1,
-//              built in shared memory from the sign bits), B = the queries' LUTs (s8).
-//              The int32 sum wrapped to 16 bits equals the reference's i16 wraparound
-//              accumulation (fastscan.rs:170-227).
-//   rerank     int_ip[v][i] = sum_d code_u8[v][d] * q_i8[i][d] over K = D bytes, A = the
-//              list's codes unpacked to one byte per dimension, B = the queries' q_i8
-//              (quantizer.rs:382-400).
+//   FastScan   raw[v][i] = sum_g LUT_i[g][nib_g(v)]                    (fastscan.rs:170-227)
+//              = onehot(v) . LUT_i over K = 16 G bytes: A = one-hot rows (u8 0/1, one
+//              16-byte group per 4 dimensions, built in shared memory from the sign bits),
+//              B = the queries' LUTs (s8).  The int32 sum wrapped to 16 bits equals the
+//              reference's i16 wraparound accumulation.  Only lists longer than n_cand.
+//   rerank     int_ip[v][i] = sum_d code_u8[v][d] * q_i8[i][d] over K = D bytes
+//              (quantizer.rs:382-400): A = the codes unpacked to one byte per dimension,
+//              B = the queries' q_i8 in dimension order.
 //
-// The kept set of each (query, list) pair is the reference's FastScan heap result, found
-// with the same closed form as the SIMT scan (search_kernels.cu) on the 16-bit scores;
-// the rerank epilogue writes (distance key, rank << 48 | FastScan key << 32 | position)
-// of every kept row to the query's candidate region, exactly like the SIMT scan.
+// Each operand row is built once per item: the one-hot rows of the list serve every query
+// of the item, and each query's LUT slab serves every row tile.  The kept set of each
+// (query, list) pair is the reference's FastScan heap result (fastscan.rs:86-146), found
+// with the same closed form as the SIMT scan (search_kernels.cu) on the 16-bit scores; the
+// rerank epilogue writes (distance key, rank << 48 | FastScan key << 32 | position) of every
+// kept row to the query's candidate region, exactly like the SIMT scan.
 //
 // Warp roles (17 warps):
-//   warps 0-7   builders: fetch items, write each 256-byte K step of the A (rows) and B
-//               (queries) operands into a 3-stage ring (128-byte swizzle, K-major), the
-//               global loads of step s+1 issued before the stores of step s
+//   warps 0-7   builders: fetch items (warp 0), then write the operand stages of the item
+//               in MMA order -- per K slab of 128 bytes one B stage (the queries) and T A
+//               stages (the row tiles) -- into two rings (A: kNA x 16 KiB, B: kNB x 16 KiB,
+//               128-byte swizzle, K-major); the global loads of stage g + kPF are in
+//               flight while stage g is written
 //   warps 8-15  epilogue: FastScan scores TMEM -> shared memory, the kept set of each
-//               query, then per rerank tile the distances of the kept rows
+//               query (warp per query), the distances of the kept rows (thread per row)
 //   warp 16     TMEM allocation and the single-thread MMA issuer
-// Hand-offs are mbarriers: stage full (8 builder arrivals) / empty (tcgen05.commit),
-// item slot full / empty, FastScan accumulators full / copied out, and two rerank
-// accumulators full / free, so building, MMAs, selection and epilogues of consecutive
-// tiles and items overlap.  Every wait is bounded (2 s); on expiry the kernel records an
-// error code, every role leaves its loop, and the TMEM is freed.
+// TMEM holds two items' accumulators (256 columns each): item j's FastScan GEMM, then its
+// rerank GEMM (in the same columns once the scores are copied out), while the epilogue
+// finishes item j - 1.  Hand-offs are mbarriers; every wait is bounded (2 s): on expiry
+// the kernel records an error code, every role leaves its loop, and the TMEM is freed.
 #include <cstdint>
 
 #include "common.cuh"
@@ -43,47 +47,47 @@ namespace {
 constexpr int kBuildWarps = 8, kEpiWarps = 8;
 constexpr int kCtrlWarp = kBuildWarps + kEpiWarps;  // 16
 constexpr int kThreads = (kCtrlWarp + 1) * 32;      // 544
+constexpr int kBuildThreads = kBuildWarps * 32;     // 256
 constexpr int kRows = 128;                          // MMA M: list rows per tile
-constexpr int kQ = 32;                              // MMA N: queries per item
-constexpr int kSlab = 128;                          // K bytes per swizzle slab
-constexpr int kStepSlabs = 2;                       // K bytes per pipeline step: 256
-constexpr int kASlab = kRows * kSlab;               // 16 KiB
-constexpr int kBSlab = kQ * kSlab;                  // 4 KiB
-constexpr int kAStage = kASlab * kStepSlabs;        // 32 KiB
-constexpr int kStageBytes = kAStage + kBSlab * kStepSlabs;  // 40 KiB
-constexpr int kNS = 3;                              // stages
-constexpr int kMaxTiles = 8;                        // FastScan accumulators resident in TMEM
-constexpr int kMaxRows = kMaxTiles * kRows;         // 1024
-constexpr int kTmemCols = 512;
-constexpr int kIpCol0 = kMaxTiles * kQ;             // 256 and 288: rerank accumulators
-constexpr int kMaxWords = kMaxRows / 32;            // kept-bitmap words per query
-constexpr int kSlots = 4;                           // item slots in flight
+constexpr int kMaxQ = 128;                          // MMA N limit: queries per item
+constexpr int kHalfCols = 256;                      // TMEM columns of one item
+constexpr int kTmemCols = 2 * kHalfCols;
+constexpr int kSlab = 128;                          // K bytes per stage (one swizzle atom)
+constexpr int kStageBytes = kRows * kSlab;          // 16 KiB
+constexpr int kNA = 4, kNB = 2;                     // ring stages
+constexpr int kScoreCap = kHalfCols * kRows;        // T * 128 * N <= 32768 scores
+constexpr int kWordCap = kScoreCap / 32;
+constexpr int kSlots = 3;                           // items in flight
+constexpr int kPF = 3;                              // stages loaded ahead
 constexpr uint32_t kWaitLimit = 1u << 26;
+static_assert(kMaxQ * 8 <= 4 * kBuildThreads, "a B stage is at most four 16-byte chunks per builder");
+static_assert(kTcMaxRows <= 16 * kRows, "16 row tiles of 16 queries fill one item's TMEM columns");
 
 // kind::i8 instruction descriptor: D s32 (bits 4-5 = 2), A u8 (bits 7-9 = 0), B s8
 // (bits 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kIdescI8 =
-    (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(kQ >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
+__device__ __forceinline__ uint32_t idesc_i8(int n) {
+    return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
+}
 
 struct ItemSlot {
-    int item, n, nq, pad;
+    int item, n, nq, T;  // item < 0: no more work
+    int N, fs, list, pad;
     int64_t beg;
-    int q[kQ], rank[kQ];
-    int64_t base[kQ];  // candidate region of each query's (query, probe) pair
-    QueryParams qp[kQ];
+    int q[kMaxQ], rank[kMaxQ], bsi[kMaxQ];
+    int64_t base[kMaxQ];  // candidate region of each query's (query, probe) pair
+    QueryParams qp[kMaxQ];
 };
 
 struct TcSmem {
-    int16_t sc[kQ][kMaxRows];        // FastScan scores of the current item
-    uint32_t bitmap[kQ][kMaxWords];  // kept rows per query
-    int prefix[kQ][kMaxWords];       // kept rows before each bitmap word
-    int used_fs[kQ];
+    int16_t sc[kScoreCap];      // FastScan scores [query][row], row stride T * 128
+    uint32_t bitmap[kWordCap];  // kept rows [query][word], word stride T * 4
+    int prefix[kWordCap];       // kept rows before each bitmap word
+    int used_fs[kMaxQ];         // the query's kept set came from the FastScan selection
     uint32_t hist[kEpiWarps][256];
     ItemSlot slot[kSlots];
-    uint64_t full[kNS], empty[kNS];
+    uint64_t a_full[kNA], a_empty[kNA], b_full[kNB], b_empty[kNB];
     uint64_t item_full[kSlots], item_empty[kSlots];
-    uint64_t fs_full, fs_free;
-    uint64_t ip_full[2], ip_free[2];
+    uint64_t fs_full[2], fs_free[2], rr_full[2], tmem_free[2];
     uint32_t tmem;
     volatile int abort;
 };
@@ -132,12 +136,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 }
 
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                        uint32_t accumulate) {
+                                        uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdescI8), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -148,13 +152,11 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-          "=r"(v[14]), "=r"(v[15])
+          "=r"(v[7])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -185,40 +187,80 @@ __device__ __forceinline__ bool filtered(const uint64_t* words, int64_t len, int
     return (words[u >> 6] >> (u & 63)) & 1ull;
 }
 
-// Global loads of one builder thread for one pipeline step.
-struct StepLoad {
-    uint32_t sign;  // FastScan: 8 groups of sign nibbles
-    uint4 a[8];     // rerank: the row's codes for this step
-    uint4 b[2];     // the queries' LUT / q_i8 chunks
+// One-hot row chunk of a 4-bit FastScan nibble: byte `nib` of the 16 is 1.
+__device__ __forceinline__ uint4 onehot16(uint32_t nib) {
+    const uint32_t bit = 1u << (8 * (nib & 3u));
+    const uint32_t w = nib >> 2;
+    return make_uint4(w == 0 ? bit : 0u, w == 1 ? bit : 0u, w == 2 ? bit : 0u, w == 3 ? bit : 0u);
+}
+
+// dp4a-layout q_i8 (per 8 dimensions: the 4 even ones, then the 4 odd ones) to dimension
+// order, 16 dimensions.
+__device__ __forceinline__ uint4 q_natural(uint4 v) {
+    return make_uint4(__byte_perm(v.x, v.y, 0x5140), __byte_perm(v.x, v.y, 0x7362),
+                      __byte_perm(v.z, v.w, 0x5140), __byte_perm(v.z, v.w, 0x7362));
+}
+
+// Global loads of one builder thread for one stage.
+struct StageLoad {
+    uint4 v[4];
 };
+
+// Stage g of an item (per K slab: one B stage, then the T A stages; FastScan slabs first):
+// kind 0 FastScan B (LUTs), 1 FastScan A (one-hot rows), 2 rerank B (q_i8), 3 rerank A
+// (codes).
+struct StageRef {
+    int kind, s, t;
+};
+
+__device__ __forceinline__ StageRef stage_of(int g, int per, int fs_stages) {
+    StageRef r;
+    const int fs = g < fs_stages;
+    const int gg = fs ? g : g - fs_stages;
+    r.s = gg / per;
+    const int u = gg - r.s * per;
+    r.t = u - 1;
+    r.kind = (fs ? 0 : 2) + (u > 0 ? 1 : 0);
+    return r;
+}
+
+// Hint: the byte range [p, p + bytes) into L2 (p and bytes multiples of 16, bytes > 0).
+__device__ __forceinline__ void l2_prefetch(const void* p, uint64_t bytes) {
+    const uint64_t cap = 1ull << 20;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p),
+                 "r"((uint32_t)(bytes < cap ? bytes : cap))
+                 : "memory");
+}
 
 __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+    uint8_t* ring_a = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                  ~(uintptr_t)1023);
-    TcSmem& sm = *reinterpret_cast<TcSmem*>(stages + kNS * kStageBytes);
+    uint8_t* ring_b = ring_a + kNA * kStageBytes;
+    TcSmem& sm = *reinterpret_cast<TcSmem*>(ring_b + kNB * kStageBytes);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool l2 = a.metric_l2 != 0;
-    const int sign_bytes = a.D / 8;
-    const int nkc_fs = a.D / 64;                       // K = 16 G = 4 D bytes, 256 per step
-    const int Dp = (a.D + kSlab - 1) / kSlab * kSlab;  // rerank K, zero padded
-    const int slabs_rr = Dp / kSlab;
-    const int nkc_rr = (slabs_rr + kStepSlabs - 1) / kStepSlabs;
+    const int fs_slabs = a.D / 32;                   // K = 16 G = 4 D bytes
+    const int rr_slabs = (a.D + kSlab - 1) / kSlab;  // K = D bytes
 
     if (tid == 0) {
-        for (int s = 0; s < kNS; ++s) {
-            mbar_init(&sm.full[s], kBuildWarps);
-            mbar_init(&sm.empty[s], 1);
+        for (int s = 0; s < kNA; ++s) {
+            mbar_init(&sm.a_full[s], kBuildWarps);
+            mbar_init(&sm.a_empty[s], 1);
+        }
+        for (int s = 0; s < kNB; ++s) {
+            mbar_init(&sm.b_full[s], kBuildWarps);
+            mbar_init(&sm.b_empty[s], 1);
         }
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(&sm.item_full[s], 1);
-            mbar_init(&sm.item_empty[s], 1 + kEpiWarps);
+            mbar_init(&sm.item_empty[s], kBuildWarps + 1 + kEpiWarps);
         }
-        mbar_init(&sm.fs_full, 1);
-        mbar_init(&sm.fs_free, kEpiWarps);
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&sm.ip_full[b], 1);
-            mbar_init(&sm.ip_free[b], kEpiWarps);
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(&sm.fs_full[h], 1);
+            mbar_init(&sm.fs_free[h], kEpiWarps);
+            mbar_init(&sm.rr_full[h], 1);
+            mbar_init(&sm.tmem_free[h], kEpiWarps);
         }
         sm.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -242,13 +284,23 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     if (warp < kBuildWarps) {
         // ------------------------------------------------------------ builders
         const int bt = tid;                            // 0..255
-        const int r = bt & (kRows - 1), h = bt >> 7;   // row, slab of the step
-        uint32_t gstep = 0;
+        const int r = bt & (kRows - 1), hh = bt >> 7;  // A stages: row r, chunks 4hh..4hh+3
+        uint32_t ga = 0, gb = 0;                       // ring positions (the MMA's sequence)
+        int next_it = -1;                              // warp 0 lane 0: the item fetched ahead
+        auto fetch_item = [&]() -> int {
+            for (;;) {
+                const int it = atomicAdd(a.item_counter, 1);
+                if (it >= *a.n_items) return it;
+                // tensor-core items of non-empty lists (an empty list has no candidates)
+                const int4 rec = a.items[it];
+                if (rec.w == 1 && a.list_off[rec.x + 1] > a.list_off[rec.x]) return it;
+            }
+        };
         for (int j = 0;; ++j) {
             const int si = j % kSlots;
             ItemSlot& S = sm.slot[si];
             if (warp == 0) {
-                // publish the next item once every consumer released the slot
+                // publish the next item once every role released the slot
                 bool free_ok = j < kSlots || mbar_wait(&sm.item_empty[si], ((j / kSlots) - 1) & 1, &sm.abort);
                 free_ok = __all_sync(0xffffffffu, free_ok);
                 if (!free_ok) {
@@ -257,12 +309,16 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
                 int it = 0;
                 if (lane == 0) {
-                    for (;;) {
-                        it = atomicAdd(a.item_counter, 1);
-                        if (it >= *a.n_items) break;
-                        const int l = a.items[it].x;
-                        const int64_t n = a.list_off[l + 1] - a.list_off[l];
-                        if (n > a.n_cand && n <= kMaxRows) break;
+                    it = next_it >= 0 ? next_it : fetch_item();
+                    next_it = it < *a.n_items ? fetch_item() : it;
+                    if (next_it < *a.n_items) {
+                        // the following item's list into L2 while this one is scanned
+                        const int l = a.items[next_it].x;
+                        const int64_t b0 = a.list_off[l], n = a.list_off[l + 1] - b0;
+                        l2_prefetch(a.codes + b0 * a.code_bytes, (uint64_t)n * a.code_bytes);
+                        l2_prefetch(a.fs + a.fs_blk_off[l] * (int64_t)a.nchunks * 32,
+                                    (uint64_t)((n + 31) / 32) * a.nchunks * 256);
+                        l2_prefetch(a.meta + b0, (uint64_t)n * 16);
                     }
                 }
                 it = __shfl_sync(0xffffffffu, it, 0);
@@ -271,19 +327,29 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 } else {
                     const int4 rec = a.items[it];
                     const int64_t beg = a.list_off[rec.x];
+                    const int n = (int)(a.list_off[rec.x + 1] - beg);
                     if (lane == 0) {
                         S.item = it;
                         S.beg = beg;
-                        S.n = (int)(a.list_off[rec.x + 1] - beg);
+                        S.n = n;
                         S.nq = rec.z;
+                        S.T = (n + kRows - 1) / kRows;
+                        S.N = (rec.z + 15) & ~15;
+                        S.fs = n > a.n_cand ? 1 : 0;
+                        S.list = rec.x;
                     }
-                    if (lane < rec.z) {
-                        const int2 pr = a.lq[rec.y + lane];
-                        S.q[lane] = pr.x;
-                        S.rank[lane] = pr.y;
-                        S.base[lane] = (int64_t)pr.x * a.q_stride +
-                                       a.pair_off[(int64_t)pr.x * (a.nprobe + 1) + pr.y];
-                        S.qp[lane] = a.qp[pr.x];
+                    for (int i = lane; i < rec.z; i += 32) {
+                        const int2 pr = a.lq[rec.y + i];
+                        S.q[i] = pr.x;
+                        S.rank[i] = pr.y;
+                        S.base[i] = (int64_t)pr.x * a.q_stride + a.pair_off[(int64_t)pr.x * (a.nprobe + 1) + pr.y];
+                        S.qp[i] = a.qp[pr.x];
+                        int b = -1;
+                        if (a.fused && a.bitsets) {
+                            b = a.query_bitset ? a.query_bitset[pr.x] : 0;
+                            if (b < 0 || b >= a.n_bitsets) b = -1;
+                        }
+                        S.bsi[i] = b;
                     }
                 }
                 __syncwarp();
@@ -295,131 +361,151 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 break;
             }
             if (S.item < 0) break;
-            const int n = S.n, nq = S.nq;
+            const int n = S.n, nq = S.nq, T = S.T;
             const int64_t beg = S.beg;
-            const int ntiles = (n + kRows - 1) / kRows;
-            const int nfs = ntiles * nkc_fs, nsteps = nfs + ntiles * nkc_rr;
-            auto load = [&](int st, StepLoad& L) {
-                if (st < nfs) {
-                    const int t = st / nkc_fs, kc = st % nkc_fs;
-                    const int v = t * kRows + r;
-                    L.sign = v < n ? *reinterpret_cast<const uint32_t*>(
-                                         a.signs + (beg + v) * (int64_t)sign_bytes + kc * 8 + h * 4)
-                                   : 0u;
+            const int per = T + 1;
+            const int fs_stages = S.fs ? fs_slabs * per : 0;
+            const int nst = fs_stages + rr_slabs * per;
+            const uint2* fsl = a.fs + a.fs_blk_off[S.list] * (int64_t)a.nchunks * 32;
+            auto load = [&](int g, StageLoad& L) {
+                if (g >= nst) return;
+                const StageRef st = stage_of(g, per, fs_stages);
+                if (st.kind == 0 || st.kind == 2) {
+                    // queries' LUT (kind 0) or q_i8 (kind 2) slab: 16-byte chunk c of query i
 #pragma unroll
-                    for (int m = 0; m < 2; ++m) {
-                        const int idx = bt + m * 256, i = idx >> 4, cc = idx & 15;
-                        L.b[m] = i < nq ? *reinterpret_cast<const uint4*>(
-                                              a.lut + ((int64_t)S.q[i] * a.G + kc * 16 + cc) * 16)
-                                        : make_uint4(0u, 0u, 0u, 0u);
-                    }
-                } else {
-                    const int s2 = st - nfs, t = s2 / nkc_rr, kc = s2 % nkc_rr;
-                    const int v = t * kRows + r;
-                    const int d0 = kc * 256 + h * 128;  // this thread's 128 dimensions
-                    const uint8_t* crow = a.codes + (beg + v) * (int64_t)a.code_bytes;
-                    if (a.nbits == 8) {
-#pragma unroll
-                        for (int u = 0; u < 8; ++u)
-                            L.a[u] = (v < n && d0 + 16 * u < a.D)
-                                         ? *reinterpret_cast<const uint4*>(crow + d0 + 16 * u)
-                                         : make_uint4(0u, 0u, 0u, 0u);
-                    } else {
-#pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            L.a[u] = (v < n && d0 + 32 * u < a.D)
-                                         ? *reinterpret_cast<const uint4*>(crow + d0 / 2 + 16 * u)
-                                         : make_uint4(0u, 0u, 0u, 0u);
-                    }
-#pragma unroll
-                    for (int m = 0; m < 2; ++m) {
-                        const int idx = bt + m * 256, i = idx >> 4, cc = idx & 15;
-                        const int dq = kc * 256 + cc * 16;
-                        L.b[m] = (i < nq && dq < a.D)
-                                     ? *reinterpret_cast<const uint4*>(a.q_i8 + (int64_t)S.q[i] * a.D + dq)
-                                     : make_uint4(0u, 0u, 0u, 0u);
-                    }
-                }
-            };
-            auto build = [&](int st, const StepLoad& L, uint8_t* A) {
-                uint8_t* B = A + kAStage;
-                if (st < nfs) {
-                    // one-hot rows: the 8 groups of this thread's slab, 16 bytes each
-#pragma unroll
-                    for (int jg = 0; jg < 8; ++jg) {
-                        const uint32_t nib = (L.sign >> (4 * jg)) & 15u;
-                        const uint32_t bit = 1u << (8 * (nib & 3u));
-                        uint4 o;
-                        o.x = (nib >> 2) == 0 ? bit : 0u;
-                        o.y = (nib >> 2) == 1 ? bit : 0u;
-                        o.z = (nib >> 2) == 2 ? bit : 0u;
-                        o.w = (nib >> 2) == 3 ? bit : 0u;
-                        *reinterpret_cast<uint4*>(A + h * kASlab + sw_off(r, jg)) = o;
-                    }
-#pragma unroll
-                    for (int m = 0; m < 2; ++m) {
-                        const int idx = bt + m * 256, i = idx >> 4, cc = idx & 15;
-                        uint4 w = L.b[m];
-                        w.x ^= 0x80808080u;  // offset-binary LUT byte -> s8
-                        w.y ^= 0x80808080u;
-                        w.z ^= 0x80808080u;
-                        w.w ^= 0x80808080u;
-                        *reinterpret_cast<uint4*>(B + (cc >> 3) * kBSlab + sw_off(i, cc & 7)) = w;
-                    }
-                } else {
-                    if (a.nbits == 8) {
-#pragma unroll
-                        for (int u = 0; u < 8; ++u)
-                            *reinterpret_cast<uint4*>(A + h * kASlab + sw_off(r, u)) = L.a[u];
-                    } else {  // 4-bit, low nibble = even dimension: 16 code bytes -> 32 dims
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const uint4 c = L.a[u];
-                            const uint32_t lo0 = c.x & 0x0F0F0F0Fu, hi0 = (c.x >> 4) & 0x0F0F0F0Fu;
-                            const uint32_t lo1 = c.y & 0x0F0F0F0Fu, hi1 = (c.y >> 4) & 0x0F0F0F0Fu;
-                            const uint32_t lo2 = c.z & 0x0F0F0F0Fu, hi2 = (c.z >> 4) & 0x0F0F0F0Fu;
-                            const uint32_t lo3 = c.w & 0x0F0F0F0Fu, hi3 = (c.w >> 4) & 0x0F0F0F0Fu;
-                            *reinterpret_cast<uint4*>(A + h * kASlab + sw_off(r, 2 * u)) =
-                                make_uint4(__byte_perm(lo0, hi0, 0x5140), __byte_perm(lo0, hi0, 0x7362),
-                                           __byte_perm(lo1, hi1, 0x5140), __byte_perm(lo1, hi1, 0x7362));
-                            *reinterpret_cast<uint4*>(A + h * kASlab + sw_off(r, 2 * u + 1)) =
-                                make_uint4(__byte_perm(lo2, hi2, 0x5140), __byte_perm(lo2, hi2, 0x7362),
-                                           __byte_perm(lo3, hi3, 0x5140), __byte_perm(lo3, hi3, 0x7362));
+                    for (int m = 0; m < 4; ++m) {
+                        const int idx = bt + m * kBuildThreads, i = idx >> 3, c = idx & 7;
+                        L.v[m] = make_uint4(0u, 0u, 0u, 0u);
+                        if (i < nq) {
+                            const int q = S.q[i];
+                            if (st.kind == 0) {
+                                L.v[m] = __ldg(reinterpret_cast<const uint4*>(
+                                    a.lut + ((int64_t)q * a.G * 16 + st.s * kSlab + c * 16)));
+                            } else if (st.s * kSlab + c * 16 < a.D) {
+                                L.v[m] = __ldg(reinterpret_cast<const uint4*>(
+                                    a.q_i8p + ((int64_t)q * a.D + st.s * kSlab + c * 16)));
+                            }
                         }
                     }
+                } else {
+                    const int v = st.t * kRows + r;
+                    if (v >= n) return;
+                    if (st.kind == 1) {
+                        // sign nibbles of slabs 2c and 2c + 1 of row v (FastScan block layout)
+                        const uint2 w = __ldg(fsl + ((int64_t)(v >> 5) * a.nchunks + (st.s >> 1)) * 32 + (v & 31));
+                        L.v[0].x = w.x;
+                        L.v[0].y = w.y;
+                    } else {
+                        const int d0 = st.s * kSlab + hh * 64;  // this thread's 64 dimensions
+                        if (d0 >= a.D) return;
+                        const uint8_t* crow = a.codes + (beg + v) * (int64_t)a.code_bytes;
+                        if (a.nbits == 8) {
 #pragma unroll
-                    for (int m = 0; m < 2; ++m) {
-                        const int idx = bt + m * 256, i = idx >> 4, cc = idx & 15;
-                        *reinterpret_cast<uint4*>(B + (cc >> 3) * kBSlab + sw_off(i, cc & 7)) = L.b[m];
+                            for (int u = 0; u < 4; ++u)
+                                L.v[u] = __ldg(reinterpret_cast<const uint4*>(crow + d0 + 16 * u));
+                        } else {
+                            L.v[0] = __ldg(reinterpret_cast<const uint4*>(crow + d0 / 2));
+                            L.v[1] = __ldg(reinterpret_cast<const uint4*>(crow + d0 / 2 + 16));
+                        }
                     }
                 }
             };
-            StepLoad cur, nxt;
-            load(0, cur);
-            bool ok = true;
-            for (int st = 0; st < nsteps; ++st, ++gstep) {
-                if (st + 1 < nsteps) load(st + 1, nxt);
-                const uint32_t s = gstep % kNS, use = gstep / kNS;
-                const bool freed = use == 0 || mbar_wait(&sm.empty[s], (use - 1) & 1, &sm.abort);
-                if (!__all_sync(0xffffffffu, freed)) {
-                    ok = false;
-                    break;
+            auto build = [&](const StageRef& st, const StageLoad& L, uint8_t* X) {
+                if (st.kind == 0 || st.kind == 2) {
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        const int idx = bt + m * kBuildThreads, i = idx >> 3, c = idx & 7;
+                        if (i < S.N) {
+                            uint4 w = L.v[m];
+                            if (st.kind == 0) {
+                                // offset-binary LUT byte -> s8 (padding queries read 0 ->
+                                // -128: their accumulator columns are never read)
+                                w.x ^= 0x80808080u;
+                                w.y ^= 0x80808080u;
+                                w.z ^= 0x80808080u;
+                                w.w ^= 0x80808080u;
+                            } else if (a.nbits == 4) {
+                                w = q_natural(w);
+                            }
+                            *reinterpret_cast<uint4*>(X + sw_off(i, c)) = w;
+                        }
+                    }
+                } else {
+                    const int v = st.t * kRows + r;
+                    if (v >= n) return;  // rows past the list: their accumulators are never read
+                    if (st.kind == 1) {
+                        const uint32_t word = (st.s & 1) ? L.v[0].y : L.v[0].x;
+                        const uint32_t bits = word >> (16 * hh);
+#pragma unroll
+                        for (int jg = 0; jg < 4; ++jg)
+                            *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + jg)) = onehot16((bits >> (4 * jg)) & 15u);
+                    } else {
+                        const int d0 = st.s * kSlab + hh * 64;
+                        if (d0 >= a.D) return;
+                        if (a.nbits == 8) {
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + u)) = L.v[u];
+                        } else {  // 4-bit, low nibble = even dimension: 32 code bytes -> 64 dims
+#pragma unroll
+                            for (int u = 0; u < 2; ++u) {
+                                const uint4 c = L.v[u];
+                                const uint32_t lo0 = c.x & 0x0F0F0F0Fu, hi0 = (c.x >> 4) & 0x0F0F0F0Fu;
+                                const uint32_t lo1 = c.y & 0x0F0F0F0Fu, hi1 = (c.y >> 4) & 0x0F0F0F0Fu;
+                                const uint32_t lo2 = c.z & 0x0F0F0F0Fu, hi2 = (c.z >> 4) & 0x0F0F0F0Fu;
+                                const uint32_t lo3 = c.w & 0x0F0F0F0Fu, hi3 = (c.w >> 4) & 0x0F0F0F0Fu;
+                                *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + 2 * u)) =
+                                    make_uint4(__byte_perm(lo0, hi0, 0x5140), __byte_perm(lo0, hi0, 0x7362),
+                                               __byte_perm(lo1, hi1, 0x5140), __byte_perm(lo1, hi1, 0x7362));
+                                *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + 2 * u + 1)) =
+                                    make_uint4(__byte_perm(lo2, hi2, 0x5140), __byte_perm(lo2, hi2, 0x7362),
+                                               __byte_perm(lo3, hi3, 0x5140), __byte_perm(lo3, hi3, 0x7362));
+                            }
+                        }
+                    }
                 }
-                build(st, cur, stages + s * kStageBytes);
+            };
+            // write stage g from cur after issuing the loads of stage g + kPF into pf
+            auto step = [&](int g, StageLoad& cur, StageLoad& pf) -> bool {
+                load(g + kPF, pf);
+                const StageRef st = stage_of(g, per, fs_stages);
+                const bool is_b = (st.kind & 1) == 0;
+                const uint32_t pos = is_b ? gb : ga;
+                const int ns = is_b ? kNB : kNA;
+                const uint32_t s = pos % ns, use = pos / ns;
+                uint64_t* empty = is_b ? &sm.b_empty[s] : &sm.a_empty[s];
+                const bool freed = use == 0 || mbar_wait(empty, (use - 1) & 1, &sm.abort);
+                if (!__all_sync(0xffffffffu, freed)) return false;
+                build(st, cur, (is_b ? ring_b : ring_a) + s * kStageBytes);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.full[s]);
-                cur = nxt;
+                if (lane == 0) mbar_arrive(is_b ? &sm.b_full[s] : &sm.a_full[s]);
+                if (is_b)
+                    ++gb;
+                else
+                    ++ga;
+                return true;
+            };
+            StageLoad L0, L1, L2, L3;
+            load(0, L0);
+            load(1, L1);
+            load(2, L2);
+            bool ok = true;
+            for (int g = 0; g < nst && ok; g += 4) {
+                ok = step(g, L0, L3);
+                if (ok && g + 1 < nst) ok = step(g + 1, L1, L0);
+                if (ok && g + 2 < nst) ok = step(g + 2, L2, L1);
+                if (ok && g + 3 < nst) ok = step(g + 3, L3, L2);
             }
             if (!ok) {
                 fail(6);
                 break;
             }
+            if (lane == 0) mbar_arrive(&sm.item_empty[si]);
         }
     } else if (warp == kCtrlWarp) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            uint32_t gstep = 0, gtile = 0;
+            uint32_t ga = 0, gb = 0;
             for (int j = 0;; ++j) {
                 const int si = j % kSlots;
                 const ItemSlot& S = sm.slot[si];
@@ -428,53 +514,49 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     break;
                 }
                 if (S.item < 0) break;
-                const int ntiles = (S.n + kRows - 1) / kRows;
-                bool ok = true;
-                // FastScan accumulators are free once the epilogue copied the previous item's
-                if (j >= 1 && !mbar_wait(&sm.fs_free, (j - 1) & 1, &sm.abort)) ok = false;
-                for (int t = 0; t < ntiles && ok; ++t)
-                    for (int kc = 0; kc < nkc_fs; ++kc, ++gstep) {
-                        const uint32_t s = gstep % kNS;
-                        if (!mbar_wait(&sm.full[s], (gstep / kNS) & 1, &sm.abort)) {
+                const int T = S.T, N = S.N;
+                const uint32_t idesc = idesc_i8(N);
+                const uint32_t h = j & 1, use = j >> 1;
+                const uint32_t dcol = tmem + h * kHalfCols;
+                bool ok = use == 0 || mbar_wait(&sm.tmem_free[h], (use - 1) & 1, &sm.abort);
+                // one GEMM phase: per slab, the B stage then the T A stages (nk K-steps of 32)
+                auto gemm = [&](int slabs, int k_bytes) {
+                    for (int s = 0; s < slabs && ok; ++s) {
+                        const uint32_t bs = gb % kNB;
+                        if (!mbar_wait(&sm.b_full[bs], (gb / kNB) & 1, &sm.abort)) {
                             ok = false;
                             break;
                         }
-                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                        const uint32_t abase = smem_u32(stages + s * kStageBytes), bbase = abase + kAStage;
-                        for (int sl = 0; sl < kStepSlabs; ++sl)
-#pragma unroll
-                            for (int k4 = 0; k4 < kSlab / 32; ++k4)
-                                umma_i8(tmem + (uint32_t)(t * kQ), sw128_desc(abase + sl * kASlab + k4 * 32),
-                                        sw128_desc(bbase + sl * kBSlab + k4 * 32),
-                                        (kc > 0 || sl > 0 || k4 > 0) ? 1u : 0u);
-                        umma_commit(&sm.empty[s]);
-                    }
-                if (ok) umma_commit(&sm.fs_full);
-                for (int t = 0; t < ntiles && ok; ++t, ++gtile) {
-                    const uint32_t b = gtile & 1u, use = gtile >> 1;
-                    if (use >= 1 && !mbar_wait(&sm.ip_free[b], (use - 1) & 1, &sm.abort)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t dcol = tmem + (uint32_t)(kIpCol0 + b * kQ);
-                    for (int kc = 0; kc < nkc_rr; ++kc, ++gstep) {
-                        const uint32_t s = gstep % kNS;
-                        if (!mbar_wait(&sm.full[s], (gstep / kNS) & 1, &sm.abort)) {
-                            ok = false;
-                            break;
+                        const int nk = min(kSlab, k_bytes - s * kSlab) / 32;
+                        const uint32_t bbase = smem_u32(ring_b + bs * kStageBytes);
+                        for (int t = 0; t < T; ++t) {
+                            const uint32_t as = ga % kNA;
+                            if (!mbar_wait(&sm.a_full[as], (ga / kNA) & 1, &sm.abort)) {
+                                ok = false;
+                                break;
+                            }
+                            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                            const uint32_t abase = smem_u32(ring_a + as * kStageBytes);
+                            for (int k4 = 0; k4 < nk; ++k4)
+                                umma_i8(dcol + (uint32_t)(t * N), sw128_desc(abase + k4 * 32),
+                                        sw128_desc(bbase + k4 * 32), idesc, (s > 0 || k4 > 0) ? 1u : 0u);
+                            umma_commit(&sm.a_empty[as]);
+                            ++ga;
                         }
-                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                        const uint32_t abase = smem_u32(stages + s * kStageBytes), bbase = abase + kAStage;
-                        const int nsl = min(kStepSlabs, slabs_rr - kc * kStepSlabs);
-                        for (int sl = 0; sl < nsl; ++sl)
-#pragma unroll
-                            for (int k4 = 0; k4 < kSlab / 32; ++k4)
-                                umma_i8(dcol, sw128_desc(abase + sl * kASlab + k4 * 32),
-                                        sw128_desc(bbase + sl * kBSlab + k4 * 32),
-                                        (kc > 0 || sl > 0 || k4 > 0) ? 1u : 0u);
-                        umma_commit(&sm.empty[s]);
+                        if (!ok) break;
+                        umma_commit(&sm.b_empty[bs]);
+                        ++gb;
                     }
-                    if (ok) umma_commit(&sm.ip_full[b]);
+                };
+                if (ok && S.fs) {
+                    gemm(fs_slabs, 4 * a.D);
+                    if (ok) umma_commit(&sm.fs_full[h]);
+                    // the rerank reuses the columns once the epilogue copied the scores out
+                    if (ok && !mbar_wait(&sm.fs_free[h], use & 1, &sm.abort)) ok = false;
+                }
+                if (ok) {
+                    gemm(rr_slabs, a.D);
+                    if (ok) umma_commit(&sm.rr_full[h]);
                 }
                 if (!ok) {
                     fail(7);
@@ -489,9 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         // Every failed wait turns into `bad`, which is ORed over the epilogue warps at the
         // next barrier; all of them leave the loop together.
         const int e = warp - kBuildWarps;             // 0..7
-        const int quarter = warp & 3, half = e >> 2;  // TMEM lanes 32*quarter.., queries 16*half..
+        const int quarter = warp & 3, half = e >> 2;  // TMEM lanes 32*quarter.., column half
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        uint32_t gtile = 0;
         for (int j = 0;; ++j) {
             const int si = j % kSlots;
             const ItemSlot& S = sm.slot[si];
@@ -501,23 +582,30 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 break;
             }
             if (S.item < 0) break;
-            const int n = S.n, nq = S.nq;
+            const int n = S.n, nq = S.nq, T = S.T, N = S.N;
             const int64_t beg = S.beg;
-            const int ntiles = (n + kRows - 1) / kRows;
+            const int NP = T * kRows, W = T * 4;  // score row stride, bitmap words per query
+            const uint32_t h = j & 1, use = j >> 1;
+            const uint32_t dcol = tmem + h * kHalfCols + lane_base;
+            const int c_lo = half * (N >> 1), c_hi = c_lo + (N >> 1);
             // FastScan scores: TMEM -> shared memory (16-bit wrap)
-            bad = !__all_sync(0xffffffffu, mbar_wait(&sm.fs_full, j & 1, &sm.abort));
-            if (!bad) {
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                for (int t = 0; t < ntiles; ++t) {
-                    uint32_t v16[16];
-                    tmem_ld16(tmem + lane_base + (uint32_t)(t * kQ + half * 16), v16);
-                    const int v = t * kRows + quarter * 32 + lane;
+            if (S.fs) {
+                bad = !__all_sync(0xffffffffu, mbar_wait(&sm.fs_full[h], use & 1, &sm.abort));
+                if (!bad) {
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    for (int t = 0; t < T; ++t) {
+                        const int v = t * kRows + quarter * 32 + lane;
+                        for (int c = c_lo; c < c_hi; c += 8) {
+                            uint32_t v8[8];
+                            tmem_ld8(dcol + (uint32_t)(t * N + c), v8);
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) sm.sc[half * 16 + jj][v] = (int16_t)v16[jj];
+                            for (int jj = 0; jj < 8; ++jj) sm.sc[(c + jj) * NP + v] = (int16_t)v8[jj];
+                        }
+                    }
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.fs_free[h]);
                 }
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.fs_free);
             }
             if (epi_sync_or(bad)) {
                 fail(8);
@@ -525,12 +613,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             }
             // the kept set of each query (warp per query)
             for (int i = e; i < nq; i += kEpiWarps) {
-                const int q = S.q[i];
-                const uint64_t* bw = nullptr;
-                if (a.fused && a.bitsets) {
-                    const int b = a.query_bitset ? a.query_bitset[q] : 0;
-                    if (b >= 0 && b < a.n_bitsets) bw = a.bitsets + (int64_t)b * a.bitset_words;
-                }
+                const int bsi = S.bsi[i];
+                const uint64_t* bw = bsi >= 0 ? a.bitsets + (int64_t)bsi * a.bitset_words : nullptr;
                 auto live = [&](int v) { return !bw || !filtered(bw, a.bitset_len, a.ids[beg + v]); };
                 int n_live = n;
                 if (bw) {
@@ -538,21 +622,23 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     for (int v = lane; v < n; v += 32) c += live(v) ? 1 : 0;
                     n_live = warp_sum(c);
                 }
-                const int16_t* s = sm.sc[i];
-                const int npad = ntiles * kRows;
+                const int16_t* sv = sm.sc + i * NP;
+                uint32_t* bm = sm.bitmap + i * W;
+                int* px = sm.prefix + i * W;
                 int n_c = 0;
-                if (n_live > a.n_cand) {
+                if (S.fs && n_live > a.n_cand) {
                     // s* = n_cand-th largest score among live rows (key = 32767 - score); the
                     // kept set is every row above s* plus the s*-rows the reference's heap keeps
                     auto key_at = [&](int v, uint32_t& k) {
                         if (!live(v)) return false;
-                        k = (uint32_t)(32767 - (int)s[v]);
+                        k = (uint32_t)(32767 - (int)sv[v]);
                         return true;
                     };
-                    int c_gt = 0;
-                    const uint32_t tau = warp_radix_kth(n, a.n_cand, key_at, sm.hist[e], &c_gt);
-                    int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = 0;
-                    for (int base = 0; base < n; base += 32) {
+                    int c_gt = 0, c_eq = 0;
+                    const uint32_t tau = warp_radix_kth16(n, a.n_cand, key_at, sm.hist[e], &c_gt, &c_eq);
+                    // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
+                    int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = c_gt;
+                    for (int base = 0; c_gt + c_eq != a.n_cand && base < n; base += 32) {
                         const int v = base + lane;
                         uint32_t k = 0xFFFFFFFFu;
                         const bool valid = v < n && key_at(v, k);
@@ -571,9 +657,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         cnt_ge += c;
                         cnt_gt += __popc(bgt);
                     }
-                    const int m_drop = c_gt - gt_f;
+                    const int m_drop = c_gt - gt_f;  // lowest-index ties evicted by later rows
                     int eq_seen = 0;
-                    for (int base = 0; base < npad; base += 32) {
+                    for (int base = 0; base < NP; base += 32) {
                         const int v = base + lane;
                         uint32_t k = 0xFFFFFFFFu;
                         const bool valid = v < n && key_at(v, k);
@@ -584,67 +670,73 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         const bool keep = gt || (eq && eq_rank > m_drop);
                         const unsigned bk = __ballot_sync(0xffffffffu, keep);
                         if (lane == 0) {
-                            sm.bitmap[i][base >> 5] = bk;
-                            sm.prefix[i][base >> 5] = n_c;
+                            bm[base >> 5] = bk;
+                            px[base >> 5] = n_c;
                         }
                         n_c += __popc(bk);
                         eq_seen += __popc(beq);
                     }
                     if (lane == 0) sm.used_fs[i] = 1;
                 } else {
-                    for (int base = 0; base < npad; base += 32) {
+                    // every live row is kept, in list order
+                    for (int base = 0; base < NP; base += 32) {
                         const int v = base + lane;
                         const unsigned bk = __ballot_sync(0xffffffffu, v < n && live(v));
                         if (lane == 0) {
-                            sm.bitmap[i][base >> 5] = bk;
-                            sm.prefix[i][base >> 5] = n_c;
+                            bm[base >> 5] = bk;
+                            px[base >> 5] = n_c;
                         }
                         n_c += __popc(bk);
                     }
                     if (lane == 0) sm.used_fs[i] = 0;
                 }
                 n_c = min(n_c, a.n_cand);
-                // unused entries of the pair's region (rows removed by the filter)
+                // unused entries of the pair's region of min(|list|, n_cand) entries (rows
+                // removed by the filter)
                 const int64_t rb = S.base[i];
-                for (int jj = n_c + lane; jj < a.n_cand; jj += 32) {
+                const int cap = min(n, a.n_cand);
+                for (int jj = n_c + lane; jj < cap; jj += 32) {
                     a.cand_tie[rb + jj] = ~0ull;
                     a.cand_key[rb + jj] = 0xFFFFFFFFu;
                 }
             }
-            if (epi_sync_or(false)) break;
-            // rerank epilogue per tile: distances of the kept rows
-            for (int t = 0; t < ntiles && !bad; ++t, ++gtile) {
-                const uint32_t b = gtile & 1u, use = gtile >> 1;
-                if (!__all_sync(0xffffffffu, mbar_wait(&sm.ip_full[b], use & 1, &sm.abort))) {
-                    bad = true;
-                    break;
-                }
+            bad = epi_sync_or(false);
+            // rerank epilogue: thread per row, the distances of the kept (query, row) pairs
+            if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait(&sm.rr_full[h], use & 1, &sm.abort));
+            if (!bad) {
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                uint32_t ip[16];
-                tmem_ld16(tmem + lane_base + (uint32_t)(kIpCol0 + b * kQ + half * 16), ip);
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.ip_free[b]);
-                const int v = t * kRows + quarter * 32 + lane;
-                if (v < n) {
-                    const float4 m = __ldg(a.meta + beg + v);
-                    const int wi = v >> 5;
-                    const uint32_t below = (1u << (v & 31)) - 1u;
-#pragma unroll 4
-                    for (int jj = 0; jj < 16; ++jj) {
-                        const int i = half * 16 + jj;
-                        if (i >= nq) break;
-                        const uint32_t word = sm.bitmap[i][wi];
-                        if (!((word >> (v & 31)) & 1u)) continue;
-                        const int pos = sm.prefix[i][wi] + __popc(word & below);
-                        if (pos >= a.n_cand) continue;
-                        const uint32_t fkey = sm.used_fs[i] ? (uint32_t)(32767 - (int)sm.sc[i][v]) : 0u;
-                        const float dist = rerank_distance((int)ip[jj], m, S.qp[i], a.nbits, l2);
-                        const int64_t dst = S.base[i] + pos;
-                        a.cand_key[dst] = total_order_key(dist);
-                        a.cand_tie[dst] = ((uint64_t)S.rank[i] << 48) | ((uint64_t)fkey << 32) | (uint32_t)v;
+                for (int t = 0; t < T; ++t) {
+                    const int v = t * kRows + quarter * 32 + lane;
+                    const bool row_ok = v < n;
+                    const float4 m = row_ok ? __ldg(a.meta + beg + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const int wi = t * 4 + quarter;
+                    const uint32_t below = (1u << lane) - 1u;
+                    for (int c = c_lo; c < c_hi; c += 8) {
+                        uint32_t ip[8];
+                        tmem_ld8(dcol + (uint32_t)(t * N + c), ip);
+                        if (!row_ok) continue;
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) {
+                            const int i = c + jj;
+                            if (i >= nq) break;
+                            const uint32_t word = sm.bitmap[i * W + wi];
+                            if (!((word >> lane) & 1u)) continue;
+                            const int pos = sm.prefix[i * W + wi] + __popc(word & below);
+                            if (pos >= a.n_cand) continue;
+                            const int score = sm.sc[i * NP + v];
+                            const bool ufs = sm.used_fs[i] != 0;
+                            const uint32_t fkey = ufs ? (uint32_t)(32767 - score) : 0u;
+                            const float dist = rerank_distance((int)ip[jj], m, S.qp[i], a.nbits, l2);
+                            const int64_t dst = S.base[i] + pos;
+                            a.cand_key[dst] = total_order_key(dist);
+                            a.cand_tie[dst] = ((uint64_t)S.rank[i] << 48) | ((uint64_t)fkey << 32) | (uint32_t)v;
+                            if (a.cand_dbg) a.cand_dbg[dst] = make_int2((int)ip[jj], ufs ? score : INT32_MIN);
+                        }
                     }
                 }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.tmem_free[h]);
             }
             // the next item rewrites the scores and bitmaps
             if (epi_sync_or(bad)) {
@@ -666,9 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
 
 }  // namespace
 
-int scan_tc_max_rows() { return kMaxRows; }
-
-size_t scan_tc_smem_bytes() { return (size_t)kNS * kStageBytes + sizeof(TcSmem) + 1024; }
+size_t scan_tc_smem_bytes() { return (size_t)(kNA + kNB) * kStageBytes + sizeof(TcSmem) + 1024; }
 
 void launch_scan_tc(const TcScanArgs& a, int grid, cudaStream_t s) {
     const size_t smem = scan_tc_smem_bytes();

@@ -1126,9 +1126,24 @@ __global__ void count_lists_kernel(const int32_t* __restrict__ probes, int64_t n
     }
 }
 
+// Queries per item of list l: tensor-core items for lists of at most tc_max_rows rows,
+// SIMT items of qpi queries otherwise.
+__device__ __forceinline__ int list_item_queries(const int64_t* list_off, int l, int tc_max_rows,
+                                                 int qpi, int* kind) {
+    const int64_t n = list_off[l + 1] - list_off[l];
+    if (tc_max_rows > 0 && n <= tc_max_rows) {
+        *kind = 1;
+        return tc_queries_per_item(n);
+    }
+    *kind = 0;
+    return qpi;
+}
+
 // Single CTA of 1024 threads: exclusive scans of cnt and of items-per-list.
 __global__ void __launch_bounds__(1024) prefix_lists_kernel(const int* __restrict__ cnt, int nlist,
-                                                          int qpi, int* __restrict__ lq_off,
+                                                          const int64_t* __restrict__ list_off,
+                                                          int tc_max_rows, int qpi,
+                                                          int* __restrict__ lq_off,
                                                           int* __restrict__ item_off,
                                                           int* __restrict__ n_items) {
     __shared__ int wsum_a[32], wsum_b[32];
@@ -1139,7 +1154,9 @@ __global__ void __launch_bounds__(1024) prefix_lists_kernel(const int* __restric
     for (int base = 0; base < nlist; base += 1024) {
         const int l = base + threadIdx.x;
         const int a = l < nlist ? cnt[l] : 0;
-        const int b = (a + qpi - 1) / qpi;
+        int kind = 0;
+        const int per = l < nlist ? list_item_queries(list_off, l, tc_max_rows, qpi, &kind) : 1;
+        const int b = (a + per - 1) / per;
         const int ia = warp_inclusive_scan(a), ib = warp_inclusive_scan(b);
         if (lane == 31) {
             wsum_a[w] = ia;
@@ -1189,12 +1206,15 @@ __global__ void scatter_pairs_kernel(const int32_t* __restrict__ probes, int64_t
 }
 
 __global__ void make_items_kernel(const int* __restrict__ cnt, const int* __restrict__ lq_off,
-                                  const int* __restrict__ item_off, int nlist, int qpi,
+                                  const int* __restrict__ item_off, int nlist,
+                                  const int64_t* __restrict__ list_off, int tc_max_rows, int qpi,
                                   int4* __restrict__ items) {
     for (int l = blockIdx.x * blockDim.x + threadIdx.x; l < nlist; l += gridDim.x * blockDim.x) {
         const int c = cnt[l];
+        int kind = 0;
+        const int per = list_item_queries(list_off, l, tc_max_rows, qpi, &kind);
         int o = item_off[l];
-        for (int s = 0; s < c; s += qpi) items[o++] = make_int4(l, lq_off[l] + s, min(qpi, c - s), 0);
+        for (int s = 0; s < c; s += per) items[o++] = make_int4(l, lq_off[l] + s, min(per, c - s), kind);
     }
 }
 
@@ -1492,7 +1512,7 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
         const int l = it.x;
         const int64_t beg = a.list_off[l];
         const int n = (int)(a.list_off[l + 1] - beg);
-        if (n > a.n_cand && n <= a.tc_rows) continue;  // scanned by scan_tc_kernel
+        if (it.w != 0) continue;  // a tensor-core item (scan_tc_kernel)
         // the item's queries, staged once (no dependent global loads in the rerank loops)
         if (tid < it.z) {
             const int2 pr = a.lq[it.y + tid];
@@ -1543,9 +1563,10 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                         a.cand_tie[dst] = ~0ull;
                     } else {
                         const float4 m = __ldg(a.meta + row);
-                        a.cand_key[dst] =
-                            total_order_key(rerank_distance(lane < 4 ? ipx : ipy, m, sm.qp[i], a.nbits, l2));
+                        const int ipv = lane < 4 ? ipx : ipy;
+                        a.cand_key[dst] = total_order_key(rerank_distance(ipv, m, sm.qp[i], a.nbits, l2));
                         a.cand_tie[dst] = ((uint64_t)sm.rank[i] << 48) | (uint32_t)v;
+                        if (a.cand_dbg) a.cand_dbg[dst] = make_int2(ipv, INT32_MIN);
                     }
                 }
             }
@@ -1735,6 +1756,7 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                             if (pos < a.n_cand) {
                                 my_tie[pos] = rank_bits | ((uint64_t)k << 32) | (uint32_t)v;
                                 if (my_sv) my_sv[pos] = (uint16_t)v;
+                                if (a.cand_dbg) a.cand_dbg[rbase + pos].y = 32767 - (int)k;
                             }
                         }
                         n_c += __popc(bk);
@@ -1749,6 +1771,7 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                             const int pos = n_c + __popc(bk & lanemask_lt());
                             my_tie[pos] = rank_bits | (uint32_t)v;
                             if (my_sv) my_sv[pos] = (uint16_t)v;
+                            if (a.cand_dbg) a.cand_dbg[rbase + pos].y = INT32_MIN;
                         }
                         n_c += __popc(bk);
                     }
@@ -1806,8 +1829,9 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                     const int jl = j0 + lane;
                     if (lane < 8 && jl < nc_i) {
                         const float4 m = __ldg(a.meta + beg + row_of(jl));
-                        a.cand_key[rb + jl] = total_order_key(
-                            rerank_distance(lane < 4 ? ipx : ipy, m, qpi, a.nbits, l2));
+                        const int ipv = lane < 4 ? ipx : ipy;
+                        a.cand_key[rb + jl] = total_order_key(rerank_distance(ipv, m, qpi, a.nbits, l2));
+                        if (a.cand_dbg) a.cand_dbg[rb + jl].x = ipv;
                     }
                 }
             }
@@ -2215,16 +2239,19 @@ void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, i
 }
 
 void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist,
-                        const uint8_t* owned, int qpi, int* cnt, int* cursor, int* lq_off,
-                        int* item_off, int* n_items, int2* lq, int4* items, cudaStream_t s) {
+                        const uint8_t* owned, const int64_t* list_off, int tc_max_rows, int qpi,
+                        int* cnt, int* cursor, int* lq_off, int* item_off, int* n_items, int2* lq,
+                        int4* items, cudaStream_t s) {
     cudaMemsetAsync(cnt, 0, sizeof(int) * nlist, s);
     cudaMemsetAsync(cursor, 0, sizeof(int) * nlist, s);
     const int64_t pairs = nq * nprobe;
     const int blocks = (int)std::min<int64_t>((pairs + 255) / 256, 4096);
     count_lists_kernel<<<blocks, 256, 0, s>>>(probes, pairs, nlist, owned, cnt);
-    prefix_lists_kernel<<<1, 1024, 0, s>>>(cnt, nlist, qpi, lq_off, item_off, n_items);
+    prefix_lists_kernel<<<1, 1024, 0, s>>>(cnt, nlist, list_off, tc_max_rows, qpi, lq_off, item_off,
+                                           n_items);
     scatter_pairs_kernel<<<blocks, 256, 0, s>>>(probes, nq, nprobe, nlist, owned, lq_off, cursor, lq);
-    make_items_kernel<<<(nlist + 255) / 256, 256, 0, s>>>(cnt, lq_off, item_off, nlist, qpi, items);
+    make_items_kernel<<<(nlist + 255) / 256, 256, 0, s>>>(cnt, lq_off, item_off, nlist, list_off,
+                                                          tc_max_rows, qpi, items);
 }
 
 size_t scan_smem_bytes(int D) {

@@ -297,6 +297,37 @@ class IvfUsqIndex:
                     centroid_score=sc[:, 1], q_norm_sq=sc[:, 2], lut_scale=sc[:, 3],
                     q_i8_sum=sc[:, 4].copy().view(np.int32))
 
+    def debug_candidates(self, query: np.ndarray, k: int, nprobe: int, filter_mode: int = FILTER_NONE,
+                         bitsets: np.ndarray | None = None, bitset_len: int = 0,
+                         query_bitset: np.ndarray | None = None, cap: int = 1 << 16) -> list:
+        """The list scan's kept candidates of each query, in the reference's candidate order
+        (the oracle's `candidates` format: list, local, fs, int_ip, dist per query)."""
+        q = np.ascontiguousarray(query, np.float32).reshape(-1, self.config.dim)
+        nq = q.shape[0]
+        counts = np.zeros(nq, np.int64)
+        lists = np.zeros((nq, cap), np.int32)
+        local = np.zeros((nq, cap), np.int64)
+        fs = np.zeros((nq, cap), np.int32)
+        iip = np.zeros((nq, cap), np.int32)
+        dist = np.zeros((nq, cap), np.float32)
+        bp, nbs, qbp = None, 0, None
+        if bitsets is not None and filter_mode != FILTER_NONE:
+            bitsets = np.ascontiguousarray(bitsets, np.uint64)
+            if bitsets.ndim == 1:
+                bitsets = bitsets[None, :]
+            nbs = bitsets.shape[0]
+            bp = _p(bitsets, L.u64p)
+            if query_bitset is not None:
+                query_bitset = np.ascontiguousarray(query_bitset, np.int32)
+                qbp = _p(query_bitset, L.i32p)
+        _check(L.lib().hanns_gpu_ivf_usq_debug_candidates(
+            self._h, _p(q, L.f32p), nq, max(int(k), 1), max(int(nprobe), 1),
+            filter_mode if bp is not None else 0, bp, bitset_len, nbs, qbp, cap,
+            _p(counts, L.i64p), _p(lists, L.i32p), _p(local, L.i64p), _p(fs, L.i32p),
+            _p(iip, L.i32p), _p(dist, L.f32p)), "debug_candidates")
+        return [dict(list=lists[i, :c], local=local[i, :c], fs=fs[i, :c], int_ip=iip[i, :c],
+                     dist=dist[i, :c]) for i, c in enumerate(counts)]
+
     # ------------------------------------------------------------ misc
     def set_nprobe(self, nprobe: int):
         """set_nprobe (src/faiss/ivf_usq.rs:224-226): clamp to 1..=nlist."""

@@ -251,6 +251,21 @@ int32_t hanns_gpu_ivf_usq_debug_query(HannsIvfUsqHandle* h, const float* queries
                                       int32_t nprobe, int32_t* probes, float* q_rot, int8_t* q_i8,
                                       int8_t* lut, float* scalars);
 
+/* Debug: the list scan's kept candidates of each query -- the reference's candidate vector
+ * of search_single (src/faiss/ivf_usq.rs:547-588: probe order, FastScan order inside a list
+ * that ran it, fastscan.rs:140-144) -- written at q * cap: list, position in the list,
+ * FastScan score (INT32_MIN where FastScan did not select the row), int_ip (quantizer.rs
+ * :382-400) and distance; counts[q] = entries of query q.  filter_mode as in
+ * hanns_gpu_ivf_usq_search (fused filtering removes rows before the selection).  All
+ * queries must fit one internal batch; HANNS_INVALID_ARG / an error if cap is too small. */
+int32_t hanns_gpu_ivf_usq_debug_candidates(HannsIvfUsqHandle* h, const float* queries, int64_t nq,
+                                           int32_t k, int32_t nprobe, int32_t filter_mode,
+                                           const uint64_t* bitsets, int64_t bitset_len,
+                                           int64_t n_bitsets, const int32_t* query_bitset,
+                                           int64_t cap, int64_t* counts, int32_t* lists,
+                                           int64_t* local, int32_t* fs, int32_t* int_ip,
+                                           float* dists);
+
 /* Multi-GPU list sharding: keep only lists l with owner[l] == rank, where owner is a
  * longest-processing-time assignment of lists (by size) to world ranks.  Search then
  * returns this shard's top-k with merge keys. */

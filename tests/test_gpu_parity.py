@@ -493,16 +493,17 @@ def test_config_8bit_k100_deletion_bitsets(gpu, oracle_mod):
 
 
 def test_config_3072_dims_8bit(gpu, oracle_mod):
-    """The shape of the 3,072-dimension configuration (8-bit codes, inner product, k = 10,
-    nprobe 24 of 32 lists) on a GPU-built index: D > 1024 takes the 8 x 8 rotation tiles
-    and the rerank without prefetched code registers."""
+    """The shape of the 3,072-dimension configuration (8-bit codes, inner product, k = 10)
+    on a GPU-built index: 12 lists of ~500 rows, so that lists exceed the 8-bit n_cand of
+    300 and FastScan runs (nprobe 8); D > 1024 takes the 8 x 8 rotation tiles."""
     from hanns_b200.ivf_usq import SearchRequest
     from tests.golden.make_golden import mixture
     O = oracle_mod
-    idx, rng = _gpu_built(3072, 32, 8, 1, 6000, 16, 0.4, 3)
+    idx, rng = _gpu_built(3072, 12, 8, 1, 6000, 16, 0.4, 3)
     art = idx.export_artifact()
+    assert (np.diff(art["list_offsets"]) > O.n_candidates(8, 10)).sum() >= 4
     q, _ = mixture(rng, 64, 3072, 16, 0.4, True)
-    e_ids, e_d, _ = O.OracleIndex(art).search(q, 10, 24)
-    r = idx.search(q, SearchRequest(top_k=10, nprobe=24))
+    e_ids, e_d, _ = O.OracleIndex(art).search(q, 10, 8)
+    r = idx.search(q, SearchRequest(top_k=10, nprobe=8))
     assert np.array_equal(r.ids.reshape(e_ids.shape), e_ids)
     assert bits_eq(r.distances.reshape(e_ids.shape), e_d)
