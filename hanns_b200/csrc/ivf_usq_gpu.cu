@@ -361,16 +361,12 @@ void IvfUsqGpu::train(const float* h_data, int64_t n, int kmeans_iters, uint64_t
     std::vector<float> h_shift(nlist_);
     std::vector<int32_t> h_assign;
     std::vector<float> row(dim_);
-    const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(n, (1ll << 28) / nlist_));
-    DevBuf<float> dist;
-    dist.reserve((size_t)chunk * nlist_);
     constexpr float kTolerance = 1e-2f;  // KMeans::new (kmeans.rs:44-56)
     for (int it = 0; it < kmeans_iters; ++it) {
-        for (int64_t b = 0; b < n; b += chunk) {
-            const int64_t m = std::min(chunk, n - b);
-            launch_coarse_l2(x.p + b * dim_, m, centroids_.p, nlist_, dim_, dist.p, stream_);
-            launch_argmin_rows(dist.p, m, nlist_, assign.p + b, stream_);
-        }
+        // nearest centroid of every row: the search's coarse step with one probe (the
+        // lowest id among equally near centroids, as a strict-less argmin keeps)
+        update_centroid_norms();
+        coarse_probes(x.p, n, 1, assign.p, stream_);
         HANNS_CUDA_OK(cudaMemsetAsync(sums.p, 0, sizeof(long long) * nlist_ * dim_, stream_));
         HANNS_CUDA_OK(cudaMemsetAsync(counts.p, 0, sizeof(int) * nlist_, stream_));
         launch_kmeans_accumulate(x.p, n, dim_, assign.p, sums.p, counts.p, stream_);
@@ -428,7 +424,6 @@ void IvfUsqGpu::add(const float* h_data, int64_t n, const int64_t* h_ids) {
     const int64_t chunk = 65536;
     DevBuf<float> x, res, nsq;
     DevBuf<float> rot;  // chunk*D floats followed by chunk*D code bytes (encode scratch)
-    DevBuf<float> dist;
     DevBuf<int32_t> asg;
     DevBuf<uint8_t> ncodes, nsigns;
     DevBuf<float4> nmeta;
@@ -436,8 +431,6 @@ void IvfUsqGpu::add(const float* h_data, int64_t n, const int64_t* h_ids) {
     nsigns.reserve((size_t)n * (D_ / 8));
     nmeta.reserve((size_t)n);
     asg.reserve((size_t)n);
-    const int64_t cchunk = std::max<int64_t>(1, std::min<int64_t>(chunk, (1ll << 28) / nlist_));
-    dist.reserve((size_t)cchunk * nlist_);
     for (int64_t b = 0; b < n; b += chunk) {
         const int64_t m = std::min(chunk, n - b);
         h2d(x, h_data + b * dim_, (size_t)m * dim_, stream_);
@@ -449,11 +442,9 @@ void IvfUsqGpu::add(const float* h_data, int64_t n, const int64_t* h_ids) {
         launch_rotate(res.p, m, D_, D_, Pc_.p, rot.p, stream_);
         launch_encode_rotated(rot.p, m, D_, nbits_, nsq.p, ncodes.p + b * code_bytes_,
                               nsigns.p + b * (D_ / 8), nmeta.p + b, stream_);
-        for (int64_t c = 0; c < m; c += cchunk) {
-            const int64_t mm = std::min(cchunk, m - c);
-            launch_coarse_l2(x.p + c * dim_, mm, centroids_.p, nlist_, dim_, dist.p, stream_);
-            launch_argmin_rows(dist.p, mm, nlist_, asg.p + b + c, stream_);
-        }
+        // nearest centroid (find_best_centroid, ivf_usq.rs:611-625): the search's coarse
+        // step with one probe -- the same centroid, lowest id among equally near ones
+        coarse_probes(x.p, m, 1, asg.p + b, stream_);
         HANNS_CUDA_OK(cudaGetLastError());
     }
     std::vector<int32_t> h_asg(n);

@@ -1785,7 +1785,9 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
                 if (lane == 0) sm.nc[w] = n_c;
             }
             // a full group reranks warp by warp the query each warp just selected (its own
-            // sm.nc / sv / ties): the warp only waits for itself
+            // sm.nc / sv / ties): the warp only waits for itself.  This holds because a full
+            // group has one warp per query (wpq = kScanWarps / nq_here = 1, so iq == w
+            // below); a different warp-to-query mapping needs the block barrier back.
             if (nq_here == kScanWarps)
                 __syncwarp();
             else
@@ -1796,7 +1798,7 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
             // j = part*8 + 0..7, part = w % wpq, stepping by wpq*8: groups of 8 lanes take
             // j0 + grp and j0 + 4 + grp (their code loads issued together), then lanes 0-7
             // each finish one of the 8 (distance, key store) in parallel
-            const int wpq = kScanWarps / nq_here;
+            const int wpq = kScanWarps / nq_here;  // 1 for a full group: iq == w
             const int iq = w / wpq, part = w - iq * wpq;
             if (iq < nq_here) {
                 const int nc_i = sm.nc[iq];

@@ -56,3 +56,19 @@ def test_static_scratch_coarse_probes_match_search_path():
     assert rc == 2
     assert "scratch" in _lib.last_error()
     assert int(out.min()) == -7 and int(out.max()) == -7
+    # every device that loads the library has its own copy of the scratch array: with a
+    # second GPU, one call with that device current (its own queries and centroids) equals
+    # the search path of an index living on that device
+    if L.hanns_gpu_device_count() >= 2:
+        idx1 = IvfUsqIndex.from_artifact(art, device=1)
+        qn = z["queries"][:64].astype(np.float32)
+        expected = idx1.debug_query(qn, 6)["probes"]
+        with torch.cuda.device(1):
+            q1 = torch.from_numpy(qn).cuda(1)
+            c1 = torch.from_numpy(np.ascontiguousarray(art["centroids"], np.float32)).cuda(1)
+            o1 = torch.full((64, 6), -7, dtype=torch.int32, device="cuda:1")
+            rc = L.hanns_gpu_coarse_probes_static(q1.data_ptr(), 64, c1.data_ptr(), nlist, d, 6,
+                                                  o1.data_ptr(), torch.cuda.current_stream(1).cuda_stream)
+            assert rc == 0, _lib.last_error()
+            torch.cuda.synchronize(1)
+        assert np.array_equal(o1.cpu().numpy(), expected)
