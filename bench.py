@@ -54,11 +54,13 @@ WORKLOADS = {
     # the 8x-compression variant of D: 4-bit codes, FastScan runs on lists above 150 rows
     "D4": dict(n=260_000, d=3072, comps=256, sigma=0.4, nq=5_000, nlist=1024, nprobe=24, k=10,
                nbits=4, metric=1, seed=3, normalise=True),
-    # scale-out shape: one step is one 16,384-query batch of the 100,000-query set; every
-    # list is at most n_cand = 1,500 rows, so FastScan never runs and the rerank is the scan
+    # scale-out shape: a step is one query batch of 16,384 (the configuration's batch size
+    # for its 100,000-query set); lists average ~305 rows, below n_cand = 1,500, so
+    # FastScan never runs and the rerank is the whole scan.  k-means on 16 rows per list
+    # (1 Mi rows), 10 iterations: the build is not timed.
     "E": dict(n=20_000_000, d=768, comps=16384, sigma=0.5, nq=16_384, nlist=65536, nprobe=64,
               k=100, nbits=4, metric=1, seed=19, normalise=True, train_per_list=16,
-              kmeans_iters=10, query_set=100_000),
+              kmeans_iters=10),
 }
 TRAIN_ROWS_PER_LIST = 64
 KMEANS_ITERS = 25  # KMeans::new max_iter (src/quantization/kmeans.rs:44-56), early stop at shift < 1e-2
@@ -125,8 +127,8 @@ def extra_queries(w, device, r):
     return _mixture_draw(w, centres, g2, w["nq"])
 
 
-def exact_topk(base, queries, k, metric, base_chunk=1 << 22):
-    """Exact fp32 top-k ids (no TF32), base rows taken 4 Mi at a time."""
+def exact_topk(base, queries, k, metric, base_chunk=1 << 20):
+    """Exact fp32 top-k ids (no TF32), base rows taken 1 Mi at a time."""
     import torch
     torch.backends.cuda.matmul.allow_tf32 = False
     out = []
