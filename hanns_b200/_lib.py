@@ -134,6 +134,8 @@ SIGNATURES = [
     ("hanns_gpu_ivf_usq_debug_candidates", C.c_int32,
      [vp, f32p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, u64p, C.c_int64, C.c_int64, i32p,
       C.c_int64, i64p, i32p, i64p, i32p, i32p, f32p]),
+    ("hanns_gpu_ivf_usq_set_scan_wait_ns", C.c_int32, [vp, C.c_uint64]),
+    ("hanns_gpu_debug_inject_fault", C.c_int32, [C.c_char_p]),
     ("hanns_gpu_ivf_usq_shard", C.c_int32, [vp, C.c_int32, C.c_int32]),
     ("hanns_gpu_ivf_usq_search_shard_device", C.c_int32,
      [vp, vp, C.c_int64, C.c_int32, C.c_int32, vp, vp, vp, vp]),

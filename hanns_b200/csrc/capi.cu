@@ -673,6 +673,27 @@ int32_t hanns_gpu_ivf_usq_debug_candidates(HannsIvfUsqHandle* h, const float* qu
     });
 }
 
+int32_t hanns_gpu_ivf_usq_set_scan_wait_ns(HannsIvfUsqHandle* h, uint64_t ns) {
+    if (!h || ns == 0) return HANNS_INVALID_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->idx->mutex());
+        h->idx->set_scan_wait_ns(ns);
+    });
+}
+
+int32_t hanns_gpu_debug_inject_fault(const char* what) {
+    if (!what) return HANNS_INVALID_ARG;
+    int mask = 0;
+    if (std::strcmp(what, "alloc") == 0)
+        mask = hanns::kFaultAlloc;
+    else if (std::strcmp(what, "h2d") == 0)
+        mask = hanns::kFaultH2D;
+    else if (std::strcmp(what, "none") != 0)
+        return HANNS_INVALID_ARG;
+    hanns::set_fault_injection(mask);
+    return HANNS_OK;
+}
+
 int32_t hanns_gpu_ivf_usq_shard(HannsIvfUsqHandle* h, int32_t rank, int32_t world) {
     if (!h) return HANNS_INVALID_ARG;
     return guarded([&] {

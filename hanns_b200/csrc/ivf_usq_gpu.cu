@@ -2,6 +2,8 @@
 #include "ivf_usq_gpu.h"
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -48,7 +50,19 @@ int64_t n_candidates(int nbits, int64_t k) {
 template <class T>
 void h2d(DevBuf<T>& b, const T* src, size_t count, cudaStream_t s) {
     b.reserve(count);
+    if (count && fault_injected(kFaultH2D))
+        throw CudaError(cudaErrorInvalidValue, "cudaMemcpyAsync (injected host-to-device fault)",
+                        __FILE__, __LINE__);
     if (count) HANNS_CUDA_OK(cudaMemcpyAsync(b.p, src, count * sizeof(T), cudaMemcpyHostToDevice, s));
+}
+
+std::atomic<int>& fault_mask() {
+    static std::atomic<int> m{[] {
+        const char* e = std::getenv("HANNS_GPU_FAULT");
+        if (!e) return 0;
+        return (std::strcmp(e, "alloc") == 0 ? kFaultAlloc : 0) | (std::strcmp(e, "h2d") == 0 ? kFaultH2D : 0);
+    }()};
+    return m;
 }
 
 constexpr int kQueriesPerItem = 32;
@@ -57,6 +71,9 @@ constexpr int kQueriesPerItem = 32;
 
 // Entries of one query's candidate region: the probes' min(|list|, n_cand) summed is at
 // most nprobe * min(n_cand, longest list) and at most the index size.
+bool fault_injected(int what) { return (fault_mask().load(std::memory_order_relaxed) & what) != 0; }
+void set_fault_injection(int mask) { fault_mask().store(mask); }
+
 int64_t IvfUsqGpu::cand_stride(int nprobe, int k) const {
     const int64_t per = std::min<int64_t>(n_candidates(nbits_, k), std::max(max_list_, 1));
     const int64_t st = std::max<int64_t>(1, std::min<int64_t>((int64_t)nprobe * per, std::max<int64_t>(ntotal_, 1)));
@@ -619,6 +636,9 @@ int64_t IvfUsqGpu::prepare_batch(const float* d_q, const float* h_q, int64_t nb,
         for (int c = 0; c < nchunks; ++c) {
             const int64_t q0 = c * per, m = std::min(per, nb - q0);
             if (m <= 0) break;
+            if (fault_injected(kFaultH2D))
+                throw CudaError(cudaErrorInvalidValue, "cudaMemcpyAsync (injected host-to-device fault)",
+                                __FILE__, __LINE__);
             HANNS_CUDA_OK(cudaMemcpyAsync(const_cast<float*>(d_q) + q0 * dim_, h_q + q0 * dim_,
                                           sizeof(float) * m * dim_, cudaMemcpyHostToDevice,
                                           copy_stream_));
@@ -764,6 +784,7 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         t.lut = st.lut;
         t.q_i8p = st.q_i8p;
         t.cand_dbg = a.cand_dbg;
+        t.wait_ns = scan_wait_ns_;
         t.lq = w_lq_.p;
         t.items = w_items_.p;
         t.n_items = w_counters_.p;
@@ -917,9 +938,16 @@ void IvfUsqGpu::next_slot(int first, int last) {
 void IvfUsqGpu::check_tc_scan() {
     if (!used_tc_) return;
     if (cudaEventQuery(ev_scan_err_) != cudaSuccess) return;
-    if (*h_scan_err_ != 0)
+    const int code = *h_scan_err_;
+    if (code != 0) {
+        // reported once: the flag is cleared so that the next search starts clean (the
+        // kernel freed its TMEM and returned; the context stays usable)
+        HANNS_CUDA_OK(cudaMemsetAsync(w_scan_err_.p, 0, sizeof(int), stream_));
+        HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
+        *h_scan_err_ = 0;
         throw std::runtime_error("tensor-core list scan: a bounded wait expired (code " +
-                                 std::to_string(*h_scan_err_) + ")");
+                                 std::to_string(code) + ")");
+    }
 }
 
 // stage e = ev[e] -> ev[e + 1] for first <= e < last (stages 2-3 from the rotation stream's

@@ -19,6 +19,14 @@ namespace hanns {
 
 struct QueryParams;
 
+// Host-side fault injection (tests of the error paths; no device is ever faulted): a bit
+// set here makes the next device allocations (kFaultAlloc) or host-to-device copies
+// (kFaultH2D) fail as if the CUDA call had returned an error.  Set by
+// hanns_gpu_debug_inject_fault or, at load, by HANNS_GPU_FAULT=alloc|h2d.
+constexpr int kFaultAlloc = 1, kFaultH2D = 2;
+bool fault_injected(int what);
+void set_fault_injection(int mask);
+
 // Grow-only device buffer.
 template <class T>
 struct DevBuf {
@@ -37,7 +45,8 @@ struct DevBuf {
         if (count <= n && p) return;
         release();
         if (count == 0) count = 1;
-        cudaError_t e = cudaMalloc(&p, count * sizeof(T));
+        cudaError_t e = fault_injected(kFaultAlloc) ? cudaErrorMemoryAllocation
+                                                    : cudaMalloc(&p, count * sizeof(T));
         if (e != cudaSuccess) {
             p = nullptr;
             throw CudaError(e, "cudaMalloc", __FILE__, __LINE__);
@@ -132,6 +141,7 @@ class IvfUsqGpu {
     int metric() const { return metric_; }
     int nprobe() const { return nprobe_; }
     void set_nprobe(int p) { nprobe_ = p < 1 ? 1 : (p > nlist_ ? nlist_ : p); }
+    void set_scan_wait_ns(uint64_t ns) { scan_wait_ns_ = ns; }
     bool trained() const { return trained_; }
     int64_t count() const { return ntotal_; }
     int64_t size_bytes() const;
@@ -225,6 +235,7 @@ class IvfUsqGpu {
     int* h_scan_err_ = nullptr;       // pinned: error code of the tensor-core list scan
     cudaEvent_t ev_scan_err_ = nullptr;  // completes when h_scan_err_ holds the last scan's code
     bool debug_candidates_ = false;      // scans also write (int_ip, FastScan score) per candidate
+    uint64_t scan_wait_ns_ = 2000000000ull;  // tensor-core scan: limit of each wait on a role
     DevBuf<int2> w_cand_dbg_;
     DevBuf<int> w_scan_err_;
     int sm_count_ = 0;

@@ -102,6 +102,7 @@ struct TcScanArgs {
     uint64_t* cand_tie;
     int2* cand_dbg;         // nullable, as in ScanArgs
     int* err_flag;          // set to a nonzero code when a bounded wait expired
+    uint64_t wait_ns;       // limit of every wait on another role (2 s by default)
 };
 
 // USQ rerank of caller-chosen stored rows: out[q * m + j] = distance of row rows[q*m+j]

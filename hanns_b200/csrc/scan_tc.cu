@@ -33,8 +33,9 @@
 //   warp 16     TMEM allocation and the single-thread MMA issuer
 // TMEM holds two items' accumulators (256 columns each): item j's FastScan GEMM, then its
 // rerank GEMM (in the same columns once the scores are copied out), while the epilogue
-// finishes item j - 1.  Hand-offs are mbarriers; every wait is bounded (2 s): on expiry
-// the kernel records an error code, every role leaves its loop, and the TMEM is freed.
+// finishes item j - 1.  Hand-offs are mbarriers; every wait is bounded (wait_ns, 2 s by
+// default): on expiry the kernel records an error code, every role leaves its loop, the
+// MMAs already issued complete, and the TMEM is freed.
 #include <cstdint>
 
 #include "common.cuh"
@@ -88,6 +89,7 @@ struct TcSmem {
     uint64_t a_full[kNA], a_empty[kNA], b_full[kNB], b_empty[kNB];
     uint64_t item_full[kSlots], item_empty[kSlots];
     uint64_t fs_full[2], fs_free[2], rr_full[2], tmem_free[2];
+    uint64_t drain;  // the MMA issuer's last commit: every MMA it issued has completed
     uint32_t tmem;
     volatile int abort;
 };
@@ -110,9 +112,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Bounded wait for the phase with the given parity (2 s or kWaitLimit polls, or until
-// another role raised the abort flag).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// Bounded wait for the phase with the given parity (limit_ns, at most kWaitLimit polls,
+// or until another role raised the abort flag).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns) {
     const uint32_t addr = smem_u32(bar);
     const uint64_t t0 = global_ns();
     for (uint32_t it = 0; it < kWaitLimit; ++it) {
@@ -125,7 +128,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
-        if ((it & 255) == 255 && (*abort || global_ns() - t0 > 2000000000ull)) return false;
+        if ((it & 255) == 255 && (*abort || global_ns() - t0 > limit_ns)) return false;
     }
     return false;
 }
@@ -262,6 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             mbar_init(&sm.rr_full[h], 1);
             mbar_init(&sm.tmem_free[h], kEpiWarps);
         }
+        mbar_init(&sm.drain, 1);
         sm.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -276,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = sm.tmem;
+    const uint64_t wl = a.wait_ns;
     auto fail = [&](int code) {
         if (!sm.abort) atomicExch(a.err_flag, code);
         sm.abort = 1;
@@ -301,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             ItemSlot& S = sm.slot[si];
             if (warp == 0) {
                 // publish the next item once every role released the slot
-                bool free_ok = j < kSlots || mbar_wait(&sm.item_empty[si], ((j / kSlots) - 1) & 1, &sm.abort);
+                bool free_ok = j < kSlots || mbar_wait(&sm.item_empty[si], ((j / kSlots) - 1) & 1, &sm.abort, wl);
                 free_ok = __all_sync(0xffffffffu, free_ok);
                 if (!free_ok) {
                     fail(5);
@@ -355,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.item_full[si]);
             }
-            const bool got = __all_sync(0xffffffffu, mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort));
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort, wl));
             if (!got) {
                 fail(5);
                 break;
@@ -473,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 const int ns = is_b ? kNB : kNA;
                 const uint32_t s = pos % ns, use = pos / ns;
                 uint64_t* empty = is_b ? &sm.b_empty[s] : &sm.a_empty[s];
-                const bool freed = use == 0 || mbar_wait(empty, (use - 1) & 1, &sm.abort);
+                const bool freed = use == 0 || mbar_wait(empty, (use - 1) & 1, &sm.abort, wl);
                 if (!__all_sync(0xffffffffu, freed)) return false;
                 build(st, cur, (is_b ? ring_b : ring_a) + s * kStageBytes);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -506,10 +511,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             uint32_t ga = 0, gb = 0;
+            uint32_t fs_items[2] = {0u, 0u};  // FastScan items per TMEM half (fs_full / fs_free phases)
             for (int j = 0;; ++j) {
                 const int si = j % kSlots;
                 const ItemSlot& S = sm.slot[si];
-                if (!mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort)) {
+                if (!mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort, wl)) {
                     fail(7);
                     break;
                 }
@@ -518,12 +524,12 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 const uint32_t idesc = idesc_i8(N);
                 const uint32_t h = j & 1, use = j >> 1;
                 const uint32_t dcol = tmem + h * kHalfCols;
-                bool ok = use == 0 || mbar_wait(&sm.tmem_free[h], (use - 1) & 1, &sm.abort);
+                bool ok = use == 0 || mbar_wait(&sm.tmem_free[h], (use - 1) & 1, &sm.abort, wl);
                 // one GEMM phase: per slab, the B stage then the T A stages (nk K-steps of 32)
                 auto gemm = [&](int slabs, int k_bytes) {
                     for (int s = 0; s < slabs && ok; ++s) {
                         const uint32_t bs = gb % kNB;
-                        if (!mbar_wait(&sm.b_full[bs], (gb / kNB) & 1, &sm.abort)) {
+                        if (!mbar_wait(&sm.b_full[bs], (gb / kNB) & 1, &sm.abort, wl)) {
                             ok = false;
                             break;
                         }
@@ -531,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         const uint32_t bbase = smem_u32(ring_b + bs * kStageBytes);
                         for (int t = 0; t < T; ++t) {
                             const uint32_t as = ga % kNA;
-                            if (!mbar_wait(&sm.a_full[as], (ga / kNA) & 1, &sm.abort)) {
+                            if (!mbar_wait(&sm.a_full[as], (ga / kNA) & 1, &sm.abort, wl)) {
                                 ok = false;
                                 break;
                             }
@@ -549,10 +555,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     }
                 };
                 if (ok && S.fs) {
+                    const uint32_t fu = fs_items[h]++;
                     gemm(fs_slabs, 4 * a.D);
                     if (ok) umma_commit(&sm.fs_full[h]);
                     // the rerank reuses the columns once the epilogue copied the scores out
-                    if (ok && !mbar_wait(&sm.fs_free[h], use & 1, &sm.abort)) ok = false;
+                    if (ok && !mbar_wait(&sm.fs_free[h], fu & 1, &sm.abort, wl)) ok = false;
                 }
                 if (ok) {
                     gemm(rr_slabs, a.D);
@@ -564,6 +571,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
                 mbar_arrive(&sm.item_empty[si]);
             }
+            // before the TMEM is freed, every MMA issued (also after an abort) completes;
+            // this wait ignores the abort flag and gives up after 0.5 s
+            umma_commit(&sm.drain);
+            int no_abort = 0;
+            if (!mbar_wait(&sm.drain, 0, &no_abort, 500000000ull)) fail(10);
         }
         __syncwarp();
     } else {
@@ -573,10 +585,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         const int e = warp - kBuildWarps;             // 0..7
         const int quarter = warp & 3, half = e >> 2;  // TMEM lanes 32*quarter.., column half
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        uint32_t fs_items[2] = {0u, 0u};  // as the MMA issuer counts them
         for (int j = 0;; ++j) {
             const int si = j % kSlots;
             const ItemSlot& S = sm.slot[si];
-            bool bad = !__all_sync(0xffffffffu, mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort));
+            bool bad = !__all_sync(0xffffffffu, mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort, wl));
             if (epi_sync_or(bad)) {
                 fail(8);
                 break;
@@ -590,7 +603,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             const int c_lo = half * (N >> 1), c_hi = c_lo + (N >> 1);
             // FastScan scores: TMEM -> shared memory (16-bit wrap)
             if (S.fs) {
-                bad = !__all_sync(0xffffffffu, mbar_wait(&sm.fs_full[h], use & 1, &sm.abort));
+                const uint32_t fu = fs_items[h]++;
+                bad = !__all_sync(0xffffffffu, mbar_wait(&sm.fs_full[h], fu & 1, &sm.abort, wl));
                 if (!bad) {
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     for (int t = 0; t < T; ++t) {
@@ -702,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             }
             bad = epi_sync_or(false);
             // rerank epilogue: thread per row, the distances of the kept (query, row) pairs
-            if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait(&sm.rr_full[h], use & 1, &sm.abort));
+            if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait(&sm.rr_full[h], use & 1, &sm.abort, wl));
             if (!bad) {
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 for (int t = 0; t < T; ++t) {

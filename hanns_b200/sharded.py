@@ -76,9 +76,8 @@ class ShardedIvfUsq:
         parts = np.zeros(5, np.int64)
         _check(lib.hanns_gpu_ivf_usq_query_state_bytes(index._h, self.nprobe, _i64(parts)),
                "query_state_bytes")
-        import os
-        # q_i8 in dimension order is read by the tensor-core scan only
-        self.n_state = 5 if os.environ.get("HANNS_GPU_SCAN") == "tc" else 4
+        # probes, scalars, FastScan LUT, q_i8 (dp4a layout): both list scans read these four
+        self.n_state = 4
         self.parts = [int(b) for b in parts[:self.n_state]]
         u8 = dict(dtype=torch.uint8, device=self.dev)
         W, n, kk = self.world, self.batch, self.k

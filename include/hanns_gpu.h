@@ -266,6 +266,18 @@ int32_t hanns_gpu_ivf_usq_debug_candidates(HannsIvfUsqHandle* h, const float* qu
                                            int64_t* local, int32_t* fs, int32_t* int_ip,
                                            float* dists);
 
+/* Failure testing (no counterpart in the reference, which has no device): the limit of
+ * each bounded wait inside the tensor-core list scan (2 s by default).  A wait that runs
+ * out makes the scan record an error, finish the MMAs it issued, free its tensor memory
+ * and return; the search then fails with an error code (once) and the next search runs
+ * normally. */
+int32_t hanns_gpu_ivf_usq_set_scan_wait_ns(HannsIvfUsqHandle* h, uint64_t ns);
+/* Failure testing: make the library's next device allocations ("alloc") or host-to-device
+ * copies ("h2d") fail as if CUDA had returned an error, or stop doing so ("none").  Only
+ * the host sees the fault; no kernel runs on bad memory.  HANNS_GPU_FAULT=alloc|h2d sets
+ * the same at load. */
+int32_t hanns_gpu_debug_inject_fault(const char* what);
+
 /* Multi-GPU list sharding: keep only lists l with owner[l] == rank, where owner is a
  * longest-processing-time assignment of lists (by size) to world ranks.  Search then
  * returns this shard's top-k with merge keys. */

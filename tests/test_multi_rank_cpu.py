@@ -110,3 +110,57 @@ def test_shard_owners_balanced():
         loads = np.bincount(owner, weights=w, minlength=world)
         assert owner.min() >= 0 and owner.max() < world
         assert loads.max() - loads.min() <= w.max()
+
+
+def _rank_loss_worker(rank, world, port, mode, out):
+    import datetime
+    import sys
+    import time
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import torch
+    import torch.distributed as dist
+
+    from hanns_b200.sharded import gather_query_state
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    # a short group timeout is what ends a collective whose peer never arrives
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=4))
+    full = [torch.zeros(8 * world, dtype=torch.uint8)]
+    local = [torch.full((8,), rank, dtype=torch.uint8)]
+    gather_query_state(full, local)  # one healthy exchange step
+    ok = full[0].view(world, 8).tolist() == [[r] * 8 for r in range(world)]
+    if rank == world - 1:
+        if mode == "exit":
+            os._exit(0)  # the rank dies between steps, no collective in flight
+        time.sleep(15)   # the rank stalls: it never joins the next step
+        os._exit(0)
+    t0 = time.time()
+    try:
+        gather_query_state(full, local)
+        out[rank] = ("no error", time.time() - t0, ok)
+    except Exception as e:  # the survivor learns of the loss on the host
+        out[rank] = (type(e).__name__, time.time() - t0, ok)
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_rank_loss_ends_the_next_exchange(mode):
+    """Failure detection of the multi-GPU protocol, on CPU ranks (gloo): after one good
+    all-gather of query state, the last rank exits (or stalls) between steps.  The other
+    rank's next all-gather ends with an error -- at once when the peer's connection closes,
+    within the group's 4 s timeout when it stalls -- instead of waiting for ever."""
+    import torch.multiprocessing as mp
+    mgr = mp.Manager()
+    out = mgr.dict()
+    port = _free_port()
+    ctx = mp.start_processes(_rank_loss_worker, args=(2, port, mode, out), nprocs=2,
+                             start_method="spawn", join=False)
+    import time
+    deadline = time.time() + 60
+    while not ctx.join(timeout=2) and time.time() < deadline:
+        pass
+    err, waited, ok = out[0]
+    assert ok
+    assert err != "no error"
+    assert waited < 12.0
