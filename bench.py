@@ -80,6 +80,39 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def int8_peak():
+    """Dense int8 tensor rate: the B200 runs int8 (like fp8) at twice its dense bf16 rate
+    (4.5 vs 2.25 P nominal), so the peak is 2 x the measured cuBLAS bf16 burst figure."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return 2.0 * float(json.load(f)["bf16_tflops"]), "derived: 2 x measured bf16 burst"
+    except Exception:
+        return 2.0 * 1590.0, "derived: 2 x fallback bf16 burst"
+
+
+def scan_tc_ops(art, probes, k, nbits, tc_max_rows=2048):
+    """int8 MMA operations (2 per multiply-add) the tensor-core list scan issues for one
+    batch: per item (one list, up to tc_queries_per_item queries, N rounded up to 16) the
+    FastScan GEMM (K = 4 D, lists above n_cand) and the rerank GEMM (K = D) over all T
+    tiles of 128 rows."""
+    from oracle.oracle import n_candidates
+    D = int(art["padded_dim"])
+    ncand = n_candidates(nbits, k)
+    sizes = np.diff(np.asarray(art["list_offsets"], dtype=np.int64))
+    pr = probes.reshape(-1)
+    q_per_list = np.bincount(pr[(pr >= 0) & (pr < sizes.shape[0])], minlength=sizes.shape[0])
+    ops = 0
+    for l in np.nonzero((q_per_list > 0) & (sizes > 0) & (sizes <= tc_max_rows))[0]:
+        n, q = int(sizes[l]), int(q_per_list[l])
+        t = (n + 127) // 128
+        qpi = min(128, (256 // t) & ~15)
+        kk = D + (4 * D if n > ncand else 0)
+        full, rest = divmod(q, qpi)
+        nsum = full * qpi + ((rest + 15) // 16) * 16
+        ops += 2 * 128 * t * nsum * kk
+    return ops
+
+
 # ------------------------------------------------------------------ data
 def _mixture_draw(w, centres, g, n):
     import torch
@@ -246,6 +279,30 @@ def index_stats(art, probes, k, nbits):
             "n_cand": int(ncand),
             "pairs_with_fastscan": float((psz > ncand).mean()) if psz.size else 0.0,
             "reranked_rows_per_query": float(np.minimum(psz, ncand).sum() / max(probes.shape[0], 1))}
+
+
+def scan_roofline_tc(workload, alg_bytes, ops, scan_s, world):
+    """Roofline of the tensor-core list scan (the dominant stage): executed int8 MMA ops
+    per launch over the live CUDA-event time against the dense int8 rate; beside it the
+    per-(query, probe) stream bytes of the reference's loop (algorithmic_*) and the DRAM
+    bytes ncu measured for one launch (dram_*)."""
+    peak, src = int8_peak()
+    hbm, hbm_kind = peaks()
+    kernel = "scan_tc_kernel"
+    traffic, ncu_ms, path = measured_traffic(workload, kernel) if world == 1 else (None, None, None)
+    achieved = ops / scan_s / 1e12
+    roof = {"kernel": kernel, "bound": "tensor", "unit": "TOPS", "achieved": achieved, "peak": peak,
+            "frac": achieved / peak, "peak_source": src, "launch_ms": scan_s * 1e3,
+            "mma_ops_per_launch": ops, "traffic": traffic,
+            "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch ({path}, "
+                               f"{ncu_ms} ms under ncu)") if traffic else "no ncu capture for this workload",
+            "algorithmic_bytes_per_launch": alg_bytes, "algorithmic_gbs": alg_bytes / scan_s / 1e9,
+            "algorithmic_frac_of_hbm": alg_bytes / scan_s / 1e9 / hbm, "hbm_peak_gbs": hbm,
+            "hbm_peak_source": hbm_kind}
+    if traffic:
+        roof["dram_gbs"] = traffic / scan_s / 1e9
+        roof["dram_frac_of_hbm"] = roof["dram_gbs"] / hbm
+    return roof
 
 
 def scan_roofline(workload, alg_bytes, scan_s, world):
@@ -614,7 +671,11 @@ def run_ours(args, w, rank, world, local_rank):
         probes = probes[own[probes]]
     alg = scan_bytes(art_local, probes, k, w["nbits"])
     scan_s = statistics.median(scan_ms) / 1e3
-    roof = scan_roofline(args.workload, alg, scan_s, world)
+    if os.environ.get("HANNS_GPU_SCAN") == "simt":
+        roof = scan_roofline(args.workload, alg, scan_s, world)
+    else:
+        roof = scan_roofline_tc(args.workload, alg, scan_tc_ops(art_local, probes, k, w["nbits"]),
+                                scan_s, world)
 
     # ---- recall and parity sample
     rec = None
