@@ -785,6 +785,8 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         t.q_i8p = st.q_i8p;
         t.cand_dbg = a.cand_dbg;
         t.wait_ns = scan_wait_ns_;
+        w_tc_scores_.reserve((size_t)sm_count_ * kTcScoreScratch);
+        t.scores = w_tc_scores_.p;
         t.lq = w_lq_.p;
         t.items = w_items_.p;
         t.n_items = w_counters_.p;

@@ -1,10 +1,10 @@
 // scan_tc.cu -- list scan on the sm_100a tensor cores.
 //
-// One persistent CTA per SM takes items (one list of at most kTcMaxRows rows, up to 128 of
-// the queries that probe it).  The list's rows are the MMA's M side, in T tiles of 128;
-// the item's queries are its N side (N = queries rounded up to 16, T * N <= 256).  Both
-// integer stages of the reference's search are int8 GEMMs (tcgen05.mma kind::i8, int32
-// accumulation in TMEM, exact):
+// One persistent CTA per SM takes items: one list of at most kTcMaxRows rows and up to 128
+// of the queries that probe it.  The list's rows are the MMA's M side, in T tiles of 128;
+// the item's queries are its N side (N = queries rounded up to 16).  Both integer stages of
+// the reference's search are int8 GEMMs (tcgen05.mma kind::i8, int32 accumulation in TMEM,
+// exact):
 //
 //   FastScan   raw[v][i] = sum_g LUT_i[g][nib_g(v)]                    (fastscan.rs:170-227)
 //              = onehot(v) . LUT_i over K = 16 G bytes: A = one-hot rows (u8 0/1, one
@@ -15,27 +15,31 @@
 //              (quantizer.rs:382-400): A = the codes unpacked to one byte per dimension,
 //              B = the queries' q_i8 in dimension order.
 //
-// Each operand row is built once per item: the one-hot rows of the list serve every query
-// of the item, and each query's LUT slab serves every row tile.  The kept set of each
-// (query, list) pair is the reference's FastScan heap result (fastscan.rs:86-146), found
-// with the same closed form as the SIMT scan (search_kernels.cu) on the 16-bit scores; the
-// rerank epilogue writes (distance key, rank << 48 | FastScan key << 32 | position) of every
-// kept row to the query's candidate region, exactly like the SIMT scan.
+// An item's row tiles are processed in groups of Tg = 256 / N tiles ("units"): a unit's
+// accumulators (Tg x N columns) fill one half of the 512 TMEM columns, and consecutive
+// units alternate halves, so the GEMMs of one unit overlap the epilogue of the previous
+// one.  Each one-hot / code row is built once per item; the queries' slab is built once
+// per unit.  An item runs its FastScan units, then (after the kept sets are known) its
+// rerank units.  The kept set of each (query, list) pair is the reference's FastScan heap
+// result (fastscan.rs:86-146), found with the same closed form as the SIMT scan
+// (search_kernels.cu) on the 16-bit scores; the rerank epilogue writes (distance key,
+// rank << 48 | FastScan key << 32 | position) of every kept row to the query's candidate
+// region, exactly like the SIMT scan.
 //
 // Warp roles (17 warps):
 //   warps 0-7   builders: fetch items (warp 0), then write the operand stages of the item
-//               in MMA order -- per K slab of 128 bytes one B stage (the queries) and T A
-//               stages (the row tiles) -- into two rings (A: kNA x 16 KiB, B: kNB x 16 KiB,
-//               128-byte swizzle, K-major); the global loads of stage g + kPF are in
-//               flight while stage g is written
-//   warps 8-15  epilogue: FastScan scores TMEM -> shared memory, the kept set of each
-//               query (warp per query), the distances of the kept rows (thread per row)
+//               in MMA order -- per unit and K slab of 128 bytes one B stage (the queries)
+//               and the unit's A stages (its row tiles) -- into two rings (A: kNA x 16 KiB,
+//               B: kNB x 16 KiB; 128-byte swizzle, K-major); the global loads of stage
+//               g + kPF are in flight while stage g is written
+//   warps 8-15  epilogue: FastScan scores TMEM -> shared memory (or the CTA's global
+//               scratch when an item's scores exceed 64 KiB), the kept set of each query
+//               (warp per query), the distances of the kept rows (thread per row)
 //   warp 16     TMEM allocation and the single-thread MMA issuer
-// TMEM holds two items' accumulators (256 columns each): item j's FastScan GEMM, then its
-// rerank GEMM (in the same columns once the scores are copied out), while the epilogue
-// finishes item j - 1.  Hand-offs are mbarriers; every wait is bounded (wait_ns, 2 s by
-// default): on expiry the kernel records an error code, every role leaves its loop, the
-// MMAs already issued complete, and the TMEM is freed.
+// Hand-offs are mbarriers, waited on with try_wait (the hardware suspends the waiting
+// threads); every wait is bounded (wait_ns, 2 s by default): on expiry the kernel records
+// an error code, every role leaves its loop, the MMAs already issued complete, and the
+// TMEM is freed.
 #include <cstdint>
 
 #include "common.cuh"
@@ -51,18 +55,19 @@ constexpr int kThreads = (kCtrlWarp + 1) * 32;      // 544
 constexpr int kBuildThreads = kBuildWarps * 32;     // 256
 constexpr int kRows = 128;                          // MMA M: list rows per tile
 constexpr int kMaxQ = 128;                          // MMA N limit: queries per item
-constexpr int kHalfCols = 256;                      // TMEM columns of one item
+constexpr int kHalfCols = 256;                      // TMEM columns of one unit
 constexpr int kTmemCols = 2 * kHalfCols;
 constexpr int kSlab = 128;                          // K bytes per stage (one swizzle atom)
 constexpr int kStageBytes = kRows * kSlab;          // 16 KiB
 constexpr int kNA = 4, kNB = 2;                     // ring stages
-constexpr int kScoreCap = kHalfCols * kRows;        // T * 128 * N <= 32768 scores
-constexpr int kWordCap = kScoreCap / 32;
-constexpr int kSlots = 3;                           // items in flight
+constexpr int kScoreCap = 32768;                    // FastScan scores held in shared memory
+constexpr int kWordCap = 4096;                      // kept-row bitmap words: N * T * 4
+constexpr int kSlots = 2;                           // items in flight
 constexpr int kPF = 3;                              // stages loaded ahead
-constexpr uint32_t kWaitLimit = 1u << 26;
+constexpr uint32_t kWaitLimit = 1u << 24;
 static_assert(kMaxQ * 8 <= 4 * kBuildThreads, "a B stage is at most four 16-byte chunks per builder");
-static_assert(kTcMaxRows <= 16 * kRows, "16 row tiles of 16 queries fill one item's TMEM columns");
+static_assert(kTcScoreScratch >= (int64_t)kMaxQ * kTcMaxRows, "score scratch of one item");
+static_assert(kWordCap * 32 >= 1024 * kRows, "N * T <= 1024 (tc_queries_per_item)");
 
 // kind::i8 instruction descriptor: D s32 (bits 4-5 = 2), A u8 (bits 7-9 = 0), B s8
 // (bits 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
@@ -71,8 +76,8 @@ __device__ __forceinline__ uint32_t idesc_i8(int n) {
 }
 
 struct ItemSlot {
-    int item, n, nq, T;  // item < 0: no more work
-    int N, fs, list, pad;
+    int item, n, nq, T;   // item < 0: no more work
+    int N, fs, list, Tg;  // Tg: row tiles per unit
     int64_t beg;
     int q[kMaxQ], rank[kMaxQ], bsi[kMaxQ];
     int64_t base[kMaxQ];  // candidate region of each query's (query, probe) pair
@@ -88,7 +93,7 @@ struct TcSmem {
     ItemSlot slot[kSlots];
     uint64_t a_full[kNA], a_empty[kNA], b_full[kNB], b_empty[kNB];
     uint64_t item_full[kSlots], item_empty[kSlots];
-    uint64_t fs_full[2], fs_free[2], rr_full[2], tmem_free[2];
+    uint64_t acc_full[2], acc_free[2];  // per TMEM half: a unit's GEMMs done / read out
     uint64_t drain;  // the MMA issuer's last commit: every MMA it issued has completed
     uint32_t tmem;
     volatile int abort;
@@ -112,8 +117,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Bounded wait for the phase with the given parity (limit_ns, at most kWaitLimit polls,
-// or until another role raised the abort flag).
+// Bounded wait for the phase with the given parity: try_wait suspends the thread in
+// hardware between checks; gives up after limit_ns, kWaitLimit tries, or once another role
+// raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint64_t limit_ns) {
     const uint32_t addr = smem_u32(bar);
@@ -122,13 +128,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
-            "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
             "selp.u32 %0, 1, 0, p;\n\t}"
             : "=r"(done)
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
-        if ((it & 255) == 255 && (*abort || global_ns() - t0 > limit_ns)) return false;
+        if (*abort || global_ns() - t0 > limit_ns) return false;
     }
     return false;
 }
@@ -209,20 +215,43 @@ struct StageLoad {
     uint4 v[4];
 };
 
-// Stage g of an item (per K slab: one B stage, then the T A stages; FastScan slabs first):
-// kind 0 FastScan B (LUTs), 1 FastScan A (one-hot rows), 2 rerank B (q_i8), 3 rerank A
-// (codes).
+// The units of an item: ng groups of Tg row tiles (the last one has last_nt), first the
+// FastScan units (when FastScan runs), then the rerank units.
+struct ItemGeo {
+    int Tg, ng, last_nt, fs_slabs, rr_slabs, fs_stages;  // fs_stages: stages of all FS units
+    __device__ int unit_tiles(int g) const { return g == ng - 1 ? last_nt : Tg; }
+};
+
+__device__ __forceinline__ ItemGeo item_geo(int T, int N, bool fs, int fs_slabs, int rr_slabs) {
+    ItemGeo g;
+    g.Tg = min(T, max(1, kHalfCols / N));
+    g.ng = (T + g.Tg - 1) / g.Tg;
+    g.last_nt = T - (g.ng - 1) * g.Tg;
+    g.fs_slabs = fs ? fs_slabs : 0;
+    g.rr_slabs = rr_slabs;
+    g.fs_stages = g.fs_slabs * ((g.ng - 1) * (1 + g.Tg) + 1 + g.last_nt);
+    return g;
+}
+
+// Stage g of an item (per unit and K slab: one B stage, then the unit's A stages): kind 0
+// FastScan B (LUTs), 1 FastScan A (one-hot rows), 2 rerank B (q_i8), 3 rerank A (codes);
+// s = K slab, t = row tile.
 struct StageRef {
     int kind, s, t;
 };
 
-__device__ __forceinline__ StageRef stage_of(int g, int per, int fs_stages) {
+__device__ __forceinline__ StageRef stage_of(int g, const ItemGeo& geo) {
+    const bool fs = g < geo.fs_stages;
+    const int gg = fs ? g : g - geo.fs_stages;
+    const int S = fs ? geo.fs_slabs : geo.rr_slabs;
+    const int per_full = S * (1 + geo.Tg);
+    const int grp = min(gg / per_full, geo.ng - 1);
+    const int rem = gg - grp * per_full;
+    const int nt = geo.unit_tiles(grp);
     StageRef r;
-    const int fs = g < fs_stages;
-    const int gg = fs ? g : g - fs_stages;
-    r.s = gg / per;
-    const int u = gg - r.s * per;
-    r.t = u - 1;
+    r.s = rem / (1 + nt);
+    const int u = rem - r.s * (1 + nt);
+    r.t = grp * geo.Tg + u - 1;
     r.kind = (fs ? 0 : 2) + (u > 0 ? 1 : 0);
     return r;
 }
@@ -245,6 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     const bool l2 = a.metric_l2 != 0;
     const int fs_slabs = a.D / 32;                   // K = 16 G = 4 D bytes
     const int rr_slabs = (a.D + kSlab - 1) / kSlab;  // K = D bytes
+    int16_t* const sc_global = a.scores + (int64_t)blockIdx.x * kTcScoreScratch;
 
     if (tid == 0) {
         for (int s = 0; s < kNA; ++s) {
@@ -260,10 +290,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             mbar_init(&sm.item_empty[s], kBuildWarps + 1 + kEpiWarps);
         }
         for (int h = 0; h < 2; ++h) {
-            mbar_init(&sm.fs_full[h], 1);
-            mbar_init(&sm.fs_free[h], kEpiWarps);
-            mbar_init(&sm.rr_full[h], 1);
-            mbar_init(&sm.tmem_free[h], kEpiWarps);
+            mbar_init(&sm.acc_full[h], 1);
+            mbar_init(&sm.acc_free[h], kEpiWarps);
         }
         mbar_init(&sm.drain, 1);
         sm.abort = 0;
@@ -316,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 if (lane == 0) {
                     it = next_it >= 0 ? next_it : fetch_item();
                     next_it = it < *a.n_items ? fetch_item() : it;
-                    if (next_it < *a.n_items) {
+                    if (next_it < *a.n_items) {  // (a non-empty list)
                         // the following item's list into L2 while this one is scanned
                         const int l = a.items[next_it].x;
                         const int64_t b0 = a.list_off[l], n = a.list_off[l + 1] - b0;
@@ -334,14 +362,16 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     const int64_t beg = a.list_off[rec.x];
                     const int n = (int)(a.list_off[rec.x + 1] - beg);
                     if (lane == 0) {
+                        const int T = (n + kRows - 1) / kRows, N = (rec.z + 15) & ~15;
                         S.item = it;
                         S.beg = beg;
                         S.n = n;
                         S.nq = rec.z;
-                        S.T = (n + kRows - 1) / kRows;
-                        S.N = (rec.z + 15) & ~15;
+                        S.T = T;
+                        S.N = N;
                         S.fs = n > a.n_cand ? 1 : 0;
                         S.list = rec.x;
+                        S.Tg = min(T, max(1, kHalfCols / N));
                     }
                     for (int i = lane; i < rec.z; i += 32) {
                         const int2 pr = a.lq[rec.y + i];
@@ -366,15 +396,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 break;
             }
             if (S.item < 0) break;
-            const int n = S.n, nq = S.nq, T = S.T;
+            const int n = S.n, nq = S.nq;
             const int64_t beg = S.beg;
-            const int per = T + 1;
-            const int fs_stages = S.fs ? fs_slabs * per : 0;
-            const int nst = fs_stages + rr_slabs * per;
+            const ItemGeo geo = item_geo(S.T, S.N, S.fs != 0, fs_slabs, rr_slabs);
+            const int nst = geo.fs_stages + geo.rr_slabs * ((geo.ng - 1) * (1 + geo.Tg) + 1 + geo.last_nt);
             const uint2* fsl = a.fs + a.fs_blk_off[S.list] * (int64_t)a.nchunks * 32;
             auto load = [&](int g, StageLoad& L) {
                 if (g >= nst) return;
-                const StageRef st = stage_of(g, per, fs_stages);
+                const StageRef st = stage_of(g, geo);
                 if (st.kind == 0 || st.kind == 2) {
                     // queries' LUT (kind 0) or q_i8 (kind 2) slab: 16-byte chunk c of query i
 #pragma unroll
@@ -472,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             // write stage g from cur after issuing the loads of stage g + kPF into pf
             auto step = [&](int g, StageLoad& cur, StageLoad& pf) -> bool {
                 load(g + kPF, pf);
-                const StageRef st = stage_of(g, per, fs_stages);
+                const StageRef st = stage_of(g, geo);
                 const bool is_b = (st.kind & 1) == 0;
                 const uint32_t pos = is_b ? gb : ga;
                 const int ns = is_b ? kNB : kNA;
@@ -510,8 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     } else if (warp == kCtrlWarp) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            uint32_t ga = 0, gb = 0;
-            uint32_t fs_items[2] = {0u, 0u};  // FastScan items per TMEM half (fs_full / fs_free phases)
+            uint32_t ga = 0, gb = 0, uc = 0;  // ring positions, units so far
             for (int j = 0;; ++j) {
                 const int si = j % kSlots;
                 const ItemSlot& S = sm.slot[si];
@@ -520,13 +548,19 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     break;
                 }
                 if (S.item < 0) break;
-                const int T = S.T, N = S.N;
+                const int N = S.N;
                 const uint32_t idesc = idesc_i8(N);
-                const uint32_t h = j & 1, use = j >> 1;
-                const uint32_t dcol = tmem + h * kHalfCols;
-                bool ok = use == 0 || mbar_wait(&sm.tmem_free[h], (use - 1) & 1, &sm.abort, wl);
-                // one GEMM phase: per slab, the B stage then the T A stages (nk K-steps of 32)
-                auto gemm = [&](int slabs, int k_bytes) {
+                const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs);
+                bool ok = true;
+                // one unit: per slab the B stage then the unit's A stages (nk K-steps of 32)
+                // into half uc & 1, once the epilogue read out the unit two before
+                auto unit = [&](int slabs, int k_bytes, int nt) {
+                    const uint32_t h = uc & 1, use = uc >> 1;
+                    const uint32_t dcol = tmem + h * kHalfCols;
+                    if (use >= 1 && !mbar_wait(&sm.acc_free[h], (use - 1) & 1, &sm.abort, wl)) {
+                        ok = false;
+                        return;
+                    }
                     for (int s = 0; s < slabs && ok; ++s) {
                         const uint32_t bs = gb % kNB;
                         if (!mbar_wait(&sm.b_full[bs], (gb / kNB) & 1, &sm.abort, wl)) {
@@ -535,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         }
                         const int nk = min(kSlab, k_bytes - s * kSlab) / 32;
                         const uint32_t bbase = smem_u32(ring_b + bs * kStageBytes);
-                        for (int t = 0; t < T; ++t) {
+                        for (int t = 0; t < nt; ++t) {
                             const uint32_t as = ga % kNA;
                             if (!mbar_wait(&sm.a_full[as], (ga / kNA) & 1, &sm.abort, wl)) {
                                 ok = false;
@@ -553,18 +587,12 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         umma_commit(&sm.b_empty[bs]);
                         ++gb;
                     }
+                    if (ok) umma_commit(&sm.acc_full[h]);
+                    ++uc;
                 };
-                if (ok && S.fs) {
-                    const uint32_t fu = fs_items[h]++;
-                    gemm(fs_slabs, 4 * a.D);
-                    if (ok) umma_commit(&sm.fs_full[h]);
-                    // the rerank reuses the columns once the epilogue copied the scores out
-                    if (ok && !mbar_wait(&sm.fs_free[h], fu & 1, &sm.abort, wl)) ok = false;
-                }
-                if (ok) {
-                    gemm(rr_slabs, a.D);
-                    if (ok) umma_commit(&sm.rr_full[h]);
-                }
+                for (int g = 0; g < geo.ng && ok && geo.fs_slabs > 0; ++g)
+                    unit(geo.fs_slabs, 4 * a.D, geo.unit_tiles(g));
+                for (int g = 0; g < geo.ng && ok; ++g) unit(geo.rr_slabs, a.D, geo.unit_tiles(g));
                 if (!ok) {
                     fail(7);
                     break;
@@ -585,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         const int e = warp - kBuildWarps;             // 0..7
         const int quarter = warp & 3, half = e >> 2;  // TMEM lanes 32*quarter.., column half
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        uint32_t fs_items[2] = {0u, 0u};  // as the MMA issuer counts them
+        uint32_t uc = 0;  // units so far (the MMA issuer's count)
         for (int j = 0;; ++j) {
             const int si = j % kSlots;
             const ItemSlot& S = sm.slot[si];
@@ -595,31 +623,44 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 break;
             }
             if (S.item < 0) break;
-            const int n = S.n, nq = S.nq, T = S.T, N = S.N;
+            const int n = S.n, nq = S.nq, N = S.N;
             const int64_t beg = S.beg;
-            const int NP = T * kRows, W = T * 4;  // score row stride, bitmap words per query
-            const uint32_t h = j & 1, use = j >> 1;
-            const uint32_t dcol = tmem + h * kHalfCols + lane_base;
+            const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs);
+            const int NP = S.T * kRows, W = S.T * 4;  // score row stride, bitmap words per query
+            int16_t* const scp = N * NP <= kScoreCap ? sm.sc : sc_global;
             const int c_lo = half * (N >> 1), c_hi = c_lo + (N >> 1);
-            // FastScan scores: TMEM -> shared memory (16-bit wrap)
-            if (S.fs) {
-                const uint32_t fu = fs_items[h]++;
-                bad = !__all_sync(0xffffffffu, mbar_wait(&sm.fs_full[h], fu & 1, &sm.abort, wl));
-                if (!bad) {
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    for (int t = 0; t < T; ++t) {
-                        const int v = t * kRows + quarter * 32 + lane;
-                        for (int c = c_lo; c < c_hi; c += 8) {
-                            uint32_t v8[8];
-                            tmem_ld8(dcol + (uint32_t)(t * N + c), v8);
-#pragma unroll
-                            for (int jj = 0; jj < 8; ++jj) sm.sc[(c + jj) * NP + v] = (int16_t)v8[jj];
-                        }
-                    }
-                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&sm.fs_free[h]);
+            // waits for the next unit's accumulators; false on a failed wait
+            auto unit_begin = [&](uint32_t& dcol) -> bool {
+                const uint32_t h = uc & 1, use = uc >> 1;
+                dcol = tmem + h * kHalfCols + lane_base;
+                const bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.acc_full[h], use & 1, &sm.abort, wl));
+                if (ok) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                return ok;
+            };
+            auto unit_end = [&]() {
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.acc_free[uc & 1]);
+                ++uc;
+            };
+            // FastScan units: scores TMEM -> shared memory or scratch (16-bit wrap)
+            for (int g = 0; g < geo.ng && geo.fs_slabs > 0 && !bad; ++g) {
+                uint32_t dcol;
+                if (!unit_begin(dcol)) {
+                    bad = true;
+                    break;
                 }
+                const int t0 = g * geo.Tg, nt = geo.unit_tiles(g);
+                for (int t = 0; t < nt; ++t) {
+                    const int v = (t0 + t) * kRows + quarter * 32 + lane;
+                    for (int c = c_lo; c < c_hi; c += 8) {
+                        uint32_t v8[8];
+                        tmem_ld8(dcol + (uint32_t)(t * N + c), v8);
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) scp[(c + jj) * NP + v] = (int16_t)v8[jj];
+                    }
+                }
+                unit_end();
             }
             if (epi_sync_or(bad)) {
                 fail(8);
@@ -636,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     for (int v = lane; v < n; v += 32) c += live(v) ? 1 : 0;
                     n_live = warp_sum(c);
                 }
-                const int16_t* sv = sm.sc + i * NP;
+                const int16_t* sv = scp + i * NP;
                 uint32_t* bm = sm.bitmap + i * W;
                 int* px = sm.prefix + i * W;
                 int n_c = 0;
@@ -715,15 +756,19 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
             }
             bad = epi_sync_or(false);
-            // rerank epilogue: thread per row, the distances of the kept (query, row) pairs
-            if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait(&sm.rr_full[h], use & 1, &sm.abort, wl));
-            if (!bad) {
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                for (int t = 0; t < T; ++t) {
-                    const int v = t * kRows + quarter * 32 + lane;
+            // rerank units: thread per row, the distances of the kept (query, row) pairs
+            for (int g = 0; g < geo.ng && !bad; ++g) {
+                uint32_t dcol;
+                if (!unit_begin(dcol)) {
+                    bad = true;
+                    break;
+                }
+                const int t0 = g * geo.Tg, nt = geo.unit_tiles(g);
+                for (int t = 0; t < nt; ++t) {
+                    const int v = (t0 + t) * kRows + quarter * 32 + lane;
                     const bool row_ok = v < n;
                     const float4 m = row_ok ? __ldg(a.meta + beg + v) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    const int wi = t * 4 + quarter;
+                    const int wi = (t0 + t) * 4 + quarter;
                     const uint32_t below = (1u << lane) - 1u;
                     for (int c = c_lo; c < c_hi; c += 8) {
                         uint32_t ip[8];
@@ -737,8 +782,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                             if (!((word >> lane) & 1u)) continue;
                             const int pos = sm.prefix[i * W + wi] + __popc(word & below);
                             if (pos >= a.n_cand) continue;
-                            const int score = sm.sc[i * NP + v];
                             const bool ufs = sm.used_fs[i] != 0;
+                            const int score = ufs ? (int)scp[i * NP + v] : 0;
                             const uint32_t fkey = ufs ? (uint32_t)(32767 - score) : 0u;
                             const float dist = rerank_distance((int)ip[jj], m, S.qp[i], a.nbits, l2);
                             const int64_t dst = S.base[i] + pos;
@@ -748,9 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         }
                     }
                 }
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.tmem_free[h]);
+                unit_end();
             }
             // the next item rewrites the scores and bitmaps
             if (epi_sync_or(bad)) {
