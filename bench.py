@@ -508,6 +508,7 @@ def run_ours(args, w, rank, world, local_rank):
             sh = SplitShardedIvfUsq(idx, k, nprobe, nq)
         else:
             sh = ShardedIvfUsq(idx, k, nprobe, nq)
+            sh.timing = True
         sh.scan_ms = []
 
     def run_steps(n):
@@ -546,11 +547,20 @@ def run_ours(args, w, rank, world, local_rank):
     calls = args.steps if world == 1 else 2 * args.steps
     st_sum, st_cnt, _ = idx.stage_ms_recent(calls)
     scan_ms = [float(st_sum[5]) / max(int(st_cnt[5]), 1)]
+    rank_stages = None
     if world > 1:
         launches[0] = sh.launches
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+        if not split:
+            # per-rank stage medians of the timed batches (CUDA events), max and min over ranks
+            mine_st = sh.stage_times(args.steps)
+            every = [None] * world
+            dist.all_gather_object(every, mine_st)
+            rank_stages = {kk: {"max": max(e[kk] for e in every), "min": min(e[kk] for e in every),
+                                "rank_of_max": int(np.argmax([e[kk] for e in every]))}
+                           for kk in mine_st}
     job_nq = nq if (world == 1 or split) else nq * world
     value = job_nq * args.steps / (ms / 1e3)
     stages = idx.stage_ms().tolist()
@@ -717,6 +727,7 @@ def run_ours(args, w, rank, world, local_rank):
         "index_stats": stats,
         "parity_vs_oracle": parity, "parity_vs_single_gpu": shard_parity,
         "stage_ms_last_step": dict(zip(IvfUsqIndex.STAGES, stages)),
+        "rank_stage_ms": rank_stages,
     }
     print(json.dumps(line), flush=True)
 

@@ -94,6 +94,9 @@ class ShardedIvfUsq:
         self.launches = 0
         self._stream = None
         self._mstream = None
+        # per-batch CUDA events of search_device when True (stage_times() reads them)
+        self.timing = False
+        self._ev = []
 
     def _work_stream(self, stream):
         """The stream the library calls run on: `stream`, or one of the module's own (the
@@ -157,6 +160,9 @@ class ShardedIvfUsq:
         a2a = [None, None]      # works of the all-to-all that last read sh[b]
         pending = None  # (index, slot, gather works) of the batch whose state is in flight
         n = len(batches)
+        # timing: per batch six events -- prepare begin / end, scan begin (state gathered) /
+        # end on the work stream, all-to-all done / merge done on the merge stream
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(n)] if self.timing else None
         with torch.cuda.stream(st):
             for i in range(n + 1):
                 nxt = None
@@ -164,7 +170,11 @@ class ShardedIvfUsq:
                     slot = i % 2
                     if before:
                         before(i)
+                    if ev:
+                        ev[i][0].record(st)
                     self._prepare(batches[i], slot, sp)
+                    if ev:
+                        ev[i][1].record(st)
                     if prepared:
                         prepared(i)
                     nxt = (i, slot, gather_query_state(self.st_full[slot], self.st_local[slot],
@@ -175,23 +185,57 @@ class ShardedIvfUsq:
                         w.wait()
                     for w in a2a[b] or ():
                         w.wait()  # batch j-2's all-to-all has read sh[b]
+                    if ev:
+                        ev[j][2].record(st)
                     self._scan(b, sp, b)
+                    if ev:
+                        ev[j][3].record(st)
                     if merged[b] is not None:
                         st.wait_event(merged[b])  # batch j-2's merge has read recv[b]
                     a2a[b] = return_partials(self.recv[b], self.sh[b], self.group, async_op=True)
                     with torch.cuda.stream(ms):
                         for w in a2a[b]:
                             w.wait()
+                        if ev:
+                            ev[j][4].record(ms)
                         ids, dist_ = outs[j]
                         self._merge(ids, dist_, ms.cuda_stream, b)
+                        if ev:
+                            ev[j][5].record(ms)
                         merged[b] = torch.cuda.Event()
                         merged[b].record(ms)
                         if after:
                             after(j)
                 pending = nxt
+        if ev:
+            self._ev.extend(ev)
         st.wait_stream(ms)
         if cur != st:
             cur.wait_stream(st)
+
+    def stage_times(self, last: int = 0):
+        """Median ms per batch of each stage over the batches timed so far (the last `last`
+        when > 0): prepare; state wait (from the end of the next batch's preparation to the
+        start of the scan: the all-gather not hidden behind that preparation); scan;
+        all-to-all (scan end to shard rows received); merge; step (prepare begin to the
+        next batch's prepare begin).  Waits for the events; clears them."""
+        import statistics
+        ev = self._ev[-last:] if last else self._ev
+        self._ev = []
+        if not ev:
+            return {}
+        for e in ev:
+            e[5].synchronize()
+        rows = {"prepare": [], "state_wait": [], "scan": [], "all_to_all": [], "merge": [], "step": []}
+        for i, e in enumerate(ev):
+            rows["prepare"].append(e[0].elapsed_time(e[1]))
+            rows["scan"].append(e[2].elapsed_time(e[3]))
+            rows["all_to_all"].append(e[3].elapsed_time(e[4]))
+            rows["merge"].append(e[4].elapsed_time(e[5]))
+            if i + 1 < len(ev):
+                rows["state_wait"].append(ev[i + 1][1].elapsed_time(e[2]))
+                rows["step"].append(e[0].elapsed_time(ev[i + 1][0]))
+        return {k: statistics.median(v) for k, v in rows.items() if v}
 
     def search_host(self, queries, out_ids, out_dists):
         """Searches this rank's batches from host memory.
