@@ -216,14 +216,19 @@ def load_artifact(name):
     return {k: (z[k].item() if z[k].ndim == 0 else z[k]) for k in z.files}
 
 
-def get_artifact(name, w, base, device):
-    """Frozen index of the workload: built with the GPU build path once, cached on disk."""
+def get_artifact(name, w, base, device, cache=None):
+    """Frozen index of the workload: built with the GPU build path once, cached on disk
+    (by default only indexes of at most 4 Mi rows: the 20 M-row one is ~12 GB)."""
     p = cache_path(name)
     if os.path.exists(p):
         return load_artifact(name)
     idx = build_index(w, base.cpu().numpy(), device)
     art = idx.export_artifact()
     idx.close()
+    if cache is None:
+        cache = w["n"] <= (1 << 22)
+    if not cache:
+        return art
     os.makedirs(CACHE_DIR, exist_ok=True)
     tmp = p + f".tmp{os.getpid()}.npz"
     np.savez(tmp, **art)
@@ -753,7 +758,7 @@ def main():
     w = WORKLOADS[args.workload]
     if args.prepare_artifact:
         base, _ = make_data(w, "cuda")
-        get_artifact(args.workload, w, base, 0)
+        get_artifact(args.workload, w, base, 0, cache=True)
         return
     if args.impl == "reference":
         run_reference(args, w, rank, world)
