@@ -485,11 +485,14 @@ def run_ours(args, w, rank, world, local_rank):
     base, queries = make_data(w, dev)
     # rank 0 builds the index with the GPU build path (or loads the cached artifact);
     # the other ranks load what rank 0 wrote
-    if rank == 0:
+    # (an index too large for the disk cache is built by every rank at once: the GPU build
+    # is deterministic, so all ranks hold the same index)
+    shared_cache = w["n"] <= (1 << 22)
+    if rank == 0 or not shared_cache:
         art = get_artifact(args.workload, w, base, local_rank)
     if world > 1:
         dist.barrier()
-        if rank != 0:
+        if rank != 0 and shared_cache:
             art = get_artifact(args.workload, w, base, local_rank)
     idx = IvfUsqIndex.from_artifact(art, device=local_rank)
     if args.no_recall:
