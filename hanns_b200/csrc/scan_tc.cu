@@ -22,9 +22,9 @@
 // per unit.  An item runs its FastScan units, then (after the kept sets are known) its
 // rerank units.  The kept set of each (query, list) pair is the reference's FastScan heap
 // result (fastscan.rs:86-146), found with the same closed form as the SIMT scan
-// (search_kernels.cu) on the 16-bit scores; the rerank epilogue writes (distance key,
-// rank << 48 | FastScan key << 32 | position) of every kept row to the query's candidate
-// region, exactly like the SIMT scan.
+// (search_kernels.cu) on the 16-bit scores; as in the SIMT scan, the selection writes each
+// kept row's tie key (rank << 48 | FastScan key << 32 | position) and the rerank epilogue
+// its distance key to the query's candidate region.
 //
 // Warp roles (17 warps):
 //   warps 0-7   builders: fetch items (warp 0), then write the operand stages of the item
@@ -32,9 +32,10 @@
 //               and the unit's A stages (its row tiles) -- into two rings (A: kNA x 16 KiB,
 //               B: kNB x 16 KiB; 128-byte swizzle, K-major); the global loads of stage
 //               g + kPF are in flight while stage g is written
-//   warps 8-15  epilogue: FastScan scores TMEM -> shared memory (or the CTA's global
-//               scratch when an item's scores exceed 64 KiB), the kept set of each query
-//               (warp per query), the distances of the kept rows (thread per row)
+//   warps 8-15  epilogue: FastScan scores TMEM -> the CTA's global scratch (L2), the kept
+//               set of each query (warp per query, its score row staged in shared memory)
+//               with the candidates' tie keys, the distances of the kept rows (thread per
+//               row)
 //   warp 16     TMEM allocation and the single-thread MMA issuer
 // Hand-offs are mbarriers, waited on with try_wait (the hardware suspends the waiting
 // threads); every wait is bounded (wait_ns, 2 s by default): on expiry the kernel records
@@ -60,7 +61,6 @@ constexpr int kTmemCols = 2 * kHalfCols;
 constexpr int kSlab = 128;                          // K bytes per stage (one swizzle atom)
 constexpr int kStageBytes = kRows * kSlab;          // 16 KiB
 constexpr int kNA = 4, kNB = 2;                     // ring stages
-constexpr int kScoreCap = 32768;                    // FastScan scores held in shared memory
 constexpr int kWordCap = 4096;                      // kept-row bitmap words: N * T * 4
 constexpr int kSlots = 2;                           // items in flight
 constexpr int kPF = 3;                              // stages loaded ahead
@@ -85,10 +85,11 @@ struct ItemSlot {
 };
 
 struct TcSmem {
-    int16_t sc[kScoreCap];      // FastScan scores [query][row], row stride T * 128
+    // one query's FastScan scores at a time per epilogue warp, double-buffered (the next
+    // query's row is copied in while the current one is selected)
+    int16_t stage[kEpiWarps][2][kTcMaxRows];
     uint32_t bitmap[kWordCap];  // kept rows [query][word], word stride T * 4
     int prefix[kWordCap];       // kept rows before each bitmap word
-    int used_fs[kMaxQ];         // the query's kept set came from the FastScan selection
     uint32_t hist[kEpiWarps][256];
     ItemSlot slot[kSlots];
     uint64_t a_full[kNA], a_empty[kNA], b_full[kNB], b_empty[kNB];
@@ -254,6 +255,15 @@ __device__ __forceinline__ StageRef stage_of(int g, const ItemGeo& geo) {
     r.t = grp * geo.Tg + u - 1;
     r.kind = (fs ? 0 : 2) + (u > 0 ? 1 : 0);
     return r;
+}
+
+// Copies the first n scores of a score row (global, 256-byte aligned) into a staging buffer
+// (shared, 16-byte aligned) with 16-byte cp.async by the 32 lanes of a warp, as one group.
+__device__ __forceinline__ void stage_row(int16_t* dst, const int16_t* src, int n, int lane) {
+    const uint32_t d = smem_u32(dst);
+    for (int c = lane; c * 8 < n; c += 32)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + c * 16), "l"(src + c * 8) : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
 // Hint: the byte range [p, p + bytes) into L2 (p and bytes multiples of 16, bytes > 0).
@@ -627,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             const int64_t beg = S.beg;
             const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs);
             const int NP = S.T * kRows, W = S.T * 4;  // score row stride, bitmap words per query
-            int16_t* const scp = N * NP <= kScoreCap ? sm.sc : sc_global;
+            int16_t* const scp = sc_global;
             const int c_lo = half * (N >> 1), c_hi = c_lo + (N >> 1);
             // waits for the next unit's accumulators; false on a failed wait
             auto unit_begin = [&](uint32_t& dcol) -> bool {
@@ -662,12 +672,25 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
                 unit_end();
             }
+            __threadfence();  // the scores are read back (through L2) by other warps' copies
             if (epi_sync_or(bad)) {
                 fail(8);
                 break;
             }
-            // the kept set of each query (warp per query)
-            for (int i = e; i < nq; i += kEpiWarps) {
+            // the kept set of each query (warp per query) and its candidates' tie keys
+            int sb = 0;  // staging buffer of the current query
+            if (S.fs && e < nq) stage_row(sm.stage[e][0], scp + e * NP, n, lane);
+            for (int i = e; i < nq; i += kEpiWarps, sb ^= 1) {
+                if (S.fs) {
+                    // the next query's row into the other buffer, then wait for this one's
+                    if (i + kEpiWarps < nq) {
+                        stage_row(sm.stage[e][sb ^ 1], scp + (i + kEpiWarps) * NP, n, lane);
+                        asm volatile("cp.async.wait_group 1;" ::: "memory");
+                    } else {
+                        asm volatile("cp.async.wait_group 0;" ::: "memory");
+                    }
+                    __syncwarp();
+                }
                 const int bsi = S.bsi[i];
                 const uint64_t* bw = bsi >= 0 ? a.bitsets + (int64_t)bsi * a.bitset_words : nullptr;
                 auto live = [&](int v) { return !bw || !filtered(bw, a.bitset_len, a.ids[beg + v]); };
@@ -677,9 +700,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     for (int v = lane; v < n; v += 32) c += live(v) ? 1 : 0;
                     n_live = warp_sum(c);
                 }
-                const int16_t* sv = scp + i * NP;
+                const int16_t* sv = sm.stage[e][sb];
                 uint32_t* bm = sm.bitmap + i * W;
                 int* px = sm.prefix + i * W;
+                const int64_t rb = S.base[i];
+                const uint64_t rank_bits = (uint64_t)S.rank[i] << 48;
                 int n_c = 0;
                 if (S.fs && n_live > a.n_cand) {
                     // s* = n_cand-th largest score among live rows (key = 32767 - score); the
@@ -728,27 +753,40 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                             bm[base >> 5] = bk;
                             px[base >> 5] = n_c;
                         }
+                        if (keep) {
+                            const int pos = n_c + __popc(bk & lanemask_lt());
+                            if (pos < a.n_cand) {
+                                a.cand_tie[rb + pos] = rank_bits | ((uint64_t)k << 32) | (uint32_t)v;
+                                if (a.cand_dbg) a.cand_dbg[rb + pos].y = 32767 - (int)k;
+                            }
+                        }
                         n_c += __popc(bk);
                         eq_seen += __popc(beq);
                     }
-                    if (lane == 0) sm.used_fs[i] = 1;
                 } else {
                     // every live row is kept, in list order
                     for (int base = 0; base < NP; base += 32) {
                         const int v = base + lane;
-                        const unsigned bk = __ballot_sync(0xffffffffu, v < n && live(v));
+                        const bool keep = v < n && live(v);
+                        const unsigned bk = __ballot_sync(0xffffffffu, keep);
                         if (lane == 0) {
                             bm[base >> 5] = bk;
                             px[base >> 5] = n_c;
                         }
+                        if (keep) {
+                            const int pos = n_c + __popc(bk & lanemask_lt());
+                            if (pos < a.n_cand) {
+                                a.cand_tie[rb + pos] = rank_bits | (uint32_t)v;
+                                if (a.cand_dbg) a.cand_dbg[rb + pos].y = INT32_MIN;
+                            }
+                        }
                         n_c += __popc(bk);
                     }
-                    if (lane == 0) sm.used_fs[i] = 0;
                 }
+                __syncwarp();  // the staging buffer is rewritten two queries later
                 n_c = min(n_c, a.n_cand);
                 // unused entries of the pair's region of min(|list|, n_cand) entries (rows
                 // removed by the filter)
-                const int64_t rb = S.base[i];
                 const int cap = min(n, a.n_cand);
                 for (int jj = n_c + lane; jj < cap; jj += 32) {
                     a.cand_tie[rb + jj] = ~0ull;
@@ -782,14 +820,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                             if (!((word >> lane) & 1u)) continue;
                             const int pos = sm.prefix[i * W + wi] + __popc(word & below);
                             if (pos >= a.n_cand) continue;
-                            const bool ufs = sm.used_fs[i] != 0;
-                            const int score = ufs ? (int)scp[i * NP + v] : 0;
-                            const uint32_t fkey = ufs ? (uint32_t)(32767 - score) : 0u;
                             const float dist = rerank_distance((int)ip[jj], m, S.qp[i], a.nbits, l2);
                             const int64_t dst = S.base[i] + pos;
-                            a.cand_key[dst] = total_order_key(dist);
-                            a.cand_tie[dst] = ((uint64_t)S.rank[i] << 48) | ((uint64_t)fkey << 32) | (uint32_t)v;
-                            if (a.cand_dbg) a.cand_dbg[dst] = make_int2((int)ip[jj], ufs ? score : INT32_MIN);
+                            a.cand_key[dst] = total_order_key(dist);  // (its tie: the selection)
+                            if (a.cand_dbg) a.cand_dbg[dst].x = (int)ip[jj];
                         }
                     }
                 }
