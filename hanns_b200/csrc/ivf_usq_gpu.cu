@@ -787,6 +787,13 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         t.wait_ns = scan_wait_ns_;
         w_tc_scores_.reserve((size_t)sm_count_ * kTcScoreScratch);
         t.scores = w_tc_scores_.p;
+        const char* prof_env = std::getenv("HANNS_GPU_SCAN_PROFILE");
+        const bool prof = prof_env && prof_env[0] == '1';
+        if (prof) {
+            w_tc_prof_.reserve((size_t)sm_count_ * kTcProfSlots);
+            HANNS_CUDA_OK(cudaMemsetAsync(w_tc_prof_.p, 0, sizeof(unsigned long long) * sm_count_ * kTcProfSlots, s));
+            t.prof = w_tc_prof_.p;
+        }
         t.lq = w_lq_.p;
         t.items = w_items_.p;
         t.n_items = w_counters_.p;
@@ -807,6 +814,25 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         t.err_flag = w_scan_err_.p;
         launch_scan_tc(t, sm_count_, s);
         launches += 1;
+        if (t.prof) {
+            // per-CTA averages of the role counters (scan_tc.cu), one line on stderr
+            std::vector<unsigned long long> h((size_t)sm_count_ * kTcProfSlots);
+            HANNS_CUDA_OK(cudaMemcpyAsync(h.data(), w_tc_prof_.p, sizeof(unsigned long long) * h.size(),
+                                          cudaMemcpyDeviceToHost, s));
+            HANNS_CUDA_OK(cudaStreamSynchronize(s));
+            static const char* names[] = {"build", "build_wait_slot", "build_wait_item", "mma_wait_full",
+                                          "mma_wait_free", "mma", "epi_wait_acc", "epi_copy",
+                                          "epi_select", "epi_rerank", "epi_wait_item", "epi",
+                                          "items", "stages"};
+            std::fprintf(stderr, "TC_SCAN_PROFILE ctas=%d", sm_count_);
+            for (int k = 0; k < 14; ++k) {
+                double sum = 0;
+                for (int c = 0; c < sm_count_; ++c) sum += (double)h[(size_t)c * kTcProfSlots + k];
+                std::fprintf(stderr, k < 12 ? " %s=%.3fms" : " %s=%.1f", names[k],
+                             k < 12 ? sum / sm_count_ / 1e6 : sum / sm_count_);
+            }
+            std::fprintf(stderr, "\n");
+        }
     }
     launch_scan(a, grid, s);
     launches += 1;

@@ -238,6 +238,7 @@ class IvfUsqGpu {
     uint64_t scan_wait_ns_ = 2000000000ull;  // tensor-core scan: limit of each wait on a role
     DevBuf<int2> w_cand_dbg_;
     DevBuf<int16_t> w_tc_scores_;  // tensor-core scan: FastScan scores of items too big for smem
+    DevBuf<unsigned long long> w_tc_prof_;  // tensor-core scan: role time counters (profiling)
     DevBuf<int> w_scan_err_;
     int sm_count_ = 0;
     // stages: coarse GEMM, coarse select, rotate, query state, group, scan, merge; then total

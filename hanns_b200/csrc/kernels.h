@@ -101,6 +101,9 @@ struct TcScanArgs {
     uint64_t* cand_tie;
     int2* cand_dbg;         // nullable, as in ScanArgs
     int16_t* scores;        // per CTA kTcScoreScratch FastScan scores (items too big for smem)
+    // nullable: per CTA kTcProfSlots nanosecond counters of where each role spends its time
+    // (HANNS_GPU_SCAN_PROFILE=1; see scan_tc.cu)
+    unsigned long long* prof;
     int* err_flag;          // set to a nonzero code when a bounded wait expired
     uint64_t wait_ns;       // limit of every wait on another role (2 s by default)
 };
@@ -211,6 +214,7 @@ size_t scan_smem_bytes(int D);
 size_t scan_tc_smem_bytes();
 // FastScan scores of one item at most (128 queries x kTcMaxRows rows), per CTA of the scan
 constexpr int64_t kTcScoreScratch = 128ll * kTcMaxRows;
+constexpr int kTcProfSlots = 16;
 void launch_scan_tc(const TcScanArgs& a, int grid, cudaStream_t s);
 int scan_grid_size(int D);
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s);

@@ -274,6 +274,15 @@ __device__ __forceinline__ void l2_prefetch(const void* p, uint64_t bytes) {
                  : "memory");
 }
 
+// Time-breakdown counters (a.prof, per CTA; ns of the globaltimer, one lane per role):
+//   0 builder item loop  1 builder empty-slot waits  2 builder item waits
+//   3 MMA full-stage waits  4 MMA accumulator-free waits  5 MMA item loop
+//   6 epilogue accumulator waits  7 FastScan copy-out  8 selection  9 rerank epilogue
+//   10 epilogue item waits  11 epilogue item loop  12 items  13 stages
+enum ProfSlot { kPBuild, kPBuildWaitSlot, kPBuildWaitItem, kPMmaWaitFull, kPMmaWaitFree, kPMma,
+                kPEpiWaitAcc, kPEpiCopy, kPEpiSelect, kPEpiRerank, kPEpiWaitItem, kPEpi, kPItems,
+                kPStages };
+
 __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring_a = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -319,6 +328,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = sm.tmem;
     const uint64_t wl = a.wait_ns;
+    unsigned long long* const prof = a.prof ? a.prof + (int64_t)blockIdx.x * kTcProfSlots : nullptr;
+    // a profiling lane adds the time since t to slot k
+    auto padd = [&](bool mine, int k, uint64_t t) {
+        if (prof && mine) prof[k] += global_ns() - t;
+    };
     auto fail = [&](int code) {
         if (!sm.abort) atomicExch(a.err_flag, code);
         sm.abort = 1;
@@ -339,12 +353,15 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 if (rec.w == 1 && a.list_off[rec.x + 1] > a.list_off[rec.x]) return it;
             }
         };
+        const bool pl = warp == 0 && lane == 0;  // the builders' profiling lane
         for (int j = 0;; ++j) {
             const int si = j % kSlots;
             ItemSlot& S = sm.slot[si];
+            const uint64_t t_item = prof ? global_ns() : 0;
             if (warp == 0) {
                 // publish the next item once every role released the slot
                 bool free_ok = j < kSlots || mbar_wait(&sm.item_empty[si], ((j / kSlots) - 1) & 1, &sm.abort, wl);
+                padd(pl, kPBuildWaitItem, t_item);
                 free_ok = __all_sync(0xffffffffu, free_ok);
                 if (!free_ok) {
                     fail(5);
@@ -517,7 +534,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 const int ns = is_b ? kNB : kNA;
                 const uint32_t s = pos % ns, use = pos / ns;
                 uint64_t* empty = is_b ? &sm.b_empty[s] : &sm.a_empty[s];
+                const uint64_t t_w = prof ? global_ns() : 0;
                 const bool freed = use == 0 || mbar_wait(empty, (use - 1) & 1, &sm.abort, wl);
+                padd(pl, kPBuildWaitSlot, t_w);
                 if (!__all_sync(0xffffffffu, freed)) return false;
                 build(st, cur, (is_b ? ring_b : ring_a) + s * kStageBytes);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -545,6 +564,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 break;
             }
             if (lane == 0) mbar_arrive(&sm.item_empty[si]);
+            padd(pl, kPBuild, t_item);
+            if (prof && pl) {
+                prof[kPItems] += 1;
+                prof[kPStages] += (unsigned long long)nst;
+            }
         }
     } else if (warp == kCtrlWarp) {
         // ------------------------------------------------------------ MMA issuer
@@ -558,6 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     break;
                 }
                 if (S.item < 0) break;
+                const uint64_t t_item = prof ? global_ns() : 0;
                 const int N = S.N;
                 const uint32_t idesc = idesc_i8(N);
                 const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs);
@@ -567,24 +592,30 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 auto unit = [&](int slabs, int k_bytes, int nt) {
                     const uint32_t h = uc & 1, use = uc >> 1;
                     const uint32_t dcol = tmem + h * kHalfCols;
+                    const uint64_t t_f = prof ? global_ns() : 0;
                     if (use >= 1 && !mbar_wait(&sm.acc_free[h], (use - 1) & 1, &sm.abort, wl)) {
                         ok = false;
                         return;
                     }
+                    padd(true, kPMmaWaitFree, t_f);
                     for (int s = 0; s < slabs && ok; ++s) {
                         const uint32_t bs = gb % kNB;
+                        uint64_t t_w = prof ? global_ns() : 0;
                         if (!mbar_wait(&sm.b_full[bs], (gb / kNB) & 1, &sm.abort, wl)) {
                             ok = false;
                             break;
                         }
+                        padd(true, kPMmaWaitFull, t_w);
                         const int nk = min(kSlab, k_bytes - s * kSlab) / 32;
                         const uint32_t bbase = smem_u32(ring_b + bs * kStageBytes);
                         for (int t = 0; t < nt; ++t) {
                             const uint32_t as = ga % kNA;
+                            t_w = prof ? global_ns() : 0;
                             if (!mbar_wait(&sm.a_full[as], (ga / kNA) & 1, &sm.abort, wl)) {
                                 ok = false;
                                 break;
                             }
+                            padd(true, kPMmaWaitFull, t_w);
                             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                             const uint32_t abase = smem_u32(ring_a + as * kStageBytes);
                             for (int k4 = 0; k4 < nk; ++k4)
@@ -608,6 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     break;
                 }
                 mbar_arrive(&sm.item_empty[si]);
+                padd(true, kPMma, t_item);
             }
             // before the TMEM is freed, every MMA issued (also after an abort) completes;
             // this wait ignores the abort flag and gives up after 0.5 s
@@ -624,10 +656,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         const int quarter = warp & 3, half = e >> 2;  // TMEM lanes 32*quarter.., column half
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         uint32_t uc = 0;  // units so far (the MMA issuer's count)
+        const bool pl = e == 0 && lane == 0;  // the epilogue's profiling lane
         for (int j = 0;; ++j) {
             const int si = j % kSlots;
             const ItemSlot& S = sm.slot[si];
+            const uint64_t t_item = prof ? global_ns() : 0;
             bool bad = !__all_sync(0xffffffffu, mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort, wl));
+            padd(pl, kPEpiWaitItem, t_item);
+            const uint64_t t_body = prof ? global_ns() : 0;
             if (epi_sync_or(bad)) {
                 fail(8);
                 break;
@@ -643,7 +679,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             auto unit_begin = [&](uint32_t& dcol) -> bool {
                 const uint32_t h = uc & 1, use = uc >> 1;
                 dcol = tmem + h * kHalfCols + lane_base;
+                const uint64_t t_w = prof ? global_ns() : 0;
                 const bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.acc_full[h], use & 1, &sm.abort, wl));
+                padd(pl, kPEpiWaitAcc, t_w);
                 if (ok) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 return ok;
             };
@@ -653,7 +691,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 if (lane == 0) mbar_arrive(&sm.acc_free[uc & 1]);
                 ++uc;
             };
-            // FastScan units: scores TMEM -> shared memory or scratch (16-bit wrap)
+            // FastScan units: scores TMEM -> the scratch (16-bit wrap)
+            const uint64_t t_copy = prof ? global_ns() : 0;
             for (int g = 0; g < geo.ng && geo.fs_slabs > 0 && !bad; ++g) {
                 uint32_t dcol;
                 if (!unit_begin(dcol)) {
@@ -677,6 +716,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 fail(8);
                 break;
             }
+            padd(pl, kPEpiCopy, t_copy);
+            const uint64_t t_sel = prof ? global_ns() : 0;
             // the kept set of each query (warp per query) and its candidates' tie keys
             int sb = 0;  // staging buffer of the current query
             if (S.fs && e < nq) stage_row(sm.stage[e][0], scp + e * NP, n, lane);
@@ -794,6 +835,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
             }
             bad = epi_sync_or(false);
+            padd(pl, kPEpiSelect, t_sel);
+            const uint64_t t_rr = prof ? global_ns() : 0;
             // rerank units: thread per row, the distances of the kept (query, row) pairs
             for (int g = 0; g < geo.ng && !bad; ++g) {
                 uint32_t dcol;
@@ -834,6 +877,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 fail(9);
                 break;
             }
+            padd(pl, kPEpiRerank, t_rr);
+            padd(pl, kPEpi, t_body);
             if (lane == 0) mbar_arrive(&sm.item_empty[si]);
         }
     }
