@@ -65,7 +65,7 @@ constexpr int kWordCap = 4096;                      // kept-row bitmap words: N 
 constexpr int kSlots = 2;                           // items in flight
 constexpr int kPF = 3;                              // stages loaded ahead
 constexpr uint32_t kWaitLimit = 1u << 24;
-static_assert(kMaxQ * 8 <= 4 * kBuildThreads, "a B stage is at most four 16-byte chunks per builder");
+static_assert(kMaxQ * 8 <= 2 * 2 * kBuildThreads, "a B stage: two steps of two 16-byte chunks per builder");
 static_assert(kTcScoreScratch >= (int64_t)kMaxQ * kTcMaxRows, "score scratch of one item");
 static_assert(kWordCap * 32 >= 1024 * kRows, "N * T <= 1024 (tc_queries_per_item)");
 
@@ -211,49 +211,71 @@ __device__ __forceinline__ uint4 q_natural(uint4 v) {
                       __byte_perm(v.z, v.w, 0x5140), __byte_perm(v.z, v.w, 0x7362));
 }
 
-// Global loads of one builder thread for one stage.
+// Global loads of one builder thread for one step (a stage or half of one).
 struct StageLoad {
-    uint4 v[4];
+    uint4 v[2];
 };
 
 // The units of an item: ng groups of Tg row tiles (the last one has last_nt), first the
-// FastScan units (when FastScan runs), then the rerank units.
+// FastScan units (when FastScan runs), then the rerank units.  The builders write a stage
+// in one or two steps of at most two 16-byte loads per thread: B stages of more than 64
+// queries and 8-bit rerank A stages take two (pb, pa).
 struct ItemGeo {
-    int Tg, ng, last_nt, fs_slabs, rr_slabs, fs_stages;  // fs_stages: stages of all FS units
+    int Tg, ng, last_nt, fs_slabs, rr_slabs, pb, pa_rr, fs_steps;  // fs_steps: all FS units
     __device__ int unit_tiles(int g) const { return g == ng - 1 ? last_nt : Tg; }
 };
 
-__device__ __forceinline__ ItemGeo item_geo(int T, int N, bool fs, int fs_slabs, int rr_slabs) {
+__device__ __forceinline__ ItemGeo item_geo(int T, int N, bool fs, int fs_slabs, int rr_slabs,
+                                            int nbits) {
     ItemGeo g;
     g.Tg = min(T, max(1, kHalfCols / N));
     g.ng = (T + g.Tg - 1) / g.Tg;
     g.last_nt = T - (g.ng - 1) * g.Tg;
     g.fs_slabs = fs ? fs_slabs : 0;
     g.rr_slabs = rr_slabs;
-    g.fs_stages = g.fs_slabs * ((g.ng - 1) * (1 + g.Tg) + 1 + g.last_nt);
+    g.pb = N > 64 ? 2 : 1;
+    g.pa_rr = nbits == 8 ? 2 : 1;
+    g.fs_steps = g.fs_slabs * ((g.ng - 1) * (g.pb + g.Tg) + g.pb + g.last_nt);
     return g;
 }
 
-// Stage g of an item (per unit and K slab: one B stage, then the unit's A stages): kind 0
-// FastScan B (LUTs), 1 FastScan A (one-hot rows), 2 rerank B (q_i8), 3 rerank A (codes);
-// s = K slab, t = row tile.
+__device__ __forceinline__ int item_steps(const ItemGeo& g) {
+    return g.fs_steps + g.rr_slabs * ((g.ng - 1) * (g.pb + g.Tg * g.pa_rr) + g.pb + g.last_nt * g.pa_rr);
+}
+
+// Step g of an item (per unit and K slab: the B stage, then the unit's A stages, each in
+// its parts): kind 0 FastScan B (LUTs), 1 FastScan A (one-hot rows), 2 rerank B (q_i8),
+// 3 rerank A (codes); s = K slab, t = row tile; part of the stage, last = its final part.
 struct StageRef {
-    int kind, s, t;
+    int kind, s, t, part;
+    bool last;
 };
 
 __device__ __forceinline__ StageRef stage_of(int g, const ItemGeo& geo) {
-    const bool fs = g < geo.fs_stages;
-    const int gg = fs ? g : g - geo.fs_stages;
+    const bool fs = g < geo.fs_steps;
+    const int gg = fs ? g : g - geo.fs_steps;
     const int S = fs ? geo.fs_slabs : geo.rr_slabs;
-    const int per_full = S * (1 + geo.Tg);
+    const int pa = fs ? 1 : geo.pa_rr;
+    const int per_full = S * (geo.pb + geo.Tg * pa);
     const int grp = min(gg / per_full, geo.ng - 1);
     const int rem = gg - grp * per_full;
     const int nt = geo.unit_tiles(grp);
+    const int per_slab = geo.pb + nt * pa;
     StageRef r;
-    r.s = rem / (1 + nt);
-    const int u = rem - r.s * (1 + nt);
-    r.t = grp * geo.Tg + u - 1;
-    r.kind = (fs ? 0 : 2) + (u > 0 ? 1 : 0);
+    r.s = rem / per_slab;
+    const int u = rem - r.s * per_slab;
+    if (u < geo.pb) {
+        r.kind = fs ? 0 : 2;
+        r.t = -1;
+        r.part = u;
+        r.last = u == geo.pb - 1;
+    } else {
+        const int ua = u - geo.pb;
+        r.kind = fs ? 1 : 3;
+        r.t = grp * geo.Tg + ua / pa;
+        r.part = ua - (ua / pa) * pa;
+        r.last = r.part == pa - 1;
+    }
     return r;
 }
 
@@ -425,17 +447,18 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             if (S.item < 0) break;
             const int n = S.n, nq = S.nq;
             const int64_t beg = S.beg;
-            const ItemGeo geo = item_geo(S.T, S.N, S.fs != 0, fs_slabs, rr_slabs);
-            const int nst = geo.fs_stages + geo.rr_slabs * ((geo.ng - 1) * (1 + geo.Tg) + 1 + geo.last_nt);
+            const ItemGeo geo = item_geo(S.T, S.N, S.fs != 0, fs_slabs, rr_slabs, a.nbits);
+            const int nst = item_steps(geo);
             const uint2* fsl = a.fs + a.fs_blk_off[S.list] * (int64_t)a.nchunks * 32;
             auto load = [&](int g, StageLoad& L) {
                 if (g >= nst) return;
                 const StageRef st = stage_of(g, geo);
                 if (st.kind == 0 || st.kind == 2) {
-                    // queries' LUT (kind 0) or q_i8 (kind 2) slab: 16-byte chunk c of query i
+                    // queries' LUT (kind 0) or q_i8 (kind 2) slab, queries 64 * part + 0..63:
+                    // 16-byte chunk c of query i
 #pragma unroll
-                    for (int m = 0; m < 4; ++m) {
-                        const int idx = bt + m * kBuildThreads, i = idx >> 3, c = idx & 7;
+                    for (int m = 0; m < 2; ++m) {
+                        const int idx = bt + m * kBuildThreads, i = (idx >> 3) + 64 * st.part, c = idx & 7;
                         L.v[m] = make_uint4(0u, 0u, 0u, 0u);
                         if (i < nq) {
                             const int q = S.q[i];
@@ -460,10 +483,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         const int d0 = st.s * kSlab + hh * 64;  // this thread's 64 dimensions
                         if (d0 >= a.D) return;
                         const uint8_t* crow = a.codes + (beg + v) * (int64_t)a.code_bytes;
-                        if (a.nbits == 8) {
+                        if (a.nbits == 8) {  // part p: dimensions d0 + 32 p .. d0 + 32 p + 31
 #pragma unroll
-                            for (int u = 0; u < 4; ++u)
-                                L.v[u] = __ldg(reinterpret_cast<const uint4*>(crow + d0 + 16 * u));
+                            for (int u = 0; u < 2; ++u)
+                                L.v[u] = __ldg(reinterpret_cast<const uint4*>(crow + d0 + 32 * st.part + 16 * u));
                         } else {
                             L.v[0] = __ldg(reinterpret_cast<const uint4*>(crow + d0 / 2));
                             L.v[1] = __ldg(reinterpret_cast<const uint4*>(crow + d0 / 2 + 16));
@@ -474,8 +497,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             auto build = [&](const StageRef& st, const StageLoad& L, uint8_t* X) {
                 if (st.kind == 0 || st.kind == 2) {
 #pragma unroll
-                    for (int m = 0; m < 4; ++m) {
-                        const int idx = bt + m * kBuildThreads, i = idx >> 3, c = idx & 7;
+                    for (int m = 0; m < 2; ++m) {
+                        const int idx = bt + m * kBuildThreads, i = (idx >> 3) + 64 * st.part, c = idx & 7;
                         if (i < S.N) {
                             uint4 w = L.v[m];
                             if (st.kind == 0) {
@@ -505,7 +528,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         if (d0 >= a.D) return;
                         if (a.nbits == 8) {
 #pragma unroll
-                            for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + u)) = L.v[u];
+                            for (int u = 0; u < 2; ++u)
+                                *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + 2 * st.part + u)) = L.v[u];
                         } else {  // 4-bit, low nibble = even dimension: 32 code bytes -> 64 dims
 #pragma unroll
                             for (int u = 0; u < 2; ++u) {
@@ -533,19 +557,23 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 const uint32_t pos = is_b ? gb : ga;
                 const int ns = is_b ? kNB : kNA;
                 const uint32_t s = pos % ns, use = pos / ns;
-                uint64_t* empty = is_b ? &sm.b_empty[s] : &sm.a_empty[s];
-                const uint64_t t_w = prof ? global_ns() : 0;
-                const bool freed = use == 0 || mbar_wait(empty, (use - 1) & 1, &sm.abort, wl);
-                padd(pl, kPBuildWaitSlot, t_w);
-                if (!__all_sync(0xffffffffu, freed)) return false;
+                if (st.part == 0) {
+                    uint64_t* empty = is_b ? &sm.b_empty[s] : &sm.a_empty[s];
+                    const uint64_t t_w = prof ? global_ns() : 0;
+                    const bool freed = use == 0 || mbar_wait(empty, (use - 1) & 1, &sm.abort, wl);
+                    padd(pl, kPBuildWaitSlot, t_w);
+                    if (!__all_sync(0xffffffffu, freed)) return false;
+                }
                 build(st, cur, (is_b ? ring_b : ring_a) + s * kStageBytes);
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(is_b ? &sm.b_full[s] : &sm.a_full[s]);
-                if (is_b)
-                    ++gb;
-                else
-                    ++ga;
+                if (st.last) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(is_b ? &sm.b_full[s] : &sm.a_full[s]);
+                    if (is_b)
+                        ++gb;
+                    else
+                        ++ga;
+                }
                 return true;
             };
             StageLoad L0, L1, L2, L3;
@@ -585,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 const uint64_t t_item = prof ? global_ns() : 0;
                 const int N = S.N;
                 const uint32_t idesc = idesc_i8(N);
-                const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs);
+                const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs, a.nbits);
                 bool ok = true;
                 // one unit: per slab the B stage then the unit's A stages (nk K-steps of 32)
                 // into half uc & 1, once the epilogue read out the unit two before
@@ -671,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             if (S.item < 0) break;
             const int n = S.n, nq = S.nq, N = S.N;
             const int64_t beg = S.beg;
-            const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs);
+            const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs, a.nbits);
             const int NP = S.T * kRows, W = S.T * 4;  // score row stride, bitmap words per query
             int16_t* const scp = sc_global;
             const int c_lo = half * (N >> 1), c_hi = c_lo + (N >> 1);
