@@ -9,7 +9,8 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libhanns_gpu.so")
+# HANNS_GPU_LIB: another build of the same library (an experiment's variant)
+LIB_PATH = os.environ.get("HANNS_GPU_LIB") or os.path.join(HERE, "lib", "libhanns_gpu.so")
 
 f32p = C.POINTER(C.c_float)
 i64p = C.POINTER(C.c_int64)

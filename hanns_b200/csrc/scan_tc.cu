@@ -243,41 +243,14 @@ __device__ __forceinline__ int item_steps(const ItemGeo& g) {
     return g.fs_steps + g.rr_slabs * ((g.ng - 1) * (g.pb + g.Tg * g.pa_rr) + g.pb + g.last_nt * g.pa_rr);
 }
 
-// Step g of an item (per unit and K slab: the B stage, then the unit's A stages, each in
-// its parts): kind 0 FastScan B (LUTs), 1 FastScan A (one-hot rows), 2 rerank B (q_i8),
-// 3 rerank A (codes); s = K slab, t = row tile; part of the stage, last = its final part.
+// A builder step (per unit and K slab: the B stage, then the unit's A stages, each in its
+// parts): kind 0 FastScan B (LUTs), 1 FastScan A (one-hot rows), 2 rerank B (q_i8), 3 rerank
+// A (codes); s = K slab, t = row tile; part of the stage, last = its final part.
 struct StageRef {
     int kind, s, t, part;
     bool last;
 };
 
-__device__ __forceinline__ StageRef stage_of(int g, const ItemGeo& geo) {
-    const bool fs = g < geo.fs_steps;
-    const int gg = fs ? g : g - geo.fs_steps;
-    const int S = fs ? geo.fs_slabs : geo.rr_slabs;
-    const int pa = fs ? 1 : geo.pa_rr;
-    const int per_full = S * (geo.pb + geo.Tg * pa);
-    const int grp = min(gg / per_full, geo.ng - 1);
-    const int rem = gg - grp * per_full;
-    const int nt = geo.unit_tiles(grp);
-    const int per_slab = geo.pb + nt * pa;
-    StageRef r;
-    r.s = rem / per_slab;
-    const int u = rem - r.s * per_slab;
-    if (u < geo.pb) {
-        r.kind = fs ? 0 : 2;
-        r.t = -1;
-        r.part = u;
-        r.last = u == geo.pb - 1;
-    } else {
-        const int ua = u - geo.pb;
-        r.kind = fs ? 1 : 3;
-        r.t = grp * geo.Tg + ua / pa;
-        r.part = ua - (ua / pa) * pa;
-        r.last = r.part == pa - 1;
-    }
-    return r;
-}
 
 // Copies the first n scores of a score row (global, 256-byte aligned) into a staging buffer
 // (shared, 16-byte aligned) with 16-byte cp.async by the 32 lanes of a warp, as one group.
@@ -286,6 +259,50 @@ __device__ __forceinline__ void stage_row(int16_t* dst, const int16_t* src, int 
     for (int c = lane; c * 8 < n; c += 32)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + c * 16), "l"(src + c * 8) : "memory");
     asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// A builder's position in its item's steps: phase (0 FastScan, 1 rerank), unit, K slab, and
+// place u in the slab (u < pb: part u of the B stage; else part of A stage (u - pb) / pa).
+// Advanced step by step (no division per step).
+struct StepPos {
+    int phase, grp, s, u;
+};
+
+__device__ __forceinline__ StepPos step_begin(const ItemGeo& geo) {
+    StepPos p;
+    p.phase = geo.fs_slabs > 0 ? 0 : 1;
+    p.grp = p.s = p.u = 0;
+    return p;
+}
+
+__device__ __forceinline__ StageRef step_ref(const StepPos& p, const ItemGeo& geo) {
+    StageRef r;
+    r.s = p.s;
+    if (p.u < geo.pb) {
+        r.kind = p.phase ? 2 : 0;
+        r.t = -1;
+        r.part = p.u;
+        r.last = p.u == geo.pb - 1;
+    } else {
+        const int pa = p.phase ? geo.pa_rr : 1;  // 1 or 2
+        const int ua = p.u - geo.pb, tt = pa == 2 ? ua >> 1 : ua;
+        r.kind = p.phase ? 3 : 1;
+        r.t = p.grp * geo.Tg + tt;
+        r.part = ua - tt * pa;
+        r.last = r.part == pa - 1;
+    }
+    return r;
+}
+
+__device__ __forceinline__ void step_next(StepPos& p, const ItemGeo& geo) {
+    const int pa = p.phase ? geo.pa_rr : 1;
+    if (++p.u < geo.pb + geo.unit_tiles(p.grp) * pa) return;
+    p.u = 0;
+    if (++p.s < (p.phase ? geo.rr_slabs : geo.fs_slabs)) return;
+    p.s = 0;
+    if (++p.grp < geo.ng) return;
+    p.grp = 0;
+    p.phase = 1;  // (past the rerank phase the item is over: the step count bounds it)
 }
 
 // Hint: the byte range [p, p + bytes) into L2 (p and bytes multiples of 16, bytes > 0).
@@ -450,9 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             const ItemGeo geo = item_geo(S.T, S.N, S.fs != 0, fs_slabs, rr_slabs, a.nbits);
             const int nst = item_steps(geo);
             const uint2* fsl = a.fs + a.fs_blk_off[S.list] * (int64_t)a.nchunks * 32;
-            auto load = [&](int g, StageLoad& L) {
-                if (g >= nst) return;
-                const StageRef st = stage_of(g, geo);
+            auto load = [&](const StageRef& st, StageLoad& L) {
                 if (st.kind == 0 || st.kind == 2) {
                     // queries' LUT (kind 0) or q_i8 (kind 2) slab, queries 64 * part + 0..63:
                     // 16-byte chunk c of query i
@@ -550,9 +565,16 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
             };
             // write stage g from cur after issuing the loads of stage g + kPF into pf
+            StepPos pc = step_begin(geo), pp = pc;  // the step written, the step loaded next
+            auto load_next = [&](int g, StageLoad& L) {
+                if (g >= nst) return;
+                load(step_ref(pp, geo), L);
+                step_next(pp, geo);
+            };
             auto step = [&](int g, StageLoad& cur, StageLoad& pf) -> bool {
-                load(g + kPF, pf);
-                const StageRef st = stage_of(g, geo);
+                load_next(g + kPF, pf);
+                const StageRef st = step_ref(pc, geo);
+                step_next(pc, geo);
                 const bool is_b = (st.kind & 1) == 0;
                 const uint32_t pos = is_b ? gb : ga;
                 const int ns = is_b ? kNB : kNA;
@@ -577,9 +599,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 return true;
             };
             StageLoad L0, L1, L2, L3;
-            load(0, L0);
-            load(1, L1);
-            load(2, L2);
+            load_next(0, L0);
+            load_next(1, L1);
+            load_next(2, L2);
             bool ok = true;
             for (int g = 0; g < nst && ok; g += 4) {
                 ok = step(g, L0, L3);
