@@ -63,7 +63,7 @@ constexpr int kStageBytes = kRows * kSlab;          // 16 KiB
 constexpr int kNA = 4, kNB = 2;                     // ring stages
 constexpr int kWordCap = 4096;                      // kept-row bitmap words: N * T * 4
 constexpr int kSlots = 2;                           // items in flight
-constexpr int kPF = 3;                              // stages loaded ahead
+constexpr int kPF = 2;                              // steps loaded ahead
 constexpr uint32_t kWaitLimit = 1u << 24;
 static_assert(kMaxQ * 8 <= 2 * 2 * kBuildThreads, "a B stage: two steps of two 16-byte chunks per builder");
 static_assert(kTcScoreScratch >= (int64_t)kMaxQ * kTcMaxRows, "score scratch of one item");
@@ -90,7 +90,6 @@ struct TcSmem {
     int16_t stage[kEpiWarps][2][kTcMaxRows];
     uint32_t bitmap[kWordCap];  // kept rows [query][word], word stride T * 4
     int prefix[kWordCap];       // kept rows before each bitmap word
-    uint32_t hist[kEpiWarps][256];
     ItemSlot slot[kSlots];
     uint64_t a_full[kNA], a_empty[kNA], b_full[kNB], b_empty[kNB];
     uint64_t item_full[kSlots], item_empty[kSlots];
@@ -598,16 +597,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
                 return true;
             };
-            StageLoad L0, L1, L2, L3;
+            StageLoad L0, L1, L2;
             load_next(0, L0);
             load_next(1, L1);
-            load_next(2, L2);
             bool ok = true;
-            for (int g = 0; g < nst && ok; g += 4) {
-                ok = step(g, L0, L3);
+            for (int g = 0; g < nst && ok; g += 3) {
+                ok = step(g, L0, L2);
                 if (ok && g + 1 < nst) ok = step(g + 1, L1, L0);
                 if (ok && g + 2 < nst) ok = step(g + 2, L2, L1);
-                if (ok && g + 3 < nst) ok = step(g + 3, L3, L2);
             }
             if (!ok) {
                 fail(6);
@@ -784,13 +781,21 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
                 const int bsi = S.bsi[i];
                 const uint64_t* bw = bsi >= 0 ? a.bitsets + (int64_t)bsi * a.bitset_words : nullptr;
-                auto live = [&](int v) { return !bw || !filtered(bw, a.bitset_len, a.ids[beg + v]); };
-                int n_live = n;
-                if (bw) {
-                    int c = 0;
-                    for (int v = lane; v < n; v += 32) c += live(v) ? 1 : 0;
-                    n_live = warp_sum(c);
-                }
+                // the live rows, as this lane's bits: row v = lane + 32 j is bit j of lm0 (j < 32)
+                // or of lm1 (j >= 32); n <= kTcMaxRows = 2048 rows
+                uint32_t lm0 = 0u, lm1 = 0u;
+                for (int v = lane, j = 0; v < n; v += 32, ++j)
+                    if (!bw || !filtered(bw, a.bitset_len, a.ids[beg + v])) {
+                        if (j < 32)
+                            lm0 |= 1u << j;
+                        else
+                            lm1 |= 1u << (j - 32);
+                    }
+                auto live = [&](int v) {
+                    const int j = v >> 5;
+                    return (((j < 32 ? lm0 : lm1) >> (j & 31)) & 1u) != 0u;
+                };
+                const int n_live = __reduce_add_sync(0xffffffffu, __popc(lm0) + __popc(lm1));
                 const int16_t* sv = sm.stage[e][sb];
                 uint32_t* bm = sm.bitmap + i * W;
                 int* px = sm.prefix + i * W;
@@ -805,8 +810,30 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         k = (uint32_t)(32767 - (int)sv[v]);
                         return true;
                     };
-                    int c_gt = 0, c_eq = 0;
-                    const uint32_t tau = warp_radix_kth16(n, a.n_cand, key_at, sm.hist[e], &c_gt, &c_eq);
+                    // s*: binary search on the score, counting live rows with score >= t by
+                    // per-lane tallies and one warp reduction per probe (no shared atomics)
+                    auto count_ge = [&](int t) {
+                        int c = 0;
+                        for (int v = lane; v < n; v += 32) c += (live(v) && (int)sv[v] >= t) ? 1 : 0;
+                        return (int)__reduce_add_sync(0xffffffffu, (unsigned)c);
+                    };
+                    int lo = 32767, hi = -32768;
+                    for (int v = lane; v < n; v += 32)
+                        if (live(v)) {
+                            lo = min(lo, (int)sv[v]);
+                            hi = max(hi, (int)sv[v]);
+                        }
+                    lo = __reduce_min_sync(0xffffffffu, lo);  // count_ge(lo) = n_live > n_cand
+                    hi = __reduce_max_sync(0xffffffffu, hi);
+                    while (lo < hi) {
+                        const int mid = lo + ((hi - lo + 1) >> 1);
+                        if (count_ge(mid) >= a.n_cand)
+                            lo = mid;
+                        else
+                            hi = mid - 1;
+                    }
+                    const int c_gt = count_ge(lo + 1), c_eq = count_ge(lo) - c_gt;
+                    const uint32_t tau = (uint32_t)(32767 - lo);  // the key of s*
                     // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
                     int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = c_gt;
                     for (int base = 0; c_gt + c_eq != a.n_cand && base < n; base += 32) {
