@@ -90,6 +90,7 @@ struct TcSmem {
     int16_t stage[kEpiWarps][2][kTcMaxRows];
     uint32_t bitmap[kWordCap];  // kept rows [query][word], word stride T * 4
     int prefix[kWordCap];       // kept rows before each bitmap word
+    uint32_t hist[kEpiWarps][256];
     ItemSlot slot[kSlots];
     uint64_t a_full[kNA], a_empty[kNA], b_full[kNB], b_empty[kNB];
     uint64_t item_full[kSlots], item_empty[kSlots];
@@ -810,30 +811,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         k = (uint32_t)(32767 - (int)sv[v]);
                         return true;
                     };
-                    // s*: binary search on the score, counting live rows with score >= t by
-                    // per-lane tallies and one warp reduction per probe (no shared atomics)
-                    auto count_ge = [&](int t) {
-                        int c = 0;
-                        for (int v = lane; v < n; v += 32) c += (live(v) && (int)sv[v] >= t) ? 1 : 0;
-                        return (int)__reduce_add_sync(0xffffffffu, (unsigned)c);
-                    };
-                    int lo = 32767, hi = -32768;
-                    for (int v = lane; v < n; v += 32)
-                        if (live(v)) {
-                            lo = min(lo, (int)sv[v]);
-                            hi = max(hi, (int)sv[v]);
-                        }
-                    lo = __reduce_min_sync(0xffffffffu, lo);  // count_ge(lo) = n_live > n_cand
-                    hi = __reduce_max_sync(0xffffffffu, hi);
-                    while (lo < hi) {
-                        const int mid = lo + ((hi - lo + 1) >> 1);
-                        if (count_ge(mid) >= a.n_cand)
-                            lo = mid;
-                        else
-                            hi = mid - 1;
-                    }
-                    const int c_gt = count_ge(lo + 1), c_eq = count_ge(lo) - c_gt;
-                    const uint32_t tau = (uint32_t)(32767 - lo);  // the key of s*
+                    int c_gt = 0, c_eq = 0;
+                    const uint32_t tau = warp_radix_kth16(n, a.n_cand, key_at, sm.hist[e], &c_gt, &c_eq);
                     // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
                     int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = c_gt;
                     for (int base = 0; c_gt + c_eq != a.n_cand && base < n; base += 32) {
