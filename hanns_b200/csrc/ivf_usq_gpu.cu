@@ -702,13 +702,16 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     w_lq_.reserve((size_t)nb * nprobe);
     w_items_.reserve((size_t)nb * nprobe);
     HANNS_CUDA_OK(cudaMemsetAsync(w_counters_.p, 0, 3 * sizeof(int), s));
-    // lists of at most kTcMaxRows rows take the tensor-core scan (HANNS_GPU_SCAN=simt: none)
+    // lists of at most kTcMaxRows rows take the tensor-core scan; HANNS_GPU_SCAN=simt: none,
+    // =hybrid: only lists without FastScan (|list| <= n_cand)
+    const int n_cand = (int)n_candidates(nbits_, k);
     const char* scan_mode = std::getenv("HANNS_GPU_SCAN");
     const bool use_tc = !(scan_mode && std::strcmp(scan_mode, "simt") == 0);
+    const bool hybrid = scan_mode && std::strcmp(scan_mode, "hybrid") == 0;
+    const int tc_rows = !use_tc ? 0 : hybrid ? std::min(kTcMaxRows, n_cand) : kTcMaxRows;
     launch_group_pairs(st.probes, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr, list_off_.p,
-                       use_tc ? kTcMaxRows : 0, kQueriesPerItem, w_cnt_.p, w_cursor_.p,
-                       w_lq_off_.p, w_item_off_.p, w_counters_.p, w_lq_.p, w_items_.p, s);
-    const int n_cand = (int)n_candidates(nbits_, k);
+                       tc_rows, kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p, w_item_off_.p,
+                       w_counters_.p, w_lq_.p, w_items_.p, s);
     const int64_t q_stride = cand_stride(nprobe, k);
     w_pair_off_.reserve((size_t)nb * (nprobe + 1));
     launch_pair_offsets(st.probes, nb, nprobe, list_off_.p, nlist_, sharded_ ? owned_.p : nullptr,

@@ -124,8 +124,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint64_t limit_ns) {
     const uint32_t addr = smem_u32(bar);
-    const uint64_t t0 = global_ns();
-    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+    auto try_wait = [&]() {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -134,7 +133,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
             : "=r"(done)
             : "r"(addr), "r"(parity)
             : "memory");
-        if (done) return true;
+        return done != 0;
+    };
+    if (try_wait()) return true;  // (most waits: no timer read)
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+        if (try_wait()) return true;
         if (*abort || global_ns() - t0 > limit_ns) return false;
     }
     return false;
@@ -144,6 +148,9 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
+// The descriptor of saddr + 32 k bytes (a K step of 32 bytes inside the swizzle atom):
+// the start address field counts 16-byte units.
+__device__ __forceinline__ uint64_t desc_k(uint64_t d, int k4) { return d + (uint64_t)(2 * k4); }
 
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                         uint32_t idesc, uint32_t accumulate) {
@@ -655,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         }
                         padd(true, kPMmaWaitFull, t_w);
                         const int nk = min(kSlab, k_bytes - s * kSlab) / 32;
-                        const uint32_t bbase = smem_u32(ring_b + bs * kStageBytes);
+                        const uint64_t bd = sw128_desc(smem_u32(ring_b + bs * kStageBytes));
                         for (int t = 0; t < nt; ++t) {
                             const uint32_t as = ga % kNA;
                             t_w = prof ? global_ns() : 0;
@@ -665,10 +672,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                             }
                             padd(true, kPMmaWaitFull, t_w);
                             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                            const uint32_t abase = smem_u32(ring_a + as * kStageBytes);
+                            const uint64_t ad = sw128_desc(smem_u32(ring_a + as * kStageBytes));
                             for (int k4 = 0; k4 < nk; ++k4)
-                                umma_i8(dcol + (uint32_t)(t * N), sw128_desc(abase + k4 * 32),
-                                        sw128_desc(bbase + k4 * 32), idesc, (s > 0 || k4 > 0) ? 1u : 0u);
+                                umma_i8(dcol + (uint32_t)(t * N), desc_k(ad, k4), desc_k(bd, k4), idesc,
+                                        (s > 0 || k4 > 0) ? 1u : 0u);
                             umma_commit(&sm.a_empty[as]);
                             ++ga;
                         }
@@ -811,8 +818,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         k = (uint32_t)(32767 - (int)sv[v]);
                         return true;
                     };
-                    int c_gt = 0, c_eq = 0;
-                    const uint32_t tau = warp_radix_kth16(n, a.n_cand, key_at, sm.hist[e], &c_gt, &c_eq);
+                    // range-adaptive radix passes (a query's scores cluster: bins spread over
+                    // the range it spans collide far less than fixed high-byte bins)
+                    int c_gt = 0;
+                    const uint32_t tau = warp_radix_kth(n, a.n_cand, key_at, sm.hist[e], &c_gt);
+                    const int c_eq = -1;  // not counted: the boundary pass below always runs
                     // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
                     int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = c_gt;
                     for (int base = 0; c_gt + c_eq != a.n_cand && base < n; base += 32) {
