@@ -27,11 +27,11 @@
 // its distance key to the query's candidate region.
 //
 // Warp roles (17 warps):
-//   warps 0-7   builders: fetch items (warp 0), then write the operand stages of the item
-//               in MMA order -- per unit and K slab of 128 bytes one B stage (the queries)
-//               and the unit's A stages (its row tiles) -- into two rings (A: kNA x 16 KiB,
-//               B: kNB x 16 KiB; 128-byte swizzle, K-major); the global loads of stage
-//               g + kPF are in flight while stage g is written
+//   warps 0-7   builders: fetch items (warp 0), then write the operand stages of the item --
+//               per unit and K slab of 128 bytes one B stage (the queries) and the unit's A
+//               stages (its row tiles) -- into two rings (A: kNA x 16 KiB, B: kNB x 16 KiB;
+//               128-byte swizzle, K-major); a warp builds a whole stage (round robin over
+//               the warps) from bytes it copies in with cp.async
 //   warps 8-15  epilogue: FastScan scores TMEM -> the CTA's global scratch (L2), the kept
 //               set of each query (warp per query, its score row staged in shared memory)
 //               with the candidates' tie keys, the distances of the kept rows (thread per
@@ -53,7 +53,6 @@ namespace {
 constexpr int kBuildWarps = 8, kEpiWarps = 8;
 constexpr int kCtrlWarp = kBuildWarps + kEpiWarps;  // 16
 constexpr int kThreads = (kCtrlWarp + 1) * 32;      // 544
-constexpr int kBuildThreads = kBuildWarps * 32;     // 256
 constexpr int kRows = 128;                          // MMA M: list rows per tile
 constexpr int kMaxQ = 128;                          // MMA N limit: queries per item
 constexpr int kHalfCols = 256;                      // TMEM columns of one unit
@@ -63,9 +62,7 @@ constexpr int kStageBytes = kRows * kSlab;          // 16 KiB
 constexpr int kNA = 4, kNB = 2;                     // ring stages
 constexpr int kWordCap = 4096;                      // kept-row bitmap words: N * T * 4
 constexpr int kSlots = 2;                           // items in flight
-constexpr int kPF = 2;                              // steps loaded ahead
 constexpr uint32_t kWaitLimit = 1u << 24;
-static_assert(kMaxQ * 8 <= 2 * 2 * kBuildThreads, "a B stage: two steps of two 16-byte chunks per builder");
 static_assert(kTcScoreScratch >= (int64_t)kMaxQ * kTcMaxRows, "score scratch of one item");
 static_assert(kWordCap * 32 >= 1024 * kRows, "N * T <= 1024 (tc_queries_per_item)");
 
@@ -218,98 +215,72 @@ __device__ __forceinline__ uint4 q_natural(uint4 v) {
                       __byte_perm(v.z, v.w, 0x5140), __byte_perm(v.z, v.w, 0x7362));
 }
 
-// Global loads of one builder thread for one step (a stage or half of one).
-struct StageLoad {
-    uint4 v[2];
-};
-
 // The units of an item: ng groups of Tg row tiles (the last one has last_nt), first the
-// FastScan units (when FastScan runs), then the rerank units.  The builders write a stage
-// in one or two steps of at most two 16-byte loads per thread: B stages of more than 64
-// queries and 8-bit rerank A stages take two (pb, pa).
+// FastScan units (when FastScan runs), then the rerank units.  Per unit and K slab the MMA
+// consumes one B stage (the queries) and then the unit's A stages (its row tiles).
 struct ItemGeo {
-    int Tg, ng, last_nt, fs_slabs, rr_slabs, pb, pa_rr, fs_steps;  // fs_steps: all FS units
+    int Tg, ng, last_nt, fs_slabs, rr_slabs, fs_stages;  // fs_stages: stages of all FS units
     __device__ int unit_tiles(int g) const { return g == ng - 1 ? last_nt : Tg; }
 };
 
-__device__ __forceinline__ ItemGeo item_geo(int T, int N, bool fs, int fs_slabs, int rr_slabs,
-                                            int nbits) {
+__device__ __forceinline__ ItemGeo item_geo(int T, int N, bool fs, int fs_slabs, int rr_slabs) {
     ItemGeo g;
     g.Tg = min(T, max(1, kHalfCols / N));
     g.ng = (T + g.Tg - 1) / g.Tg;
     g.last_nt = T - (g.ng - 1) * g.Tg;
     g.fs_slabs = fs ? fs_slabs : 0;
     g.rr_slabs = rr_slabs;
-    g.pb = N > 64 ? 2 : 1;
-    g.pa_rr = nbits == 8 ? 2 : 1;
-    g.fs_steps = g.fs_slabs * ((g.ng - 1) * (g.pb + g.Tg) + g.pb + g.last_nt);
+    g.fs_stages = g.fs_slabs * (g.ng + T);
     return g;
 }
 
-__device__ __forceinline__ int item_steps(const ItemGeo& g) {
-    return g.fs_steps + g.rr_slabs * ((g.ng - 1) * (g.pb + g.Tg * g.pa_rr) + g.pb + g.last_nt * g.pa_rr);
-}
-
-// A builder step (per unit and K slab: the B stage, then the unit's A stages, each in its
-// parts): kind 0 FastScan B (LUTs), 1 FastScan A (one-hot rows), 2 rerank B (q_i8), 3 rerank
-// A (codes); s = K slab, t = row tile; part of the stage, last = its final part.
-struct StageRef {
-    int kind, s, t, part;
-    bool last;
+// Stage g of an item: kind 0 FastScan B (LUTs), 1 FastScan A (one-hot rows), 2 rerank B
+// (q_i8), 3 rerank A (codes); s = K slab, t = row tile; idx = its place among the item's B
+// stages (kinds 0, 2) or A stages (kinds 1, 3), i.e. its ring position after the item's first.
+struct StageInfo {
+    int kind, s, t, idx;
 };
 
+__device__ __forceinline__ StageInfo stage_info(int g, const ItemGeo& geo, int T) {
+    const bool fs = g < geo.fs_stages;
+    const int gg = fs ? g : g - geo.fs_stages;
+    const int S = fs ? geo.fs_slabs : geo.rr_slabs;
+    const int per_full = S * (1 + geo.Tg);
+    const int grp = min(gg / per_full, geo.ng - 1);
+    const int rem = gg - grp * per_full;
+    const int nt = geo.unit_tiles(grp);
+    StageInfo r;
+    r.s = rem / (1 + nt);
+    const int u = rem - r.s * (1 + nt);
+    if (u == 0) {
+        r.kind = fs ? 0 : 2;
+        r.t = -1;
+        r.idx = (fs ? 0 : geo.fs_slabs * geo.ng) + grp * S + r.s;
+    } else {
+        r.kind = fs ? 1 : 3;
+        r.t = grp * geo.Tg + u - 1;
+        r.idx = (fs ? 0 : geo.fs_slabs * T) + grp * S * geo.Tg + r.s * nt + (u - 1);
+    }
+    return r;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+// This lane's copies so far have landed in shared memory.
+__device__ __forceinline__ void cp_async_drain() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
 
 // Copies the first n scores of a score row (global, 256-byte aligned) into a staging buffer
 // (shared, 16-byte aligned) with 16-byte cp.async by the 32 lanes of a warp, as one group.
 __device__ __forceinline__ void stage_row(int16_t* dst, const int16_t* src, int n, int lane) {
     const uint32_t d = smem_u32(dst);
-    for (int c = lane; c * 8 < n; c += 32)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + c * 16), "l"(src + c * 8) : "memory");
+    for (int c = lane; c * 8 < n; c += 32) cp_async16(d + c * 16, src + c * 8);
     asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
-// A builder's position in its item's steps: phase (0 FastScan, 1 rerank), unit, K slab, and
-// place u in the slab (u < pb: part u of the B stage; else part of A stage (u - pb) / pa).
-// Advanced step by step (no division per step).
-struct StepPos {
-    int phase, grp, s, u;
-};
-
-__device__ __forceinline__ StepPos step_begin(const ItemGeo& geo) {
-    StepPos p;
-    p.phase = geo.fs_slabs > 0 ? 0 : 1;
-    p.grp = p.s = p.u = 0;
-    return p;
-}
-
-__device__ __forceinline__ StageRef step_ref(const StepPos& p, const ItemGeo& geo) {
-    StageRef r;
-    r.s = p.s;
-    if (p.u < geo.pb) {
-        r.kind = p.phase ? 2 : 0;
-        r.t = -1;
-        r.part = p.u;
-        r.last = p.u == geo.pb - 1;
-    } else {
-        const int pa = p.phase ? geo.pa_rr : 1;  // 1 or 2
-        const int ua = p.u - geo.pb, tt = pa == 2 ? ua >> 1 : ua;
-        r.kind = p.phase ? 3 : 1;
-        r.t = p.grp * geo.Tg + tt;
-        r.part = ua - tt * pa;
-        r.last = r.part == pa - 1;
-    }
-    return r;
-}
-
-__device__ __forceinline__ void step_next(StepPos& p, const ItemGeo& geo) {
-    const int pa = p.phase ? geo.pa_rr : 1;
-    if (++p.u < geo.pb + geo.unit_tiles(p.grp) * pa) return;
-    p.u = 0;
-    if (++p.s < (p.phase ? geo.rr_slabs : geo.fs_slabs)) return;
-    p.s = 0;
-    if (++p.grp < geo.ng) return;
-    p.grp = 0;
-    p.phase = 1;  // (past the rerank phase the item is over: the step count bounds it)
 }
 
 // Hint: the byte range [p, p + bytes) into L2 (p and bytes multiples of 16, bytes > 0).
@@ -343,11 +314,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
 
     if (tid == 0) {
         for (int s = 0; s < kNA; ++s) {
-            mbar_init(&sm.a_full[s], kBuildWarps);
+            mbar_init(&sm.a_full[s], 1);
             mbar_init(&sm.a_empty[s], 1);
         }
         for (int s = 0; s < kNB; ++s) {
-            mbar_init(&sm.b_full[s], kBuildWarps);
+            mbar_init(&sm.b_full[s], 1);
             mbar_init(&sm.b_empty[s], 1);
         }
         for (int s = 0; s < kSlots; ++s) {
@@ -386,10 +357,13 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
 
     if (warp < kBuildWarps) {
         // ------------------------------------------------------------ builders
-        const int bt = tid;                            // 0..255
-        const int r = bt & (kRows - 1), hh = bt >> 7;  // A stages: row r, chunks 4hh..4hh+3
-        uint32_t ga = 0, gb = 0;                       // ring positions (the MMA's sequence)
-        int next_it = -1;                              // warp 0 lane 0: the item fetched ahead
+        // Warp w builds the item's stages w, w + 8, w + 16, ... whole: the raw bytes arrive
+        // by cp.async in the stage's ring slot and are transformed there by the lane that
+        // copied them (LUT sign flip, q_i8 to dimension order) or expanded row by row in
+        // ascending rounds of 32 rows (one-hot rows from the sign words, 4-bit codes unpacked)
+        // from raw bytes parked at the slot's end, which no round overwrites before reading.
+        uint32_t ga = 0, gb = 0;  // ring positions of the item's first A / B stage
+        int next_it = -1;         // warp 0 lane 0: the item fetched ahead
         auto fetch_item = [&]() -> int {
             for (;;) {
                 const int it = atomicAdd(a.item_counter, 1);
@@ -469,155 +443,146 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 break;
             }
             if (S.item < 0) break;
-            const int n = S.n, nq = S.nq;
+            const int n = S.n, nq = S.nq, N = S.N, T = S.T;
             const int64_t beg = S.beg;
-            const ItemGeo geo = item_geo(S.T, S.N, S.fs != 0, fs_slabs, rr_slabs, a.nbits);
-            const int nst = item_steps(geo);
+            const ItemGeo geo = item_geo(T, N, S.fs != 0, fs_slabs, rr_slabs);
+            const int nb_st = (geo.fs_slabs + geo.rr_slabs) * geo.ng;  // B stages of the item
+            const int na_st = (geo.fs_slabs + geo.rr_slabs) * T;       // A stages
+            const int nst = na_st + nb_st;
             const uint2* fsl = a.fs + a.fs_blk_off[S.list] * (int64_t)a.nchunks * 32;
-            auto load = [&](const StageRef& st, StageLoad& L) {
-                if (st.kind == 0 || st.kind == 2) {
-                    // queries' LUT (kind 0) or q_i8 (kind 2) slab, queries 64 * part + 0..63:
-                    // 16-byte chunk c of query i
-#pragma unroll
-                    for (int m = 0; m < 2; ++m) {
-                        const int idx = bt + m * kBuildThreads, i = (idx >> 3) + 64 * st.part, c = idx & 7;
-                        L.v[m] = make_uint4(0u, 0u, 0u, 0u);
-                        if (i < nq) {
-                            const int q = S.q[i];
-                            if (st.kind == 0) {
-                                L.v[m] = __ldg(reinterpret_cast<const uint4*>(
-                                    a.lut + ((int64_t)q * a.G * 16 + st.s * kSlab + c * 16)));
-                            } else if (st.s * kSlab + c * 16 < a.D) {
-                                L.v[m] = __ldg(reinterpret_cast<const uint4*>(
-                                    a.q_i8p + ((int64_t)q * a.D + st.s * kSlab + c * 16)));
-                            }
-                        }
-                    }
-                } else {
-                    const int v = st.t * kRows + r;
-                    if (v >= n) return;
-                    if (st.kind == 1) {
-                        // sign nibbles of slabs 2c and 2c + 1 of row v (FastScan block layout)
-                        const uint2 w = __ldg(fsl + ((int64_t)(v >> 5) * a.nchunks + (st.s >> 1)) * 32 + (v & 31));
-                        L.v[0].x = w.x;
-                        L.v[0].y = w.y;
-                    } else {
-                        const int d0 = st.s * kSlab + hh * 64;  // this thread's 64 dimensions
-                        if (d0 >= a.D) return;
-                        const uint8_t* crow = a.codes + (beg + v) * (int64_t)a.code_bytes;
-                        if (a.nbits == 8) {  // part p: dimensions d0 + 32 p .. d0 + 32 p + 31
-#pragma unroll
-                            for (int u = 0; u < 2; ++u)
-                                L.v[u] = __ldg(reinterpret_cast<const uint4*>(crow + d0 + 32 * st.part + 16 * u));
-                        } else {
-                            L.v[0] = __ldg(reinterpret_cast<const uint4*>(crow + d0 / 2));
-                            L.v[1] = __ldg(reinterpret_cast<const uint4*>(crow + d0 / 2 + 16));
-                        }
-                    }
+            bool ok = true;
+            for (int g = warp; g < nst; g += kBuildWarps) {
+                const StageInfo st = stage_info(g, geo, T);
+                const bool is_b = (st.kind & 1) == 0;
+                const uint32_t pos = (is_b ? gb : ga) + (uint32_t)st.idx;
+                const int ns = is_b ? kNB : kNA;
+                const uint32_t slot = pos % ns, use = pos / ns;
+                const uint64_t t_w = prof ? global_ns() : 0;
+                const bool freed = use == 0 ||
+                                   mbar_wait(is_b ? &sm.b_empty[slot] : &sm.a_empty[slot], (use - 1) & 1, &sm.abort, wl);
+                padd(pl, kPBuildWaitSlot, t_w);
+                if (!__all_sync(0xffffffffu, freed)) {
+                    ok = false;
+                    break;
                 }
-            };
-            auto build = [&](const StageRef& st, const StageLoad& L, uint8_t* X) {
-                if (st.kind == 0 || st.kind == 2) {
-#pragma unroll
-                    for (int m = 0; m < 2; ++m) {
-                        const int idx = bt + m * kBuildThreads, i = (idx >> 3) + 64 * st.part, c = idx & 7;
-                        if (i < S.N) {
-                            uint4 w = L.v[m];
-                            if (st.kind == 0) {
-                                // offset-binary LUT byte -> s8 (padding queries read 0 ->
-                                // -128: their accumulator columns are never read)
-                                w.x ^= 0x80808080u;
-                                w.y ^= 0x80808080u;
-                                w.z ^= 0x80808080u;
-                                w.w ^= 0x80808080u;
-                            } else if (a.nbits == 4) {
-                                w = q_natural(w);
+                uint8_t* X = (is_b ? ring_b : ring_a) + slot * kStageBytes;
+                const uint32_t xs = smem_u32(X);
+                if (is_b) {
+                    // queries' LUT (kind 0) or q_i8 (kind 2) slab: chunk c of query i
+                    const int nch = N * 8;
+                    for (int idx = lane; idx < nch; idx += 32) {
+                        const int i = idx >> 3, c = idx & 7;
+                        if (i >= nq) continue;  // padding query: its columns are never read
+                        const int q = S.q[i];
+                        if (st.kind == 0)
+                            cp_async16(xs + sw_off(i, c), a.lut + ((int64_t)q * a.G * 16 + st.s * kSlab + c * 16));
+                        else if (st.s * kSlab + c * 16 < a.D)
+                            cp_async16(xs + sw_off(i, c), a.q_i8p + ((int64_t)q * a.D + st.s * kSlab + c * 16));
+                    }
+                    cp_async_drain();
+                    if (st.kind == 0 || a.nbits == 4) {
+                        for (int idx = lane; idx < nch; idx += 32) {
+                            const int i = idx >> 3, c = idx & 7;
+                            if (i >= nq || (st.kind == 2 && st.s * kSlab + c * 16 >= a.D)) continue;
+                            uint4* w = reinterpret_cast<uint4*>(X + sw_off(i, c));
+                            uint4 v = *w;
+                            if (st.kind == 0) {  // offset-binary LUT byte -> s8
+                                v.x ^= 0x80808080u;
+                                v.y ^= 0x80808080u;
+                                v.z ^= 0x80808080u;
+                                v.w ^= 0x80808080u;
+                            } else {
+                                v = q_natural(v);
                             }
-                            *reinterpret_cast<uint4*>(X + sw_off(i, c)) = w;
+                            *w = v;
                         }
                     }
+                } else if (st.kind == 1) {
+                    // one-hot rows: the slab's sign word of each row (4 bytes) at the slot's end
+                    const uint32_t raw = xs + kStageBytes - 4 * kRows;
+                    for (int r = lane; r < kRows; r += 32) {
+                        const int v = st.t * kRows + r;
+                        if (v < n)
+                            cp_async4(raw + 4 * r, reinterpret_cast<const uint8_t*>(
+                                                        fsl + ((int64_t)(v >> 5) * a.nchunks + (st.s >> 1)) * 32 + (v & 31)) +
+                                                        4 * (st.s & 1));
+                    }
+                    cp_async_drain();
+                    __syncwarp();
+#pragma unroll 1
+                    for (int r = lane; r < kRows; r += 32) {
+                        const int v = st.t * kRows + r;
+                        const uint32_t word = v < n ? *reinterpret_cast<const uint32_t*>(X + kStageBytes - 4 * kRows + 4 * r) : 0u;
+                        __syncwarp();  // the round's raw words are read before its rows overwrite them
+                        if (v < n) {
+#pragma unroll
+                            for (int c = 0; c < 8; ++c)
+                                *reinterpret_cast<uint4*>(X + sw_off(r, c)) = onehot16((word >> (4 * c)) & 15u);
+                        }
+                        __syncwarp();
+                    }
+                } else if (a.nbits == 8) {
+                    // 8-bit codes are the operand: straight into their swizzled places
+                    for (int idx = lane; idx < kRows * 8; idx += 32) {
+                        const int r = idx >> 3, c = idx & 7;
+                        const int v = st.t * kRows + r, d = st.s * kSlab + c * 16;
+                        if (v < n && d < a.D)
+                            cp_async16(xs + sw_off(r, c), a.codes + (beg + v) * (int64_t)a.code_bytes + d);
+                    }
+                    cp_async_drain();
                 } else {
-                    const int v = st.t * kRows + r;
-                    if (v >= n) return;  // rows past the list: their accumulators are never read
-                    if (st.kind == 1) {
-                        const uint32_t word = (st.s & 1) ? L.v[0].y : L.v[0].x;
-                        const uint32_t bits = word >> (16 * hh);
+                    // 4-bit codes: the slab's 64 packed bytes of each row at the slot's second half
+                    const uint32_t raw = xs + kStageBytes / 2;
+                    for (int idx = lane; idx < kRows * 4; idx += 32) {
+                        const int r = idx >> 2, jj = idx & 3;
+                        const int v = st.t * kRows + r;
+                        if (v < n && st.s * kSlab + 32 * jj < a.D)
+                            cp_async16(raw + 64 * r + 16 * jj,
+                                       a.codes + (beg + v) * (int64_t)a.code_bytes + st.s * (kSlab / 2) + 16 * jj);
+                    }
+                    cp_async_drain();
+                    __syncwarp();
+                    const int nj = min(4, (a.D - st.s * kSlab) / 32);  // 32-dimension quarters
+#pragma unroll 1
+                    for (int r = lane; r < kRows; r += 32) {
+                        const int v = st.t * kRows + r;
+                        uint4 c4[4];
 #pragma unroll
-                        for (int jg = 0; jg < 4; ++jg)
-                            *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + jg)) = onehot16((bits >> (4 * jg)) & 15u);
-                    } else {
-                        const int d0 = st.s * kSlab + hh * 64;
-                        if (d0 >= a.D) return;
-                        if (a.nbits == 8) {
+                        for (int jj = 0; jj < 4; ++jj)
+                            c4[jj] = (v < n && jj < nj) ? *reinterpret_cast<const uint4*>(X + kStageBytes / 2 + 64 * r + 16 * jj)
+                                                        : make_uint4(0u, 0u, 0u, 0u);
+                        __syncwarp();  // the round's raw rows are read before its rows overwrite them
+                        if (v < n) {
 #pragma unroll
-                            for (int u = 0; u < 2; ++u)
-                                *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + 2 * st.part + u)) = L.v[u];
-                        } else {  // 4-bit, low nibble = even dimension: 32 code bytes -> 64 dims
-#pragma unroll
-                            for (int u = 0; u < 2; ++u) {
-                                const uint4 c = L.v[u];
+                            for (int jj = 0; jj < 4; ++jj) {
+                                if (jj >= nj) break;
+                                // low nibble = even dimension: 16 code bytes -> 32 dimensions
+                                const uint4 c = c4[jj];
                                 const uint32_t lo0 = c.x & 0x0F0F0F0Fu, hi0 = (c.x >> 4) & 0x0F0F0F0Fu;
                                 const uint32_t lo1 = c.y & 0x0F0F0F0Fu, hi1 = (c.y >> 4) & 0x0F0F0F0Fu;
                                 const uint32_t lo2 = c.z & 0x0F0F0F0Fu, hi2 = (c.z >> 4) & 0x0F0F0F0Fu;
                                 const uint32_t lo3 = c.w & 0x0F0F0F0Fu, hi3 = (c.w >> 4) & 0x0F0F0F0Fu;
-                                *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + 2 * u)) =
+                                *reinterpret_cast<uint4*>(X + sw_off(r, 2 * jj)) =
                                     make_uint4(__byte_perm(lo0, hi0, 0x5140), __byte_perm(lo0, hi0, 0x7362),
                                                __byte_perm(lo1, hi1, 0x5140), __byte_perm(lo1, hi1, 0x7362));
-                                *reinterpret_cast<uint4*>(X + sw_off(r, 4 * hh + 2 * u + 1)) =
+                                *reinterpret_cast<uint4*>(X + sw_off(r, 2 * jj + 1)) =
                                     make_uint4(__byte_perm(lo2, hi2, 0x5140), __byte_perm(lo2, hi2, 0x7362),
                                                __byte_perm(lo3, hi3, 0x5140), __byte_perm(lo3, hi3, 0x7362));
                             }
                         }
+                        __syncwarp();
                     }
                 }
-            };
-            // write stage g from cur after issuing the loads of stage g + kPF into pf
-            StepPos pc = step_begin(geo), pp = pc;  // the step written, the step loaded next
-            auto load_next = [&](int g, StageLoad& L) {
-                if (g >= nst) return;
-                load(step_ref(pp, geo), L);
-                step_next(pp, geo);
-            };
-            auto step = [&](int g, StageLoad& cur, StageLoad& pf) -> bool {
-                load_next(g + kPF, pf);
-                const StageRef st = step_ref(pc, geo);
-                step_next(pc, geo);
-                const bool is_b = (st.kind & 1) == 0;
-                const uint32_t pos = is_b ? gb : ga;
-                const int ns = is_b ? kNB : kNA;
-                const uint32_t s = pos % ns, use = pos / ns;
-                if (st.part == 0) {
-                    uint64_t* empty = is_b ? &sm.b_empty[s] : &sm.a_empty[s];
-                    const uint64_t t_w = prof ? global_ns() : 0;
-                    const bool freed = use == 0 || mbar_wait(empty, (use - 1) & 1, &sm.abort, wl);
-                    padd(pl, kPBuildWaitSlot, t_w);
-                    if (!__all_sync(0xffffffffu, freed)) return false;
-                }
-                build(st, cur, (is_b ? ring_b : ring_a) + s * kStageBytes);
-                if (st.last) {
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(is_b ? &sm.b_full[s] : &sm.a_full[s]);
-                    if (is_b)
-                        ++gb;
-                    else
-                        ++ga;
-                }
-                return true;
-            };
-            StageLoad L0, L1, L2;
-            load_next(0, L0);
-            load_next(1, L1);
-            bool ok = true;
-            for (int g = 0; g < nst && ok; g += 3) {
-                ok = step(g, L0, L2);
-                if (ok && g + 1 < nst) ok = step(g + 1, L1, L0);
-                if (ok && g + 2 < nst) ok = step(g + 2, L2, L1);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(is_b ? &sm.b_full[slot] : &sm.a_full[slot]);
             }
             if (!ok) {
                 fail(6);
                 break;
             }
+            ga += (uint32_t)na_st;
+            gb += (uint32_t)nb_st;
             if (lane == 0) mbar_arrive(&sm.item_empty[si]);
             padd(pl, kPBuild, t_item);
             if (prof && pl) {
@@ -640,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 const uint64_t t_item = prof ? global_ns() : 0;
                 const int N = S.N;
                 const uint32_t idesc = idesc_i8(N);
-                const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs, a.nbits);
+                const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs);
                 bool ok = true;
                 // one unit: per slab the B stage then the unit's A stages (nk K-steps of 32)
                 // into half uc & 1, once the epilogue read out the unit two before
@@ -726,7 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             if (S.item < 0) break;
             const int n = S.n, nq = S.nq, N = S.N;
             const int64_t beg = S.beg;
-            const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs, a.nbits);
+            const ItemGeo geo = item_geo(S.T, N, S.fs != 0, fs_slabs, rr_slabs);
             const int NP = S.T * kRows, W = S.T * 4;  // score row stride, bitmap words per query
             int16_t* const scp = sc_global;
             const int c_lo = half * (N >> 1), c_hi = c_lo + (N >> 1);
