@@ -93,6 +93,8 @@ struct TcSmem {
     uint64_t item_full[kSlots], item_empty[kSlots];
     uint64_t acc_full[2], acc_free[2];  // per TMEM half: a unit's GEMMs done / read out
     uint64_t drain;  // the MMA issuer's last commit: every MMA it issued has completed
+    // per ring slot: how many of its positions had their builder pass the empty wait
+    uint32_t a_tick[kNA], b_tick[kNB];
     uint32_t tmem;
     volatile int abort;
 };
@@ -137,6 +139,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (uint32_t it = 0; it < kWaitLimit; ++it) {
         if (try_wait()) return true;
         if (*abort || global_ns() - t0 > limit_ns) return false;
+    }
+    return false;
+}
+
+// Bounded wait until a ring slot's ticket reaches `use`: the builder of the slot's previous
+// position has passed its own empty wait.  Stages are built by several warps out of order,
+// and a parity wait cannot tell the phase it waits for from the one two phases older; with
+// the ticket the empty barrier has always completed the phase before the awaited one.
+__device__ __forceinline__ bool ticket_wait(const volatile uint32_t* tk, uint32_t use,
+                                            volatile int* abort, uint64_t limit_ns) {
+    if (*tk == use) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+        if (*tk == use) return true;
+        if (*abort || global_ns() - t0 > limit_ns) return false;
+        __nanosleep(20);
     }
     return false;
 }
@@ -316,10 +334,12 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         for (int s = 0; s < kNA; ++s) {
             mbar_init(&sm.a_full[s], 1);
             mbar_init(&sm.a_empty[s], 1);
+            sm.a_tick[s] = 0;
         }
         for (int s = 0; s < kNB; ++s) {
             mbar_init(&sm.b_full[s], 1);
             mbar_init(&sm.b_empty[s], 1);
+            sm.b_tick[s] = 0;
         }
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(&sm.item_full[s], 1);
@@ -458,12 +478,18 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 const int ns = is_b ? kNB : kNA;
                 const uint32_t slot = pos % ns, use = pos / ns;
                 const uint64_t t_w = prof ? global_ns() : 0;
-                const bool freed = use == 0 ||
-                                   mbar_wait(is_b ? &sm.b_empty[slot] : &sm.a_empty[slot], (use - 1) & 1, &sm.abort, wl);
+                volatile uint32_t* tk = is_b ? &sm.b_tick[slot] : &sm.a_tick[slot];
+                const bool freed = ticket_wait(tk, use, &sm.abort, wl) &&
+                                   (use == 0 || mbar_wait(is_b ? &sm.b_empty[slot] : &sm.a_empty[slot],
+                                                          (use - 1) & 1, &sm.abort, wl));
                 padd(pl, kPBuildWaitSlot, t_w);
                 if (!__all_sync(0xffffffffu, freed)) {
                     ok = false;
                     break;
+                }
+                if (lane == 0) {
+                    __threadfence_block();
+                    *tk = use + 1;  // the slot's next position may wait for this one's use
                 }
                 uint8_t* X = (is_b ? ring_b : ring_a) + slot * kStageBytes;
                 const uint32_t xs = smem_u32(X);
