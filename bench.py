@@ -105,7 +105,7 @@ def scan_tc_ops(art, probes, k, nbits, tc_max_rows=2048):
     for l in np.nonzero((q_per_list > 0) & (sizes > 0) & (sizes <= tc_max_rows))[0]:
         n, q = int(sizes[l]), int(q_per_list[l])
         t = (n + 127) // 128
-        qpi = min(128, (1024 // t) & ~15)
+        qpi = min(128, (256 // t) & ~15)  # tc_queries_per_item: N * T <= 256
         kk = D + (4 * D if n > ncand else 0)
         full, rest = divmod(q, qpi)
         nsum = full * qpi + ((rest + 15) // 16) * 16

@@ -788,8 +788,6 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         t.q_i8p = st.q_i8p;
         t.cand_dbg = a.cand_dbg;
         t.wait_ns = scan_wait_ns_;
-        w_tc_scores_.reserve((size_t)sm_count_ * kTcScoreScratch);
-        t.scores = w_tc_scores_.p;
         const char* prof_env = std::getenv("HANNS_GPU_SCAN_PROFILE");
         const bool prof = prof_env && prof_env[0] == '1';
         if (prof) {

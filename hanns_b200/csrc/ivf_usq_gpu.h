@@ -237,7 +237,6 @@ class IvfUsqGpu {
     bool debug_candidates_ = false;      // scans also write (int_ip, FastScan score) per candidate
     uint64_t scan_wait_ns_ = 2000000000ull;  // tensor-core scan: limit of each wait on a role
     DevBuf<int2> w_cand_dbg_;
-    DevBuf<int16_t> w_tc_scores_;  // tensor-core scan: FastScan scores of items too big for smem
     DevBuf<unsigned long long> w_tc_prof_;  // tensor-core scan: role time counters (profiling)
     DevBuf<int> w_scan_err_;
     int sm_count_ = 0;

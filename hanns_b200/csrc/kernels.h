@@ -67,11 +67,13 @@ struct ScanArgs {
 // Lists of at most kTcMaxRows rows are scanned by the tensor-core kernel (scan_tc.cu),
 // longer ones by the SIMT kernel.  A tensor-core item holds one list's rows in T =
 // ceil(n / 128) tiles of 128 (the MMA's M) and up to 128 queries (the MMA's N, a multiple
-// of 16) with N * T <= 1024 (the kept-row bitmaps of an item fit in shared memory).
+// of 16) with N * T <= kTcItemCols: one GEMM's accumulators fit in half of the TMEM, and
+// the item's FastScan scores and kept-row bitmaps fit in shared memory.
 constexpr int kTcMaxRows = 2048;
+constexpr int kTcItemCols = 256;
 HANNS_HD inline int tc_queries_per_item(long long n) {
     const int t = (int)((n + 127) / 128);
-    const int q = (1024 / (t < 1 ? 1 : t)) & ~15;
+    const int q = (kTcItemCols / (t < 1 ? 1 : t)) & ~15;
     return q > 128 ? 128 : q;
 }
 
@@ -100,7 +102,6 @@ struct TcScanArgs {
     uint32_t* cand_key;
     uint64_t* cand_tie;
     int2* cand_dbg;         // nullable, as in ScanArgs
-    int16_t* scores;        // per CTA kTcScoreScratch FastScan scores (items too big for smem)
     // nullable: per CTA kTcProfSlots nanosecond counters of where each role spends its time
     // (HANNS_GPU_SCAN_PROFILE=1; see scan_tc.cu)
     unsigned long long* prof;
@@ -212,8 +213,6 @@ void launch_pair_offsets(const int32_t* probes, int64_t nq, int nprobe, const in
                          cudaStream_t s);
 size_t scan_smem_bytes(int D);
 size_t scan_tc_smem_bytes();
-// FastScan scores of one item at most (128 queries x kTcMaxRows rows), per CTA of the scan
-constexpr int64_t kTcScoreScratch = 128ll * kTcMaxRows;
 constexpr int kTcProfSlots = 16;
 void launch_scan_tc(const TcScanArgs& a, int grid, cudaStream_t s);
 int scan_grid_size(int D);
