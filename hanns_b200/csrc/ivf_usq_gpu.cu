@@ -838,34 +838,45 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     launch_scan(a, grid, s);
     launches += 1;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[6], s));
-    // 5. each (query, probe) pair's top-k into a compact region of nprobe * k entries
-    w_cmp_key_.reserve((size_t)nb * nprobe * k);
-    w_cmp_tie_.reserve((size_t)nb * nprobe * k);
-    CompactArgs c{};
-    c.nq = nb;
-    c.nprobe = nprobe;
-    c.k = k;
-    c.cand_key = w_cand_key_.p;
-    c.cand_tie = w_cand_tie_.p;
-    c.pair_off = w_pair_off_.p;
-    c.q_stride = q_stride;
-    c.out_key = w_cmp_key_.p;
-    c.out_tie = w_cmp_tie_.p;
-    launch_compact_pairs(c, s);
-    launches += 1;
-    // 6. merge over the compact regions
-    w_mkey_.reserve((size_t)nb * k);
-    w_mtie_.reserve((size_t)nb * k);
+    // 5-6. the top k of each query over its candidate regions: one block per query
+    // (k <= kMergeMaxK), else each (query, probe) pair's top-k into a compact region of
+    // nprobe * k entries and a warp per query over those
+    const bool direct = k <= kMergeMaxK;
+    if (!direct) {
+        w_cmp_key_.reserve((size_t)nb * nprobe * k);
+        w_cmp_tie_.reserve((size_t)nb * nprobe * k);
+        CompactArgs c{};
+        c.nq = nb;
+        c.nprobe = nprobe;
+        c.k = k;
+        c.cand_key = w_cand_key_.p;
+        c.cand_tie = w_cand_tie_.p;
+        c.pair_off = w_pair_off_.p;
+        c.q_stride = q_stride;
+        c.out_key = w_cmp_key_.p;
+        c.out_tie = w_cmp_tie_.p;
+        launch_compact_pairs(c, s);
+        launches += 1;
+        w_mkey_.reserve((size_t)nb * k);
+        w_mtie_.reserve((size_t)nb * k);
+    }
     MergeArgs m{};
     m.nq = nb;
     m.nprobe = nprobe;
     m.k = k;
     m.nlist = nlist_;
-    m.cand_key = w_cmp_key_.p;
-    m.cand_tie = w_cmp_tie_.p;
-    m.pair_off = nullptr;
-    m.q_stride = (int64_t)nprobe * k;
-    m.fixed_total = nprobe * k;
+    if (direct) {
+        m.cand_key = w_cand_key_.p;
+        m.cand_tie = w_cand_tie_.p;
+        m.pair_off = w_pair_off_.p;
+        m.q_stride = q_stride;
+    } else {
+        m.cand_key = w_cmp_key_.p;
+        m.cand_tie = w_cmp_tie_.p;
+        m.pair_off = nullptr;
+        m.q_stride = (int64_t)nprobe * k;
+        m.fixed_total = nprobe * k;
+    }
     m.probes = st.probes;
     m.list_off = list_off_.p;
     m.ids = ids_.p;
@@ -883,7 +894,10 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     }
     m.shard_mode = d_keys ? 1 : 0;
     m.out_keys = d_keys;
-    launch_merge(m, s);
+    if (direct)
+        launch_merge_direct(m, s);
+    else
+        launch_merge(m, s);
     launches += 1;
     used_tc_ = used_tc_ || use_tc;
     if (use_tc) {

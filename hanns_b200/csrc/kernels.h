@@ -219,6 +219,9 @@ int scan_grid_size(int D);
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s);
 void launch_compact_pairs(const CompactArgs& a, cudaStream_t s);
 void launch_merge(const MergeArgs& a, cudaStream_t s);
+// One block per query over the scan's candidate regions (no compaction); k <= kMergeMaxK.
+constexpr int kMergeMaxK = 1024;
+void launch_merge_direct(const MergeArgs& a, cudaStream_t s);
 void launch_merge_shards(const float* dists, const uint64_t* keys, const int64_t* ids, int world,
                          int64_t nq, int k, int64_t* out_ids, float* out_dists, cudaStream_t s);
 

@@ -89,6 +89,9 @@ struct ItemSlot {
     int64_t beg;
     int q[kMaxQ], rank[kMaxQ], bsi[kMaxQ];
     int64_t base[kMaxQ];  // candidate region of each query's (query, probe) pair
+    // the query constants of the rerank distance (QueryParams fields)
+    float q_scale[kMaxQ], centroid_score[kMaxQ], q_norm_sq[kMaxQ];
+    int q_i8_sum[kMaxQ];
 };
 
 struct TcSmem {
@@ -288,9 +291,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     const uint32_t tmem = sm.tmem;
     const uint64_t wl = a.wait_ns;
     unsigned long long* const prof = a.prof ? a.prof + (int64_t)blockIdx.x * kTcProfSlots : nullptr;
-    // a profiling lane adds the time since t to slot k
-    auto padd = [&](bool mine, int k, uint64_t t) {
-        if (prof && mine) prof[k] += global_ns() - t;
+    // a profiling lane adds the time since t to a counter of its role (kept in a register;
+    // each role's profiling lane stores its counters once, after its loop)
+    auto padd = [&](bool mine, uint64_t& acc, uint64_t t) {
+        if (prof && mine) acc += global_ns() - t;
     };
     auto fail = [&](int code) {
         if (!sm.abort) atomicExch(a.err_flag, code);
@@ -307,13 +311,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         uint8_t* const X = (is_b ? ring_b : ring_a) + my * kStageBytes;
         const uint32_t xs = smem_u32(X);
         const bool pl = warp == 0 && lane == 0;  // the builders' profiling lane
+        uint64_t p_loop = 0, p_wslot = 0, p_witem = 0, p_items = 0, p_stages = 0;
         uint32_t gpos = 0;  // ring position of the item's first stage in this warp's ring
         for (int j = 0;; ++j) {
             const int si = j % kSlots;
             const ItemSlot& S = sm.slot[si];
             const uint64_t t_item = prof ? global_ns() : 0;
             const bool got = __all_sync(0xffffffffu, mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort, wl));
-            padd(pl, kPBuildWaitItem, t_item);
+            padd(pl, p_witem, t_item);
             if (!got) {
                 fail(5);
                 break;
@@ -372,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
                 const uint64_t t_w = prof ? global_ns() : 0;
                 const bool freed = use == 0 || mbar_wait(empty, (use - 1) & 1, &sm.abort, wl);
-                padd(pl, kPBuildWaitSlot, t_w);
+                padd(pl, p_wslot, t_w);
                 if (!__all_sync(0xffffffffu, freed)) {
                     ok = false;
                     break;
@@ -450,16 +455,22 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             gpos += (uint32_t)nst;
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.item_empty[si]);
-            padd(pl, kPBuild, t_item);
-            if (prof && pl) {
-                prof[kPItems] += 1;
-                prof[kPStages] += (unsigned long long)((fss + rr_slabs) * (T + 1));
-            }
+            padd(pl, p_loop, t_item);
+            p_items += 1;
+            p_stages += (uint64_t)((fss + rr_slabs) * (T + 1));
+        }
+        if (prof && pl) {
+            prof[kPBuild] = p_loop;
+            prof[kPBuildWaitSlot] = p_wslot;
+            prof[kPBuildWaitItem] = p_witem;
+            prof[kPItems] = p_items;
+            prof[kPStages] = p_stages;
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             uint32_t ga = 0, gb = 0, uc = 0;  // ring positions, GEMMs so far
+            uint64_t p_wfull = 0, p_wfree = 0, p_loop = 0;
             for (int j = 0;; ++j) {
                 const int si = j % kSlots;
                 const ItemSlot& S = sm.slot[si];
@@ -481,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         ok = false;
                         return;
                     }
-                    padd(true, kPMmaWaitFree, t_f);
+                    padd(true, p_wfree, t_f);
                     for (int s = 0; s < slabs && ok; ++s) {
                         const uint32_t bs = gb % kNB;
                         uint64_t t_w = prof ? global_ns() : 0;
@@ -489,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                             ok = false;
                             break;
                         }
-                        padd(true, kPMmaWaitFull, t_w);
+                        padd(true, p_wfull, t_w);
                         const int nk = min(kSlab, k_bytes - s * kSlab) / 32;
                         const uint64_t bd = sw128_desc(smem_u32(ring_b + bs * kStageBytes));
                         for (int t = 0; t < T; ++t) {
@@ -499,10 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                                 ok = false;
                                 break;
                             }
-                            padd(true, kPMmaWaitFull, t_w);
-                            // the stages' generic-proxy writes (stores, cp.async) before the
-                            // tensor core's reads
-                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                            padd(true, p_wfull, t_w);
                             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                             const uint64_t ad = sw128_desc(smem_u32(ring_a + as * kStageBytes));
                             for (int k4 = 0; k4 < nk; ++k4)
@@ -525,10 +533,15 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     break;
                 }
                 mbar_arrive(&sm.item_empty[si]);
-                padd(true, kPMma, t_item);
+                padd(true, p_loop, t_item);
             }
             // before the TMEM is freed, every MMA issued (also after an abort) completes;
             // this wait ignores the abort flag and gives up after 0.5 s
+            if (prof) {
+                prof[kPMmaWaitFull] = p_wfull;
+                prof[kPMmaWaitFree] = p_wfree;
+                prof[kPMma] = p_loop;
+            }
             umma_commit(&sm.drain);
             int no_abort = 0;
             if (!mbar_wait(&sm.drain, 0, &no_abort, 500000000ull)) fail(10);
@@ -593,6 +606,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     S.q[i] = pr.x;
                     S.rank[i] = pr.y;
                     S.base[i] = (int64_t)pr.x * a.q_stride + a.pair_off[(int64_t)pr.x * (a.nprobe + 1) + pr.y];
+                    const QueryParams qp = a.qp[pr.x];
+                    S.q_scale[i] = qp.q_scale;
+                    S.centroid_score[i] = qp.centroid_score;
+                    S.q_norm_sq[i] = qp.q_norm_sq;
+                    S.q_i8_sum[i] = qp.q_i8_sum;
                     int b = -1;
                     if (a.fused && a.bitsets) {
                         b = a.query_bitset ? a.query_bitset[pr.x] : 0;
@@ -614,13 +632,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         uint32_t uc = 0;  // GEMMs so far (the MMA issuer's count)
         const bool pl = e == 0 && lane == 0;  // the epilogue's profiling lane
+        uint64_t p_wacc = 0, p_copy = 0, p_sel = 0, p_rr = 0, p_witem = 0, p_loop = 0;
         const int lut_bias = 128 * a.G;       // offset-binary LUT: the u8 sum's excess
         for (int j = 0;; ++j) {
             const int si = j % kSlots;
             const ItemSlot& S = sm.slot[si];
             const uint64_t t_item = prof ? global_ns() : 0;
             bool bad = !__all_sync(0xffffffffu, mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort, wl));
-            padd(pl, kPEpiWaitItem, t_item);
+            padd(pl, p_witem, t_item);
             const uint64_t t_body = prof ? global_ns() : 0;
             if (epi_sync_or(bad)) {
                 fail(8);
@@ -637,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 dcol = tmem + h * kHalfCols + lane_base;
                 const uint64_t t_w = prof ? global_ns() : 0;
                 const bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.acc_full[h], use & 1, &sm.abort, wl));
-                padd(pl, kPEpiWaitAcc, t_w);
+                padd(pl, p_wacc, t_w);
                 if (ok) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 return ok;
             };
@@ -671,12 +690,28 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 fail(8);
                 break;
             }
-            padd(pl, kPEpiCopy, t_copy);
+            padd(pl, p_copy, t_copy);
             const uint64_t t_sel = prof ? global_ns() : 0;
             // the kept set of each query (warp per query) and its candidates' tie keys
             for (int i = e; i < nq; i += kEpiWarps) {
                 const int bsi = S.bsi[i];
                 const uint64_t* bw = bsi >= 0 ? a.bitsets + (int64_t)bsi * a.bitset_words : nullptr;
+                if (!S.fs && !bw) {
+                    // |list| <= n_cand and no filter: every row is kept at its own position
+                    // (the bitmap in closed form)
+                    for (int w = lane; w < W; w += 32) {
+                        const int lo = 32 * w;
+                        sm.bitmap[i * W + w] = lo >= n ? 0u : (n - lo >= 32 ? 0xFFFFFFFFu : (1u << (n - lo)) - 1u);
+                        sm.prefix[i * W + w] = min(lo, n);
+                    }
+                    const int64_t rb = S.base[i];
+                    const uint64_t rank_bits = (uint64_t)S.rank[i] << 48;
+                    for (int v = lane; v < n; v += 32) {
+                        a.cand_tie[rb + v] = rank_bits | (uint32_t)v;
+                        if (a.cand_dbg) a.cand_dbg[rb + v].y = INT32_MIN;
+                    }
+                    continue;
+                }
                 // the live rows, as this lane's bits: row v = lane + 32 j is bit j of lm0 (j < 32)
                 // or of lm1 (j >= 32); n <= kTcMaxRows = 2048 rows
                 uint32_t lm0 = 0u, lm1 = 0u;
@@ -785,7 +820,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
             }
             bad = epi_sync_or(false);
-            padd(pl, kPEpiSelect, t_sel);
+            padd(pl, p_sel, t_sel);
             const uint64_t t_rr = prof ? global_ns() : 0;
             // rerank: thread per row, the distances of the kept (query, row) pairs
             uint32_t dcol;
@@ -800,19 +835,24 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     for (int c = c_lo; c < c_hi && c < nq; c += 8) {
                         uint32_t ip[8];
                         tmem_ld8(dcol + (uint32_t)(t * N + c), ip);
-                        if (!row_ok) continue;
+                        // the 8 queries are independent: every load is unconditional (query
+                        // index clamped), only the distance and its store are predicated
 #pragma unroll
                         for (int jj = 0; jj < 8; ++jj) {
-                            const int i = c + jj;
-                            if (i >= nq) break;
+                            const int i = min(c + jj, nq - 1);
                             const uint32_t word = sm.bitmap[i * W + wi];
-                            if (!((word >> lane) & 1u)) continue;
                             const int pos = sm.prefix[i * W + wi] + __popc(word & below);
-                            if (pos >= a.n_cand) continue;
-                            const float dist = rerank_distance((int)ip[jj], m, a.qp[S.q[i]], a.nbits, l2);
+                            QueryParams qp;
+                            qp.q_scale = S.q_scale[i];
+                            qp.centroid_score = S.centroid_score[i];
+                            qp.q_norm_sq = S.q_norm_sq[i];
+                            qp.q_i8_sum = S.q_i8_sum[i];
                             const int64_t dst = S.base[i] + pos;
-                            a.cand_key[dst] = total_order_key(dist);  // (its tie: the selection)
-                            if (a.cand_dbg) a.cand_dbg[dst].x = (int)ip[jj];
+                            if (row_ok && c + jj < nq && ((word >> lane) & 1u) && pos < a.n_cand) {
+                                const float dist = rerank_distance((int)ip[jj], m, qp, a.nbits, l2);
+                                a.cand_key[dst] = total_order_key(dist);  // (its tie: the selection)
+                                if (a.cand_dbg) a.cand_dbg[dst].x = (int)ip[jj];
+                            }
                         }
                     }
                 }
@@ -823,9 +863,17 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 fail(9);
                 break;
             }
-            padd(pl, kPEpiRerank, t_rr);
-            padd(pl, kPEpi, t_body);
+            padd(pl, p_rr, t_rr);
+            padd(pl, p_loop, t_body);
             if (lane == 0) mbar_arrive(&sm.item_empty[si]);
+        }
+        if (prof && pl) {
+            prof[kPEpiWaitAcc] = p_wacc;
+            prof[kPEpiCopy] = p_copy;
+            prof[kPEpiSelect] = p_sel;
+            prof[kPEpiRerank] = p_rr;
+            prof[kPEpiWaitItem] = p_witem;
+            prof[kPEpi] = p_loop;
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

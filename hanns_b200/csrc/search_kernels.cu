@@ -2088,6 +2088,184 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
     }
 }
 
+// ============================================================================
+// Final merge, one 256-thread block per query (k <= kMergeMaxK): the top k of all kept
+// candidates of the query's probes by (distance key, tie = probe rank << 48 | FastScan key
+// << 32 | position), sorted -- the same result as compact_pairs_kernel + merge_kernel.
+// The query's keys are read once (into shared memory when they fit); a block radix
+// select finds the k-th smallest key tau; ties are read only for the entries taken and
+// for those at tau.  Unused entries carry key 0xFFFFFFFF and tie ~0 (the scans' fill):
+// they sort after every valid entry, and at tau = 0xFFFFFFFF only valid ties are taken.
+// ============================================================================
+constexpr int kMergeKeyCap = 8192;  // keys of one query held in shared memory
+constexpr int kMergeEqCap = 256;    // ties at tau ranked at once
+
+struct MergeSmem {
+    uint32_t hist[kSelBins];
+    uint32_t list[kSelList];
+    int bcast[8];
+    int cnt[4];
+    unsigned long long best;
+    uint64_t eq[kMergeEqCap];
+};
+
+__global__ void __launch_bounds__(kSelThreads) merge_direct_kernel(MergeArgs a) {
+    __shared__ MergeSmem ms;
+    extern __shared__ __align__(16) uint8_t mdyn[];  // sel ties [k], sel keys [k], keys [cap]
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int64_t q = blockIdx.x;
+    const int k = a.k;
+    uint64_t* st = reinterpret_cast<uint64_t*>(mdyn);
+    uint32_t* sk = reinterpret_cast<uint32_t*>(st + k);
+    uint32_t* ks = sk + k;
+    const int total = a.pair_off[q * (a.nprobe + 1) + a.nprobe];
+    const uint32_t* gk = a.cand_key + q * a.q_stride;
+    const uint64_t* gt = a.cand_tie + q * a.q_stride;
+    const bool in_smem = total <= kMergeKeyCap;
+    if (tid < 4) ms.cnt[tid] = 0;
+    int n_lt = 0;  // entries below 0xFFFFFFFF (all valid)
+    for (int e = tid; e < total; e += kSelThreads) {
+        const uint32_t kk = gk[e];
+        if (in_smem) ks[e] = kk;
+        n_lt += kk != 0xFFFFFFFFu ? 1 : 0;
+    }
+    const uint32_t* keys = in_smem ? ks : gk;
+    n_lt = warp_sum(n_lt);
+    __syncthreads();
+    if (lane == 0) atomicAdd(&ms.cnt[0], n_lt);
+    __syncthreads();
+    n_lt = ms.cnt[0];
+    uint32_t tau = 0xFFFFFFFFu;
+    if (n_lt >= k)
+        tau = block_select_kth(
+            [&](auto f) {
+                for (int e = threadIdx.x; e < total; e += kSelThreads) {
+                    const uint32_t kk = keys[e];
+                    if (kk != 0xFFFFFFFFu) f(kk);
+                }
+            },
+            k, ms.hist, ms.list, ms.bcast);
+    // the entries below tau (any order) and the valid ties at tau
+    for (int e = tid; e < total; e += kSelThreads) {
+        const uint32_t kk = keys[e];
+        if (kk < tau) {
+            const int p = atomicAdd(&ms.cnt[1], 1);
+            sk[p] = kk;
+            st[p] = gt[e];
+        } else if (kk == tau) {
+            const uint64_t t = gt[e];
+            if (t != ~0ull) {
+                const int p = atomicAdd(&ms.cnt[2], 1);
+                if (p < kMergeEqCap) ms.eq[p] = t;
+            }
+        }
+    }
+    __syncthreads();
+    const int less = ms.cnt[1], n_eq = ms.cnt[2];
+    const int need = min(k - less, n_eq);
+    const int take = less + need;
+    if (n_eq <= kMergeEqCap) {
+        // the `need` smallest ties at tau (a query's ties are distinct): rank among them
+        for (int j = tid; j < n_eq; j += kSelThreads) {
+            const uint64_t t = ms.eq[j];
+            int r = 0;
+            for (int i = 0; i < n_eq; ++i) r += ms.eq[i] < t ? 1 : 0;
+            if (r < need) {
+                sk[less + r] = tau;
+                st[less + r] = t;
+            }
+        }
+    } else {
+        // many entries at tau: the smallest remaining tie, need times
+        uint64_t floor_t = 0;
+        for (int r = 0; r < need; ++r) {
+            if (tid == 0) ms.best = ~0ull;
+            __syncthreads();
+            uint64_t best = ~0ull;
+            for (int e = tid; e < total; e += kSelThreads) {
+                if (keys[e] != tau) continue;
+                const uint64_t t = gt[e];
+                if (t != ~0ull && (r == 0 || t > floor_t) && t < best) best = t;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+                best = ob < best ? ob : best;
+            }
+            if (lane == 0) atomicMin(&ms.best, (unsigned long long)best);
+            __syncthreads();
+            floor_t = ms.best;
+            if (tid == 0) {
+                sk[less + r] = tau;
+                st[less + r] = floor_t;
+            }
+        }
+    }
+    __syncthreads();
+    // sorted row: each taken entry's rank by (key, tie)
+    for (int i = tid; i < k; i += kSelThreads) {
+        if (i >= take) {
+            a.out_ids[q * k + i] = -1;
+            a.out_dists[q * k + i] = __int_as_float(0x7f800000);
+            if (a.shard_mode) a.out_keys[q * k + i] = ~0ull;
+            continue;
+        }
+        const uint32_t ki = sk[i];
+        const uint64_t ti = st[i];
+        int rank = 0;
+        for (int j = 0; j < take; ++j) {
+            const uint32_t kj = sk[j];
+            rank += (kj < ki || (kj == ki && st[j] < ti)) ? 1 : 0;
+        }
+        const int r = (int)(ti >> 48);
+        const uint32_t idx = (uint32_t)(ti & 0xFFFFFFFFull);
+        int64_t id = -1;
+        if (r < a.nprobe) {
+            const int l = a.probes[q * a.nprobe + r];
+            if (l >= 0 && l < a.nlist && idx < (uint32_t)(a.list_off[l + 1] - a.list_off[l]))
+                id = a.ids[a.list_off[l] + idx];
+        }
+        a.out_ids[q * k + rank] = id;
+        a.out_dists[q * k + rank] = key_to_float(ki);
+        if (a.shard_mode) a.out_keys[q * k + rank] = ti;
+    }
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    if (a.post_bitsets) {  // reference post-filter: drop filtered ids, keep order
+        const uint64_t* bw = nullptr;
+        const int b = a.query_bitset ? a.query_bitset[q] : 0;
+        if (b >= 0 && b < a.n_bitsets) bw = a.post_bitsets + (int64_t)b * a.bitset_words;
+        int n_out = 0;
+        for (int base = 0; base < k; base += 32) {
+            const int i = base + lane;
+            int64_t id = 0;
+            float dd = 0;
+            bool keep = false;
+            if (i < k) {
+                id = a.out_ids[q * k + i];
+                dd = a.out_dists[q * k + i];
+                keep = !bw || !bit_filtered(bw, a.bitset_len, id);
+            }
+            const unsigned bk = __ballot_sync(0xffffffffu, keep);
+            __syncwarp();
+            if (keep) {
+                const int pos = n_out + __popc(bk & lanemask_lt());
+                a.out_ids[q * k + pos] = id;
+                a.out_dists[q * k + pos] = dd;
+            }
+            n_out += __popc(bk);
+            __syncwarp();
+        }
+        for (int i = n_out + lane; i < k; i += 32) {
+            a.out_ids[q * k + i] = -1;
+            a.out_dists[q * k + i] = __int_as_float(0x7f800000);
+        }
+        if (lane == 0 && a.out_counts) a.out_counts[q] = n_out;
+    } else if (lane == 0 && a.out_counts) {
+        a.out_counts[q] = k;
+    }
+}
+
 }  // namespace hanns
 
 namespace hanns {
@@ -2301,6 +2479,13 @@ void launch_compact_pairs(const CompactArgs& a, cudaStream_t s) {
 void launch_merge(const MergeArgs& a, cudaStream_t s) {
     if (a.nq <= 0) return;
     merge_kernel<<<(unsigned)((a.nq + 3) / 4), 128, 0, s>>>(a);
+}
+
+void launch_merge_direct(const MergeArgs& a, cudaStream_t s) {
+    if (a.nq <= 0) return;
+    const size_t smem = (size_t)a.k * 12 + (size_t)kMergeKeyCap * 4;
+    HANNS_CUDA_OK(cudaFuncSetAttribute(merge_direct_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    merge_direct_kernel<<<(unsigned)a.nq, kSelThreads, smem, s>>>(a);
 }
 
 void launch_merge_shards(const float* dists, const uint64_t* keys, const int64_t* ids, int world,

@@ -86,26 +86,29 @@ __device__ uint32_t warp_radix_kth(int n, int kth, KeyAt key_at, uint32_t* hist,
             }
         }
         __syncwarp();
-        int s = 0;
+        // this lane's 8 bins, in registers: the bin search below needs no further loads
+        int hv[8], s = 0;
 #pragma unroll
-        for (int b = 0; b < 8; ++b) s += (int)hist[lane * 8 + b];
+        for (int b = 0; b < 8; ++b) {
+            hv[b] = (int)hist[lane * 8 + b];
+            s += hv[b];
+        }
         const int incl = warp_inclusive_scan(s);
         const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
         const int src = __ffs(hit) - 1;  // hit != 0 because remaining <= total
-        int bin = 0, before = 0;
-        if (lane == src) {
-            int c = incl - s;
-            for (int b = 0; b < 8; ++b) {
-                const int h = (int)hist[lane * 8 + b];
-                if (c + h >= remaining) {
-                    bin = lane * 8 + b;
-                    break;
-                }
-                c += h;
+        // every lane finds the first of its bins that reaches `remaining` (the answer is src's)
+        int c = incl - s, bin = 7, before = 0;
+        bool found = false;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            if (!found && c + hv[b] >= remaining) {
+                found = true;
+                bin = b;
+                before = c;
             }
-            before = c;
+            c += hv[b];
         }
-        bin = __shfl_sync(0xffffffffu, bin, src);
+        bin = __shfl_sync(0xffffffffu, lane * 8 + bin, src);
         before = __shfl_sync(0xffffffffu, before, src);
         less += before;
         remaining -= before;
