@@ -21,6 +21,7 @@ namespace {
 // 180 GB HBM); per-query kernels index queries in grid.y in tiles of >= 8, so 262,144
 // queries per batch stay inside the 65,535 grid.y limit.
 constexpr int64_t kCandBudget = 16ll << 30;
+constexpr int64_t kFsBudget = 8ll << 30;  // FastScan scratch: 6 bytes per entry
 constexpr int64_t kMaxBatch = 262144;
 }  // namespace
 
@@ -79,6 +80,42 @@ int64_t IvfUsqGpu::cand_stride(int nprobe, int k) const {
     const int64_t st = std::max<int64_t>(1, std::min<int64_t>((int64_t)nprobe * per, std::max<int64_t>(ntotal_, 1)));
     if (st > (int64_t)INT32_MAX) throw std::invalid_argument("nprobe x candidates per probe too large");
     return st;
+}
+
+int IvfUsqGpu::scan_tc_rows(int n_cand) const {
+    const char* mode = std::getenv("HANNS_GPU_SCAN");
+    if (mode && std::strcmp(mode, "simt") == 0) return 0;
+    if (mode && std::strcmp(mode, "hybrid") == 0) return std::min(kTcMaxRows, n_cand);
+    return kTcMaxRows;
+}
+
+int64_t IvfUsqGpu::fs_stride(int nprobe, int n_cand, int tc_rows) {
+    if (tc_rows <= n_cand) return 0;
+    if (fs_stride_key_[0] == nprobe && fs_stride_key_[1] == n_cand && fs_stride_key_[2] == tc_rows)
+        return fs_stride_val_;
+    std::vector<int64_t> sz;
+    for (int l = 0; l < nlist_; ++l) {
+        const int64_t n = h_list_off_[l + 1] - h_list_off_[l];
+        if (n > n_cand && n <= tc_rows) sz.push_back(n);
+    }
+    const size_t m = std::min<size_t>(sz.size(), (size_t)nprobe);
+    std::partial_sort(sz.begin(), sz.begin() + m, sz.end(), std::greater<int64_t>());
+    int64_t sum = 0;
+    for (size_t i = 0; i < m; ++i) sum += sz[i];
+    fs_stride_key_[0] = nprobe;
+    fs_stride_key_[1] = n_cand;
+    fs_stride_key_[2] = tc_rows;
+    fs_stride_val_ = sum;
+    return sum;
+}
+
+int64_t IvfUsqGpu::batch_limit(int nprobe, int k) {
+    // candidate regions: 12 bytes per entry; FastScan scratch: 6 bytes per entry
+    int64_t nb = std::max<int64_t>(1, kCandBudget / (cand_stride(nprobe, k) * 12));
+    const int n_cand = (int)n_candidates(nbits_, k);
+    const int64_t fs = fs_stride(nprobe, n_cand, scan_tc_rows(n_cand));
+    if (fs > 0) nb = std::min<int64_t>(nb, std::max<int64_t>(1, kFsBudget / (fs * 6)));
+    return std::min<int64_t>(nb, kMaxBatch);
 }
 
 IvfUsqGpu::IvfUsqGpu(int dim, int nlist, int nbits, int metric, uint64_t rotation_seed, int nprobe,
@@ -152,6 +189,7 @@ int64_t IvfUsqGpu::size_bytes() const {
 
 void IvfUsqGpu::set_list_layout(const std::vector<int64_t>& h_off) {
     h_list_off_ = h_off;
+    fs_stride_key_[0] = -1;
     max_list_ = 1;
     std::vector<int64_t> blk(nlist_ + 1, 0);
     for (int l = 0; l < nlist_; ++l) {
@@ -705,17 +743,21 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     // lists of at most kTcMaxRows rows take the tensor-core scan; HANNS_GPU_SCAN=simt: none,
     // =hybrid: only lists without FastScan (|list| <= n_cand)
     const int n_cand = (int)n_candidates(nbits_, k);
-    const char* scan_mode = std::getenv("HANNS_GPU_SCAN");
-    const bool use_tc = !(scan_mode && std::strcmp(scan_mode, "simt") == 0);
-    const bool hybrid = scan_mode && std::strcmp(scan_mode, "hybrid") == 0;
-    const int tc_rows = !use_tc ? 0 : hybrid ? std::min(kTcMaxRows, n_cand) : kTcMaxRows;
+    const int tc_rows = scan_tc_rows(n_cand);
+    const bool use_tc = tc_rows > 0;
+    const int64_t fss = fs_stride(nprobe, n_cand, tc_rows);
     launch_group_pairs(st.probes, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr, list_off_.p,
                        tc_rows, kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p, w_item_off_.p,
                        w_counters_.p, w_lq_.p, w_items_.p, s);
     const int64_t q_stride = cand_stride(nprobe, k);
     w_pair_off_.reserve((size_t)nb * (nprobe + 1));
+    if (fss > 0) {
+        w_fs_off_.reserve((size_t)nb * nprobe);
+        w_fs_sc_.reserve((size_t)nb * fss);
+        w_fs_ip_.reserve((size_t)nb * fss);
+    }
     launch_pair_offsets(st.probes, nb, nprobe, list_off_.p, nlist_, sharded_ ? owned_.p : nullptr,
-                        n_cand, w_pair_off_.p, s);
+                        n_cand, w_pair_off_.p, tc_rows, fss > 0 ? w_fs_off_.p : nullptr, s);
     launches += 5;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[5], s));
     // 4. list scan: kept candidates of every (query, probe) pair with their distance keys
@@ -787,6 +829,10 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         t.lut = st.lut;
         t.q_i8p = st.q_i8p;
         t.cand_dbg = a.cand_dbg;
+        t.fs_off = w_fs_off_.p;
+        t.fs_stride = fss;
+        t.fs_sc = w_fs_sc_.p;
+        t.fs_ip = w_fs_ip_.p;
         t.wait_ns = scan_wait_ns_;
         const char* prof_env = std::getenv("HANNS_GPU_SCAN_PROFILE");
         const bool prof = prof_env && prof_env[0] == '1';
@@ -837,6 +883,37 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     }
     launch_scan(a, grid, s);
     launches += 1;
+    if (fss > 0) {
+        // kept sets and distances of the tensor-core FastScan pairs
+        FsSelectArgs f{};
+        f.nq = nb;
+        f.nprobe = nprobe;
+        f.n_cand = n_cand;
+        f.nbits = nbits_;
+        f.metric_l2 = a.metric_l2;
+        f.fused = a.fused;
+        f.probes = st.probes;
+        f.list_off = list_off_.p;
+        f.ids = ids_.p;
+        f.meta = meta_.p;
+        f.qp = st.qp;
+        f.fs_off = w_fs_off_.p;
+        f.fs_stride = fss;
+        f.fs_sc = w_fs_sc_.p;
+        f.fs_ip = w_fs_ip_.p;
+        f.pair_off = w_pair_off_.p;
+        f.q_stride = q_stride;
+        f.bitsets = a.bitsets;
+        f.bitset_len = a.bitset_len;
+        f.bitset_words = a.bitset_words;
+        f.n_bitsets = a.n_bitsets;
+        f.query_bitset = a.query_bitset;
+        f.cand_key = w_cand_key_.p;
+        f.cand_tie = w_cand_tie_.p;
+        f.cand_dbg = a.cand_dbg;
+        launch_fs_select(f, s);
+        launches += 1;
+    }
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[6], s));
     // 5-6. the top k of each query over its candidate regions: one block per query
     // (k <= kMergeMaxK), else each (query, probe) pair's top-k into a compact region of
@@ -930,9 +1007,7 @@ void IvfUsqGpu::run_search(const float* d_queries, const float* h_queries, int64
     cudaStream_t s = stream ? stream : stream_;
     const int k = std::max(opt.k, 1);
     const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
-    // batch size bounded by the candidate regions (12 bytes per entry)
-    int64_t nb_max = std::max<int64_t>(1, kCandBudget / (cand_stride(nprobe, k) * 12));
-    nb_max = std::min<int64_t>(nb_max, kMaxBatch);
+    const int64_t nb_max = batch_limit(nprobe, k);
     last_launches_ = 0;
     begin_call();
     for (int64_t b = 0; b < nq; b += nb_max) {
@@ -1097,8 +1172,7 @@ void IvfUsqGpu::search_prepared_device(int64_t nq, const SearchOptions& opt, Que
     const int k = std::max(opt.k, 1);
     const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
     const int G = D_ / 4;
-    int64_t nb_max = std::max<int64_t>(1, kCandBudget / (cand_stride(nprobe, k) * 12));
-    nb_max = std::min<int64_t>(nb_max, kMaxBatch);
+    const int64_t nb_max = batch_limit(nprobe, k);
     last_launches_ = 0;
     begin_call();
     for (int64_t b = 0; b < nq; b += nb_max) {
@@ -1170,7 +1244,8 @@ void IvfUsqGpu::debug_candidates(const float* h_queries, int64_t nq, const Searc
     const int k = std::max(opt.k, 1);
     const int nprobe = std::max(1, std::min(opt.nprobe, nlist_));
     const int64_t stride = cand_stride(nprobe, k);
-    if (nq > std::min<int64_t>(kMaxBatch, std::max<int64_t>(1, kCandBudget / (stride * 12))))
+    (void)stride;
+    if (nq > batch_limit(nprobe, k))
         throw std::invalid_argument("debug_candidates: more queries than one internal batch");
     std::vector<int64_t> ids((size_t)nq * k), cnt(nq);
     std::vector<float> d((size_t)nq * k);

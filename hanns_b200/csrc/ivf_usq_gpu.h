@@ -179,6 +179,16 @@ class IvfUsqGpu {
                     uint64_t* d_keys, cudaStream_t stream);
     void set_list_layout(const std::vector<int64_t>& h_off);
     int64_t cand_stride(int nprobe, int k) const;
+    // lists of at most this many rows take the tensor-core scan (HANNS_GPU_SCAN: default all
+    // lists up to kTcMaxRows, =hybrid only those without FastScan, =simt none)
+    int scan_tc_rows(int n_cand) const;
+    // entries of one query's region of the FastScan scratch: the nprobe longest lists that
+    // the tensor-core scan runs FastScan on (n_cand < |list| <= tc_rows); cached
+    int64_t fs_stride(int nprobe, int n_cand, int tc_rows);
+    // queries per internal batch: candidate regions and FastScan scratch within budget
+    int64_t batch_limit(int nprobe, int k);
+    int fs_stride_key_[3] = {-1, -1, -1};
+    int64_t fs_stride_val_ = 0;
     void update_centroid_norms();
     // returns the number of kernels launched
     int64_t coarse_probes(const float* d_q, int64_t nb, int nprobe, int32_t* d_probes,
@@ -237,6 +247,9 @@ class IvfUsqGpu {
     bool debug_candidates_ = false;      // scans also write (int_ip, FastScan score) per candidate
     uint64_t scan_wait_ns_ = 2000000000ull;  // tensor-core scan: limit of each wait on a role
     DevBuf<int2> w_cand_dbg_;
+    DevBuf<int> w_fs_off_;       // per (query, probe): place in the FastScan scratch, -1: none
+    DevBuf<int16_t> w_fs_sc_;    // FastScan scratch: scores of every row of FastScan pairs
+    DevBuf<int32_t> w_fs_ip_;    //                   and their int_ip
     DevBuf<unsigned long long> w_tc_prof_;  // tensor-core scan: role time counters (profiling)
     DevBuf<int> w_scan_err_;
     int sm_count_ = 0;

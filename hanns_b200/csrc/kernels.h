@@ -102,12 +102,44 @@ struct TcScanArgs {
     uint32_t* cand_key;
     uint64_t* cand_tie;
     int2* cand_dbg;         // nullable, as in ScanArgs
+    // FastScan pairs (|list| > n_cand): every row's score and int_ip to the FastScan scratch
+    // at query * fs_stride + fs_off[query * nprobe + rank] (fs_select_kernel takes it from there)
+    const int* fs_off;
+    int64_t fs_stride;
+    int16_t* fs_sc;
+    int32_t* fs_ip;
     // nullable: per CTA kTcProfSlots nanosecond counters of where each role spends its time
     // (HANNS_GPU_SCAN_PROFILE=1; see scan_tc.cu)
     unsigned long long* prof;
     int* err_flag;          // set to a nonzero code when a bounded wait expired
     uint64_t wait_ns;       // limit of every wait on another role (2 s by default)
 };
+
+// Kept sets of the tensor-core FastScan pairs from the FastScan scratch (warp per pair): the
+// reference heap's kept set of the 16-bit scores, each kept row's distance (from its int_ip)
+// and tie to the pair's candidate region.
+struct FsSelectArgs {
+    int64_t nq;
+    int nprobe, n_cand, nbits, metric_l2, fused;
+    const int32_t* probes;
+    const int64_t* list_off;
+    const int64_t* ids;
+    const float4* meta;
+    const QueryParams* qp;
+    const int* fs_off;
+    int64_t fs_stride;
+    const int16_t* fs_sc;
+    const int32_t* fs_ip;
+    const int* pair_off;
+    int64_t q_stride;
+    const uint64_t* bitsets;
+    int64_t bitset_len, bitset_words, n_bitsets;
+    const int32_t* query_bitset;
+    uint32_t* cand_key;
+    uint64_t* cand_tie;
+    int2* cand_dbg;  // nullable
+};
+void launch_fs_select(const FsSelectArgs& a, cudaStream_t s);
 
 // USQ rerank of caller-chosen stored rows: out[q * m + j] = distance of row rows[q*m+j]
 // (+inf for rows outside [0, ntotal)).
@@ -208,9 +240,13 @@ void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist
                         int4* items, cudaStream_t s);
 // pair_off[q][r] = sum over earlier probes of min(|list|, n_cand) (0 for lists this
 // index does not own); pair_off[q][nprobe] = the query's candidate total
+// pair_off: per query the candidate regions of its probes (min(|list|, n_cand) entries each).
+// fs_off (nullable): per (query, probe) the offset of a tensor-core FastScan pair (n_cand <
+// |list| <= tc_rows) in the query's region of the FastScan scratch (|list| entries each), -1
+// for other pairs.
 void launch_pair_offsets(const int32_t* probes, int64_t nq, int nprobe, const int64_t* list_off,
-                         int nlist, const uint8_t* owned, int n_cand, int* pair_off,
-                         cudaStream_t s);
+                         int nlist, const uint8_t* owned, int n_cand, int* pair_off, int tc_rows,
+                         int* fs_off, cudaStream_t s);
 size_t scan_smem_bytes(int D);
 size_t scan_tc_smem_bytes();
 constexpr int kTcProfSlots = 16;

@@ -20,11 +20,11 @@
 //
 // An item's FastScan GEMM (T x N accumulator columns <= 256) fills one half of the 512
 // TMEM columns and its rerank GEMM the other half; consecutive GEMMs alternate halves, so
-// one GEMM overlaps the epilogue of the one before.  The kept set of each (query, list)
-// pair is the reference's FastScan heap result (fastscan.rs:86-146), found with the same
-// closed form as the SIMT scan (search_kernels.cu) on the 16-bit scores, which the
-// epilogue keeps in shared memory; the selection writes each kept row's tie key
-// (rank << 48 | FastScan key << 32 | position) and the rerank epilogue its distance key
+// one GEMM overlaps the epilogue of the one before.  A FastScan item's epilogue streams
+// every (row, query) score and int_ip to the FastScan scratch, from which fs_select_kernel
+// (search_kernels.cu, a warp per pair at full occupancy) takes the reference's heap kept set
+// (fastscan.rs:86-146) and the kept rows' distances.  A rerank-only item keeps every live
+// row: its epilogue writes each kept row's distance key and tie key (rank << 48 | position)
 // to the query's candidate region.
 //
 // Operands stream through two rings of 16 KiB stages (128 rows x 128 K bytes, 128-byte
@@ -41,8 +41,9 @@
 //   warps 6-7   B builders: the queries' LUT or q_i8p slab rows, cp.async
 //               Copies complete on the slot's full barrier (cp.async.mbarrier.arrive): a
 //               builder never waits for its loads.
-//   warps 8-15  epilogue: FastScan scores TMEM -> shared memory, the kept set of each
-//               query (warp per query), the distances of the kept rows (thread per row)
+//   warps 8-15  epilogue (thread per row): FastScan items' scores and int_ip TMEM -> the
+//               FastScan scratch; rerank-only items' kept rows (bitmaps) and their
+//               distances and ties
 //   warp 16     TMEM allocation and the single-thread MMA issuer
 //   warp 17     item scheduler: takes items, fills the item slots, prefetches the next
 //               item's list into L2
@@ -53,7 +54,6 @@
 
 #include "common.cuh"
 #include "kernels.h"
-#include "warp_select.cuh"
 
 namespace hanns {
 namespace {
@@ -89,16 +89,15 @@ struct ItemSlot {
     int64_t beg;
     int q[kMaxQ], rank[kMaxQ], bsi[kMaxQ];
     int64_t base[kMaxQ];  // candidate region of each query's (query, probe) pair
+    int64_t fsb[kMaxQ];   // FastScan items: the pair's place in the FastScan scratch
     // the query constants of the rerank distance (QueryParams fields)
     float q_scale[kMaxQ], centroid_score[kMaxQ], q_norm_sq[kMaxQ];
     int q_i8_sum[kMaxQ];
 };
 
 struct TcSmem {
-    int16_t sc[kTcItemCols * kRows];  // FastScan scores of the item: [query][row], stride T * 128
-    uint32_t bitmap[kWordCap];        // kept rows [query][word], word stride T * 4
-    int prefix[kWordCap];             // kept rows before each bitmap word
-    uint32_t hist[kEpiWarps][256];
+    uint32_t bitmap[kWordCap];  // kept rows of rerank-only items [query][word], word stride T * 4
+    int prefix[kWordCap];       // kept rows before each bitmap word
     ItemSlot slot[kSlots];
     uint64_t a_full[kNA], a_empty[kNA], b_full[kNB], b_empty[kNB];
     uint64_t item_full[kSlots], item_empty[kSlots];
@@ -606,6 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     S.q[i] = pr.x;
                     S.rank[i] = pr.y;
                     S.base[i] = (int64_t)pr.x * a.q_stride + a.pair_off[(int64_t)pr.x * (a.nprobe + 1) + pr.y];
+                    S.fsb[i] = n > a.n_cand ? (int64_t)pr.x * a.fs_stride + a.fs_off[(int64_t)pr.x * a.nprobe + pr.y] : 0;
                     const QueryParams qp = a.qp[pr.x];
                     S.q_scale[i] = qp.q_scale;
                     S.centroid_score[i] = qp.centroid_score;
@@ -648,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             if (S.item < 0) break;
             const int n = S.n, nq = S.nq, N = S.N, T = S.T;
             const int64_t beg = S.beg;
-            const int NP = T * kRows, W = T * 4;  // score row stride, bitmap words per query
+            const int NP = T * kRows, W = T * 4;  // rows incl. padding, bitmap words per query
             const int c_lo = half * (N >> 1), c_hi = c_lo + (N >> 1);
             // waits for the next GEMM's accumulators; false on a failed wait
             auto gemm_begin = [&](uint32_t& dcol) -> bool {
@@ -666,163 +666,86 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 if (lane == 0) mbar_arrive(&sm.acc_free[uc & 1]);
                 ++uc;
             };
-            // FastScan: scores TMEM -> shared memory (16-bit wrap of the signed-LUT sum)
             const uint64_t t_copy = prof ? global_ns() : 0;
             if (S.fs) {
-                uint32_t dcol;
-                if (!gemm_begin(dcol)) {
-                    bad = true;
-                } else {
+                // FastScan item: every row's score (16-bit wrap of the signed-LUT sum) and then
+                // its int_ip to the FastScan scratch; fs_select_kernel takes the kept sets
+                for (int g = 0; g < 2 && !bad; ++g) {
+                    const uint64_t t_g = prof ? global_ns() : 0;
+                    uint32_t dcol;
+                    if (!gemm_begin(dcol)) {
+                        bad = true;
+                        break;
+                    }
                     for (int t = 0; t < T; ++t) {
                         const int v = t * kRows + quarter * 32 + lane;
                         for (int c = c_lo; c < c_hi && c < nq; c += 8) {
-                            uint32_t v8[8];
-                            tmem_ld8(dcol + (uint32_t)(t * N + c), v8);
+                            uint32_t x[8];
+                            tmem_ld8(dcol + (uint32_t)(t * N + c), x);
+                            if (v >= n) continue;
 #pragma unroll
-                            for (int jj = 0; jj < 8; ++jj)
-                                if (c + jj < nq) sm.sc[(c + jj) * NP + v] = (int16_t)((int)v8[jj] - lut_bias);
+                            for (int jj = 0; jj < 8; ++jj) {
+                                if (c + jj >= nq) break;
+                                const int64_t o = S.fsb[c + jj] + v;
+                                if (g == 0)
+                                    a.fs_sc[o] = (int16_t)((int)x[jj] - lut_bias);
+                                else
+                                    a.fs_ip[o] = (int32_t)x[jj];
+                            }
                         }
                     }
                     gemm_end();
+                    padd(pl, g == 0 ? p_copy : p_rr, t_g);
                 }
+                if (epi_sync_or(bad)) {
+                    fail(8);
+                    break;
+                }
+                padd(pl, p_loop, t_body);
+                if (lane == 0) mbar_arrive(&sm.item_empty[si]);
+                continue;
             }
-            if (epi_sync_or(bad)) {  // (also: every warp's scores are visible)
-                fail(8);
-                break;
-            }
-            padd(pl, p_copy, t_copy);
             const uint64_t t_sel = prof ? global_ns() : 0;
-            // the kept set of each query (warp per query) and its candidates' tie keys
-            for (int i = e; i < nq; i += kEpiWarps) {
-                const int bsi = S.bsi[i];
-                const uint64_t* bw = bsi >= 0 ? a.bitsets + (int64_t)bsi * a.bitset_words : nullptr;
-                if (!S.fs && !bw) {
-                    // |list| <= n_cand and no filter: every row is kept at its own position
-                    // (the bitmap in closed form)
-                    for (int w = lane; w < W; w += 32) {
+            // rerank-only item (|list| <= n_cand): every live row is kept.  The kept rows as
+            // bitmap words (row v is bit v % 32 of word v / 32) with the kept rows before each
+            // word: without a filter in closed form (thread per query), else a warp per query.
+            {
+                const int qpw = (nq + kEpiWarps - 1) / kEpiWarps;
+                const int i = e * qpw + lane;
+                if (lane < qpw && i < nq && S.bsi[i] < 0) {
+                    for (int w = 0; w < W; ++w) {
                         const int lo = 32 * w;
                         sm.bitmap[i * W + w] = lo >= n ? 0u : (n - lo >= 32 ? 0xFFFFFFFFu : (1u << (n - lo)) - 1u);
                         sm.prefix[i * W + w] = min(lo, n);
                     }
-                    const int64_t rb = S.base[i];
-                    const uint64_t rank_bits = (uint64_t)S.rank[i] << 48;
-                    for (int v = lane; v < n; v += 32) {
-                        a.cand_tie[rb + v] = rank_bits | (uint32_t)v;
-                        if (a.cand_dbg) a.cand_dbg[rb + v].y = INT32_MIN;
-                    }
-                    continue;
                 }
-                // the live rows, as this lane's bits: row v = lane + 32 j is bit j of lm0 (j < 32)
-                // or of lm1 (j >= 32); n <= kTcMaxRows = 2048 rows
-                uint32_t lm0 = 0u, lm1 = 0u;
-                for (int v = lane, jb = 0; v < n; v += 32, ++jb)
-                    if (!bw || !filtered(bw, a.bitset_len, a.ids[beg + v])) {
-                        if (jb < 32)
-                            lm0 |= 1u << jb;
-                        else
-                            lm1 |= 1u << (jb - 32);
-                    }
-                auto live = [&](int v) {
-                    const int jb = v >> 5;
-                    return (((jb < 32 ? lm0 : lm1) >> (jb & 31)) & 1u) != 0u;
-                };
-                const int n_live = __reduce_add_sync(0xffffffffu, __popc(lm0) + __popc(lm1));
-                const int16_t* sv = sm.sc + i * NP;
-                uint32_t* bm = sm.bitmap + i * W;
-                int* px = sm.prefix + i * W;
-                const int64_t rb = S.base[i];
-                const uint64_t rank_bits = (uint64_t)S.rank[i] << 48;
+            }
+            for (int i = e; i < nq; i += kEpiWarps) {
+                const int bsi = S.bsi[i];
+                if (bsi < 0) continue;
+                const uint64_t* bw = a.bitsets + (int64_t)bsi * a.bitset_words;
                 int n_c = 0;
-                if (S.fs && n_live > a.n_cand) {
-                    // s* = n_cand-th largest score among live rows (key = 32767 - score); the
-                    // kept set is every row above s* plus the s*-rows the reference's heap keeps
-                    auto key_at = [&](int v, uint32_t& k) {
-                        if (!live(v)) return false;
-                        k = (uint32_t)(32767 - (int)sv[v]);
-                        return true;
-                    };
-                    int c_gt = 0;
-                    const uint32_t tau = warp_radix_kth(n, a.n_cand, key_at, sm.hist[e], &c_gt);
-                    // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
-                    int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = c_gt;
-                    for (int base = 0; base < n; base += 32) {
-                        const int v = base + lane;
-                        uint32_t k = 0xFFFFFFFFu;
-                        const bool valid = v < n && key_at(v, k);
-                        const bool ge = valid && k <= tau, gt = valid && k < tau;
-                        const unsigned bge = __ballot_sync(0xffffffffu, ge);
-                        const unsigned bgt = __ballot_sync(0xffffffffu, gt);
-                        const int c = __popc(bge);
-                        if (cnt_ge + c >= a.n_cand) {
-                            const int need = a.n_cand - cnt_ge;
-                            const bool here = ge && __popc(bge & lanemask_le()) == need;
-                            const int pos = __ffs(__ballot_sync(0xffffffffu, here)) - 1;
-                            p_end = base + pos;
-                            gt_f = cnt_gt + __popc(bgt & (pos == 31 ? 0xffffffffu : ((2u << pos) - 1u)));
-                            break;
-                        }
-                        cnt_ge += c;
-                        cnt_gt += __popc(bgt);
+                for (int base = 0; base < NP; base += 32) {
+                    const int v = base + lane;
+                    const unsigned bk =
+                        __ballot_sync(0xffffffffu, v < n && !filtered(bw, a.bitset_len, a.ids[beg + v]));
+                    if (lane == 0) {
+                        sm.bitmap[i * W + (base >> 5)] = bk;
+                        sm.prefix[i * W + (base >> 5)] = n_c;
                     }
-                    const int m_drop = c_gt - gt_f;  // lowest-index ties evicted by later rows
-                    int eq_seen = 0;
-                    for (int base = 0; base < NP; base += 32) {
-                        const int v = base + lane;
-                        uint32_t k = 0xFFFFFFFFu;
-                        const bool valid = v < n && key_at(v, k);
-                        const bool gt = valid && k < tau;
-                        const bool eq = valid && k == tau && v <= p_end;
-                        const unsigned beq = __ballot_sync(0xffffffffu, eq);
-                        const int eq_rank = eq_seen + __popc(beq & lanemask_le());
-                        const bool keep = gt || (eq && eq_rank > m_drop);
-                        const unsigned bk = __ballot_sync(0xffffffffu, keep);
-                        if (lane == 0) {
-                            bm[base >> 5] = bk;
-                            px[base >> 5] = n_c;
-                        }
-                        if (keep) {
-                            const int pos = n_c + __popc(bk & lanemask_lt());
-                            if (pos < a.n_cand) {
-                                a.cand_tie[rb + pos] = rank_bits | ((uint64_t)k << 32) | (uint32_t)v;
-                                if (a.cand_dbg) a.cand_dbg[rb + pos].y = 32767 - (int)k;
-                            }
-                        }
-                        n_c += __popc(bk);
-                        eq_seen += __popc(beq);
-                    }
-                } else {
-                    // every live row is kept, in list order
-                    for (int base = 0; base < NP; base += 32) {
-                        const int v = base + lane;
-                        const bool keep = v < n && live(v);
-                        const unsigned bk = __ballot_sync(0xffffffffu, keep);
-                        if (lane == 0) {
-                            bm[base >> 5] = bk;
-                            px[base >> 5] = n_c;
-                        }
-                        if (keep) {
-                            const int pos = n_c + __popc(bk & lanemask_lt());
-                            if (pos < a.n_cand) {
-                                a.cand_tie[rb + pos] = rank_bits | (uint32_t)v;
-                                if (a.cand_dbg) a.cand_dbg[rb + pos].y = INT32_MIN;
-                            }
-                        }
-                        n_c += __popc(bk);
-                    }
+                    n_c += __popc(bk);
                 }
-                n_c = min(n_c, a.n_cand);
-                // unused entries of the pair's region of min(|list|, n_cand) entries (rows
-                // removed by the filter)
-                const int cap = min(n, a.n_cand);
-                for (int jj = n_c + lane; jj < cap; jj += 32) {
+                // unused entries of the pair's region of |list| entries (rows removed by the filter)
+                const int64_t rb = S.base[i];
+                for (int jj = n_c + lane; jj < n; jj += 32) {
                     a.cand_tie[rb + jj] = ~0ull;
                     a.cand_key[rb + jj] = 0xFFFFFFFFu;
                 }
             }
-            bad = epi_sync_or(false);
+            bad = epi_sync_or(false);  // (every bitmap is visible after it)
             padd(pl, p_sel, t_sel);
             const uint64_t t_rr = prof ? global_ns() : 0;
-            // rerank: thread per row, the distances of the kept (query, row) pairs
+            // rerank: thread per row, the distance and tie keys of the kept (query, row) pairs
             uint32_t dcol;
             if (!bad && !gemm_begin(dcol)) bad = true;
             if (!bad) {
@@ -836,7 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         uint32_t ip[8];
                         tmem_ld8(dcol + (uint32_t)(t * N + c), ip);
                         // the 8 queries are independent: every load is unconditional (query
-                        // index clamped), only the distance and its store are predicated
+                        // index clamped), only the distance and its stores are predicated
 #pragma unroll
                         for (int jj = 0; jj < 8; ++jj) {
                             const int i = min(c + jj, nq - 1);
@@ -848,10 +771,12 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                             qp.q_norm_sq = S.q_norm_sq[i];
                             qp.q_i8_sum = S.q_i8_sum[i];
                             const int64_t dst = S.base[i] + pos;
-                            if (row_ok && c + jj < nq && ((word >> lane) & 1u) && pos < a.n_cand) {
+                            const uint64_t rank_bits = (uint64_t)S.rank[i] << 48;
+                            if (row_ok && c + jj < nq && ((word >> lane) & 1u)) {
                                 const float dist = rerank_distance((int)ip[jj], m, qp, a.nbits, l2);
-                                a.cand_key[dst] = total_order_key(dist);  // (its tie: the selection)
-                                if (a.cand_dbg) a.cand_dbg[dst].x = (int)ip[jj];
+                                a.cand_key[dst] = total_order_key(dist);
+                                a.cand_tie[dst] = rank_bits | (uint32_t)v;  // (no FastScan key)
+                                if (a.cand_dbg) a.cand_dbg[dst] = make_int2((int)ip[jj], INT32_MIN);
                             }
                         }
                     }

@@ -1223,22 +1223,30 @@ __global__ void make_items_kernel(const int* __restrict__ cnt, const int* __rest
 __global__ void pair_offsets_kernel(const int32_t* __restrict__ probes, int64_t nq, int nprobe,
                                     const int64_t* __restrict__ list_off, int nlist,
                                     const uint8_t* __restrict__ owned, int n_cand,
-                                    int* __restrict__ pair_off) {
+                                    int* __restrict__ pair_off, int tc_rows, int* __restrict__ fs_off) {
     const int lane = (int)lane_id();
     const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (q >= nq) return;
-    int carry = 0;
+    int carry = 0, fs_carry = 0;
     for (int r0 = 0; r0 < nprobe; r0 += 32) {
         const int r = r0 + lane;
-        int cap = 0;
+        int cap = 0, fs_n = 0;
         if (r < nprobe) {
             const int l = probes[q * nprobe + r];
-            if (l >= 0 && l < nlist && (!owned || owned[l]))
-                cap = (int)min(list_off[l + 1] - list_off[l], (int64_t)n_cand);
+            if (l >= 0 && l < nlist && (!owned || owned[l])) {
+                const int64_t n = list_off[l + 1] - list_off[l];
+                cap = (int)min(n, (int64_t)n_cand);
+                if (n > n_cand && n <= tc_rows) fs_n = (int)n;  // a tensor-core FastScan pair
+            }
         }
         const int inc = warp_inclusive_scan(cap);
         if (r < nprobe) pair_off[q * (nprobe + 1) + r] = carry + inc - cap;
         carry += __shfl_sync(0xffffffffu, inc, 31);
+        if (fs_off) {
+            const int finc = warp_inclusive_scan(fs_n);
+            if (r < nprobe) fs_off[q * nprobe + r] = fs_n > 0 ? fs_carry + finc - fs_n : -1;
+            fs_carry += __shfl_sync(0xffffffffu, finc, 31);
+        }
     }
     if (lane == 0) pair_off[q * (nprobe + 1) + nprobe] = carry;
 }
@@ -2089,6 +2097,120 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
 }
 
 // ============================================================================
+// Kept sets of the tensor-core FastScan pairs (n_cand < |list| <= the tensor-core row limit):
+// the tensor-core scan wrote every row's 16-bit FastScan score and int_ip of the pair to the
+// FastScan scratch; a warp per pair takes the reference heap's kept set with the closed form
+// of scan_lists_kernel (src/quantization/usq/fastscan.rs:86-146) and writes each kept row's
+// distance key (src/quantization/usq/quantizer.rs:274-288) and tie to the pair's region.
+// ============================================================================
+__global__ void __launch_bounds__(256) fs_select_kernel(FsSelectArgs a) {
+    __shared__ uint32_t hist[8][256];
+    const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    const int64_t pr = (int64_t)blockIdx.x * 8 + w;
+    if (pr >= a.nq * a.nprobe) return;
+    const int fo = a.fs_off[pr];
+    if (fo < 0) return;
+    const int64_t q = pr / a.nprobe;
+    const int r = (int)(pr - q * a.nprobe);
+    const int l = a.probes[pr];
+    const int64_t beg = a.list_off[l];
+    const int n = (int)(a.list_off[l + 1] - beg);
+    const int16_t* sc = a.fs_sc + q * a.fs_stride + fo;
+    const int32_t* ip = a.fs_ip + q * a.fs_stride + fo;
+    const QueryParams qp = a.qp[q];
+    const bool l2 = a.metric_l2 != 0;
+    const int64_t rbase = q * a.q_stride + a.pair_off[q * (a.nprobe + 1) + r];
+    const uint64_t* bw = nullptr;
+    if (a.fused && a.bitsets) {
+        const int b = a.query_bitset ? a.query_bitset[q] : 0;
+        if (b >= 0 && b < a.n_bitsets) bw = a.bitsets + (int64_t)b * a.bitset_words;
+    }
+    auto live = [&](int v) { return !bw || !bit_filtered(bw, a.bitset_len, a.ids[beg + v]); };
+    int n_live = n;
+    if (bw) {
+        int c = 0;
+        for (int v = lane; v < n; v += 32) c += live(v) ? 1 : 0;
+        n_live = warp_sum(c);
+    }
+    const uint64_t rank_bits = (uint64_t)r << 48;
+    // kept row v at position pos: its distance and tie (fs_key ~0: no FastScan key)
+    auto emit = [&](int v, int pos, uint32_t fs_key) {
+        const float dist = rerank_distance(ip[v], __ldg(a.meta + beg + v), qp, a.nbits, l2);
+        a.cand_key[rbase + pos] = total_order_key(dist);
+        a.cand_tie[rbase + pos] = rank_bits | (fs_key != 0xFFFFFFFFu ? (uint64_t)fs_key << 32 : 0ull) | (uint32_t)v;
+        if (a.cand_dbg)
+            a.cand_dbg[rbase + pos] = make_int2(ip[v], fs_key != 0xFFFFFFFFu ? 32767 - (int)fs_key : INT32_MIN);
+    };
+    int n_c = 0;
+    if (n_live > a.n_cand) {
+        // s* = n_cand-th largest score among live rows (key = 32767 - score)
+        auto key_at = [&](int v, uint32_t& k) {
+            if (!live(v)) return false;
+            k = (uint32_t)(32767 - (int)sc[v]);
+            return true;
+        };
+        int c_gt = 0, c_eq = 0;
+        const uint32_t tau = warp_radix_kth16(n, a.n_cand, key_at, hist[w], &c_gt, &c_eq);
+        // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
+        // When exactly n_cand rows score >= s*, F is all of them (no pass needed).
+        int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = c_gt;
+        for (int base = 0; c_gt + c_eq != a.n_cand && base < n; base += 32) {
+            const int v = base + lane;
+            uint32_t k = 0xFFFFFFFFu;
+            const bool valid = v < n && key_at(v, k);
+            const bool ge = valid && k <= tau, gt = valid && k < tau;
+            const unsigned bge = __ballot_sync(0xffffffffu, ge);
+            const unsigned bgt = __ballot_sync(0xffffffffu, gt);
+            const int c = __popc(bge);
+            if (cnt_ge + c >= a.n_cand) {
+                const int need = a.n_cand - cnt_ge;
+                const bool here = ge && __popc(bge & lanemask_le()) == need;
+                const int pos = __ffs(__ballot_sync(0xffffffffu, here)) - 1;
+                p_end = base + pos;
+                gt_f = cnt_gt + __popc(bgt & (pos == 31 ? 0xffffffffu : ((2u << pos) - 1u)));
+                break;
+            }
+            cnt_ge += c;
+            cnt_gt += __popc(bgt);
+        }
+        const int m_drop = c_gt - gt_f;  // lowest-index ties evicted by later rows
+        int eq_seen = 0;
+        for (int base = 0; base < n; base += 32) {
+            const int v = base + lane;
+            uint32_t k = 0xFFFFFFFFu;
+            const bool valid = v < n && key_at(v, k);
+            const bool gt = valid && k < tau;
+            const bool eq = valid && k == tau && v <= p_end;
+            const unsigned beq = __ballot_sync(0xffffffffu, eq);
+            const int eq_rank = eq_seen + __popc(beq & lanemask_le());
+            const bool keep = gt || (eq && eq_rank > m_drop);
+            const unsigned bk = __ballot_sync(0xffffffffu, keep);
+            if (keep) {
+                const int pos = n_c + __popc(bk & lanemask_lt());
+                if (pos < a.n_cand) emit(v, pos, k);
+            }
+            n_c += __popc(bk);
+            eq_seen += __popc(beq);
+        }
+    } else {
+        // every live row is kept, in list order
+        for (int base = 0; base < n; base += 32) {
+            const int v = base + lane;
+            const bool keep = v < n && live(v);
+            const unsigned bk = __ballot_sync(0xffffffffu, keep);
+            if (keep) emit(v, n_c + __popc(bk & lanemask_lt()), 0xFFFFFFFFu);
+            n_c += __popc(bk);
+        }
+    }
+    n_c = min(n_c, a.n_cand);
+    // unused entries of the pair's region of n_cand entries (rows removed by the filter)
+    for (int j = n_c + lane; j < a.n_cand; j += 32) {
+        a.cand_tie[rbase + j] = ~0ull;
+        a.cand_key[rbase + j] = 0xFFFFFFFFu;
+    }
+}
+
+// ============================================================================
 // Final merge, one 256-thread block per query (k <= kMergeMaxK): the top k of all kept
 // candidates of the query's probes by (distance key, tie = probe rank << 48 | FastScan key
 // << 32 | position), sorted -- the same result as compact_pairs_kernel + merge_kernel.
@@ -2451,11 +2573,11 @@ int scan_grid_size(int D) {
 }
 
 void launch_pair_offsets(const int32_t* probes, int64_t nq, int nprobe, const int64_t* list_off,
-                         int nlist, const uint8_t* owned, int n_cand, int* pair_off,
-                         cudaStream_t s) {
+                         int nlist, const uint8_t* owned, int n_cand, int* pair_off, int tc_rows,
+                         int* fs_off, cudaStream_t s) {
     if (nq <= 0) return;
     pair_offsets_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(probes, nq, nprobe, list_off, nlist,
-                                                                owned, n_cand, pair_off);
+                                                                owned, n_cand, pair_off, tc_rows, fs_off);
 }
 
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s) {
@@ -2479,6 +2601,11 @@ void launch_compact_pairs(const CompactArgs& a, cudaStream_t s) {
 void launch_merge(const MergeArgs& a, cudaStream_t s) {
     if (a.nq <= 0) return;
     merge_kernel<<<(unsigned)((a.nq + 3) / 4), 128, 0, s>>>(a);
+}
+
+void launch_fs_select(const FsSelectArgs& a, cudaStream_t s) {
+    const int64_t pairs = a.nq * a.nprobe;
+    if (pairs > 0) fs_select_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(a);
 }
 
 void launch_merge_direct(const MergeArgs& a, cudaStream_t s) {
