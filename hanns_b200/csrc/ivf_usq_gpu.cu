@@ -870,13 +870,14 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
             static const char* names[] = {"build", "build_wait_slot", "build_wait_item", "mma_wait_full",
                                           "mma_wait_free", "mma", "epi_wait_acc", "epi_copy",
                                           "epi_select", "epi_rerank", "epi_wait_item", "epi",
-                                          "items", "stages"};
+                                          "items", "stages", "build_store", "build_fence"};
             std::fprintf(stderr, "TC_SCAN_PROFILE ctas=%d", sm_count_);
-            for (int k = 0; k < 14; ++k) {
+            for (int k = 0; k < 16; ++k) {
                 double sum = 0;
                 for (int c = 0; c < sm_count_; ++c) sum += (double)h[(size_t)c * kTcProfSlots + k];
-                std::fprintf(stderr, k < 12 ? " %s=%.3fms" : " %s=%.1f", names[k],
-                             k < 12 ? sum / sm_count_ / 1e6 : sum / sm_count_);
+                const bool count = k == 12 || k == 13;
+                std::fprintf(stderr, count ? " %s=%.1f" : " %s=%.3fms", names[k],
+                             count ? sum / sm_count_ : sum / sm_count_ / 1e6);
             }
             std::fprintf(stderr, "\n");
         }
