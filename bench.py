@@ -287,10 +287,11 @@ def index_stats(art, probes, k, nbits):
 
 
 def scan_roofline_tc(workload, alg_bytes, ops, scan_s, world):
-    """Roofline of the tensor-core list scan (the dominant stage): executed int8 MMA ops
-    per launch over the live CUDA-event time against the dense int8 rate; beside it the
-    per-(query, probe) stream bytes of the reference's loop (algorithmic_*) and the DRAM
-    bytes ncu measured for one launch (dram_*)."""
+    """Roofline of the tensor-core list scan kernel (the dominant kernel): executed int8 MMA
+    ops per launch over its live CUDA-event launch time against the dense int8 rate; beside
+    it the per-(query, probe) stream bytes of the reference's loop (algorithmic_*) and the
+    DRAM bytes ncu measured for one launch (dram_*).  Neither the tensor pipe nor DRAM is
+    the limit: `limiter` names what is."""
     peak, src = int8_peak()
     hbm, hbm_kind = peaks()
     kernel = "scan_tc_kernel"
@@ -303,7 +304,11 @@ def scan_roofline_tc(workload, alg_bytes, ops, scan_s, world):
                                f"{ncu_ms} ms under ncu)") if traffic else "no ncu capture for this workload",
             "algorithmic_bytes_per_launch": alg_bytes, "algorithmic_gbs": alg_bytes / scan_s / 1e9,
             "algorithmic_frac_of_hbm": alg_bytes / scan_s / 1e9 / hbm, "hbm_peak_gbs": hbm,
-            "hbm_peak_source": hbm_kind}
+            "hbm_peak_source": hbm_kind,
+            "limiter": "operand staging: per 16 KiB K slab the builder warps expand sign bits to "
+                       "one-hot rows / unpack codes in shared memory and hand the stage to the "
+                       "single MMA-issuing thread through an mbarrier round trip; at 64-128 "
+                       "queries per item each stage carries ~0.1 us of tensor work"}
     if traffic:
         roof["dram_gbs"] = traffic / scan_s / 1e9
         roof["dram_frac_of_hbm"] = roof["dram_gbs"] / hbm
@@ -555,6 +560,10 @@ def run_ours(args, w, rank, world, local_rank):
     calls = args.steps if world == 1 else 2 * args.steps
     st_sum, st_cnt, _ = idx.stage_ms_recent(calls)
     scan_ms = [float(st_sum[5]) / max(int(st_cnt[5]), 1)]
+    # the list scan's kernels, each timed by CUDA events on the launching stream
+    kt_sum, kt_cnt = idx.scan_kernel_ms_recent(calls)
+    scan_kernels_ms = {name: float(kt_sum[i]) / max(int(kt_cnt[i]), 1)
+                       for i, name in enumerate(IvfUsqIndex.SCAN_KERNELS)}
     rank_stages = None
     if world > 1:
         launches[0] = sh.launches
@@ -688,12 +697,13 @@ def run_ours(args, w, rank, world, local_rank):
         own = np.diff(art_local["list_offsets"]) > 0
         probes = probes[own[probes]]
     alg = scan_bytes(art_local, probes, k, w["nbits"])
-    scan_s = statistics.median(scan_ms) / 1e3
     if os.environ.get("HANNS_GPU_SCAN") == "simt":
-        roof = scan_roofline(args.workload, alg, scan_s, world)
+        roof = scan_roofline(args.workload, alg, scan_kernels_ms["scan_simt"] / 1e3, world)
     else:
         roof = scan_roofline_tc(args.workload, alg, scan_tc_ops(art_local, probes, k, w["nbits"]),
-                                scan_s, world)
+                                scan_kernels_ms["scan_tc"] / 1e3, world)
+    roof["scan_stage_ms"] = statistics.median(scan_ms)
+    roof["scan_kernels_ms"] = scan_kernels_ms
 
     # ---- recall and parity sample
     rec = None

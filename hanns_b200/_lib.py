@@ -126,6 +126,7 @@ SIGNATURES = [
       vp, vp]),
     ("hanns_gpu_ivf_usq_stage_ms", C.c_int32, [vp, f32p]),
     ("hanns_gpu_ivf_usq_stage_ms_recent", C.c_int32, [vp, C.c_int32, f32p, i32p]),
+    ("hanns_gpu_ivf_usq_scan_kernel_ms_recent", C.c_int32, [vp, C.c_int32, f32p, i32p]),
     ("hanns_gpu_ivf_usq_last_launches", C.c_int64, [vp]),
     ("hanns_gpu_ivf_usq_set_nprobe", C.c_int32, [vp, C.c_int32]),
     ("hanns_gpu_ivf_usq_count", C.c_int64, [vp]),

@@ -625,6 +625,14 @@ int32_t hanns_gpu_ivf_usq_stage_ms_recent(HannsIvfUsqHandle* h, int32_t n_calls,
     return rc == HANNS_OK ? covered : -rc;
 }
 
+int32_t hanns_gpu_ivf_usq_scan_kernel_ms_recent(HannsIvfUsqHandle* h, int32_t n_calls, float* out3,
+                                                int32_t* counts3) {
+    if (!h || !out3 || !counts3 || n_calls <= 0) return HANNS_INVALID_ARG;
+    int covered = 0;
+    const int32_t rc = guarded([&] { covered = h->idx->scan_kernel_ms(n_calls, out3, counts3); });
+    return rc == HANNS_OK ? covered : -rc;
+}
+
 int64_t hanns_gpu_ivf_usq_last_launches(const HannsIvfUsqHandle* h) {
     return h ? h->idx->last_launches() : 0;
 }

@@ -165,6 +165,7 @@ void IvfUsqGpu::ensure_stream() {
         HANNS_CUDA_OK(cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming));
         for (auto& sl : ring_) {
             for (auto& e : sl.aux) HANNS_CUDA_OK(cudaEventCreate(&e));
+            for (auto& e : sl.kt) HANNS_CUDA_OK(cudaEventCreate(&e));
             for (auto& e : sl.ev) HANNS_CUDA_OK(cudaEventCreate(&e));
         }
         for (auto& e : ev_up_) HANNS_CUDA_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -859,6 +860,7 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         t.cand_key = w_cand_key_.p;
         t.cand_tie = w_cand_tie_.p;
         t.err_flag = w_scan_err_.p;
+        if (time_it) HANNS_CUDA_OK(cudaEventRecord(cur_->kt[0], s));
         launch_scan_tc(t, sm_count_, s);
         launches += 1;
         if (t.prof) {
@@ -882,8 +884,13 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
             std::fprintf(stderr, "\n");
         }
     }
+    if (time_it) {
+        if (!use_tc) HANNS_CUDA_OK(cudaEventRecord(cur_->kt[0], s));
+        HANNS_CUDA_OK(cudaEventRecord(cur_->kt[1], s));
+    }
     launch_scan(a, grid, s);
     launches += 1;
+    if (time_it) HANNS_CUDA_OK(cudaEventRecord(cur_->kt[2], s));
     if (fss > 0) {
         // kept sets and distances of the tensor-core FastScan pairs
         FsSelectArgs f{};
@@ -914,6 +921,10 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         f.cand_dbg = a.cand_dbg;
         launch_fs_select(f, s);
         launches += 1;
+    }
+    if (time_it) {
+        HANNS_CUDA_OK(cudaEventRecord(cur_->kt[3], s));
+        cur_->kt_timed = true;
     }
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[6], s));
     // 5-6. the top k of each query over its candidate regions: one block per query
@@ -1044,6 +1055,7 @@ void IvfUsqGpu::next_slot(int first, int last) {
     cur_->first = first;
     cur_->last = last;
     cur_->aux_timed = false;
+    cur_->kt_timed = false;
     ev_ = cur_->ev;
     ev_aux_ = cur_->aux;
     ++slot_seq_;
@@ -1099,6 +1111,29 @@ int IvfUsqGpu::stage_ms(int n_calls, float* out, int* counts) {
             HANNS_CUDA_OK(cudaEventElapsedTime(&t, sl.ev[sl.first], sl.ev[sl.last]));
             out[kStages] += t;
             if (counts) ++counts[kStages];
+        }
+    }
+    return covered;
+}
+
+int IvfUsqGpu::scan_kernel_ms(int n_calls, float* out3, int* counts3) {
+    for (int e = 0; e < 3; ++e) {
+        out3[e] = 0;
+        counts3[e] = 0;
+    }
+    int covered = 0;
+    for (auto it = calls_.rbegin(); it != calls_.rend() && covered < n_calls; ++it, ++covered) {
+        if (slot_seq_ - it->first > kEvRing) break;  // its slots were reused
+        for (int j = 0; j < it->second; ++j) {
+            const StageSlot& sl = ring_[(it->first + j) % kEvRing];
+            if (!sl.kt_timed) continue;
+            HANNS_CUDA_OK(cudaEventSynchronize(sl.kt[3]));
+            for (int e = 0; e < 3; ++e) {
+                float t;
+                HANNS_CUDA_OK(cudaEventElapsedTime(&t, sl.kt[e], sl.kt[e + 1]));
+                out3[e] += t;
+                ++counts3[e];
+            }
         }
     }
     return covered;

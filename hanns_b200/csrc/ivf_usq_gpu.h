@@ -151,6 +151,9 @@ class IvfUsqGpu {
     // events.  counts (nullable): batches that timed each stage.  Returns the number of
     // calls covered (calls older than the event ring are not).
     int stage_ms(int n_calls, float* out, int* counts = nullptr);
+    // device ms of the list scan's kernels {tensor-core scan, SIMT scan, FastScan selection}
+    // summed over the batches of the last n_calls calls; counts3: batches timed
+    int scan_kernel_ms(int n_calls, float* out3, int* counts3);
     int64_t last_launches() const { return last_launches_; }
     std::mutex& mutex() { return mu_; }
 
@@ -260,6 +263,10 @@ class IvfUsqGpu {
         cudaEvent_t ev[kStages + 1] = {};
         cudaEvent_t aux[3] = {};  // rotation start / end, query state end (aux stream)
         bool aux_timed = false;
+        // inside the list scan: before the tensor-core kernel, after it, after the SIMT scan,
+        // after the FastScan selection
+        cudaEvent_t kt[4] = {};
+        bool kt_timed = false;
         int first = 0, last = 0;  // events first..last were recorded
     };
     StageSlot ring_[kEvRing];

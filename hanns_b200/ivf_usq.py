@@ -276,6 +276,19 @@ class IvfUsqIndex:
             _check(-rc, "stage_ms_recent")
         return out, cnt, int(rc)
 
+    SCAN_KERNELS = ("scan_tc", "scan_simt", "fs_select")
+
+    def scan_kernel_ms_recent(self, n_calls: int):
+        """(sum of device ms per list-scan kernel (names in SCAN_KERNELS), batches timed)
+        over the last n_calls search calls."""
+        out = np.zeros(3, np.float32)
+        cnt = np.zeros(3, np.int32)
+        rc = L.lib().hanns_gpu_ivf_usq_scan_kernel_ms_recent(self._h, int(n_calls), _p(out, L.f32p),
+                                                             _p(cnt, L.i32p))
+        if rc < 0:
+            _check(-rc, "scan_kernel_ms_recent")
+        return out, cnt
+
     def last_launches(self) -> int:
         return int(L.lib().hanns_gpu_ivf_usq_last_launches(self._h))
 

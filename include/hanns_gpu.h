@@ -238,6 +238,11 @@ int32_t hanns_gpu_ivf_usq_stage_ms(HannsIvfUsqHandle* h, float* out8);
  * Returns how many calls it covered, or -(error code). */
 int32_t hanns_gpu_ivf_usq_stage_ms_recent(HannsIvfUsqHandle* h, int32_t n_calls, float* out8,
                                           int32_t* counts8);
+/* Device time (ms) of the list scan's kernels, out3 = {tensor-core list scan, SIMT list scan,
+ * FastScan kept-set selection}, summed over the batches of the last n_calls search calls;
+ * counts3 = batches timed.  Returns how many calls it covered, or -(error code). */
+int32_t hanns_gpu_ivf_usq_scan_kernel_ms_recent(HannsIvfUsqHandle* h, int32_t n_calls, float* out3,
+                                                int32_t* counts3);
 /* Number of kernel launches of the last search. */
 int64_t hanns_gpu_ivf_usq_last_launches(const HannsIvfUsqHandle* h);
 int32_t hanns_gpu_ivf_usq_set_nprobe(HannsIvfUsqHandle* h, int32_t nprobe);
