@@ -96,7 +96,7 @@ int64_t IvfUsqGpu::fs_stride(int nprobe, int n_cand, int tc_rows) {
     std::vector<int64_t> sz;
     for (int l = 0; l < nlist_; ++l) {
         const int64_t n = h_list_off_[l + 1] - h_list_off_[l];
-        if (n > n_cand && n <= tc_rows) sz.push_back(n);
+        if (n > n_cand && n <= tc_rows) sz.push_back((n + 7) & ~7ll);  // (regions padded to 8)
     }
     const size_t m = std::min<size_t>(sz.size(), (size_t)nprobe);
     std::partial_sort(sz.begin(), sz.begin() + m, sz.end(), std::greater<int64_t>());

@@ -1236,7 +1236,8 @@ __global__ void pair_offsets_kernel(const int32_t* __restrict__ probes, int64_t 
             if (l >= 0 && l < nlist && (!owned || owned[l])) {
                 const int64_t n = list_off[l + 1] - list_off[l];
                 cap = (int)min(n, (int64_t)n_cand);
-                if (n > n_cand && n <= tc_rows) fs_n = (int)n;  // a tensor-core FastScan pair
+                // a tensor-core FastScan pair: |list| entries, padded to 8 (16-byte regions)
+                if (n > n_cand && n <= tc_rows) fs_n = (int)((n + 7) & ~7ll);
             }
         }
         const int inc = warp_inclusive_scan(cap);
@@ -2103,8 +2104,144 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
 // of scan_lists_kernel (src/quantization/usq/fastscan.rs:86-146) and writes each kept row's
 // distance key (src/quantization/usq/quantizer.rs:274-288) and tie to the pair's region.
 // ============================================================================
-__global__ void __launch_bounds__(256) fs_select_kernel(FsSelectArgs a) {
+// Packed halfword compare result (0xFFFF per true half) -> 2 bits, low half first.
+__device__ __forceinline__ uint32_t half_bits(uint32_t m) { return (m & 1u) | ((m >> 15) & 2u); }
+
+// Position of the k-th (1-based) set bit of x (x has at least k).
+__device__ __forceinline__ int nth_set_bit64(uint64_t x, int k) {
+    for (int i = 1; i < k; ++i) x &= x - 1ull;
+    return __ffsll((long long)x) - 1;
+}
+
+// Kept set and distances of one unfiltered tensor-core FastScan pair (n_cand < n <= 64 PW
+// rows), a warp with the pair's scores in registers: lane l holds rows l * 2 PW .. + 2 PW
+// (list order is lane-major) as packed halfwords.  s* = the n_cand-th largest score by
+// binary search on the score (packed compares, one warp reduction per probe); the heap
+// boundary and the evicted ties at s* from per-lane row masks and warp prefix sums; the
+// kept rows' int_ip and metadata are loaded four rows at a time before their distances.
+template <int PW>
+__device__ void fs_select_regs(const FsSelectArgs& a, int64_t q, int r, int64_t beg, int n,
+                               const int16_t* gsc, const int32_t* gip, int lane, uint32_t* kept) {
+    constexpr int RPL = 2 * PW;  // rows per lane
+    const int row0 = lane * RPL;
+    const int npad = (n + 7) & ~7;  // the pair's scratch region
+    uint32_t sw[PW];
+#pragma unroll
+    for (int k = 0; k < PW / 4; ++k) {
+        const int rr = row0 + 8 * k;
+        const uint4 x = rr < npad ? __ldg(reinterpret_cast<const uint4*>(gsc + rr))
+                                  : make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
+        sw[4 * k] = x.x;
+        sw[4 * k + 1] = x.y;
+        sw[4 * k + 2] = x.z;
+        sw[4 * k + 3] = x.w;
+    }
+    const uint64_t valid = row0 >= n ? 0ull
+                                     : (n - row0 >= RPL ? (RPL == 64 ? ~0ull : (1ull << RPL) - 1ull)
+                                                        : (1ull << (n - row0)) - 1ull);
+    // rows >= n read as -32768: never counted by the search (its probes are > the minimum)
+    uint32_t mx = 0x80008000u, mn = 0x7FFF7FFFu;
+#pragma unroll
+    for (int wi = 0; wi < PW; ++wi) {
+        const uint32_t hm = ((valid >> (2 * wi)) & 1ull ? 0x0000FFFFu : 0u) | ((valid >> (2 * wi + 1)) & 1ull ? 0xFFFF0000u : 0u);
+        sw[wi] = (sw[wi] & hm) | (0x80008000u & ~hm);
+        mx = __vmaxs2(mx, sw[wi]);
+        mn = __vmins2(mn, (sw[wi] & hm) | (0x7FFF7FFFu & ~hm));
+    }
+    const int smax = __reduce_max_sync(0xffffffffu, max((int)(int16_t)(mx & 0xFFFFu), (int)(int16_t)(mx >> 16)));
+    const int smin = __reduce_min_sync(0xffffffffu, min((int)(int16_t)(mn & 0xFFFFu), (int)(int16_t)(mn >> 16)));
+    // s* = the largest y with (rows scoring >= y) >= n_cand: that count is n > n_cand at
+    // smin and 0 at smax + 1; c_hi ends as the rows above s*
+    int lo = smin, hi = smax + 1, c_hi = 0;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        const uint32_t yy = (uint32_t)(uint16_t)mid * 0x10001u;
+        uint32_t cp = 0u;  // per-half counts (each at most PW)
+#pragma unroll
+        for (int wi = 0; wi < PW; ++wi) cp += __vsetges2(sw[wi], yy);
+        const int c = (int)__reduce_add_sync(0xffffffffu, (cp & 0xFFFFu) + (cp >> 16));
+        if (c >= a.n_cand) {
+            lo = mid;
+        } else {
+            hi = mid;
+            c_hi = c;
+        }
+    }
+    const int s_star = lo, c_gt = c_hi;
+    const uint32_t ss = (uint32_t)(uint16_t)s_star * 0x10001u;
+    uint64_t ge = 0ull, gt = 0ull;
+#pragma unroll
+    for (int wi = 0; wi < PW; ++wi) {
+        ge |= (uint64_t)half_bits(__vcmpges2(sw[wi], ss)) << (2 * wi);
+        gt |= (uint64_t)half_bits(__vcmpgts2(sw[wi], ss)) << (2 * wi);
+    }
+    ge &= valid;
+    gt &= valid;
+    // boundary: p_end = the n_cand-th row with score >= s*, gt_f = rows above s* up to it
+    const int cge = __popcll(ge), cgt = __popcll(gt);
+    const int pge = warp_inclusive_scan(cge) - cge, pgt = warp_inclusive_scan(cgt) - cgt;
+    const bool here = pge < a.n_cand && pge + cge >= a.n_cand;
+    int pe = 0, gf = 0;
+    if (here) {
+        const int idx = nth_set_bit64(ge, a.n_cand - pge);
+        pe = row0 + idx;
+        gf = pgt + __popcll(gt & (idx == 63 ? ~0ull : ((2ull << idx) - 1ull)));
+    }
+    const int src = __ffs(__ballot_sync(0xffffffffu, here)) - 1;
+    const int p_end = __shfl_sync(0xffffffffu, pe, src);
+    const int m_drop = c_gt - __shfl_sync(0xffffffffu, gf, src);  // lowest-index ties evicted
+    // rows at s* up to p_end, without the first m_drop of them in list order
+    const uint64_t le_p = row0 > p_end ? 0ull : (p_end - row0 >= RPL - 1 ? ~0ull : (2ull << (p_end - row0)) - 1ull);
+    uint64_t eqm = ge & ~gt & le_p;
+    const int ceq = __popcll(eqm), peq = warp_inclusive_scan(ceq) - ceq;
+    for (int d = min(max(m_drop - peq, 0), ceq); d > 0; --d) eqm &= eqm - 1ull;
+    const uint64_t keep = gt | eqm;
+    const int ck = __popcll(keep), pk = warp_inclusive_scan(ck) - ck;
+    // the kept rows (row, score) in list order to the warp's list, then their distance keys
+    // and ties with every lane busy
+#pragma unroll
+    for (int j = 0; j < RPL; ++j) {
+        if (!((keep >> j) & 1ull)) continue;
+        const int pos = pk + __popcll(keep & ((1ull << j) - 1ull));
+        const uint32_t sv = (j & 1) ? (sw[j >> 1] >> 16) : (sw[j >> 1] & 0xFFFFu);
+        if (pos < a.n_cand) kept[pos] = ((uint32_t)(row0 + j) << 16) | sv;
+    }
+    __syncwarp();
+    const int n_kept = min(__shfl_sync(0xffffffffu, pk + ck, 31), a.n_cand);
+    const QueryParams qp = a.qp[q];
+    const bool l2 = a.metric_l2 != 0;
+    const int64_t rbase = q * a.q_stride + a.pair_off[q * (a.nprobe + 1) + r];
+    const uint64_t rank_bits = (uint64_t)r << 48;
+    for (int e0 = 0; e0 < n_kept; e0 += 64) {
+        // two entries per lane, their loads issued together
+        int ipv[2];
+        float4 mv[2];
+        uint32_t ent[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int e = e0 + 32 * h + lane;
+            ent[h] = e < n_kept ? kept[e] : 0u;
+            const int v = (int)(ent[h] >> 16);
+            ipv[h] = e < n_kept ? __ldg(gip + v) : 0;
+            mv[h] = e < n_kept ? __ldg(a.meta + beg + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int e = e0 + 32 * h + lane;
+            if (e >= n_kept) continue;
+            const int v = (int)(ent[h] >> 16), sv = (int)(int16_t)(ent[h] & 0xFFFFu);
+            const float dist = rerank_distance(ipv[h], mv[h], qp, a.nbits, l2);
+            a.cand_key[rbase + e] = total_order_key(dist);
+            a.cand_tie[rbase + e] = rank_bits | ((uint64_t)(uint32_t)(32767 - sv) << 32) | (uint32_t)v;
+            if (a.cand_dbg) a.cand_dbg[rbase + e] = make_int2(ipv[h], sv);
+        }
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(256, 4) fs_select_kernel(FsSelectArgs a) {
     __shared__ uint32_t hist[8][256];
+    __shared__ uint32_t kept_rows[8][1024];  // register path: each warp's kept (row, score)
     const int w = threadIdx.x >> 5, lane = (int)lane_id();
     const int64_t pr = (int64_t)blockIdx.x * 8 + w;
     if (pr >= a.nq * a.nprobe) return;
@@ -2124,6 +2261,14 @@ __global__ void __launch_bounds__(256) fs_select_kernel(FsSelectArgs a) {
     if (a.fused && a.bitsets) {
         const int b = a.query_bitset ? a.query_bitset[q] : 0;
         if (b >= 0 && b < a.n_bitsets) bw = a.bitsets + (int64_t)b * a.bitset_words;
+    }
+    if (!bw && n <= 1024) {
+        // unfiltered (every row live, n > n_cand): the pair's scores in registers
+        if (n <= 512)
+            fs_select_regs<8>(a, q, r, beg, n, sc, ip, lane, kept_rows[w]);
+        else
+            fs_select_regs<16>(a, q, r, beg, n, sc, ip, lane, kept_rows[w]);
+        return;
     }
     auto live = [&](int v) { return !bw || !bit_filtered(bw, a.bitset_len, a.ids[beg + v]); };
     int n_live = n;
