@@ -621,10 +621,13 @@ __device__ uint32_t block_radix_kth(const float* row, int n, int kth, uint32_t* 
 // One 256-thread block per query with the approximate row staged in shared memory
 // (nlist small enough); same result as coarse_select_exact_kernel.
 __global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
-    const float* __restrict__ approx, const float* __restrict__ q, int64_t nq,
+    float* approx, const float* __restrict__ q, int64_t nq,
     const float* __restrict__ cent, int nlist, int d, int nprobe, float cmax, float dot_rel,
-    const int* __restrict__ tc_err, int32_t* __restrict__ probes, int* __restrict__ fallbacks) {
-    extern __shared__ __align__(16) float sm[];  // row[nlist4], qs[d4], hist[kSelBins], list[kSelList]
+    const int* __restrict__ tc_err, int32_t* __restrict__ probes, int* __restrict__ fallbacks,
+    int row_in_smem) {
+    // row[nlist4] (when row_in_smem; else the row stays in global memory), qs[d4],
+    // hist[kSelBins], list[kSelList]
+    extern __shared__ __align__(16) float sm[];
     __shared__ int bcast[8];
     __shared__ float red[kSelThreads / 32];
     __shared__ int cidx[kCoarseCap];
@@ -633,14 +636,16 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
     __shared__ double thr_s;
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int64_t qi = blockIdx.x;
-    float* row = sm;
-    float* qs = sm + ((nlist + 3) & ~3);
+    float* row = row_in_smem ? sm : approx + qi * nlist;
+    float* qs = row_in_smem ? sm + ((nlist + 3) & ~3) : sm;
     uint32_t* hist = reinterpret_cast<uint32_t*>(qs + ((d + 3) & ~3));
     uint32_t* list = hist + kSelBins;
     // stage the approximate row and the query: every load of a thread is issued before
     // its first store, so the staging costs one memory round trip per 4 loads
     const float* grow = approx + qi * nlist;
-    if ((nlist & 3) == 0) {
+    if (!row_in_smem) {
+        // (read in place by the selection passes below)
+    } else if ((nlist & 3) == 0) {
         const float4* g4 = reinterpret_cast<const float4*>(grow);
         float4* r4 = reinterpret_cast<float4*>(row);
         const int n4 = nlist >> 2;
@@ -2641,11 +2646,14 @@ int launch_coarse_select(float* approx, const float* q, int64_t nq, const float*
     }
     const size_t blk_bytes =
         ((size_t)((nlist + 3) & ~3) + ((d + 3) & ~3) + kSelBins + kSelList) * sizeof(float);
-    if (blk_bytes <= 112 * 1024) {
+    // (the row in global memory: many lists -- each pass reads it from there)
+    const size_t blk_bytes_g = ((size_t)((d + 3) & ~3) + kSelBins + kSelList) * sizeof(float);
+    if (blk_bytes <= 112 * 1024 || blk_bytes_g <= 112 * 1024) {
+        const bool in_smem = blk_bytes <= 112 * 1024;
         cudaFuncSetAttribute(coarse_select_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              112 * 1024);
-        coarse_select_block_kernel<<<(unsigned)nq, kSelThreads, blk_bytes, s>>>(
-            approx, q, nq, cent, nlist, d, nprobe, cmax, dot_rel, tc_err, probes, fallbacks);
+        coarse_select_block_kernel<<<(unsigned)nq, kSelThreads, in_smem ? blk_bytes : blk_bytes_g, s>>>(
+            approx, q, nq, cent, nlist, d, nprobe, cmax, dot_rel, tc_err, probes, fallbacks, in_smem ? 1 : 0);
     } else {
         const size_t qbytes = (size_t)4 * d * sizeof(float);
         cudaFuncSetAttribute(coarse_select_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

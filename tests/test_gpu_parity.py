@@ -316,7 +316,8 @@ def _empty_artifact(cent, D, nbits=4, metric=0):
 
 @pytest.mark.parametrize("nlist,d,nprobe,normalise", [
     (4096, 768, 32, True),     # block-per-query select (row in shared memory)
-    (40000, 64, 16, False),    # warp-per-query select (row in global memory)
+    (40000, 64, 16, False),    # block-per-query select (row left in global memory)
+    (65536, 768, 64, True),    # the 20 M-row configuration's coarse shape (row in global memory)
     (2048, 96, 300, True),     # nprobe > 256: exact kernels
 ])
 def test_coarse_fast_path_equals_exact(gpu, oracle_mod, nlist, d, nprobe, normalise):
