@@ -618,6 +618,35 @@ __device__ uint32_t block_radix_kth(const float* row, int n, int kth, uint32_t* 
         kth, hist, list, bcast);
 }
 
+// The same over a row left in global memory (n % 4 == 0, 16-byte aligned): four 16-byte
+// loads of a thread in flight before any of their values is counted.
+__device__ uint32_t block_radix_kth_g4(const float* row, int n, int kth, uint32_t* hist,
+                                       uint32_t* list, int* bcast) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const int n4 = n >> 2;
+    return block_select_kth(
+        [&](auto f) {
+            for (int b = threadIdx.x; b < n4; b += 4 * kSelThreads) {
+                float4 t[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int i = b + j * kSelThreads;
+                    if (i < n4) t[j] = __ldcg(r4 + i);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (b + j * kSelThreads < n4) {
+                        f(total_order_key(t[j].x));
+                        f(total_order_key(t[j].y));
+                        f(total_order_key(t[j].z));
+                        f(total_order_key(t[j].w));
+                    }
+                }
+            }
+        },
+        kth, hist, list, bcast);
+}
+
 // One 256-thread block per query with the approximate row staged in shared memory
 // (nlist small enough); same result as coarse_select_exact_kernel.
 __global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
@@ -689,15 +718,39 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_block_kernel(
     __syncthreads();
     qn = 0.0f;
     for (int i = 0; i < kSelThreads / 32; ++i) qn = __fadd_rn(qn, red[i]);
-    const float tau = key_to_float(block_radix_kth(row, nlist, nprobe, hist, list, bcast));
+    const bool vec_g = !row_in_smem && (nlist & 3) == 0;
+    const float tau = key_to_float(vec_g ? block_radix_kth_g4(row, nlist, nprobe, hist, list, bcast)
+                                         : block_radix_kth(row, nlist, nprobe, hist, list, bcast));
     if (tid == 0) thr_s = coarse_threshold(tau, qn, cmax, d, dot_rel);
     __syncthreads();
     const double thr = thr_s;
-    for (int c = tid; c < nlist; c += kSelThreads) {
-        if ((double)row[c] <= thr) {
+    auto candidate = [&](int c, float v) {
+        if ((double)v <= thr) {
             const int pos = atomicAdd(&cnt_s, 1);
             if (pos < kCoarseCap) cidx[pos] = c;
         }
+    };
+    if (vec_g) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        const int n4 = nlist >> 2;
+        for (int b = tid; b < n4; b += 4 * kSelThreads) {
+            float4 t[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (b + j * kSelThreads < n4) t[j] = __ldcg(r4 + b + j * kSelThreads);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = b + j * kSelThreads;
+                if (i < n4) {
+                    candidate(4 * i, t[j].x);
+                    candidate(4 * i + 1, t[j].y);
+                    candidate(4 * i + 2, t[j].z);
+                    candidate(4 * i + 3, t[j].w);
+                }
+            }
+        }
+    } else {
+        for (int c = tid; c < nlist; c += kSelThreads) candidate(c, row[c]);
     }
     __syncthreads();
     const int cnt = cnt_s;
@@ -2408,27 +2461,46 @@ __global__ void __launch_bounds__(kSelThreads) merge_direct_kernel(MergeArgs a) 
     __syncthreads();
     n_lt = ms.cnt[0];
     uint32_t tau = 0xFFFFFFFFu;
+    // (four keys of a thread loaded before any is counted: the keys may be in global memory)
     if (n_lt >= k)
         tau = block_select_kth(
             [&](auto f) {
-                for (int e = threadIdx.x; e < total; e += kSelThreads) {
-                    const uint32_t kk = keys[e];
-                    if (kk != 0xFFFFFFFFu) f(kk);
+                for (int b = threadIdx.x; b < total; b += 4 * kSelThreads) {
+                    uint32_t t[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int e = b + j * kSelThreads;
+                        t[j] = e < total ? keys[e] : 0xFFFFFFFFu;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (t[j] != 0xFFFFFFFFu) f(t[j]);
                 }
             },
             k, ms.hist, ms.list, ms.bcast);
     // the entries below tau (any order) and the valid ties at tau
-    for (int e = tid; e < total; e += kSelThreads) {
-        const uint32_t kk = keys[e];
-        if (kk < tau) {
-            const int p = atomicAdd(&ms.cnt[1], 1);
-            sk[p] = kk;
-            st[p] = gt[e];
-        } else if (kk == tau) {
-            const uint64_t t = gt[e];
-            if (t != ~0ull) {
-                const int p = atomicAdd(&ms.cnt[2], 1);
-                if (p < kMergeEqCap) ms.eq[p] = t;
+    for (int b = tid; b < total; b += 4 * kSelThreads) {
+        uint32_t t[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = b + j * kSelThreads;
+            t[j] = e < total ? keys[e] : 0xFFFFFFFFu;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = b + j * kSelThreads;
+            if (e >= total) continue;
+            const uint32_t kk = t[j];
+            if (kk < tau) {
+                const int p = atomicAdd(&ms.cnt[1], 1);
+                sk[p] = kk;
+                st[p] = gt[e];
+            } else if (kk == tau) {
+                const uint64_t tt = gt[e];
+                if (tt != ~0ull) {
+                    const int p = atomicAdd(&ms.cnt[2], 1);
+                    if (p < kMergeEqCap) ms.eq[p] = tt;
+                }
             }
         }
     }
