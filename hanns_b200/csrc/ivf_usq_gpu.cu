@@ -737,10 +737,10 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     w_cursor_.reserve(nlist_ + 1);
     w_lq_off_.reserve(nlist_ + 1);
     w_item_off_.reserve(nlist_ + 1);
-    w_counters_.reserve(3);
+    w_counters_.reserve(4);
     w_lq_.reserve((size_t)nb * nprobe);
     w_items_.reserve((size_t)nb * nprobe);
-    HANNS_CUDA_OK(cudaMemsetAsync(w_counters_.p, 0, 3 * sizeof(int), s));
+    HANNS_CUDA_OK(cudaMemsetAsync(w_counters_.p, 0, 4 * sizeof(int), s));
     // lists of at most kTcMaxRows rows take the tensor-core scan; HANNS_GPU_SCAN=simt: none,
     // =hybrid: only lists without FastScan (|list| <= n_cand)
     const int n_cand = (int)n_candidates(nbits_, k);
@@ -919,7 +919,10 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         f.cand_key = w_cand_key_.p;
         f.cand_tie = w_cand_tie_.p;
         f.cand_dbg = a.cand_dbg;
-        launch_fs_select(f, s);
+        f.lq = w_lq_.p;
+        f.n_lq = w_lq_off_.p + nlist_;
+        f.unit_counter = w_counters_.p + 3;
+        launch_fs_select(f, sm_count_ * 4, s);
         launches += 1;
     }
     if (time_it) {
@@ -946,9 +949,9 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         c.out_tie = w_cmp_tie_.p;
         launch_compact_pairs(c, s);
         launches += 1;
-        w_mkey_.reserve((size_t)nb * k);
-        w_mtie_.reserve((size_t)nb * k);
     }
+    w_mkey_.reserve((size_t)nb * k);
+    w_mtie_.reserve((size_t)nb * k);
     MergeArgs m{};
     m.nq = nb;
     m.nprobe = nprobe;

@@ -138,8 +138,13 @@ struct FsSelectArgs {
     uint32_t* cand_key;
     uint64_t* cand_tie;
     int2* cand_dbg;  // nullable
+    // the grouping step's pairs (this rank's, grouped by list) and their number; persistent
+    // warps claim them from unit_counter (zeroed before the launch)
+    const int2* lq;
+    const int* n_lq;
+    int* unit_counter;
 };
-void launch_fs_select(const FsSelectArgs& a, cudaStream_t s);
+void launch_fs_select(const FsSelectArgs& a, int grid, cudaStream_t s);
 
 // USQ rerank of caller-chosen stored rows: out[q * m + j] = distance of row rows[q*m+j]
 // (+inf for rows outside [0, ntotal)).
@@ -255,7 +260,8 @@ int scan_grid_size(int D);
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s);
 void launch_compact_pairs(const CompactArgs& a, cudaStream_t s);
 void launch_merge(const MergeArgs& a, cudaStream_t s);
-// One block per query over the scan's candidate regions (no compaction); k <= kMergeMaxK.
+// Over the scan's candidate regions (no compaction), eight queries per block; k <= kMergeMaxK.
+// sel_key / sel_tie: [nq][k] scratch.
 constexpr int kMergeMaxK = 1024;
 void launch_merge_direct(const MergeArgs& a, cudaStream_t s);
 void launch_merge_shards(const float* dists, const uint64_t* keys, const int64_t* ids, int world,

@@ -1340,62 +1340,67 @@ struct ScanSmem {
 // ============================================================================
 __device__ int warp_select_topk(const uint32_t* keys, const uint64_t* ties, int total, int k,
                                 uint32_t* sk, uint64_t* st, uint32_t* hist) {
+    // Unused entries carry key 0xFFFFFFFF and tie ~0 (the scans' fill and compact padding):
+    // tau is found on the keys alone (four loads of a lane in flight); ties are read for the
+    // entries taken and for those at tau (at tau = 0xFFFFFFFF only valid ties are taken).
     const int lane = (int)lane_id();
-    auto key_at = [&](int e, uint32_t& kk) {
-        if (ties[e] == ~0ull) return false;
-        kk = keys[e];
-        return true;
-    };
-    int n_valid = 0;
-    for (int e = lane; e < total; e += 32) n_valid += ties[e] != ~0ull ? 1 : 0;
-    n_valid = warp_sum(n_valid);
-    const int take = min(k, n_valid);
-    int written = 0;
-    if (take > 0) {
-        int less = 0;
-        uint32_t tau = 0xFFFFFFFFu;
-        if (n_valid > k) tau = warp_radix_kth(total, k, key_at, hist, &less);
-        for (int base = 0; base < total; base += 32) {
-            const int e = base + lane;
-            uint32_t kk = 0;
-            const bool ok = e < total && key_at(e, kk);
-            const bool lt = ok && (n_valid <= k || kk < tau);
-            const unsigned bl = __ballot_sync(0xffffffffu, lt);
-            if (lt) {
-                const int pos = written + __popc(bl & lanemask_lt());
-                sk[pos] = kk;
-                st[pos] = ties[e];
-            }
-            written += __popc(bl);
-        }
-        // ties at tau: chosen in increasing (probe rank, fastscan key, index) order
-        uint64_t floor_t = 0;
-        bool have_floor = false;
-        while (written < take) {
-            uint64_t best = ~0ull;
-            for (int e = lane; e < total; e += 32) {
-                uint32_t kk;
-                if (key_at(e, kk) && kk == tau) {
-                    const uint64_t t = ties[e];
-                    if ((!have_floor || t > floor_t) && t < best) best = t;
-                }
-            }
+    int n_lt = 0;
+    for (int b = lane; b < total; b += 128) {
+        uint32_t t[4];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
-                best = ob < best ? ob : best;
-            }
-            if (lane == 0) {
-                sk[written] = tau;
-                st[written] = best;
-            }
-            floor_t = best;
-            have_floor = true;
-            ++written;
+        for (int j = 0; j < 4; ++j) t[j] = b + 32 * j < total ? keys[b + 32 * j] : 0xFFFFFFFFu;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) n_lt += t[j] != 0xFFFFFFFFu ? 1 : 0;
+    }
+    n_lt = warp_sum(n_lt);
+    uint32_t tau = 0xFFFFFFFFu;
+    if (n_lt >= k) {
+        auto key_at = [&](int e, uint32_t& kk) {
+            kk = keys[e];
+            return kk != 0xFFFFFFFFu;
+        };
+        int less = 0;
+        tau = warp_radix_kth(total, k, key_at, hist, &less);
+    }
+    int written = 0;
+    for (int base = 0; base < total; base += 32) {
+        const int e = base + lane;
+        const uint32_t kk = e < total ? keys[e] : 0xFFFFFFFFu;
+        const bool lt = kk < tau;
+        const unsigned bl = __ballot_sync(0xffffffffu, lt);
+        if (lt) {
+            const int pos = written + __popc(bl & lanemask_lt());
+            sk[pos] = kk;
+            st[pos] = ties[e];
         }
+        written += __popc(bl);
+    }
+    // entries at tau with a valid tie, in increasing (probe rank, fastscan key, index) order
+    uint64_t floor_t = 0;
+    bool have_floor = false;
+    while (written < k) {
+        uint64_t best = ~0ull;
+        for (int e = lane; e < total; e += 32) {
+            if (keys[e] != tau) continue;
+            const uint64_t t = ties[e];
+            if (t != ~0ull && (!have_floor || t > floor_t) && t < best) best = t;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+            best = ob < best ? ob : best;
+        }
+        if (best == ~0ull) break;  // no further valid entry
+        if (lane == 0) {
+            sk[written] = tau;
+            st[written] = best;
+        }
+        floor_t = best;
+        have_floor = true;
+        ++written;
     }
     __syncwarp();
-    return take;
+    return written;
 }
 
 __device__ __forceinline__ int32_t wrap16(int32_t v) { return (int32_t)(int16_t)v; }
@@ -2076,16 +2081,17 @@ __global__ void __launch_bounds__(128) compact_pairs_kernel(CompactArgs a) {
 // Final merge: per query (one warp) top-k over all kept candidates of its probes,
 // ordered by (distance key, probe rank, FastScan key, list position).
 // ============================================================================
-__global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
-    __shared__ uint32_t hist[4][256];
-    const int w = threadIdx.x >> 5, lane = (int)lane_id();
-    const int64_t q = (int64_t)blockIdx.x * 4 + w;
-    if (q >= a.nq) return;
+// One query by one warp (sel_key / sel_tie: its [k] scratch).
+__device__ void merge_query_warp(const MergeArgs& a, int64_t q, uint32_t* hist_w) {
+    const int lane = (int)lane_id();
     const int total = a.fixed_total > 0 ? a.fixed_total : a.pair_off[q * (a.nprobe + 1) + a.nprobe];
     uint32_t* sk = a.sel_key + q * a.k;
     uint64_t* st = a.sel_tie + q * a.k;  // probe rank << 48 | fastscan key << 32 | index
-    const int take = warp_select_topk(a.cand_key + q * a.q_stride, a.cand_tie + q * a.q_stride,
-                                      total, a.k, sk, st, hist[w]);
+    const int take = total <= 32 * 8
+                         ? warp_select_topk_small<8>(a.cand_key + q * a.q_stride, a.cand_tie + q * a.q_stride,
+                                                     total, a.k, sk, st, hist_w)
+                         : warp_select_topk(a.cand_key + q * a.q_stride, a.cand_tie + q * a.q_stride,
+                                            total, a.k, sk, st, hist_w);
     // sort the selected entries by (key, tie) and write the row
     for (int i = lane; i < a.k; i += 32) {
         if (i >= take) {
@@ -2297,16 +2303,12 @@ __device__ void fs_select_regs(const FsSelectArgs& a, int64_t q, int r, int64_t 
     __syncwarp();
 }
 
-__global__ void __launch_bounds__(256, 4) fs_select_kernel(FsSelectArgs a) {
-    __shared__ uint32_t hist[8][256];
-    __shared__ uint32_t kept_rows[8][1024];  // register path: each warp's kept (row, score)
-    const int w = threadIdx.x >> 5, lane = (int)lane_id();
-    const int64_t pr = (int64_t)blockIdx.x * 8 + w;
-    if (pr >= a.nq * a.nprobe) return;
+// One (query, probe) pair of the FastScan selection, by one warp.
+__device__ void fs_select_pair(const FsSelectArgs& a, int64_t q, int r, int lane, uint32_t* hist_w,
+                               uint32_t* kept_w) {
+    const int64_t pr = q * a.nprobe + r;
     const int fo = a.fs_off[pr];
     if (fo < 0) return;
-    const int64_t q = pr / a.nprobe;
-    const int r = (int)(pr - q * a.nprobe);
     const int l = a.probes[pr];
     const int64_t beg = a.list_off[l];
     const int n = (int)(a.list_off[l + 1] - beg);
@@ -2323,9 +2325,9 @@ __global__ void __launch_bounds__(256, 4) fs_select_kernel(FsSelectArgs a) {
     if (!bw && n <= 1024) {
         // unfiltered (every row live, n > n_cand): the pair's scores in registers
         if (n <= 512)
-            fs_select_regs<8>(a, q, r, beg, n, sc, ip, lane, kept_rows[w]);
+            fs_select_regs<8>(a, q, r, beg, n, sc, ip, lane, kept_w);
         else
-            fs_select_regs<16>(a, q, r, beg, n, sc, ip, lane, kept_rows[w]);
+            fs_select_regs<16>(a, q, r, beg, n, sc, ip, lane, kept_w);
         return;
     }
     auto live = [&](int v) { return !bw || !bit_filtered(bw, a.bitset_len, a.ids[beg + v]); };
@@ -2353,7 +2355,7 @@ __global__ void __launch_bounds__(256, 4) fs_select_kernel(FsSelectArgs a) {
             return true;
         };
         int c_gt = 0, c_eq = 0;
-        const uint32_t tau = warp_radix_kth16(n, a.n_cand, key_at, hist[w], &c_gt, &c_eq);
+        const uint32_t tau = warp_radix_kth16(n, a.n_cand, key_at, hist_w, &c_gt, &c_eq);
         // F = first n_cand rows (in list order) with score >= s*; gt_F = rows > s* in F.
         // When exactly n_cand rows score >= s*, F is all of them (no pass needed).
         int cnt_ge = 0, cnt_gt = 0, p_end = n, gt_f = c_gt;
@@ -2413,6 +2415,25 @@ __global__ void __launch_bounds__(256, 4) fs_select_kernel(FsSelectArgs a) {
     }
 }
 
+// Persistent warps over the grouping step's pairs (this rank's, grouped by list), eight
+// pairs per claim.
+__global__ void __launch_bounds__(256, 4) fs_select_kernel(FsSelectArgs a) {
+    __shared__ uint32_t hist[8][256];
+    __shared__ uint32_t kept_rows[8][1024];  // register path: each warp's kept (row, score)
+    const int w = threadIdx.x >> 5, lane = (int)lane_id();
+    const int total = *a.n_lq;
+    for (;;) {
+        int u0 = 0;
+        if (lane == 0) u0 = atomicAdd(a.unit_counter, 8);
+        u0 = __shfl_sync(0xffffffffu, u0, 0);
+        if (u0 >= total) return;
+        for (int u = u0; u < min(u0 + 8, total); ++u) {
+            const int2 pr = a.lq[u];
+            fs_select_pair(a, pr.x, pr.y, lane, hist[w], kept_rows[w]);
+        }
+    }
+}
+
 // ============================================================================
 // Final merge, one 256-thread block per query (k <= kMergeMaxK): the top k of all kept
 // candidates of the query's probes by (distance key, tie = probe rank << 48 | FastScan key
@@ -2434,11 +2455,9 @@ struct MergeSmem {
     uint64_t eq[kMergeEqCap];
 };
 
-__global__ void __launch_bounds__(kSelThreads) merge_direct_kernel(MergeArgs a) {
-    __shared__ MergeSmem ms;
-    extern __shared__ __align__(16) uint8_t mdyn[];  // sel ties [k], sel keys [k], keys [cap]
+// One query by the whole block (mdyn: sel ties [k], sel keys [k], keys [kMergeKeyCap]).
+__device__ void merge_query_block(const MergeArgs& a, int64_t q, MergeSmem& ms, uint8_t* mdyn) {
     const int tid = threadIdx.x, lane = tid & 31;
-    const int64_t q = blockIdx.x;
     const int k = a.k;
     uint64_t* st = reinterpret_cast<uint64_t*>(mdyn);
     uint32_t* sk = reinterpret_cast<uint32_t*>(st + k);
@@ -2574,8 +2593,7 @@ __global__ void __launch_bounds__(kSelThreads) merge_direct_kernel(MergeArgs a) 
         if (a.shard_mode) a.out_keys[q * k + rank] = ti;
     }
     __syncthreads();
-    if (threadIdx.x >= 32) return;
-    if (a.post_bitsets) {  // reference post-filter: drop filtered ids, keep order
+    if (threadIdx.x < 32 && a.post_bitsets) {  // reference post-filter: drop filtered ids, keep order
         const uint64_t* bw = nullptr;
         const int b = a.query_bitset ? a.query_bitset[q] : 0;
         if (b >= 0 && b < a.n_bitsets) bw = a.post_bitsets + (int64_t)b * a.bitset_words;
@@ -2605,9 +2623,42 @@ __global__ void __launch_bounds__(kSelThreads) merge_direct_kernel(MergeArgs a) 
             a.out_dists[q * k + i] = __int_as_float(0x7f800000);
         }
         if (lane == 0 && a.out_counts) a.out_counts[q] = n_out;
-    } else if (lane == 0 && a.out_counts) {
+    } else if (threadIdx.x == 0 && a.out_counts) {
         a.out_counts[q] = k;
     }
+    __syncthreads();  // (the next query reuses the shared memory)
+}
+
+// Eight queries per block: each by a warp when every one has at most kMergeWarpMax
+// candidates (many small regions, e.g. a list shard's), else one after another by the
+// whole block.
+constexpr int kMergeWarpMax = 2048;
+__global__ void __launch_bounds__(kSelThreads) merge_direct_kernel(MergeArgs a) {
+    __shared__ MergeSmem ms;
+    __shared__ int small_s;
+    extern __shared__ __align__(16) uint8_t mdyn[];
+    const int64_t q0 = (int64_t)blockIdx.x * 8;
+    const int nq_b = (int)(a.nq - q0 < 8 ? a.nq - q0 : 8);
+    if (threadIdx.x == 0) {
+        int mx = 0;
+        for (int i = 0; i < nq_b; ++i) mx = max(mx, a.pair_off[(q0 + i) * (a.nprobe + 1) + a.nprobe]);
+        small_s = mx <= kMergeWarpMax ? 1 : 0;
+    }
+    __syncthreads();
+    if (small_s) {
+        const int w = threadIdx.x >> 5;
+        if (w < nq_b) merge_query_warp(a, q0 + w, ms.hist + 256 * w);
+        return;
+    }
+    for (int i = 0; i < nq_b; ++i) merge_query_block(a, q0 + i, ms, mdyn);
+}
+
+__global__ void __launch_bounds__(128) merge_kernel(MergeArgs a) {
+    __shared__ uint32_t hist[4][256];
+    const int w = threadIdx.x >> 5;
+    const int64_t q = (int64_t)blockIdx.x * 4 + w;
+    if (q >= a.nq) return;
+    merge_query_warp(a, q, hist[w]);
 }
 
 }  // namespace hanns
@@ -2828,16 +2879,15 @@ void launch_merge(const MergeArgs& a, cudaStream_t s) {
     merge_kernel<<<(unsigned)((a.nq + 3) / 4), 128, 0, s>>>(a);
 }
 
-void launch_fs_select(const FsSelectArgs& a, cudaStream_t s) {
-    const int64_t pairs = a.nq * a.nprobe;
-    if (pairs > 0) fs_select_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(a);
+void launch_fs_select(const FsSelectArgs& a, int grid, cudaStream_t s) {
+    if (a.nq * a.nprobe > 0) fs_select_kernel<<<grid, 256, 0, s>>>(a);
 }
 
 void launch_merge_direct(const MergeArgs& a, cudaStream_t s) {
     if (a.nq <= 0) return;
     const size_t smem = (size_t)a.k * 12 + (size_t)kMergeKeyCap * 4;
     HANNS_CUDA_OK(cudaFuncSetAttribute(merge_direct_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    merge_direct_kernel<<<(unsigned)a.nq, kSelThreads, smem, s>>>(a);
+    merge_direct_kernel<<<(unsigned)((a.nq + 7) / 8), kSelThreads, smem, s>>>(a);
 }
 
 void launch_merge_shards(const float* dists, const uint64_t* keys, const int64_t* ids, int world,
