@@ -761,6 +761,10 @@ def main():
     ap.add_argument("--no-recall", action="store_true", help="skip exact ground truth (frees the base early)")
     ap.add_argument("--prepare-artifact", action="store_true",
                     help="build and cache the workload's frozen index, then exit")
+    ap.add_argument("--scale", type=int, default=1,
+                    help="divide the workload's rows, lists and queries by this factor (list sizes "
+                         "and queries per list unchanged): the small case of the same kernels for "
+                         "ncu captures; not a bench line")
     ap.add_argument("--split", action="store_true",
                     help="N > 1: one batch split over the ranks (strong scaling) instead of one "
                          "batch per rank (weak scaling)")
@@ -768,7 +772,12 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.scale > 1:
+        for key in ("n", "nlist", "nq"):
+            w[key] //= args.scale
+        args.workload = f"{args.workload}_scale{args.scale}"
+        WORKLOADS[args.workload] = w
     if args.prepare_artifact:
         base, _ = make_data(w, "cuda")
         get_artifact(args.workload, w, base, 0, cache=True)
