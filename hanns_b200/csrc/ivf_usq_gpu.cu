@@ -921,7 +921,6 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         f.cand_dbg = a.cand_dbg;
         f.lq = w_lq_.p;
         f.n_lq = w_lq_off_.p + nlist_;
-        f.unit_counter = w_counters_.p + 3;
         launch_fs_select(f, sm_count_ * 4, s);
         launches += 1;
     }

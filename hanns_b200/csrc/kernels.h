@@ -138,11 +138,9 @@ struct FsSelectArgs {
     uint32_t* cand_key;
     uint64_t* cand_tie;
     int2* cand_dbg;  // nullable
-    // the grouping step's pairs (this rank's, grouped by list) and their number; persistent
-    // warps claim them from unit_counter (zeroed before the launch)
+    // the grouping step's pairs (this rank's, grouped by list) and their number
     const int2* lq;
     const int* n_lq;
-    int* unit_counter;
 };
 void launch_fs_select(const FsSelectArgs& a, int grid, cudaStream_t s);
 

@@ -2415,22 +2415,17 @@ __device__ void fs_select_pair(const FsSelectArgs& a, int64_t q, int r, int lane
     }
 }
 
-// Persistent warps over the grouping step's pairs (this rank's, grouped by list), eight
-// pairs per claim.
+// Persistent warps over the grouping step's pairs (this rank's, grouped by list), round
+// robin: the pairs of one list (same cost) go to different warps.
 __global__ void __launch_bounds__(256, 4) fs_select_kernel(FsSelectArgs a) {
     __shared__ uint32_t hist[8][256];
     __shared__ uint32_t kept_rows[8][1024];  // register path: each warp's kept (row, score)
     const int w = threadIdx.x >> 5, lane = (int)lane_id();
     const int total = *a.n_lq;
-    for (;;) {
-        int u0 = 0;
-        if (lane == 0) u0 = atomicAdd(a.unit_counter, 8);
-        u0 = __shfl_sync(0xffffffffu, u0, 0);
-        if (u0 >= total) return;
-        for (int u = u0; u < min(u0 + 8, total); ++u) {
-            const int2 pr = a.lq[u];
-            fs_select_pair(a, pr.x, pr.y, lane, hist[w], kept_rows[w]);
-        }
+    const int n_warps = gridDim.x * 8;
+    for (int u = blockIdx.x * 8 + w; u < total; u += n_warps) {
+        const int2 pr = a.lq[u];
+        fs_select_pair(a, pr.x, pr.y, lane, hist[w], kept_rows[w]);
     }
 }
 
