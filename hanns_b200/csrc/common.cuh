@@ -46,7 +46,8 @@ struct QueryParams {
     float q_norm_sq;       // ||q||^2 of the raw query
     float lut_scale;
     int32_t q_i8_sum;
-    int32_t pad[3];
+    float q_sum;           // sum of q_rot in dimension order from -0.0 (1-bit rerank)
+    int32_t pad[2];
 };
 
 // score_with_meta + distance, in the reference's operation order
@@ -70,6 +71,59 @@ __device__ __forceinline__ float rerank_distance(int iip, float4 m, const QueryP
         score = __fadd_rn(p.centroid_score, __fdiv_rn(__fmul_rn(m.x, ip), m.w));
     }
     return l2 ? __fsub_rn(__fadd_rn(p.q_norm_sq, m.y), __fmul_rn(2.0f, score)) : -score;
+}
+
+// The same distance from an f32 inner product (the reference's non-VNNI paths).
+__device__ __forceinline__ float rerank_distance_ip(float ip, float4 m, const QueryParams& p, bool l2) {
+    const float score = m.w <= 1e-12f ? p.centroid_score : __fadd_rn(p.centroid_score, __fdiv_rn(__fmul_rn(m.x, ip), m.w));
+    return l2 ? __fsub_rn(__fadd_rn(p.q_norm_sq, m.y), __fmul_rn(2.0f, score)) : -score;
+}
+
+// compute_ip_scalar (quantizer.rs, nbits other than 1, 4, 8): codes from the LSB-first bit
+// stream (packed.rs), each decoded as raw * scale + offset, summed in dimension order from
+// +0.0, unfused.
+__device__ inline float ip_scalar(const uint8_t* packed, const float* q_rot, int D, int nbits, float vmax,
+                                  int code_bytes) {
+    const float scale = __fdiv_rn(__fmul_rn(2.0f, vmax), fmaxf((float)(1u << nbits), 1.0f));
+    const float offset = -vmax;
+    const uint32_t mask = (1u << nbits) - 1u;
+    uint32_t buf = 0;
+    int bits = 0, byte_idx = 0;
+    float ip = 0.0f;
+    for (int i = 0; i < D; ++i) {
+        while (bits < nbits) {
+            const uint32_t next = byte_idx < code_bytes ? (uint32_t)packed[byte_idx] : 0u;
+            buf |= next << bits;
+            bits += 8;
+            ++byte_idx;
+        }
+        const uint32_t raw = buf & mask;
+        buf >>= nbits;
+        bits -= nbits;
+        const float decoded = __fadd_rn(__fmul_rn((float)raw, scale), offset);
+        ip = __fadd_rn(ip, __fmul_rn(q_rot[i], decoded));
+    }
+    return ip;
+}
+
+// compute_ip_1bit (quantizer.rs, AVX-512 path): 16 lanes of the selected q_rot values over
+// 16-dimension chunks, the halving tree of _mm512_reduce_add_ps, then vmax * (sum - q_sum).
+__device__ inline float ip_1bit(const uint8_t* packed, const float* q_rot, int D, float vmax, float q_sum) {
+    float lanes[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) lanes[j] = 0.0f;
+    for (int c = 0; c < D / 16; ++c) {
+        const uint32_t m = (uint32_t)packed[2 * c] | ((uint32_t)packed[2 * c + 1] << 8);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) lanes[j] = __fadd_rn(lanes[j], ((m >> j) & 1u) ? q_rot[c * 16 + j] : 0.0f);
+    }
+    float s8[8], s4[4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s8[i] = __fadd_rn(lanes[i], lanes[i + 8]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s4[i] = __fadd_rn(s8[i], s8[i + 4]);
+    const float fs = __fadd_rn(__fadd_rn(s4[0], s4[2]), __fadd_rn(s4[1], s4[3]));
+    return __fmul_rn(vmax, __fsub_rn(fs, q_sum));
 }
 
 // Packed two-lane fp32 arithmetic of sm_100 (add/sub/mul/fma .rn.f32x2): each lane is

@@ -83,6 +83,7 @@ int64_t IvfUsqGpu::cand_stride(int nprobe, int k) const {
 }
 
 int IvfUsqGpu::scan_tc_rows(int n_cand) const {
+    if (nbits_ != 4 && nbits_ != 8) return 0;  // (the f32 reranks run on the SIMT scan)
     const char* mode = std::getenv("HANNS_GPU_SCAN");
     if (mode && std::strcmp(mode, "simt") == 0) return 0;
     if (mode && std::strcmp(mode, "hybrid") == 0) return std::min(kTcMaxRows, n_cand);
@@ -179,8 +180,14 @@ void IvfUsqGpu::ensure_stream() {
 }
 
 void IvfUsqGpu::check_supported() const {
+    if (nbits_ < 1 || nbits_ > 8) throw std::domain_error("IVF-USQ codes of 1 to 8 bits only");
+}
+
+void IvfUsqGpu::check_int_rerank(const char* what) const {
+    check_supported();
     if (nbits_ != 4 && nbits_ != 8)
-        throw std::domain_error("this build searches 4-bit and 8-bit IVF-USQ codes only");
+        throw std::domain_error(std::string(what) + ": 4-bit and 8-bit codes only in this build "
+                                "(other widths: single-GPU search)");
 }
 
 int64_t IvfUsqGpu::size_bytes() const {
@@ -475,7 +482,7 @@ void IvfUsqGpu::train(const float* h_data, int64_t n, int kmeans_iters, uint64_t
 void IvfUsqGpu::add(const float* h_data, int64_t n, const int64_t* h_ids) {
     DeviceGuard g(device_);
     if (!trained_) throw std::invalid_argument("index not trained, call train() first");
-    check_supported();
+    check_int_rerank("GPU encoder");
     if (n <= 0) return;
     const int64_t chunk = 65536;
     DevBuf<float> x, res, nsq;
@@ -802,6 +809,7 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     a.cand_key = w_cand_key_.p;
     a.cand_tie = w_cand_tie_.p;
     a.scores = w_scores_.p;
+    a.q_rot = w_qrot_.p;  // (this batch's rotated queries, from prepare_batch)
     a.max_len = (int)per_warp;
     if (debug_candidates_) {
         w_cand_dbg_.reserve((size_t)nb * q_stride);
@@ -1145,7 +1153,7 @@ void IvfUsqGpu::rerank_rows_device(const float* d_queries, int64_t nq, const int
                                    int m, float* d_dists, cudaStream_t stream) {
     DeviceGuard g(device_);
     if (!trained_) throw std::invalid_argument("index not trained");
-    check_supported();
+    check_int_rerank("rerank_rows");
     if (nq <= 0 || m <= 0) throw std::invalid_argument("empty rerank request");
     cudaStream_t s = stream ? stream : stream_;
     const int G = D_ / 4;
@@ -1181,7 +1189,7 @@ void IvfUsqGpu::prepare_device(const float* d_queries, int64_t nq, int nprobe, Q
                                cudaStream_t stream) {
     DeviceGuard g(device_);
     if (!trained_) throw std::invalid_argument("index not trained");
-    check_supported();
+    check_int_rerank("prepared (sharded) search");
     if (nq <= 0) throw std::invalid_argument("query dimension mismatch");
     if (!st.probes || !st.qp || !st.lut || !st.q_i8p) throw std::invalid_argument("null query state");
     cudaStream_t s = stream ? stream : stream_;
@@ -1203,7 +1211,7 @@ void IvfUsqGpu::search_prepared_device(int64_t nq, const SearchOptions& opt, Que
                                        uint64_t* d_keys, cudaStream_t stream) {
     DeviceGuard g(device_);
     if (!trained_) throw std::invalid_argument("index not trained");
-    check_supported();
+    check_int_rerank("prepared (sharded) search");
     if (nq <= 0) throw std::invalid_argument("query dimension mismatch");
     if (!st.probes || !st.qp || !st.lut || !st.q_i8p) throw std::invalid_argument("null query state");
     cudaStream_t s = stream ? stream : stream_;

@@ -159,6 +159,7 @@ class IvfUsqGpu {
 
    private:
     void check_supported() const;
+    void check_int_rerank(const char* what) const;  // 4-bit / 8-bit only
     void upload_rotation_centroid();
     void rebuild_fastscan();
     void ensure_stream();

@@ -55,6 +55,7 @@ struct ScanArgs {
     int2* cand_dbg;
     // FastScan scores scratch: per CTA, kScanWarps rows of max_len (the longest list)
     int16_t* scores;
+    const float* q_rot;  // [nq][D]: the f32 rerank of nbits other than 4 and 8
     int max_len;
 };
 

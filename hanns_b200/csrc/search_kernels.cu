@@ -1115,13 +1115,16 @@ __global__ void __launch_bounds__(128) query_state_kernel(
     __syncthreads();
     if (!valid) return;
     // sequential sums (Rust Sum<f32> starts from -0.0), from shared memory
-    float cs = -0.0f, qn = -0.0f;
+    float cs = -0.0f, qn = -0.0f, qsum = -0.0f;
     if (lane == 1)
         for (int i = 0; i < D; ++i) cs = __fadd_rn(cs, __fmul_rn(r[i], rc_s[i]));
     if (lane == 2)
         for (int i = 0; i < d; ++i) qn = __fadd_rn(qn, __fmul_rn(xq[i], xq[i]));
+    if (lane == 3)
+        for (int i = 0; i < D; ++i) qsum = __fadd_rn(qsum, r[i]);
     cs = __shfl_sync(0xffffffffu, cs, 1);
     qn = __shfl_sync(0xffffffffu, qn, 2);
+    qsum = __shfl_sync(0xffffffffu, qsum, 3);
     float m = 0.0f;
     for (int i = lane; i < D; i += 32) m = fmaxf(m, fabsf(r[i]));
     m = fmaxf(warp_max(m), 1e-6f);
@@ -1166,7 +1169,8 @@ __global__ void __launch_bounds__(128) query_state_kernel(
         p.q_norm_sq = qn;
         p.lut_scale = lut_scale;
         p.q_i8_sum = s;
-        p.pad[0] = p.pad[1] = p.pad[2] = 0;
+        p.q_sum = qsum;
+        p.pad[0] = p.pad[1] = 0;
         qp[qi] = p;
     }
 }
@@ -1872,7 +1876,28 @@ __global__ void __launch_bounds__(kScanThreads, 4) scan_lists_kernel(ScanArgs a)
             // each finish one of the 8 (distance, key store) in parallel
             const int wpq = kScanWarps / nq_here;  // 1 for a full group: iq == w
             const int iq = w / wpq, part = w - iq * wpq;
-            if (iq < nq_here) {
+            if (iq < nq_here && a.nbits != 4 && a.nbits != 8) {
+                // f32 rerank (1-bit chains, or the scalar dequantised sum): a lane per kept
+                // candidate; the query's q_rot values are the same address in every lane
+                const int nc_i = sm.nc[iq];
+                const uint16_t* svi = sm.sv[iq];
+                const int64_t rb = sm.qbase[qg + iq];
+                const QueryParams& qpi = sm.qp[qg + iq];
+                const float* qr = a.q_rot + (int64_t)sm.q[qg + iq] * a.D;
+                for (int j0 = part * 32; j0 < nc_i; j0 += wpq * 32) {
+                    const int j = j0 + lane;
+                    if (j >= nc_i) continue;
+                    const uint32_t v = use_sv ? (uint32_t)svi[j] : (uint32_t)a.cand_tie[rb + j];
+                    const float4 m = __ldg(a.meta + beg + v);
+                    const uint8_t* cr = a.codes + (beg + v) * a.code_bytes;
+                    float ip = 0.0f;
+                    if (m.w > 1e-12f)
+                        ip = a.nbits == 1 ? ip_1bit(cr, qr, a.D, m.z, qpi.q_sum)
+                                          : ip_scalar(cr, qr, a.D, a.nbits, m.z, a.code_bytes);
+                    a.cand_key[rb + j] = total_order_key(rerank_distance_ip(ip, m, qpi, l2));
+                    if (a.cand_dbg) a.cand_dbg[rb + j].x = INT32_MIN;
+                }
+            } else if (iq < nq_here) {
                 const int nc_i = sm.nc[iq];
                 const uint8_t* qrow = qsm + iq * qld;
                 const uint16_t* svi = sm.sv[iq];

@@ -508,3 +508,31 @@ def test_config_3072_dims_8bit(gpu, oracle_mod):
     r = idx.search(q, SearchRequest(top_k=10, nprobe=8))
     assert np.array_equal(r.ids.reshape(e_ids.shape), e_ids)
     assert bits_eq(r.distances.reshape(e_ids.shape), e_d)
+
+
+@pytest.mark.parametrize("nbits,metric", [(1, 0), (2, 1), (3, 0), (6, 1), (7, 0)])
+def test_search_bit_exact_other_widths(gpu, oracle_mod, nbits, metric):
+    """Code widths other than 4 and 8 (single-GPU search): FastScan and the kept sets as for
+    every width, then the reference's f32 reranks on the SIMT scan -- the 1-bit sixteen
+    chains and tree, the scalar dequantised sum in dimension order for the others.  Ids,
+    distance bits and every kept candidate equal the oracle's."""
+    from hanns_b200.ivf_usq import IvfUsqIndex, SearchRequest
+    from tests.golden.make_golden import mixture
+    O = oracle_mod
+    rng = np.random.default_rng(600 + nbits)
+    x, _ = mixture(rng, 3000, 96, 8, 0.4, metric == 1)
+    q, _ = mixture(rng, 40, 96, 8, 0.4, metric == 1)
+    art = O.build_artifact(x, 6, nbits, metric, rotation_seed=4, kmeans_iters=4, kmeans_seed=1)
+    assert (np.diff(art["list_offsets"]) > O.n_candidates(nbits, 10)).any()  # FastScan runs
+    idx = IvfUsqIndex.from_artifact(art)
+    oi = O.OracleIndex(art)
+    e_ids, e_d, _ = oi.search(q, 10, 3)
+    r = idx.search(q, SearchRequest(top_k=10, nprobe=3))
+    assert np.array_equal(r.ids.reshape(e_ids.shape), e_ids)
+    assert bits_eq(r.distances.reshape(e_ids.shape), e_d)
+    got = idx.debug_candidates(q[:8], 10, 3)
+    for i in range(8):
+        exp = oi.candidates(q[i], 10, 3)
+        for key in ("list", "local", "fs", "int_ip"):
+            assert np.array_equal(got[i][key], exp[key]), (i, key)
+        assert np.array_equal(got[i]["dist"].view(np.uint32), exp["dist"].view(np.uint32)), i
