@@ -27,25 +27,25 @@
 // row: its epilogue writes each kept row's distance key and tie key (rank << 48 | position)
 // to the query's candidate region.
 //
-// Operands stream through two rings of 16 KiB stages (128 rows x 128 K bytes, 128-byte
-// swizzle, K-major): A (kNA slots, the row tiles) and B (kNB slots, the queries).  Per
+// Operands stream through two rings of 32 KiB stages (128 rows x 256 K bytes: two 128-byte
+// swizzle atoms, K-major): A (kNA slots, the row tiles) and B (kNB slots, the queries).  Per
 // GEMM and K slab the MMA consumes one B stage and then the T A stages.  Each ring slot
 // has one builder warp, which fills the slot's positions in ring order, so every wait of
 // a builder on its slot's empty barrier is for the phase right after the last one it saw.
 //
-// Warp roles (18 warps; five of them share an SM sub-partition, hence at most 96
-// registers a thread):
-//   warps 0-5   A builders: one-hot rows (sign words loaded into registers before the slot
-//               is free, then expanded), 4-bit codes (loaded the same way, unpacked),
-//               8-bit codes (cp.async straight into their swizzled places)
-//   warps 6-7   B builders: the queries' LUT or q_i8p slab rows, cp.async
+// Warp roles (16 warps, four per SM sub-partition):
+//   warps 0-3   A builders.  One-hot rows (sign bytes loaded into registers before the slot
+//               is free, then expanded), 4-bit codes (the first of four rounds loaded, the
+//               rest prefetched into L1, unpacked), 8-bit codes (cp.async straight into
+//               their swizzled places)
+//   warps 4-5   B builders: the queries' LUT or q_i8p slab rows, cp.async
 //               Copies complete on the slot's full barrier (cp.async.mbarrier.arrive): a
-//               builder never waits for its loads.
-//   warps 8-15  epilogue (thread per row): FastScan items' scores and int_ip TMEM -> the
+//               builder never waits for them.
+//   warps 6-13  epilogue (thread per row): FastScan items' scores and int_ip TMEM -> the
 //               FastScan scratch; rerank-only items' kept rows (bitmaps) and their
 //               distances and ties
-//   warp 16     TMEM allocation and the single-thread MMA issuer
-//   warp 17     item scheduler: takes items, fills the item slots, prefetches the next
+//   warp 14     TMEM allocation and the single-thread MMA issuer
+//   warp 15     item scheduler: takes items, fills the item slots, prefetches the next
 //               item's list into L2
 // Every wait is bounded (wait_ns, 2 s by default): on expiry the kernel records an error
 // code, every role leaves its loop, the MMAs already issued complete, and the TMEM is
@@ -58,18 +58,20 @@
 namespace hanns {
 namespace {
 
-constexpr int kNA = 6, kNB = 2;                   // ring slots, one builder warp each
-constexpr int kBuildWarps = kNA + kNB;            // warps 0-5 A, 6-7 B
-constexpr int kEpiWarps = 8;                      // warps 8-15
-constexpr int kMmaWarp = kBuildWarps + kEpiWarps;  // 16
-constexpr int kSchedWarp = kMmaWarp + 1;          // 17
-constexpr int kThreads = (kSchedWarp + 1) * 32;   // 576
+constexpr int kNA = 4, kNB = 2;                   // ring slots, one builder warp each
+constexpr int kBuildWarps = kNA + kNB;            // warps 0-3 A, 4-5 B
+constexpr int kEpiWarps = 8;                      // warps 6-13
+constexpr int kMmaWarp = kBuildWarps + kEpiWarps;  // 14
+constexpr int kSchedWarp = kMmaWarp + 1;          // 15
+constexpr int kThreads = (kSchedWarp + 1) * 32;   // 512
 constexpr int kRows = 128;                        // MMA M: list rows per tile
 constexpr int kMaxQ = 128;                        // queries per item
 constexpr int kHalfCols = 256;                    // TMEM columns of one GEMM
 constexpr int kTmemCols = 2 * kHalfCols;
-constexpr int kSlab = 128;                        // K bytes per stage (one swizzle atom)
-constexpr int kStageBytes = kRows * kSlab;        // 16 KiB
+constexpr int kAtom = 128;                        // K bytes of one 128-byte swizzle atom
+constexpr int kAtomBytes = kRows * kAtom;         // 16 KiB: 128 rows of one atom
+constexpr int kSlab = 2 * kAtom;                  // K bytes per stage (two atoms)
+constexpr int kStageBytes = 2 * kAtomBytes;       // 32 KiB
 constexpr int kWordCap = kTcItemCols * 4;         // kept-row bitmap words: N * T * 4
 constexpr int kSlots = 2;                         // items in flight
 constexpr uint32_t kWaitLimit = 1u << 24;
@@ -160,9 +162,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// The descriptor of saddr + 32 k bytes (a K step of 32 bytes inside the swizzle atom):
-// the start address field counts 16-byte units.
-__device__ __forceinline__ uint64_t desc_k(uint64_t d, int k4) { return d + (uint64_t)(2 * k4); }
+// The descriptor of K step k4 (32 bytes) of a stage whose descriptor is d: atom k4 / 4
+// (kAtomBytes further), 32 (k4 % 4) bytes into it; the start address field counts
+// 16-byte units.
+__device__ __forceinline__ uint64_t desc_k(uint64_t d, int k4) {
+    return d + (uint64_t)((k4 >> 2) * (kAtomBytes >> 4) + 2 * (k4 & 3));
+}
 
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                         uint32_t idesc, uint32_t accumulate) {
@@ -205,9 +210,10 @@ __device__ __forceinline__ bool epi_sync_or(bool v) {
     return r != 0;
 }
 
-// Byte offset of the 16-byte chunk c (0..7) of row r inside one 128-byte-swizzled slab.
+// Byte offset of the 16-byte K chunk c (0..15) of row r inside a stage: chunks 0-7 in the
+// first 128-byte-swizzled atom (128 rows x 128 bytes), chunks 8-15 in the second.
 __device__ __forceinline__ uint32_t sw_off(int r, int c) {
-    return (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
+    return (uint32_t)(c >> 3) * (uint32_t)kAtomBytes + (uint32_t)r * 128u + ((uint32_t)((c & 7) ^ (r & 7)) << 4);
 }
 
 __device__ __forceinline__ bool filtered(const uint64_t* words, int64_t len, int64_t id) {
@@ -253,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     TcSmem& sm = *reinterpret_cast<TcSmem*>(ring_b + kNB * kStageBytes);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool l2 = a.metric_l2 != 0;
-    const int fs_slabs = a.D / 32;                   // K = 16 G = 4 D bytes
+    const int fs_slabs = a.D / 64;                   // K = 16 G = 4 D bytes
     const int rr_slabs = (a.D + kSlab - 1) / kSlab;  // K = D bytes
 
     if (tid == 0) {
@@ -346,33 +352,40 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     s = fsp ? sl : sl - fss;
                 }
                 // the A stage's raw words, loaded before the slot is free
-                uint32_t wv[4] = {0u, 0u, 0u, 0u};  // one-hot: the sign word of rows lane + 32 k
-                uint4 c4[8];                       // 4-bit codes: the first half of the slab's raw bytes
-                const int nj = min(4, (a.D - s * kSlab) / 32);  // 32-dimension quarters of the slab
+                uint2 wv[4];  // one-hot: the 8 sign bytes (64 dimensions) of rows lane + 32 k
+                uint4 c4[8];  // 4-bit codes: the first of four rounds of the slab's raw bytes
+                const int nj = min(8, (a.D - s * kSlab) / 32);  // 32-dimension quarters of the slab
+                // 4-bit raw quarter of round rd, step m (rows r = 32 rd + 8 (m / 2) + lane / 4;
+                // quarter jj = lane % 4 + 4 (m % 2)): its address and whether it exists
+                auto q4src = [&](int rd, int m, bool& has) {
+                    const int r = 32 * rd + 8 * (m >> 1) + (lane >> 2), jj = (lane & 3) + 4 * (m & 1);
+                    const int v = t * kRows + r;
+                    has = v < n && jj < nj;
+                    return a.codes + (beg + v) * (int64_t)a.code_bytes + s * (kSlab / 2) + 16 * jj;
+                };
                 if (!is_b && fsp) {
-                    // sign word of row v for slab s: 4 bytes of the row's 8-byte chunk s / 2
+                    // sign bytes of row v for slab s (64 dimensions): the row's 8-byte chunk s
                     // (layout [block of 32 rows][chunk][row in block])
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         const int v = t * kRows + 32 * k + lane;
-                        if (v < n)
-                            wv[k] = __ldg(reinterpret_cast<const uint32_t*>(
-                                fsl + ((((int64_t)(t * 4 + k) * a.nchunks + (s >> 1)) * 32 + lane) * 8 + 4 * (s & 1))));
+                        wv[k] = v < n ? __ldg(reinterpret_cast<const uint2*>(
+                                            fsl + ((((int64_t)(t * 4 + k) * a.nchunks + s) * 32 + lane) * 8)))
+                                      : make_uint2(0u, 0u);
                     }
                 } else if (!is_b && a.nbits == 4) {
-                    // rows r = 8 m + lane / 4 (m < 16), 16-byte quarter jj = lane % 4: the first
-                    // 64 rows into registers, the other 64 into L1 (loaded after the first
-                    // half's stores)
+                    // round 0 into registers, rounds 1-3 into L1 (loaded after the stores before)
 #pragma unroll
-                    for (int m = 0; m < 16; ++m) {
-                        const int r = 8 * m + (lane >> 2), jj = lane & 3, v = t * kRows + r;
-                        const uint8_t* src = a.codes + (beg + v) * (int64_t)a.code_bytes + s * (kSlab / 2) + 16 * jj;
-                        if (m < 8)
-                            c4[m] = (v < n && jj < nj) ? __ldg(reinterpret_cast<const uint4*>(src))
-                                                       : make_uint4(0u, 0u, 0u, 0u);
-                        else if (v < n && jj < nj)
-                            asm volatile("prefetch.global.L1 [%0];" ::"l"(src));
-                    }
+                    for (int rd = 0; rd < 4; ++rd)
+#pragma unroll
+                        for (int m = 0; m < 8; ++m) {
+                            bool has;
+                            const uint8_t* src = q4src(rd, m, has);
+                            if (rd == 0)
+                                c4[m] = has ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
+                            else if (has)
+                                asm volatile("prefetch.global.L1 [%0];" ::"l"(src));
+                        }
                 }
                 const uint64_t t_w = prof ? global_ns() : 0;
                 const bool freed = use == 0 || mbar_wait(empty, (use - 1) & 1, &sm.abort, wl);
@@ -383,8 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
                 if (is_b) {
                     // queries' LUT (FastScan) or q_i8p (rerank) slab: chunk c of query i
-                    for (int e = lane; e < N * 8; e += 32) {
-                        const int i = e >> 3, c = e & 7;
+                    for (int e = lane; e < N * 16; e += 32) {
+                        const int i = e >> 4, c = e & 15;
                         if (i >= nq) break;  // padding queries: their columns are never read
                         const int64_t q = S.q[i];
                         if (fsp)
@@ -399,40 +412,38 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                         const int r = 32 * k + lane;
                         if (t * kRows + r < n) {
 #pragma unroll
-                            for (int c = 0; c < 8; ++c)
-                                *reinterpret_cast<uint4*>(X + sw_off(r, c)) = onehot16((wv[k] >> (4 * c)) & 15u);
+                            for (int c = 0; c < 16; ++c)
+                                *reinterpret_cast<uint4*>(X + sw_off(r, c)) =
+                                    onehot16(((c < 8 ? wv[k].x : wv[k].y) >> (4 * (c & 7))) & 15u);
                         }
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mbar_arrive(full);
                 } else if (a.nbits == 8) {
                     // 8-bit codes are the operand: straight into their swizzled places
-                    for (int e = lane; e < kRows * 8; e += 32) {
-                        const int r = e >> 3, c = e & 7;
+                    for (int e = lane; e < kRows * 16; e += 32) {
+                        const int r = e >> 4, c = e & 15;
                         const int v = t * kRows + r, d = s * kSlab + c * 16;
                         if (v < n && d < a.D)
                             cp_async16(xs + sw_off(r, c), a.codes + (beg + v) * (int64_t)a.code_bytes + d);
                     }
                     cp_async_arrive(full);
                 } else {
-                    // 4-bit codes: a 16-byte quarter (32 dimensions, 4 code words of 8) becomes
+                    // 4-bit codes: a 16-byte quarter jj (32 dimensions, 4 code words of 8) becomes
                     // chunks 2 jj and 2 jj + 1: per word its low nibbles, then its high ones
-                    const int jj = lane & 3;
 #pragma unroll 1
-                    for (int half = 0; half < 2; ++half) {
-                        if (half == 1) {
+                    for (int rd = 0; rd < 4; ++rd) {
+                        if (rd > 0) {
 #pragma unroll
                             for (int m = 0; m < 8; ++m) {
-                                const int v = t * kRows + 64 + 8 * m + (lane >> 2);
-                                c4[m] = (v < n && jj < nj)
-                                            ? __ldg(reinterpret_cast<const uint4*>(a.codes + (beg + v) * (int64_t)a.code_bytes +
-                                                                                  s * (kSlab / 2) + 16 * jj))
-                                            : make_uint4(0u, 0u, 0u, 0u);
+                                bool has;
+                                const uint8_t* src = q4src(rd, m, has);
+                                c4[m] = has ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
                             }
                         }
 #pragma unroll
                         for (int m = 0; m < 8; ++m) {
-                            const int r = 64 * half + 8 * m + (lane >> 2);
+                            const int r = 32 * rd + 8 * (m >> 1) + (lane >> 2), jj = (lane & 3) + 4 * (m & 1);
                             if (t * kRows + r < n && jj < nj) {
                                 const uint4 c = c4[m];
                                 const uint32_t M = 0x0F0F0F0Fu;
