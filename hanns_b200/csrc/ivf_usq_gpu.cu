@@ -21,7 +21,7 @@ namespace {
 // 180 GB HBM); per-query kernels index queries in grid.y in tiles of >= 8, so 262,144
 // queries per batch stay inside the 65,535 grid.y limit.
 constexpr int64_t kCandBudget = 16ll << 30;
-constexpr int64_t kFsBudget = 8ll << 30;  // FastScan scratch: 6 bytes per entry
+constexpr int64_t kFsBudget = 16ll << 30;  // FastScan scratch: 6 bytes per entry
 constexpr int64_t kMaxBatch = 262144;
 }  // namespace
 
