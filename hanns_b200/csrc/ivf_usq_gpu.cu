@@ -764,8 +764,17 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
         w_fs_sc_.reserve((size_t)nb * fss);
         w_fs_ip_.reserve((size_t)nb * fss);
     }
+    // a FastScan pair's region holds only its top k when that cannot change the query's
+    // top k (every entry of the top k is in its own pair's top k); the debug entry wants
+    // every kept candidate
+    PairTrunc tr;
+    tr.fs_keep = (!debug_candidates_ && k < n_cand && n_cand <= kFsRegRows / 2) ? k : 0;
+    tr.fused = opt.filter_mode == 2 ? 1 : 0;
+    tr.bitsets = opt.d_bitsets;
+    tr.n_bitsets = opt.d_bitsets ? opt.n_bitsets : 0;
+    tr.query_bitset = opt.d_query_bitset;
     launch_pair_offsets(st.probes, nb, nprobe, list_off_.p, nlist_, sharded_ ? owned_.p : nullptr,
-                        n_cand, w_pair_off_.p, tc_rows, fss > 0 ? w_fs_off_.p : nullptr, s);
+                        n_cand, w_pair_off_.p, tc_rows, fss > 0 ? w_fs_off_.p : nullptr, tr, s);
     launches += 5;
     if (time_it) HANNS_CUDA_OK(cudaEventRecord(ev_[5], s));
     // 4. list scan: kept candidates of every (query, probe) pair with their distance keys

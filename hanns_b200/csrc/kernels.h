@@ -244,13 +244,28 @@ void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist
                         int4* items, cudaStream_t s);
 // pair_off[q][r] = sum over earlier probes of min(|list|, n_cand) (0 for lists this
 // index does not own); pair_off[q][nprobe] = the query's candidate total
-// pair_off: per query the candidate regions of its probes (min(|list|, n_cand) entries each).
+// pair_off: per query the candidate regions of its probes (min(|list|, n_cand) entries each,
+// min(|list|, n_cand, fs_keep) for the FastScan pairs PairTrunc truncates).
 // fs_off (nullable): per (query, probe) the offset of a tensor-core FastScan pair (n_cand <
 // |list| <= tc_rows) in the query's region of the FastScan scratch (|list| entries each), -1
 // for other pairs.
+// Lists of at most kFsRegRows rows take fs_select's register path (scores in registers,
+// kept rows in a per-warp shared buffer of kFsRegRows entries).
+constexpr int kFsRegRows = 1024;
+// Region truncation of the FastScan pairs: with fs_keep > 0 (k < n_cand <= kFsRegRows / 2,
+// no debug candidates) every FastScan pair on fs_select's register path -- |list| <=
+// kFsRegRows and no fused filter for its query -- gets a region of min(n_cand, fs_keep)
+// entries, and fs_select writes the pair's top fs_keep there.
+struct PairTrunc {
+    int fs_keep = 0;
+    int fused = 0;
+    const uint64_t* bitsets = nullptr;
+    int64_t n_bitsets = 0;
+    const int32_t* query_bitset = nullptr;
+};
 void launch_pair_offsets(const int32_t* probes, int64_t nq, int nprobe, const int64_t* list_off,
                          int nlist, const uint8_t* owned, int n_cand, int* pair_off, int tc_rows,
-                         int* fs_off, cudaStream_t s);
+                         int* fs_off, const PairTrunc& tr, cudaStream_t s);
 size_t scan_smem_bytes(int D);
 size_t scan_tc_smem_bytes();
 constexpr int kTcProfSlots = 16;

@@ -902,6 +902,30 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
     if (w == 0) warp_select_stable(grow, nlist, nprobe, hist, ckey, cidx, probes + qi * nprobe);
 }
 
+// coarse_rescore_kernel's staging of the centroid rows (d % 4 == 0 and d > kRsStageMinD;
+// shorter rows stream from L2 into each thread's chain, exact_l2): dims per chunk, padded
+// row stride (floats; +4 keeps the 16-byte row reads of 8 consecutive lanes on distinct
+// banks)
+constexpr int kRsStageMinD = 1024;
+constexpr int kRsChunk = 64;
+constexpr int kRsLd = kRsChunk + 4;
+__host__ __device__ inline bool rescore_staged(int d) { return (d & 3) == 0 && d > kRsStageMinD; }
+inline size_t coarse_rescore_smem(int d) {
+    return ((size_t)((d + 3) & ~3) + (rescore_staged(d) ? 2 * (size_t)kCoarseRescoreMax * kRsLd : 0)) *
+           sizeof(float);
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Order of the candidates coarse_select_reg_kernel left in rs (per query: count, ||q||^2,
 // up to kCoarseRescoreMax centroid ids, their approximate scores a).  Each a bounds the
 // reference's sequential sum E(c) = exact_l2(q, c):
@@ -911,12 +935,13 @@ __global__ void __launch_bounds__(kSelThreads) coarse_select_reg_kernel(
 // them; a candidate whose interval meets another's gets its exact sum (one thread, the
 // reference's order), and such pairs are ordered by (exact key, centroid id) -- the stable
 // sort.  Typically a handful of the ~nprobe candidates of a query need the exact sum.
+template <bool STAGED>
 __global__ void __launch_bounds__(kCoarseRescoreMax) coarse_rescore_kernel(const float* __restrict__ q, int64_t nq,
                                                                  const float* __restrict__ cent, int d,
                                                                  int nprobe, float cmax, float dot_rel,
                                                                  const int* __restrict__ rs,
                                                                  int32_t* __restrict__ probes) {
-    extern __shared__ __align__(16) float qsm[];  // [d]
+    extern __shared__ __align__(16) float qsm[];  // [d], then the staged rows
     __shared__ double lo_s[kCoarseRescoreMax], hi_s[kCoarseRescoreMax];
     __shared__ uint32_t ckey[kCoarseRescoreMax];
     __shared__ int cidx[kCoarseRescoreMax];
@@ -950,9 +975,72 @@ __global__ void __launch_bounds__(kCoarseRescoreMax) coarse_rescore_kernel(const
     __syncthreads();
     if (any_s) {
         for (int i = tid; i < d; i += kCoarseRescoreMax) qsm[i] = q[qi * d + i];
-        __syncthreads();
-        if (need) ckey[tid] = total_order_key(exact_l2(qsm, cent + (int64_t)ci * d, d));
-        __syncthreads();
+        if (STAGED) {
+            // the needed centroid rows, kRsChunk dims at a time, staged in shared memory by
+            // all threads with coalesced 16-byte copies (double buffered: the next chunk is
+            // in flight while the sums run); each needing thread then continues its row's
+            // sequential sum from shared memory
+            float* rows = qsm + ((d + 3) & ~3);  // [2][kCoarseRescoreMax][kRsLd]
+            int* slot_ci = need_s;  // reused below: slot -> centroid id
+            __shared__ int nn_s;
+            if (tid == 0) nn_s = 0;
+            __syncthreads();
+            int slot = -1;
+            if (need) {
+                slot = atomicAdd(&nn_s, 1);
+            }
+            __syncthreads();
+            const int nn = nn_s;
+            if (need) slot_ci[slot] = ci;
+            __syncthreads();
+            const int nchunk = (d + kRsChunk - 1) / kRsChunk;
+            auto stage = [&](int c) {
+                float* dst = rows + (c & 1) * (kCoarseRescoreMax * kRsLd);
+                const int c0 = c * kRsChunk;
+                for (int e = tid; e < nn * (kRsChunk / 4); e += kCoarseRescoreMax) {
+                    const int j = e / (kRsChunk / 4), p4 = e - j * (kRsChunk / 4);
+                    if (c0 + 4 * p4 < d)
+                        cp_async16(dst + j * kRsLd + 4 * p4, cent + (int64_t)slot_ci[j] * d + c0 + 4 * p4);
+                }
+                cp_async_commit();
+            };
+            stage(0);
+            float acc = -0.0f;
+            for (int c = 0; c < nchunk; ++c) {
+                if (c + 1 < nchunk) {
+                    stage(c + 1);
+                    cp_async_wait<1>();
+                } else {
+                    cp_async_wait<0>();
+                }
+                __syncthreads();
+                if (need) {
+                    const float* rj = rows + (c & 1) * (kCoarseRescoreMax * kRsLd) + slot * kRsLd;
+                    const int c0 = c * kRsChunk, len = min(kRsChunk, d - c0);
+                    for (int i = 0; i < len; i += 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(rj + i);
+                        const float4 qv = *reinterpret_cast<const float4*>(qsm + c0 + i);
+                        float df = __fsub_rn(qv.x, v.x);
+                        acc = __fadd_rn(acc, __fmul_rn(df, df));
+                        df = __fsub_rn(qv.y, v.y);
+                        acc = __fadd_rn(acc, __fmul_rn(df, df));
+                        df = __fsub_rn(qv.z, v.z);
+                        acc = __fadd_rn(acc, __fmul_rn(df, df));
+                        df = __fsub_rn(qv.w, v.w);
+                        acc = __fadd_rn(acc, __fmul_rn(df, df));
+                    }
+                }
+                __syncthreads();  // the buffer is restaged two chunks on
+            }
+            if (need) ckey[tid] = total_order_key(acc);
+            // need_s held slot ids; the rank pass reads it as the need flags again
+            need_s[tid] = need ? 1 : 0;
+            __syncthreads();
+        } else {
+            __syncthreads();
+            if (need) ckey[tid] = total_order_key(exact_l2(qsm, cent + (int64_t)ci * d, d));
+            __syncthreads();
+        }
     }
     if (tid < cnt) {
         const uint32_t ki = need ? ckey[tid] : 0u;
@@ -1087,6 +1175,113 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x
     }
 }
 
+// rotate_kernel for large D: the same chains and tree, with the query tile staged a chunk
+// of CW columns at a time ([CW][QT+4] floats, so any D fits in two CTAs per SM).  A
+// half-warp owns R consecutive rows; the loads of P's next 64-column block are issued
+// before the FMAs of this one, so the L2 round trip hides under them.  Each chain still
+// adds its terms in column order: q_rot is bit-identical to rotate_kernel's.
+template <int QT, int R>
+__global__ void __launch_bounds__(256, 2) rotate_chunked_kernel(const float* __restrict__ x, int64_t nq,
+                                                        int d, int D, int CW,
+                                                        const float* __restrict__ Pc,
+                                                        float* __restrict__ out) {
+    constexpr int LD = QT + 4;
+    extern __shared__ __align__(16) float xs[];  // [CW][LD]
+    const int64_t q0 = (int64_t)blockIdx.y * QT;
+    const int half = threadIdx.x >> 4, j = threadIdx.x & 15;
+    const unsigned hmask = 0xFFFFu << (threadIdx.x & 16);
+    const int rbase = blockIdx.x * (16 * R) + half * R;
+    const bool active = rbase < D;  // D % 64 == 0 and R divides 64: all R rows exist
+    const float4* p0 = reinterpret_cast<const float4*>(Pc + (int64_t)(active ? rbase : 0) * D) + j;
+    const int D4r = D / 4;  // float4 per row
+    float acc[R][QT];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int t = 0; t < QT; ++t) acc[r][t] = 0.0f;
+    for (int c0 = 0; c0 < D; c0 += CW) {
+        const int cw = min(CW, D - c0);
+        if (c0 > 0) __syncthreads();  // every lane is done with the previous chunk
+        // fill: each thread moves 4 consecutive dims of one query (16-byte loads when
+        // d % 4 == 0); consecutive threads take consecutive queries so the transposed
+        // stores hit consecutive banks
+        const int cw4 = cw / 4;
+#pragma unroll 4
+        for (int e = threadIdx.x; e < QT * cw4; e += blockDim.x) {
+            const int t = e % QT, cl = (e / QT) * 4, c = c0 + cl;
+            const int64_t qq = q0 + t;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (qq < nq) {
+                if ((d & 3) == 0) {
+                    if (c < d) {
+                        const float4 f = __ldg(reinterpret_cast<const float4*>(x + qq * d + c));
+                        v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (c + k < d) v[k] = x[qq * d + c + k];
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) xs[(cl + k) * LD + t] = v[k];
+        }
+        __syncthreads();
+        if (!active) continue;
+        const int tb0 = c0 / 64, ntb = cw / 64;
+        float4 p4[R], pn[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) p4[r] = __ldg(p0 + (int64_t)r * D4r + tb0 * 16);
+        for (int u = 0; u < ntb; ++u) {
+            if (u + 1 < ntb) {
+#pragma unroll
+                for (int r = 0; r < R; ++r) pn[r] = __ldg(p0 + (int64_t)r * D4r + (tb0 + u + 1) * 16);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4* xv = reinterpret_cast<const float4*>(xs + (64 * u + 16 * k + j) * LD);
+#pragma unroll
+                for (int t4 = 0; t4 < QT / 4; ++t4) {
+                    const float4 v = xv[t4];
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        const float p = k == 0 ? p4[r].x : k == 1 ? p4[r].y : k == 2 ? p4[r].z : p4[r].w;
+                        acc[r][4 * t4 + 0] = __fmaf_rn(p, v.x, acc[r][4 * t4 + 0]);
+                        acc[r][4 * t4 + 1] = __fmaf_rn(p, v.y, acc[r][4 * t4 + 1]);
+                        acc[r][4 * t4 + 2] = __fmaf_rn(p, v.z, acc[r][4 * t4 + 2]);
+                        acc[r][4 * t4 + 3] = __fmaf_rn(p, v.w, acc[r][4 * t4 + 3]);
+                    }
+                }
+            }
+            if (u + 1 < ntb) {
+#pragma unroll
+                for (int r = 0; r < R; ++r) p4[r] = pn[r];
+            }
+        }
+    }
+    if (!active) return;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int t = 0; t < QT; ++t) {
+            float v = acc[r][t];
+            v = __fadd_rn(v, __shfl_down_sync(hmask, v, 8, 16));
+            v = __fadd_rn(v, __shfl_down_sync(hmask, v, 4, 16));
+            v = __fadd_rn(v, __shfl_down_sync(hmask, v, 2, 16));
+            v = __fadd_rn(v, __shfl_down_sync(hmask, v, 1, 16));
+            acc[r][t] = v;
+        }
+    if (j == 0) {
+#pragma unroll
+        for (int t = 0; t < QT; ++t)
+            if (q0 + t < nq)
+#pragma unroll
+                for (int r4 = 0; r4 < R; r4 += 4)
+                    *reinterpret_cast<float4*>(out + (q0 + t) * D + rbase + r4) =
+                        make_float4(acc[r4][t], acc[r4 + 1][t], acc[r4 + 2][t], acc[r4 + 3][t]);
+    }
+}
+
 __device__ __forceinline__ float lut_entry(const float* q4, int nib) {
     float v = 0.0f;
 #pragma unroll
@@ -1114,17 +1309,23 @@ __global__ void __launch_bounds__(128) query_state_kernel(
     }
     __syncthreads();
     if (!valid) return;
-    // sequential sums (Rust Sum<f32> starts from -0.0), from shared memory
-    float cs = -0.0f, qn = -0.0f, qsum = -0.0f;
-    if (lane == 1)
-        for (int i = 0; i < D; ++i) cs = __fadd_rn(cs, __fmul_rn(r[i], rc_s[i]));
-    if (lane == 2)
-        for (int i = 0; i < d; ++i) qn = __fadd_rn(qn, __fmul_rn(xq[i], xq[i]));
-    if (lane == 3)
-        for (int i = 0; i < D; ++i) qsum = __fadd_rn(qsum, r[i]);
-    cs = __shfl_sync(0xffffffffu, cs, 1);
-    qn = __shfl_sync(0xffffffffu, qn, 2);
-    qsum = __shfl_sync(0xffffffffu, qsum, 3);
+    // sequential sums (Rust Sum<f32> starts from -0.0), from shared memory, side by side
+    // in one loop on lanes 1-3 (no divergent serial passes): lane 1 sum(r * rc), lane 2
+    // sum(x * x), lane 3 sum(r), its terms as r * 1.0 (exact)
+    float ch = -0.0f;
+    if (lane >= 1 && lane <= 3) {
+        const float* a = lane == 2 ? xq : r;
+        const float* b = lane == 2 ? xq : rc_s;
+        const int n = lane == 2 ? d : D;
+#pragma unroll 8
+        for (int i = 0; i < n; ++i) {
+            const float bv = lane == 3 ? 1.0f : b[i];
+            ch = __fadd_rn(ch, __fmul_rn(a[i], bv));
+        }
+    }
+    const float cs = __shfl_sync(0xffffffffu, ch, 1);
+    const float qn = __shfl_sync(0xffffffffu, ch, 2);
+    const float qsum = __shfl_sync(0xffffffffu, ch, 3);
     float m = 0.0f;
     for (int i = lane; i < D; i += 32) m = fmaxf(m, fabsf(r[i]));
     m = fmaxf(warp_max(m), 1e-6f);
@@ -1285,10 +1486,18 @@ __global__ void make_items_kernel(const int* __restrict__ cnt, const int* __rest
 __global__ void pair_offsets_kernel(const int32_t* __restrict__ probes, int64_t nq, int nprobe,
                                     const int64_t* __restrict__ list_off, int nlist,
                                     const uint8_t* __restrict__ owned, int n_cand,
-                                    int* __restrict__ pair_off, int tc_rows, int* __restrict__ fs_off) {
+                                    int* __restrict__ pair_off, int tc_rows, int* __restrict__ fs_off,
+                                    PairTrunc tr) {
     const int lane = (int)lane_id();
     const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (q >= nq) return;
+    // the query's FastScan pairs on fs_select's register path (no fused filter, |list| <=
+    // kFsRegRows) keep only their top fs_keep entries
+    bool trunc = tr.fs_keep > 0 && fs_off;
+    if (trunc && tr.fused && tr.bitsets) {
+        const int b = tr.query_bitset ? tr.query_bitset[q] : 0;
+        if (b >= 0 && b < tr.n_bitsets) trunc = false;
+    }
     int carry = 0, fs_carry = 0;
     for (int r0 = 0; r0 < nprobe; r0 += 32) {
         const int r = r0 + lane;
@@ -1299,7 +1508,10 @@ __global__ void pair_offsets_kernel(const int32_t* __restrict__ probes, int64_t 
                 const int64_t n = list_off[l + 1] - list_off[l];
                 cap = (int)min(n, (int64_t)n_cand);
                 // a tensor-core FastScan pair: |list| entries, padded to 8 (16-byte regions)
-                if (n > n_cand && n <= tc_rows) fs_n = (int)((n + 7) & ~7ll);
+                if (n > n_cand && n <= tc_rows) {
+                    fs_n = (int)((n + 7) & ~7ll);
+                    if (trunc && n <= kFsRegRows) cap = min(cap, tr.fs_keep);
+                }
             }
         }
         const int inc = warp_inclusive_scan(cap);
@@ -2210,7 +2422,8 @@ __device__ __forceinline__ int nth_set_bit64(uint64_t x, int k) {
 // kept rows' int_ip and metadata are loaded four rows at a time before their distances.
 template <int PW>
 __device__ void fs_select_regs(const FsSelectArgs& a, int64_t q, int r, int64_t beg, int n,
-                               const int16_t* gsc, const int32_t* gip, int lane, uint32_t* kept) {
+                               const int16_t* gsc, const int32_t* gip, int lane, uint32_t* kept,
+                               uint32_t* hist) {
     constexpr int RPL = 2 * PW;  // rows per lane
     const int row0 = lane * RPL;
     const int npad = (n + 7) & ~7;  // the pair's scratch region
@@ -2299,8 +2512,14 @@ __device__ void fs_select_regs(const FsSelectArgs& a, int64_t q, int r, int64_t 
     const int n_kept = min(__shfl_sync(0xffffffffu, pk + ck, 31), a.n_cand);
     const QueryParams qp = a.qp[q];
     const bool l2 = a.metric_l2 != 0;
-    const int64_t rbase = q * a.q_stride + a.pair_off[q * (a.nprobe + 1) + r];
+    const int* po = a.pair_off + q * (a.nprobe + 1) + r;
+    const int64_t rbase = q * a.q_stride + po[0];
     const uint64_t rank_bits = (uint64_t)r << 48;
+    // a region of cap < n_kept entries (the pair offsets kept room for the pair's top k
+    // only): the distance keys go to kk first, then the cap smallest by (key, tie)
+    const int cap = po[1] - po[0];
+    const bool trunc = cap < n_kept;
+    uint32_t* kk = kept + kFsRegRows / 2;  // (trunc only when n_cand <= kFsRegRows / 2)
     for (int e0 = 0; e0 < n_kept; e0 += 64) {
         // two entries per lane, their loads issued together
         int ipv[2];
@@ -2320,9 +2539,105 @@ __device__ void fs_select_regs(const FsSelectArgs& a, int64_t q, int r, int64_t 
             if (e >= n_kept) continue;
             const int v = (int)(ent[h] >> 16), sv = (int)(int16_t)(ent[h] & 0xFFFFu);
             const float dist = rerank_distance(ipv[h], mv[h], qp, a.nbits, l2);
+            if (trunc) {
+                kk[e] = total_order_key(dist);
+                continue;
+            }
             a.cand_key[rbase + e] = total_order_key(dist);
             a.cand_tie[rbase + e] = rank_bits | ((uint64_t)(uint32_t)(32767 - sv) << 32) | (uint32_t)v;
             if (a.cand_dbg) a.cand_dbg[rbase + e] = make_int2(ipv[h], sv);
+        }
+    }
+    __syncwarp();
+    if (!trunc) return;
+    // the pair's top cap by (key, FastScan key, row) -- the merge's order inside one pair, so
+    // the query's top k over all pairs is unchanged.
+    auto tie_of = [&](int e) {
+        const uint32_t en = kept[e];
+        return rank_bits | ((uint64_t)(uint32_t)(32767 - (int)(int16_t)(en & 0xFFFFu)) << 32) | (en >> 16);
+    };
+    // Fast path: the cap-th smallest of the 32 lane minima bounds the cap-th smallest key
+    // from above (those cap lanes hold cap entries at or below it; at least cap lanes hold
+    // entries because n_kept > cap and cap <= 32).  The entries at or below the bound --
+    // usually little more than cap -- take one lane each and are ranked by (key, tie),
+    // which is unique, with a shuffle loop; ranks < cap are written in order.
+    if (cap <= 32) {
+        uint32_t lm = 0xFFFFFFFFu;
+        for (int e = lane; e < n_kept; e += 32) lm = min(lm, kk[e]);
+        uint32_t bound = 0;
+        for (int i = 0; i < cap; ++i) {
+            bound = __reduce_min_sync(0xffffffffu, lm);
+            const unsigned b = __ballot_sync(0xffffffffu, lm == bound);
+            if (lane == __ffs(b) - 1) lm = 0xFFFFFFFFu;
+        }
+        int nc = 0;
+        for (int e0 = 0; e0 < n_kept; e0 += 32) {
+            const int e = e0 + lane;
+            const bool in = e < n_kept && kk[e] <= bound;
+            const unsigned b = __ballot_sync(0xffffffffu, in);
+            if (in && nc + __popc(b & lanemask_lt()) < 32) hist[nc + __popc(b & lanemask_lt())] = (uint32_t)e;
+            nc += __popc(b);
+        }
+        __syncwarp();
+        if (nc <= 32) {
+            const int e = lane < nc ? (int)hist[lane] : 0;
+            const uint32_t key = lane < nc ? kk[e] : 0xFFFFFFFFu;
+            const uint64_t tie = lane < nc ? tie_of(e) : ~0ull;
+            int rk = 0;
+            for (int j = 0; j < nc; ++j) {
+                const uint32_t kj = __shfl_sync(0xffffffffu, key, j);
+                const uint64_t tj = __shfl_sync(0xffffffffu, tie, j);
+                rk += (kj < key || (kj == key && tj < tie)) ? 1 : 0;
+            }
+            if (lane < nc && rk < cap) {
+                a.cand_key[rbase + rk] = key;
+                a.cand_tie[rbase + rk] = tie;
+            }
+            __syncwarp();
+            return;
+        }
+        __syncwarp();
+    }
+    // general path: tau = the cap-th smallest key, every entry below it, then the smallest
+    // (FastScan key, row) among the entries at tau
+    int n_less = 0;
+    const uint32_t tau = warp_radix_kth(
+        n_kept, cap,
+        [&](int i, uint32_t& key) {
+            key = kk[i];
+            return true;
+        },
+        hist, &n_less);
+    int n_w = 0;
+    for (int b = 0; b < n_kept; b += 32) {
+        const int e = b + lane;
+        const bool take = e < n_kept && kk[e] < tau;
+        const unsigned bt = __ballot_sync(0xffffffffu, take);
+        if (take) {
+            const int pos = n_w + __popc(bt & lanemask_lt());
+            a.cand_key[rbase + pos] = kk[e];
+            a.cand_tie[rbase + pos] = tie_of(e);
+        }
+        n_w += __popc(bt);
+    }
+    // ties at tau (rare: equal distances): the smallest remaining tie, one at a time
+    uint64_t floor_t = 0;
+    for (bool first = true; n_w < cap; ++n_w, first = false) {
+        uint64_t best = ~0ull;
+        for (int e = lane; e < n_kept; e += 32) {
+            if (kk[e] != tau) continue;
+            const uint64_t t = tie_of(e);
+            if ((first || t > floor_t) && t < best) best = t;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+            best = ob < best ? ob : best;
+        }
+        floor_t = best;
+        if (lane == 0) {
+            a.cand_key[rbase + n_w] = tau;
+            a.cand_tie[rbase + n_w] = best;
         }
     }
     __syncwarp();
@@ -2347,12 +2662,12 @@ __device__ void fs_select_pair(const FsSelectArgs& a, int64_t q, int r, int lane
         const int b = a.query_bitset ? a.query_bitset[q] : 0;
         if (b >= 0 && b < a.n_bitsets) bw = a.bitsets + (int64_t)b * a.bitset_words;
     }
-    if (!bw && n <= 1024) {
+    if (!bw && n <= kFsRegRows) {
         // unfiltered (every row live, n > n_cand): the pair's scores in registers
-        if (n <= 512)
-            fs_select_regs<8>(a, q, r, beg, n, sc, ip, lane, kept_w);
+        if (n <= kFsRegRows / 2)
+            fs_select_regs<8>(a, q, r, beg, n, sc, ip, lane, kept_w, hist_w);
         else
-            fs_select_regs<16>(a, q, r, beg, n, sc, ip, lane, kept_w);
+            fs_select_regs<16>(a, q, r, beg, n, sc, ip, lane, kept_w, hist_w);
         return;
     }
     auto live = [&](int v) { return !bw || !bit_filtered(bw, a.bitset_len, a.ids[beg + v]); };
@@ -2444,7 +2759,7 @@ __device__ void fs_select_pair(const FsSelectArgs& a, int64_t q, int r, int lane
 // robin: the pairs of one list (same cost) go to different warps.
 __global__ void __launch_bounds__(256, 4) fs_select_kernel(FsSelectArgs a) {
     __shared__ uint32_t hist[8][256];
-    __shared__ uint32_t kept_rows[8][1024];  // register path: each warp's kept (row, score)
+    __shared__ uint32_t kept_rows[8][kFsRegRows];  // register path: each warp's kept (row, score)
     const int w = threadIdx.x >> 5, lane = (int)lane_id();
     const int total = *a.n_lq;
     const int n_warps = gridDim.x * 8;
@@ -2782,9 +3097,18 @@ int launch_coarse_select(float* approx, const float* q, int64_t nq, const float*
         else if (nv4 == 2) go(coarse_select_reg_kernel<2>);
         else if (nv4 == 3) go(coarse_select_reg_kernel<3>);
         else go(coarse_select_reg_kernel<4>);
-        if (rs)
-            coarse_rescore_kernel<<<(unsigned)nq, kCoarseRescoreMax, (size_t)d * sizeof(float), s>>>(
-                q, nq, cent, d, nprobe, cmax, dot_rel, rs, probes);
+        if (rs) {
+            const size_t rs_bytes = coarse_rescore_smem(d);
+            if (rescore_staged(d)) {
+                cudaFuncSetAttribute(coarse_rescore_kernel<true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rs_bytes);
+                coarse_rescore_kernel<true><<<(unsigned)nq, kCoarseRescoreMax, rs_bytes, s>>>(
+                    q, nq, cent, d, nprobe, cmax, dot_rel, rs, probes);
+            } else {
+                coarse_rescore_kernel<false><<<(unsigned)nq, kCoarseRescoreMax, rs_bytes, s>>>(
+                    q, nq, cent, d, nprobe, cmax, dot_rel, rs, probes);
+            }
+        }
         return rs ? 2 : 1;
     }
     const size_t blk_bytes =
@@ -2819,11 +3143,25 @@ void launch_rotation_chain_major(const float* P, int D, float* Pc, cudaStream_t 
 void launch_rotate(const float* x, int64_t nq, int d, int D, const float* Pc, float* out,
                    cudaStream_t s) {
     if (nq <= 0) return;
-    constexpr int QT = 8, R = 8;
-    const size_t smem = (size_t)D * (QT + 4) * sizeof(float);
-    cudaFuncSetAttribute(rotate_kernel<QT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (D <= 1024) {
+        // the whole query tile in shared memory (at most 48 KB: two CTAs per SM)
+        constexpr int QT = 8, R = 8;
+        const size_t smem = (size_t)D * (QT + 4) * sizeof(float);
+        cudaFuncSetAttribute(rotate_kernel<QT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        dim3 grid((D + 16 * R - 1) / (16 * R), (unsigned)((nq + QT - 1) / QT));
+        rotate_kernel<QT, R><<<grid, 256, smem, s>>>(x, nq, d, D, Pc, out);
+        return;
+    }
+    // larger D: 768-column chunks of the query tile (61 KB: still two CTAs per SM, where
+    // the whole tile would allow one), 16 queries x 4 rows per thread with the next block
+    // of P prefetched (P crosses L2 once per 16 queries; it no longer fits the L1s)
+    constexpr int QT = 16, R = 4;
+    const int CW = 768;
+    const size_t smem = (size_t)CW * (QT + 4) * sizeof(float);
+    cudaFuncSetAttribute(rotate_chunked_kernel<QT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
     dim3 grid((D + 16 * R - 1) / (16 * R), (unsigned)((nq + QT - 1) / QT));
-    rotate_kernel<QT, R><<<grid, 256, smem, s>>>(x, nq, d, D, Pc, out);
+    rotate_chunked_kernel<QT, R><<<grid, 256, smem, s>>>(x, nq, d, D, CW, Pc, out);
 }
 
 void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, int D,
@@ -2870,10 +3208,10 @@ int scan_grid_size(int D) {
 
 void launch_pair_offsets(const int32_t* probes, int64_t nq, int nprobe, const int64_t* list_off,
                          int nlist, const uint8_t* owned, int n_cand, int* pair_off, int tc_rows,
-                         int* fs_off, cudaStream_t s) {
+                         int* fs_off, const PairTrunc& tr, cudaStream_t s) {
     if (nq <= 0) return;
     pair_offsets_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(probes, nq, nprobe, list_off, nlist,
-                                                                owned, n_cand, pair_off, tc_rows, fs_off);
+                                                                owned, n_cand, pair_off, tc_rows, fs_off, tr);
 }
 
 void launch_scan(const ScanArgs& a, int grid, cudaStream_t s) {
