@@ -44,7 +44,8 @@
 //   warps 6-13  epilogue (thread per row): FastScan items' scores and int_ip TMEM -> the
 //               FastScan scratch; rerank-only items' kept rows (bitmaps) and their
 //               distances and ties
-//   warp 14     TMEM allocation and the single-thread MMA issuer
+//   warp 14     TMEM allocation and the MMA issuer (the whole warp runs the loop with
+//               warp-uniform descriptors; one elected lane issues the MMAs and commits)
 //   warp 15     item scheduler: takes items, fills the item slots, prefetches the next
 //               item's list into L2
 // Every wait is bounded (wait_ns, 2 s by default): on expiry the kernel records an error
@@ -169,19 +170,27 @@ __device__ __forceinline__ uint64_t desc_k(uint64_t d, int k4) {
     return d + (uint64_t)((k4 >> 2) * (kAtomBytes >> 4) + 2 * (k4 & 3));
 }
 
-__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                        uint32_t idesc, uint32_t accumulate) {
+// D (+)= A B^T, kind::i8 (u8 A; u8 or s8 B by idesc), issued by the one lane elect.sync
+// picks (the lowest active lane) while the whole warp executes the instruction with
+// warp-uniform operands.
+__device__ __forceinline__ void umma_i8_elect(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+// tcgen05.commit by the elected lane: the barrier's phase completes once every MMA that
+// lane issued so far has completed.
+__device__ __forceinline__ void umma_commit_elect(uint64_t* bar) {
     asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
             smem_u32(bar))
         : "memory");
 }
@@ -478,14 +487,22 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // The whole warp runs the loop, so the ring positions and descriptors are
+        // warp-uniform values; every lane waits on the barriers (the warp proceeds only if
+        // all of them saw the phase complete), and one elected lane -- the same one each
+        // time -- issues the tcgen05.mma and tcgen05.commit instructions.
+        {
             uint32_t ga = 0, gb = 0, uc = 0;  // ring positions, GEMMs so far
             uint64_t p_wfull = 0, p_wfree = 0, p_loop = 0;
+            const bool pl = lane == 0;  // the MMA warp's profiling lane
+            auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+                return __all_sync(0xffffffffu, mbar_wait(bar, parity, &sm.abort, wl)) != 0;
+            };
             for (int j = 0;; ++j) {
                 const int si = j % kSlots;
                 const ItemSlot& S = sm.slot[si];
-                if (!mbar_wait(&sm.item_full[si], (j / kSlots) & 1, &sm.abort, wl)) {
-                    fail(7);
+                if (!wait_all(&sm.item_full[si], (j / kSlots) & 1)) {
+                    if (lane == 0) fail(7);
                     break;
                 }
                 if (S.item < 0) break;
@@ -498,63 +515,64 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     const uint32_t h = uc & 1, use = uc >> 1;
                     const uint32_t dcol = tmem + h * kHalfCols;
                     const uint64_t t_f = prof ? global_ns() : 0;
-                    if (use >= 1 && !mbar_wait(&sm.acc_free[h], (use - 1) & 1, &sm.abort, wl)) {
+                    if (use >= 1 && !wait_all(&sm.acc_free[h], (use - 1) & 1)) {
                         ok = false;
                         return;
                     }
-                    padd(true, p_wfree, t_f);
+                    padd(pl, p_wfree, t_f);
                     for (int s = 0; s < slabs && ok; ++s) {
                         const uint32_t bs = gb % kNB;
                         uint64_t t_w = prof ? global_ns() : 0;
-                        if (!mbar_wait(&sm.b_full[bs], (gb / kNB) & 1, &sm.abort, wl)) {
+                        if (!wait_all(&sm.b_full[bs], (gb / kNB) & 1)) {
                             ok = false;
                             break;
                         }
-                        padd(true, p_wfull, t_w);
+                        padd(pl, p_wfull, t_w);
                         const int nk = min(kSlab, k_bytes - s * kSlab) / 32;
                         const uint64_t bd = sw128_desc(smem_u32(ring_b + bs * kStageBytes));
                         for (int t = 0; t < T; ++t) {
                             const uint32_t as = ga % kNA;
                             t_w = prof ? global_ns() : 0;
-                            if (!mbar_wait(&sm.a_full[as], (ga / kNA) & 1, &sm.abort, wl)) {
+                            if (!wait_all(&sm.a_full[as], (ga / kNA) & 1)) {
                                 ok = false;
                                 break;
                             }
-                            padd(true, p_wfull, t_w);
+                            padd(pl, p_wfull, t_w);
                             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                             const uint64_t ad = sw128_desc(smem_u32(ring_a + as * kStageBytes));
                             for (int k4 = 0; k4 < nk; ++k4)
-                                umma_i8(dcol + (uint32_t)(t * N), desc_k(ad, k4), desc_k(bd, k4), idesc,
-                                        (s > 0 || k4 > 0) ? 1u : 0u);
-                            umma_commit(&sm.a_empty[as]);
+                                umma_i8_elect(dcol + (uint32_t)(t * N), desc_k(ad, k4), desc_k(bd, k4),
+                                              idesc, (s > 0 || k4 > 0) ? 1u : 0u);
+                            umma_commit_elect(&sm.a_empty[as]);
                             ++ga;
                         }
                         if (!ok) break;
-                        umma_commit(&sm.b_empty[bs]);
+                        umma_commit_elect(&sm.b_empty[bs]);
                         ++gb;
                     }
-                    if (ok) umma_commit(&sm.acc_full[h]);
+                    if (ok) umma_commit_elect(&sm.acc_full[h]);
                     ++uc;
                 };
                 if (S.fs) gemm(fs_slabs, 4 * a.D, idesc_i8(N, false));
                 if (ok) gemm(rr_slabs, a.D, idesc_i8(N, true));
                 if (!ok) {
-                    fail(7);
+                    if (lane == 0) fail(7);
                     break;
                 }
-                mbar_arrive(&sm.item_empty[si]);
-                padd(true, p_loop, t_item);
+                if (lane == 0) mbar_arrive(&sm.item_empty[si]);
+                padd(pl, p_loop, t_item);
             }
-            // before the TMEM is freed, every MMA issued (also after an abort) completes;
-            // this wait ignores the abort flag and gives up after 0.5 s
-            if (prof) {
+            if (prof && pl) {
                 prof[kPMmaWaitFull] = p_wfull;
                 prof[kPMmaWaitFree] = p_wfree;
                 prof[kPMma] = p_loop;
             }
-            umma_commit(&sm.drain);
+            // before the TMEM is freed, every MMA issued (also after an abort) completes;
+            // this wait ignores the abort flag and gives up after 0.5 s
+            umma_commit_elect(&sm.drain);
             int no_abort = 0;
-            if (!mbar_wait(&sm.drain, 0, &no_abort, 500000000ull)) fail(10);
+            const bool drained = __all_sync(0xffffffffu, mbar_wait(&sm.drain, 0, &no_abort, 500000000ull)) != 0;
+            if (!drained && lane == 0) fail(10);
         }
         __syncwarp();
     } else if (warp == kSchedWarp) {
