@@ -755,8 +755,8 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     const bool use_tc = tc_rows > 0;
     const int64_t fss = fs_stride(nprobe, n_cand, tc_rows);
     launch_group_pairs(st.probes, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr, list_off_.p,
-                       tc_rows, kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p, w_item_off_.p,
-                       w_counters_.p, w_lq_.p, w_items_.p, s);
+                       tc_rows, n_cand, kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p,
+                       w_item_off_.p, w_counters_.p, w_lq_.p, w_items_.p, s);
     const int64_t q_stride = cand_stride(nprobe, k);
     w_pair_off_.reserve((size_t)nb * (nprobe + 1));
     if (fss > 0) {
@@ -889,7 +889,7 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
             static const char* names[] = {"build", "build_wait_slot", "build_wait_item", "mma_wait_full",
                                           "mma_wait_free", "mma", "epi_wait_acc", "epi_copy",
                                           "epi_select", "epi_rerank", "epi_wait_item", "epi",
-                                          "items", "stages", "build_store", "build_fence"};
+                                          "items", "stages", "mma_wait_b", "unused"};
             std::fprintf(stderr, "TC_SCAN_PROFILE ctas=%d", sm_count_);
             for (int k = 0; k < 16; ++k) {
                 double sum = 0;

@@ -68,11 +68,14 @@ struct ScanArgs {
 // Lists of at most kTcMaxRows rows are scanned by the tensor-core kernel (scan_tc.cu),
 // longer ones by the SIMT kernel.  A tensor-core item holds one list's rows in T =
 // ceil(n / 128) tiles of 128 (the MMA's M) and up to 128 queries (the MMA's N, a multiple
-// of 16) with N * T <= kTcItemCols: one GEMM's accumulators fit in half of the TMEM, and
-// the item's FastScan scores and kept-row bitmaps fit in shared memory.
+// of 16).  Its GEMMs run over groups of G = min(T, kTcItemCols / N) tiles, whose
+// accumulators fit in half of the TMEM.  A FastScan list (more than n_cand rows) takes
+// 128 queries per item whatever its length; a rerank-only list at most kTcItemCols / T
+// (one group: the kept-row bitmaps of all T tiles fit in shared memory).
 constexpr int kTcMaxRows = 2048;
 constexpr int kTcItemCols = 256;
-HANNS_HD inline int tc_queries_per_item(long long n) {
+HANNS_HD inline int tc_queries_per_item(long long n, bool fastscan) {
+    if (fastscan) return 128;
     const int t = (int)((n + 127) / 128);
     const int q = (kTcItemCols / (t < 1 ? 1 : t)) & ~15;
     return q > 128 ? 128 : q;
@@ -236,12 +239,13 @@ void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, i
                         const float* rc, int nbits, QueryParams* qp, uint8_t* q_i8p,
                         int8_t* q_i8n, uint8_t* lut, cudaStream_t s);
 // Items (list, first lq index, queries, kind): lists of at most tc_max_rows rows (0:
-// none) become tensor-core items (kind 1) of tc_queries_per_item(|list|) queries, the
+// none) become tensor-core items (kind 1) of tc_queries_per_item(|list|, |list| > n_cand)
+// queries, the
 // others SIMT items (kind 0) of qpi queries.
 void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist,
-                        const uint8_t* owned, const int64_t* list_off, int tc_max_rows, int qpi,
-                        int* cnt, int* cursor, int* lq_off, int* item_off, int* n_items, int2* lq,
-                        int4* items, cudaStream_t s);
+                        const uint8_t* owned, const int64_t* list_off, int tc_max_rows, int n_cand,
+                        int qpi, int* cnt, int* cursor, int* lq_off, int* item_off, int* n_items,
+                        int2* lq, int4* items, cudaStream_t s);
 // pair_off[q][r] = sum over earlier probes of min(|list|, n_cand) (0 for lists this
 // index does not own); pair_off[q][nprobe] = the query's candidate total
 // pair_off: per query the candidate regions of its probes (min(|list|, n_cand) entries each,

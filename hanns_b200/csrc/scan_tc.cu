@@ -1,10 +1,12 @@
 // scan_tc.cu -- list scan on the sm_100a tensor cores.
 //
 // One persistent CTA per SM takes items: one list of at most kTcMaxRows rows and the
-// queries that probe it, at most kTcItemCols / T of them (tc_queries_per_item).  The
-// list's rows are the MMA's M side, in T tiles of 128; the item's queries are its N side
-// (N = queries rounded up to 16, N * T <= 256).  Both integer stages of the reference's
-// search are int8 GEMMs (tcgen05.mma kind::i8, int32 accumulation in TMEM, exact):
+// queries that probe it (tc_queries_per_item: up to 128 for a FastScan list, kTcItemCols /
+// T for a rerank-only one).  The list's rows are the MMA's M side, in T tiles of 128; the
+// item's queries are its N side (N = queries rounded up to 16).  The GEMMs run over groups
+// of G = min(T, 256 / N) row tiles, so one group's accumulators fill at most one TMEM half.
+// Both integer stages of the reference's search are int8 GEMMs (tcgen05.mma kind::i8, int32
+// accumulation in TMEM, exact):
 //
 //   FastScan   raw[v][i] = sum_g LUT_i[g][nib_g(v)]                    (fastscan.rs:170-227)
 //              = onehot(v) . LUT_i over K = 16 G bytes: A = one-hot rows (u8 0/1, one
@@ -18,9 +20,11 @@
 //              in q_i8p's order (4-bit codes: per 8 dimensions the 4 even, then the 4
 //              odd ones -- the low and the high nibbles of a 32-bit code word), B = q_i8p.
 //
-// An item's FastScan GEMM (T x N accumulator columns <= 256) fills one half of the 512
-// TMEM columns and its rerank GEMM the other half; consecutive GEMMs alternate halves, so
-// one GEMM overlaps the epilogue of the one before.  A FastScan item's epilogue streams
+// Per group, the FastScan GEMM (G x N accumulator columns <= 256) fills one half of the
+// 512 TMEM columns and the rerank GEMM the other half; consecutive GEMMs alternate halves,
+// so one GEMM overlaps the epilogue of the one before.  A list's one-hot rows and codes are
+// built once for up to 128 queries (the B stages -- the queries' operands -- are reloaded
+// per group instead).  A FastScan item's epilogue streams
 // every (row, query) score and int_ip to the FastScan scratch, from which fs_select_kernel
 // (search_kernels.cu, a warp per pair at full occupancy) takes the reference's heap kept set
 // (fastscan.rs:86-146) and the kept rows' distances.  A rerank-only item keeps every live
@@ -29,7 +33,7 @@
 //
 // Operands stream through two rings of 32 KiB stages (128 rows x 256 K bytes: two 128-byte
 // swizzle atoms, K-major): A (kNA slots, the row tiles) and B (kNB slots, the queries).  Per
-// GEMM and K slab the MMA consumes one B stage and then the T A stages.  Each ring slot
+// GEMM and K slab the MMA consumes one B stage and then the group's A stages.  Each ring slot
 // has one builder warp, which fills the slot's positions in ring order, so every wait of
 // a builder on its slot's empty barrier is for the phase right after the last one it saw.
 //
@@ -59,8 +63,8 @@
 namespace hanns {
 namespace {
 
-constexpr int kNA = 4, kNB = 2;                   // ring slots, one builder warp each
-constexpr int kBuildWarps = kNA + kNB;            // warps 0-3 A, 4-5 B
+constexpr int kNA = 3, kNB = 3;                   // ring slots, one builder warp each
+constexpr int kBuildWarps = kNA + kNB;            // warps 0-2 A, 3-5 B
 constexpr int kEpiWarps = 8;                      // warps 6-13
 constexpr int kMmaWarp = kBuildWarps + kEpiWarps;  // 14
 constexpr int kSchedWarp = kMmaWarp + 1;          // 15
@@ -73,7 +77,7 @@ constexpr int kAtom = 128;                        // K bytes of one 128-byte swi
 constexpr int kAtomBytes = kRows * kAtom;         // 16 KiB: 128 rows of one atom
 constexpr int kSlab = 2 * kAtom;                  // K bytes per stage (two atoms)
 constexpr int kStageBytes = 2 * kAtomBytes;       // 32 KiB
-constexpr int kWordCap = kTcItemCols * 4;         // kept-row bitmap words: N * T * 4
+constexpr int kWordCap = kTcItemCols * 4;         // kept-row bitmap words (rerank-only items): N * T * 4
 constexpr int kSlots = 2;                         // items in flight
 constexpr uint32_t kWaitLimit = 1u << 24;
 static_assert(kTcItemCols <= kHalfCols, "one GEMM's accumulators fill at most one TMEM half");
@@ -254,10 +258,11 @@ __device__ __forceinline__ void l2_prefetch(const void* p, uint64_t bytes) {
 //   0 builder item loop (warp 0)  1 its empty-slot waits  2 its item waits
 //   3 MMA full-stage waits  4 MMA accumulator-free waits  5 MMA item loop
 //   6 epilogue accumulator waits  7 FastScan copy-out  8 selection  9 rerank epilogue
-//   10 epilogue item waits  11 epilogue item loop  12 items  13 stages
+//   10 epilogue item waits  11 epilogue item loop  12 items  13 stages  14 the part of 3
+//   spent on B stages
 enum ProfSlot { kPBuild, kPBuildWaitSlot, kPBuildWaitItem, kPMmaWaitFull, kPMmaWaitFree, kPMma,
                 kPEpiWaitAcc, kPEpiCopy, kPEpiSelect, kPEpiRerank, kPEpiWaitItem, kPEpi, kPItems,
-                kPStages };
+                kPStages, kPMmaWaitB };
 
 __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -341,25 +346,27 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             const int n = S.n, nq = S.nq, N = S.N, T = S.T;
             const int64_t beg = S.beg;
             const int fss = S.fs ? fs_slabs : 0;
-            // this ring's stages of the item: B per slab, A per slab and row tile
-            const int nst = is_b ? fss + rr_slabs : (fss + rr_slabs) * T;
+            // this ring's stages of the item, group by group (G row tiles per GEMM): B per
+            // slab, A per slab and row tile of the group
+            const int G = min(T, kHalfCols / N), ngr = (T + G - 1) / G, nsl = fss + rr_slabs;
+            const int nst = is_b ? nsl * ngr : nsl * T;
             const uint8_t* const fsl =
                 reinterpret_cast<const uint8_t*>(a.fs + a.fs_blk_off[S.list] * (int64_t)a.nchunks * 32);
             bool ok = true;
             for (int idx = (int)(((uint32_t)my + (uint32_t)ns - gpos % (uint32_t)ns) % (uint32_t)ns); idx < nst;
                  idx += ns) {
                 const uint32_t use = (gpos + (uint32_t)idx) / (uint32_t)ns;
-                int s, t = 0;
-                bool fsp;
+                int sl, t = 0;
                 if (is_b) {
-                    fsp = idx < fss;
-                    s = fsp ? idx : idx - fss;
+                    sl = idx % nsl;
                 } else {
-                    const int sl = idx / T;
-                    t = idx - sl * T;
-                    fsp = sl < fss;
-                    s = fsp ? sl : sl - fss;
+                    const int g = min(idx / (nsl * G), ngr - 1);
+                    const int t0 = g * G, Tg = min(G, T - t0), r = idx - g * nsl * G;
+                    sl = r / Tg;
+                    t = t0 + (r - sl * Tg);
                 }
+                const bool fsp = sl < fss;
+                const int s = fsp ? sl : sl - fss;
                 // the A stage's raw words, loaded before the slot is free
                 uint2 wv[4];  // one-hot: the 8 sign bytes (64 dimensions) of rows lane + 32 k
                 uint4 c4[8];  // 4-bit codes: the first of four rounds of the slab's raw bytes
@@ -404,15 +411,19 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     break;
                 }
                 if (is_b) {
-                    // queries' LUT (FastScan) or q_i8p (rerank) slab: chunk c of query i
-                    for (int e = lane; e < N * 16; e += 32) {
-                        const int i = e >> 4, c = e & 15;
-                        if (i >= nq) break;  // padding queries: their columns are never read
-                        const int64_t q = S.q[i];
-                        if (fsp)
-                            cp_async16(xs + sw_off(i, c), a.lut + (q * a.G * 16 + s * kSlab + c * 16));
-                        else if (s * kSlab + c * 16 < a.D)
-                            cp_async16(xs + sw_off(i, c), a.q_i8p + (q * a.D + s * kSlab + c * 16));
+                    // queries' LUT (FastScan) or q_i8p (rerank) slab: lane l copies chunk
+                    // c = l % 16 of queries i = l / 16, + 2, ... (padding queries: their
+                    // columns are never read)
+                    const int c = lane & 15;
+                    const uint8_t* const src = (fsp ? a.lut : a.q_i8p) + s * kSlab + c * 16;
+                    const int64_t row = fsp ? (int64_t)a.G * 16 : (int64_t)a.D;
+                    const uint32_t dst = xs + (uint32_t)(c >> 3) * (uint32_t)kAtomBytes;
+                    const uint32_t cx = (uint32_t)(c & 7);
+                    if (fsp || s * kSlab + c * 16 < a.D) {
+#pragma unroll 4
+                        for (int i = lane >> 4; i < nq; i += 2)
+                            cp_async16(dst + (uint32_t)i * 128u + ((cx ^ (uint32_t)(i & 7)) << 4),
+                                       src + (int64_t)S.q[i] * row);
                     }
                     cp_async_arrive(full);
                 } else if (fsp) {
@@ -476,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             if (lane == 0) mbar_arrive(&sm.item_empty[si]);
             padd(pl, p_loop, t_item);
             p_items += 1;
-            p_stages += (uint64_t)((fss + rr_slabs) * (T + 1));
+            p_stages += (uint64_t)(nsl * (T + ngr));
         }
         if (prof && pl) {
             prof[kPBuild] = p_loop;
@@ -493,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         // time -- issues the tcgen05.mma and tcgen05.commit instructions.
         {
             uint32_t ga = 0, gb = 0, uc = 0;  // ring positions, GEMMs so far
-            uint64_t p_wfull = 0, p_wfree = 0, p_loop = 0;
+            uint64_t p_wfull = 0, p_wfree = 0, p_loop = 0, p_wb = 0;
             const bool pl = lane == 0;  // the MMA warp's profiling lane
             auto wait_all = [&](uint64_t* bar, uint32_t parity) {
                 return __all_sync(0xffffffffu, mbar_wait(bar, parity, &sm.abort, wl)) != 0;
@@ -508,10 +519,12 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 if (S.item < 0) break;
                 const uint64_t t_item = prof ? global_ns() : 0;
                 const int N = S.N, T = S.T;
+                const int G = min(T, kHalfCols / N), ngr = (T + G - 1) / G;
                 bool ok = true;
-                // one GEMM: per slab the B stage, then the T A stages (nk K steps of 32) into
-                // half uc & 1, once the epilogue read out the GEMM two before
-                auto gemm = [&](int slabs, int k_bytes, uint32_t idesc) {
+                // one GEMM over a group of Tg row tiles: per slab the B stage, then the Tg A
+                // stages (nk K steps of 32) into half uc & 1, once the epilogue read out the
+                // GEMM two before
+                auto gemm = [&](int slabs, int k_bytes, uint32_t idesc, int Tg) {
                     const uint32_t h = uc & 1, use = uc >> 1;
                     const uint32_t dcol = tmem + h * kHalfCols;
                     const uint64_t t_f = prof ? global_ns() : 0;
@@ -528,9 +541,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                             break;
                         }
                         padd(pl, p_wfull, t_w);
+                        padd(pl, p_wb, t_w);
                         const int nk = min(kSlab, k_bytes - s * kSlab) / 32;
                         const uint64_t bd = sw128_desc(smem_u32(ring_b + bs * kStageBytes));
-                        for (int t = 0; t < T; ++t) {
+                        for (int t = 0; t < Tg; ++t) {
                             const uint32_t as = ga % kNA;
                             t_w = prof ? global_ns() : 0;
                             if (!wait_all(&sm.a_full[as], (ga / kNA) & 1)) {
@@ -553,8 +567,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     if (ok) umma_commit_elect(&sm.acc_full[h]);
                     ++uc;
                 };
-                if (S.fs) gemm(fs_slabs, 4 * a.D, idesc_i8(N, false));
-                if (ok) gemm(rr_slabs, a.D, idesc_i8(N, true));
+                for (int g = 0; g < ngr && ok; ++g) {
+                    const int Tg = min(G, T - g * G);
+                    if (S.fs) gemm(fs_slabs, 4 * a.D, idesc_i8(N, false), Tg);
+                    if (ok) gemm(rr_slabs, a.D, idesc_i8(N, true), Tg);
+                }
                 if (!ok) {
                     if (lane == 0) fail(7);
                     break;
@@ -566,6 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 prof[kPMmaWaitFull] = p_wfull;
                 prof[kPMmaWaitFree] = p_wfree;
                 prof[kPMma] = p_loop;
+                prof[kPMmaWaitB] = p_wb;
             }
             // before the TMEM is freed, every MMA issued (also after an abort) completes;
             // this wait ignores the abort flag and gives up after 0.5 s
@@ -697,17 +715,20 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             };
             const uint64_t t_copy = prof ? global_ns() : 0;
             if (S.fs) {
-                // FastScan item: every row's score (16-bit wrap of the signed-LUT sum) and then
-                // its int_ip to the FastScan scratch; fs_select_kernel takes the kept sets
-                for (int g = 0; g < 2 && !bad; ++g) {
+                // FastScan item, group by group of G row tiles: every row's score (16-bit wrap
+                // of the signed-LUT sum) and then its int_ip to the FastScan scratch;
+                // fs_select_kernel takes the kept sets
+                const int G = min(T, kHalfCols / N), ngr = (T + G - 1) / G;
+                for (int gg = 0; gg < 2 * ngr && !bad; ++gg) {
+                    const int g = gg & 1, t0 = (gg >> 1) * G, Tg = min(G, T - t0);
                     const uint64_t t_g = prof ? global_ns() : 0;
                     uint32_t dcol;
                     if (!gemm_begin(dcol)) {
                         bad = true;
                         break;
                     }
-                    for (int t = 0; t < T; ++t) {
-                        const int v = t * kRows + quarter * 32 + lane;
+                    for (int t = 0; t < Tg; ++t) {
+                        const int v = (t0 + t) * kRows + quarter * 32 + lane;
                         for (int c = c_lo; c < c_hi && c < nq; c += 8) {
                             uint32_t x[8];
                             tmem_ld8(dcol + (uint32_t)(t * N + c), x);

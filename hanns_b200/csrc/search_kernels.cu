@@ -1392,11 +1392,11 @@ __global__ void count_lists_kernel(const int32_t* __restrict__ probes, int64_t n
 // Queries per item of list l: tensor-core items for lists of at most tc_max_rows rows,
 // SIMT items of qpi queries otherwise.
 __device__ __forceinline__ int list_item_queries(const int64_t* list_off, int l, int tc_max_rows,
-                                                 int qpi, int* kind) {
+                                                 int n_cand, int qpi, int* kind) {
     const int64_t n = list_off[l + 1] - list_off[l];
     if (tc_max_rows > 0 && n <= tc_max_rows) {
         *kind = 1;
-        return tc_queries_per_item(n);
+        return tc_queries_per_item(n, n > n_cand);
     }
     *kind = 0;
     return qpi;
@@ -1405,7 +1405,7 @@ __device__ __forceinline__ int list_item_queries(const int64_t* list_off, int l,
 // Single CTA of 1024 threads: exclusive scans of cnt and of items-per-list.
 __global__ void __launch_bounds__(1024) prefix_lists_kernel(const int* __restrict__ cnt, int nlist,
                                                           const int64_t* __restrict__ list_off,
-                                                          int tc_max_rows, int qpi,
+                                                          int tc_max_rows, int n_cand, int qpi,
                                                           int* __restrict__ lq_off,
                                                           int* __restrict__ item_off,
                                                           int* __restrict__ n_items) {
@@ -1418,7 +1418,7 @@ __global__ void __launch_bounds__(1024) prefix_lists_kernel(const int* __restric
         const int l = base + threadIdx.x;
         const int a = l < nlist ? cnt[l] : 0;
         int kind = 0;
-        const int per = l < nlist ? list_item_queries(list_off, l, tc_max_rows, qpi, &kind) : 1;
+        const int per = l < nlist ? list_item_queries(list_off, l, tc_max_rows, n_cand, qpi, &kind) : 1;
         const int b = (a + per - 1) / per;
         const int ia = warp_inclusive_scan(a), ib = warp_inclusive_scan(b);
         if (lane == 31) {
@@ -1470,12 +1470,12 @@ __global__ void scatter_pairs_kernel(const int32_t* __restrict__ probes, int64_t
 
 __global__ void make_items_kernel(const int* __restrict__ cnt, const int* __restrict__ lq_off,
                                   const int* __restrict__ item_off, int nlist,
-                                  const int64_t* __restrict__ list_off, int tc_max_rows, int qpi,
-                                  int4* __restrict__ items) {
+                                  const int64_t* __restrict__ list_off, int tc_max_rows, int n_cand,
+                                  int qpi, int4* __restrict__ items) {
     for (int l = blockIdx.x * blockDim.x + threadIdx.x; l < nlist; l += gridDim.x * blockDim.x) {
         const int c = cnt[l];
         int kind = 0;
-        const int per = list_item_queries(list_off, l, tc_max_rows, qpi, &kind);
+        const int per = list_item_queries(list_off, l, tc_max_rows, n_cand, qpi, &kind);
         int o = item_off[l];
         for (int s = 0; s < c; s += per) items[o++] = make_int4(l, lq_off[l] + s, min(per, c - s), kind);
     }
@@ -3175,19 +3175,19 @@ void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, i
 }
 
 void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist,
-                        const uint8_t* owned, const int64_t* list_off, int tc_max_rows, int qpi,
-                        int* cnt, int* cursor, int* lq_off, int* item_off, int* n_items, int2* lq,
-                        int4* items, cudaStream_t s) {
+                        const uint8_t* owned, const int64_t* list_off, int tc_max_rows, int n_cand,
+                        int qpi, int* cnt, int* cursor, int* lq_off, int* item_off, int* n_items,
+                        int2* lq, int4* items, cudaStream_t s) {
     cudaMemsetAsync(cnt, 0, sizeof(int) * nlist, s);
     cudaMemsetAsync(cursor, 0, sizeof(int) * nlist, s);
     const int64_t pairs = nq * nprobe;
     const int blocks = (int)std::min<int64_t>((pairs + 255) / 256, 4096);
     count_lists_kernel<<<blocks, 256, 0, s>>>(probes, pairs, nlist, owned, cnt);
-    prefix_lists_kernel<<<1, 1024, 0, s>>>(cnt, nlist, list_off, tc_max_rows, qpi, lq_off, item_off,
-                                           n_items);
+    prefix_lists_kernel<<<1, 1024, 0, s>>>(cnt, nlist, list_off, tc_max_rows, n_cand, qpi, lq_off,
+                                           item_off, n_items);
     scatter_pairs_kernel<<<blocks, 256, 0, s>>>(probes, nq, nprobe, nlist, owned, lq_off, cursor, lq);
     make_items_kernel<<<(nlist + 255) / 256, 256, 0, s>>>(cnt, lq_off, item_off, nlist, list_off,
-                                                          tc_max_rows, qpi, items);
+                                                          tc_max_rows, n_cand, qpi, items);
 }
 
 size_t scan_smem_bytes(int D) {
