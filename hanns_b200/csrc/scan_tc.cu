@@ -33,25 +33,26 @@
 //
 // Operands stream through two rings of 32 KiB stages (128 rows x 256 K bytes: two 128-byte
 // swizzle atoms, K-major): A (kNA slots, the row tiles) and B (kNB slots, the queries).  Per
-// GEMM and K slab the MMA consumes one B stage and then the group's A stages.  Each ring slot
-// has one builder warp, which fills the slot's positions in ring order, so every wait of
-// a builder on its slot's empty barrier is for the phase right after the last one it saw.
+// GEMM and K slab the MMA consumes one B stage and then the group's A stages.  Each A slot
+// has two builder warps (64 rows each) and each B slot one; a builder fills its slot's
+// positions in ring order, so every wait of a builder on its slot's empty barrier is for
+// the phase right after the last one it saw.
 //
-// Warp roles (16 warps, four per SM sub-partition):
-//   warps 0-3   A builders.  One-hot rows (sign bytes loaded into registers before the slot
-//               is free, then expanded), 4-bit codes (the first of four rounds loaded, the
-//               rest prefetched into L1, unpacked), 8-bit codes (cp.async straight into
-//               their swizzled places)
-//   warps 4-5   B builders: the queries' LUT or q_i8p slab rows, cp.async
+// Warp roles (15 warps):
+//   warps 0-5   A builders, two per slot.  One-hot rows (sign bytes loaded into registers
+//               before the slot is free, then expanded), 4-bit codes (the warp's first
+//               round of raw bytes loaded, the other prefetched into L1, unpacked), 8-bit
+//               codes (cp.async straight into their swizzled places)
+//   warp 6      TMEM allocation and the MMA issuer (the whole warp runs the loop with
+//               warp-uniform descriptors; one elected lane issues the MMAs and commits)
+//   warp 7      item scheduler: takes items, fills the item slots, prefetches the next
+//               item's list into L2
+//   warps 8-11  epilogue (thread per row, warp w on TMEM lanes 32 (w % 4) ..): FastScan
+//               items' scores and int_ip TMEM -> the FastScan scratch; rerank-only items'
+//               kept rows (bitmaps) and their distances and ties
+//   warps 12-14 B builders: the queries' LUT or q_i8p slab rows, cp.async
 //               Copies complete on the slot's full barrier (cp.async.mbarrier.arrive): a
 //               builder never waits for them.
-//   warps 6-13  epilogue (thread per row): FastScan items' scores and int_ip TMEM -> the
-//               FastScan scratch; rerank-only items' kept rows (bitmaps) and their
-//               distances and ties
-//   warp 14     TMEM allocation and the MMA issuer (the whole warp runs the loop with
-//               warp-uniform descriptors; one elected lane issues the MMAs and commits)
-//   warp 15     item scheduler: takes items, fills the item slots, prefetches the next
-//               item's list into L2
 // Every wait is bounded (wait_ns, 2 s by default): on expiry the kernel records an error
 // code, every role leaves its loop, the MMAs already issued complete, and the TMEM is
 // freed.
@@ -63,12 +64,18 @@
 namespace hanns {
 namespace {
 
-constexpr int kNA = 3, kNB = 3;                   // ring slots, one builder warp each
-constexpr int kBuildWarps = kNA + kNB;            // warps 0-2 A, 3-5 B
-constexpr int kEpiWarps = 8;                      // warps 6-13
-constexpr int kMmaWarp = kBuildWarps + kEpiWarps;  // 14
-constexpr int kSchedWarp = kMmaWarp + 1;          // 15
-constexpr int kThreads = (kSchedWarp + 1) * 32;   // 512
+constexpr int kNA = 3, kNB = 3;                   // ring slots
+constexpr int kAW = 2;                            // builder warps per A slot (64 rows each)
+constexpr int kAWarps = kNA * kAW;                // warps 0-5: A builders
+constexpr int kMmaWarp = kAWarps;                 // 6
+constexpr int kSchedWarp = kMmaWarp + 1;          // 7
+constexpr int kEpiWarp0 = kSchedWarp + 1;         // 8-11: epilogue, one per TMEM lane quarter
+constexpr int kEpiWarps = 4;
+constexpr int kBWarp0 = kEpiWarp0 + kEpiWarps;    // 12-14: B builders, one per B slot
+constexpr int kBuildWarps = kAWarps + kNB;        // 9
+constexpr int kRB = 128 / 32 / kAW;               // 32-row blocks per A builder warp
+constexpr int kThreads = (kBWarp0 + kNB) * 32;    // 480
+static_assert(kEpiWarp0 % 4 == 0, "epilogue warp w reads TMEM lanes 32 (w % 4) ..");
 constexpr int kRows = 128;                        // MMA M: list rows per tile
 constexpr int kMaxQ = 128;                        // queries per item
 constexpr int kHalfCols = 256;                    // TMEM columns of one GEMM
@@ -278,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
 
     if (tid == 0) {
         for (int s = 0; s < kNA; ++s) {
-            mbar_init(&sm.a_full[s], 32);  // the builder warp's 32 lanes
+            mbar_init(&sm.a_full[s], 32 * kAW);  // the builder warps' lanes
             mbar_init(&sm.a_empty[s], 1);
         }
         for (int s = 0; s < kNB; ++s) {
@@ -320,10 +327,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         sm.abort = 1;
     };
 
-    if (warp < kBuildWarps) {
+    if (warp < kAWarps || warp >= kBWarp0) {
         // ------------------------------------------------------------ builders
-        const bool is_b = warp >= kNA;
-        const int my = is_b ? warp - kNA : warp;  // the ring slot this warp fills
+        const bool is_b = warp >= kBWarp0;
+        const int my = is_b ? warp - kBWarp0 : warp / kAW;  // the ring slot this warp fills
+        const int part = is_b ? 0 : warp % kAW;              // A: rows 64 part .. + 63
         const int ns = is_b ? kNB : kNA;
         uint64_t* const full = is_b ? &sm.b_full[my] : &sm.a_full[my];
         uint64_t* const empty = is_b ? &sm.b_empty[my] : &sm.a_empty[my];
@@ -367,9 +375,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                 }
                 const bool fsp = sl < fss;
                 const int s = fsp ? sl : sl - fss;
-                // the A stage's raw words, loaded before the slot is free
-                uint2 wv[4];  // one-hot: the 8 sign bytes (64 dimensions) of rows lane + 32 k
-                uint4 c4[8];  // 4-bit codes: the first of four rounds of the slab's raw bytes
+                // the A stage's raw words, loaded before the slot is free (this warp's rows:
+                // 32 k + lane for k = kRB * part .. + kRB - 1)
+                uint2 wv[kRB];  // one-hot: the 8 sign bytes (64 dimensions) of each row
+                uint4 c4[8];    // 4-bit codes: the first of this warp's rounds of raw bytes
                 const int nj = min(8, (a.D - s * kSlab) / 32);  // 32-dimension quarters of the slab
                 // 4-bit raw quarter of round rd, step m (rows r = 32 rd + 8 (m / 2) + lane / 4;
                 // quarter jj = lane % 4 + 4 (m % 2)): its address and whether it exists
@@ -383,21 +392,23 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     // sign bytes of row v for slab s (64 dimensions): the row's 8-byte chunk s
                     // (layout [block of 32 rows][chunk][row in block])
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
+                    for (int kk = 0; kk < kRB; ++kk) {
+                        const int k = kRB * part + kk;
                         const int v = t * kRows + 32 * k + lane;
-                        wv[k] = v < n ? __ldg(reinterpret_cast<const uint2*>(
-                                            fsl + ((((int64_t)(t * 4 + k) * a.nchunks + s) * 32 + lane) * 8)))
-                                      : make_uint2(0u, 0u);
+                        wv[kk] = v < n ? __ldg(reinterpret_cast<const uint2*>(
+                                             fsl + ((((int64_t)(t * 4 + k) * a.nchunks + s) * 32 + lane) * 8)))
+                                       : make_uint2(0u, 0u);
                     }
                 } else if (!is_b && a.nbits == 4) {
-                    // round 0 into registers, rounds 1-3 into L1 (loaded after the stores before)
+                    // the warp's first round into registers, the others into L1 (loaded after
+                    // the stores before)
 #pragma unroll
-                    for (int rd = 0; rd < 4; ++rd)
+                    for (int rr = 0; rr < kRB; ++rr)
 #pragma unroll
                         for (int m = 0; m < 8; ++m) {
                             bool has;
-                            const uint8_t* src = q4src(rd, m, has);
-                            if (rd == 0)
+                            const uint8_t* src = q4src(kRB * part + rr, m, has);
+                            if (rr == 0)
                                 c4[m] = has ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
                             else if (has)
                                 asm volatile("prefetch.global.L1 [%0];" ::"l"(src));
@@ -428,20 +439,20 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     cp_async_arrive(full);
                 } else if (fsp) {
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int r = 32 * k + lane;
+                    for (int kk = 0; kk < kRB; ++kk) {
+                        const int r = 32 * (kRB * part + kk) + lane;
                         if (t * kRows + r < n) {
 #pragma unroll
                             for (int c = 0; c < 16; ++c)
                                 *reinterpret_cast<uint4*>(X + sw_off(r, c)) =
-                                    onehot16(((c < 8 ? wv[k].x : wv[k].y) >> (4 * (c & 7))) & 15u);
+                                    onehot16(((c < 8 ? wv[kk].x : wv[kk].y) >> (4 * (c & 7))) & 15u);
                         }
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mbar_arrive(full);
                 } else if (a.nbits == 8) {
                     // 8-bit codes are the operand: straight into their swizzled places
-                    for (int e = lane; e < kRows * 16; e += 32) {
+                    for (int e = part * (kRows / kAW) * 16 + lane; e < (part + 1) * (kRows / kAW) * 16; e += 32) {
                         const int r = e >> 4, c = e & 15;
                         const int v = t * kRows + r, d = s * kSlab + c * 16;
                         if (v < n && d < a.D)
@@ -452,8 +463,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
                     // 4-bit codes: a 16-byte quarter jj (32 dimensions, 4 code words of 8) becomes
                     // chunks 2 jj and 2 jj + 1: per word its low nibbles, then its high ones
 #pragma unroll 1
-                    for (int rd = 0; rd < 4; ++rd) {
-                        if (rd > 0) {
+                    for (int rd = kRB * part; rd < kRB * (part + 1); ++rd) {
+                        if (rd > kRB * part) {
 #pragma unroll
                             for (int m = 0; m < 8; ++m) {
                                 bool has;
@@ -674,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
         // ------------------------------------------------------------ epilogue
         // Every failed wait turns into `bad`, which is ORed over the epilogue warps at the
         // next barrier; all of them leave the loop together.
-        const int e = warp - kBuildWarps;             // 0..7
+        const int e = warp - kEpiWarp0;               // 0..kEpiWarps-1
         const int quarter = warp & 3, half = e >> 2;  // TMEM lanes 32*quarter.., column half
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         uint32_t uc = 0;  // GEMMs so far (the MMA issuer's count)
@@ -696,7 +707,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(TcScanArgs a) {
             const int n = S.n, nq = S.nq, N = S.N, T = S.T;
             const int64_t beg = S.beg;
             const int NP = T * kRows, W = T * 4;  // rows incl. padding, bitmap words per query
-            const int c_lo = half * (N >> 1), c_hi = c_lo + (N >> 1);
+            constexpr int kEpiHalves = kEpiWarps / 4;  // warps per TMEM lane quarter
+            const int c_lo = half * (N / kEpiHalves), c_hi = c_lo + N / kEpiHalves;
             // waits for the next GEMM's accumulators; false on a failed wait
             auto gemm_begin = [&](uint32_t& dcol) -> bool {
                 const uint32_t h = uc & 1, use = uc >> 1;
