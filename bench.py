@@ -305,10 +305,10 @@ def scan_roofline_tc(workload, alg_bytes, ops, scan_s, world):
             "algorithmic_bytes_per_launch": alg_bytes, "algorithmic_gbs": alg_bytes / scan_s / 1e9,
             "algorithmic_frac_of_hbm": alg_bytes / scan_s / 1e9 / hbm, "hbm_peak_gbs": hbm,
             "hbm_peak_source": hbm_kind,
-            "limiter": "operand staging: per 16 KiB K slab the builder warps expand sign bits to "
-                       "one-hot rows / unpack codes in shared memory and hand the stage to the "
-                       "single MMA-issuing thread through an mbarrier round trip; at 64-128 "
-                       "queries per item each stage carries ~0.1 us of tensor work"}
+            "limiter": "operand staging: the A builder warps' global loads of sign words and codes "
+                       "(long-scoreboard stalls) before they expand one-hot rows / unpack codes into "
+                       "a 32 KiB ring stage, and the mbarrier hand-off of each stage to the MMA "
+                       "warp; tensor activity also varies by SM with the list sizes of its items"}
     if traffic:
         roof["dram_gbs"] = traffic / scan_s / 1e9
         roof["dram_frac_of_hbm"] = roof["dram_gbs"] / hbm
