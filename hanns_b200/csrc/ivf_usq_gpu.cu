@@ -205,8 +205,14 @@ void IvfUsqGpu::set_list_layout(const std::vector<int64_t>& h_off) {
         max_list_ = (int)std::max<int64_t>(max_list_, len);
         blk[l + 1] = blk[l] + (len + 31) / 32;
     }
+    std::vector<int> order(nlist_);
+    for (int l = 0; l < nlist_; ++l) order[l] = l;
+    std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+        return h_off[x + 1] - h_off[x] > h_off[y + 1] - h_off[y];
+    });
     h2d(list_off_, h_off.data(), h_off.size(), stream_);
     h2d(fs_blk_off_, blk.data(), blk.size(), stream_);
+    if (nlist_ > 0) h2d(list_order_, order.data(), order.size(), stream_);
     HANNS_CUDA_OK(cudaStreamSynchronize(stream_));
 }
 
@@ -755,7 +761,7 @@ int64_t IvfUsqGpu::scan_merge_batch(int64_t nb, const SearchOptions& opt, const 
     const bool use_tc = tc_rows > 0;
     const int64_t fss = fs_stride(nprobe, n_cand, tc_rows);
     launch_group_pairs(st.probes, nb, nprobe, nlist_, sharded_ ? owned_.p : nullptr, list_off_.p,
-                       tc_rows, n_cand, kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p,
+                       list_order_.p, tc_rows, n_cand, kQueriesPerItem, w_cnt_.p, w_cursor_.p, w_lq_off_.p,
                        w_item_off_.p, w_counters_.p, w_lq_.p, w_items_.p, s);
     const int64_t q_stride = cand_stride(nprobe, k);
     w_pair_off_.reserve((size_t)nb * (nprobe + 1));

@@ -212,6 +212,9 @@ class IvfUsqGpu {
     DevBuf<uint16_t> cent_hi_, cent_lo_;  // bf16 split of the centroids [nlist][tc_k_]
     int tc_k_ = 64;
     DevBuf<int64_t> list_off_, fs_blk_off_, ids_;
+    // the lists by decreasing length (stable): the order in which the grouping step lays
+    // out the scan's items, so the persistent scans claim the longest lists first
+    DevBuf<int> list_order_;
     DevBuf<float4> meta_;
     DevBuf<uint8_t> codes_, signs_, owned_;
     DevBuf<uint2> fs_;

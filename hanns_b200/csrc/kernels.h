@@ -241,9 +241,13 @@ void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, i
 // Items (list, first lq index, queries, kind): lists of at most tc_max_rows rows (0:
 // none) become tensor-core items (kind 1) of tc_queries_per_item(|list|, |list| > n_cand)
 // queries, the
-// others SIMT items (kind 0) of qpi queries.
+// others SIMT items (kind 0) of qpi queries.  Items and pairs are laid out list by list in
+// `order` (a permutation of the lists, or null for list order); every item and pair
+// writes to places fixed by its (query, probe), so the order changes no result, only
+// which items the persistent scans claim first.
 void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist,
-                        const uint8_t* owned, const int64_t* list_off, int tc_max_rows, int n_cand,
+                        const uint8_t* owned, const int64_t* list_off, const int* order,
+                        int tc_max_rows, int n_cand,
                         int qpi, int* cnt, int* cursor, int* lq_off, int* item_off, int* n_items,
                         int2* lq, int4* items, cudaStream_t s);
 // pair_off[q][r] = sum over earlier probes of min(|list|, n_cand) (0 for lists this

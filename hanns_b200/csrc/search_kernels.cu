@@ -1402,8 +1402,10 @@ __device__ __forceinline__ int list_item_queries(const int64_t* list_off, int l,
     return qpi;
 }
 
-// Single CTA of 1024 threads: exclusive scans of cnt and of items-per-list.
+// Single CTA of 1024 threads: exclusive scans of cnt and of items-per-list, over the lists
+// in `order` (null: list order).
 __global__ void __launch_bounds__(1024) prefix_lists_kernel(const int* __restrict__ cnt, int nlist,
+                                                          const int* __restrict__ order,
                                                           const int64_t* __restrict__ list_off,
                                                           int tc_max_rows, int n_cand, int qpi,
                                                           int* __restrict__ lq_off,
@@ -1415,7 +1417,8 @@ __global__ void __launch_bounds__(1024) prefix_lists_kernel(const int* __restric
     if (threadIdx.x == 0) carry_a = carry_b = 0;
     __syncthreads();
     for (int base = 0; base < nlist; base += 1024) {
-        const int l = base + threadIdx.x;
+        const int i = base + threadIdx.x;
+        const int l = i < nlist ? (order ? order[i] : i) : nlist;
         const int a = l < nlist ? cnt[l] : 0;
         int kind = 0;
         const int per = l < nlist ? list_item_queries(list_off, l, tc_max_rows, n_cand, qpi, &kind) : 1;
@@ -3175,7 +3178,8 @@ void launch_query_state(const float* x, const float* q_rot, int64_t nq, int d, i
 }
 
 void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist,
-                        const uint8_t* owned, const int64_t* list_off, int tc_max_rows, int n_cand,
+                        const uint8_t* owned, const int64_t* list_off, const int* order,
+                        int tc_max_rows, int n_cand,
                         int qpi, int* cnt, int* cursor, int* lq_off, int* item_off, int* n_items,
                         int2* lq, int4* items, cudaStream_t s) {
     cudaMemsetAsync(cnt, 0, sizeof(int) * nlist, s);
@@ -3183,7 +3187,7 @@ void launch_group_pairs(const int32_t* probes, int64_t nq, int nprobe, int nlist
     const int64_t pairs = nq * nprobe;
     const int blocks = (int)std::min<int64_t>((pairs + 255) / 256, 4096);
     count_lists_kernel<<<blocks, 256, 0, s>>>(probes, pairs, nlist, owned, cnt);
-    prefix_lists_kernel<<<1, 1024, 0, s>>>(cnt, nlist, list_off, tc_max_rows, n_cand, qpi, lq_off,
+    prefix_lists_kernel<<<1, 1024, 0, s>>>(cnt, nlist, order, list_off, tc_max_rows, n_cand, qpi, lq_off,
                                            item_off, n_items);
     scatter_pairs_kernel<<<blocks, 256, 0, s>>>(probes, nq, nprobe, nlist, owned, lq_off, cursor, lq);
     make_items_kernel<<<(nlist + 255) / 256, 256, 0, s>>>(cnt, lq_off, item_off, nlist, list_off,
