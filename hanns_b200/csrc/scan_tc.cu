@@ -38,7 +38,7 @@
 // positions in ring order, so every wait of a builder on its slot's empty barrier is for
 // the phase right after the last one it saw.
 //
-// Warp roles (15 warps):
+// Warp roles (19 warps, 96 registers each):
 //   warps 0-5   A builders, two per slot.  One-hot rows (sign bytes loaded into registers
 //               before the slot is free, then expanded), 4-bit codes (the warp's first
 //               round of raw bytes loaded, the other prefetched into L1, unpacked), 8-bit
@@ -47,10 +47,11 @@
 //               warp-uniform descriptors; one elected lane issues the MMAs and commits)
 //   warp 7      item scheduler: takes items, fills the item slots, prefetches the next
 //               item's list into L2
-//   warps 8-11  epilogue (thread per row, warp w on TMEM lanes 32 (w % 4) ..): FastScan
-//               items' scores and int_ip TMEM -> the FastScan scratch; rerank-only items'
-//               kept rows (bitmaps) and their distances and ties
-//   warps 12-14 B builders: the queries' LUT or q_i8p slab rows, cp.async
+//   warps 8-15  epilogue (thread per row, warp w on TMEM lanes 32 (w % 4) .., warps w and
+//               w + 4 on the two halves of the item's query columns): FastScan items'
+//               scores and int_ip TMEM -> the FastScan scratch; rerank-only items' kept
+//               rows (bitmaps) and their distances and ties
+//   warps 16-18 B builders: the queries' LUT or q_i8p slab rows, cp.async
 //               Copies complete on the slot's full barrier (cp.async.mbarrier.arrive): a
 //               builder never waits for them.
 // Every wait is bounded (wait_ns, 2 s by default): on expiry the kernel records an error
@@ -69,12 +70,12 @@ constexpr int kAW = 2;                            // builder warps per A slot (6
 constexpr int kAWarps = kNA * kAW;                // warps 0-5: A builders
 constexpr int kMmaWarp = kAWarps;                 // 6
 constexpr int kSchedWarp = kMmaWarp + 1;          // 7
-constexpr int kEpiWarp0 = kSchedWarp + 1;         // 8-11: epilogue, one per TMEM lane quarter
-constexpr int kEpiWarps = 4;
-constexpr int kBWarp0 = kEpiWarp0 + kEpiWarps;    // 12-14: B builders, one per B slot
+constexpr int kEpiWarp0 = kSchedWarp + 1;         // 8-15: epilogue, two per TMEM lane quarter
+constexpr int kEpiWarps = 8;
+constexpr int kBWarp0 = kEpiWarp0 + kEpiWarps;    // 16-18: B builders, one per B slot
 constexpr int kBuildWarps = kAWarps + kNB;        // 9
 constexpr int kRB = 128 / 32 / kAW;               // 32-row blocks per A builder warp
-constexpr int kThreads = (kBWarp0 + kNB) * 32;    // 480
+constexpr int kThreads = (kBWarp0 + kNB) * 32;    // 608
 static_assert(kEpiWarp0 % 4 == 0, "epilogue warp w reads TMEM lanes 32 (w % 4) ..");
 constexpr int kRows = 128;                        // MMA M: list rows per tile
 constexpr int kMaxQ = 128;                        // queries per item
