@@ -148,6 +148,14 @@ class IvfUsqIndex:
                                                         self.config.rotation_seed, rerank_k),
                "save IVFUSQ00")
 
+    def save(self, path: str):
+        """IvfUsqIndex::save (src/faiss/ivf_usq.rs:354-406): the "IVFUSQ00" snapshot, with
+        the config's rerank_k stored as the reference stores it."""
+        self.save_ivfusq00(path, rerank_k=self.config.rerank_k)
+
+    # IvfUsqIndex::load (src/faiss/ivf_usq.rs:411-506)
+    load = load_ivfusq00
+
     def export_artifact(self) -> dict:
         shp = np.zeros(6, np.int64)
         _check(L.lib().hanns_gpu_ivf_usq_shape(self._h, _p(shp, L.i64p)), "shape")
@@ -360,3 +368,10 @@ class IvfUsqIndex:
 
     def has_raw_data(self) -> bool:
         return False
+
+    def size(self) -> int:
+        """IvfUsqIndex::size (src/faiss/ivf_usq.rs:208-222): centroid bytes plus, per stored
+        row, its id (8), four f32 factors (16) and packed code bytes."""
+        D = -(-self.config.dim // 64) * 64
+        code_bytes = (D * self.config.bits_per_dim + 7) // 8
+        return self.config.nlist * self.config.dim * 4 + self.count() * (8 + 16 + code_bytes)
